@@ -1,0 +1,689 @@
+// allreduce.cu - sm_100a all-reduce kernels and their launcher.
+//
+// One CTA is one channel; channel c walks tiles c, c + C, ... of the message
+// (protocol.h) and keeps its FIFO sequence number in device memory, so every
+// launch continues where the previous one on the same communicator stopped.
+//
+//   ring     tiny-nccl's reduce-scatter + all-gather rotation
+//            (src/ring_allreduce.cu:12-54) per channel, with 16-byte vector
+//            peer stores, pre-scale, fp32 math and a fused final
+//            reduce+store+forward step. Summation order of chunk s:
+//            ((a*x[s+1] + a*x[s+2]) + ...) + a*x[s], rounded to the wire
+//            type at every hop.
+//   one-shot every rank pushes its whole tile into every peer's mailbox and
+//            reduces all P contributions locally in rank order 0..P-1.
+//   two-shot reduce-scatter by pushing chunk j to rank j, which reduces in
+//            rank order 0..P-1, then all-gather by pushing the reduced chunk
+//            to every peer. Each rank both sends to and receives from every
+//            peer in both phases, which doubles as flow control: no credit
+//            words are needed (see the slot-reuse argument below).
+//   NVLS     copy the tile into the multicast-bound buffer, barrier, reduce
+//            this rank's share in the NVSwitch (multimem.ld_reduce), broadcast
+//            it with multimem.st, barrier, copy the tile out.
+//
+// Every wait is bounded (device.cuh); a CTA whose wait fails stops, leaves
+// its sequence number untouched and the host sees the recorded error.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "device.cuh"
+#include "launch.h"
+#include "protocol.h"
+#include "tnccl.h"
+
+namespace tnccl {
+namespace {
+
+using namespace dev;
+
+constexpr int kLdInput = 0;
+constexpr int kLdMailbox = 1;
+constexpr int kMaxThreads = 512;
+
+template <int LD>
+__device__ __forceinline__ uint4 ld16(const void* p) {
+  return LD == kLdInput ? ldInput(p) : ldMailbox(p);
+}
+
+// Scalar element access (message tails and unaligned buffers).
+template <typename T, int LD>
+__device__ __forceinline__ float ldElem(const T* p) {
+  if constexpr (sizeof(T) == 4) {
+    uint32_t v;
+    if (LD == kLdMailbox)
+      asm volatile("ld.global.cg.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    else
+      asm volatile("ld.global.cs.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return __uint_as_float(v);
+  } else {
+    unsigned short v;
+    if (LD == kLdMailbox)
+      asm volatile("ld.global.cg.b16 %0, [%1];" : "=h"(v) : "l"(p) : "memory");
+    else
+      asm volatile("ld.global.cs.b16 %0, [%1];" : "=h"(v) : "l"(p) : "memory");
+    T t = *reinterpret_cast<T*>(&v);
+    return Pack<T>::toF(t);
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void stElem(T* p, float x) {
+  *p = Pack<T>::fromF(x);
+}
+
+// dst[i] = (scale ? alpha*src[i] : src[i]) for every destination returned by
+// dstPtr(d), d < ndst. Loads are issued U at a time before any store.
+template <typename T, int LD, int U, typename DstF>
+__device__ __forceinline__ void copyOut(const T* src, uint64_t n, bool vec, bool scale,
+                                        float alpha, int ndst, DstF dstPtr) {
+  using Pk = Pack<T>;
+  constexpr int V = Pk::V;
+  const uint64_t NT = blockDim.x;
+  const uint64_t nvec = vec ? n / V : 0;
+  const uint4* s4 = reinterpret_cast<const uint4*>(src);
+  for (uint64_t base = threadIdx.x; base < nvec; base += NT * U) {
+    uint4 v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint64_t i = base + u * NT;
+      if (i < nvec) v[u] = ld16<LD>(s4 + i);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint64_t i = base + u * NT;
+      if (i < nvec) {
+        uint4 w = v[u];
+        if (scale) {
+          float f[V];
+          Pk::unpack(w, f);
+#pragma unroll
+          for (int e = 0; e < V; ++e) f[e] = scaled(alpha, f[e]);
+          w = Pk::pack(f);
+        }
+        for (int d = 0; d < ndst; ++d) st16(reinterpret_cast<uint4*>(dstPtr(d)) + i, w);
+      }
+    }
+  }
+  for (uint64_t e = nvec * V + threadIdx.x; e < n; e += NT) {
+    float f = ldElem<T, LD>(src + e);
+    if (scale) f = scaled(alpha, f);
+    for (int d = 0; d < ndst; ++d) stElem(reinterpret_cast<T*>(dstPtr(d)) + e, f);
+  }
+}
+
+// out[i] = sum_{k<P} alpha * src_k[i] in rank order, fp32 accumulation.
+// Source localIdx is read from `local` (user input), every other source from
+// srcPtr(k) (mailbox). out(i, pack) stores a 16-byte result; outElem(e, f)
+// stores a scalar result.
+template <typename T, int MAXP, int U, typename SrcF, typename OutF, typename OutElemF>
+__device__ __forceinline__ void reduceRanks(uint64_t n, bool vec, int P, int localIdx,
+                                            const T* local, float alpha, SrcF srcPtr, OutF out,
+                                            OutElemF outElem) {
+  using Pk = Pack<T>;
+  constexpr int V = Pk::V;
+  const uint64_t NT = blockDim.x;
+  const uint64_t nvec = vec ? n / V : 0;
+  for (uint64_t base = threadIdx.x; base < nvec; base += NT * U) {
+    uint4 raw[U][MAXP];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint64_t i = base + u * NT;
+      if (i < nvec) {
+#pragma unroll
+        for (int k = 0; k < MAXP; ++k) {
+          if (k < P) {
+            raw[u][k] = k == localIdx
+                            ? ldInput(reinterpret_cast<const uint4*>(local) + i)
+                            : ldMailbox(reinterpret_cast<const uint4*>(srcPtr(k)) + i);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint64_t i = base + u * NT;
+      if (i < nvec) {
+        float acc[V], f[V];
+        Pk::unpack(raw[u][0], acc);
+#pragma unroll
+        for (int e = 0; e < V; ++e) acc[e] = scaled(alpha, acc[e]);
+#pragma unroll
+        for (int k = 1; k < MAXP; ++k) {
+          if (k < P) {
+            Pk::unpack(raw[u][k], f);
+#pragma unroll
+            for (int e = 0; e < V; ++e) acc[e] = addRn(acc[e], scaled(alpha, f[e]));
+          }
+        }
+        out(i, Pk::pack(acc));
+      }
+    }
+  }
+  for (uint64_t e = nvec * V + threadIdx.x; e < n; e += NT) {
+    float acc = 0.f;
+    for (int k = 0; k < P; ++k) {
+      const float v = k == localIdx ? ldElem<T, kLdInput>(local + e)
+                                    : ldElem<T, kLdMailbox>(reinterpret_cast<const T*>(srcPtr(k)) + e);
+      acc = k == 0 ? scaled(alpha, v) : addRn(acc, scaled(alpha, v));
+    }
+    outElem(e, acc);
+  }
+}
+
+// One ring hop: out = in + alpha * x with fp32 math and one rounding to T
+// (tiny-nccl src/device.cuh:187 adds `received + local` the same way).
+template <typename T, int U, typename OutF, typename OutElemF>
+__device__ __forceinline__ void ringHop(uint64_t n, bool vec, const T* in, const T* x,
+                                        float alpha, OutF out, OutElemF outElem) {
+  using Pk = Pack<T>;
+  constexpr int V = Pk::V;
+  const uint64_t NT = blockDim.x;
+  const uint64_t nvec = vec ? n / V : 0;
+  for (uint64_t base = threadIdx.x; base < nvec; base += NT * U) {
+    uint4 a[U], b[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint64_t i = base + u * NT;
+      if (i < nvec) {
+        a[u] = ldMailbox(reinterpret_cast<const uint4*>(in) + i);
+        b[u] = ldInput(reinterpret_cast<const uint4*>(x) + i);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint64_t i = base + u * NT;
+      if (i < nvec) {
+        float fa[V], fb[V];
+        Pk::unpack(a[u], fa);
+        Pk::unpack(b[u], fb);
+#pragma unroll
+        for (int e = 0; e < V; ++e) fa[e] = addRn(fa[e], scaled(alpha, fb[e]));
+        out(i, Pk::pack(fa));
+      }
+    }
+  }
+  for (uint64_t e = nvec * V + threadIdx.x; e < n; e += NT)
+    outElem(e, addRn(ldElem<T, kLdMailbox>(in + e), scaled(alpha, ldElem<T, kLdInput>(x + e))));
+}
+
+// ---------------------------------------------------------------------------
+// Two-shot
+//
+// Slot reuse without credits (one slot per channel): rank r writes tile n+1
+// into rank j's reduce-scatter area only after it received j's all-gather
+// data for tile n, which j sends after it finished reading that area. Rank j
+// writes tile n+1 into r's all-gather area only after it received r's
+// reduce-scatter data for tile n+1, which r sends after it finished copying
+// tile n out of that area.
+// ---------------------------------------------------------------------------
+template <typename T, int MAXP>
+__global__ void __launch_bounds__(kMaxThreads)
+    twoShotKernel(const __grid_constant__ DevComm comm, const __grid_constant__ AllReduceArgs a) {
+  constexpr int V = Pack<T>::V;
+  constexpr int U = 1;
+  const int c = blockIdx.x, tid = threadIdx.x, P = comm.nranks, r = comm.rank;
+  const MailboxLayout& L = comm.layout;
+  char* const me = comm.peers[r];
+  const T* x = static_cast<const T*>(a.send);
+  T* y = static_cast<T*>(a.recv);
+  const ChunkPlan& pl = a.chunk;
+  const bool vec = a.vectorized != 0;
+  __shared__ int sFail;
+  if (tid == 0) sFail = 0;
+  uint64_t seq = comm.counters[kCounterTwoShot * kMaxChannels + c];
+  __syncthreads();
+  const uint64_t ntiles = channelTiles(pl.numTiles, pl.channels, c);
+  for (uint64_t t = 0; t < ntiles; ++t) {
+    const uint64_t tile = (uint64_t)c + t * (uint64_t)pl.channels;
+    const uint64_t want = seq + 1;
+    // 1. reduce-scatter push: chunk j of my input -> rank j (raw, unscaled).
+    for (int k = 1; k < P; ++k) {
+      const int j = (r + k) % P;
+      const Span sp = chunkSpan(pl, tile, j, V);
+      char* dst = comm.peers[j] + tsRsDataAt(L, c, r);
+      copyOut<T, kLdInput, 4>(x + sp.offset, sp.count, vec, false, 1.f, 1,
+                              [dst](int) { return dst; });
+    }
+    __syncthreads();
+    if (tid < P && tid != r) stReleaseSys(flagPtr(comm.peers[tid], tsRsFlagAt(L, c, r)), want);
+    if (tid < P && tid != r &&
+        !waitFlag(comm, flagPtr(me, tsRsFlagAt(L, c, tid)), want,
+                  whereCode(kCounterTwoShot, c, 1)))
+      sFail = 1;
+    __syncthreads();
+    if (sFail) break;
+    // 2. reduce my chunk in rank order, store it locally and push it to all.
+    const Span own = chunkSpan(pl, tile, r, V);
+    const uint64_t agOff = tsAgDataAt(L, c, r);
+    reduceRanks<T, MAXP, U>(
+        own.count, vec, P, r, x + own.offset, a.scale,
+        [&](int k) { return me + tsRsDataAt(L, c, k); },
+        [&](uint64_t i, uint4 v) {
+          st16(reinterpret_cast<uint4*>(y + own.offset) + i, v);
+          for (int k = 1; k < P; ++k) {
+            const int j = (r + k) % P;
+            st16(reinterpret_cast<uint4*>(comm.peers[j] + agOff) + i, v);
+          }
+        },
+        [&](uint64_t e, float f) {
+          stElem(y + own.offset + e, f);
+          for (int k = 1; k < P; ++k) {
+            const int j = (r + k) % P;
+            stElem(reinterpret_cast<T*>(comm.peers[j] + agOff) + e, f);
+          }
+        });
+    __syncthreads();
+    if (tid < P && tid != r) stReleaseSys(flagPtr(comm.peers[tid], tsAgFlagAt(L, c, r)), want);
+    if (tid < P && tid != r &&
+        !waitFlag(comm, flagPtr(me, tsAgFlagAt(L, c, tid)), want,
+                  whereCode(kCounterTwoShot, c, 2)))
+      sFail = 1;
+    __syncthreads();
+    if (sFail) break;
+    // 3. copy every peer's reduced chunk out.
+    for (int k = 1; k < P; ++k) {
+      const int j = (r + P - k) % P;
+      const Span sp = chunkSpan(pl, tile, j, V);
+      T* dst = y + sp.offset;
+      copyOut<T, kLdMailbox, 4>(reinterpret_cast<const T*>(me + tsAgDataAt(L, c, j)), sp.count,
+                                vec, false, 1.f, 1, [dst](int) { return dst; });
+    }
+    ++seq;
+  }
+  if (tid == 0 && !sFail) comm.counters[kCounterTwoShot * kMaxChannels + c] = seq;
+}
+
+// ---------------------------------------------------------------------------
+// One-shot: osSlots slots per channel; consumers acknowledge each slot so the
+// producer never overwrites a block that a peer has not reduced yet.
+// ---------------------------------------------------------------------------
+template <typename T, int MAXP>
+__global__ void __launch_bounds__(kMaxThreads)
+    oneShotKernel(const __grid_constant__ DevComm comm, const __grid_constant__ AllReduceArgs a) {
+  constexpr int V = Pack<T>::V;
+  constexpr int U = 1;
+  const int c = blockIdx.x, tid = threadIdx.x, P = comm.nranks, r = comm.rank;
+  const MailboxLayout& L = comm.layout;
+  const int S = L.osSlots;
+  char* const me = comm.peers[r];
+  const T* x = static_cast<const T*>(a.send);
+  T* y = static_cast<T*>(a.recv);
+  const BlockPlan& pl = a.block;
+  const bool vec = a.vectorized != 0;
+  __shared__ int sFail;
+  if (tid == 0) sFail = 0;
+  uint64_t seq = comm.counters[kCounterOneShot * kMaxChannels + c];
+  __syncthreads();
+  const uint64_t ntiles = channelTiles(pl.numTiles, pl.channels, c);
+  for (uint64_t t = 0; t < ntiles; ++t) {
+    const uint64_t tile = (uint64_t)c + t * (uint64_t)pl.channels;
+    const Span sp = blockTileSpan(pl, tile);
+    const int s = (int)(seq % (uint64_t)S);
+    const uint64_t want = seq + 1;
+    // The slot is free once every consumer acknowledged its previous use.
+    if (seq >= (uint64_t)S && tid < P && tid != r &&
+        !waitFlag(comm, flagPtr(me, osAckAt(L, c, s, tid)), seq - (uint64_t)S + 1,
+                  whereCode(kCounterOneShot, c, 0)))
+      sFail = 1;
+    __syncthreads();
+    if (sFail) break;
+    const uint64_t dataOff = osDataAt(L, c, s, r);
+    copyOut<T, kLdInput, 4>(x + sp.offset, sp.count, vec, false, 1.f, P - 1, [&](int d) {
+      return comm.peers[(r + 1 + d) % P] + dataOff;
+    });
+    __syncthreads();
+    if (tid < P && tid != r) stReleaseSys(flagPtr(comm.peers[tid], osFlagAt(L, c, s, r)), want);
+    if (tid < P && tid != r &&
+        !waitFlag(comm, flagPtr(me, osFlagAt(L, c, s, tid)), want,
+                  whereCode(kCounterOneShot, c, 1)))
+      sFail = 1;
+    __syncthreads();
+    if (sFail) break;
+    reduceRanks<T, MAXP, U>(
+        sp.count, vec, P, r, x + sp.offset, a.scale,
+        [&](int k) { return me + osDataAt(L, c, s, k); },
+        [&](uint64_t i, uint4 v) { st16(reinterpret_cast<uint4*>(y + sp.offset) + i, v); },
+        [&](uint64_t e, float f) { stElem(y + sp.offset + e, f); });
+    __syncthreads();  // every read of slot s is done
+    if (tid < P && tid != r) stReleaseSys(flagPtr(comm.peers[tid], osAckAt(L, c, s, r)), want);
+    ++seq;
+  }
+  if (tid == 0 && !sFail) comm.counters[kCounterOneShot * kMaxChannels + c] = seq;
+}
+
+// ---------------------------------------------------------------------------
+// Ring (per-channel FIFO with ready words in the consumer and credit words in
+// the producer, both polled locally).
+// ---------------------------------------------------------------------------
+template <typename T>
+struct RingChannel {
+  const DevComm* comm;
+  int c, S, next, prev;
+  char* me;
+  uint64_t sendT, recvT;
+
+  __device__ char* outSlot(uint64_t t) const {
+    return comm->peers[next] + ringDataAt(comm->layout, c, (int)(t % (uint64_t)S));
+  }
+  __device__ const T* inSlot(uint64_t t) const {
+    return reinterpret_cast<const T*>(me + ringDataAt(comm->layout, c, (int)(t % (uint64_t)S)));
+  }
+  // Thread 0 waits; the caller passes bar.sync before using the slots.
+  __device__ bool waitSend(int phase) const {
+    return waitFlag(*comm, flagPtr(me, ringCreditAt(comm->layout, c, (int)(sendT % (uint64_t)S))),
+                    sendT, whereCode(kCounterRing, c, phase));
+  }
+  __device__ bool waitRecv(int phase) const {
+    return waitFlag(*comm, flagPtr(me, ringReadyAt(comm->layout, c, (int)(recvT % (uint64_t)S))),
+                    recvT + 1, whereCode(kCounterRing, c, phase));
+  }
+  // Called by thread 0 after bar.sync.
+  __device__ void publishSend() {
+    stReleaseSys(flagPtr(comm->peers[next], ringReadyAt(comm->layout, c, (int)(sendT % (uint64_t)S))),
+                 sendT + 1);
+    ++sendT;
+  }
+  __device__ void releaseRecv() {
+    stReleaseSys(flagPtr(comm->peers[prev], ringCreditAt(comm->layout, c, (int)(recvT % (uint64_t)S))),
+                 recvT + (uint64_t)S);
+    ++recvT;
+  }
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kMaxThreads)
+    ringKernel(const __grid_constant__ DevComm comm, const __grid_constant__ AllReduceArgs a) {
+  using Pk = Pack<T>;
+  constexpr int V = Pk::V;
+  const int c = blockIdx.x, tid = threadIdx.x, P = comm.nranks, r = comm.rank;
+  const T* x = static_cast<const T*>(a.send);
+  T* y = static_cast<T*>(a.recv);
+  const ChunkPlan& pl = a.chunk;
+  const bool vec = a.vectorized != 0;
+  const float alpha = a.scale;
+  const bool scale = alpha != 1.0f;
+  __shared__ int sFail;
+  if (tid == 0) sFail = 0;
+  RingChannel<T> ch;
+  ch.comm = &comm;
+  ch.c = c;
+  ch.S = comm.layout.ringSlots;
+  ch.next = (r + 1) % P;
+  ch.prev = (r + P - 1) % P;
+  ch.me = comm.peers[r];
+  ch.sendT = ch.recvT = comm.counters[kCounterRing * kMaxChannels + c];
+  __syncthreads();
+
+  // Wait helpers: `needRecv` / `needSend` select which FIFO ends to acquire.
+  auto acquire = [&](bool needRecv, bool needSend, int phase) -> bool {
+    if (tid == 0) {
+      bool ok = true;
+      if (needRecv) ok = ch.waitRecv(phase);
+      if (ok && needSend) ok = ch.waitSend(phase);
+      if (!ok) sFail = 1;
+    }
+    __syncthreads();
+    return sFail == 0;
+  };
+  auto finish = [&](bool recvDone, bool sendDone) {
+    __syncthreads();
+    if (tid == 0) {
+      if (recvDone) ch.releaseRecv();
+      if (sendDone) ch.publishSend();
+    } else {
+      if (recvDone) ++ch.recvT;
+      if (sendDone) ++ch.sendT;
+    }
+  };
+
+  const uint64_t ntiles = channelTiles(pl.numTiles, pl.channels, c);
+  for (uint64_t t = 0; t < ntiles && !sFail; ++t) {
+    const uint64_t tile = (uint64_t)c + t * (uint64_t)pl.channels;
+    // Reduce-scatter: send chunk r-1.
+    {
+      const Span sp = chunkSpan(pl, tile, ringChunkBehind(r, 1, P), V);
+      if (!acquire(false, true, 1)) break;
+      char* out = ch.outSlot(ch.sendT);
+      copyOut<T, kLdInput, 4>(x + sp.offset, sp.count, vec, scale, alpha, 1,
+                              [out](int) { return out; });
+      finish(false, true);
+    }
+    // recv + reduce + send for distances 2..P-1.
+    bool ok = true;
+    for (int d = 2; d < P && ok; ++d) {
+      const Span sp = chunkSpan(pl, tile, ringChunkBehind(r, d, P), V);
+      if (!(ok = acquire(true, true, 2))) break;
+      const T* in = ch.inSlot(ch.recvT);
+      char* out = ch.outSlot(ch.sendT);
+      ringHop<T, 2>(
+          sp.count, vec, in, x + sp.offset, alpha,
+          [&](uint64_t i, uint4 v) { st16(reinterpret_cast<uint4*>(out) + i, v); },
+          [&](uint64_t e, float f) { stElem(reinterpret_cast<T*>(out) + e, f); });
+      finish(true, true);
+    }
+    if (!ok) break;
+    // Final reduce-scatter step: y[chunk r] = in + a*x, stored and forwarded.
+    {
+      const Span sp = chunkSpan(pl, tile, r, V);
+      if (!acquire(true, true, 3)) break;
+      const T* in = ch.inSlot(ch.recvT);
+      char* out = ch.outSlot(ch.sendT);
+      T* yo = y + sp.offset;
+      ringHop<T, 2>(
+          sp.count, vec, in, x + sp.offset, alpha,
+          [&](uint64_t i, uint4 v) {
+            st16(reinterpret_cast<uint4*>(yo) + i, v);
+            st16(reinterpret_cast<uint4*>(out) + i, v);
+          },
+          [&](uint64_t e, float f) {
+            stElem(yo + e, f);
+            stElem(reinterpret_cast<T*>(out) + e, f);
+          });
+      finish(true, true);
+    }
+    // All-gather: recv + store + forward for distances 1..P-2, then store.
+    for (int d = 1; d < P - 1 && ok; ++d) {
+      const Span sp = chunkSpan(pl, tile, ringChunkBehind(r, d, P), V);
+      if (!(ok = acquire(true, true, 4))) break;
+      const T* in = ch.inSlot(ch.recvT);
+      char* out = ch.outSlot(ch.sendT);
+      T* yo = y + sp.offset;
+      copyOut<T, kLdMailbox, 4>(in, sp.count, vec, false, 1.f, 2, [&](int k) {
+        return k == 0 ? reinterpret_cast<char*>(yo) : out;
+      });
+      finish(true, true);
+    }
+    if (!ok) break;
+    {
+      const Span sp = chunkSpan(pl, tile, ringChunkBehind(r, P - 1, P), V);
+      if (!acquire(true, false, 5)) break;
+      T* yo = y + sp.offset;
+      copyOut<T, kLdMailbox, 4>(ch.inSlot(ch.recvT), sp.count, vec, false, 1.f, 1,
+                                [yo](int) { return reinterpret_cast<char*>(yo); });
+      finish(true, false);
+    }
+  }
+  if (tid == 0 && !sFail) comm.counters[kCounterRing * kMaxChannels + c] = ch.sendT;
+}
+
+// ---------------------------------------------------------------------------
+// NVLS
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(kMaxThreads)
+    nvlsKernel(const __grid_constant__ DevComm comm, const __grid_constant__ AllReduceArgs a) {
+  using Pk = Pack<T>;
+  constexpr int V = Pk::V;
+  const int c = blockIdx.x, tid = threadIdx.x, P = comm.nranks, r = comm.rank;
+  const MailboxLayout& L = comm.layout;
+  char* const me = comm.peers[r];
+  const T* x = static_cast<const T*>(a.send);
+  T* y = static_cast<T*>(a.recv);
+  const BlockPlan& pl = a.block;
+  const bool vec = a.vectorized != 0;
+  const float alpha = a.scale;
+  const bool scale = alpha != 1.0f;
+  char* const ucIn = comm.nvlsUc + nvlsInAt(comm.nvlsTileBytes, c);
+  char* const ucOut = comm.nvlsUc + nvlsOutAt(comm.nvlsTileBytes, c);
+  char* const mcIn = comm.nvlsMc + nvlsInAt(comm.nvlsTileBytes, c);
+  char* const mcOut = comm.nvlsMc + nvlsOutAt(comm.nvlsTileBytes, c);
+  __shared__ int sFail;
+  if (tid == 0) sFail = 0;
+  uint64_t seq = comm.counters[kCounterNvls * kMaxChannels + c];
+  __syncthreads();
+
+  auto barrier = [&](int phase, uint64_t want) -> bool {
+    fenceProxyAlias();
+    __syncthreads();
+    if (tid < P && tid != r)
+      stReleaseSys(flagPtr(comm.peers[tid], nvlsFlagAt(L, phase, c, r)), want);
+    if (tid < P && tid != r &&
+        !waitFlag(comm, flagPtr(me, nvlsFlagAt(L, phase, c, tid)), want,
+                  whereCode(kCounterNvls, c, phase + 1)))
+      sFail = 1;
+    __syncthreads();
+    fenceProxyAlias();
+    return sFail == 0;
+  };
+
+  const uint64_t ntiles = channelTiles(pl.numTiles, pl.channels, c);
+  for (uint64_t t = 0; t < ntiles; ++t) {
+    const uint64_t tile = (uint64_t)c + t * (uint64_t)pl.channels;
+    const Span sp = blockTileSpan(pl, tile);
+    const uint64_t want = seq + 1;
+    copyOut<T, kLdInput, 4>(x + sp.offset, sp.count, vec, false, 1.f, 1,
+                            [ucIn](int) { return ucIn; });
+    if (!barrier(0, want)) break;
+    // Reduce this rank's share (whole vectors; padding past the tile end is
+    // reduced too but never copied out).
+    const uint64_t nvecTile = divUp(sp.count, V);
+    const Span share = blockShare(nvecTile, P, r, 1);
+    const uint64_t NT = blockDim.x;
+    for (uint64_t base = tid; base < share.count; base += NT * 2) {
+      uint4 v[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const uint64_t i = share.offset + base + u * NT;
+        if (base + u * NT < share.count) v[u] = Multimem<T>::ldReduce(mcIn + i * 16);
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const uint64_t i = share.offset + base + u * NT;
+        if (base + u * NT < share.count) {
+          uint4 w = v[u];
+          if (scale) {
+            float f[V];
+            Pk::unpack(w, f);
+#pragma unroll
+            for (int e = 0; e < V; ++e) f[e] = scaled(alpha, f[e]);
+            w = Pk::pack(f);
+          }
+          Multimem<T>::st(mcOut + i * 16, w);
+        }
+      }
+    }
+    if (!barrier(1, want)) break;
+    T* yo = y + sp.offset;
+    copyOut<T, kLdMailbox, 4>(reinterpret_cast<const T*>(ucOut), sp.count, vec, false, 1.f, 1,
+                              [yo](int) { return reinterpret_cast<char*>(yo); });
+    ++seq;
+  }
+  if (tid == 0 && !sFail) comm.counters[kCounterNvls * kMaxChannels + c] = seq;
+}
+
+// ---------------------------------------------------------------------------
+// Single rank: y = alpha * x (identity copy when alpha == 1 is done with
+// cudaMemcpyAsync by the host).
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(kMaxThreads)
+    scaleKernel(const T* __restrict__ x, T* y, uint64_t n, float alpha, int vectorized) {
+  using Pk = Pack<T>;
+  constexpr int V = Pk::V;
+  const uint64_t nvec = vectorized ? n / V : 0;
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride) {
+    float f[V];
+    Pk::unpack(ldInput(reinterpret_cast<const uint4*>(x) + i), f);
+#pragma unroll
+    for (int e = 0; e < V; ++e) f[e] = scaled(alpha, f[e]);
+    st16(reinterpret_cast<uint4*>(y) + i, Pk::pack(f));
+  }
+  for (uint64_t e = nvec * V + (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n;
+       e += stride)
+    stElem(y + e, scaled(alpha, ldElem<T, kLdInput>(x + e)));
+}
+
+template <typename T>
+cudaError_t launchTyped(const DevComm& comm, const AllReduceArgs& a, int algo, int threads,
+                        cudaStream_t stream) {
+  const dim3 block((unsigned)threads);
+  switch (algo) {
+    case TNCCL_ALGO_RING:
+      ringKernel<T><<<a.chunk.channels, block, 0, stream>>>(comm, a);
+      break;
+    case TNCCL_ALGO_TWOSHOT:
+      if (comm.nranks <= 8)
+        twoShotKernel<T, 8><<<a.chunk.channels, block, 0, stream>>>(comm, a);
+      else
+        twoShotKernel<T, 16><<<a.chunk.channels, block, 0, stream>>>(comm, a);
+      break;
+    case TNCCL_ALGO_ONESHOT:
+      if (comm.nranks <= 8)
+        oneShotKernel<T, 8><<<a.block.channels, block, 0, stream>>>(comm, a);
+      else
+        oneShotKernel<T, 16><<<a.block.channels, block, 0, stream>>>(comm, a);
+      break;
+    case TNCCL_ALGO_NVLS:
+      nvlsKernel<T><<<a.block.channels, block, 0, stream>>>(comm, a);
+      break;
+    default:
+      return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launchScaleTyped(const void* x, void* y, uint64_t n, float alpha, int vectorized,
+                             cudaStream_t stream) {
+  const uint64_t work = vectorized ? n / Pack<T>::V + 1 : n;
+  unsigned blocks = (unsigned)minU64(divUp(work, 256), 148ull * 8);
+  if (blocks == 0) blocks = 1;
+  scaleKernel<T><<<blocks, 256, 0, stream>>>(static_cast<const T*>(x), static_cast<T*>(y), n,
+                                             alpha, vectorized);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launchAllReduceKernel(const DevComm& comm, const AllReduceArgs& a, int algo,
+                                  int threads, cudaStream_t stream) {
+  if (threads > kMaxThreads) threads = kMaxThreads;
+  switch (a.dtype) {
+    case kF32:
+      return launchTyped<float>(comm, a, algo, threads, stream);
+    case kBF16:
+      return launchTyped<__nv_bfloat16>(comm, a, algo, threads, stream);
+    case kF16:
+      return launchTyped<__half>(comm, a, algo, threads, stream);
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launchScale(const void* x, void* y, uint64_t n, int dtype, float alpha,
+                        int vectorized, cudaStream_t stream) {
+  switch (dtype) {
+    case kF32:
+      return launchScaleTyped<float>(x, y, n, alpha, vectorized, stream);
+    case kBF16:
+      return launchScaleTyped<__nv_bfloat16>(x, y, n, alpha, vectorized, stream);
+    case kF16:
+      return launchScaleTyped<__half>(x, y, n, alpha, vectorized, stream);
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace tnccl

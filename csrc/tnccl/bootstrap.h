@@ -1,0 +1,68 @@
+// bootstrap.h - host control plane: unique id, AF_UNIX star rendezvous,
+// all-gather, barrier and file-descriptor passing.
+//
+// Behaviour kept from tiny-nccl (src/bootstrap.cc): the unique id names a
+// Unix-socket path; rank 0 binds it (mode 0600), accepts nranks-1 peers and
+// validates their hello (matching nranks, rank in range, no duplicate); peers
+// retry connect until the deadline; every operation has a deadline; all-gather
+// is gather-to-root then broadcast; barrier is collect-then-release; rank 0
+// unlinks the path only if it bound it.
+//
+// Added here: every frame carries a per-communicator operation number so that
+// ranks that drift out of step fail with an error instead of mis-pairing
+// messages; the hello carries a configuration hash; SCM_RIGHTS passing of
+// POSIX file descriptors (cuMem / multicast handles) as an all-gather and a
+// broadcast from rank 0; deadline expiry returns TNCCL_TIMEOUT.
+#pragma once
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include <vector>
+
+#include "tnccl.h"
+
+namespace tnccl {
+
+// Largest rank count the bootstrap accepts (descriptor messages carry one
+// descriptor per rank).
+constexpr int kMaxRankFds = 64;
+
+struct Bootstrap {
+  int rank = -1;
+  int nranks = 0;
+  int listenFd = -1;
+  int hubFd = -1;             // non-root: connection to rank 0
+  std::vector<int> peerFds;   // root: connection to every rank (index = rank)
+  char path[108] = {};
+  bool ownsPath = false;
+  bool active = false;
+  uint32_t opSeq = 0;         // bootstrap collectives issued so far
+  int timeoutMs = 30000;
+};
+
+// Encodes a fresh rendezvous path into id (random 128-bit suffix).
+tncclResult bootstrapNewId(tncclUniqueId* id);
+
+// Validates id and returns the socket path it names.
+bool bootstrapDecodeId(const tncclUniqueId& id, char (&path)[108]);
+
+tncclResult bootstrapOpen(Bootstrap* b, const tncclUniqueId& id, int nranks,
+                          int rank, uint64_t configHash, int timeoutMs);
+tncclResult bootstrapAllGather(Bootstrap* b, const void* send, void* recv,
+                               size_t bytes);
+tncclResult bootstrapBarrier(Bootstrap* b);
+
+// Every rank contributes one descriptor (or -1 when it has none, which makes
+// the collective fail on every rank). On success fds[r] holds a descriptor
+// for rank r's object, owned by the caller (fds[rank] is a duplicate of the
+// caller's own descriptor).
+tncclResult bootstrapAllGatherFds(Bootstrap* b, int myFd, int* fds);
+
+// Rank 0 passes fd (or -1 to signal failure); every other rank receives a
+// duplicate in *out (owned by the caller).
+tncclResult bootstrapBroadcastFd(Bootstrap* b, int fd, int* out);
+
+void bootstrapClose(Bootstrap* b);
+
+}  // namespace tnccl

@@ -1,0 +1,346 @@
+// comm.cc - communicator init (blocking collective) and two-phase destroy.
+//
+// Same contract as tiny-nccl src/comm.cc:118-290: capture the current device;
+// nranks == 1 needs no bootstrap; statuses are all-gathered so that every
+// rank sees a peer's failure; a failed init closes its imports, passes a
+// cleanup barrier and only then frees its export; destroy synchronizes the
+// bound stream, passes barrier #1 (all kernels done), closes every import,
+// passes barrier #2 (all importers closed) and only then frees; destroy always
+// consumes the handle and retains exported memory when teardown cannot be
+// proven safe.
+//
+// Differences: every peer (not only the next rank) is mapped and checked for
+// P2P access and native peer atomics; devices are compared by UUID rather
+// than by per-process ordinal; an NVLS multicast object is created when every
+// rank supports it; the host-mapped status block and the device-resident FIFO
+// counters are allocated here.
+#include <string.h>
+#include <unistd.h>
+
+#include <memory>
+#include <new>
+#include <vector>
+
+#include "comm.h"
+#include "driver.h"
+
+namespace tnccl {
+namespace {
+
+tncclResult firstFailure(const std::vector<PeerMeta>& metas) {
+  for (const PeerMeta& m : metas) {
+    if (m.status < TNCCL_SUCCESS || m.status >= TNCCL_NUM_RESULTS) return TNCCL_SYSTEM_ERROR;
+    if (m.status != TNCCL_SUCCESS) return (tncclResult)m.status;
+  }
+  return TNCCL_SUCCESS;
+}
+
+bool devicesUnique(const std::vector<PeerMeta>& metas) {
+  for (size_t i = 0; i < metas.size(); ++i)
+    for (size_t j = 0; j < i; ++j)
+      if (memcmp(metas[i].uuid, metas[j].uuid, sizeof(metas[i].uuid)) == 0) return false;
+  return true;
+}
+
+// Checks P2P reachability and native atomics to a peer whose device is
+// visible in this process. A peer hidden by CUDA_VISIBLE_DEVICES cannot be
+// queried; its mapping is then validated by cuMemSetAccess during import.
+tncclResult checkPeer(const tncclComm* comm, const PeerMeta& m) {
+  int peerDev = -1;
+  if (cudaDeviceGetByPCIBusId(&peerDev, m.busId) != cudaSuccess) {
+    (void)cudaGetLastError();
+    TN_INFO("rank %d: peer device %s not visible; skipping P2P attribute query",
+            comm->rank, m.busId);
+    return TNCCL_SUCCESS;
+  }
+  if (peerDev == comm->device) return TNCCL_UNSUPPORTED;
+  int can = 0, atomics = 0;
+  if (cudaDeviceCanAccessPeer(&can, comm->device, peerDev) != cudaSuccess) return TNCCL_CUDA_ERROR;
+  if (!can) {
+    TN_WARN("rank %d: no P2P access from device %d to %d", comm->rank, comm->device, peerDev);
+    return TNCCL_UNSUPPORTED;
+  }
+  if (cudaDeviceGetP2PAttribute(&atomics, cudaDevP2PAttrNativeAtomicSupported, comm->device,
+                                peerDev) != cudaSuccess)
+    return TNCCL_CUDA_ERROR;
+  if (!atomics) {
+    TN_WARN("rank %d: no native peer atomics from device %d to %d", comm->rank, comm->device,
+            peerDev);
+    return TNCCL_UNSUPPORTED;
+  }
+  return TNCCL_SUCCESS;
+}
+
+// Initial FIFO state: zero everywhere except the ring credits, which start
+// at the slot index (slot s may carry ticket s first).
+tncclResult initMailboxContents(tncclComm* comm) {
+  const MailboxLayout& L = comm->layout;
+  if (cudaMemset(comm->local.base, 0, comm->local.bytes) != cudaSuccess) return TNCCL_CUDA_ERROR;
+  std::vector<uint64_t> credits((size_t)L.channels * (size_t)L.ringSlots);
+  for (int c = 0; c < L.channels; ++c)
+    for (int s = 0; s < L.ringSlots; ++s) credits[(size_t)c * L.ringSlots + s] = (uint64_t)s;
+  if (cudaMemcpy(comm->local.base + L.ringCreditOff, credits.data(),
+                 credits.size() * sizeof(uint64_t), cudaMemcpyHostToDevice) != cudaSuccess)
+    return TNCCL_CUDA_ERROR;
+  return cudaDeviceSynchronize() == cudaSuccess ? TNCCL_SUCCESS : TNCCL_CUDA_ERROR;
+}
+
+tncclResult allocDeviceState(tncclComm* comm) {
+  void* h = nullptr;
+  if (cudaHostAlloc(&h, sizeof(DevStatus), cudaHostAllocMapped | cudaHostAllocPortable) !=
+      cudaSuccess)
+    return TNCCL_CUDA_ERROR;
+  memset(h, 0, sizeof(DevStatus));
+  comm->hostStatus = static_cast<DevStatus*>(h);
+  void* d = nullptr;
+  if (cudaHostGetDevicePointer(&d, h, 0) != cudaSuccess) return TNCCL_CUDA_ERROR;
+  comm->devStatus = static_cast<DevStatus*>(d);
+  const size_t cbytes = sizeof(uint64_t) * kNumCounterFamilies * kMaxChannels;
+  if (cudaMalloc(reinterpret_cast<void**>(&comm->counters), cbytes) != cudaSuccess)
+    return TNCCL_CUDA_ERROR;
+  if (cudaMemset(comm->counters, 0, cbytes) != cudaSuccess) return TNCCL_CUDA_ERROR;
+  return TNCCL_SUCCESS;
+}
+
+void freeDeviceState(tncclComm* comm) {
+  if (comm->counters) cudaFree(comm->counters);
+  comm->counters = nullptr;
+  if (comm->hostStatus) cudaFreeHost(comm->hostStatus);
+  comm->hostStatus = nullptr;
+  comm->devStatus = nullptr;
+}
+
+void fillDevComm(tncclComm* comm) {
+  DevComm& d = comm->dev;
+  d.rank = comm->rank;
+  d.nranks = comm->nranks;
+  d.layout = comm->layout;
+  for (int r = 0; r < kMaxRanks; ++r) d.peers[r] = nullptr;
+  for (int r = 0; r < comm->nranks; ++r)
+    d.peers[r] = r == comm->rank ? comm->local.base : comm->peers[r].base;
+  d.counters = comm->counters;
+  d.status = comm->devStatus;
+  d.timeoutNs = (uint64_t)comm->cfg.timeoutMs * 1000000ull;
+  d.nvlsEnabled = comm->nvls.enabled ? 1 : 0;
+  d.nvlsChannels = comm->nvls.channels;
+  d.nvlsTileBytes = comm->nvls.tileBytes;
+  d.nvlsUc = reinterpret_cast<char*>(comm->nvls.ucVa);
+  d.nvlsMc = reinterpret_cast<char*>(comm->nvls.mcVa);
+}
+
+void deriveThresholds(tncclComm* comm) {
+  const int P = comm->nranks;
+  // Defaults from the measured sweep on 8x B200 (benchmarks/allreduce_sweep.py);
+  // TNCCL_ONESHOT_MAX_BYTES / TNCCL_NVLS_MIN_BYTES override them.
+  uint64_t os = P <= 2 ? (512u << 10) : P <= 4 ? (256u << 10) : (128u << 10);
+  uint64_t nv = P <= 2 ? (64ull << 20) : (4ull << 20);
+  if (comm->cfg.oneShotMaxBytes > 0) os = (uint64_t)comm->cfg.oneShotMaxBytes;
+  if (comm->cfg.nvlsMinBytes > 0) nv = (uint64_t)comm->cfg.nvlsMinBytes;
+  comm->oneShotMaxBytes = os;
+  comm->nvlsMinBytes = nv;
+}
+
+// Gives up on a communicator whose export may already be mapped by peers:
+// close our imports and the control connection, keep the export alive.
+void abandonPublished(tncclComm* comm) {
+  tncclResult ignored = TNCCL_SUCCESS;
+  closePeerMailboxes(comm, &ignored);
+  bootstrapClose(&comm->bootstrap);
+}
+
+}  // namespace
+}  // namespace tnccl
+
+using namespace tnccl;
+
+extern "C" tncclResult tncclCommInitRank(tncclComm_t* out, int nranks, tncclUniqueId id,
+                                         int rank) {
+  if (out == nullptr || nranks <= 0 || rank < 0 || rank >= nranks) return TNCCL_INVALID_ARGUMENT;
+  *out = nullptr;
+  if (nranks > kMaxRanks) return TNCCL_UNSUPPORTED;
+  std::unique_ptr<tncclComm> comm(new (std::nothrow) tncclComm);
+  if (!comm) return TNCCL_SYSTEM_ERROR;
+  comm->rank = rank;
+  comm->nranks = nranks;
+  comm->cfg = loadConfig();
+  if (cudaGetDevice(&comm->device) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return TNCCL_CUDA_ERROR;
+  }
+  deriveThresholds(comm.get());
+  if (tncclResult r = allocDeviceState(comm.get()); r != TNCCL_SUCCESS) {
+    freeDeviceState(comm.get());
+    return r;
+  }
+  if (nranks == 1) {
+    fillDevComm(comm.get());
+    *out = comm.release();
+    return TNCCL_SUCCESS;
+  }
+  const DriverApi* api = driverApi();
+  if (api) api->cuDeviceGet(&comm->cuDevice, comm->device);
+
+  tncclResult r = bootstrapOpen(&comm->bootstrap, id, nranks, rank, configHash(comm->cfg),
+                                (int)comm->cfg.bootstrapTimeoutMs);
+  if (r != TNCCL_SUCCESS) {
+    freeDeviceState(comm.get());
+    return r;
+  }
+
+  LayoutConfig lc{};
+  lc.nranks = nranks;
+  lc.channels = comm->cfg.channels;
+  lc.osChannels = comm->cfg.osChannels;
+  lc.ringSlots = comm->cfg.ringSlots;
+  lc.ringChunkBytes = (uint64_t)comm->cfg.ringChunkBytes;
+  lc.tsChunkBytes = (uint64_t)comm->cfg.tsChunkBytes;
+  lc.osSlots = comm->cfg.osSlots;
+  lc.osTileBytes = (uint64_t)comm->cfg.osTileBytes;
+  lc.nvlsChannels = comm->cfg.nvlsChannels;
+  comm->layout = makeLayout(lc);
+
+  PeerMeta me{};
+  me.device = comm->device;
+  cudaDeviceProp prop{};
+  if (cudaGetDeviceProperties(&prop, comm->device) == cudaSuccess) {
+    memcpy(me.uuid, &prop.uuid, sizeof(me.uuid));
+  } else {
+    me.status = TNCCL_CUDA_ERROR;
+  }
+  if (cudaDeviceGetPCIBusId(me.busId, sizeof(me.busId), comm->device) != cudaSuccess)
+    me.status = TNCCL_CUDA_ERROR;
+  if (me.status == TNCCL_SUCCESS)
+    me.status = allocLocalMailbox(comm.get(), comm->layout.totalBytes, comm->cfg.useCuMem != 0);
+  if (me.status == TNCCL_SUCCESS) me.status = initMailboxContents(comm.get());
+  me.ipcMode = comm->ipcMode;
+  me.mailboxBytes = comm->local.bytes;
+  me.ipcHandle = comm->local.ipcHandle;
+  me.nvlsCapable = me.status == TNCCL_SUCCESS && nvlsLocallyCapable(comm.get()) ? 1 : 0;
+
+  std::vector<PeerMeta> metas((size_t)nranks);
+  r = bootstrapAllGather(&comm->bootstrap, &me, metas.data(), sizeof(me));
+  if (r != TNCCL_SUCCESS) {
+    abandonPublished(comm.get());
+    return r;
+  }
+  tncclResult status = firstFailure(metas);
+  if (status == TNCCL_SUCCESS && !devicesUnique(metas)) status = TNCCL_UNSUPPORTED;
+  for (const PeerMeta& m : metas)
+    if (status == TNCCL_SUCCESS && m.ipcMode != metas[0].ipcMode) status = TNCCL_UNSUPPORTED;
+  for (int p = 0; p < nranks && status == TNCCL_SUCCESS; ++p)
+    if (p != rank) status = checkPeer(comm.get(), metas[(size_t)p]);
+
+  // Every rank takes part in the descriptor all-gather (cuMem mode) even
+  // after a local failure, so the collective sequence stays aligned.
+  std::vector<int> fds((size_t)nranks, -1);
+  bool allCuMem = true;
+  for (const PeerMeta& m : metas) allCuMem = allCuMem && m.ipcMode == kIpcCuMem;
+  if (allCuMem && firstFailure(metas) == TNCCL_SUCCESS) {
+    r = bootstrapAllGatherFds(&comm->bootstrap, comm->local.exportFd, fds.data());
+    if (r != TNCCL_SUCCESS) {
+      abandonPublished(comm.get());
+      return r;
+    }
+  }
+  for (int p = 0; p < nranks && status == TNCCL_SUCCESS; ++p) {
+    if (p == rank) continue;
+    status = importPeerMailbox(comm.get(), p, fds[(size_t)p], metas[(size_t)p]);
+  }
+  for (int fd : fds)
+    if (fd >= 0) close(fd);
+
+  // Connection status round, then the ready barrier (tiny-nccl
+  // src/comm.cc:173-196).
+  PeerMeta conn{};
+  conn.status = status;
+  std::vector<PeerMeta> conns((size_t)nranks);
+  r = bootstrapAllGather(&comm->bootstrap, &conn, conns.data(), sizeof(conn));
+  if (r != TNCCL_SUCCESS) {
+    abandonPublished(comm.get());
+    return r;
+  }
+  status = firstFailure(conns);
+
+  // NVLS only when every rank is connected and capable.
+  bool allNvls = status == TNCCL_SUCCESS;
+  for (const PeerMeta& m : metas) allNvls = allNvls && m.nvlsCapable;
+  if (allNvls) {
+    r = setupNvls(comm.get());
+    if (r != TNCCL_SUCCESS && r != TNCCL_UNSUPPORTED) {
+      abandonPublished(comm.get());
+      return r;
+    }
+    if (r == TNCCL_UNSUPPORTED) TN_INFO("rank %d: NVLS unavailable; using P2P algorithms", rank);
+  }
+
+  r = bootstrapBarrier(&comm->bootstrap);
+  if (r != TNCCL_SUCCESS) {
+    abandonPublished(comm.get());
+    return r;
+  }
+  if (status != TNCCL_SUCCESS) {
+    tncclResult ignored = TNCCL_SUCCESS;
+    nvlsUnmap(comm.get(), &ignored);
+    closePeerMailboxes(comm.get(), &ignored);
+    tncclResult cleanup = bootstrapBarrier(&comm->bootstrap);
+    if (cleanup == TNCCL_SUCCESS) {
+      nvlsRelease(comm.get(), &ignored);
+      freeLocalMailbox(comm.get(), &ignored);
+      freeDeviceState(comm.get());
+    }
+    bootstrapClose(&comm->bootstrap);
+    return cleanup == TNCCL_SUCCESS ? status : cleanup;
+  }
+  fillDevComm(comm.get());
+  TN_INFO("rank %d/%d: device %d, ipc %s, mailbox %zu bytes, NVLS %s", rank, nranks,
+          comm->device, comm->ipcMode == kIpcCuMem ? "cuMem" : "legacy", comm->local.bytes,
+          comm->nvls.enabled ? "on" : "off");
+  *out = comm.release();
+  return TNCCL_SUCCESS;
+}
+
+extern "C" tncclResult tncclCommDestroy(tncclComm_t comm) {
+  if (comm == nullptr) return TNCCL_INVALID_ARGUMENT;
+  int original = -1;
+  if (cudaGetDevice(&original) != cudaSuccess) {
+    bootstrapClose(&comm->bootstrap);
+    delete comm;
+    return TNCCL_CUDA_ERROR;
+  }
+  if (original != comm->device && cudaSetDevice(comm->device) != cudaSuccess) {
+    bootstrapClose(&comm->bootstrap);
+    delete comm;
+    return TNCCL_CUDA_ERROR;
+  }
+  tncclResult result = TNCCL_SUCCESS;
+  if (comm->streamBound && cudaStreamSynchronize(comm->boundStream) != cudaSuccess) {
+    // A kernel may still own the mappings: break the control connection so
+    // peers take their bounded error paths; retain device memory.
+    bootstrapClose(&comm->bootstrap);
+    delete comm;
+    return TNCCL_CUDA_ERROR;
+  }
+  if (comm->nranks == 1) {
+    freeDeviceState(comm);
+    if (original != comm->device) cudaSetDevice(original);
+    delete comm;
+    return TNCCL_SUCCESS;
+  }
+  tncclResult b1 = bootstrapBarrier(&comm->bootstrap);  // every kernel has finished
+  if (b1 != TNCCL_SUCCESS) result = b1;
+  nvlsUnmap(comm, &result);
+  closePeerMailboxes(comm, &result);
+  tncclResult b2 = bootstrapBarrier(&comm->bootstrap);  // every importer has closed
+  if (b2 != TNCCL_SUCCESS && result == TNCCL_SUCCESS) result = b2;
+  if (b1 == TNCCL_SUCCESS && b2 == TNCCL_SUCCESS) {
+    nvlsRelease(comm, &result);
+    freeLocalMailbox(comm, &result);
+    freeDeviceState(comm);
+  }
+  bootstrapClose(&comm->bootstrap);
+  if (original != comm->device && cudaSetDevice(original) != cudaSuccess &&
+      result == TNCCL_SUCCESS)
+    result = TNCCL_CUDA_ERROR;
+  delete comm;
+  return result;
+}

@@ -1,0 +1,124 @@
+#include "common.h"
+
+#include <string.h>
+#include <strings.h>
+#include <unistd.h>
+
+#include <mutex>
+
+namespace tnccl {
+
+int logLevel() {
+  static int level = [] {
+    const char* v = getenv("TNCCL_DEBUG");
+    if (v == nullptr) return (int)kLogWarn;
+    if (strcasecmp(v, "NONE") == 0) return (int)kLogNone;
+    if (strcasecmp(v, "INFO") == 0) return (int)kLogInfo;
+    if (strcasecmp(v, "TRACE") == 0) return (int)kLogTrace;
+    return (int)kLogWarn;
+  }();
+  return level;
+}
+
+void logf(int level, const char* fmt, ...) {
+  if (level > logLevel()) return;
+  static std::mutex mu;
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  const char* tag = level == kLogWarn ? "WARN" : level == kLogInfo ? "INFO" : "TRACE";
+  std::lock_guard<std::mutex> lock(mu);
+  fprintf(stderr, "[tnccl pid %d] %s %s\n", (int)getpid(), tag, buf);
+}
+
+int64_t envInt(const char* name, int64_t dflt) {
+  const char* v = getenv(name);
+  if (v == nullptr || *v == '\0') return dflt;
+  char* end = nullptr;
+  long long x = strtoll(v, &end, 0);
+  if (end == v || (end && *end != '\0')) {
+    TN_WARN("ignoring malformed %s=%s", name, v);
+    return dflt;
+  }
+  return (int64_t)x;
+}
+
+std::string envStr(const char* name, const char* dflt) {
+  const char* v = getenv(name);
+  return (v == nullptr || *v == '\0') ? std::string(dflt) : std::string(v);
+}
+
+int parseAlgo(const std::string& s) {
+  if (s.empty() || strcasecmp(s.c_str(), "auto") == 0) return TNCCL_ALGO_AUTO;
+  if (strcasecmp(s.c_str(), "ring") == 0) return TNCCL_ALGO_RING;
+  if (strcasecmp(s.c_str(), "oneshot") == 0) return TNCCL_ALGO_ONESHOT;
+  if (strcasecmp(s.c_str(), "twoshot") == 0) return TNCCL_ALGO_TWOSHOT;
+  if (strcasecmp(s.c_str(), "nvls") == 0) return TNCCL_ALGO_NVLS;
+  return -1;
+}
+
+static int clampInt(int64_t v, int lo, int hi) {
+  return (int)(v < lo ? lo : v > hi ? hi : v);
+}
+
+static int64_t roundTo16(int64_t v) { return v < 16 ? 16 : (v + 15) / 16 * 16; }
+
+Config loadConfig() {
+  Config c{};
+  c.channels = clampInt(envInt("TNCCL_NCHANNELS", 32), 1, 64);
+  c.osChannels = clampInt(envInt("TNCCL_ONESHOT_CHANNELS", 16), 1, 64);
+  c.ringSlots = clampInt(envInt("TNCCL_SLOTS", 4), 2, 16);
+  c.ringChunkBytes = roundTo16(envInt("TNCCL_CHUNK_BYTES", 64 << 10));
+  c.tsChunkBytes = roundTo16(envInt("TNCCL_TWOSHOT_CHUNK_BYTES", 32 << 10));
+  c.osSlots = clampInt(envInt("TNCCL_ONESHOT_SLOTS", 2), 1, 8);
+  c.osTileBytes = roundTo16(envInt("TNCCL_ONESHOT_TILE_BYTES", 32 << 10));
+  c.nvlsChannels = clampInt(envInt("TNCCL_NVLS_CHANNELS", 32), 1, 64);
+  c.nvlsTileBytes = roundTo16(envInt("TNCCL_NVLS_TILE_BYTES", 128 << 10));
+  c.nvlsEnable = (int)envInt("TNCCL_NVLS_ENABLE", 1);
+  int algo = parseAlgo(envStr("TNCCL_ALGO", "auto"));
+  if (algo < 0) {
+    TN_WARN("unknown TNCCL_ALGO; using auto");
+    algo = TNCCL_ALGO_AUTO;
+  }
+  c.forcedAlgo = algo;
+  c.timeoutMs = envInt("TNCCL_TIMEOUT_MS", 30000);
+  if (c.timeoutMs < 1) c.timeoutMs = 1;
+  c.bootstrapTimeoutMs = envInt("TNCCL_BOOTSTRAP_TIMEOUT_MS", 30000);
+  if (c.bootstrapTimeoutMs < 1) c.bootstrapTimeoutMs = 1;
+  c.threads = clampInt(envInt("TNCCL_NTHREADS", 512), 64, 1024) / 32 * 32;
+  c.useCuMem = (int)envInt("TNCCL_CUMEM_ENABLE", 1);
+  c.oneShotMaxBytes = envInt("TNCCL_ONESHOT_MAX_BYTES", 0);
+  c.nvlsMinBytes = envInt("TNCCL_NVLS_MIN_BYTES", 0);
+  return c;
+}
+
+uint64_t configHash(const Config& c) {
+  // FNV-1a over the fields that change the device protocol or the mailbox
+  // layout. Timeouts and thread counts may differ across ranks.
+  uint64_t h = 1469598103934665603ull;
+  auto mix = [&h](int64_t v) {
+    for (int i = 0; i < 8; ++i) {
+      h ^= (uint64_t)((v >> (8 * i)) & 0xff);
+      h *= 1099511628211ull;
+    }
+  };
+  mix(c.channels);
+  mix(c.osChannels);
+  mix(c.ringSlots);
+  mix(c.ringChunkBytes);
+  mix(c.tsChunkBytes);
+  mix(c.osSlots);
+  mix(c.osTileBytes);
+  mix(c.nvlsChannels);
+  mix(c.nvlsTileBytes);
+  mix(c.nvlsEnable);
+  mix(c.forcedAlgo);
+  mix(c.useCuMem);
+  mix(c.oneShotMaxBytes);
+  mix(c.nvlsMinBytes);
+  return h;
+}
+
+}  // namespace tnccl

@@ -1,0 +1,58 @@
+// common.h - logging, environment configuration and small helpers for the
+// host side of the library.
+#pragma once
+
+#include <stdarg.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdlib.h>
+
+#include <string>
+
+#include "tnccl.h"
+
+namespace tnccl {
+
+// TNCCL_DEBUG=WARN|INFO|TRACE selects host log verbosity (default: WARN).
+enum LogLevel { kLogNone = 0, kLogWarn = 1, kLogInfo = 2, kLogTrace = 3 };
+int logLevel();
+void logf(int level, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+
+#define TN_WARN(...) ::tnccl::logf(::tnccl::kLogWarn, __VA_ARGS__)
+#define TN_INFO(...) ::tnccl::logf(::tnccl::kLogInfo, __VA_ARGS__)
+#define TN_TRACE(...) ::tnccl::logf(::tnccl::kLogTrace, __VA_ARGS__)
+
+// Integer environment variable with a default; malformed values fall back to
+// the default with a warning.
+int64_t envInt(const char* name, int64_t dflt);
+std::string envStr(const char* name, const char* dflt);
+
+// Tunables read once per communicator. They must be equal on every rank; the
+// bootstrap hello carries their hash and rank 0 rejects a mismatch.
+struct Config {
+  int channels;          // TNCCL_NCHANNELS (ring / two-shot CTAs)
+  int osChannels;        // TNCCL_ONESHOT_CHANNELS
+  int ringSlots;         // TNCCL_SLOTS
+  int64_t ringChunkBytes;  // TNCCL_CHUNK_BYTES
+  int64_t tsChunkBytes;    // TNCCL_TWOSHOT_CHUNK_BYTES
+  int osSlots;
+  int64_t osTileBytes;     // TNCCL_ONESHOT_TILE_BYTES
+  int nvlsChannels;        // TNCCL_NVLS_CHANNELS
+  int64_t nvlsTileBytes;   // TNCCL_NVLS_TILE_BYTES
+  int nvlsEnable;          // TNCCL_NVLS_ENABLE (0 off, 1 on if supported)
+  int forcedAlgo;          // TNCCL_ALGO (tncclAlgo_t)
+  int64_t timeoutMs;       // TNCCL_TIMEOUT_MS: device wait bound
+  int64_t bootstrapTimeoutMs;  // TNCCL_BOOTSTRAP_TIMEOUT_MS
+  int threads;             // TNCCL_NTHREADS (threads per CTA)
+  int useCuMem;            // TNCCL_CUMEM_ENABLE (0: legacy cudaIpc)
+  // AUTO thresholds in bytes (0 = derive from nranks).
+  int64_t oneShotMaxBytes;   // TNCCL_ONESHOT_MAX_BYTES
+  int64_t nvlsMinBytes;      // TNCCL_NVLS_MIN_BYTES
+};
+
+Config loadConfig();
+uint64_t configHash(const Config& c);
+
+int parseAlgo(const std::string& s);
+
+}  // namespace tnccl

@@ -1,0 +1,57 @@
+// devcomm.h - the plain-old-data structures handed to every kernel launch.
+//
+// tiny-nccl passes DevComm{rank, nranks, inbox, outbox} and DevWork{comm,
+// send, recv, count, baseTicket, tilesPerSegment} by value
+// (src/internal.h:24-40). Here the communicator view holds every peer's
+// mailbox (NVSwitch makes every peer one hop away), the NVLS multicast view,
+// device-resident FIFO counters (so launches replay correctly from CUDA
+// graphs) and a host-mapped status block for bounded waits.
+#pragma once
+
+#include <stdint.h>
+
+#include "protocol.h"
+
+namespace tnccl {
+
+// Host-mapped (cudaHostAllocMapped) status block polled by device waits.
+struct DevStatus {
+  volatile int32_t error;   // first tncclResult recorded by device code
+  volatile int32_t abort;   // set by tncclCommAbort; every wait polls it
+  volatile int32_t where;   // (family << 24) | (channel << 8) | phase
+  volatile int32_t pad;
+  volatile uint64_t expectedSeq;  // flag value the failed wait expected
+  volatile uint64_t observedSeq;  // flag value it last observed
+};
+
+struct DevComm {
+  int rank;
+  int nranks;
+  MailboxLayout layout;
+  char* peers[kMaxRanks];  // mailbox base of every rank (peers[rank] = local)
+  uint64_t* counters;      // device memory [kNumCounterFamilies][kMaxChannels]
+  DevStatus* status;       // device pointer of the host-mapped status block
+  uint64_t timeoutNs;      // bound for every device-side wait
+  // NVLS (valid when nvlsEnabled != 0)
+  int nvlsEnabled;
+  int nvlsChannels;
+  uint64_t nvlsTileBytes;
+  char* nvlsUc;  // this rank's unicast view of the multicast-bound region
+  char* nvlsMc;  // multicast view (multimem.* operations)
+};
+
+enum DataType : int { kF32 = 0, kBF16 = 1, kF16 = 2 };
+
+struct AllReduceArgs {
+  const void* send;
+  void* recv;
+  uint64_t count;
+  float scale;
+  int dtype;
+  int vectorized;  // 1 when send/recv are 16-byte aligned
+  // partition (ring / two-shot use chunk, one-shot / NVLS use block)
+  ChunkPlan chunk;
+  BlockPlan block;
+};
+
+}  // namespace tnccl

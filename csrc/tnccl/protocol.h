@@ -1,0 +1,310 @@
+// protocol.h - partition, tile geometry and mailbox layout shared by host
+// code, device kernels and the CPU rank model.
+//
+// Everything here is pure integer arithmetic on __host__ __device__ inline
+// functions, so the kernels, the launcher and tests/cpp/rank_model_test.cc use
+// one copy of the index math (tiny-nccl keeps its index math in
+// src/device.cuh:16-75 and re-implements it in tests/ring_model_test.cc:16-30;
+// sharing one header removes that duplication).
+//
+// Work decomposition (all algorithms):
+//   * A message of N elements is cut into tiles. For the ring and the
+//     two-shot algorithm a tile holds P chunks (one per rank); for one-shot and
+//     NVLS a tile is one contiguous block that every rank contributes in full.
+//   * Tile k is handled by channel (CTA) k % C, so one channel walks tiles
+//     c, c + C, c + 2C, ... in order. Every rank derives the same tile list
+//     from (N, P, C, chunk), so per-channel FIFO sequence numbers advance
+//     identically on all ranks without any host-side ticket.
+//   * Chunk boundaries are multiples of the 16-byte vector width V, so only
+//     the very end of the message can need scalar accesses.
+#pragma once
+
+#include <stdint.h>
+
+#if defined(__CUDACC__)
+#define TN_HD __host__ __device__ __forceinline__
+#else
+#define TN_HD inline
+#endif
+
+namespace tnccl {
+
+constexpr int kMaxRanks = 16;
+constexpr int kMaxChannels = 64;
+constexpr int kVectorBytes = 16;
+// Smallest chunk (bytes) the planners use, so that small messages occupy few
+// channels instead of many nearly empty ones.
+constexpr uint64_t kRingMinChunkBytes = 4096;
+constexpr uint64_t kTwoShotMinChunkBytes = 2048;
+constexpr uint64_t kOneShotMinTileBytes = 4096;
+constexpr uint64_t kNvlsMinTileBytes = 16384;
+
+// Counter families kept in device memory, one array of kMaxChannels each.
+enum CounterFamily : int {
+  kCounterRing = 0,
+  kCounterOneShot = 1,
+  kCounterTwoShot = 2,
+  kCounterNvls = 3,
+  kNumCounterFamilies = 4
+};
+
+TN_HD uint64_t divUp(uint64_t a, uint64_t b) { return (a + b - 1) / b; }
+TN_HD uint64_t roundUp(uint64_t a, uint64_t b) { return divUp(a, b) * b; }
+TN_HD uint64_t minU64(uint64_t a, uint64_t b) { return a < b ? a : b; }
+TN_HD uint64_t maxU64(uint64_t a, uint64_t b) { return a > b ? a : b; }
+
+struct Span {
+  uint64_t offset;  // element offset into the message
+  uint64_t count;   // elements
+};
+
+// ---------------------------------------------------------------------------
+// Chunked tiles (ring, two-shot): tile = P chunks.
+// ---------------------------------------------------------------------------
+struct ChunkPlan {
+  uint64_t count;       // N
+  uint64_t chunkElems;  // elements per chunk in a full tile (multiple of V)
+  uint64_t tileElems;   // P * chunkElems
+  uint64_t numTiles;    // ceil(N / tileElems)
+  int nranks;
+  int channels;         // channels actually used (<= requested, >= 1)
+};
+
+// Picks the chunk so that the message spreads over all channels, but never
+// exceeds the mailbox chunk capacity and never drops below minChunkElems.
+TN_HD ChunkPlan makeChunkPlan(uint64_t count, int nranks, int channels,
+                              uint64_t maxChunkElems, uint64_t minChunkElems,
+                              uint64_t vecElems) {
+  ChunkPlan p{};
+  p.count = count;
+  p.nranks = nranks;
+  uint64_t want = roundUp(divUp(count, (uint64_t)nranks * (uint64_t)channels),
+                          vecElems);
+  want = maxU64(want, minChunkElems);
+  want = minU64(want, maxChunkElems);
+  if (want == 0) want = vecElems;
+  p.chunkElems = want;
+  p.tileElems = want * (uint64_t)nranks;
+  p.numTiles = count == 0 ? 0 : divUp(count, p.tileElems);
+  uint64_t used = minU64((uint64_t)channels, p.numTiles);
+  p.channels = used == 0 ? 1 : (int)used;
+  return p;
+}
+
+// Element range of tile k.
+TN_HD Span tileSpan(const ChunkPlan& p, uint64_t tile) {
+  uint64_t base = tile * p.tileElems;
+  uint64_t len = p.count > base ? minU64(p.tileElems, p.count - base) : 0;
+  return Span{base, len};
+}
+
+// Element range of chunk j inside tile k. A full tile uses chunkElems per
+// chunk; the final partial tile spreads its remainder evenly over the ranks
+// (rounded to the vector width), so some trailing chunks may be empty.
+TN_HD Span chunkSpan(const ChunkPlan& p, uint64_t tile, int chunk,
+                     uint64_t vecElems) {
+  Span t = tileSpan(p, tile);
+  uint64_t cl = t.count == p.tileElems
+                    ? p.chunkElems
+                    : roundUp(divUp(t.count, (uint64_t)p.nranks), vecElems);
+  uint64_t off = minU64((uint64_t)chunk * cl, t.count);
+  uint64_t n = minU64(cl, t.count - off);
+  return Span{t.offset + off, n};
+}
+
+// Number of tiles channel c processes.
+TN_HD uint64_t channelTiles(uint64_t numTiles, int channels, int c) {
+  return numTiles > (uint64_t)c ? divUp(numTiles - (uint64_t)c, (uint64_t)channels)
+                                : 0;
+}
+
+// ---------------------------------------------------------------------------
+// Block tiles (one-shot, NVLS): tile = one block every rank contributes.
+// ---------------------------------------------------------------------------
+struct BlockPlan {
+  uint64_t count;
+  uint64_t tileElems;
+  uint64_t numTiles;
+  int channels;
+};
+
+TN_HD BlockPlan makeBlockPlan(uint64_t count, int channels,
+                              uint64_t maxTileElems, uint64_t minTileElems,
+                              uint64_t vecElems) {
+  BlockPlan p{};
+  p.count = count;
+  uint64_t want = roundUp(divUp(count, (uint64_t)channels), vecElems);
+  want = maxU64(want, minTileElems);
+  want = minU64(want, maxTileElems);
+  if (want == 0) want = vecElems;
+  p.tileElems = want;
+  p.numTiles = count == 0 ? 0 : divUp(count, want);
+  uint64_t used = minU64((uint64_t)channels, p.numTiles);
+  p.channels = used == 0 ? 1 : (int)used;
+  return p;
+}
+
+TN_HD Span blockTileSpan(const BlockPlan& p, uint64_t tile) {
+  uint64_t base = tile * p.tileElems;
+  uint64_t len = p.count > base ? minU64(p.tileElems, p.count - base) : 0;
+  return Span{base, len};
+}
+
+// Rank r's share of a block tile for NVLS reduce (split evenly over P ranks
+// in vector units).
+TN_HD Span blockShare(uint64_t tileCount, int nranks, int rank,
+                      uint64_t vecElems) {
+  uint64_t cl = roundUp(divUp(tileCount, (uint64_t)nranks), vecElems);
+  uint64_t off = minU64((uint64_t)rank * cl, tileCount);
+  return Span{off, minU64(cl, tileCount - off)};
+}
+
+// ---------------------------------------------------------------------------
+// Ring: chunk schedule of the reduce-scatter / all-gather rotation.
+// ---------------------------------------------------------------------------
+TN_HD int ringChunkBehind(int rank, int distance, int nranks) {
+  int s = (rank - distance) % nranks;
+  return s < 0 ? s + nranks : s;
+}
+
+// Messages per tile on every ring edge: P-1 reduce-scatter + P-1 all-gather.
+TN_HD uint64_t ringMessagesPerTile(int nranks) {
+  return 2ull * (uint64_t)(nranks - 1);
+}
+
+// ---------------------------------------------------------------------------
+// Mailbox layout. One unicast allocation per rank, mapped by every peer.
+// Flags are 64-bit sequence words; each word has exactly one writer.
+// ---------------------------------------------------------------------------
+struct MailboxLayout {
+  int nranks;
+  int channels;       // channels provisioned for ring/two-shot
+  int osChannels;     // channels provisioned for one-shot
+
+  // ring FIFO: data + ready live in the consumer, credit in the producer.
+  int ringSlots;
+  uint64_t ringChunkBytes;
+  uint64_t ringDataOff, ringReadyOff, ringCreditOff;
+
+  // two-shot: per channel, P reduce-scatter chunks + P all-gather chunks.
+  uint64_t tsChunkBytes;
+  uint64_t tsRsDataOff, tsAgDataOff, tsRsFlagOff, tsAgFlagOff;
+
+  // one-shot: per channel and slot, P blocks; flag per source, ack per consumer.
+  int osSlots;
+  uint64_t osTileBytes;
+  uint64_t osDataOff, osFlagOff, osAckOff;
+
+  // NVLS barrier words (unicast): two phases x channels x P sources.
+  int nvlsChannels;
+  uint64_t nvlsFlagOff;
+
+  uint64_t totalBytes;
+};
+
+struct LayoutConfig {
+  int nranks;
+  int channels;
+  int osChannels;
+  int ringSlots;
+  uint64_t ringChunkBytes;
+  uint64_t tsChunkBytes;
+  int osSlots;
+  uint64_t osTileBytes;
+  int nvlsChannels;
+};
+
+TN_HD uint64_t alignUp(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
+
+inline MailboxLayout makeLayout(const LayoutConfig& c) {
+  MailboxLayout L{};
+  const uint64_t P = (uint64_t)c.nranks;
+  const uint64_t C = (uint64_t)c.channels;
+  L.nranks = c.nranks;
+  L.channels = c.channels;
+  L.osChannels = c.osChannels;
+  L.ringSlots = c.ringSlots;
+  L.ringChunkBytes = c.ringChunkBytes;
+  L.tsChunkBytes = c.tsChunkBytes;
+  L.osSlots = c.osSlots;
+  L.osTileBytes = c.osTileBytes;
+  L.nvlsChannels = c.nvlsChannels;
+
+  uint64_t off = 0;
+  L.ringDataOff = off;
+  off += C * (uint64_t)c.ringSlots * c.ringChunkBytes;
+  off = alignUp(off, 4096);
+  L.tsRsDataOff = off;
+  off += C * P * c.tsChunkBytes;
+  L.tsAgDataOff = off;
+  off += C * P * c.tsChunkBytes;
+  off = alignUp(off, 4096);
+  L.osDataOff = off;
+  off += (uint64_t)c.osChannels * (uint64_t)c.osSlots * P * c.osTileBytes;
+  off = alignUp(off, 4096);
+  // Flag words. Each group starts on its own 128-byte line.
+  L.ringReadyOff = off;
+  off = alignUp(off + C * (uint64_t)c.ringSlots * 8, 128);
+  L.ringCreditOff = off;
+  off = alignUp(off + C * (uint64_t)c.ringSlots * 8, 128);
+  L.tsRsFlagOff = off;
+  off = alignUp(off + C * P * 8, 128);
+  L.tsAgFlagOff = off;
+  off = alignUp(off + C * P * 8, 128);
+  L.osFlagOff = off;
+  off = alignUp(off + (uint64_t)c.osChannels * (uint64_t)c.osSlots * P * 8, 128);
+  L.osAckOff = off;
+  off = alignUp(off + (uint64_t)c.osChannels * (uint64_t)c.osSlots * P * 8, 128);
+  L.nvlsFlagOff = off;
+  off = alignUp(off + 2ull * (uint64_t)c.nvlsChannels * P * 8, 128);
+  L.totalBytes = alignUp(off, 4096);
+  return L;
+}
+
+// Address helpers (byte offsets from a rank's mailbox base).
+TN_HD uint64_t ringDataAt(const MailboxLayout& L, int c, int s) {
+  return L.ringDataOff + ((uint64_t)c * L.ringSlots + s) * L.ringChunkBytes;
+}
+TN_HD uint64_t ringReadyAt(const MailboxLayout& L, int c, int s) {
+  return L.ringReadyOff + ((uint64_t)c * L.ringSlots + s) * 8;
+}
+TN_HD uint64_t ringCreditAt(const MailboxLayout& L, int c, int s) {
+  return L.ringCreditOff + ((uint64_t)c * L.ringSlots + s) * 8;
+}
+TN_HD uint64_t tsRsDataAt(const MailboxLayout& L, int c, int src) {
+  return L.tsRsDataOff + ((uint64_t)c * L.nranks + src) * L.tsChunkBytes;
+}
+TN_HD uint64_t tsAgDataAt(const MailboxLayout& L, int c, int src) {
+  return L.tsAgDataOff + ((uint64_t)c * L.nranks + src) * L.tsChunkBytes;
+}
+TN_HD uint64_t tsRsFlagAt(const MailboxLayout& L, int c, int src) {
+  return L.tsRsFlagOff + ((uint64_t)c * L.nranks + src) * 8;
+}
+TN_HD uint64_t tsAgFlagAt(const MailboxLayout& L, int c, int src) {
+  return L.tsAgFlagOff + ((uint64_t)c * L.nranks + src) * 8;
+}
+TN_HD uint64_t osDataAt(const MailboxLayout& L, int c, int s, int src) {
+  return L.osDataOff +
+         (((uint64_t)c * L.osSlots + s) * L.nranks + src) * L.osTileBytes;
+}
+TN_HD uint64_t osFlagAt(const MailboxLayout& L, int c, int s, int src) {
+  return L.osFlagOff + (((uint64_t)c * L.osSlots + s) * L.nranks + src) * 8;
+}
+TN_HD uint64_t osAckAt(const MailboxLayout& L, int c, int s, int consumer) {
+  return L.osAckOff +
+         (((uint64_t)c * L.osSlots + s) * L.nranks + consumer) * 8;
+}
+TN_HD uint64_t nvlsFlagAt(const MailboxLayout& L, int phase, int c, int src) {
+  return L.nvlsFlagOff +
+         (((uint64_t)phase * L.nvlsChannels + c) * L.nranks + src) * 8;
+}
+
+// NVLS multicast region: per channel an input block and an output block.
+TN_HD uint64_t nvlsInAt(uint64_t tileBytes, int c) {
+  return (uint64_t)c * 2 * tileBytes;
+}
+TN_HD uint64_t nvlsOutAt(uint64_t tileBytes, int c) {
+  return (uint64_t)c * 2 * tileBytes + tileBytes;
+}
+
+}  // namespace tnccl

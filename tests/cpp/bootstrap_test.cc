@@ -1,0 +1,234 @@
+// bootstrap_test.cc - CPU-only tests of the AF_UNIX control plane with
+// forked ranks (no GPU): id codec, rendezvous, all-gather, barrier,
+// descriptor passing, and the failure paths (bad id, nranks mismatch,
+// duplicate rank, missing rank, peer death, configuration mismatch, ranks
+// out of step). Every failure is made on the host; every wait is bounded by
+// the bootstrap deadline.
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#include <sys/mman.h>
+#include <sys/wait.h>
+#include <unistd.h>
+
+#include <functional>
+#include <string>
+#include <vector>
+
+#include "bootstrap.h"
+
+using namespace tnccl;
+
+namespace {
+
+int gFailed = 0;
+
+void report(const char* name, bool ok) {
+  printf("%-28s %s\n", name, ok ? "ok" : "FAILED");
+  fflush(stdout);
+  if (!ok) ++gFailed;
+}
+
+// Forks one child per entry of `ranks`; child i runs fn(i) and exits with
+// its return value. Returns the exit codes (or 255 for abnormal exits).
+std::vector<int> forkRanks(int n, const std::function<int(int)>& fn) {
+  std::vector<pid_t> kids;
+  for (int i = 0; i < n; ++i) {
+    pid_t p = fork();
+    if (p == 0) {
+      fflush(stdout);
+      _exit(fn(i));
+    }
+    kids.push_back(p);
+  }
+  std::vector<int> codes;
+  for (pid_t k : kids) {
+    int st = 0;
+    waitpid(k, &st, 0);
+    codes.push_back(WIFEXITED(st) ? WEXITSTATUS(st) : 255);
+  }
+  return codes;
+}
+
+int memfdWith(const std::string& text) {
+  int fd = memfd_create("tnccl-test", MFD_CLOEXEC);
+  if (fd < 0) return -1;
+  if (write(fd, text.data(), text.size()) != (ssize_t)text.size()) return -1;
+  return fd;
+}
+
+std::string readFd(int fd) {
+  char buf[64] = {};
+  ssize_t n = pread(fd, buf, sizeof(buf) - 1, 0);
+  return n > 0 ? std::string(buf, (size_t)n) : std::string();
+}
+
+void testIdCodec() {
+  tncclUniqueId id{};
+  bool ok = bootstrapNewId(&id) == TNCCL_SUCCESS;
+  char path[108];
+  ok = ok && bootstrapDecodeId(id, path) && strstr(path, "tnccl-b200-") != nullptr;
+  tncclUniqueId bad = id;
+  bad.bytes[0] ^= 0xff;  // magic
+  ok = ok && !bootstrapDecodeId(bad, path);
+  bad = id;
+  bad.bytes[16 + 5] = '!';  // a path character outside the allowed set
+  ok = ok && !bootstrapDecodeId(bad, path);
+  bad = id;
+  uint32_t len = 200;  // longer than the path field
+  memcpy(&bad.bytes[12], &len, 4);
+  ok = ok && !bootstrapDecodeId(bad, path);
+  tncclUniqueId zero{};
+  ok = ok && !bootstrapDecodeId(zero, path);
+  Bootstrap b;
+  ok = ok && bootstrapOpen(&b, zero, 2, 0, 0, 100) == TNCCL_INVALID_ARGUMENT;
+  report("id codec / bad id", ok);
+}
+
+void testRendezvous(int P) {
+  tncclUniqueId id{};
+  bootstrapNewId(&id);
+  auto codes = forkRanks(P, [&](int r) -> int {
+    Bootstrap b;
+    if (bootstrapOpen(&b, id, P, r, 42, 5000) != TNCCL_SUCCESS) return 10;
+    int64_t mine[2] = {r, 7 * r + 1};
+    std::vector<int64_t> all((size_t)P * 2);
+    if (bootstrapAllGather(&b, mine, all.data(), sizeof(mine)) != TNCCL_SUCCESS) return 11;
+    for (int p = 0; p < P; ++p)
+      if (all[(size_t)p * 2] != p || all[(size_t)p * 2 + 1] != 7 * p + 1) return 12;
+    for (int i = 0; i < 3; ++i)
+      if (bootstrapBarrier(&b) != TNCCL_SUCCESS) return 13;
+    // Descriptor all-gather: every rank shares a memfd holding its rank.
+    int fd = memfdWith("rank" + std::to_string(r));
+    std::vector<int> fds((size_t)P, -1);
+    if (bootstrapAllGatherFds(&b, fd, fds.data()) != TNCCL_SUCCESS) return 14;
+    for (int p = 0; p < P; ++p) {
+      if (readFd(fds[(size_t)p]) != "rank" + std::to_string(p)) return 15;
+      close(fds[(size_t)p]);
+    }
+    close(fd);
+    // Broadcast from rank 0.
+    int root = r == 0 ? memfdWith("root") : -1;
+    int got = -1;
+    if (bootstrapBroadcastFd(&b, root, &got) != TNCCL_SUCCESS) return 16;
+    if (readFd(got) != "root") return 17;
+    close(got);
+    if (root >= 0) close(root);
+    // Zero-byte all-gather is legal.
+    if (bootstrapAllGather(&b, nullptr, nullptr, 0) != TNCCL_SUCCESS) return 18;
+    bootstrapClose(&b);
+    return 0;
+  });
+  bool ok = true;
+  for (int c : codes) ok = ok && c == 0;
+  char path[108];
+  bootstrapDecodeId(id, path);
+  ok = ok && access(path, F_OK) != 0;  // rank 0 unlinked its socket
+  char name[64];
+  snprintf(name, sizeof(name), "rendezvous P=%d", P);
+  report(name, ok);
+  if (!ok)
+    for (size_t i = 0; i < codes.size(); ++i) printf("  rank %zu exit %d\n", i, codes[i]);
+}
+
+void testNranksMismatch() {
+  tncclUniqueId id{};
+  bootstrapNewId(&id);
+  auto codes = forkRanks(2, [&](int r) -> int {
+    Bootstrap b;
+    return (int)bootstrapOpen(&b, id, r == 0 ? 2 : 3, r == 0 ? 0 : 1, 1, 2000);
+  });
+  report("nranks mismatch", codes[0] == TNCCL_INVALID_ARGUMENT &&
+                                codes[1] == TNCCL_INVALID_ARGUMENT);
+}
+
+void testDuplicateRank() {
+  tncclUniqueId id{};
+  bootstrapNewId(&id);
+  auto codes = forkRanks(3, [&](int r) -> int {
+    Bootstrap b;
+    tncclResult res = bootstrapOpen(&b, id, 3, r == 0 ? 0 : 1, 1, 2000);
+    if (res != TNCCL_SUCCESS || r == 0) return (int)res;
+    // The claimant accepted first joined; its next collective must fail
+    // because rank 0 gave up on the rendezvous.
+    return 50 + (int)bootstrapBarrier(&b);
+  });
+  // Rank 0 rejects the second hello for rank 1; both claimants fail.
+  bool ok = codes[0] == TNCCL_INVALID_ARGUMENT && codes[1] != 0 && codes[2] != 0 &&
+            codes[1] != 50 && codes[2] != 50;
+  report("duplicate rank", ok);
+}
+
+void testConfigMismatch() {
+  tncclUniqueId id{};
+  bootstrapNewId(&id);
+  auto codes = forkRanks(2, [&](int r) -> int {
+    Bootstrap b;
+    return (int)bootstrapOpen(&b, id, 2, r, r == 0 ? 1 : 2, 2000);
+  });
+  report("config hash mismatch", codes[0] == TNCCL_INVALID_ARGUMENT &&
+                                     codes[1] == TNCCL_INVALID_ARGUMENT);
+}
+
+void testMissingRank() {
+  tncclUniqueId id{};
+  bootstrapNewId(&id);
+  // Rank 2 of 3 never starts.
+  auto codes = forkRanks(2, [&](int r) -> int {
+    Bootstrap b;
+    tncclResult res = bootstrapOpen(&b, id, 3, r, 1, 500);
+    if (r == 0) return (int)res;
+    if (res != TNCCL_SUCCESS) return 100 + (int)res;
+    // Rank 1 joined; its next collective must fail within the deadline.
+    int x = 1, all[3];
+    return 50 + (int)bootstrapAllGather(&b, &x, all, sizeof(x));
+  });
+  bool ok = codes[0] == TNCCL_TIMEOUT && codes[1] != 50;
+  report("missing rank -> timeout", ok);
+  if (!ok) printf("  codes %d %d\n", codes[0], codes[1]);
+}
+
+void testPeerDeath() {
+  tncclUniqueId id{};
+  bootstrapNewId(&id);
+  auto codes = forkRanks(3, [&](int r) -> int {
+    Bootstrap b;
+    if (bootstrapOpen(&b, id, 3, r, 1, 1000) != TNCCL_SUCCESS) return 90;
+    if (bootstrapBarrier(&b) != TNCCL_SUCCESS) return 91;
+    if (r == 2) _exit(0);  // dies without taking part in the gather
+    int x = r, all[3];
+    return (int)bootstrapAllGather(&b, &x, all, sizeof(x));
+  });
+  bool ok = codes[0] != 0 && codes[1] != 0 && codes[2] == 0;
+  report("peer death mid-gather", ok);
+  if (!ok) printf("  codes %d %d %d\n", codes[0], codes[1], codes[2]);
+}
+
+void testOutOfStep() {
+  tncclUniqueId id{};
+  bootstrapNewId(&id);
+  auto codes = forkRanks(2, [&](int r) -> int {
+    Bootstrap b;
+    if (bootstrapOpen(&b, id, 2, r, 1, 1000) != TNCCL_SUCCESS) return 90;
+    if (r == 0) return (int)bootstrapBarrier(&b);
+    int x = 1, all[2];
+    return (int)bootstrapAllGather(&b, &x, all, sizeof(x));
+  });
+  report("ranks out of step", codes[0] != 0 && codes[1] != 0);
+}
+
+}  // namespace
+
+int main() {
+  setenv("TNCCL_DEBUG", "NONE", 0);
+  testIdCodec();
+  for (int P : {2, 3, 4, 8}) testRendezvous(P);
+  testNranksMismatch();
+  testDuplicateRank();
+  testConfigMismatch();
+  testMissingRank();
+  testPeerDeath();
+  testOutOfStep();
+  printf("bootstrap_test: %s\n", gFailed ? "FAIL" : "PASS");
+  return gFailed ? 1 : 0;
+}

@@ -1,0 +1,198 @@
+"""In-tree native build for tiny_nccl_b200.
+
+Builds three shared objects next to this file (``lib/``), all for sm_100a:
+
+* ``libtnccl.so``      - the collective library (C API of ``include/tnccl.h``):
+                         bootstrap, communicator, transport and the all-reduce
+                         kernels. Links the CUDA runtime statically and resolves
+                         driver entry points at run time, so it loads on hosts
+                         without a GPU driver.
+* ``libtnccl_ops.so``  - the framework's model kernels (``csrc/ops``) behind a
+                         plain C launcher interface.
+* ``_C.*.so``          - the PyTorch binding (``csrc/torch``), compiled with g++
+                         only and linked against the two libraries above.
+
+A build is skipped when a stamp file records the same source/flag hash, so the
+``.so`` files that travel with the repository are reused as they are.
+"""
+from __future__ import annotations
+
+import concurrent.futures as cf
+import hashlib
+import os
+import subprocess
+import sys
+import sysconfig
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent.parent
+PKG = Path(__file__).resolve().parent
+LIB = PKG / "lib"
+OBJ = ROOT / "build" / "obj"
+CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
+NVCC = str(CUDA_HOME / "bin" / "nvcc")
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+CXXFLAGS = ["-O2", "-std=c++17", "-fPIC", "-Wall", "-Wextra", "-Wno-unused-parameter"]
+NVCCFLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC",
+                    "--expt-relaxed-constexpr", "-diag-suppress", "177"]
+
+TNCCL_SRC = ROOT / "csrc" / "tnccl"
+OPS_SRC = ROOT / "csrc" / "ops"
+TORCH_SRC = ROOT / "csrc" / "torch"
+INCLUDES = [f"-I{ROOT / 'include'}", f"-I{TNCCL_SRC}", f"-I{CUDA_HOME / 'include'}"]
+
+
+def _hash(paths, extra: str) -> str:
+    h = hashlib.sha256(extra.encode())
+    for p in sorted(paths):
+        h.update(str(p.relative_to(ROOT)).encode())
+        h.update(p.read_bytes())
+    return h.hexdigest()
+
+
+def _run(cmd, cwd=ROOT):
+    r = subprocess.run(cmd, cwd=cwd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"build command failed ({r.returncode}):\n{' '.join(map(str, cmd))}\n"
+                           f"{r.stdout}\n{r.stderr}")
+    return r
+
+
+def _compile(src: Path, obj: Path, extra_inc=()):
+    obj.parent.mkdir(parents=True, exist_ok=True)
+    if src.suffix == ".cu":
+        cmd = [NVCC, *NVCCFLAGS, *INCLUDES, *extra_inc, "-c", str(src), "-o", str(obj)]
+    else:
+        cmd = ["g++", *CXXFLAGS, *INCLUDES, *extra_inc, "-c", str(src), "-o", str(obj)]
+    _run(cmd)
+    return obj
+
+
+def _headers(d: Path):
+    return [p for p in d.rglob("*") if p.suffix in (".h", ".cuh", ".hpp")]
+
+
+def _build_shared(name: str, srcs, deps, link_extra=(), extra_inc=(), jobs=8) -> Path:
+    out = LIB / name
+    stamp = LIB / (name + ".stamp")
+    key = _hash(list(srcs) + list(deps), " ".join(NVCCFLAGS + CXXFLAGS + list(link_extra)))
+    if out.exists() and stamp.exists() and stamp.read_text() == key:
+        return out
+    LIB.mkdir(parents=True, exist_ok=True)
+    objdir = OBJ / name
+    with cf.ThreadPoolExecutor(max_workers=jobs) as ex:
+        objs = list(ex.map(lambda s: _compile(s, objdir / (s.stem + s.suffix.replace(".", "_") + ".o"),
+                                              extra_inc), srcs))
+    tmp = out.with_suffix(".so.tmp")
+    cmd = [NVCC, *ARCH, "-shared", "-cudart", "static", "-o", str(tmp), *map(str, objs),
+           "-Xlinker", "-rpath,$ORIGIN", *link_extra, "-lpthread", "-ldl", "-lrt"]
+    _run(cmd)
+    os.replace(tmp, out)
+    stamp.write_text(key)
+    return out
+
+
+def build_tnccl() -> Path:
+    srcs = sorted(TNCCL_SRC.glob("*.cc")) + sorted(TNCCL_SRC.glob("*.cu"))
+    deps = _headers(TNCCL_SRC) + [ROOT / "include" / "tnccl.h"]
+    return _build_shared("libtnccl.so", srcs, deps)
+
+
+def build_ops() -> Path | None:
+    srcs = sorted(OPS_SRC.glob("*.cu"))
+    if not srcs:
+        return None
+    deps = _headers(OPS_SRC)
+    return _build_shared("libtnccl_ops.so", srcs, deps, extra_inc=[f"-I{OPS_SRC}"])
+
+
+def _ext_suffix() -> str:
+    return sysconfig.get_config_var("EXT_SUFFIX") or ".so"
+
+
+def build_torch_ext() -> Path:
+    import torch.utils.cpp_extension as ce  # noqa: WPS433 (build-time only)
+
+    srcs = sorted(TORCH_SRC.glob("*.cpp"))
+    name = "_C" + _ext_suffix()
+    out = PKG / name
+    stamp = LIB / "_C.stamp"
+    import torch
+    deps = _headers(TORCH_SRC) + [ROOT / "include" / "tnccl.h"] + _headers(OPS_SRC)
+    key = _hash(list(srcs) + deps, "torch-" + torch.__version__ + " ".join(CXXFLAGS))
+    if out.exists() and stamp.exists() and stamp.read_text() == key:
+        return out
+    inc = [f"-I{p}" for p in ce.include_paths()] + [f"-I{sysconfig.get_paths()['include']}",
+                                                   f"-I{OPS_SRC}"]
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    flags = [*CXXFLAGS, "-Wno-missing-field-initializers", f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
+             "-DTORCH_EXTENSION_NAME=_C", "-DTORCH_API_INCLUDE_EXTENSION_H"]
+    objdir = OBJ / "_C"
+    objdir.mkdir(parents=True, exist_ok=True)
+
+    def comp(s: Path) -> Path:
+        o = objdir / (s.stem + ".o")
+        _run(["g++", *flags, *INCLUDES, *inc, "-c", str(s), "-o", str(o)])
+        return o
+
+    with cf.ThreadPoolExecutor(max_workers=8) as ex:
+        objs = list(ex.map(comp, srcs))
+    libdirs = ce.library_paths()
+    tmp = out.with_suffix(".tmp")
+    cmd = ["g++", "-shared", "-o", str(tmp), *map(str, objs), f"-L{LIB}", "-ltnccl",
+           "-ltnccl_ops" if (LIB / "libtnccl_ops.so").exists() else "",
+           *[f"-L{d}" for d in libdirs], "-lc10", "-ltorch", "-ltorch_cpu", "-ltorch_python",
+           f"-Wl,-rpath,$ORIGIN/lib", *[f"-Wl,-rpath,{d}" for d in libdirs]]
+    _run([c for c in cmd if c])
+    os.replace(tmp, out)
+    stamp.write_text(key)
+    return out
+
+
+BIN = ROOT / "build" / "bin"
+
+# C++ programs: (source, needs CUDA headers/runtime)
+PROGRAMS = {
+    "tnccl_allreduce": ROOT / "examples" / "allreduce.cc",
+    "allreduce_gpu_test": ROOT / "tests" / "cpp" / "allreduce_gpu_test.cc",
+    "bootstrap_test": ROOT / "tests" / "cpp" / "bootstrap_test.cc",
+    "rank_model_test": ROOT / "tests" / "cpp" / "rank_model_test.cc",
+}
+
+
+def build_programs() -> list[Path]:
+    """Builds the example and the C++ test programs into build/bin."""
+    lib = build_tnccl()
+    BIN.mkdir(parents=True, exist_ok=True)
+    outs = []
+    for name, src in PROGRAMS.items():
+        if not src.exists():
+            continue
+        out = BIN / name
+        stamp = BIN / (name + ".stamp")
+        deps = [src] + _headers(ROOT / "tests" / "cpp") + _headers(TNCCL_SRC) + \
+            [ROOT / "include" / "tnccl.h"]
+        key = _hash(deps, "prog " + " ".join(CXXFLAGS) + str(lib.stat().st_size))
+        if not (out.exists() and stamp.exists() and stamp.read_text() == key):
+            obj = OBJ / "bin" / (name + ".o")
+            obj.parent.mkdir(parents=True, exist_ok=True)
+            _run(["g++", *CXXFLAGS, "-O2", *INCLUDES, f"-I{ROOT / 'tests' / 'cpp'}", "-c",
+                  str(src), "-o", str(obj)])
+            _run([NVCC, *ARCH, "-o", str(out), str(obj), f"-L{LIB}", "-ltnccl",
+                  "-Xlinker", f"-rpath,{LIB}", "-Xlinker", "-rpath,$ORIGIN/../../tiny_nccl_b200/lib",
+                  "-lpthread"])
+            stamp.write_text(key)
+        outs.append(out)
+    return outs
+
+
+def build_all(verbose: bool = False) -> None:
+    paths = [build_tnccl(), build_ops(), build_torch_ext(), *build_programs()]
+    if verbose:
+        for p in paths:
+            if p is not None:
+                print(f"built {p.relative_to(ROOT)}", file=sys.stderr)
+
+
+if __name__ == "__main__":
+    build_all(verbose=True)
