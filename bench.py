@@ -1,0 +1,288 @@
+#!/usr/bin/env python
+"""Flagship benchmark: GPT-2 small data-parallel training throughput (tokens/s).
+
+    python bench.py --gpus 1 --steps K --warmup W
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \
+        --master-port P bench.py --gpus N --steps K --warmup W [--impl reference]
+
+Workload: GPT-2 small (12 layers, d_model 768, 12 heads,
+vocabulary 50257, context 1024), micro-batch 8 per GPU, bf16 autocast, AdamW,
+random initialisation, synthetic token ids Uniform[0, 50257) seeded per rank.
+Weak scaling: every GPU processes 8 x 1024 tokens per step.
+
+--impl tnccl (default): the framework's GPT-2 (fused sm_100a LayerNorm /
+  cross-entropy / AdamW kernels) under DistributedDataParallel with the tnccl
+  comm hook (gradient buckets all-reduced by tnccl kernels over NVLink).
+--impl reference: the unmodified tiny-nccl reference (baseline/_ref, built by
+  baseline/build_reference.sh) all-reduces the gradient buckets through its
+  public tncclAllReduceSumF32, inside stock PyTorch: Hugging Face GPT2LMHeadModel,
+  torch.optim.AdamW, DistributedDataParallel.
+
+Timing: W untimed warm-up steps; then K steps bracketed by a barrier and
+torch.cuda.synchronize(), timed with CUDA events on the training stream; the
+step time is the max over ranks. A second timed loop of K steps measures the
+same metric end to end (pinned-host token copy in, loss read back each step).
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import datetime
+import json
+import os
+import socket
+import sys
+import time
+
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "GPT-2 small DP training tokens/s"
+REF_LIB = os.path.join(ROOT, "baseline", "_ref", "lib", "libtiny_nccl_ref.so")
+
+
+def free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def setup_dist():
+    if "RANK" not in os.environ:
+        os.environ.update({"RANK": "0", "WORLD_SIZE": "1", "LOCAL_RANK": "0",
+                           "MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(free_port())})
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=180))
+    return rank, world, local, dev
+
+
+def max_over_ranks(x: float, dev) -> float:
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.item()
+
+
+class UniqueId(ctypes.Structure):
+    """tncclUniqueId: a 128-byte struct passed by value."""
+    _fields_ = [("bytes", ctypes.c_ubyte * 128)]
+
+
+class ReferenceComm:
+    """ctypes handle on the reference library (tiny-nccl public API)."""
+
+    def __init__(self, rank: int, world: int):
+        lib = ctypes.CDLL(REF_LIB)
+        lib.tncclGetUniqueId.argtypes = [ctypes.c_void_p]
+        lib.tncclCommInitRank.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int,
+                                          UniqueId, ctypes.c_int]
+        lib.tncclAllReduceSumF32.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
+                                             ctypes.c_void_p, ctypes.c_void_p]
+        lib.tncclCommDestroy.argtypes = [ctypes.c_void_p]
+        self.lib = lib
+        uid = UniqueId()
+        obj = [None]
+        if rank == 0:
+            if lib.tncclGetUniqueId(ctypes.byref(uid)) != 0:
+                raise RuntimeError("reference tncclGetUniqueId failed")
+            obj = [bytes(uid)]
+        dist.broadcast_object_list(obj, src=0)
+        ctypes.memmove(ctypes.byref(uid), obj[0], 128)
+        self.comm = ctypes.c_void_p()
+        rc = lib.tncclCommInitRank(ctypes.byref(self.comm), world, uid, rank)
+        if rc != 0:
+            raise RuntimeError(f"reference tncclCommInitRank failed ({rc})")
+        self.world = world
+
+    def all_reduce_(self, t: torch.Tensor, stream: torch.cuda.Stream):
+        rc = self.lib.tncclAllReduceSumF32(ctypes.c_void_p(t.data_ptr()),
+                                           ctypes.c_void_p(t.data_ptr()),
+                                           ctypes.c_size_t(t.numel()), self.comm,
+                                           ctypes.c_void_p(stream.cuda_stream))
+        if rc != 0:
+            raise RuntimeError(f"reference tncclAllReduceSumF32 failed ({rc})")
+
+    def destroy(self):
+        self.lib.tncclCommDestroy(self.comm)
+
+
+def build_reference_trainer(args, rank, world, dev):
+    """Stock PyTorch GPT-2 (Hugging Face) + DDP whose gradient buckets go
+    through the reference's tncclAllReduceSumF32 (fp32, then / world)."""
+    from torch.nn.parallel import DistributedDataParallel as DDP
+    from transformers import GPT2Config as HFConfig, GPT2LMHeadModel
+
+    cfg = HFConfig(n_layer=12, n_head=12, n_embd=768, vocab_size=50257, n_positions=1024,
+                   resid_pdrop=0.0, embd_pdrop=0.0, attn_pdrop=0.0)
+    torch.manual_seed(1234)
+    model = GPT2LMHeadModel(cfg).to(dev)
+    ref = ReferenceComm(rank, world)
+    side = torch.cuda.Stream(device=dev)
+
+    def hook(state, bucket):
+        buf = bucket.buffer()
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            ref.all_reduce_(buf, side)
+            buf.div_(world)
+            buf.record_stream(side)
+            fut = torch.futures.Future(devices=[dev])
+            fut.set_result(buf)
+        return fut
+
+    ddp = DDP(model, device_ids=[dev.index], bucket_cap_mb=25, gradient_as_bucket_view=True,
+              static_graph=True, broadcast_buffers=False)
+    ddp.register_comm_hook(None, hook)
+    decay = [p for p in model.parameters() if p.dim() >= 2]
+    no_decay = [p for p in model.parameters() if p.dim() < 2]
+    opt = torch.optim.AdamW([{"params": decay, "weight_decay": 0.1},
+                             {"params": no_decay, "weight_decay": 0.0}], lr=6e-4,
+                            betas=(0.9, 0.95), fused=True)
+
+    def step(idx, tgt):
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            out = ddp(input_ids=idx, labels=idx)
+        out.loss.backward()
+        opt.step()
+        opt.zero_grad(set_to_none=False)
+        return out.loss.detach()
+
+    def launches():
+        return 0  # the reference path launches no kernel of this repository
+
+    return step, launches, ref.destroy
+
+
+def build_tnccl_trainer(args, rank, world, dev):
+    import tiny_nccl_b200 as tn
+    from tiny_nccl_b200.models import GPT2, GPT2Config
+    from tiny_nccl_b200.parallel import DataParallelTrainer
+
+    comm = tn.init_from_torch_distributed(device=dev.index)
+    torch.manual_seed(1234)
+    model = GPT2(GPT2Config(), impl="fused").to(dev)
+    trainer = DataParallelTrainer(model, comm, algo=args.algo)
+
+    def launches():
+        return tn.launch_count() + tn.load().ops.launch_count()
+
+    def close():
+        torch.cuda.synchronize()
+        comm.destroy()
+
+    return trainer.step, launches, close
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="tnccl", choices=["tnccl", "reference"])
+    ap.add_argument("--batch", type=int, default=8)
+    ap.add_argument("--seq", type=int, default=1024)
+    ap.add_argument("--algo", default="auto")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    if args.impl == "reference" and not os.path.exists(REF_LIB):
+        script = os.path.join(ROOT, "baseline", "build_reference.sh")
+        if os.path.isdir("/root/reference"):
+            os.system(f"bash {script} /root/reference > /dev/null 2>&1")
+        if not os.path.exists(REF_LIB):
+            if int(os.environ.get("RANK", "0")) == 0:
+                print(json.dumps({"impl": "reference", "unavailable":
+                                  "baseline/_ref is not built and the reference source is absent"}))
+            return
+
+    rank, world, local, dev = setup_dist()
+    B, T = args.batch, args.seq
+    if args.impl == "reference":
+        step, launches, close = build_reference_trainer(args, rank, world, dev)
+    else:
+        step, launches, close = build_tnccl_trainer(args, rank, world, dev)
+
+    # Synthetic data: a pool of distinct seeded batches per rank.
+    gen = torch.Generator(device="cpu")
+    gen.manual_seed(4242 + rank)
+    pool = 4
+    host = torch.randint(0, 50257, (pool, B, T + 1), generator=gen, dtype=torch.int64)
+    host = host.pin_memory()
+    dev_batches = host.to(dev)
+
+    def run(i):
+        b = dev_batches[i % pool]
+        return step(b[:, :T], b[:, 1:])
+
+    for i in range(args.warmup):
+        run(i)
+    torch.cuda.synchronize()
+    dist.barrier()
+
+    from tiny_nccl_b200.utils import ClockSampler
+    sampler = ClockSampler(gpu_index=None).start() if rank == 0 else None
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    dist.barrier()
+    l0 = launches()
+    e0.record(stream)
+    for i in range(args.steps):
+        loss = run(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    l1 = launches()
+    dist.barrier()
+    clocks = sampler.stop() if sampler else {}
+    ms = e0.elapsed_time(e1) / args.steps
+    ms_max = max_over_ranks(ms, dev)
+    last_loss = float(loss.item())
+
+    e2e = None
+    if not args.no_e2e:
+        idx_dev = torch.empty((B, T + 1), dtype=torch.int64, device=dev)
+        torch.cuda.synchronize()
+        dist.barrier()
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            idx_dev.copy_(host[i % pool], non_blocking=True)
+            l = step(idx_dev[:, :T], idx_dev[:, 1:])
+            float(l.item())  # device -> host read of the step's loss
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+        wall_max = max_over_ranks(wall, dev)
+        e2e = {"value": world * B * T * args.steps / wall_max, "unit": "tokens/s",
+               "h2d_bytes_per_step": B * (T + 1) * 8, "d2h_bytes_per_step": 4,
+               "ms_per_step": wall_max * 1e3 / args.steps, "timing": "host wall clock, max over ranks"}
+
+    tokens_per_s = world * B * T / (ms_max * 1e-3)
+    if rank == 0:
+        from tiny_nccl_b200.models import GPT2Config
+        flops = GPT2Config().flops_per_token(T) * tokens_per_s / world
+        rec = {"metric": METRIC, "value": tokens_per_s, "unit": "tokens/s", "n_gpus": world,
+               "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
+               "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+               "dtype": "bf16", "data": "synthetic token ids Uniform[0,50257) seeded per rank; "
+                                        "random-init weights",
+               "impl": args.impl,
+               "config": {"model": "GPT-2 small (124M): 12 layers, d_model 768, 12 heads, vocab 50257",
+                          "global_batch": B * world, "micro_batch_per_gpu": B, "seq_len": T,
+                          "parallelism": f"dp{world}", "optimizer": "AdamW", "amp": "bf16 autocast",
+                          "l2": "no flush: one step touches several GB (activations, 124M-param "
+                                "weights/grads/optimizer state), far above the 126 MB L2"},
+               "clocks": clocks, "gpu_launches": int(l1 - l0), "e2e": e2e,
+               "model_tflops_per_gpu": flops / 1e12, "loss": last_loss}
+        print(json.dumps(rec), flush=True)
+    close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,61 @@
+"""NVLink primitive micro-benchmark (push stores, pull loads, push with a
+release flag per chunk, local copy) across CTA counts, thread counts and
+accesses in flight. Used to size the collective kernels.
+
+    python -m torch.distributed.run --nproc-per-node 2 --master-addr 127.0.0.1 \
+        benchmarks/p2p_microbench.py --out p2p.jsonl
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import sys
+
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--bytes", type=int, default=64 << 20)
+    ap.add_argument("--out", default="")
+    args = ap.parse_args()
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                            timeout=datetime.timedelta(seconds=60))
+    os.environ.setdefault("TNCCL_NCHANNELS", "128")
+    os.environ.setdefault("TNCCL_CHUNK_BYTES", str(1 << 20))  # large ring area as scratch
+    import tiny_nccl_b200 as tn
+    comm = tn.init_from_torch_distributed(device=local)
+    out = open(args.out, "a") if (args.out and rank == 0) else None
+    modes = {0: "push", 1: "pull", 2: "push+flag", 3: "local"}
+    for mode in (0, 1, 3, 2):
+        for ctas in (1, 8, 32, 64, 128):
+            for threads in (256, 512, 1024):
+                for unroll in ((1, 4, 8, 16) if mode != 2 else (1,)):
+                    chunks = (16 << 10, 64 << 10, 256 << 10) if mode == 2 else (0,)
+                    for chunk in chunks:
+                        dist.barrier()
+                        ms = comm._c.diag_bench(mode, args.bytes, ctas, threads, unroll, chunk, 5)
+                        t = torch.tensor([ms], device="cuda")
+                        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                        gbs = args.bytes / (t.item() * 1e-3) / 1e9
+                        rec = {"mode": modes[mode], "ctas": ctas, "threads": threads,
+                               "unroll": unroll, "chunk": chunk, "GBps": gbs,
+                               "GBps_per_cta": gbs / ctas}
+                        if rank == 0:
+                            print(json.dumps(rec), flush=True)
+                            if out:
+                                out.write(json.dumps(rec) + "\n")
+    comm.destroy()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,106 @@
+// adamw.cu - multi-tensor AdamW with decoupled weight decay, fp32 state.
+//
+// One launch covers up to 64 tensors. The grid walks 16 KiB chunks of the
+// concatenated tensors; each CTA finds its tensor by scanning the chunk
+// prefix table (at most 64 entries) and updates float4 groups:
+//   m = b1 m + (1 - b1) g,  v = b2 v + (1 - b2) g^2,
+//   p -= lr * ((m / bc1) / (sqrt(v / bc2) + eps) + wd * p).
+#include <math.h>
+
+#include "common.cuh"
+#include "tnccl_ops.h"
+
+namespace tnops {
+
+std::atomic<unsigned long long> gLaunches{0};
+
+namespace {
+
+constexpr int kChunk = 4096;  // elements per CTA iteration
+
+struct AdamArgs {
+  tnops_adamw_list list;
+  int64_t chunkStart[65];
+  float lr, b1, b2, eps, bc1, bc2, gscale;
+};
+
+__device__ __forceinline__ void adamElem(float& p, float g, float& m, float& v, float wd,
+                                         const AdamArgs& a) {
+  g *= a.gscale;
+  m = a.b1 * m + (1.f - a.b1) * g;
+  v = a.b2 * v + (1.f - a.b2) * g * g;
+  const float mh = m / a.bc1;
+  const float vh = v / a.bc2;
+  p -= a.lr * (mh / (sqrtf(vh) + a.eps) + wd * p);
+}
+
+__global__ void __launch_bounds__(256) adamwKernel(const __grid_constant__ AdamArgs a) {
+  const int64_t total = a.chunkStart[a.list.n];
+  for (int64_t chunk = blockIdx.x; chunk < total; chunk += gridDim.x) {
+    int t = 0;
+    while (t + 1 < a.list.n && a.chunkStart[t + 1] <= chunk) ++t;
+    const int64_t off = (chunk - a.chunkStart[t]) * kChunk;
+    const int64_t n = a.list.numel[t];
+    const int64_t end = off + kChunk < n ? off + kChunk : n;
+    float* p = a.list.param[t];
+    const float* g = a.list.grad[t];
+    float* m = a.list.exp_avg[t];
+    float* v = a.list.exp_avg_sq[t];
+    const float wd = a.list.weight_decay[t];
+    const bool vec = ((reinterpret_cast<uintptr_t>(p) | reinterpret_cast<uintptr_t>(g) |
+                       reinterpret_cast<uintptr_t>(m) | reinterpret_cast<uintptr_t>(v)) & 15) == 0;
+    if (vec) {
+      const int64_t v0 = off / 4, v1 = end / 4;
+      for (int64_t i = v0 + threadIdx.x; i < v1; i += blockDim.x) {
+        float4 pp = reinterpret_cast<float4*>(p)[i];
+        const float4 gg = reinterpret_cast<const float4*>(g)[i];
+        float4 mm = reinterpret_cast<float4*>(m)[i];
+        float4 vv = reinterpret_cast<float4*>(v)[i];
+        adamElem(pp.x, gg.x, mm.x, vv.x, wd, a);
+        adamElem(pp.y, gg.y, mm.y, vv.y, wd, a);
+        adamElem(pp.z, gg.z, mm.z, vv.z, wd, a);
+        adamElem(pp.w, gg.w, mm.w, vv.w, wd, a);
+        reinterpret_cast<float4*>(p)[i] = pp;
+        reinterpret_cast<float4*>(m)[i] = mm;
+        reinterpret_cast<float4*>(v)[i] = vv;
+      }
+      for (int64_t i = v1 * 4 + threadIdx.x; i < end; i += blockDim.x)
+        adamElem(p[i], g[i], m[i], v[i], wd, a);
+    } else {
+      for (int64_t i = off + threadIdx.x; i < end; i += blockDim.x)
+        adamElem(p[i], g[i], m[i], v[i], wd, a);
+    }
+  }
+}
+
+}  // namespace
+}  // namespace tnops
+
+using namespace tnops;
+
+extern "C" int tnops_adamw(const tnops_adamw_list* list, float lr, float beta1, float beta2,
+                           float eps, int64_t step, float grad_scale, cudaStream_t stream) {
+  if (list == nullptr || list->n <= 0 || list->n > 64 || step < 1)
+    return (int)cudaErrorInvalidValue;
+  AdamArgs a;
+  a.list = *list;
+  a.chunkStart[0] = 0;
+  for (int t = 0; t < list->n; ++t)
+    a.chunkStart[t + 1] = a.chunkStart[t] + (list->numel[t] + kChunk - 1) / kChunk;
+  a.lr = lr;
+  a.b1 = beta1;
+  a.b2 = beta2;
+  a.eps = eps;
+  a.bc1 = (float)(1.0 - pow((double)beta1, (double)step));
+  a.bc2 = (float)(1.0 - pow((double)beta2, (double)step));
+  a.gscale = grad_scale;
+  int64_t total = a.chunkStart[list->n];
+  int blocks = (int)(total < kSMs * 8 ? total : kSMs * 8);
+  if (blocks < 1) blocks = 1;
+  adamwKernel<<<blocks, 256, 0, stream>>>(a);
+  return launched(cudaGetLastError());
+}
+
+extern "C" unsigned long long tnops_launch_count(void) {
+  return gLaunches.load(std::memory_order_relaxed);
+}

@@ -1,0 +1,265 @@
+// layernorm.cu - fused residual add + LayerNorm (forward and backward) for a
+// fp32 residual stream with bf16 activations, one warp per row.
+//
+// Forward:  x_out = x + delta;  y = (x_out - mean) * rstd * w + b   (bf16)
+// Backward: with xhat = (x_out - mean) * rstd and gw = gy * w,
+//           dx = g_res + rstd * (gw - mean(gw) - xhat * mean(gw * xhat))
+//           dw = sum_rows gy * xhat,  db = sum_rows gy
+// dw/db are reduced deterministically: each CTA keeps per-lane column sums in
+// registers, combines its warps in shared memory and writes one partial row;
+// a second kernel sums the partial rows in a fixed order.
+#include "common.cuh"
+#include "tnccl_ops.h"
+
+namespace tnops {
+namespace {
+
+constexpr int kWarpsPerBlock = 8;
+constexpr int kPartialRows = 2 * kSMs;
+
+// K = float4 groups per lane (C <= 128 * K).
+template <int K>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32)
+    lnFwdKernel(const float* __restrict__ x, const uint16_t* __restrict__ delta,
+                const float* __restrict__ w, const float* __restrict__ b, float* __restrict__ xo,
+                uint16_t* __restrict__ y, float* __restrict__ mean, float* __restrict__ rstd,
+                int rows, int C, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int C4 = C >> 2;
+  const size_t base = (size_t)row * C;
+  const float4* xr = reinterpret_cast<const float4*>(x + base);
+  float4 v[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const int i = lane + 32 * k;
+    if (i < C4) v[k] = xr[i];
+  }
+  if (delta != nullptr) {
+    const uint2* dr = reinterpret_cast<const uint2*>(delta + base);
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const int i = lane + 32 * k;
+      if (i < C4) {
+        const float4 d = bf4(dr[i]);
+        v[k].x += d.x;
+        v[k].y += d.y;
+        v[k].z += d.z;
+        v[k].w += d.w;
+      }
+    }
+  }
+  float s = 0.f;
+  float4* xor_ = reinterpret_cast<float4*>(xo + base);
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const int i = lane + 32 * k;
+    if (i < C4) {
+      xor_[i] = v[k];
+      s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+    }
+  }
+  const float mu = warpSum(s) / (float)C;
+  float q = 0.f;
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const int i = lane + 32 * k;
+    if (i < C4) {
+      const float a = v[k].x - mu, bb = v[k].y - mu, c = v[k].z - mu, d = v[k].w - mu;
+      q += (a * a + bb * bb) + (c * c + d * d);
+    }
+  }
+  const float rs = rsqrtf(warpSum(q) / (float)C + eps);
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  const float4* b4 = reinterpret_cast<const float4*>(b);
+  uint2* yr = reinterpret_cast<uint2*>(y + base);
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const int i = lane + 32 * k;
+    if (i < C4) {
+      const float4 ww = w4[i], bb = b4[i];
+      float4 o;
+      o.x = (v[k].x - mu) * rs * ww.x + bb.x;
+      o.y = (v[k].y - mu) * rs * ww.y + bb.y;
+      o.z = (v[k].z - mu) * rs * ww.z + bb.z;
+      o.w = (v[k].w - mu) * rs * ww.w + bb.w;
+      yr[i] = tobf4(o);
+    }
+  }
+  if (lane == 0) {
+    mean[row] = mu;
+    rstd[row] = rs;
+  }
+}
+
+template <int K>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32)
+    lnBwdKernel(const uint16_t* __restrict__ gy, const float* __restrict__ gres,
+                const float* __restrict__ xo, const float* __restrict__ w,
+                const float* __restrict__ mean, const float* __restrict__ rstd,
+                float* __restrict__ dx, uint16_t* __restrict__ dxb, float* __restrict__ partial,
+                int rows, int C) {
+  __shared__ float sAcc[kWarpsPerBlock][128 * K];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int C4 = C >> 2;
+  const float invC = 1.0f / (float)C;
+  float4 dwAcc[K], dbAcc[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    dwAcc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    dbAcc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  const int stride = gridDim.x * kWarpsPerBlock;
+  for (int row = blockIdx.x * kWarpsPerBlock + warp; row < rows; row += stride) {
+    const size_t base = (size_t)row * C;
+    const float mu = mean[row], rs = rstd[row];
+    const uint2* gr = reinterpret_cast<const uint2*>(gy + base);
+    const float4* xr = reinterpret_cast<const float4*>(xo + base);
+    float4 g[K], xh[K];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const int i = lane + 32 * k;
+      if (i < C4) {
+        g[k] = bf4(gr[i]);
+        const float4 xv = xr[i];
+        xh[k] = make_float4((xv.x - mu) * rs, (xv.y - mu) * rs, (xv.z - mu) * rs,
+                            (xv.w - mu) * rs);
+        const float4 ww = w4[i];
+        const float4 gw = make_float4(g[k].x * ww.x, g[k].y * ww.y, g[k].z * ww.z, g[k].w * ww.w);
+        s1 += (gw.x + gw.y) + (gw.z + gw.w);
+        s2 += (gw.x * xh[k].x + gw.y * xh[k].y) + (gw.z * xh[k].z + gw.w * xh[k].w);
+        dwAcc[k].x += g[k].x * xh[k].x;
+        dwAcc[k].y += g[k].y * xh[k].y;
+        dwAcc[k].z += g[k].z * xh[k].z;
+        dwAcc[k].w += g[k].w * xh[k].w;
+        dbAcc[k].x += g[k].x;
+        dbAcc[k].y += g[k].y;
+        dbAcc[k].z += g[k].z;
+        dbAcc[k].w += g[k].w;
+      }
+    }
+    const float m1 = warpSum(s1) * invC, m2 = warpSum(s2) * invC;
+    const float4* rr = gres ? reinterpret_cast<const float4*>(gres + base) : nullptr;
+    float4* dr = reinterpret_cast<float4*>(dx + base);
+    uint2* dbr = dxb ? reinterpret_cast<uint2*>(dxb + base) : nullptr;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const int i = lane + 32 * k;
+      if (i < C4) {
+        const float4 ww = w4[i];
+        float4 o;
+        o.x = rs * (g[k].x * ww.x - m1 - xh[k].x * m2);
+        o.y = rs * (g[k].y * ww.y - m1 - xh[k].y * m2);
+        o.z = rs * (g[k].z * ww.z - m1 - xh[k].z * m2);
+        o.w = rs * (g[k].w * ww.w - m1 - xh[k].w * m2);
+        if (rr) {
+          const float4 r = rr[i];
+          o.x += r.x;
+          o.y += r.y;
+          o.z += r.z;
+          o.w += r.w;
+        }
+        dr[i] = o;
+        if (dbr) dbr[i] = tobf4(o);
+      }
+    }
+  }
+  // Combine the warps of this CTA, then write one partial row: dw first,
+  // then db, reusing one shared buffer.
+#pragma unroll
+  for (int pass = 0; pass < 2; ++pass) {
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const int i = lane + 32 * k;
+      if (i < C4) reinterpret_cast<float4*>(sAcc[warp])[i] = pass == 0 ? dwAcc[k] : dbAcc[k];
+    }
+    __syncthreads();
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+      float a = 0.f;
+#pragma unroll
+      for (int wv = 0; wv < kWarpsPerBlock; ++wv) a += sAcc[wv][c];
+      partial[(size_t)blockIdx.x * 2 * C + (size_t)pass * C + c] = a;
+    }
+    __syncthreads();
+  }
+}
+
+__global__ void reducePartials(const float* __restrict__ partial, float* __restrict__ dw,
+                               float* __restrict__ db, int nparts, int C) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= 2 * C) return;
+  float s = 0.f;
+  for (int p = 0; p < nparts; ++p) s += partial[(size_t)p * 2 * C + c];
+  if (c < C)
+    dw[c] = s;
+  else
+    db[c - C] = s;
+}
+
+template <int K>
+cudaError_t fwdK(const float* x, const uint16_t* d, const float* w, const float* b, float* xo,
+                 uint16_t* y, float* m, float* r, int rows, int C, float eps, cudaStream_t st) {
+  const int blocks = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock;
+  lnFwdKernel<K><<<blocks, kWarpsPerBlock * 32, 0, st>>>(x, d, w, b, xo, y, m, r, rows, C, eps);
+  return cudaGetLastError();
+}
+
+template <int K>
+cudaError_t bwdK(const uint16_t* gy, const float* gres, const float* xo, const float* w,
+                 const float* m, const float* r, float* dx, uint16_t* dxb, float* partial,
+                 int rows, int C, cudaStream_t st) {
+  int blocks = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock;
+  if (blocks > kPartialRows) blocks = kPartialRows;
+  lnBwdKernel<K><<<blocks, kWarpsPerBlock * 32, 0, st>>>(gy, gres, xo, w, m, r, dx, dxb, partial,
+                                                        rows, C);
+  return cudaGetLastError();
+}
+
+}  // namespace
+}  // namespace tnops
+
+using namespace tnops;
+
+extern "C" int tnops_ln_partial_rows(void) { return kPartialRows; }
+
+extern "C" int tnops_ln_fwd(const float* x, const uint16_t* delta, const float* w, const float* b,
+                            float* x_out, uint16_t* y, float* mean, float* rstd, int rows, int C,
+                            float eps, cudaStream_t stream) {
+  if (C % 4 != 0 || C > 128 * 16 || rows <= 0) return (int)cudaErrorInvalidValue;
+  const int K = (C + 127) / 128;
+  cudaError_t e;
+  switch (K) {
+    case 1: e = fwdK<1>(x, delta, w, b, x_out, y, mean, rstd, rows, C, eps, stream); break;
+    case 2: e = fwdK<2>(x, delta, w, b, x_out, y, mean, rstd, rows, C, eps, stream); break;
+    case 4: case 3: e = fwdK<4>(x, delta, w, b, x_out, y, mean, rstd, rows, C, eps, stream); break;
+    case 5: case 6: e = fwdK<6>(x, delta, w, b, x_out, y, mean, rstd, rows, C, eps, stream); break;
+    case 7: case 8: e = fwdK<8>(x, delta, w, b, x_out, y, mean, rstd, rows, C, eps, stream); break;
+    default: e = fwdK<16>(x, delta, w, b, x_out, y, mean, rstd, rows, C, eps, stream); break;
+  }
+  return launched(e);
+}
+
+extern "C" int tnops_ln_bwd(const uint16_t* gy, const float* g_res, const float* x_out,
+                            const float* w, const float* mean, const float* rstd, float* dx,
+                            uint16_t* dx_bf16, float* dw, float* db, float* partial, int rows,
+                            int C, cudaStream_t stream) {
+  if (C % 4 != 0 || C > 128 * 8 || rows <= 0) return (int)cudaErrorInvalidValue;
+  const int K = (C + 127) / 128;
+  cudaError_t e;
+  switch (K) {
+    case 1: e = bwdK<1>(gy, g_res, x_out, w, mean, rstd, dx, dx_bf16, partial, rows, C, stream); break;
+    case 2: e = bwdK<2>(gy, g_res, x_out, w, mean, rstd, dx, dx_bf16, partial, rows, C, stream); break;
+    case 3: case 4: e = bwdK<4>(gy, g_res, x_out, w, mean, rstd, dx, dx_bf16, partial, rows, C, stream); break;
+    case 5: case 6: e = bwdK<6>(gy, g_res, x_out, w, mean, rstd, dx, dx_bf16, partial, rows, C, stream); break;
+    default: e = bwdK<8>(gy, g_res, x_out, w, mean, rstd, dx, dx_bf16, partial, rows, C, stream); break;
+  }
+  if (launched(e) != 0) return (int)e;
+  int nparts = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock;
+  if (nparts > kPartialRows) nparts = kPartialRows;
+  reducePartials<<<(2 * C + 255) / 256, 256, 0, stream>>>(partial, dw, db, nparts, C);
+  return launched(cudaGetLastError());
+}

@@ -1,0 +1,67 @@
+// tnccl_ops.h - C launchers of the fused model kernels (libtnccl_ops.so).
+//
+// All launchers are asynchronous on `stream` and return a cudaError_t cast to
+// int (0 = success). Shapes are row-major [rows, cols]; bf16 tensors are
+// passed as raw 16-bit storage.
+#pragma once
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+// x_out = x + delta (delta optional, bf16); y = LayerNorm(x_out) * w + b in
+// bf16; mean/rstd saved in fp32. x, x_out fp32 [rows, C]; w, b fp32 [C].
+int tnops_ln_fwd(const float* x, const uint16_t* delta, const float* w, const float* b,
+                 float* x_out, uint16_t* y, float* mean, float* rstd, int rows, int C, float eps,
+                 cudaStream_t stream);
+
+// Backward of tnops_ln_fwd. gy bf16 [rows, C]; g_res fp32 [rows, C] (gradient
+// arriving through the residual stream; may be null = zeros); x_out, mean,
+// rstd from the forward. Writes dx fp32 = g_res + dLN/dx, optionally dx_bf16
+// (the same value for the bf16 `delta` input), and dw/db fp32 [C] (overwritten,
+// deterministic two-stage reduction through `partial`, which must hold
+// 2 * tnops_ln_partial_rows() * C floats).
+int tnops_ln_bwd(const uint16_t* gy, const float* g_res, const float* x_out, const float* w,
+                 const float* mean, const float* rstd, float* dx, uint16_t* dx_bf16, float* dw,
+                 float* db, float* partial, int rows, int C, cudaStream_t stream);
+int tnops_ln_partial_rows(void);
+
+// Fused softmax cross-entropy over bf16 logits [rows, V]: loss[r] =
+// logsumexp(logits[r]) - logits[r, target[r]] (fp32), and logits is
+// overwritten in place with d(mean loss)/d(logits) = (softmax - onehot)/rows
+// in bf16. Rows whose target is negative are ignored (zero loss and gradient);
+// `valid` counts the rows that are not, for the mean.
+int tnops_cross_entropy_fwd_bwd(uint16_t* logits, const int64_t* target, float* loss, int rows,
+                                int V, int valid, cudaStream_t stream);
+
+// Multiplies a bf16 tensor by the fp32 scalar *scale (device memory); no-op
+// on the device when *scale == 1.
+int tnops_scale_bf16(uint16_t* x, size_t n, const float* scale, cudaStream_t stream);
+
+// Multi-tensor AdamW step (decoupled weight decay) over up to 64 tensors per
+// call: p -= lr * (m_hat / (sqrt(v_hat) + eps) + wd * p). grads may be scaled
+// by grad_scale first. bias corrections are computed from `step` (>= 1).
+typedef struct {
+  int n;
+  float* param[64];
+  const float* grad[64];
+  float* exp_avg[64];
+  float* exp_avg_sq[64];
+  int64_t numel[64];
+  float weight_decay[64];
+} tnops_adamw_list;
+
+int tnops_adamw(const tnops_adamw_list* list, float lr, float beta1, float beta2, float eps,
+                int64_t step, float grad_scale, cudaStream_t stream);
+
+// Number of kernels the ops library launched in this process.
+unsigned long long tnops_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif

@@ -74,9 +74,10 @@ __device__ __forceinline__ void stElem(T* p, float x) {
 
 // dst[i] = (scale ? alpha*src[i] : src[i]) for every destination returned by
 // dstPtr(d), d < ndst. Loads are issued U at a time before any store.
-template <typename T, int LD, int U, typename DstF>
-__device__ __forceinline__ void copyOut(const T* src, uint64_t n, bool vec, bool scale,
-                                        float alpha, int ndst, DstF dstPtr) {
+template <typename T, int LD, int U, bool SCALE, typename DstF>
+__device__ __forceinline__ void copyOutImpl(const T* src, uint64_t n, bool vec, float alpha,
+                                            int ndst, DstF dstPtr) {
+  constexpr bool scale = SCALE;
   using Pk = Pack<T>;
   constexpr int V = Pk::V;
   const uint64_t NT = blockDim.x;
@@ -110,6 +111,17 @@ __device__ __forceinline__ void copyOut(const T* src, uint64_t n, bool vec, bool
     if (scale) f = scaled(alpha, f);
     for (int d = 0; d < ndst; ++d) stElem(reinterpret_cast<T*>(dstPtr(d)) + e, f);
   }
+}
+
+// Pure copies keep 8 loads in flight per thread; scaled copies convert
+// through fp32 and keep 4 (register budget of a 512-thread CTA).
+template <typename T, int LD, int U, typename DstF>
+__device__ __forceinline__ void copyOut(const T* src, uint64_t n, bool vec, bool scale,
+                                        float alpha, int ndst, DstF dstPtr) {
+  if (scale)
+    copyOutImpl<T, LD, (U > 4 ? 4 : U), true>(src, n, vec, alpha, ndst, dstPtr);
+  else
+    copyOutImpl<T, LD, U, false>(src, n, vec, alpha, ndst, dstPtr);
 }
 
 // out[i] = sum_{k<P} alpha * src_k[i] in rank order, fp32 accumulation.
@@ -208,20 +220,23 @@ __device__ __forceinline__ void ringHop(uint64_t n, bool vec, const T* in, const
 }
 
 // ---------------------------------------------------------------------------
-// Two-shot
+// Two-shot, software-pipelined over two slots per channel:
 //
-// Slot reuse without credits (one slot per channel): rank r writes tile n+1
-// into rank j's reduce-scatter area only after it received j's all-gather
-// data for tile n, which j sends after it finished reading that area. Rank j
-// writes tile n+1 into r's all-gather area only after it received r's
-// reduce-scatter data for tile n+1, which r sends after it finished copying
-// tile n out of that area.
+//   push RS(0); publish RS(0)
+//   for n: wait RS(n); reduce n -> y and push AG(n); publish AG(n)
+//          push RS(n+1); publish RS(n+1)        <- overlaps peers' AG(n)
+//          wait AG(n); copy AG(n) out
+//
+// Slot reuse needs no credit words. Rank r writes RS(n+2) into slot n%2 of
+// rank j only after it waited for j's AG(n), which j publishes after it
+// finished reading RS(n). Rank j writes AG(n+2) into slot n%2 of rank r only
+// after it received r's RS(n+2), which r pushes after it copied AG(n) out.
 // ---------------------------------------------------------------------------
 template <typename T, int MAXP>
 __global__ void __launch_bounds__(kMaxThreads)
     twoShotKernel(const __grid_constant__ DevComm comm, const __grid_constant__ AllReduceArgs a) {
   constexpr int V = Pack<T>::V;
-  constexpr int U = 1;
+  constexpr int U = MAXP <= 2 ? 4 : MAXP <= 4 ? 2 : 1;
   const int c = blockIdx.x, tid = threadIdx.x, P = comm.nranks, r = comm.rank;
   const MailboxLayout& L = comm.layout;
   char* const me = comm.peers[r];
@@ -231,34 +246,50 @@ __global__ void __launch_bounds__(kMaxThreads)
   const bool vec = a.vectorized != 0;
   __shared__ int sFail;
   if (tid == 0) sFail = 0;
-  uint64_t seq = comm.counters[kCounterTwoShot * kMaxChannels + c];
+  const uint64_t seq0 = comm.counters[kCounterTwoShot * kMaxChannels + c];
   __syncthreads();
   const uint64_t ntiles = channelTiles(pl.numTiles, pl.channels, c);
-  for (uint64_t t = 0; t < ntiles; ++t) {
-    const uint64_t tile = (uint64_t)c + t * (uint64_t)pl.channels;
-    const uint64_t want = seq + 1;
-    // 1. reduce-scatter push: chunk j of my input -> rank j (raw, unscaled).
+  auto tileOf = [&](uint64_t t) { return (uint64_t)c + t * (uint64_t)pl.channels; };
+  auto slotOf = [&](uint64_t t) { return (int)((seq0 + t) % kTwoShotSlots); };
+
+  // Reduce-scatter push of local tile t: chunk j of my input -> rank j.
+  auto pushRS = [&](uint64_t t) {
+    const uint64_t tile = tileOf(t);
+    const int slot = slotOf(t);
     for (int k = 1; k < P; ++k) {
       const int j = (r + k) % P;
       const Span sp = chunkSpan(pl, tile, j, V);
-      char* dst = comm.peers[j] + tsRsDataAt(L, c, r);
-      copyOut<T, kLdInput, 4>(x + sp.offset, sp.count, vec, false, 1.f, 1,
+      char* dst = comm.peers[j] + tsRsDataAt(L, c, slot, r);
+      copyOut<T, kLdInput, 8>(x + sp.offset, sp.count, vec, false, 1.f, 1,
                               [dst](int) { return dst; });
     }
     __syncthreads();
-    if (tid < P && tid != r) stReleaseSys(flagPtr(comm.peers[tid], tsRsFlagAt(L, c, r)), want);
-    if (tid < P && tid != r &&
-        !waitFlag(comm, flagPtr(me, tsRsFlagAt(L, c, tid)), want,
-                  whereCode(kCounterTwoShot, c, 1)))
-      sFail = 1;
+    if (tid < P && tid != r)
+      stReleaseSys(flagPtr(comm.peers[tid], tsRsFlagAt(L, c, slot, r)), seq0 + t + 1);
+  };
+  auto waitAll = [&](bool ag, uint64_t t, int phase) -> bool {
+    const int slot = slotOf(t);
+    if (tid < P && tid != r) {
+      const uint64_t off = ag ? tsAgFlagAt(L, c, slot, tid) : tsRsFlagAt(L, c, slot, tid);
+      if (!waitFlag(comm, flagPtr(me, off), seq0 + t + 1, whereCode(kCounterTwoShot, c, phase)))
+        sFail = 1;
+    }
     __syncthreads();
-    if (sFail) break;
-    // 2. reduce my chunk in rank order, store it locally and push it to all.
+    return sFail == 0;
+  };
+
+  if (ntiles > 0) pushRS(0);
+  uint64_t done = 0;
+  for (uint64_t t = 0; t < ntiles; ++t) {
+    if (!waitAll(false, t, 1)) break;
+    const uint64_t tile = tileOf(t);
+    const int slot = slotOf(t);
+    // Reduce my chunk in rank order, store it locally and push it to all.
     const Span own = chunkSpan(pl, tile, r, V);
-    const uint64_t agOff = tsAgDataAt(L, c, r);
+    const uint64_t agOff = tsAgDataAt(L, c, slot, r);
     reduceRanks<T, MAXP, U>(
         own.count, vec, P, r, x + own.offset, a.scale,
-        [&](int k) { return me + tsRsDataAt(L, c, k); },
+        [&](int k) { return me + tsRsDataAt(L, c, slot, k); },
         [&](uint64_t i, uint4 v) {
           st16(reinterpret_cast<uint4*>(y + own.offset) + i, v);
           for (int k = 1; k < P; ++k) {
@@ -274,24 +305,24 @@ __global__ void __launch_bounds__(kMaxThreads)
           }
         });
     __syncthreads();
-    if (tid < P && tid != r) stReleaseSys(flagPtr(comm.peers[tid], tsAgFlagAt(L, c, r)), want);
-    if (tid < P && tid != r &&
-        !waitFlag(comm, flagPtr(me, tsAgFlagAt(L, c, tid)), want,
-                  whereCode(kCounterTwoShot, c, 2)))
-      sFail = 1;
-    __syncthreads();
-    if (sFail) break;
-    // 3. copy every peer's reduced chunk out.
+    if (tid < P && tid != r)
+      stReleaseSys(flagPtr(comm.peers[tid], tsAgFlagAt(L, c, slot, r)), seq0 + t + 1);
+    // Start the next tile's reduce-scatter while the peers finish this one.
+    if (t + 1 < ntiles) pushRS(t + 1);
+    if (!waitAll(true, t, 2)) break;
+    // Copy every peer's reduced chunk out.
     for (int k = 1; k < P; ++k) {
       const int j = (r + P - k) % P;
       const Span sp = chunkSpan(pl, tile, j, V);
       T* dst = y + sp.offset;
-      copyOut<T, kLdMailbox, 4>(reinterpret_cast<const T*>(me + tsAgDataAt(L, c, j)), sp.count,
-                                vec, false, 1.f, 1, [dst](int) { return dst; });
+      copyOut<T, kLdMailbox, 8>(reinterpret_cast<const T*>(me + tsAgDataAt(L, c, slot, j)),
+                                sp.count, vec, false, 1.f, 1, [dst](int) { return dst; });
     }
-    ++seq;
+    done = t + 1;
   }
-  if (tid == 0 && !sFail) comm.counters[kCounterTwoShot * kMaxChannels + c] = seq;
+  // Every thread has passed the final barrier of the loop (or broke out on
+  // a failure seen by all), so thread 0 can record the new sequence number.
+  if (tid == 0 && !sFail) comm.counters[kCounterTwoShot * kMaxChannels + c] = seq0 + done;
 }
 
 // ---------------------------------------------------------------------------
@@ -302,7 +333,7 @@ template <typename T, int MAXP>
 __global__ void __launch_bounds__(kMaxThreads)
     oneShotKernel(const __grid_constant__ DevComm comm, const __grid_constant__ AllReduceArgs a) {
   constexpr int V = Pack<T>::V;
-  constexpr int U = 1;
+  constexpr int U = MAXP <= 2 ? 4 : MAXP <= 4 ? 2 : 1;
   const int c = blockIdx.x, tid = threadIdx.x, P = comm.nranks, r = comm.rank;
   const MailboxLayout& L = comm.layout;
   const int S = L.osSlots;
@@ -329,7 +360,7 @@ __global__ void __launch_bounds__(kMaxThreads)
     __syncthreads();
     if (sFail) break;
     const uint64_t dataOff = osDataAt(L, c, s, r);
-    copyOut<T, kLdInput, 4>(x + sp.offset, sp.count, vec, false, 1.f, P - 1, [&](int d) {
+    copyOut<T, kLdInput, 8>(x + sp.offset, sp.count, vec, false, 1.f, P - 1, [&](int d) {
       return comm.peers[(r + 1 + d) % P] + dataOff;
     });
     __syncthreads();
@@ -445,7 +476,7 @@ __global__ void __launch_bounds__(kMaxThreads)
       const Span sp = chunkSpan(pl, tile, ringChunkBehind(r, 1, P), V);
       if (!acquire(false, true, 1)) break;
       char* out = ch.outSlot(ch.sendT);
-      copyOut<T, kLdInput, 4>(x + sp.offset, sp.count, vec, scale, alpha, 1,
+      copyOut<T, kLdInput, 8>(x + sp.offset, sp.count, vec, scale, alpha, 1,
                               [out](int) { return out; });
       finish(false, true);
     }
@@ -489,7 +520,7 @@ __global__ void __launch_bounds__(kMaxThreads)
       const T* in = ch.inSlot(ch.recvT);
       char* out = ch.outSlot(ch.sendT);
       T* yo = y + sp.offset;
-      copyOut<T, kLdMailbox, 4>(in, sp.count, vec, false, 1.f, 2, [&](int k) {
+      copyOut<T, kLdMailbox, 8>(in, sp.count, vec, false, 1.f, 2, [&](int k) {
         return k == 0 ? reinterpret_cast<char*>(yo) : out;
       });
       finish(true, true);
@@ -499,7 +530,7 @@ __global__ void __launch_bounds__(kMaxThreads)
       const Span sp = chunkSpan(pl, tile, ringChunkBehind(r, P - 1, P), V);
       if (!acquire(true, false, 5)) break;
       T* yo = y + sp.offset;
-      copyOut<T, kLdMailbox, 4>(ch.inSlot(ch.recvT), sp.count, vec, false, 1.f, 1,
+      copyOut<T, kLdMailbox, 8>(ch.inSlot(ch.recvT), sp.count, vec, false, 1.f, 1,
                                 [yo](int) { return reinterpret_cast<char*>(yo); });
       finish(true, false);
     }
@@ -552,7 +583,7 @@ __global__ void __launch_bounds__(kMaxThreads)
     const uint64_t tile = (uint64_t)c + t * (uint64_t)pl.channels;
     const Span sp = blockTileSpan(pl, tile);
     const uint64_t want = seq + 1;
-    copyOut<T, kLdInput, 4>(x + sp.offset, sp.count, vec, false, 1.f, 1,
+    copyOut<T, kLdInput, 8>(x + sp.offset, sp.count, vec, false, 1.f, 1,
                             [ucIn](int) { return ucIn; });
     if (!barrier(0, want)) break;
     // Reduce this rank's share (whole vectors; padding past the tile end is
@@ -560,15 +591,16 @@ __global__ void __launch_bounds__(kMaxThreads)
     const uint64_t nvecTile = divUp(sp.count, V);
     const Span share = blockShare(nvecTile, P, r, 1);
     const uint64_t NT = blockDim.x;
-    for (uint64_t base = tid; base < share.count; base += NT * 2) {
-      uint4 v[2];
+    constexpr int UN = 4;  // switch reductions in flight per thread
+    for (uint64_t base = tid; base < share.count; base += NT * UN) {
+      uint4 v[UN];
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
+      for (int u = 0; u < UN; ++u) {
         const uint64_t i = share.offset + base + u * NT;
         if (base + u * NT < share.count) v[u] = Multimem<T>::ldReduce(mcIn + i * 16);
       }
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
+      for (int u = 0; u < UN; ++u) {
         const uint64_t i = share.offset + base + u * NT;
         if (base + u * NT < share.count) {
           uint4 w = v[u];
@@ -585,7 +617,7 @@ __global__ void __launch_bounds__(kMaxThreads)
     }
     if (!barrier(1, want)) break;
     T* yo = y + sp.offset;
-    copyOut<T, kLdMailbox, 4>(reinterpret_cast<const T*>(ucOut), sp.count, vec, false, 1.f, 1,
+    copyOut<T, kLdMailbox, 8>(reinterpret_cast<const T*>(ucOut), sp.count, vec, false, 1.f, 1,
                               [yo](int) { return reinterpret_cast<char*>(yo); });
     ++seq;
   }
@@ -624,13 +656,21 @@ cudaError_t launchTyped(const DevComm& comm, const AllReduceArgs& a, int algo, i
       ringKernel<T><<<a.chunk.channels, block, 0, stream>>>(comm, a);
       break;
     case TNCCL_ALGO_TWOSHOT:
-      if (comm.nranks <= 8)
+      if (comm.nranks <= 2)
+        twoShotKernel<T, 2><<<a.chunk.channels, block, 0, stream>>>(comm, a);
+      else if (comm.nranks <= 4)
+        twoShotKernel<T, 4><<<a.chunk.channels, block, 0, stream>>>(comm, a);
+      else if (comm.nranks <= 8)
         twoShotKernel<T, 8><<<a.chunk.channels, block, 0, stream>>>(comm, a);
       else
         twoShotKernel<T, 16><<<a.chunk.channels, block, 0, stream>>>(comm, a);
       break;
     case TNCCL_ALGO_ONESHOT:
-      if (comm.nranks <= 8)
+      if (comm.nranks <= 2)
+        oneShotKernel<T, 2><<<a.block.channels, block, 0, stream>>>(comm, a);
+      else if (comm.nranks <= 4)
+        oneShotKernel<T, 4><<<a.block.channels, block, 0, stream>>>(comm, a);
+      else if (comm.nranks <= 8)
         oneShotKernel<T, 8><<<a.block.channels, block, 0, stream>>>(comm, a);
       else
         oneShotKernel<T, 16><<<a.block.channels, block, 0, stream>>>(comm, a);

@@ -1,5 +1,7 @@
 #include "common.h"
 
+#include "protocol.h"
+
 #include <string.h>
 #include <strings.h>
 #include <unistd.h>
@@ -67,15 +69,15 @@ static int64_t roundTo16(int64_t v) { return v < 16 ? 16 : (v + 15) / 16 * 16; }
 
 Config loadConfig() {
   Config c{};
-  c.channels = clampInt(envInt("TNCCL_NCHANNELS", 32), 1, 64);
-  c.osChannels = clampInt(envInt("TNCCL_ONESHOT_CHANNELS", 16), 1, 64);
+  c.channels = clampInt(envInt("TNCCL_NCHANNELS", 64), 1, kMaxChannels);
+  c.osChannels = clampInt(envInt("TNCCL_ONESHOT_CHANNELS", 16), 1, kMaxChannels);
   c.ringSlots = clampInt(envInt("TNCCL_SLOTS", 4), 2, 16);
-  c.ringChunkBytes = roundTo16(envInt("TNCCL_CHUNK_BYTES", 64 << 10));
-  c.tsChunkBytes = roundTo16(envInt("TNCCL_TWOSHOT_CHUNK_BYTES", 32 << 10));
+  c.ringChunkBytes = roundTo16(envInt("TNCCL_CHUNK_BYTES", 256 << 10));
+  c.tsChunkBytes = roundTo16(envInt("TNCCL_TWOSHOT_CHUNK_BYTES", 128 << 10));
   c.osSlots = clampInt(envInt("TNCCL_ONESHOT_SLOTS", 2), 1, 8);
   c.osTileBytes = roundTo16(envInt("TNCCL_ONESHOT_TILE_BYTES", 32 << 10));
-  c.nvlsChannels = clampInt(envInt("TNCCL_NVLS_CHANNELS", 32), 1, 64);
-  c.nvlsTileBytes = roundTo16(envInt("TNCCL_NVLS_TILE_BYTES", 128 << 10));
+  c.nvlsChannels = clampInt(envInt("TNCCL_NVLS_CHANNELS", 64), 1, kMaxChannels);
+  c.nvlsTileBytes = roundTo16(envInt("TNCCL_NVLS_TILE_BYTES", 256 << 10));
   c.nvlsEnable = (int)envInt("TNCCL_NVLS_ENABLE", 1);
   int algo = parseAlgo(envStr("TNCCL_ALGO", "auto"));
   if (algo < 0) {
@@ -87,7 +89,7 @@ Config loadConfig() {
   if (c.timeoutMs < 1) c.timeoutMs = 1;
   c.bootstrapTimeoutMs = envInt("TNCCL_BOOTSTRAP_TIMEOUT_MS", 30000);
   if (c.bootstrapTimeoutMs < 1) c.bootstrapTimeoutMs = 1;
-  c.threads = clampInt(envInt("TNCCL_NTHREADS", 512), 64, 1024) / 32 * 32;
+  c.threads = clampInt(envInt("TNCCL_NTHREADS", 512), 64, 512) / 32 * 32;
   c.useCuMem = (int)envInt("TNCCL_CUMEM_ENABLE", 1);
   c.oneShotMaxBytes = envInt("TNCCL_ONESHOT_MAX_BYTES", 0);
   c.nvlsMinBytes = envInt("TNCCL_NVLS_MIN_BYTES", 0);

@@ -51,7 +51,7 @@ __device__ __forceinline__ int whereCode(int family, int channel, int phase) {
   return (family << 24) | (channel << 8) | phase;
 }
 
-__device__ __noinline__ void recordFailure(const DevComm& comm, int code, int where,
+static __device__ __noinline__ void recordFailure(const DevComm& comm, int code, int where,
                                            uint64_t expected, uint64_t observed) {
   DevStatus* s = comm.status;
   if (s->error == 0) {
@@ -67,7 +67,7 @@ __device__ __noinline__ void recordFailure(const DevComm& comm, int code, int wh
 // an error raised elsewhere, the wall-clock bound (globaltimer) and an
 // iteration bound; any of them ends the wait with false. The code TNCCL_TIMEOUT
 // (5) or TNCCL_ABORTED (6) is recorded in the host-mapped status block.
-__device__ __noinline__ bool waitSlow(const DevComm& comm, const uint64_t* flag,
+static __device__ __noinline__ bool waitSlow(const DevComm& comm, const uint64_t* flag,
                                       uint64_t target, int where) {
   const uint64_t start = globalTimerNs();
   const uint64_t maxPolls = comm.timeoutNs / 16 + 4096;  // polls take >= 16 ns

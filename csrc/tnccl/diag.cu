@@ -1,0 +1,126 @@
+// diag.cu - NVLink / HBM primitive micro-benchmarks used to size the
+// collective kernels (tncclDiagBench in diag.h). Each mode moves `bytes`
+// between this rank's mailbox and the next rank's mailbox with `ctas` CTAs of
+// `threads` threads and `unroll` 16-byte accesses in flight per thread:
+//   0 push   : weak 16-byte stores into the peer's mailbox
+//   1 pull   : 16-byte loads from the peer's mailbox (summed so they count)
+//   2 push+flag: push in `chunk`-byte pieces, each followed by bar.sync and a
+//              st.release.sys flag to the peer (the cost of publishing)
+//   3 local  : copy within this rank's mailbox
+// The caller runs the same mode on every rank at the same time; no kernel
+// waits on another rank, so there is nothing to time out.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "comm.h"
+#include "device.cuh"
+#include "diag.h"
+
+namespace tnccl {
+namespace {
+
+using namespace dev;
+
+template <int U>
+__global__ void diagKernel(char* local, char* peer, uint64_t bytes, int mode, uint64_t chunk,
+                           uint64_t* peerFlag, unsigned* sink) {
+  const uint64_t per = bytes / gridDim.x / 16 * 16;
+  const uint64_t base = per * blockIdx.x;
+  const uint64_t nvec = per / 16;
+  const uint64_t NT = blockDim.x;
+  uint32_t acc = 0;
+  if (mode == 2) {
+    const uint64_t cvec = chunk / 16;
+    uint64_t seq = 0;
+    for (uint64_t c0 = 0; c0 < nvec; c0 += cvec) {
+      const uint64_t c1 = c0 + cvec < nvec ? c0 + cvec : nvec;
+      for (uint64_t i = c0 + threadIdx.x; i < c1; i += NT) {
+        uint4 v = make_uint4((uint32_t)i, 1, 2, 3);
+        st16(peer + base + i * 16, v);
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) stReleaseSys(peerFlag + blockIdx.x, ++seq);
+    }
+  } else {
+    for (uint64_t b = threadIdx.x; b < nvec; b += NT * U) {
+      uint4 v[U];
+      if (mode == 0) {
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const uint64_t i = b + u * NT;
+          if (i < nvec) st16(peer + base + i * 16, make_uint4((uint32_t)i, 1, 2, 3));
+        }
+        continue;
+      }
+      char* src = mode == 1 ? peer : local;
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const uint64_t i = b + u * NT;
+        if (i < nvec) v[u] = ldMailbox(src + base + i * 16);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const uint64_t i = b + u * NT;
+        if (i < nvec) {
+          if (mode == 1)
+            acc += v[u].x ^ v[u].w;
+          else
+            st16(local + bytes + base + i * 16, v[u]);
+        }
+      }
+    }
+  }
+  if (acc == 0x12345678u) *sink = acc;
+}
+
+}  // namespace
+}  // namespace tnccl
+
+using namespace tnccl;
+
+extern "C" tncclResult tncclDiagBench(tncclComm_t comm, int mode, size_t bytes, int ctas,
+                                      int threads, int unroll, size_t chunk, int iters,
+                                      cudaStream_t stream, float* msPerIter) {
+  if (comm == nullptr || msPerIter == nullptr || comm->nranks < 2 || ctas < 1 || threads < 32 ||
+      threads > 1024 || iters < 1)
+    return TNCCL_INVALID_ARGUMENT;
+  const int next = (comm->rank + 1) % comm->nranks;
+  // Use the ring data area (and, for mode 3, its second half as destination).
+  const size_t area = (size_t)comm->layout.channels *
+                                                     comm->layout.ringSlots *
+                                                     comm->layout.ringChunkBytes;
+  if (bytes == 0 || bytes * (mode == 3 ? 2 : 1) > area) return TNCCL_INVALID_ARGUMENT;
+  char* local = comm->local.base + comm->layout.ringDataOff;
+  char* peer = comm->dev.peers[next] + comm->layout.ringDataOff;
+  // Flag words and the sink live in the scratch area after the payload, so
+  // no FIFO sequence word is touched.
+  const size_t tail = (bytes * (mode == 3 ? 2 : 1) + 255) / 256 * 256;
+  if (tail + 8 * (size_t)ctas + 256 > area) return TNCCL_INVALID_ARGUMENT;
+  uint64_t* flag = reinterpret_cast<uint64_t*>(peer + tail);
+  unsigned* sink = reinterpret_cast<unsigned*>(local + tail + 8 * (size_t)ctas);
+  cudaEvent_t e0, e1;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  auto launch = [&]() {
+    switch (unroll) {
+      case 1: diagKernel<1><<<ctas, threads, 0, stream>>>(local, peer, bytes, mode, chunk, flag, sink); break;
+      case 2: diagKernel<2><<<ctas, threads, 0, stream>>>(local, peer, bytes, mode, chunk, flag, sink); break;
+      case 8: diagKernel<8><<<ctas, threads, 0, stream>>>(local, peer, bytes, mode, chunk, flag, sink); break;
+      case 16: diagKernel<16><<<ctas, threads, 0, stream>>>(local, peer, bytes, mode, chunk, flag, sink); break;
+      default: diagKernel<4><<<ctas, threads, 0, stream>>>(local, peer, bytes, mode, chunk, flag, sink); break;
+    }
+  };
+  launch();
+  cudaEventRecord(e0, stream);
+  for (int i = 0; i < iters; ++i) launch();
+  cudaEventRecord(e1, stream);
+  cudaError_t err = cudaEventSynchronize(e1);
+  float ms = 0.f;
+  if (err == cudaSuccess) err = cudaEventElapsedTime(&ms, e0, e1);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  gLaunchCount.fetch_add((unsigned long long)iters + 1, std::memory_order_relaxed);
+  if (err != cudaSuccess) return TNCCL_CUDA_ERROR;
+  *msPerIter = ms / (float)iters;
+  return TNCCL_SUCCESS;
+}

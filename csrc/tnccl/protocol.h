@@ -30,7 +30,7 @@
 namespace tnccl {
 
 constexpr int kMaxRanks = 16;
-constexpr int kMaxChannels = 64;
+constexpr int kMaxChannels = 128;
 constexpr int kVectorBytes = 16;
 // Smallest chunk (bytes) the planners use, so that small messages occupy few
 // channels instead of many nearly empty ones.
@@ -38,6 +38,8 @@ constexpr uint64_t kRingMinChunkBytes = 4096;
 constexpr uint64_t kTwoShotMinChunkBytes = 2048;
 constexpr uint64_t kOneShotMinTileBytes = 4096;
 constexpr uint64_t kNvlsMinTileBytes = 16384;
+// Two-shot keeps two tiles in flight per channel.
+constexpr int kTwoShotSlots = 2;
 
 // Counter families kept in device memory, one array of kMaxChannels each.
 enum CounterFamily : int {
@@ -186,7 +188,9 @@ struct MailboxLayout {
   uint64_t ringChunkBytes;
   uint64_t ringDataOff, ringReadyOff, ringCreditOff;
 
-  // two-shot: per channel, P reduce-scatter chunks + P all-gather chunks.
+  // two-shot: per channel and slot, P reduce-scatter chunks + P all-gather
+  // chunks (two slots so that one tile's all-gather overlaps the next
+  // tile's reduce-scatter).
   uint64_t tsChunkBytes;
   uint64_t tsRsDataOff, tsAgDataOff, tsRsFlagOff, tsAgFlagOff;
 
@@ -235,9 +239,9 @@ inline MailboxLayout makeLayout(const LayoutConfig& c) {
   off += C * (uint64_t)c.ringSlots * c.ringChunkBytes;
   off = alignUp(off, 4096);
   L.tsRsDataOff = off;
-  off += C * P * c.tsChunkBytes;
+  off += C * kTwoShotSlots * P * c.tsChunkBytes;
   L.tsAgDataOff = off;
-  off += C * P * c.tsChunkBytes;
+  off += C * kTwoShotSlots * P * c.tsChunkBytes;
   off = alignUp(off, 4096);
   L.osDataOff = off;
   off += (uint64_t)c.osChannels * (uint64_t)c.osSlots * P * c.osTileBytes;
@@ -248,9 +252,9 @@ inline MailboxLayout makeLayout(const LayoutConfig& c) {
   L.ringCreditOff = off;
   off = alignUp(off + C * (uint64_t)c.ringSlots * 8, 128);
   L.tsRsFlagOff = off;
-  off = alignUp(off + C * P * 8, 128);
+  off = alignUp(off + C * kTwoShotSlots * P * 8, 128);
   L.tsAgFlagOff = off;
-  off = alignUp(off + C * P * 8, 128);
+  off = alignUp(off + C * kTwoShotSlots * P * 8, 128);
   L.osFlagOff = off;
   off = alignUp(off + (uint64_t)c.osChannels * (uint64_t)c.osSlots * P * 8, 128);
   L.osAckOff = off;
@@ -271,17 +275,20 @@ TN_HD uint64_t ringReadyAt(const MailboxLayout& L, int c, int s) {
 TN_HD uint64_t ringCreditAt(const MailboxLayout& L, int c, int s) {
   return L.ringCreditOff + ((uint64_t)c * L.ringSlots + s) * 8;
 }
-TN_HD uint64_t tsRsDataAt(const MailboxLayout& L, int c, int src) {
-  return L.tsRsDataOff + ((uint64_t)c * L.nranks + src) * L.tsChunkBytes;
+TN_HD uint64_t tsSlotIndex(const MailboxLayout& L, int c, int slot, int src) {
+  return ((uint64_t)c * kTwoShotSlots + (uint64_t)slot) * L.nranks + src;
 }
-TN_HD uint64_t tsAgDataAt(const MailboxLayout& L, int c, int src) {
-  return L.tsAgDataOff + ((uint64_t)c * L.nranks + src) * L.tsChunkBytes;
+TN_HD uint64_t tsRsDataAt(const MailboxLayout& L, int c, int slot, int src) {
+  return L.tsRsDataOff + tsSlotIndex(L, c, slot, src) * L.tsChunkBytes;
 }
-TN_HD uint64_t tsRsFlagAt(const MailboxLayout& L, int c, int src) {
-  return L.tsRsFlagOff + ((uint64_t)c * L.nranks + src) * 8;
+TN_HD uint64_t tsAgDataAt(const MailboxLayout& L, int c, int slot, int src) {
+  return L.tsAgDataOff + tsSlotIndex(L, c, slot, src) * L.tsChunkBytes;
 }
-TN_HD uint64_t tsAgFlagAt(const MailboxLayout& L, int c, int src) {
-  return L.tsAgFlagOff + ((uint64_t)c * L.nranks + src) * 8;
+TN_HD uint64_t tsRsFlagAt(const MailboxLayout& L, int c, int slot, int src) {
+  return L.tsRsFlagOff + tsSlotIndex(L, c, slot, src) * 8;
+}
+TN_HD uint64_t tsAgFlagAt(const MailboxLayout& L, int c, int slot, int src) {
+  return L.tsAgFlagOff + tsSlotIndex(L, c, slot, src) * 8;
 }
 TN_HD uint64_t osDataAt(const MailboxLayout& L, int c, int s, int src) {
   return L.osDataOff +

@@ -1,0 +1,149 @@
+// ops_ext.cpp - PyTorch binding of the model kernels (csrc/ops). Each entry
+// validates its tensors and calls the C launcher on the current CUDA stream;
+// a launcher error raises instead of falling back to another implementation.
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+#include <torch/extension.h>
+
+#include <vector>
+
+#include "tnccl_ops.h"
+
+namespace py = pybind11;
+
+namespace {
+
+cudaStream_t streamOf(const at::Tensor& t) {
+  return c10::cuda::getCurrentCUDAStream(t.get_device()).stream();
+}
+
+void need(const at::Tensor& t, at::ScalarType st, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+  TORCH_CHECK(t.scalar_type() == st, name, " has dtype ", t.scalar_type(), ", expected ", st);
+}
+
+void ok(int rc, const char* what) {
+  TORCH_CHECK(rc == 0, what, " failed: ", cudaGetErrorString((cudaError_t)rc));
+}
+
+uint16_t* bf(at::Tensor& t) { return reinterpret_cast<uint16_t*>(t.data_ptr()); }
+const uint16_t* bf(const at::Tensor& t) { return reinterpret_cast<const uint16_t*>(t.data_ptr()); }
+
+// x fp32 [rows, C], optional delta bf16 [rows, C] -> x_out, y (bf16), mean, rstd
+std::vector<at::Tensor> lnFwd(const at::Tensor& x, const c10::optional<at::Tensor>& delta,
+                              const at::Tensor& w, const at::Tensor& b, double eps) {
+  need(x, at::kFloat, "x");
+  need(w, at::kFloat, "weight");
+  need(b, at::kFloat, "bias");
+  const int64_t C = x.size(-1);
+  const int64_t rows = x.numel() / C;
+  TORCH_CHECK(w.numel() == C && b.numel() == C, "LayerNorm parameters must have C elements");
+  if (delta) {
+    need(*delta, at::kBFloat16, "delta");
+    TORCH_CHECK(delta->numel() == x.numel(), "delta must match x");
+  }
+  c10::cuda::CUDAGuard g(x.device());
+  auto xo = at::empty_like(x);
+  auto y = at::empty(x.sizes(), x.options().dtype(at::kBFloat16));
+  auto mean = at::empty({rows}, x.options());
+  auto rstd = at::empty({rows}, x.options());
+  ok(tnops_ln_fwd(x.data_ptr<float>(), delta ? bf(*delta) : nullptr, w.data_ptr<float>(),
+                  b.data_ptr<float>(), xo.data_ptr<float>(), bf(y), mean.data_ptr<float>(),
+                  rstd.data_ptr<float>(), (int)rows, (int)C, (float)eps, streamOf(x)),
+     "tnops_ln_fwd");
+  return {xo, y, mean, rstd};
+}
+
+std::vector<at::Tensor> lnBwd(const at::Tensor& gy, const c10::optional<at::Tensor>& gres,
+                              const at::Tensor& xo, const at::Tensor& w, const at::Tensor& mean,
+                              const at::Tensor& rstd, bool wantBf16) {
+  need(gy, at::kBFloat16, "grad_y");
+  need(xo, at::kFloat, "x_out");
+  need(w, at::kFloat, "weight");
+  if (gres) need(*gres, at::kFloat, "grad_residual");
+  const int64_t C = xo.size(-1);
+  const int64_t rows = xo.numel() / C;
+  c10::cuda::CUDAGuard g(xo.device());
+  auto dx = at::empty_like(xo);
+  at::Tensor dxb;
+  if (wantBf16) dxb = at::empty(xo.sizes(), xo.options().dtype(at::kBFloat16));
+  auto dw = at::empty({C}, xo.options());
+  auto db = at::empty({C}, xo.options());
+  auto partial = at::empty({(int64_t)tnops_ln_partial_rows() * 2 * C}, xo.options());
+  ok(tnops_ln_bwd(bf(gy), gres ? gres->data_ptr<float>() : nullptr, xo.data_ptr<float>(),
+                  w.data_ptr<float>(), mean.data_ptr<float>(), rstd.data_ptr<float>(),
+                  dx.data_ptr<float>(), wantBf16 ? bf(dxb) : nullptr, dw.data_ptr<float>(),
+                  db.data_ptr<float>(), partial.data_ptr<float>(), (int)rows, (int)C,
+                  streamOf(xo)),
+     "tnops_ln_bwd");
+  return {dx, wantBf16 ? dxb : at::Tensor(), dw, db};
+}
+
+// logits bf16 [rows, V] (overwritten with d mean-loss / d logits), targets int64
+at::Tensor crossEntropy(at::Tensor logits, const at::Tensor& target, int64_t valid) {
+  need(logits, at::kBFloat16, "logits");
+  need(target, at::kLong, "target");
+  TORCH_CHECK(logits.dim() == 2 && target.numel() == logits.size(0), "shape mismatch");
+  c10::cuda::CUDAGuard g(logits.device());
+  auto loss = at::empty({logits.size(0)}, logits.options().dtype(at::kFloat));
+  ok(tnops_cross_entropy_fwd_bwd(bf(logits), target.data_ptr<int64_t>(), loss.data_ptr<float>(),
+                                 (int)logits.size(0), (int)logits.size(1), (int)valid,
+                                 streamOf(logits)),
+     "tnops_cross_entropy_fwd_bwd");
+  return loss;
+}
+
+void scaleBf16(at::Tensor x, const at::Tensor& scale) {
+  need(x, at::kBFloat16, "x");
+  need(scale, at::kFloat, "scale");
+  c10::cuda::CUDAGuard g(x.device());
+  ok(tnops_scale_bf16(bf(x), (size_t)x.numel(), scale.data_ptr<float>(), streamOf(x)),
+     "tnops_scale_bf16");
+}
+
+void adamw(const std::vector<at::Tensor>& params, const std::vector<at::Tensor>& grads,
+           const std::vector<at::Tensor>& m, const std::vector<at::Tensor>& v,
+           const std::vector<double>& wd, double lr, double b1, double b2, double eps,
+           int64_t step, double gscale) {
+  const size_t n = params.size();
+  TORCH_CHECK(grads.size() == n && m.size() == n && v.size() == n && wd.size() == n,
+              "adamw: list lengths differ");
+  if (n == 0) return;
+  c10::cuda::CUDAGuard g(params[0].device());
+  cudaStream_t st = streamOf(params[0]);
+  for (size_t base = 0; base < n; base += 64) {
+    tnops_adamw_list L{};
+    L.n = (int)std::min<size_t>(64, n - base);
+    for (int i = 0; i < L.n; ++i) {
+      const size_t k = base + (size_t)i;
+      need(params[k], at::kFloat, "param");
+      need(grads[k], at::kFloat, "grad");
+      need(m[k], at::kFloat, "exp_avg");
+      need(v[k], at::kFloat, "exp_avg_sq");
+      L.param[i] = params[k].data_ptr<float>();
+      L.grad[i] = grads[k].data_ptr<float>();
+      L.exp_avg[i] = m[k].data_ptr<float>();
+      L.exp_avg_sq[i] = v[k].data_ptr<float>();
+      L.numel[i] = params[k].numel();
+      L.weight_decay[i] = (float)wd[k];
+    }
+    ok(tnops_adamw(&L, (float)lr, (float)b1, (float)b2, (float)eps, step, (float)gscale, st),
+       "tnops_adamw");
+  }
+}
+
+}  // namespace
+
+void registerOps(py::module_& m) {
+  py::module_ ops = m.def_submodule("ops", "fused sm_100a model kernels");
+  ops.attr("available") = true;
+  ops.def("ln_fwd", &lnFwd, py::arg("x"), py::arg("delta"), py::arg("weight"), py::arg("bias"),
+          py::arg("eps"));
+  ops.def("ln_bwd", &lnBwd, py::arg("grad_y"), py::arg("grad_residual"), py::arg("x_out"),
+          py::arg("weight"), py::arg("mean"), py::arg("rstd"), py::arg("want_bf16"));
+  ops.def("cross_entropy_fwd_bwd", &crossEntropy);
+  ops.def("scale_bf16_", &scaleBf16);
+  ops.def("adamw", &adamw);
+  ops.def("launch_count", []() { return tnops_launch_count(); });
+}

@@ -1,0 +1,221 @@
+// tnccl_ext.cpp - PyTorch binding of the collective library.
+//
+// Exposes a Communicator class over the C API of include/tnccl.h. Tensors are
+// validated here (device, dtype, contiguity, shape); the collective is
+// enqueued on the caller's current CUDA stream (the first call binds the
+// communicator to that stream, as the C API requires).
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+#include <torch/extension.h>
+
+#include <string>
+
+#include "diag.h"
+#include "tnccl.h"
+
+namespace py = pybind11;
+
+namespace {
+
+void check(tncclResult r, const char* what) {
+  if (r != TNCCL_SUCCESS)
+    throw std::runtime_error(std::string(what) + ": " + tncclGetErrorString(r) + " (" +
+                             std::to_string((int)r) + ")");
+}
+
+tncclDataType_t toDtype(const at::Tensor& t) {
+  switch (t.scalar_type()) {
+    case at::kFloat:
+      return tncclFloat32;
+    case at::kBFloat16:
+      return tncclBfloat16;
+    case at::kHalf:
+      return tncclFloat16;
+    default:
+      throw std::invalid_argument("tnccl: dtype must be float32, bfloat16 or float16");
+  }
+}
+
+tncclAlgo_t parseAlgo(const std::string& a) {
+  if (a == "auto") return TNCCL_ALGO_AUTO;
+  if (a == "ring") return TNCCL_ALGO_RING;
+  if (a == "oneshot") return TNCCL_ALGO_ONESHOT;
+  if (a == "twoshot") return TNCCL_ALGO_TWOSHOT;
+  if (a == "nvls") return TNCCL_ALGO_NVLS;
+  throw std::invalid_argument("tnccl: unknown algorithm '" + a + "'");
+}
+
+tncclRedOp_t parseOp(const std::string& op) {
+  if (op == "sum") return tncclSum;
+  if (op == "avg") return tncclAvg;
+  throw std::invalid_argument("tnccl: op must be 'sum' or 'avg'");
+}
+
+class Communicator {
+ public:
+  Communicator(const py::bytes& id, int nranks, int rank) {
+    std::string s = id;
+    if (s.size() != sizeof(tncclUniqueId))
+      throw std::invalid_argument("tnccl: unique id must be 128 bytes");
+    tncclUniqueId uid;
+    memcpy(uid.bytes, s.data(), sizeof(uid.bytes));
+    tncclResult r;
+    {
+      py::gil_scoped_release nogil;  // blocking collective
+      r = tncclCommInitRank(&comm_, nranks, uid, rank);
+    }
+    check(r, "tncclCommInitRank");
+    check(tncclCommGetInfo(comm_, &info_), "tncclCommGetInfo");
+  }
+
+  at::Tensor allReduce(at::Tensor input, c10::optional<at::Tensor> output, const std::string& op,
+                       double scale, const std::string& algo) {
+    live();
+    TORCH_CHECK(input.is_cuda(), "tnccl: input must be a CUDA tensor");
+    TORCH_CHECK(input.get_device() == info_.device, "tnccl: input is on device ",
+                input.get_device(), " but the communicator uses device ", info_.device);
+    TORCH_CHECK(input.is_contiguous(), "tnccl: input must be contiguous");
+    at::Tensor out = output.has_value() ? *output : input;
+    TORCH_CHECK(out.is_cuda() && out.get_device() == info_.device && out.is_contiguous(),
+                "tnccl: output must be a contiguous tensor on the communicator's device");
+    TORCH_CHECK(out.scalar_type() == input.scalar_type() && out.numel() == input.numel(),
+                "tnccl: output must match the input's dtype and size");
+    c10::cuda::CUDAGuard guard(info_.device);
+    cudaStream_t stream = c10::cuda::getCurrentCUDAStream(info_.device).stream();
+    check(tncclAllReduceEx(input.data_ptr(), out.data_ptr(), (size_t)input.numel(),
+                           toDtype(input), parseOp(op), (float)scale, parseAlgo(algo), comm_,
+                           stream),
+          "tncclAllReduceEx");
+    return out;
+  }
+
+  // Raw-pointer variant for callers that manage their own buffers (bench
+  // harness, CUDA-graph capture of preallocated buffers).
+  void allReducePtr(uint64_t send, uint64_t recv, uint64_t count, int dtype, const std::string& op,
+                    double scale, const std::string& algo, uint64_t stream) {
+    live();
+    c10::cuda::CUDAGuard guard(info_.device);
+    check(tncclAllReduceEx(reinterpret_cast<const void*>(send), reinterpret_cast<void*>(recv),
+                           (size_t)count, (tncclDataType_t)dtype, parseOp(op), (float)scale,
+                           parseAlgo(algo), comm_, reinterpret_cast<cudaStream_t>(stream)),
+          "tncclAllReduceEx");
+  }
+
+  std::string selectAlgo(int64_t numel, at::ScalarType st) {
+    live();
+    at::Tensor probe = at::empty({0}, at::TensorOptions().dtype(st));
+    tncclAlgo_t a;
+    check(tncclCommSelectAlgo(comm_, (size_t)numel, toDtype(probe), &a), "tncclCommSelectAlgo");
+    return tncclAlgoName(a);
+  }
+
+  int asyncError() {
+    live();
+    tncclResult r;
+    check(tncclCommGetAsyncError(comm_, &r), "tncclCommGetAsyncError");
+    return (int)r;
+  }
+
+  void abort() {
+    live();
+    check(tncclCommAbort(comm_), "tncclCommAbort");
+  }
+
+  void destroy() {
+    if (comm_ == nullptr) return;
+    tncclComm_t c = comm_;
+    comm_ = nullptr;
+    tncclResult r;
+    {
+      py::gil_scoped_release nogil;
+      r = tncclCommDestroy(c);
+    }
+    check(r, "tncclCommDestroy");
+  }
+
+  py::dict info() const {
+    py::dict d;
+    d["rank"] = info_.rank;
+    d["nranks"] = info_.nranks;
+    d["device"] = info_.device;
+    d["channels"] = info_.channels;
+    d["nvls"] = (bool)info_.nvlsEnabled;
+    d["ipc"] = info_.ipcMode == 1 ? "cumem" : info_.ipcMode == 2 ? "cudaipc" : "none";
+    d["mailbox_bytes"] = (uint64_t)info_.mailboxBytes;
+    d["nvls_bytes"] = (uint64_t)info_.nvlsBytes;
+    d["oneshot_max_bytes"] = (uint64_t)info_.sizeThresholds[0];
+    d["nvls_min_bytes"] = (uint64_t)info_.sizeThresholds[1];
+    return d;
+  }
+
+  // Diagnostic: mean ms per launch of one NVLink/HBM primitive (diag.cu).
+  double diagBench(int mode, uint64_t bytes, int ctas, int threads, int unroll, uint64_t chunk,
+                   int iters) {
+    live();
+    c10::cuda::CUDAGuard guard(info_.device);
+    float ms = 0.f;
+    cudaStream_t stream = c10::cuda::getCurrentCUDAStream(info_.device).stream();
+    tncclResult r;
+    {
+      py::gil_scoped_release nogil;
+      r = tncclDiagBench(comm_, mode, (size_t)bytes, ctas, threads, unroll, (size_t)chunk, iters,
+                         stream, &ms);
+    }
+    check(r, "tncclDiagBench");
+    return ms;
+  }
+
+  int rank() const { return info_.rank; }
+  int size() const { return info_.nranks; }
+  int device() const { return info_.device; }
+  bool alive() const { return comm_ != nullptr; }
+
+ private:
+  void live() const {
+    if (comm_ == nullptr) throw std::runtime_error("tnccl: communicator was destroyed");
+  }
+  tncclComm_t comm_ = nullptr;
+  tncclCommInfo info_{};
+};
+
+py::bytes getUniqueId() {
+  tncclUniqueId id;
+  check(tncclGetUniqueId(&id), "tncclGetUniqueId");
+  return py::bytes(reinterpret_cast<const char*>(id.bytes), sizeof(id.bytes));
+}
+
+}  // namespace
+
+void registerOps(py::module_& m);  // ops_ext.cpp
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "tnccl-b200 native binding";
+  py::class_<Communicator>(m, "Communicator")
+      .def(py::init<const py::bytes&, int, int>(), py::arg("unique_id"), py::arg("nranks"),
+           py::arg("rank"))
+      .def("all_reduce", &Communicator::allReduce, py::arg("input"),
+           py::arg("output") = py::none(), py::arg("op") = "sum", py::arg("scale") = 1.0,
+           py::arg("algo") = "auto")
+      .def("all_reduce_ptr", &Communicator::allReducePtr, py::arg("send"), py::arg("recv"),
+           py::arg("count"), py::arg("dtype"), py::arg("op") = "sum", py::arg("scale") = 1.0,
+           py::arg("algo") = "auto", py::arg("stream") = 0)
+      .def("select_algo", &Communicator::selectAlgo)
+      .def("async_error", &Communicator::asyncError)
+      .def("abort", &Communicator::abort)
+      .def("destroy", &Communicator::destroy)
+      .def("info", &Communicator::info)
+      .def("diag_bench", &Communicator::diagBench)
+      .def_property_readonly("rank", &Communicator::rank)
+      .def_property_readonly("size", &Communicator::size)
+      .def_property_readonly("device", &Communicator::device)
+      .def_property_readonly("alive", &Communicator::alive);
+  m.def("get_unique_id", &getUniqueId);
+  m.def("launch_count", []() { return tncclGetLaunchCount(); });
+  m.def("error_string", [](int r) { return std::string(tncclGetErrorString((tncclResult)r)); });
+  m.def("version", []() {
+    int v = 0;
+    tncclGetVersion(&v);
+    return v;
+  });
+  registerOps(m);
+}

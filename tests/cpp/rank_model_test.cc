@@ -132,6 +132,8 @@ struct Job {
 float rnd(int t, float f) { return oracle::roundTo(t, f); }
 
 bool twoShot(World& w, int r, const Job& j, uint64_t count) {
+  // Same two-slot pipeline as twoShotKernel: RS(n+1) is pushed between
+  // publishing AG(n) and waiting for the peers' AG(n).
   const Config& c = w.cfg;
   const int P = c.P;
   const MailboxLayout& L = w.L;
@@ -140,43 +142,51 @@ bool twoShot(World& w, int r, const Job& j, uint64_t count) {
   std::vector<float>& y = (*j.y)[(size_t)r];
   for (int ch = 0; ch < pl.channels; ++ch) {
     uint64_t& seq = w.counters[(size_t)r][kCounterTwoShot * kMaxChannels + ch];
-    for (uint64_t t = 0; t < channelTiles(pl.numTiles, pl.channels, ch); ++t) {
-      const uint64_t tile = (uint64_t)ch + t * (uint64_t)pl.channels;
-      const uint64_t want = seq + 1;
+    const uint64_t seq0 = seq;
+    const uint64_t ntiles = channelTiles(pl.numTiles, pl.channels, ch);
+    auto tileOf = [&](uint64_t t) { return (uint64_t)ch + t * (uint64_t)pl.channels; };
+    auto slotOf = [&](uint64_t t) { return (int)((seq0 + t) % kTwoShotSlots); };
+    auto pushRS = [&](uint64_t t) {
       for (int k = 1; k < P; ++k) {
         const int dst = (r + k) % P;
-        Span sp = chunkSpan(pl, tile, dst, c.vec);
-        float* out = w.data(dst, tsRsDataAt(L, ch, r));
+        Span sp = chunkSpan(pl, tileOf(t), dst, c.vec);
+        float* out = w.data(dst, tsRsDataAt(L, ch, slotOf(t), r));
         for (uint64_t e = 0; e < sp.count; ++e) out[e] = x[sp.offset + e];
       }
       for (int p = 0; p < P; ++p)
-        if (p != r) w.publish(r, p, tsRsFlagAt(L, ch, r), want);
+        if (p != r) w.publish(r, p, tsRsFlagAt(L, ch, slotOf(t), r), seq0 + t + 1);
+    };
+    if (ntiles > 0) pushRS(0);
+    for (uint64_t t = 0; t < ntiles; ++t) {
+      const int slot = slotOf(t);
+      const uint64_t want = seq0 + t + 1;
       for (int p = 0; p < P; ++p)
-        if (p != r && !w.wait(r, tsRsFlagAt(L, ch, p), want)) return false;
-      Span own = chunkSpan(pl, tile, r, c.vec);
+        if (p != r && !w.wait(r, tsRsFlagAt(L, ch, slot, p), want)) return false;
+      Span own = chunkSpan(pl, tileOf(t), r, c.vec);
       for (uint64_t e = 0; e < own.count; ++e) {
         float acc = 0;
         for (int k = 0; k < P; ++k) {
-          float v = k == r ? x[own.offset + e] : w.data(r, tsRsDataAt(L, ch, k))[e];
+          float v = k == r ? x[own.offset + e] : w.data(r, tsRsDataAt(L, ch, slot, k))[e];
           acc = k == 0 ? oracle::mul(j.alpha, v) : oracle::add(acc, oracle::mul(j.alpha, v));
         }
         acc = rnd(j.dtype, acc);
         y[own.offset + e] = acc;
         for (int p = 0; p < P; ++p)
-          if (p != r) w.data(p, tsAgDataAt(L, ch, r))[e] = acc;
+          if (p != r) w.data(p, tsAgDataAt(L, ch, slot, r))[e] = acc;
       }
       for (int p = 0; p < P; ++p)
-        if (p != r) w.publish(r, p, tsAgFlagAt(L, ch, r), want);
+        if (p != r) w.publish(r, p, tsAgFlagAt(L, ch, slot, r), want);
+      if (t + 1 < ntiles) pushRS(t + 1);
       for (int p = 0; p < P; ++p)
-        if (p != r && !w.wait(r, tsAgFlagAt(L, ch, p), want)) return false;
+        if (p != r && !w.wait(r, tsAgFlagAt(L, ch, slot, p), want)) return false;
       for (int k = 1; k < P; ++k) {
         const int src = (r + P - k) % P;
-        Span sp = chunkSpan(pl, tile, src, c.vec);
-        const float* in = w.data(r, tsAgDataAt(L, ch, src));
+        Span sp = chunkSpan(pl, tileOf(t), src, c.vec);
+        const float* in = w.data(r, tsAgDataAt(L, ch, slot, src));
         for (uint64_t e = 0; e < sp.count; ++e) y[sp.offset + e] = in[e];
       }
-      ++seq;
     }
+    seq = seq0 + ntiles;
   }
   return true;
 }

@@ -1,0 +1,47 @@
+"""Collective library on GPUs: single-rank path through the PyTorch layer,
+multi-rank correctness (skipped with fewer than 2 GPUs), the C example."""
+import os
+
+import pytest
+import torch
+
+from conftest import ROOT, gpu_count, run, torchrun
+
+pytestmark = pytest.mark.gpu
+
+
+def test_single_rank_paths(built):
+    import tiny_nccl_b200 as tn
+    comm = tn.Communicator(tn.get_unique_id(), 1, 0, device=0)
+    x = torch.randn(1 << 20, device="cuda")
+    y = torch.empty_like(x)
+    n0 = tn.launch_count()
+    comm.all_reduce(x, y)  # identity copy
+    torch.testing.assert_close(y, x, atol=0, rtol=0)
+    comm.all_reduce(x, y, scale=0.5)  # fused pre-scale kernel
+    torch.testing.assert_close(y, x * 0.5, atol=0, rtol=0)
+    xb = torch.randn(12345, device="cuda").to(torch.bfloat16)
+    comm.all_reduce(xb, op="avg", scale=3.0)
+    assert tn.launch_count() >= n0 + 2
+    with pytest.raises(RuntimeError):
+        comm.all_reduce(torch.randn(4))  # CPU tensor
+    comm.destroy()
+
+
+def test_example_single_gpu(built):
+    r = run([os.path.join(ROOT, "build", "bin", "tnccl_allreduce"), "1", "1048576"], timeout=120)
+    assert r.returncode == 0 and "all ranks: ok" in r.stdout, r.stdout + r.stderr
+
+
+@pytest.mark.skipif(gpu_count() < 2, reason="needs 2 GPUs")
+def test_two_rank_bit_exact(built):
+    r = run([os.path.join(ROOT, "build", "bin", "allreduce_gpu_test"), "2", "quick"], timeout=600,
+            env={"TNCCL_TIMEOUT_MS": "10000"})
+    assert r.returncode == 0, r.stdout + r.stderr
+
+
+@pytest.mark.skipif(gpu_count() < 2, reason="needs 2 GPUs")
+def test_two_rank_config2_stress(built):
+    r = run([os.path.join(ROOT, "build", "bin", "allreduce_gpu_test"), "2", "stress"], timeout=600,
+            env={"TNCCL_TIMEOUT_MS": "10000"})
+    assert r.returncode == 0, r.stdout + r.stderr

@@ -40,6 +40,7 @@ TNCCL_SRC = ROOT / "csrc" / "tnccl"
 OPS_SRC = ROOT / "csrc" / "ops"
 TORCH_SRC = ROOT / "csrc" / "torch"
 INCLUDES = [f"-I{ROOT / 'include'}", f"-I{TNCCL_SRC}", f"-I{CUDA_HOME / 'include'}"]
+TORCH_EXTRA_INC = [f"-I{TNCCL_SRC}"]
 
 
 def _hash(paths, extra: str) -> str:
@@ -141,7 +142,8 @@ def build_torch_ext() -> Path:
     tmp = out.with_suffix(".tmp")
     cmd = ["g++", "-shared", "-o", str(tmp), *map(str, objs), f"-L{LIB}", "-ltnccl",
            "-ltnccl_ops" if (LIB / "libtnccl_ops.so").exists() else "",
-           *[f"-L{d}" for d in libdirs], "-lc10", "-ltorch", "-ltorch_cpu", "-ltorch_python",
+           *[f"-L{d}" for d in libdirs], "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu",
+           "-ltorch_cuda", "-ltorch_python",
            f"-Wl,-rpath,$ORIGIN/lib", *[f"-Wl,-rpath,{d}" for d in libdirs]]
     _run([c for c in cmd if c])
     os.replace(tmp, out)

@@ -1,0 +1,4 @@
+"""Models trained with the framework."""
+from .gpt2 import GPT2, GPT2Config
+
+__all__ = ["GPT2", "GPT2Config"]

@@ -1,0 +1,103 @@
+"""Autograd wrappers of the fused sm_100a model kernels (csrc/ops).
+
+Every function calls the native kernel; there is no PyTorch fallback. A
+missing extension or an unsupported shape raises.
+"""
+from __future__ import annotations
+
+import torch
+
+from .._native import load
+
+
+def _ops():
+    return load().ops
+
+
+class _AddLayerNorm(torch.autograd.Function):
+    """x_out = x + delta (optional); y = LayerNorm(x_out) in bf16.
+
+    The residual stream x stays fp32; delta (a bf16 sub-layer output) is added
+    in the same pass that normalises, and the backward returns the residual
+    gradient (fp32) and the sub-layer gradient (bf16) from one kernel.
+    """
+
+    @staticmethod
+    def forward(ctx, x, delta, weight, bias, eps):
+        C = x.shape[-1]
+        x2 = x.reshape(-1, C)
+        d2 = delta.reshape(-1, C) if delta is not None else None
+        x_out, y, mean, rstd = _ops().ln_fwd(x2, d2, weight, bias, eps)
+        ctx.save_for_backward(x_out, weight, mean, rstd)
+        ctx.has_delta = delta is not None
+        ctx.shape = x.shape
+        return x_out.view(x.shape), y.view(x.shape)
+
+    @staticmethod
+    def backward(ctx, g_xout, g_y):
+        x_out, weight, mean, rstd = ctx.saved_tensors
+        C = ctx.shape[-1]
+        if g_y is None:
+            g_y = torch.zeros(x_out.shape, dtype=torch.bfloat16, device=x_out.device)
+        gres = g_xout.reshape(-1, C).contiguous() if g_xout is not None else None
+        dx, dxb, dw, db = _ops().ln_bwd(g_y.reshape(-1, C).contiguous(), gres, x_out, weight,
+                                        mean, rstd, ctx.has_delta)
+        ddelta = dxb.view(ctx.shape) if ctx.has_delta else None
+        return dx.view(ctx.shape), ddelta, dw, db, None
+
+
+def add_layer_norm(x: torch.Tensor, delta: torch.Tensor, weight: torch.Tensor,
+                   bias: torch.Tensor, eps: float = 1e-5):
+    """Returns (x + delta, LayerNorm(x + delta)) with x fp32, delta bf16."""
+    x_out, y = _AddLayerNorm.apply(x, delta.contiguous(), weight, bias, eps)
+    return x_out, y
+
+
+def layer_norm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor,
+               eps: float = 1e-5) -> torch.Tensor:
+    """bf16 LayerNorm of a fp32 input."""
+    return _AddLayerNorm.apply(x.contiguous(), None, weight, bias, eps)[1]
+
+
+class _CrossEntropy(torch.autograd.Function):
+    """Mean softmax cross-entropy of bf16 logits. The forward kernel also
+    writes d(loss)/d(logits) into the logits buffer, so the backward only
+    rescales when the incoming gradient is not 1 (checked on the device)."""
+
+    @staticmethod
+    def forward(ctx, logits, target):
+        valid = int(target.numel())
+        per_row = _ops().cross_entropy_fwd_bwd(logits, target, valid)
+        ctx.save_for_backward(logits)
+        return per_row.sum() / valid
+
+    @staticmethod
+    def backward(ctx, g):
+        (dlogits,) = ctx.saved_tensors
+        _ops().scale_bf16_(dlogits, g.reshape(1).float().contiguous())
+        return dlogits, None
+
+
+def cross_entropy(logits: torch.Tensor, target: torch.Tensor,
+                  reuse_logits: bool = True) -> torch.Tensor:
+    """Mean cross-entropy of [rows, V] logits against int64 targets.
+
+    With ``reuse_logits`` (the default, used for the model's temporary logits)
+    the gradient is written into the logits storage during the forward pass,
+    so the logits values are gone afterwards; pass False to keep them (the
+    kernel then works on a copy)."""
+    if logits.dtype != torch.bfloat16:
+        logits = logits.to(torch.bfloat16)
+    elif not reuse_logits:
+        logits = logits.clone()
+    return _CrossEntropy.apply(logits.contiguous(), target.contiguous())
+
+
+def linear_gelu(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
+    """GELU(tanh)(x W^T + b): cuBLAS GEMM with fused bias, tanh-GELU kernel."""
+    return torch.nn.functional.gelu(torch.nn.functional.linear(x, weight, bias),
+                                    approximate="tanh")
+
+
+def launch_count() -> int:
+    return _ops().launch_count()

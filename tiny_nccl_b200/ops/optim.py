@@ -1,0 +1,55 @@
+"""AdamW on the multi-tensor sm_100a kernel (csrc/ops/adamw.cu).
+
+Semantics of torch.optim.AdamW (decoupled weight decay, bias correction).
+Parameters are grouped by weight decay: 2-D weights decay, biases, LayerNorm
+gains and embeddings tables of positions follow the usual GPT-2 recipe via
+the `no_decay` predicate.
+"""
+from __future__ import annotations
+
+import torch
+
+from .._native import load
+
+
+class AdamW(torch.optim.Optimizer):
+    def __init__(self, params, lr=6e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1):
+        defaults = dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay)
+        super().__init__(params, defaults)
+        self._step = 0
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        loss = closure() if closure is not None else None
+        self._step += 1
+        ops = load().ops
+        for group in self.param_groups:
+            ps, gs, ms, vs, wds = [], [], [], [], []
+            for p in group["params"]:
+                if p.grad is None:
+                    continue
+                st = self.state[p]
+                if not st:
+                    st["exp_avg"] = torch.zeros_like(p, memory_format=torch.contiguous_format)
+                    st["exp_avg_sq"] = torch.zeros_like(p, memory_format=torch.contiguous_format)
+                ps.append(p)
+                gs.append(p.grad if p.grad.is_contiguous() else p.grad.contiguous())
+                ms.append(st["exp_avg"])
+                vs.append(st["exp_avg_sq"])
+                wds.append(float(group["weight_decay"]))
+            if ps:
+                b1, b2 = group["betas"]
+                ops.adamw(ps, gs, ms, vs, wds, float(group["lr"]), float(b1), float(b2),
+                          float(group["eps"]), self._step, 1.0)
+        return loss
+
+
+def gpt2_param_groups(model: torch.nn.Module, weight_decay: float = 0.1):
+    """2-D weights decay; biases and LayerNorm parameters do not."""
+    decay, no_decay = [], []
+    for _, p in model.named_parameters():
+        if not p.requires_grad:
+            continue
+        (decay if p.dim() >= 2 else no_decay).append(p)
+    return [{"params": decay, "weight_decay": weight_decay},
+            {"params": no_decay, "weight_decay": 0.0}]

@@ -1,0 +1,118 @@
+"""Communicator creation and the tensor-level all-reduce.
+
+A communicator is created collectively by every rank: rank 0 draws a unique id
+(a rendezvous path for the AF_UNIX bootstrap) and shares it through any
+key-value store, typically the ``torch.distributed`` TCPStore of the job. The
+tensor data never goes through the store or the bootstrap socket; it moves
+over NVLink through the library's mailboxes.
+
+Mirrors tiny-nccl's ``tncclGetUniqueId`` / ``tncclCommInitRank`` /
+``tncclAllReduceSumF32`` / ``tncclCommDestroy`` (include/tnccl.h:25-51) with
+dtype, pre-scale and algorithm choice added.
+"""
+from __future__ import annotations
+
+import torch
+
+from .._native import load
+
+ALGOS = ("auto", "ring", "oneshot", "twoshot", "nvls")
+
+
+def get_unique_id() -> bytes:
+    """128-byte rendezvous id (same role as tncclGetUniqueId)."""
+    return load().get_unique_id()
+
+
+class Communicator:
+    """One rank's handle on a tnccl communicator.
+
+    Creation and :meth:`destroy` are blocking collectives. The communicator
+    captures the current CUDA device at creation; the first collective binds it
+    to the caller's current stream and later collectives must use that stream.
+    """
+
+    def __init__(self, unique_id: bytes, nranks: int, rank: int, device: int | None = None):
+        if device is not None:
+            torch.cuda.set_device(device)
+        self._c = load().Communicator(unique_id, nranks, rank)
+
+    # -- properties -----------------------------------------------------------
+    @property
+    def rank(self) -> int:
+        return self._c.rank
+
+    @property
+    def size(self) -> int:
+        return self._c.size
+
+    @property
+    def device(self) -> torch.device:
+        return torch.device("cuda", self._c.device)
+
+    def info(self) -> dict:
+        return self._c.info()
+
+    # -- collectives ----------------------------------------------------------
+    def all_reduce(self, tensor: torch.Tensor, out: torch.Tensor | None = None, op: str = "sum",
+                   scale: float = 1.0, algo: str = "auto") -> torch.Tensor:
+        """out = sum over ranks of (scale * tensor) with fp32 accumulation.
+
+        In place when ``out`` is None. ``op="avg"`` multiplies the pre-scale by
+        1/nranks. Enqueued on the current CUDA stream; returns immediately.
+        """
+        return self._c.all_reduce(tensor, out, op, float(scale), algo)
+
+    def all_reduce_ptr(self, send: int, recv: int, count: int, dtype: torch.dtype,
+                       op: str = "sum", scale: float = 1.0, algo: str = "auto",
+                       stream: int | None = None) -> None:
+        """Pointer-level all-reduce for preallocated buffers."""
+        code = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}[dtype]
+        if stream is None:
+            stream = torch.cuda.current_stream(self.device).cuda_stream
+        self._c.all_reduce_ptr(send, recv, count, code, op, float(scale), algo, stream)
+
+    def select_algo(self, numel: int, dtype: torch.dtype) -> str:
+        return self._c.select_algo(numel, dtype)
+
+    # -- failure handling -----------------------------------------------------
+    def async_error(self) -> int:
+        """0 when no device wait failed, else a tncclResult code (5: timeout)."""
+        return self._c.async_error()
+
+    def check(self) -> None:
+        err = self._c.async_error()
+        if err:
+            raise RuntimeError(f"tnccl: {load().error_string(err)}")
+
+    def abort(self) -> None:
+        self._c.abort()
+
+    def destroy(self) -> None:
+        self._c.destroy()
+
+    @property
+    def alive(self) -> bool:
+        return self._c.alive
+
+
+def init_from_store(store, rank: int, world_size: int, key: str = "tnccl/uid",
+                    device: int | None = None) -> Communicator:
+    """Creates a communicator, sharing the unique id through ``store``
+    (anything with ``set(key, bytes)`` and a blocking ``get(key)``)."""
+    if rank == 0:
+        uid = get_unique_id()
+        store.set(key, uid)
+    else:
+        uid = bytes(store.get(key))
+    return Communicator(uid, world_size, rank, device=device)
+
+
+def init_from_torch_distributed(key: str = "tnccl/uid", device: int | None = None) -> Communicator:
+    """Creates a communicator over the ranks of the default process group."""
+    import torch.distributed as dist
+
+    if not dist.is_initialized():
+        raise RuntimeError("torch.distributed is not initialized")
+    store = dist.distributed_c10d._get_default_store()
+    return init_from_store(store, dist.get_rank(), dist.get_world_size(), key=key, device=device)

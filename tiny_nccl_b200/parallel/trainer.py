@@ -1,0 +1,49 @@
+"""Data-parallel training step: DistributedDataParallel with the tnccl comm
+hook (gradient buckets all-reduced on a side stream, 1/world fused into the
+kernel, overlapped with backward) and the fused AdamW kernel.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+from torch.nn.parallel import DistributedDataParallel as DDP
+
+from ..ops.optim import AdamW, gpt2_param_groups
+from .comm import Communicator
+from .ddp import register_tnccl_hook
+
+
+class DataParallelTrainer:
+    def __init__(self, model: torch.nn.Module, comm: Communicator, lr: float = 6e-4,
+                 weight_decay: float = 0.1, betas=(0.9, 0.95), bucket_cap_mb: int = 25,
+                 algo: str = "auto", wire_dtype: torch.dtype | None = None,
+                 amp_dtype: torch.dtype = torch.bfloat16):
+        if not dist.is_initialized():
+            raise RuntimeError("DataParallelTrainer needs torch.distributed initialised")
+        self.comm = comm
+        self.model = model
+        self.amp_dtype = amp_dtype
+        dev = comm.device
+        self.ddp = DDP(model, device_ids=[dev.index], output_device=dev.index,
+                       bucket_cap_mb=bucket_cap_mb, gradient_as_bucket_view=True,
+                       static_graph=True, broadcast_buffers=False)
+        self.hook_state = register_tnccl_hook(self.ddp, comm, algo=algo, wire_dtype=wire_dtype)
+        self.opt = AdamW(gpt2_param_groups(model, weight_decay), lr=lr, betas=betas)
+
+    def step(self, idx: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
+        """One optimizer step; returns the (device) loss without synchronizing."""
+        with torch.autocast("cuda", dtype=self.amp_dtype):
+            loss = self.ddp(idx, targets)
+        loss.backward()
+        self.opt.step()
+        self.opt.zero_grad(set_to_none=False)
+        return loss.detach()
+
+    def state_dict(self) -> dict:
+        return {"model": self.model.state_dict(), "opt": self.opt.state_dict(),
+                "step": self.opt._step}
+
+    def load_state_dict(self, sd: dict) -> None:
+        self.model.load_state_dict(sd["model"])
+        self.opt.load_state_dict(sd["opt"])
+        self.opt._step = sd["step"]
