@@ -263,3 +263,56 @@ extern "C" int tnops_ln_bwd(const uint16_t* gy, const float* g_res, const float*
   reducePartials<<<(2 * C + 255) / 256, 256, 0, stream>>>(partial, dw, db, nparts, C);
   return launched(cudaGetLastError());
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of tnops_ln_bwd (declared in tnops_noalloc.h; no
+// counterpart in the tiny-nccl reference). The partial-sum scratch is a
+// file-scope device array; host code must not pass the array's name to a
+// kernel (on the host it is only a stand-in symbol), so its device address is
+// looked up once per device with cudaGetSymbolAddress and cached.
+// ---------------------------------------------------------------------------
+#include <stdio.h>
+
+#include <mutex>
+
+#include "tnops_noalloc.h"
+
+namespace tnops {
+namespace {
+
+constexpr int kNoAllocMaxDevices = 64;
+static __device__ __align__(256) float gLnBwdScratch[2 * kPartialRows * TNOPS_NOALLOC_MAX_C];
+std::mutex gScratchMutex;
+float* gScratchAddr[kNoAllocMaxDevices] = {};
+
+}  // namespace
+}  // namespace tnops
+
+extern "C" int tnops_ln_bwd_noalloc(const uint16_t* gy, const float* g_res, const float* x_out,
+                                    const float* w, const float* mean, const float* rstd,
+                                    float* dx, uint16_t* dx_bf16, float* dw, float* db, int rows,
+                                    int C, cudaStream_t stream) {
+  if (C > TNOPS_NOALLOC_MAX_C) {
+    fprintf(stderr,
+            "tnops_ln_bwd_noalloc: C = %d exceeds the built-in scratch limit of %d columns\n", C,
+            TNOPS_NOALLOC_MAX_C);
+    return (int)cudaErrorInvalidValue;
+  }
+  int device = -1;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return (int)e;
+  if (device < 0 || device >= kNoAllocMaxDevices) return (int)cudaErrorInvalidDevice;
+  float* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(gScratchMutex);
+    if (gScratchAddr[device] == nullptr) {
+      void* p = nullptr;
+      e = cudaGetSymbolAddress(&p, gLnBwdScratch);
+      if (e != cudaSuccess) return (int)e;
+      gScratchAddr[device] = static_cast<float*>(p);
+    }
+    scratch = gScratchAddr[device];
+  }
+  return tnops_ln_bwd(gy, g_res, x_out, w, mean, rstd, dx, dx_bf16, dw, db, scratch, rows, C,
+                      stream);
+}
