@@ -1,0 +1,93 @@
+"""Per-phase timing of the all-reduce kernels from the device tracer.
+
+With TNCCL_TRACE=1 every channel records {globaltimer, (family, phase, tile)}
+at each phase boundary. This script runs a few all-reduces of one size and
+algorithm on every rank and prints, per phase transition, the mean and the
+spread of the time channel 0..C-1 spend between consecutive marks.
+
+    TNCCL_TRACE=1 python -m torch.distributed.run --nproc-per-node 2 \
+        --master-addr 127.0.0.1 benchmarks/trace_phases.py --algo twoshot --bytes 64M
+"""
+from __future__ import annotations
+
+import argparse
+import collections
+import datetime
+import json
+import os
+import sys
+
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+NAMES = {
+    2: {0: "tile start", 1: "RS arrived", 2: "reduced+AG published", 3: "next RS pushed",
+        4: "AG arrived", 5: "copied out"},
+    1: {0: "tile start", 1: "slot free", 2: "pushed+published", 3: "peers arrived",
+        4: "reduced+acked"},
+    3: {0: "tile start", 1: "copied in", 2: "barrier 1", 3: "switch reduce+store",
+        4: "barrier 2", 5: "copied out"},
+}
+FAMILY = {"ring": 0, "oneshot": 1, "twoshot": 2, "nvls": 3}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--algo", default="twoshot")
+    ap.add_argument("--bytes", default="64M")
+    ap.add_argument("--iters", type=int, default=3)
+    ap.add_argument("--out", default="")
+    args = ap.parse_args()
+    assert os.environ.get("TNCCL_TRACE") == "1", "run with TNCCL_TRACE=1"
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=60))
+    import tiny_nccl_b200 as tn
+
+    mult = {"K": 1 << 10, "M": 1 << 20, "G": 1 << 30}
+    size = int(args.bytes[:-1]) * mult[args.bytes[-1]]
+    comm = tn.init_from_torch_distributed(device=rank)
+    x = torch.randn(size // 4, device=dev)
+    y = torch.empty_like(x)
+    s = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(s):
+        for _ in range(args.iters):
+            comm.all_reduce(x, y, algo=args.algo)
+    torch.cuda.synchronize()
+    fam = FAMILY[args.algo]
+    deltas = collections.defaultdict(list)
+    spans = []
+    for c in range(128):
+        rec = comm._c.trace_read(c, 1 << 16)
+        if not rec:
+            continue
+        ev = [(rec[2 * i], rec[2 * i + 1]) for i in range(len(rec) // 2)]
+        ev = [(t, (tag >> 16) & 0xFF, tag & 0xFFFF) for t, tag in ev if (tag >> 24) == fam]
+        if not ev:
+            continue
+        spans.append(ev[-1][0] - ev[0][0])
+        for (t0, p0, _), (t1, p1, _) in zip(ev, ev[1:]):
+            deltas[(p0, p1)].append(t1 - t0)
+    summary = {f"{NAMES.get(fam, {}).get(a, a)} -> {NAMES.get(fam, {}).get(b, b)}":
+               {"mean_us": sum(v) / len(v) / 1e3, "n": len(v)} for (a, b), v in sorted(deltas.items())}
+    rec = {"rank": rank, "algo": args.algo, "bytes": size, "phases": summary,
+           "channel_span_us_mean": sum(spans) / max(1, len(spans)) / 1e3}
+    allrec = [None] * world
+    dist.all_gather_object(allrec, rec)
+    if rank == 0:
+        for r in allrec:
+            print(json.dumps(r))
+        if args.out:
+            with open(args.out, "a") as f:
+                for r in allrec:
+                    f.write(json.dumps(r) + "\n")
+    torch.cuda.synchronize()
+    comm.destroy()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

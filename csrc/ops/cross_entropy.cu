@@ -6,9 +6,11 @@
 // (now resident in L2) and overwrites it in place with the gradient of the
 // mean loss, (softmax - onehot(target)) / valid. HBM traffic is one read and
 // one write of the logits, instead of materialising fp32 log-probabilities.
-// Rows are V * 2 bytes long, so a row may start at any 2-byte offset: each
-// row is split into a scalar head up to the first 16-byte boundary, a 16-byte
-// vector body and a scalar tail.
+// A row holds V classes followed by (ld - V) padding columns (a vocabulary
+// padded to a multiple of 128 keeps the LM-head GEMMs on aligned tensor-core
+// kernels); padding columns take no part in the softmax and get gradient 0.
+// A row may start at any 2-byte offset: it is split into a scalar head up to
+// the first 16-byte boundary, a 16-byte vector body and a scalar tail.
 #include <float.h>
 
 #include "common.cuh"
@@ -40,9 +42,9 @@ __device__ __forceinline__ void accumulate(MaxSum& st, const float* v, int n) {
 
 __global__ void __launch_bounds__(kThreads)
     ceKernel(uint16_t* __restrict__ logits, const int64_t* __restrict__ target,
-             float* __restrict__ loss, int V, float invValid) {
+             float* __restrict__ loss, int V, int ld, float invValid) {
   const int r = blockIdx.x;
-  uint16_t* row = logits + (size_t)r * V;
+  uint16_t* row = logits + (size_t)r * ld;
   const int64_t tgt = target[r];
   const uintptr_t addr = reinterpret_cast<uintptr_t>(row);
   int head = (int)(((16 - (addr & 15)) & 15) >> 1);
@@ -124,6 +126,7 @@ __global__ void __launch_bounds__(kThreads)
     if (i == tgt) p -= 1.f;
     row[i] = f2bf(p * scale);
   }
+  for (int i = V + threadIdx.x; i < ld; i += kThreads) row[i] = 0;
 }
 
 __global__ void scaleBf16(uint16_t* __restrict__ x, size_t n, const float* __restrict__ scale) {
@@ -140,10 +143,11 @@ __global__ void scaleBf16(uint16_t* __restrict__ x, size_t n, const float* __res
 using namespace tnops;
 
 extern "C" int tnops_cross_entropy_fwd_bwd(uint16_t* logits, const int64_t* target, float* loss,
-                                           int rows, int V, int valid, cudaStream_t stream) {
-  if (rows <= 0 || V <= 0) return (int)cudaErrorInvalidValue;
+                                           int rows, int V, int ld, int valid,
+                                           cudaStream_t stream) {
+  if (rows <= 0 || V <= 0 || ld < V) return (int)cudaErrorInvalidValue;
   const float inv = valid > 0 ? 1.0f / (float)valid : 0.f;
-  ceKernel<<<rows, kThreads, 0, stream>>>(logits, target, loss, V, inv);
+  ceKernel<<<rows, kThreads, 0, stream>>>(logits, target, loss, V, ld, inv);
   return launched(cudaGetLastError());
 }
 

@@ -94,7 +94,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
 }
 
 template <int K>
-__global__ void __launch_bounds__(kWarpsPerBlock * 32)
+__global__ void __launch_bounds__(kWarpsPerBlock * 32, 2)
     lnBwdKernel(const uint16_t* __restrict__ gy, const float* __restrict__ gres,
                 const float* __restrict__ xo, const float* __restrict__ w,
                 const float* __restrict__ mean, const float* __restrict__ rstd,
@@ -188,16 +188,29 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
   }
 }
 
-__global__ void reducePartials(const float* __restrict__ partial, float* __restrict__ dw,
-                               float* __restrict__ db, int nparts, int C) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= 2 * C) return;
-  float s = 0.f;
-  for (int p = 0; p < nparts; ++p) s += partial[(size_t)p * 2 * C + c];
-  if (c < C)
-    dw[c] = s;
-  else
-    db[c - C] = s;
+// One CTA per 32 columns of [dw | db]: its 8 warps sum disjoint sets of
+// partial rows (coalesced 128-byte reads), then warp 0 adds the 8 warp sums
+// in a fixed order, so the result does not depend on scheduling.
+__global__ void __launch_bounds__(256)
+    reducePartials(const float* __restrict__ partial, float* __restrict__ dw,
+                   float* __restrict__ db, int nparts, int C) {
+  __shared__ float s[8][33];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int col = blockIdx.x * 32 + lane;
+  float acc = 0.f;
+  if (col < 2 * C)
+    for (int p = warp; p < nparts; p += 8) acc += partial[(size_t)p * 2 * C + col];
+  s[warp][lane] = acc;
+  __syncthreads();
+  if (warp == 0 && col < 2 * C) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t += s[w][lane];
+    if (col < C)
+      dw[col] = t;
+    else
+      db[col - C] = t;
+  }
 }
 
 template <int K>
@@ -260,7 +273,7 @@ extern "C" int tnops_ln_bwd(const uint16_t* gy, const float* g_res, const float*
   if (launched(e) != 0) return (int)e;
   int nparts = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock;
   if (nparts > kPartialRows) nparts = kPartialRows;
-  reducePartials<<<(2 * C + 255) / 256, 256, 0, stream>>>(partial, dw, db, nparts, C);
+  reducePartials<<<(2 * C + 31) / 32, 256, 0, stream>>>(partial, dw, db, nparts, C);
   return launched(cudaGetLastError());
 }
 

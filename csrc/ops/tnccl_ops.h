@@ -31,13 +31,14 @@ int tnops_ln_bwd(const uint16_t* gy, const float* g_res, const float* x_out, con
                  float* db, float* partial, int rows, int C, cudaStream_t stream);
 int tnops_ln_partial_rows(void);
 
-// Fused softmax cross-entropy over bf16 logits [rows, V]: loss[r] =
-// logsumexp(logits[r]) - logits[r, target[r]] (fp32), and logits is
-// overwritten in place with d(mean loss)/d(logits) = (softmax - onehot)/rows
-// in bf16. Rows whose target is negative are ignored (zero loss and gradient);
-// `valid` counts the rows that are not, for the mean.
+// Fused softmax cross-entropy over bf16 logits [rows, ld] whose first V
+// columns are classes (the rest is padding): loss[r] = logsumexp(logits[r,:V])
+// - logits[r, target[r]] (fp32), and logits is overwritten in place with
+// d(mean loss)/d(logits) = (softmax - onehot)/valid in bf16 (0 in padding
+// columns). Rows whose target is negative are ignored (zero loss and
+// gradient); `valid` counts the rows that are not, for the mean.
 int tnops_cross_entropy_fwd_bwd(uint16_t* logits, const int64_t* target, float* loss, int rows,
-                                int V, int valid, cudaStream_t stream);
+                                int V, int ld, int valid, cudaStream_t stream);
 
 // Multiplies a bf16 tensor by the fp32 scalar *scale (device memory); no-op
 // on the device when *scale == 1.

@@ -281,7 +281,9 @@ __global__ void __launch_bounds__(kMaxThreads)
   if (ntiles > 0) pushRS(0);
   uint64_t done = 0;
   for (uint64_t t = 0; t < ntiles; ++t) {
+    traceMark(comm, c, kCounterTwoShot, 0, t);
     if (!waitAll(false, t, 1)) break;
+    traceMark(comm, c, kCounterTwoShot, 1, t);
     const uint64_t tile = tileOf(t);
     const int slot = slotOf(t);
     // Reduce my chunk in rank order, store it locally and push it to all.
@@ -307,9 +309,12 @@ __global__ void __launch_bounds__(kMaxThreads)
     __syncthreads();
     if (tid < P && tid != r)
       stReleaseSys(flagPtr(comm.peers[tid], tsAgFlagAt(L, c, slot, r)), seq0 + t + 1);
+    traceMark(comm, c, kCounterTwoShot, 2, t);
     // Start the next tile's reduce-scatter while the peers finish this one.
     if (t + 1 < ntiles) pushRS(t + 1);
+    traceMark(comm, c, kCounterTwoShot, 3, t);
     if (!waitAll(true, t, 2)) break;
+    traceMark(comm, c, kCounterTwoShot, 4, t);
     // Copy every peer's reduced chunk out.
     for (int k = 1; k < P; ++k) {
       const int j = (r + P - k) % P;
@@ -318,6 +323,7 @@ __global__ void __launch_bounds__(kMaxThreads)
       copyOut<T, kLdMailbox, 8>(reinterpret_cast<const T*>(me + tsAgDataAt(L, c, slot, j)),
                                 sp.count, vec, false, 1.f, 1, [dst](int) { return dst; });
     }
+    traceMark(comm, c, kCounterTwoShot, 5, t);
     done = t + 1;
   }
   // Every thread has passed the final barrier of the loop (or broke out on
@@ -352,6 +358,7 @@ __global__ void __launch_bounds__(kMaxThreads)
     const Span sp = blockTileSpan(pl, tile);
     const int s = (int)(seq % (uint64_t)S);
     const uint64_t want = seq + 1;
+    traceMark(comm, c, kCounterOneShot, 0, t);
     // The slot is free once every consumer acknowledged its previous use.
     if (seq >= (uint64_t)S && tid < P && tid != r &&
         !waitFlag(comm, flagPtr(me, osAckAt(L, c, s, tid)), seq - (uint64_t)S + 1,
@@ -359,18 +366,21 @@ __global__ void __launch_bounds__(kMaxThreads)
       sFail = 1;
     __syncthreads();
     if (sFail) break;
+    traceMark(comm, c, kCounterOneShot, 1, t);
     const uint64_t dataOff = osDataAt(L, c, s, r);
     copyOut<T, kLdInput, 8>(x + sp.offset, sp.count, vec, false, 1.f, P - 1, [&](int d) {
       return comm.peers[(r + 1 + d) % P] + dataOff;
     });
     __syncthreads();
     if (tid < P && tid != r) stReleaseSys(flagPtr(comm.peers[tid], osFlagAt(L, c, s, r)), want);
+    traceMark(comm, c, kCounterOneShot, 2, t);
     if (tid < P && tid != r &&
         !waitFlag(comm, flagPtr(me, osFlagAt(L, c, s, tid)), want,
                   whereCode(kCounterOneShot, c, 1)))
       sFail = 1;
     __syncthreads();
     if (sFail) break;
+    traceMark(comm, c, kCounterOneShot, 3, t);
     reduceRanks<T, MAXP, U>(
         sp.count, vec, P, r, x + sp.offset, a.scale,
         [&](int k) { return me + osDataAt(L, c, s, k); },
@@ -378,6 +388,7 @@ __global__ void __launch_bounds__(kMaxThreads)
         [&](uint64_t e, float f) { stElem(y + sp.offset + e, f); });
     __syncthreads();  // every read of slot s is done
     if (tid < P && tid != r) stReleaseSys(flagPtr(comm.peers[tid], osAckAt(L, c, s, r)), want);
+    traceMark(comm, c, kCounterOneShot, 4, t);
     ++seq;
   }
   if (tid == 0 && !sFail) comm.counters[kCounterOneShot * kMaxChannels + c] = seq;
@@ -583,9 +594,12 @@ __global__ void __launch_bounds__(kMaxThreads)
     const uint64_t tile = (uint64_t)c + t * (uint64_t)pl.channels;
     const Span sp = blockTileSpan(pl, tile);
     const uint64_t want = seq + 1;
+    traceMark(comm, c, kCounterNvls, 0, t);
     copyOut<T, kLdInput, 8>(x + sp.offset, sp.count, vec, false, 1.f, 1,
                             [ucIn](int) { return ucIn; });
+    traceMark(comm, c, kCounterNvls, 1, t);
     if (!barrier(0, want)) break;
+    traceMark(comm, c, kCounterNvls, 2, t);
     // Reduce this rank's share (whole vectors; padding past the tile end is
     // reduced too but never copied out).
     const uint64_t nvecTile = divUp(sp.count, V);
@@ -615,10 +629,13 @@ __global__ void __launch_bounds__(kMaxThreads)
         }
       }
     }
+    traceMark(comm, c, kCounterNvls, 3, t);
     if (!barrier(1, want)) break;
+    traceMark(comm, c, kCounterNvls, 4, t);
     T* yo = y + sp.offset;
     copyOut<T, kLdMailbox, 8>(reinterpret_cast<const T*>(ucOut), sp.count, vec, false, 1.f, 1,
                               [yo](int) { return reinterpret_cast<char*>(yo); });
+    traceMark(comm, c, kCounterNvls, 5, t);
     ++seq;
   }
   if (tid == 0 && !sFail) comm.counters[kCounterNvls * kMaxChannels + c] = seq;

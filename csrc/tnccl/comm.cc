@@ -99,12 +99,30 @@ tncclResult allocDeviceState(tncclComm* comm) {
   if (cudaMalloc(reinterpret_cast<void**>(&comm->counters), cbytes) != cudaSuccess)
     return TNCCL_CUDA_ERROR;
   if (cudaMemset(comm->counters, 0, cbytes) != cudaSuccess) return TNCCL_CUDA_ERROR;
+  if (cudaMalloc(reinterpret_cast<void**>(&comm->diagWord), sizeof(uint64_t)) != cudaSuccess)
+    return TNCCL_CUDA_ERROR;
+  if (cudaMemset(comm->diagWord, 0, sizeof(uint64_t)) != cudaSuccess) return TNCCL_CUDA_ERROR;
+  if (comm->cfg.traceEvents > 0) {
+    const size_t tb = (size_t)kMaxChannels * comm->cfg.traceEvents * 2 * sizeof(uint64_t);
+    if (cudaMalloc(reinterpret_cast<void**>(&comm->trace), tb) != cudaSuccess ||
+        cudaMalloc(reinterpret_cast<void**>(&comm->traceCount), kMaxChannels * sizeof(uint32_t)) !=
+            cudaSuccess)
+      return TNCCL_CUDA_ERROR;
+    cudaMemset(comm->trace, 0, tb);
+    cudaMemset(comm->traceCount, 0, kMaxChannels * sizeof(uint32_t));
+  }
   return TNCCL_SUCCESS;
 }
 
 void freeDeviceState(tncclComm* comm) {
   if (comm->counters) cudaFree(comm->counters);
   comm->counters = nullptr;
+  if (comm->diagWord) cudaFree(comm->diagWord);
+  comm->diagWord = nullptr;
+  if (comm->trace) cudaFree(comm->trace);
+  if (comm->traceCount) cudaFree(comm->traceCount);
+  comm->trace = nullptr;
+  comm->traceCount = nullptr;
   if (comm->hostStatus) cudaFreeHost(comm->hostStatus);
   comm->hostStatus = nullptr;
   comm->devStatus = nullptr;
@@ -126,6 +144,9 @@ void fillDevComm(tncclComm* comm) {
   d.nvlsTileBytes = comm->nvls.tileBytes;
   d.nvlsUc = reinterpret_cast<char*>(comm->nvls.ucVa);
   d.nvlsMc = reinterpret_cast<char*>(comm->nvls.mcVa);
+  d.trace = comm->trace;
+  d.traceCount = comm->traceCount;
+  d.traceEvents = (uint32_t)comm->cfg.traceEvents;
 }
 
 void deriveThresholds(tncclComm* comm) {

@@ -88,6 +88,9 @@ struct tncclComm {
   tnccl::NvlsState nvls;
   tnccl::DevComm dev{};
   uint64_t* counters = nullptr;
+  uint64_t* diagWord = nullptr;  // device word that nothing writes (self tests)
+  uint64_t* trace = nullptr;      // TNCCL_TRACE records (devcomm.h)
+  uint32_t* traceCount = nullptr;
   tnccl::DevStatus* hostStatus = nullptr;
   tnccl::DevStatus* devStatus = nullptr;
   cudaStream_t boundStream = nullptr;

@@ -93,6 +93,8 @@ Config loadConfig() {
   c.useCuMem = (int)envInt("TNCCL_CUMEM_ENABLE", 1);
   c.oneShotMaxBytes = envInt("TNCCL_ONESHOT_MAX_BYTES", 0);
   c.nvlsMinBytes = envInt("TNCCL_NVLS_MIN_BYTES", 0);
+  c.traceEvents = envInt("TNCCL_TRACE", 0) ? clampInt(envInt("TNCCL_TRACE_EVENTS", 4096), 16, 1 << 20)
+                                            : 0;
   return c;
 }
 

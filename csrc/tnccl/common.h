@@ -48,6 +48,7 @@ struct Config {
   // AUTO thresholds in bytes (0 = derive from nranks).
   int64_t oneShotMaxBytes;   // TNCCL_ONESHOT_MAX_BYTES
   int64_t nvlsMinBytes;      // TNCCL_NVLS_MIN_BYTES
+  int traceEvents;           // TNCCL_TRACE=1: records per channel (TNCCL_TRACE_EVENTS)
 };
 
 Config loadConfig();

@@ -38,7 +38,17 @@ struct DevComm {
   uint64_t nvlsTileBytes;
   char* nvlsUc;  // this rank's unicast view of the multicast-bound region
   char* nvlsMc;  // multicast view (multimem.* operations)
+  // Phase tracer (TNCCL_TRACE=1): per channel a ring of traceEvents records
+  // {globaltimer ns, tag}; traceCount[c] counts records written. Null when off.
+  uint64_t* trace;
+  uint32_t* traceCount;
+  uint32_t traceEvents;
 };
+
+// Tag of one trace record: algorithm family, phase, tile index (low 16 bits).
+constexpr uint64_t traceTag(int family, int phase, uint64_t tile) {
+  return ((uint64_t)family << 24) | ((uint64_t)phase << 16) | (tile & 0xffffu);
+}
 
 enum DataType : int { kF32 = 0, kBF16 = 1, kF16 = 2 };
 

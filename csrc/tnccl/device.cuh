@@ -104,6 +104,17 @@ __device__ __forceinline__ bool waitFlag(const DevComm& comm, const uint64_t* fl
   return waitSlow(comm, flag, target, where);
 }
 
+// Records a phase boundary of channel c (thread 0 only; no-op when tracing
+// is off).
+__device__ __forceinline__ void traceMark(const DevComm& comm, int c, int family, int phase,
+                                          uint64_t tile) {
+  if (comm.trace == nullptr || threadIdx.x != 0) return;
+  const uint32_t i = comm.traceCount[c]++;
+  uint64_t* rec = comm.trace + ((uint64_t)c * comm.traceEvents + i % comm.traceEvents) * 2;
+  rec[0] = globalTimerNs();
+  rec[1] = traceTag(family, phase, tile);
+}
+
 __device__ __forceinline__ uint64_t* flagPtr(char* base, uint64_t off) {
   return reinterpret_cast<uint64_t*>(base + off);
 }

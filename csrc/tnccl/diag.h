@@ -20,3 +20,30 @@ tncclResult tncclDiagBench(tncclComm_t comm, int mode, size_t bytes, int ctas, i
 #ifdef __cplusplus
 }
 #endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+// Launches one kernel that waits, bounded by timeoutMs, on a device word that
+// is never written. After the stream completes, tncclCommGetAsyncError
+// reports TNCCL_TIMEOUT and the communicator refuses further collectives.
+tncclResult tncclDiagWaitTimeout(tncclComm_t comm, int timeoutMs, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+// Copies the phase-trace records (TNCCL_TRACE=1) of channel `channel` into
+// out (pairs of {globaltimer ns, tag}, oldest first, at most maxRecords) and
+// stores their number in *n. Synchronizes the device first.
+tncclResult tncclCommTraceRead(tncclComm_t comm, int channel, unsigned long long* out,
+                               size_t maxRecords, size_t* n);
+
+#ifdef __cplusplus
+}
+#endif

@@ -80,15 +80,20 @@ std::vector<at::Tensor> lnBwd(const at::Tensor& gy, const c10::optional<at::Tens
   return {dx, wantBf16 ? dxb : at::Tensor(), dw, db};
 }
 
-// logits bf16 [rows, V] (overwritten with d mean-loss / d logits), targets int64
-at::Tensor crossEntropy(at::Tensor logits, const at::Tensor& target, int64_t valid) {
+// logits bf16 [rows, ld] with `classes` real columns (overwritten with
+// d mean-loss / d logits), targets int64
+at::Tensor crossEntropy(at::Tensor logits, const at::Tensor& target, int64_t valid,
+                        int64_t classes) {
   need(logits, at::kBFloat16, "logits");
   need(target, at::kLong, "target");
   TORCH_CHECK(logits.dim() == 2 && target.numel() == logits.size(0), "shape mismatch");
+  const int64_t ld = logits.size(1);
+  if (classes <= 0) classes = ld;
+  TORCH_CHECK(classes <= ld, "more classes than logits columns");
   c10::cuda::CUDAGuard g(logits.device());
   auto loss = at::empty({logits.size(0)}, logits.options().dtype(at::kFloat));
   ok(tnops_cross_entropy_fwd_bwd(bf(logits), target.data_ptr<int64_t>(), loss.data_ptr<float>(),
-                                 (int)logits.size(0), (int)logits.size(1), (int)valid,
+                                 (int)logits.size(0), (int)classes, (int)ld, (int)valid,
                                  streamOf(logits)),
      "tnops_cross_entropy_fwd_bwd");
   return loss;
@@ -142,7 +147,8 @@ void registerOps(py::module_& m) {
           py::arg("eps"));
   ops.def("ln_bwd", &lnBwd, py::arg("grad_y"), py::arg("grad_residual"), py::arg("x_out"),
           py::arg("weight"), py::arg("mean"), py::arg("rstd"), py::arg("want_bf16"));
-  ops.def("cross_entropy_fwd_bwd", &crossEntropy);
+  ops.def("cross_entropy_fwd_bwd", &crossEntropy, py::arg("logits"), py::arg("target"),
+          py::arg("valid"), py::arg("classes") = 0);
   ops.def("scale_bf16_", &scaleBf16);
   ops.def("adamw", &adamw);
   ops.def("launch_count", []() { return tnops_launch_count(); });

@@ -6,9 +6,11 @@
 // communicator to that stream, as the C API requires).
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
+#include <pybind11/stl.h>
 #include <torch/extension.h>
 
 #include <string>
+#include <vector>
 
 #include "diag.h"
 #include "tnccl.h"
@@ -165,6 +167,25 @@ class Communicator {
     return ms;
   }
 
+  // Self test of the bounded device waits (see tncclDiagWaitTimeout).
+  void diagWaitTimeout(int timeoutMs) {
+    live();
+    c10::cuda::CUDAGuard guard(info_.device);
+    check(tncclDiagWaitTimeout(comm_, timeoutMs,
+                               c10::cuda::getCurrentCUDAStream(info_.device).stream()),
+          "tncclDiagWaitTimeout");
+  }
+
+  // Phase-trace records of one channel as a flat list [t0, tag0, t1, tag1, ...].
+  std::vector<uint64_t> traceRead(int channel, int64_t maxRecords) {
+    live();
+    std::vector<unsigned long long> buf((size_t)maxRecords * 2);
+    size_t n = 0;
+    check(tncclCommTraceRead(comm_, channel, buf.data(), (size_t)maxRecords, &n),
+          "tncclCommTraceRead");
+    return std::vector<uint64_t>(buf.begin(), buf.begin() + 2 * n);
+  }
+
   int rank() const { return info_.rank; }
   int size() const { return info_.nranks; }
   int device() const { return info_.device; }
@@ -205,6 +226,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("destroy", &Communicator::destroy)
       .def("info", &Communicator::info)
       .def("diag_bench", &Communicator::diagBench)
+      .def("diag_wait_timeout", &Communicator::diagWaitTimeout)
+      .def("trace_read", &Communicator::traceRead)
       .def_property_readonly("rank", &Communicator::rank)
       .def_property_readonly("size", &Communicator::size)
       .def_property_readonly("device", &Communicator::device)

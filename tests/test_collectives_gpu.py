@@ -45,3 +45,20 @@ def test_two_rank_config2_stress(built):
     r = run([os.path.join(ROOT, "build", "bin", "allreduce_gpu_test"), "2", "stress"], timeout=600,
             env={"TNCCL_TIMEOUT_MS": "10000"})
     assert r.returncode == 0, r.stdout + r.stderr
+
+
+def test_bounded_wait_self_test(built):
+    """A device wait on a word nothing writes gives up after its bound and
+    reports TNCCL_TIMEOUT; the communicator then refuses collectives."""
+    import time
+
+    import tiny_nccl_b200 as tn
+    comm = tn.Communicator(tn.get_unique_id(), 1, 0, device=0)
+    t0 = time.time()
+    comm._c.diag_wait_timeout(300)
+    torch.cuda.synchronize()
+    assert 0.2 < time.time() - t0 < 20
+    assert comm.async_error() == 5
+    with pytest.raises(RuntimeError):
+        comm.all_reduce(torch.ones(16, device="cuda"), scale=2.0)
+    comm.destroy()

@@ -1,0 +1,33 @@
+"""Multi-process tests. GPU ones need 2 GPUs (skipped otherwise); the store
+exchange runs on CPU with gloo ranks."""
+import pytest
+
+from conftest import gpu_count, torchrun
+
+
+@pytest.mark.skipif(gpu_count() > 0, reason="CPU-only behaviour")
+def test_store_exchange_cpu_ranks(built):
+    r = torchrun(2, ["tests/workers/store_exchange_worker.py"], timeout=180)
+    assert r.returncode == 0 and "PASS" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(gpu_count() < 2, reason="needs 2 GPUs")
+def test_ddp_hook_matches_nccl_ddp(built):
+    r = torchrun(2, ["tests/workers/ddp_hook_worker.py"], timeout=600)
+    assert r.returncode == 0 and "PASS" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(gpu_count() < 2, reason="needs 2 GPUs")
+def test_cuda_graph_capture_replay(built):
+    r = torchrun(2, ["tests/workers/graph_capture_worker.py"], timeout=600)
+    assert r.returncode == 0 and "PASS" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(gpu_count() < 2, reason="needs 2 GPUs")
+def test_bounded_wait_timeout_two_ranks(built):
+    env = {"TNCCL_TIMEOUT_MS": "1500", "TNCCL_NVLS_ENABLE": "0", "NCCL_NVLS_ENABLE": "0"}
+    r = torchrun(2, ["tests/workers/timeout_worker.py"], timeout=300, env=env)
+    assert r.returncode == 0 and "PASS" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]

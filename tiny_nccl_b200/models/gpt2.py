@@ -34,9 +34,20 @@ class GPT2Config:
     n_embd: int = 768
     vocab_size: int = 50257
     block_size: int = 1024
+    # Rows of the token-embedding / LM-head matrix are padded to a multiple of
+    # this, so the LM-head GEMMs (N = vocabulary) run on aligned tensor-core
+    # kernels; padded rows are never looked up and padded logits are excluded
+    # from the softmax, so the model computes exactly the same function.
+    vocab_multiple: int = 128
+
+    @property
+    def vocab_padded(self) -> int:
+        m = self.vocab_multiple
+        return (self.vocab_size + m - 1) // m * m
 
     @property
     def n_params(self) -> int:
+        """Parameters of the model (padding rows of the embedding excluded)."""
         d, v, L, t = self.n_embd, self.vocab_size, self.n_layer, self.block_size
         per_layer = 12 * d * d + 13 * d
         return v * d + t * d + L * per_layer + 2 * d
@@ -89,7 +100,7 @@ class GPT2(nn.Module):
             raise ValueError(f"unknown impl {impl!r}")
         self.impl = impl
         c = self.cfg
-        self.wte = nn.Embedding(c.vocab_size, c.n_embd)
+        self.wte = nn.Embedding(c.vocab_padded, c.n_embd)
         self.wpe = nn.Embedding(c.block_size, c.n_embd)
         self.blocks = nn.ModuleList([Block(c) for _ in range(c.n_layer)])
         self.ln_f = nn.LayerNorm(c.n_embd)
@@ -114,6 +125,7 @@ class GPT2(nn.Module):
                 p.normal_(0.0, proj_std, generator=g)
             else:
                 p.normal_(0.0, std, generator=g)
+        self.wte.weight[self.cfg.vocab_size:].zero_()  # padding rows
 
     def _ops(self):
         from .. import ops
@@ -131,9 +143,10 @@ class GPT2(nn.Module):
             x = blk.forward_torch(x)
         x = self.ln_f(x)
         if targets is None:
-            return F.linear(x[:, -1], self.wte.weight)
+            return F.linear(x[:, -1], self.wte.weight)[..., :self.cfg.vocab_size]
         logits = F.linear(x, self.wte.weight)
-        return F.cross_entropy(logits.view(B * T, -1).float(), targets.reshape(-1))
+        V = self.cfg.vocab_size
+        return F.cross_entropy(logits.view(B * T, -1)[:, :V].float(), targets.reshape(-1))
 
     def _forward_fused(self, x: torch.Tensor, targets: torch.Tensor | None):
         """Residual stream kept in fp32; every residual add is fused with the
@@ -151,6 +164,6 @@ class GPT2(nn.Module):
             nxt = self.blocks[i + 1].ln_1 if i + 1 < L else self.ln_f
             x, h = ops.add_layer_norm(x, m, nxt.weight, nxt.bias)
         if targets is None:
-            return F.linear(h.view(B, T, C)[:, -1], self.wte.weight)
+            return F.linear(h.view(B, T, C)[:, -1], self.wte.weight)[..., :self.cfg.vocab_size]
         logits = F.linear(h, self.wte.weight)
-        return ops.cross_entropy(logits, targets.reshape(-1))
+        return ops.cross_entropy(logits, targets.reshape(-1), classes=self.cfg.vocab_size)

@@ -65,9 +65,9 @@ class _CrossEntropy(torch.autograd.Function):
     rescales when the incoming gradient is not 1 (checked on the device)."""
 
     @staticmethod
-    def forward(ctx, logits, target):
+    def forward(ctx, logits, target, classes):
         valid = int(target.numel())
-        per_row = _ops().cross_entropy_fwd_bwd(logits, target, valid)
+        per_row = _ops().cross_entropy_fwd_bwd(logits, target, valid, classes)
         ctx.save_for_backward(logits)
         return per_row.sum() / valid
 
@@ -75,12 +75,14 @@ class _CrossEntropy(torch.autograd.Function):
     def backward(ctx, g):
         (dlogits,) = ctx.saved_tensors
         _ops().scale_bf16_(dlogits, g.reshape(1).float().contiguous())
-        return dlogits, None
+        return dlogits, None, None
 
 
 def cross_entropy(logits: torch.Tensor, target: torch.Tensor,
-                  reuse_logits: bool = True) -> torch.Tensor:
-    """Mean cross-entropy of [rows, V] logits against int64 targets.
+                  reuse_logits: bool = True, classes: int = 0) -> torch.Tensor:
+    """Mean cross-entropy of [rows, ld] logits against int64 targets, over the
+    first ``classes`` columns (all columns when 0; the rest is vocabulary
+    padding, excluded from the softmax and given zero gradient).
 
     With ``reuse_logits`` (the default, used for the model's temporary logits)
     the gradient is written into the logits storage during the forward pass,
@@ -90,7 +92,7 @@ def cross_entropy(logits: torch.Tensor, target: torch.Tensor,
         logits = logits.to(torch.bfloat16)
     elif not reuse_logits:
         logits = logits.clone()
-    return _CrossEntropy.apply(logits.contiguous(), target.contiguous())
+    return _CrossEntropy.apply(logits.contiguous(), target.contiguous(), int(classes))
 
 
 def linear_gelu(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:

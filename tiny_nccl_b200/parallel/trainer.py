@@ -36,7 +36,7 @@ class DataParallelTrainer:
             loss = self.ddp(idx, targets)
         loss.backward()
         self.opt.step()
-        self.opt.zero_grad(set_to_none=False)
+        self.opt.zero_grad(set_to_none=True)
         return loss.detach()
 
     def state_dict(self) -> dict:
