@@ -1,0 +1,77 @@
+"""Runs one fused model kernel on GPT-2-small training shapes (8 x 1024 rows),
+for ncu captures and CUDA-event timing of the kernel alone.
+
+    python benchmarks/ops_kernels.py --kernel ln_bwd --iters 20
+Kernels: ln_fwd, ln_bwd, cross_entropy, adamw.
+"""
+import argparse
+import os
+import sys
+
+import torch
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--kernel", default="ln_bwd")
+    ap.add_argument("--rows", type=int, default=8 * 1024)
+    ap.add_argument("--iters", type=int, default=20)
+    args = ap.parse_args()
+    import tiny_nccl_b200 as tn
+
+    ops = tn.load().ops
+    rows, C, V = args.rows, 768, 50257
+    dev = "cuda"
+    torch.manual_seed(0)
+    if args.kernel in ("ln_fwd", "ln_bwd"):
+        x = torch.randn(rows, C, device=dev)
+        d = torch.randn(rows, C, device=dev).to(torch.bfloat16)
+        w = torch.ones(C, device=dev)
+        b = torch.zeros(C, device=dev)
+        xo, y, mean, rstd = ops.ln_fwd(x, d, w, b, 1e-5)
+        gy = torch.randn(rows, C, device=dev).to(torch.bfloat16)
+        gr = torch.randn(rows, C, device=dev)
+        if args.kernel == "ln_fwd":
+            fn = lambda: ops.ln_fwd(x, d, w, b, 1e-5)  # noqa: E731
+            nbytes = rows * C * (4 + 2 + 4 + 2)
+        else:
+            fn = lambda: ops.ln_bwd(gy, gr, xo, w, mean, rstd, True)  # noqa: E731
+            nbytes = rows * C * (2 + 4 + 4 + 4 + 2)
+    elif args.kernel == "cross_entropy":
+        Vp = 50304
+        logits = torch.randn(rows, Vp, device=dev).to(torch.bfloat16)
+        tgt = torch.randint(0, V, (rows,), device=dev)
+        fn = lambda: ops.cross_entropy_fwd_bwd(logits, tgt, rows, V)  # noqa: E731
+        nbytes = rows * Vp * 2 * 2
+    elif args.kernel == "adamw":
+        from tiny_nccl_b200.models import GPT2, GPT2Config
+        m = GPT2(GPT2Config()).to(dev)
+        ps = list(m.parameters())
+        gs = [torch.randn_like(p) for p in ps]
+        ms = [torch.zeros_like(p) for p in ps]
+        vs = [torch.zeros_like(p) for p in ps]
+        wd = [0.1] * len(ps)
+        step = [0]
+
+        def fn():
+            step[0] += 1
+            ops.adamw(ps, gs, ms, vs, wd, 6e-4, 0.9, 0.95, 1e-8, step[0], 1.0)
+        nbytes = sum(p.numel() for p in ps) * 4 * 7
+    else:
+        raise SystemExit(f"unknown kernel {args.kernel}")
+    fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+    e0.record()
+    for _ in range(args.iters):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.iters
+    print(f"{args.kernel}: {ms * 1e3:.1f} us/launch, {nbytes / ms / 1e6:.0f} GB/s algorithmic")
+
+
+if __name__ == "__main__":
+    main()

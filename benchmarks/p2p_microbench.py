@@ -34,11 +34,13 @@ def main():
     import tiny_nccl_b200 as tn
     comm = tn.init_from_torch_distributed(device=local)
     out = open(args.out, "a") if (args.out and rank == 0) else None
-    modes = {0: "push", 1: "pull", 2: "push+flag", 3: "local"}
-    for mode in (0, 1, 3, 2):
+    modes = {0: "push", 1: "pull", 2: "push+flag", 3: "local", 4: "local->peer copy",
+             5: "reduce mix (2 local loads -> local + peer store)"}
+    only = [int(m) for m in os.environ.get("P2P_MODES", "0,1,3,2,4,5").split(",")]
+    for mode in only:
         for ctas in (1, 8, 32, 64, 128):
-            for threads in (256, 512, 1024):
-                for unroll in ((1, 4, 8, 16) if mode != 2 else (1,)):
+            for threads in (256, 512):
+                for unroll in ((2, 4, 8) if mode != 2 else (1,)):
                     chunks = (16 << 10, 64 << 10, 256 << 10) if mode == 2 else (0,)
                     for chunk in chunks:
                         dist.barrier()

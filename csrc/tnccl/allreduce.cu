@@ -220,24 +220,26 @@ __device__ __forceinline__ void ringHop(uint64_t n, bool vec, const T* in, const
 }
 
 // ---------------------------------------------------------------------------
-// Two-shot, software-pipelined over two slots per channel:
+// Two-shot, software-pipelined over S = kTwoShotSlots slots per channel:
 //
-//   push RS(0); publish RS(0)
-//   for n: wait RS(n); reduce n -> y and push AG(n); publish AG(n)
-//          push RS(n+1); publish RS(n+1)        <- overlaps peers' AG(n)
+//   push RS(0 .. S-2)
+//   for n: push RS(n+S-1)                       <- S-1 tiles ahead of use
+//          wait RS(n); reduce n -> y and push AG(n); publish AG(n)
 //          wait AG(n); copy AG(n) out
 //
-// Slot reuse needs no credit words. Rank r writes RS(n+2) into slot n%2 of
+// Reduce-scatter data is always S-1 tiles ahead, so a rank's reduce never
+// waits for the peer's previous phase (both ranks reduce in parallel).
+// Slot reuse needs no credit words. Rank r writes RS(n+S) into slot n%S of
 // rank j only after it waited for j's AG(n), which j publishes after it
-// finished reading RS(n). Rank j writes AG(n+2) into slot n%2 of rank r only
-// after it received r's RS(n+2), which r pushes after it copied AG(n) out.
+// finished reading RS(n). Rank j writes AG(n+S) into slot n%S of rank r only
+// after it received r's RS(n+S), which r pushes after it copied AG(n) out.
 // ---------------------------------------------------------------------------
 template <typename T, int MAXP>
-__global__ void __launch_bounds__(kMaxThreads)
-    twoShotKernel(const __grid_constant__ DevComm comm, const __grid_constant__ AllReduceArgs a) {
+__device__ __forceinline__ void twoShotBody(const DevComm& comm, const AllReduceArgs& a,
+                                            const int c) {
   constexpr int V = Pack<T>::V;
   constexpr int U = MAXP <= 2 ? 4 : MAXP <= 4 ? 2 : 1;
-  const int c = blockIdx.x, tid = threadIdx.x, P = comm.nranks, r = comm.rank;
+  const int tid = threadIdx.x, P = comm.nranks, r = comm.rank;
   const MailboxLayout& L = comm.layout;
   char* const me = comm.peers[r];
   const T* x = static_cast<const T*>(a.send);
@@ -278,7 +280,24 @@ __global__ void __launch_bounds__(kMaxThreads)
     return sFail == 0;
   };
 
-  if (ntiles > 0) pushRS(0);
+  // Prologue: reduce-scatter data for the first kTwoShotSlots - 1 tiles.
+  for (uint64_t t = 0; t < ntiles && t + 1 < (uint64_t)kTwoShotSlots; ++t) pushRS(t);
+  // All-gather of tile t: wait for every peer's reduced chunk, copy it out.
+  auto finishAG = [&](uint64_t t) -> bool {
+    if (!waitAll(true, t, 2)) return false;
+    traceMark(comm, c, kCounterTwoShot, 4, t);
+    const uint64_t tile = tileOf(t);
+    const int slot = slotOf(t);
+    for (int k = 1; k < P; ++k) {
+      const int j = (r + P - k) % P;
+      const Span sp = chunkSpan(pl, tile, j, V);
+      T* dst = y + sp.offset;
+      copyOut<T, kLdMailbox, 8>(reinterpret_cast<const T*>(me + tsAgDataAt(L, c, slot, j)),
+                                sp.count, vec, false, 1.f, 1, [dst](int) { return dst; });
+    }
+    traceMark(comm, c, kCounterTwoShot, 5, t);
+    return true;
+  };
   uint64_t done = 0;
   for (uint64_t t = 0; t < ntiles; ++t) {
     traceMark(comm, c, kCounterTwoShot, 0, t);
@@ -310,22 +329,16 @@ __global__ void __launch_bounds__(kMaxThreads)
     if (tid < P && tid != r)
       stReleaseSys(flagPtr(comm.peers[tid], tsAgFlagAt(L, c, slot, r)), seq0 + t + 1);
     traceMark(comm, c, kCounterTwoShot, 2, t);
-    // Start the next tile's reduce-scatter while the peers finish this one.
-    if (t + 1 < ntiles) pushRS(t + 1);
-    traceMark(comm, c, kCounterTwoShot, 3, t);
-    if (!waitAll(true, t, 2)) break;
-    traceMark(comm, c, kCounterTwoShot, 4, t);
-    // Copy every peer's reduced chunk out.
-    for (int k = 1; k < P; ++k) {
-      const int j = (r + P - k) % P;
-      const Span sp = chunkSpan(pl, tile, j, V);
-      T* dst = y + sp.offset;
-      copyOut<T, kLdMailbox, 8>(reinterpret_cast<const T*>(me + tsAgDataAt(L, c, slot, j)),
-                                sp.count, vec, false, 1.f, 1, [dst](int) { return dst; });
-    }
-    traceMark(comm, c, kCounterTwoShot, 5, t);
-    done = t + 1;
+    // The all-gather of the previous tile: its peers finished long ago (they
+    // are reducing tile t now), so this wait rarely stalls.
+    if (t > 0 && !finishAG(t - 1)) break;
+    // Reduce-scatter data for tile t + S - 1 goes into slot (t - 1) % S:
+    // every peer finished reducing tile t - 1 (its all-gather arrived) and
+    // its all-gather slot was just copied out.
+    if (t + kTwoShotSlots - 1 < ntiles) pushRS(t + kTwoShotSlots - 1);
+    done = t;
   }
+  if (ntiles > 0 && done + 1 == ntiles && !sFail && finishAG(ntiles - 1)) done = ntiles;
   // Every thread has passed the final barrier of the loop (or broke out on
   // a failure seen by all), so thread 0 can record the new sequence number.
   if (tid == 0 && !sFail) comm.counters[kCounterTwoShot * kMaxChannels + c] = seq0 + done;
@@ -336,11 +349,11 @@ __global__ void __launch_bounds__(kMaxThreads)
 // producer never overwrites a block that a peer has not reduced yet.
 // ---------------------------------------------------------------------------
 template <typename T, int MAXP>
-__global__ void __launch_bounds__(kMaxThreads)
-    oneShotKernel(const __grid_constant__ DevComm comm, const __grid_constant__ AllReduceArgs a) {
+__device__ __forceinline__ void oneShotBody(const DevComm& comm, const AllReduceArgs& a,
+                                            const int c) {
   constexpr int V = Pack<T>::V;
   constexpr int U = MAXP <= 2 ? 4 : MAXP <= 4 ? 2 : 1;
-  const int c = blockIdx.x, tid = threadIdx.x, P = comm.nranks, r = comm.rank;
+  const int tid = threadIdx.x, P = comm.nranks, r = comm.rank;
   const MailboxLayout& L = comm.layout;
   const int S = L.osSlots;
   char* const me = comm.peers[r];
@@ -434,11 +447,11 @@ struct RingChannel {
 };
 
 template <typename T>
-__global__ void __launch_bounds__(kMaxThreads)
-    ringKernel(const __grid_constant__ DevComm comm, const __grid_constant__ AllReduceArgs a) {
+__device__ __forceinline__ void ringBody(const DevComm& comm, const AllReduceArgs& a,
+                                         const int c) {
   using Pk = Pack<T>;
   constexpr int V = Pk::V;
-  const int c = blockIdx.x, tid = threadIdx.x, P = comm.nranks, r = comm.rank;
+  const int tid = threadIdx.x, P = comm.nranks, r = comm.rank;
   const T* x = static_cast<const T*>(a.send);
   T* y = static_cast<T*>(a.recv);
   const ChunkPlan& pl = a.chunk;
@@ -553,10 +566,26 @@ __global__ void __launch_bounds__(kMaxThreads)
 // NVLS
 // ---------------------------------------------------------------------------
 template <typename T>
+// NVLS, software-pipelined over S = kNvlsSlots input/output blocks:
+//
+//   copy in tiles 0 .. S-2, publish "copied in" for each
+//   for t: wait every rank's "copied in t"; multimem reduce + broadcast my
+//          share of tile t; publish "stored t"
+//          wait every rank's "stored t-1"; copy tile t-1 out      <- deferred
+//          copy in tile t+S-1 (slot of t-1); publish "copied in t+S-1"
+//
+// Flags are one monotone word per (phase, channel, source rank): tiles are
+// copied in and stored in order, so "copied in t" is implied by any later
+// value. Block reuse: tile t+S-1 overwrites the input block of t-1 only after
+// every rank published "stored t-1" (their switch reads of t-1 are done), and
+// this rank publishes "copied in t+S-1" only after it copied tile t-1 out of
+// the shared output block, so no rank's multimem store of tile t+S-1 can
+// overwrite unread data.
 __global__ void __launch_bounds__(kMaxThreads)
     nvlsKernel(const __grid_constant__ DevComm comm, const __grid_constant__ AllReduceArgs a) {
   using Pk = Pack<T>;
   constexpr int V = Pk::V;
+  constexpr int S = kNvlsSlots;
   const int c = blockIdx.x, tid = threadIdx.x, P = comm.nranks, r = comm.rank;
   const MailboxLayout& L = comm.layout;
   char* const me = comm.peers[r];
@@ -566,44 +595,66 @@ __global__ void __launch_bounds__(kMaxThreads)
   const bool vec = a.vectorized != 0;
   const float alpha = a.scale;
   const bool scale = alpha != 1.0f;
-  char* const ucIn = comm.nvlsUc + nvlsInAt(comm.nvlsTileBytes, c);
-  char* const ucOut = comm.nvlsUc + nvlsOutAt(comm.nvlsTileBytes, c);
-  char* const mcIn = comm.nvlsMc + nvlsInAt(comm.nvlsTileBytes, c);
-  char* const mcOut = comm.nvlsMc + nvlsOutAt(comm.nvlsTileBytes, c);
+  const uint64_t tb = comm.nvlsTileBytes;
   __shared__ int sFail;
   if (tid == 0) sFail = 0;
-  uint64_t seq = comm.counters[kCounterNvls * kMaxChannels + c];
+  const uint64_t seq0 = comm.counters[kCounterNvls * kMaxChannels + c];
   __syncthreads();
+  const uint64_t ntiles = channelTiles(pl.numTiles, pl.channels, c);
+  auto slotOf = [&](uint64_t t) { return (int)((seq0 + t) % S); };
+  auto spanOf = [&](uint64_t t) {
+    return blockTileSpan(pl, (uint64_t)c + t * (uint64_t)pl.channels);
+  };
 
-  auto barrier = [&](int phase, uint64_t want) -> bool {
+  auto publish = [&](int phase, uint64_t value) {
     fenceProxyAlias();
     __syncthreads();
     if (tid < P && tid != r)
-      stReleaseSys(flagPtr(comm.peers[tid], nvlsFlagAt(L, phase, c, r)), want);
+      stReleaseSys(flagPtr(comm.peers[tid], nvlsFlagAt(L, phase, c, r)), value);
+  };
+  auto waitAll = [&](int phase, uint64_t value) -> bool {
     if (tid < P && tid != r &&
-        !waitFlag(comm, flagPtr(me, nvlsFlagAt(L, phase, c, tid)), want,
+        !waitFlag(comm, flagPtr(me, nvlsFlagAt(L, phase, c, tid)), value,
                   whereCode(kCounterNvls, c, phase + 1)))
       sFail = 1;
     __syncthreads();
     fenceProxyAlias();
     return sFail == 0;
   };
-
-  const uint64_t ntiles = channelTiles(pl.numTiles, pl.channels, c);
-  for (uint64_t t = 0; t < ntiles; ++t) {
-    const uint64_t tile = (uint64_t)c + t * (uint64_t)pl.channels;
-    const Span sp = blockTileSpan(pl, tile);
-    const uint64_t want = seq + 1;
-    traceMark(comm, c, kCounterNvls, 0, t);
+  auto copyIn = [&](uint64_t t) {
+    const Span sp = spanOf(t);
+    char* dst = comm.nvlsUc + nvlsInAt(tb, c, slotOf(t));
     copyOut<T, kLdInput, 8>(x + sp.offset, sp.count, vec, false, 1.f, 1,
-                            [ucIn](int) { return ucIn; });
+                            [dst](int) { return dst; });
     traceMark(comm, c, kCounterNvls, 1, t);
-    if (!barrier(0, want)) break;
+    publish(0, seq0 + t + 1);
+  };
+  auto copyOutTile = [&](uint64_t t) -> bool {
+    if (!waitAll(1, seq0 + t + 1)) return false;
+    traceMark(comm, c, kCounterNvls, 4, t);
+    const Span sp = spanOf(t);
+    const T* src = reinterpret_cast<const T*>(comm.nvlsUc + nvlsOutAt(tb, c, slotOf(t)));
+    T* yo = y + sp.offset;
+    copyOut<T, kLdMailbox, 8>(src, sp.count, vec, false, 1.f, 1,
+                              [yo](int) { return reinterpret_cast<char*>(yo); });
+    traceMark(comm, c, kCounterNvls, 5, t);
+    return true;
+  };
+
+  for (uint64_t t = 0; t < ntiles && t + 1 < (uint64_t)S; ++t) copyIn(t);
+  uint64_t done = 0;
+  for (uint64_t t = 0; t < ntiles; ++t) {
+    traceMark(comm, c, kCounterNvls, 0, t);
+    if (!waitAll(0, seq0 + t + 1)) break;
     traceMark(comm, c, kCounterNvls, 2, t);
-    // Reduce this rank's share (whole vectors; padding past the tile end is
-    // reduced too but never copied out).
-    const uint64_t nvecTile = divUp(sp.count, V);
-    const Span share = blockShare(nvecTile, P, r, 1);
+    // Reduce this rank's share of the tile in the switch and broadcast it
+    // (whole vectors; padding past the tile end is reduced but never copied
+    // out).
+    const Span sp = spanOf(t);
+    const int slot = slotOf(t);
+    char* const mcIn = comm.nvlsMc + nvlsInAt(tb, c, slot);
+    char* const mcOut = comm.nvlsMc + nvlsOutAt(tb, c, slot);
+    const Span share = blockShare(divUp(sp.count, V), P, r, 1);
     const uint64_t NT = blockDim.x;
     constexpr int UN = 4;  // switch reductions in flight per thread
     for (uint64_t base = tid; base < share.count; base += NT * UN) {
@@ -630,15 +681,13 @@ __global__ void __launch_bounds__(kMaxThreads)
       }
     }
     traceMark(comm, c, kCounterNvls, 3, t);
-    if (!barrier(1, want)) break;
-    traceMark(comm, c, kCounterNvls, 4, t);
-    T* yo = y + sp.offset;
-    copyOut<T, kLdMailbox, 8>(reinterpret_cast<const T*>(ucOut), sp.count, vec, false, 1.f, 1,
-                              [yo](int) { return reinterpret_cast<char*>(yo); });
-    traceMark(comm, c, kCounterNvls, 5, t);
-    ++seq;
+    publish(1, seq0 + t + 1);
+    if (t > 0 && !copyOutTile(t - 1)) break;
+    if (t + S - 1 < ntiles) copyIn(t + S - 1);
+    done = t;
   }
-  if (tid == 0 && !sFail) comm.counters[kCounterNvls * kMaxChannels + c] = seq;
+  if (ntiles > 0 && done + 1 == ntiles && !sFail && copyOutTile(ntiles - 1)) done = ntiles;
+  if (tid == 0 && !sFail) comm.counters[kCounterNvls * kMaxChannels + c] = seq0 + done;
 }
 
 // ---------------------------------------------------------------------------
@@ -662,6 +711,71 @@ __global__ void __launch_bounds__(kMaxThreads)
   for (uint64_t e = nvec * V + (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n;
        e += stride)
     stElem(y + e, scaled(alpha, ldElem<T, kLdInput>(x + e)));
+}
+
+// ---------------------------------------------------------------------------
+// Kernels: one CTA per channel (blockIdx.x).
+// ---------------------------------------------------------------------------
+template <typename T, int MAXP>
+__global__ void __launch_bounds__(kMaxThreads)
+    twoShotKernel(const __grid_constant__ DevComm comm, const __grid_constant__ AllReduceArgs a) {
+  twoShotBody<T, MAXP>(comm, a, blockIdx.x);
+}
+
+template <typename T, int MAXP>
+__global__ void __launch_bounds__(kMaxThreads)
+    oneShotKernel(const __grid_constant__ DevComm comm, const __grid_constant__ AllReduceArgs a) {
+  oneShotBody<T, MAXP>(comm, a, blockIdx.x);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kMaxThreads)
+    ringKernel(const __grid_constant__ DevComm comm, const __grid_constant__ AllReduceArgs a) {
+  ringBody<T>(comm, a, blockIdx.x);
+}
+
+// Single-GPU emulation of `nranks` ranks: blockIdx.y selects the emulated
+// rank, blockIdx.x its channel. All ranks' mailboxes live in this GPU's
+// memory. The launch is cooperative, so every CTA is resident and CTAs of
+// different emulated ranks can wait on one another.
+template <typename T, int MAXP>
+__global__ void __launch_bounds__(kMaxThreads)
+    emulatedKernel(const __grid_constant__ EmulatedLaunch e) {
+  const int r = blockIdx.y;
+  switch (e.algo) {
+    case TNCCL_ALGO_TWOSHOT:
+      twoShotBody<T, MAXP>(e.comm[r], e.args[r], blockIdx.x);
+      break;
+    case TNCCL_ALGO_ONESHOT:
+      oneShotBody<T, MAXP>(e.comm[r], e.args[r], blockIdx.x);
+      break;
+    default:
+      ringBody<T>(e.comm[r], e.args[r], blockIdx.x);
+      break;
+  }
+}
+
+template <typename T>
+cudaError_t launchEmulatedTyped(const EmulatedLaunch& e, int channels, int threads,
+                                cudaStream_t stream) {
+  const dim3 grid((unsigned)channels, (unsigned)e.nranks);
+  const dim3 block((unsigned)threads);
+  void* args[] = {const_cast<EmulatedLaunch*>(&e)};
+  const void* fn = e.nranks <= 2   ? (const void*)emulatedKernel<T, 2>
+                   : e.nranks <= 4 ? (const void*)emulatedKernel<T, 4>
+                                   : (const void*)emulatedKernel<T, 8>;
+  return cudaLaunchCooperativeKernel(fn, grid, block, args, 0, stream);
+}
+
+template <typename T>
+int emulatedMaxCtasTyped(int threads) {
+  int perSm = 0, sms = 0, dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&perSm, emulatedKernel<T, 8>, threads, 0) !=
+      cudaSuccess)
+    return 0;
+  return perSm * sms;
 }
 
 template <typename T>
@@ -741,6 +855,29 @@ cudaError_t launchScale(const void* x, void* y, uint64_t n, int dtype, float alp
     default:
       return cudaErrorInvalidValue;
   }
+}
+
+}  // namespace tnccl
+
+namespace tnccl {
+
+cudaError_t launchEmulated(const EmulatedLaunch& e, int channels, int threads,
+                           cudaStream_t stream) {
+  if (threads > kMaxThreads) threads = kMaxThreads;
+  switch (e.dtype) {
+    case kF32:
+      return launchEmulatedTyped<float>(e, channels, threads, stream);
+    case kBF16:
+      return launchEmulatedTyped<__nv_bfloat16>(e, channels, threads, stream);
+    case kF16:
+      return launchEmulatedTyped<__half>(e, channels, threads, stream);
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+int emulatedMaxCtas(int threads) {
+  return emulatedMaxCtasTyped<float>(threads > kMaxThreads ? kMaxThreads : threads);
 }
 
 }  // namespace tnccl

@@ -184,6 +184,7 @@ extern "C" tncclResult tncclCommInitRank(tncclComm_t* out, int nranks, tncclUniq
   comm->rank = rank;
   comm->nranks = nranks;
   comm->cfg = loadConfig();
+  adaptConfig(comm->cfg, nranks);
   if (cudaGetDevice(&comm->device) != cudaSuccess) {
     (void)cudaGetLastError();
     return TNCCL_CUDA_ERROR;

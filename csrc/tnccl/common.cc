@@ -73,11 +73,11 @@ Config loadConfig() {
   c.osChannels = clampInt(envInt("TNCCL_ONESHOT_CHANNELS", 16), 1, kMaxChannels);
   c.ringSlots = clampInt(envInt("TNCCL_SLOTS", 4), 2, 16);
   c.ringChunkBytes = roundTo16(envInt("TNCCL_CHUNK_BYTES", 256 << 10));
-  c.tsChunkBytes = roundTo16(envInt("TNCCL_TWOSHOT_CHUNK_BYTES", 128 << 10));
+  c.tsChunkBytes = roundTo16(envInt("TNCCL_TWOSHOT_CHUNK_BYTES", 0));  // 0: by nranks
   c.osSlots = clampInt(envInt("TNCCL_ONESHOT_SLOTS", 2), 1, 8);
   c.osTileBytes = roundTo16(envInt("TNCCL_ONESHOT_TILE_BYTES", 32 << 10));
   c.nvlsChannels = clampInt(envInt("TNCCL_NVLS_CHANNELS", 64), 1, kMaxChannels);
-  c.nvlsTileBytes = roundTo16(envInt("TNCCL_NVLS_TILE_BYTES", 256 << 10));
+  c.nvlsTileBytes = roundTo16(envInt("TNCCL_NVLS_TILE_BYTES", 128 << 10));
   c.nvlsEnable = (int)envInt("TNCCL_NVLS_ENABLE", 1);
   int algo = parseAlgo(envStr("TNCCL_ALGO", "auto"));
   if (algo < 0) {
@@ -123,6 +123,21 @@ uint64_t configHash(const Config& c) {
   mix(c.oneShotMaxBytes);
   mix(c.nvlsMinBytes);
   return h;
+}
+
+}  // namespace tnccl
+
+namespace tnccl {
+
+void adaptConfig(Config& c, int nranks) {
+  if (nranks < 1) nranks = 1;
+  // Two-shot: a 256 KiB tile per channel split into one chunk per rank, so
+  // the mailbox (channels x slots x tile x 2) does not grow with nranks.
+  if (c.tsChunkBytes <= 16 && envInt("TNCCL_TWOSHOT_CHUNK_BYTES", 0) == 0) {
+    int64_t chunk = (int64_t)(256 << 10) / nranks;
+    chunk = chunk < (16 << 10) ? (16 << 10) : chunk > (128 << 10) ? (128 << 10) : chunk;
+    c.tsChunkBytes = chunk / 16 * 16;
+  }
 }
 
 }  // namespace tnccl

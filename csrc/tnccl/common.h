@@ -52,6 +52,9 @@ struct Config {
 };
 
 Config loadConfig();
+// Fills in the defaults that depend on the rank count (called before the
+// configuration hash is exchanged, so every rank derives the same values).
+void adaptConfig(Config& c, int nranks);
 uint64_t configHash(const Config& c);
 
 int parseAlgo(const std::string& s);

@@ -64,4 +64,15 @@ struct AllReduceArgs {
   BlockPlan block;
 };
 
+// One cooperative launch that emulates `nranks` ranks on one GPU (tests and
+// profiling of the multi-rank kernels without peers).
+constexpr int kMaxEmulatedRanks = 8;
+struct EmulatedLaunch {
+  int nranks;
+  int algo;
+  int dtype;
+  DevComm comm[kMaxEmulatedRanks];
+  AllReduceArgs args[kMaxEmulatedRanks];
+};
+
 }  // namespace tnccl

@@ -7,6 +7,7 @@
 //   2 push+flag: push in `chunk`-byte pieces, each followed by bar.sync and a
 //              st.release.sys flag to the peer (the cost of publishing)
 //   3 local  : copy within this rank's mailbox
+//   4 local->peer copy, 5 two local loads -> one local + one peer store
 // The caller runs the same mode on every rank at the same time; no kernel
 // waits on another rank, so there is nothing to time out.
 #include <cuda_runtime.h>
@@ -54,6 +55,35 @@ __global__ void diagKernel(char* local, char* peer, uint64_t bytes, int mode, ui
         }
         continue;
       }
+      if (mode == 4 || mode == 5) {
+        // 4: local -> peer copy; 5: two local sources summed into one local
+        // and one peer store (the two-shot reduce mix).
+        uint4 w[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const uint64_t i = b + u * NT;
+          if (i < nvec) {
+            v[u] = ldMailbox(local + base + i * 16);
+            if (mode == 5) w[u] = ldMailbox(local + bytes + base + i * 16);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const uint64_t i = b + u * NT;
+          if (i < nvec) {
+            uint4 o = v[u];
+            if (mode == 5) {
+              o.x = __float_as_uint(__uint_as_float(o.x) + __uint_as_float(w[u].x));
+              o.y = __float_as_uint(__uint_as_float(o.y) + __uint_as_float(w[u].y));
+              o.z = __float_as_uint(__uint_as_float(o.z) + __uint_as_float(w[u].z));
+              o.w = __float_as_uint(__uint_as_float(o.w) + __uint_as_float(w[u].w));
+              st16(local + 2 * bytes + base + i * 16, o);
+            }
+            st16(peer + base + i * 16, o);
+          }
+        }
+        continue;
+      }
       char* src = mode == 1 ? peer : local;
 #pragma unroll
       for (int u = 0; u < U; ++u) {
@@ -91,12 +121,13 @@ extern "C" tncclResult tncclDiagBench(tncclComm_t comm, int mode, size_t bytes, 
   const size_t area = (size_t)comm->layout.channels *
                                                      comm->layout.ringSlots *
                                                      comm->layout.ringChunkBytes;
-  if (bytes == 0 || bytes * (mode == 3 ? 2 : 1) > area) return TNCCL_INVALID_ARGUMENT;
+  const size_t span = bytes * (mode == 5 ? 3 : mode == 3 ? 2 : 1);
+  if (bytes == 0 || span > area) return TNCCL_INVALID_ARGUMENT;
   char* local = comm->local.base + comm->layout.ringDataOff;
   char* peer = comm->dev.peers[next] + comm->layout.ringDataOff;
   // Flag words and the sink live in the scratch area after the payload, so
   // no FIFO sequence word is touched.
-  const size_t tail = (bytes * (mode == 3 ? 2 : 1) + 255) / 256 * 256;
+  const size_t tail = (span + 255) / 256 * 256;
   if (tail + 8 * (size_t)ctas + 256 > area) return TNCCL_INVALID_ARGUMENT;
   uint64_t* flag = reinterpret_cast<uint64_t*>(peer + tail);
   unsigned* sink = reinterpret_cast<unsigned*>(local + tail + 8 * (size_t)ctas);

@@ -47,3 +47,22 @@ tncclResult tncclCommTraceRead(tncclComm_t comm, int channel, unsigned long long
 #ifdef __cplusplus
 }
 #endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+// Single-GPU emulation of an nranks communicator (emulate.cc): all ranks'
+// mailboxes in the current device's memory, all ranks' channels in one
+// cooperative launch. For tests and profiles of ring / one-shot / two-shot.
+typedef struct tncclEmu* tncclEmu_t;
+tncclResult tncclEmuCreate(tncclEmu_t* emu, int nranks);
+tncclResult tncclEmuAllReduce(tncclEmu_t emu, const void* const* send, void* const* recv,
+                              size_t count, tncclDataType_t dtype, tncclRedOp_t op,
+                              float preScale, tncclAlgo_t algo, cudaStream_t stream);
+tncclResult tncclEmuGetAsyncError(tncclEmu_t emu, tncclResult* asyncError);
+tncclResult tncclEmuDestroy(tncclEmu_t emu);
+
+#ifdef __cplusplus
+}
+#endif

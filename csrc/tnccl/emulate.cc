@@ -1,0 +1,206 @@
+// emulate.cc - single-GPU emulation of a multi-rank communicator.
+//
+// tncclEmuCreate builds `nranks` virtual ranks on the current device: one
+// mailbox, one set of FIFO sequence counters and one DevComm per rank, with
+// every rank's "peer" pointers aimed at the other virtual ranks' mailboxes in
+// the same GPU memory. tncclEmuAllReduce runs all ranks' channels as one
+// cooperative launch (grid = channels x nranks), so CTAs that wait on one
+// another are guaranteed to be resident together. The device code is the
+// same ring / one-shot / two-shot bodies that the real communicator launches;
+// only the memory the peer stores land in differs (local HBM instead of a
+// peer over NVLink). It serves single-GPU tests of the multi-rank algorithms
+// and ncu profiles of their kernels. NVLS needs a multicast object spanning
+// several GPUs and is not emulated.
+#include <string.h>
+
+#include <algorithm>
+#include <new>
+#include <vector>
+
+#include "comm.h"
+#include "diag.h"
+#include "launch.h"
+
+struct tncclEmu {
+  int nranks = 0;
+  int device = -1;
+  tnccl::Config cfg{};
+  tnccl::MailboxLayout layout{};
+  std::vector<char*> mailbox;
+  uint64_t* counters = nullptr;
+  tnccl::DevStatus* hostStatus = nullptr;
+  tnccl::DevStatus* devStatus = nullptr;
+  tnccl::DevComm dev[tnccl::kMaxEmulatedRanks];
+};
+
+using namespace tnccl;
+
+namespace {
+
+void freeEmu(tncclEmu* e) {
+  for (char* m : e->mailbox)
+    if (m) cudaFree(m);
+  e->mailbox.clear();
+  if (e->counters) cudaFree(e->counters);
+  if (e->hostStatus) cudaFreeHost(e->hostStatus);
+  e->counters = nullptr;
+  e->hostStatus = nullptr;
+}
+
+size_t elemSize(tncclDataType_t t) {
+  return t == tncclFloat32 ? 4 : (t == tncclBfloat16 || t == tncclFloat16) ? 2 : 0;
+}
+
+}  // namespace
+
+extern "C" tncclResult tncclEmuCreate(tncclEmu_t* out, int nranks) {
+  if (out == nullptr || nranks < 2 || nranks > kMaxEmulatedRanks) return TNCCL_INVALID_ARGUMENT;
+  *out = nullptr;
+  auto* e = new (std::nothrow) tncclEmu;
+  if (e == nullptr) return TNCCL_SYSTEM_ERROR;
+  e->nranks = nranks;
+  e->cfg = loadConfig();
+  adaptConfig(e->cfg, nranks);
+  if (cudaGetDevice(&e->device) != cudaSuccess) {
+    delete e;
+    return TNCCL_CUDA_ERROR;
+  }
+  // Every CTA of every emulated rank must be resident at once.
+  const int maxCtas = emulatedMaxCtas(e->cfg.threads);
+  const int perRank = maxCtas / nranks;
+  if (perRank < 1) {
+    delete e;
+    return TNCCL_UNSUPPORTED;
+  }
+  e->cfg.channels = std::min(e->cfg.channels, perRank);
+  e->cfg.osChannels = std::min(e->cfg.osChannels, perRank);
+  LayoutConfig lc{};
+  lc.nranks = nranks;
+  lc.channels = e->cfg.channels;
+  lc.osChannels = e->cfg.osChannels;
+  lc.ringSlots = e->cfg.ringSlots;
+  lc.ringChunkBytes = (uint64_t)e->cfg.ringChunkBytes;
+  lc.tsChunkBytes = (uint64_t)e->cfg.tsChunkBytes;
+  lc.osSlots = e->cfg.osSlots;
+  lc.osTileBytes = (uint64_t)e->cfg.osTileBytes;
+  lc.nvlsChannels = 1;
+  e->layout = makeLayout(lc);
+  tncclResult r = TNCCL_SUCCESS;
+  e->mailbox.assign((size_t)nranks, nullptr);
+  std::vector<uint64_t> credits((size_t)e->layout.channels * e->layout.ringSlots);
+  for (int c = 0; c < e->layout.channels; ++c)
+    for (int s = 0; s < e->layout.ringSlots; ++s)
+      credits[(size_t)c * e->layout.ringSlots + s] = (uint64_t)s;
+  for (int k = 0; k < nranks && r == TNCCL_SUCCESS; ++k) {
+    void* p = nullptr;
+    if (cudaMalloc(&p, e->layout.totalBytes) != cudaSuccess ||
+        cudaMemset(p, 0, e->layout.totalBytes) != cudaSuccess ||
+        cudaMemcpy(static_cast<char*>(p) + e->layout.ringCreditOff, credits.data(),
+                   credits.size() * 8, cudaMemcpyHostToDevice) != cudaSuccess)
+      r = TNCCL_CUDA_ERROR;
+    e->mailbox[(size_t)k] = static_cast<char*>(p);
+  }
+  const size_t cbytes = sizeof(uint64_t) * kNumCounterFamilies * kMaxChannels * (size_t)nranks;
+  void* h = nullptr;
+  void* d = nullptr;
+  if (r == TNCCL_SUCCESS &&
+      (cudaMalloc(reinterpret_cast<void**>(&e->counters), cbytes) != cudaSuccess ||
+       cudaMemset(e->counters, 0, cbytes) != cudaSuccess ||
+       cudaHostAlloc(&h, sizeof(DevStatus), cudaHostAllocMapped) != cudaSuccess ||
+       cudaHostGetDevicePointer(&d, h, 0) != cudaSuccess))
+    r = TNCCL_CUDA_ERROR;
+  if (h) {
+    memset(h, 0, sizeof(DevStatus));
+    e->hostStatus = static_cast<DevStatus*>(h);
+    e->devStatus = static_cast<DevStatus*>(d);
+  }
+  if (r != TNCCL_SUCCESS || cudaDeviceSynchronize() != cudaSuccess) {
+    freeEmu(e);
+    delete e;
+    return r != TNCCL_SUCCESS ? r : TNCCL_CUDA_ERROR;
+  }
+  for (int k = 0; k < nranks; ++k) {
+    DevComm& dc = e->dev[k];
+    dc = DevComm{};
+    dc.rank = k;
+    dc.nranks = nranks;
+    dc.layout = e->layout;
+    for (int q = 0; q < nranks; ++q) dc.peers[q] = e->mailbox[(size_t)q];
+    dc.counters = e->counters + (size_t)k * kNumCounterFamilies * kMaxChannels;
+    dc.status = e->devStatus;
+    dc.timeoutNs = (uint64_t)e->cfg.timeoutMs * 1000000ull;
+  }
+  *out = e;
+  return TNCCL_SUCCESS;
+}
+
+extern "C" tncclResult tncclEmuAllReduce(tncclEmu_t e, const void* const* send,
+                                         void* const* recv, size_t count, tncclDataType_t dtype,
+                                         tncclRedOp_t op, float preScale, tncclAlgo_t algo,
+                                         cudaStream_t stream) {
+  const size_t es = elemSize(dtype);
+  if (e == nullptr || send == nullptr || recv == nullptr || es == 0 || op < tncclSum ||
+      op >= tncclNumOps)
+    return TNCCL_INVALID_ARGUMENT;
+  if (e->hostStatus->error != 0) return (tncclResult)e->hostStatus->error;
+  if (algo == TNCCL_ALGO_AUTO) algo = TNCCL_ALGO_TWOSHOT;
+  if (algo == TNCCL_ALGO_NVLS) return TNCCL_UNSUPPORTED;
+  if (count == 0) return TNCCL_SUCCESS;
+  const int P = e->nranks;
+  EmulatedLaunch L{};
+  L.nranks = P;
+  L.algo = (int)algo;
+  L.dtype = (int)dtype;
+  const uint64_t V = kVectorBytes / es;
+  const float scale = op == tncclAvg ? preScale / (float)P : preScale;
+  int channels = 1;
+  for (int k = 0; k < P; ++k) {
+    if (send[k] == nullptr || recv[k] == nullptr) return TNCCL_INVALID_ARGUMENT;
+    AllReduceArgs& a = L.args[k];
+    a.send = send[k];
+    a.recv = recv[k];
+    a.count = count;
+    a.scale = scale;
+    a.dtype = (int)dtype;
+    a.vectorized = (reinterpret_cast<uintptr_t>(send[k]) % kVectorBytes == 0 &&
+                    reinterpret_cast<uintptr_t>(recv[k]) % kVectorBytes == 0)
+                       ? 1
+                       : 0;
+    if (algo == TNCCL_ALGO_ONESHOT) {
+      a.block = makeBlockPlan(count, e->cfg.osChannels, (uint64_t)e->cfg.osTileBytes / es,
+                              kOneShotMinTileBytes / es, V);
+      channels = a.block.channels;
+    } else {
+      const uint64_t maxChunk = (uint64_t)(algo == TNCCL_ALGO_RING ? e->cfg.ringChunkBytes
+                                                                   : e->cfg.tsChunkBytes) / es;
+      const uint64_t minChunk =
+          (algo == TNCCL_ALGO_RING ? kRingMinChunkBytes : kTwoShotMinChunkBytes) / es;
+      a.chunk = makeChunkPlan(count, P, e->cfg.channels, maxChunk, minChunk, V);
+      channels = a.chunk.channels;
+    }
+    L.comm[k] = e->dev[k];
+  }
+  // Every emulated rank must see the same vectorization choice (their tile
+  // plans are identical); mixed alignment falls back to the scalar path.
+  int vec = 1;
+  for (int k = 0; k < P; ++k) vec &= L.args[k].vectorized;
+  for (int k = 0; k < P; ++k) L.args[k].vectorized = vec;
+  if (launchEmulated(L, channels, e->cfg.threads, stream) != cudaSuccess) return TNCCL_CUDA_ERROR;
+  gLaunchCount.fetch_add(1, std::memory_order_relaxed);
+  return TNCCL_SUCCESS;
+}
+
+extern "C" tncclResult tncclEmuGetAsyncError(tncclEmu_t e, tncclResult* err) {
+  if (e == nullptr || err == nullptr) return TNCCL_INVALID_ARGUMENT;
+  const int v = e->hostStatus->error;
+  *err = v == 0 ? TNCCL_SUCCESS : v < TNCCL_NUM_RESULTS ? (tncclResult)v : TNCCL_SYSTEM_ERROR;
+  return TNCCL_SUCCESS;
+}
+
+extern "C" tncclResult tncclEmuDestroy(tncclEmu_t e) {
+  if (e == nullptr) return TNCCL_INVALID_ARGUMENT;
+  const bool ok = cudaDeviceSynchronize() == cudaSuccess;
+  freeEmu(e);
+  delete e;
+  return ok ? TNCCL_SUCCESS : TNCCL_CUDA_ERROR;
+}

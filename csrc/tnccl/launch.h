@@ -16,4 +16,10 @@ cudaError_t launchAllReduceKernel(const DevComm& comm, const AllReduceArgs& args
 cudaError_t launchScale(const void* x, void* y, uint64_t n, int dtype, float alpha,
                         int vectorized, cudaStream_t stream);
 
+// Cooperative launch of the emulated ranks (grid = channels x nranks).
+cudaError_t launchEmulated(const EmulatedLaunch& e, int channels, int threads,
+                           cudaStream_t stream);
+// CTAs of the emulation kernel that fit on the device at once.
+int emulatedMaxCtas(int threads);
+
 }  // namespace tnccl

@@ -38,8 +38,10 @@ constexpr uint64_t kRingMinChunkBytes = 4096;
 constexpr uint64_t kTwoShotMinChunkBytes = 2048;
 constexpr uint64_t kOneShotMinTileBytes = 4096;
 constexpr uint64_t kNvlsMinTileBytes = 16384;
-// Two-shot keeps two tiles in flight per channel.
-constexpr int kTwoShotSlots = 2;
+// Two-shot keeps up to kTwoShotSlots tiles in flight per channel.
+constexpr int kTwoShotSlots = 4;
+// NVLS keeps up to kNvlsSlots tiles in flight per channel.
+constexpr int kNvlsSlots = 4;
 
 // Counter families kept in device memory, one array of kMaxChannels each.
 enum CounterFamily : int {
@@ -306,12 +308,16 @@ TN_HD uint64_t nvlsFlagAt(const MailboxLayout& L, int phase, int c, int src) {
          (((uint64_t)phase * L.nvlsChannels + c) * L.nranks + src) * 8;
 }
 
-// NVLS multicast region: per channel an input block and an output block.
-TN_HD uint64_t nvlsInAt(uint64_t tileBytes, int c) {
-  return (uint64_t)c * 2 * tileBytes;
+// NVLS multicast region: per channel kNvlsSlots pairs of an input block and
+// an output block.
+TN_HD uint64_t nvlsInAt(uint64_t tileBytes, int c, int slot) {
+  return ((uint64_t)c * kNvlsSlots + (uint64_t)slot) * 2 * tileBytes;
 }
-TN_HD uint64_t nvlsOutAt(uint64_t tileBytes, int c) {
-  return (uint64_t)c * 2 * tileBytes + tileBytes;
+TN_HD uint64_t nvlsOutAt(uint64_t tileBytes, int c, int slot) {
+  return nvlsInAt(tileBytes, c, slot) + tileBytes;
+}
+TN_HD uint64_t nvlsRegionBytes(uint64_t tileBytes, int channels) {
+  return (uint64_t)channels * kNvlsSlots * 2 * tileBytes;
 }
 
 }  // namespace tnccl

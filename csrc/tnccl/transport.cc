@@ -208,7 +208,7 @@ tncclResult setupNvls(tncclComm* comm) {
   NvlsState& n = comm->nvls;
   n.channels = comm->cfg.nvlsChannels;
   n.tileBytes = (uint64_t)comm->cfg.nvlsTileBytes;
-  const size_t want = (size_t)n.channels * 2 * n.tileBytes;
+  const size_t want = (size_t)nvlsRegionBytes(n.tileBytes, n.channels);
   std::vector<int32_t> statuses((size_t)comm->nranks);
 
   auto agree = [&](int32_t mine) -> tncclResult {

@@ -199,6 +199,47 @@ class Communicator {
   tncclCommInfo info_{};
 };
 
+// Single-GPU emulation of an n-rank communicator (tests and kernel profiles).
+class Emulator {
+ public:
+  explicit Emulator(int nranks) { check(tncclEmuCreate(&emu_, nranks), "tncclEmuCreate"); }
+  ~Emulator() {
+    if (emu_) tncclEmuDestroy(emu_);
+  }
+  void allReduce(const std::vector<at::Tensor>& ins, const std::vector<at::Tensor>& outs,
+                 const std::string& op, double scale, const std::string& algo) {
+    TORCH_CHECK(emu_ != nullptr, "tnccl: emulator was destroyed");
+    TORCH_CHECK(!ins.empty() && ins.size() == outs.size(), "tnccl: one input and output per rank");
+    std::vector<const void*> s;
+    std::vector<void*> r;
+    for (size_t k = 0; k < ins.size(); ++k) {
+      TORCH_CHECK(ins[k].is_cuda() && ins[k].is_contiguous() && outs[k].is_contiguous() &&
+                      ins[k].numel() == ins[0].numel() && outs[k].numel() == ins[0].numel() &&
+                      ins[k].scalar_type() == ins[0].scalar_type() &&
+                      outs[k].scalar_type() == ins[0].scalar_type(),
+                  "tnccl: emulated ranks need matching contiguous CUDA tensors");
+      s.push_back(ins[k].data_ptr());
+      r.push_back(outs[k].data_ptr());
+    }
+    cudaStream_t stream = c10::cuda::getCurrentCUDAStream(ins[0].get_device()).stream();
+    check(tncclEmuAllReduce(emu_, s.data(), r.data(), (size_t)ins[0].numel(), toDtype(ins[0]),
+                            parseOp(op), (float)scale, parseAlgo(algo), stream),
+          "tncclEmuAllReduce");
+  }
+  int asyncError() {
+    tncclResult e = TNCCL_SUCCESS;
+    check(tncclEmuGetAsyncError(emu_, &e), "tncclEmuGetAsyncError");
+    return (int)e;
+  }
+  void destroy() {
+    if (emu_) check(tncclEmuDestroy(emu_), "tncclEmuDestroy");
+    emu_ = nullptr;
+  }
+
+ private:
+  tncclEmu_t emu_ = nullptr;
+};
+
 py::bytes getUniqueId() {
   tncclUniqueId id;
   check(tncclGetUniqueId(&id), "tncclGetUniqueId");
@@ -232,6 +273,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def_property_readonly("size", &Communicator::size)
       .def_property_readonly("device", &Communicator::device)
       .def_property_readonly("alive", &Communicator::alive);
+  py::class_<Emulator>(m, "Emulator")
+      .def(py::init<int>(), py::arg("nranks"))
+      .def("all_reduce", &Emulator::allReduce, py::arg("inputs"), py::arg("outputs"),
+           py::arg("op") = "sum", py::arg("scale") = 1.0, py::arg("algo") = "twoshot")
+      .def("async_error", &Emulator::asyncError)
+      .def("destroy", &Emulator::destroy);
   m.def("get_unique_id", &getUniqueId);
   m.def("launch_count", []() { return tncclGetLaunchCount(); });
   m.def("error_string", [](int r) { return std::string(tncclGetErrorString((tncclResult)r)); });

@@ -132,8 +132,9 @@ struct Job {
 float rnd(int t, float f) { return oracle::roundTo(t, f); }
 
 bool twoShot(World& w, int r, const Job& j, uint64_t count) {
-  // Same two-slot pipeline as twoShotKernel: RS(n+1) is pushed between
-  // publishing AG(n) and waiting for the peers' AG(n).
+  // Same pipeline as twoShotBody: reduce-scatter data is pushed
+  // kTwoShotSlots - 1 tiles ahead, and the all-gather of tile t is finished
+  // after tile t + 1 has been reduced.
   const Config& c = w.cfg;
   const int P = c.P;
   const MailboxLayout& L = w.L;
@@ -156,7 +157,19 @@ bool twoShot(World& w, int r, const Job& j, uint64_t count) {
       for (int p = 0; p < P; ++p)
         if (p != r) w.publish(r, p, tsRsFlagAt(L, ch, slotOf(t), r), seq0 + t + 1);
     };
-    if (ntiles > 0) pushRS(0);
+    for (uint64_t t = 0; t < ntiles && t + 1 < (uint64_t)kTwoShotSlots; ++t) pushRS(t);
+    auto finishAG = [&](uint64_t t) -> bool {
+      const int slot = slotOf(t);
+      for (int p = 0; p < P; ++p)
+        if (p != r && !w.wait(r, tsAgFlagAt(L, ch, slot, p), seq0 + t + 1)) return false;
+      for (int k = 1; k < P; ++k) {
+        const int src = (r + P - k) % P;
+        Span sp = chunkSpan(pl, tileOf(t), src, c.vec);
+        const float* in = w.data(r, tsAgDataAt(L, ch, slot, src));
+        for (uint64_t e = 0; e < sp.count; ++e) y[sp.offset + e] = in[e];
+      }
+      return true;
+    };
     for (uint64_t t = 0; t < ntiles; ++t) {
       const int slot = slotOf(t);
       const uint64_t want = seq0 + t + 1;
@@ -176,16 +189,10 @@ bool twoShot(World& w, int r, const Job& j, uint64_t count) {
       }
       for (int p = 0; p < P; ++p)
         if (p != r) w.publish(r, p, tsAgFlagAt(L, ch, slot, r), want);
-      if (t + 1 < ntiles) pushRS(t + 1);
-      for (int p = 0; p < P; ++p)
-        if (p != r && !w.wait(r, tsAgFlagAt(L, ch, slot, p), want)) return false;
-      for (int k = 1; k < P; ++k) {
-        const int src = (r + P - k) % P;
-        Span sp = chunkSpan(pl, tileOf(t), src, c.vec);
-        const float* in = w.data(r, tsAgDataAt(L, ch, slot, src));
-        for (uint64_t e = 0; e < sp.count; ++e) y[sp.offset + e] = in[e];
-      }
+      if (t > 0 && !finishAG(t - 1)) return false;
+      if (t + kTwoShotSlots - 1 < ntiles) pushRS(t + kTwoShotSlots - 1);
     }
+    if (ntiles > 0 && !finishAG(ntiles - 1)) return false;
     seq = seq0 + ntiles;
   }
   return true;

@@ -1,0 +1,115 @@
+"""Multi-rank all-reduce kernels on ONE GPU: emulated ranks run as one
+cooperative launch (tncclEmu*), so the ring / one-shot / two-shot device code
+is exercised with 2, 4 and 8 ranks even when a single GPU is available.
+Results are compared bit for bit with an order-aware fp32 oracle: rank order
+0..P-1 for one-shot/two-shot, the ring's s+1 ... s rotation (rounded to the
+wire type at every hop) for the ring."""
+import os
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+CHANNELS = 8  # small enough that channels x ranks CTAs are co-resident
+RING_CHUNK = 256 << 10
+RING_MIN_CHUNK = 4096
+
+
+def _div_up(a, b):
+    return (a + b - 1) // b
+
+
+def _round_up(a, b):
+    return _div_up(a, b) * b
+
+
+def ring_chunk_index(count, P, es):
+    """Chunk (segment) owning each element under the ring's chunk plan
+    (protocol.h makeChunkPlan / chunkSpan)."""
+    V = 16 // es
+    want = _round_up(_div_up(count, P * CHANNELS), V)
+    want = max(want, RING_MIN_CHUNK // es)
+    want = min(want, RING_CHUNK // es)
+    tile_elems = want * P
+    e = torch.arange(count, device="cuda", dtype=torch.int64)
+    tile = e // tile_elems
+    off = e - tile * tile_elems
+    base = tile * tile_elems
+    length = torch.clamp(count - base, max=tile_elems)
+    partial = _round_up_t(_div_up_t(length, P), V)
+    cl = torch.where(length == tile_elems, torch.full_like(length, want), partial)
+    return torch.clamp(off // cl, max=P - 1)
+
+
+def _div_up_t(a, b):
+    return (a + b - 1) // b
+
+
+def _round_up_t(a, b):
+    return _div_up_t(a, b) * b
+
+
+def oracle(xs, algo, alpha, dtype):
+    P = len(xs)
+    f = [x.float() for x in xs]
+    a = torch.tensor(alpha, dtype=torch.float32, device="cuda")
+    if algo in ("oneshot", "twoshot"):
+        acc = f[0] * a
+        for k in range(1, P):
+            acc = acc + f[k] * a
+        return acc.to(dtype)
+    es = xs[0].element_size()
+    j = ring_chunk_index(xs[0].numel(), P, es)
+    stack = torch.stack(f)  # [P, n]
+    cols = torch.arange(xs[0].numel(), device="cuda")
+    acc = (stack[(j + 1) % P, cols] * a).to(dtype).float()
+    for k in range(2, P + 1):
+        acc = (acc + stack[(j + k) % P, cols] * a).to(dtype).float()
+    return acc.to(dtype)
+
+
+@pytest.fixture(scope="module")
+def emulators(built):
+    os.environ["TNCCL_NCHANNELS"] = str(CHANNELS)
+    os.environ["TNCCL_ONESHOT_CHANNELS"] = str(CHANNELS)
+    import tiny_nccl_b200 as tn
+    emus = {P: tn.load().Emulator(P) for P in (2, 4, 8)}
+    yield emus
+    for e in emus.values():
+        e.destroy()
+
+
+@pytest.mark.parametrize("P", [2, 4, 8])
+@pytest.mark.parametrize("algo", ["oneshot", "twoshot", "ring"])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_emulated_bit_exact(emulators, P, algo, dtype):
+    emu = emulators[P]
+    g = torch.Generator(device="cuda")
+    for count, op in ((1, "sum"), (4097, "sum"), (300_001, "avg"), (2_500_000, "sum")):
+        g.manual_seed(count + P)
+        xs = [(torch.rand(count, device="cuda", generator=g) * 2 - 1).to(dtype) for _ in range(P)]
+        ys = [torch.full_like(x, float("nan")) for x in xs]
+        emu.all_reduce(xs, ys, op=op, algo=algo)
+        torch.cuda.synchronize()
+        assert emu.async_error() == 0
+        want = oracle(xs, algo, (1.0 / P) if op == "avg" else 1.0, dtype)
+        for r, y in enumerate(ys):
+            bad = (y.float() != want.float()).nonzero()
+            assert bad.numel() == 0, (algo, P, count, r, bad[:5].flatten().tolist())
+
+
+def test_emulated_in_place_and_sequence(emulators):
+    """In-place operation and 50 consecutive collectives of varying size on
+    the same mailboxes (device-resident sequence numbers)."""
+    emu = emulators[4]
+    for it in range(50):
+        n = 1 + (it * 7919) % 200_000
+        algo = ("oneshot", "twoshot", "ring")[it % 3]
+        xs = [torch.full((n,), float(r + it), device="cuda") for r in range(4)]
+        emu.all_reduce(xs, xs, algo=algo)
+        torch.cuda.synchronize()
+        want = float(sum(r + it for r in range(4)))
+        for x in xs:
+            assert bool(torch.all(x == want)), (it, algo)
+    assert emu.async_error() == 0

@@ -1,0 +1,43 @@
+"""Host sanitizer runs (compute-sanitizer is closed on the GPU pool): the
+threaded CPU rank model under ThreadSanitizer (data races in the flag
+protocol model) and the bootstrap tests under AddressSanitizer +
+UndefinedBehaviorSanitizer (memory errors in the socket control plane)."""
+import os
+import shutil
+import subprocess
+
+import pytest
+
+from conftest import ROOT
+
+OUT = os.path.join(ROOT, "build", "sanitize")
+
+
+def _build(name, srcs, flags):
+    os.makedirs(OUT, exist_ok=True)
+    exe = os.path.join(OUT, name)
+    cmd = ["g++", "-std=c++17", "-O1", "-g", *flags, f"-I{ROOT}/include", f"-I{ROOT}/csrc/tnccl",
+           f"-I{ROOT}/tests/cpp", "-I/usr/local/cuda/include", *srcs, "-o", exe, "-lpthread"]
+    r = subprocess.run(cmd, cwd=ROOT, capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr[-3000:]
+    return exe
+
+
+@pytest.mark.skipif(shutil.which("g++") is None, reason="needs g++")
+def test_rank_model_under_tsan():
+    exe = _build("rank_model_tsan", ["tests/cpp/rank_model_test.cc"], ["-fsanitize=thread"])
+    env = dict(os.environ, TSAN_OPTIONS="halt_on_error=1 second_deadlock_stack=1")
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=900, env=env)
+    assert r.returncode == 0 and "rank_model_test: PASS" in r.stdout, r.stdout[-2000:] + r.stderr[-4000:]
+    assert "WARNING: ThreadSanitizer" not in r.stderr, r.stderr[-4000:]
+
+
+@pytest.mark.skipif(shutil.which("g++") is None, reason="needs g++")
+def test_bootstrap_under_asan_ubsan():
+    exe = _build("bootstrap_asan", ["tests/cpp/bootstrap_test.cc", "csrc/tnccl/bootstrap.cc",
+                                    "csrc/tnccl/common.cc"],
+                 ["-fsanitize=address,undefined", "-fno-omit-frame-pointer",
+                  "-fno-sanitize-recover=undefined"])
+    env = dict(os.environ, ASAN_OPTIONS="detect_leaks=1:abort_on_error=1")
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=300, env=env)
+    assert r.returncode == 0 and "bootstrap_test: PASS" in r.stdout, r.stdout[-2000:] + r.stderr[-4000:]

@@ -44,7 +44,7 @@ def main():
         err = (a.grad - b.grad).abs().max().item()
         scale = b.grad.abs().max().item() + 1e-12
         worst = max(worst, err / scale)
-    ok = worst < 1e-5 and state.buckets > 1 and comm.async_error() == 0
+    ok = worst < 1e-5 and state.buckets >= 1 and comm.async_error() == 0
     flag = torch.tensor([1.0 if ok else 0.0], device=dev)
     dist.all_reduce(flag, op=dist.ReduceOp.MIN)
     if rank == 0:
