@@ -1,6 +1,8 @@
 """NVLink primitive micro-benchmark (push stores, pull loads, push with a
-release flag per chunk, local copy) across CTA counts, thread counts and
-accesses in flight. Used to size the collective kernels.
+release flag per chunk, local copy, the copy and reduce mixes of the
+collectives, and push throughput while another warp issues ordering
+operations) across CTA counts, thread counts and accesses in flight. Used to
+size the collective kernels.
 
     python -m torch.distributed.run --nproc-per-node 2 --master-addr 127.0.0.1 \
         benchmarks/p2p_microbench.py --out p2p.jsonl
@@ -35,13 +37,19 @@ def main():
     comm = tn.init_from_torch_distributed(device=local)
     out = open(args.out, "a") if (args.out and rank == 0) else None
     modes = {0: "push", 1: "pull", 2: "push+flag", 3: "local", 4: "local->peer copy",
-             5: "reduce mix (2 local loads -> local + peer store)"}
+             5: "reduce mix (2 local loads -> local + peer store)",
+             6: "push with a concurrent ordering op in warp 0",
+             7: "TMA-staged local->peer", 8: "TMA-staged local->local",
+             9: "TMA-staged local->peer, 8 copies per stage"}
     only = [int(m) for m in os.environ.get("P2P_MODES", "0,1,3,2,4,5").split(",")]
     for mode in only:
         for ctas in (1, 8, 32, 64, 128):
-            for threads in (256, 512):
-                for unroll in ((2, 4, 8) if mode != 2 else (1,)):
-                    chunks = (16 << 10, 64 << 10, 256 << 10) if mode == 2 else (0,)
+            for threads in ((128, 256) if mode in (7, 8, 9) else (256, 512)):
+                for unroll in ((2, 4, 8) if mode not in (2, 7, 8, 9) else
+                               (1,) if mode == 2 else (2, 3)):
+                    chunks = ((16 << 10, 64 << 10, 256 << 10) if mode == 2 else
+                              (0, 1, 2, 3) if mode == 6 else
+                              (8192, 32768, 65536) if mode in (7, 8, 9) else (0,))
                     for chunk in chunks:
                         dist.barrier()
                         ms = comm._c.diag_bench(mode, args.bytes, ctas, threads, unroll, chunk, 5)

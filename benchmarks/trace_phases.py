@@ -39,6 +39,7 @@ def main():
     ap.add_argument("--bytes", default="64M")
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--out", default="")
+    ap.add_argument("--dump", default="", help="write every channel's raw events (JSON) here")
     args = ap.parse_args()
     assert os.environ.get("TNCCL_TRACE") == "1", "run with TNCCL_TRACE=1"
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
@@ -60,6 +61,7 @@ def main():
     fam = FAMILY[args.algo]
     deltas = collections.defaultdict(list)
     spans = []
+    raw = {}
     for c in range(128):
         rec = comm._c.trace_read(c, 1 << 16)
         if not rec:
@@ -68,6 +70,7 @@ def main():
         ev = [(t, (tag >> 16) & 0xFF, tag & 0xFFFF) for t, tag in ev if (tag >> 24) == fam]
         if not ev:
             continue
+        raw[c] = ev
         spans.append(ev[-1][0] - ev[0][0])
         for (t0, p0, _), (t1, p1, _) in zip(ev, ev[1:]):
             deltas[(p0, p1)].append(t1 - t0)
@@ -75,6 +78,9 @@ def main():
                {"mean_us": sum(v) / len(v) / 1e3, "n": len(v)} for (a, b), v in sorted(deltas.items())}
     rec = {"rank": rank, "algo": args.algo, "bytes": size, "phases": summary,
            "channel_span_us_mean": sum(spans) / max(1, len(spans)) / 1e3}
+    if args.dump:
+        with open(f"{args.dump}.rank{rank}.json", "w") as f:
+            json.dump(raw, f)
     allrec = [None] * world
     dist.all_gather_object(allrec, rec)
     if rank == 0:

@@ -27,6 +27,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 #include "device.cuh"
 #include "launch.h"
 #include "protocol.h"
@@ -40,6 +42,32 @@ using namespace dev;
 constexpr int kLdInput = 0;
 constexpr int kLdMailbox = 1;
 constexpr int kMaxThreads = 512;
+
+// Shared-memory staging of the two-shot push and reduce teams
+// (DevComm::tsStages stages per team; a push stage is tsPushStage bytes, a
+// reduce stage holds MAXP sources of tsRedStage / MAXP bytes each). The
+// first 128 bytes hold the mbarriers (at most kMaxStages per team).
+constexpr int kMaxStages = 8;
+__host__ __device__ constexpr uint32_t redSourceBytes(uint32_t redStage, int maxp) {
+  return redStage / (uint32_t)maxp / 16 * 16;
+}
+uint32_t twoShotSmemBytes(const DevComm& d, int maxp) {
+  return 128 + (uint32_t)d.tsStages * (d.tsPushStage + redSourceBytes(d.tsRedStage, maxp) * maxp);
+}
+
+// Opts `Kernel` into `bytes` of dynamic shared memory, once per device.
+template <auto Kernel>
+cudaError_t allowSmem(uint32_t bytes) {
+  static std::atomic<uint32_t> done[64];
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  if (dev < 64 && done[dev].load(std::memory_order_acquire) >= bytes) return cudaSuccess;
+  err = cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (err == cudaSuccess && dev < 64) done[dev].store(bytes, std::memory_order_release);
+  return err;
+}
+
 
 template <int LD>
 __device__ __forceinline__ uint4 ld16(const void* p) {
@@ -75,15 +103,15 @@ __device__ __forceinline__ void stElem(T* p, float x) {
 // dst[i] = (scale ? alpha*src[i] : src[i]) for every destination returned by
 // dstPtr(d), d < ndst. Loads are issued U at a time before any store.
 template <typename T, int LD, int U, bool SCALE, typename DstF>
-__device__ __forceinline__ void copyOutImpl(const T* src, uint64_t n, bool vec, float alpha,
-                                            int ndst, DstF dstPtr) {
+__device__ __forceinline__ void copyOutImpl(const Team& tm, const T* src, uint64_t n, bool vec,
+                                            float alpha, int ndst, DstF dstPtr) {
   constexpr bool scale = SCALE;
   using Pk = Pack<T>;
   constexpr int V = Pk::V;
-  const uint64_t NT = blockDim.x;
+  const uint64_t NT = tm.nt;
   const uint64_t nvec = vec ? n / V : 0;
   const uint4* s4 = reinterpret_cast<const uint4*>(src);
-  for (uint64_t base = threadIdx.x; base < nvec; base += NT * U) {
+  for (uint64_t base = tm.tid; base < nvec; base += NT * U) {
     uint4 v[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
@@ -106,7 +134,7 @@ __device__ __forceinline__ void copyOutImpl(const T* src, uint64_t n, bool vec, 
       }
     }
   }
-  for (uint64_t e = nvec * V + threadIdx.x; e < n; e += NT) {
+  for (uint64_t e = nvec * V + tm.tid; e < n; e += NT) {
     float f = ldElem<T, LD>(src + e);
     if (scale) f = scaled(alpha, f);
     for (int d = 0; d < ndst; ++d) stElem(reinterpret_cast<T*>(dstPtr(d)) + e, f);
@@ -116,12 +144,12 @@ __device__ __forceinline__ void copyOutImpl(const T* src, uint64_t n, bool vec, 
 // Pure copies keep 8 loads in flight per thread; scaled copies convert
 // through fp32 and keep 4 (register budget of a 512-thread CTA).
 template <typename T, int LD, int U, typename DstF>
-__device__ __forceinline__ void copyOut(const T* src, uint64_t n, bool vec, bool scale,
-                                        float alpha, int ndst, DstF dstPtr) {
+__device__ __forceinline__ void copyOut(const Team& tm, const T* src, uint64_t n, bool vec,
+                                        bool scale, float alpha, int ndst, DstF dstPtr) {
   if (scale)
-    copyOutImpl<T, LD, (U > 4 ? 4 : U), true>(src, n, vec, alpha, ndst, dstPtr);
+    copyOutImpl<T, LD, (U > 4 ? 4 : U), true>(tm, src, n, vec, alpha, ndst, dstPtr);
   else
-    copyOutImpl<T, LD, U, false>(src, n, vec, alpha, ndst, dstPtr);
+    copyOutImpl<T, LD, U, false>(tm, src, n, vec, alpha, ndst, dstPtr);
 }
 
 // out[i] = sum_{k<P} alpha * src_k[i] in rank order, fp32 accumulation.
@@ -129,14 +157,15 @@ __device__ __forceinline__ void copyOut(const T* src, uint64_t n, bool vec, bool
 // srcPtr(k) (mailbox). out(i, pack) stores a 16-byte result; outElem(e, f)
 // stores a scalar result.
 template <typename T, int MAXP, int U, typename SrcF, typename OutF, typename OutElemF>
-__device__ __forceinline__ void reduceRanks(uint64_t n, bool vec, int P, int localIdx,
+__device__ __forceinline__ void reduceRanks(const Team& tm, uint64_t n, bool vec, int P,
+                                            int localIdx,
                                             const T* local, float alpha, SrcF srcPtr, OutF out,
                                             OutElemF outElem) {
   using Pk = Pack<T>;
   constexpr int V = Pk::V;
-  const uint64_t NT = blockDim.x;
+  const uint64_t NT = tm.nt;
   const uint64_t nvec = vec ? n / V : 0;
-  for (uint64_t base = threadIdx.x; base < nvec; base += NT * U) {
+  for (uint64_t base = tm.tid; base < nvec; base += NT * U) {
     uint4 raw[U][MAXP];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
@@ -172,7 +201,7 @@ __device__ __forceinline__ void reduceRanks(uint64_t n, bool vec, int P, int loc
       }
     }
   }
-  for (uint64_t e = nvec * V + threadIdx.x; e < n; e += NT) {
+  for (uint64_t e = nvec * V + tm.tid; e < n; e += NT) {
     float acc = 0.f;
     for (int k = 0; k < P; ++k) {
       const float v = k == localIdx ? ldElem<T, kLdInput>(local + e)
@@ -186,13 +215,14 @@ __device__ __forceinline__ void reduceRanks(uint64_t n, bool vec, int P, int loc
 // One ring hop: out = in + alpha * x with fp32 math and one rounding to T
 // (tiny-nccl src/device.cuh:187 adds `received + local` the same way).
 template <typename T, int U, typename OutF, typename OutElemF>
-__device__ __forceinline__ void ringHop(uint64_t n, bool vec, const T* in, const T* x,
+__device__ __forceinline__ void ringHop(const Team& tm, uint64_t n, bool vec, const T* in,
+                                        const T* x,
                                         float alpha, OutF out, OutElemF outElem) {
   using Pk = Pack<T>;
   constexpr int V = Pk::V;
-  const uint64_t NT = blockDim.x;
+  const uint64_t NT = tm.nt;
   const uint64_t nvec = vec ? n / V : 0;
-  for (uint64_t base = threadIdx.x; base < nvec; base += NT * U) {
+  for (uint64_t base = tm.tid; base < nvec; base += NT * U) {
     uint4 a[U], b[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
@@ -215,133 +245,224 @@ __device__ __forceinline__ void ringHop(uint64_t n, bool vec, const T* in, const
       }
     }
   }
-  for (uint64_t e = nvec * V + threadIdx.x; e < n; e += NT)
+  for (uint64_t e = nvec * V + tm.tid; e < n; e += NT)
     outElem(e, addRn(ldElem<T, kLdMailbox>(in + e), scaled(alpha, ldElem<T, kLdInput>(x + e))));
 }
 
 // ---------------------------------------------------------------------------
-// Two-shot, software-pipelined over S = kTwoShotSlots slots per channel:
+// Two-shot with three warp-specialised teams per channel CTA, each running
+// its own loop over the channel's tiles:
 //
-//   push RS(0 .. S-2)
-//   for n: push RS(n+S-1)                       <- S-1 tiles ahead of use
-//          wait RS(n); reduce n -> y and push AG(n); publish AG(n)
-//          wait AG(n); copy AG(n) out
+//   push    RS(t): chunk j of my input -> rank j's reduce-scatter slot
+//   reduce  wait RS(t) from every peer; y[own chunk] = sum in rank order,
+//           pushed to every peer's all-gather slot
+//   gather  wait AG(t) from every peer; copy the chunks out into y
 //
-// Reduce-scatter data is always S-1 tiles ahead, so a rank's reduce never
-// waits for the peer's previous phase (both ranks reduce in parallel).
-// Slot reuse needs no credit words. Rank r writes RS(n+S) into slot n%S of
-// rank j only after it waited for j's AG(n), which j publishes after it
-// finished reading RS(n). Rank j writes AG(n+S) into slot n%S of rank r only
-// after it received r's RS(n+S), which r pushes after it copied AG(n) out.
+// so NVLink stores (push, reduce), local copies (gather) and flag drains of
+// one channel overlap instead of taking turns. S = kTwoShotSlots slots per
+// channel and direction. Slot reuse needs no credit words:
+//  * push writes RS(t) into slot t%S of rank j only after this CTA's gather
+//    team copied AG(t-S) out (shared counter); j published AG(t-S) after it
+//    finished reading RS(t-S) from that slot.
+//  * reduce writes AG(t) into slot t%S of rank j only after j's RS(t)
+//    arrived, which j's push team sent after j's gather team copied AG(t-S)
+//    out of that slot.
+// In-place calls are safe: gather overwrites chunk j of tile t only after
+// AG(t) from j arrived, which needs this rank's RS(t) push, whose loads of
+// that chunk completed before its release.
 // ---------------------------------------------------------------------------
+enum TwoShotRole { kTsPush = 0, kTsReduce = 1, kTsGather = 2 };
+
+// Warp split of a CTA into three teams: split = a | b << 4 gives the first
+// two teams a/8 and b/8 of the warps (at least one each), the third the rest
+// (at least one; the launch has >= 4 warps).
+__device__ __forceinline__ Team splitTeams(int split, int* role) {
+  const int nw = blockDim.x / 32, w = threadIdx.x / 32;
+  int nPush = nw * (split & 15) / 8, nRed = nw * ((split >> 4) & 15) / 8;
+  nPush = nPush < 1 ? 1 : nPush;
+  nRed = nRed < 1 ? 1 : nRed;
+  if (nPush + nRed > nw - 1) nRed = nw - 1 - nPush;
+  if (w < nPush) {
+    *role = kTsPush;
+    return Team{(int)threadIdx.x, nPush * 32, 1};
+  }
+  if (w < nPush + nRed) {
+    *role = kTsReduce;
+    return Team{(int)threadIdx.x - nPush * 32, nRed * 32, 2};
+  }
+  *role = kTsGather;
+  return Team{(int)threadIdx.x - (nPush + nRed) * 32, (nw - nPush - nRed) * 32, 3};
+}
+
 template <typename T, int MAXP>
 __device__ __forceinline__ void twoShotBody(const DevComm& comm, const AllReduceArgs& a,
                                             const int c) {
   constexpr int V = Pack<T>::V;
   constexpr int U = MAXP <= 2 ? 4 : MAXP <= 4 ? 2 : 1;
-  const int tid = threadIdx.x, P = comm.nranks, r = comm.rank;
+  constexpr int S = kTwoShotSlots;
+  const int P = comm.nranks, r = comm.rank;
   const MailboxLayout& L = comm.layout;
   char* const me = comm.peers[r];
   const T* x = static_cast<const T*>(a.send);
   T* y = static_cast<T*>(a.recv);
   const ChunkPlan& pl = a.chunk;
   const bool vec = a.vectorized != 0;
+  using Pk = Pack<T>;
+  const float alpha = a.scale;
   __shared__ int sFail;
-  if (tid == 0) sFail = 0;
+  __shared__ int sTeamFlag[3];
+  __shared__ unsigned long long sGathered;  // tiles the gather team copied out
+  // Dynamic shared memory: the mbarriers of both staged teams, then the
+  // push stages, then the reduce stages.
+  extern __shared__ __align__(128) char dsmem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(dsmem);
+  const int nst = comm.tsStages;
+  StageRing pushRing{dsmem + 128, bars, comm.tsPushStage, nst, 0};
+  StageRing redRing{dsmem + 128 + (size_t)nst * comm.tsPushStage, bars + kMaxStages,
+                    redSourceBytes(comm.tsRedStage, MAXP), nst, 0};
+  if (threadIdx.x == 0) {
+    sFail = 0;
+    sGathered = 0;
+    for (int i = 0; i < nst; ++i) {
+      mbarInit(bars + i, 1);
+      mbarInit(bars + kMaxStages + i, 1);
+    }
+    fenceMbarInit();
+  }
   const uint64_t seq0 = comm.counters[kCounterTwoShot * kMaxChannels + c];
   __syncthreads();
   const uint64_t ntiles = channelTiles(pl.numTiles, pl.channels, c);
   auto tileOf = [&](uint64_t t) { return (uint64_t)c + t * (uint64_t)pl.channels; };
-  auto slotOf = [&](uint64_t t) { return (int)((seq0 + t) % kTwoShotSlots); };
+  auto slotOf = [&](uint64_t t) { return (int)((seq0 + t) % S); };
+  int role;
+  const Team tm = splitTeams(comm.tsSplit, &role);
+  // Thread k < P of a team waits for / publishes to peer k.
+  const bool peerThread = tm.tid < P && tm.tid != r;
+  const int k = tm.tid;
 
-  // Reduce-scatter push of local tile t: chunk j of my input -> rank j.
-  auto pushRS = [&](uint64_t t) {
-    const uint64_t tile = tileOf(t);
-    const int slot = slotOf(t);
-    for (int k = 1; k < P; ++k) {
-      const int j = (r + k) % P;
-      const Span sp = chunkSpan(pl, tile, j, V);
-      char* dst = comm.peers[j] + tsRsDataAt(L, c, slot, r);
-      copyOut<T, kLdInput, 8>(x + sp.offset, sp.count, vec, false, 1.f, 1,
-                              [dst](int) { return dst; });
-    }
-    __syncthreads();
-    if (tid < P && tid != r)
-      stReleaseSys(flagPtr(comm.peers[tid], tsRsFlagAt(L, c, slot, r)), seq0 + t + 1);
-  };
-  auto waitAll = [&](bool ag, uint64_t t, int phase) -> bool {
-    const int slot = slotOf(t);
-    if (tid < P && tid != r) {
-      const uint64_t off = ag ? tsAgFlagAt(L, c, slot, tid) : tsRsFlagAt(L, c, slot, tid);
-      if (!waitFlag(comm, flagPtr(me, off), seq0 + t + 1, whereCode(kCounterTwoShot, c, phase)))
+  if (role == kTsPush) {
+    for (uint64_t t = 0; t < ntiles; ++t) {
+      if (t >= (uint64_t)S) {
+        if (tm.lead() && !waitLocal(comm, &sGathered, t - S + 1, &sFail,
+                                    whereCode(kCounterTwoShot, c, 3)))
+          sFail = 1;
+        tm.sync();
+        if (sFail) break;
+      }
+      const uint64_t tile = tileOf(t);
+      const int slot = slotOf(t);
+      bool ok = true;
+      for (int d = 1; d < P && ok; ++d) {
+        const int j = (r + d) % P;
+        const Span sp = chunkSpan(pl, tile, j, V);
+        char* dst = comm.peers[j] + tsRsDataAt(L, c, slot, r);
+        // 16-byte vectors staged through shared memory by TMA, then the
+        // scalar tail (or everything, for unaligned buffers).
+        const uint64_t nv = vec ? sp.count / V : 0;
+        if (nv > 0)
+          ok = stageStream<1>(
+              comm, tm, pushRing, 1, nv, [&](int) -> const void* { return x + sp.offset; },
+              [&](uint64_t i, const uint4* v) { st16(reinterpret_cast<uint4*>(dst) + i, v[0]); },
+              whereCode(kCounterTwoShot, c, 6), sTeamFlag + 0);
+        char* dtail = dst + nv * 16;
+        copyOut<T, kLdInput, 8>(tm, x + sp.offset + nv * V, sp.count - nv * V, false, false, 1.f,
+                                1, [dtail](int) { return dtail; });
+      }
+      if (!ok) {
         sFail = 1;
+        break;
+      }
+      tm.sync();
+      if (peerThread) stReleaseSys(flagPtr(comm.peers[k], tsRsFlagAt(L, c, slot, r)), seq0 + t + 1);
+      traceMark(comm, c, kCounterTwoShot, 0, t, tm.lead());
     }
-    __syncthreads();
-    return sFail == 0;
-  };
-
-  // Prologue: reduce-scatter data for the first kTwoShotSlots - 1 tiles.
-  for (uint64_t t = 0; t < ntiles && t + 1 < (uint64_t)kTwoShotSlots; ++t) pushRS(t);
-  // All-gather of tile t: wait for every peer's reduced chunk, copy it out.
-  auto finishAG = [&](uint64_t t) -> bool {
-    if (!waitAll(true, t, 2)) return false;
-    traceMark(comm, c, kCounterTwoShot, 4, t);
-    const uint64_t tile = tileOf(t);
-    const int slot = slotOf(t);
-    for (int k = 1; k < P; ++k) {
-      const int j = (r + P - k) % P;
-      const Span sp = chunkSpan(pl, tile, j, V);
-      T* dst = y + sp.offset;
-      copyOut<T, kLdMailbox, 8>(reinterpret_cast<const T*>(me + tsAgDataAt(L, c, slot, j)),
-                                sp.count, vec, false, 1.f, 1, [dst](int) { return dst; });
+  } else if (role == kTsReduce) {
+    for (uint64_t t = 0; t < ntiles; ++t) {
+      const int slot = slotOf(t);
+      if (peerThread && !waitFlag(comm, flagPtr(me, tsRsFlagAt(L, c, slot, k)), seq0 + t + 1,
+                                  whereCode(kCounterTwoShot, c, 1)))
+        sFail = 1;
+      tm.sync();
+      if (sFail) break;
+      traceMark(comm, c, kCounterTwoShot, 1, t, tm.lead());
+      const Span own = chunkSpan(pl, tileOf(t), r, V);
+      const uint64_t agOff = tsAgDataAt(L, c, slot, r);
+      // Vector part: every rank's contribution staged through shared memory
+      // by TMA (own input from x, the others from the reduce-scatter slots),
+      // summed in rank order in fp32, stored to y and pushed to every peer.
+      const uint64_t nv = vec ? own.count / V : 0;
+      if (nv > 0 &&
+          !stageStream<MAXP>(
+              comm, tm, redRing, P, nv,
+              [&](int q) -> const void* {
+                return q == r ? static_cast<const void*>(x + own.offset)
+                              : static_cast<const void*>(me + tsRsDataAt(L, c, slot, q));
+              },
+              [&](uint64_t i, const uint4* v) {
+                float acc[V], f[V];
+                Pk::unpack(v[0], acc);
+#pragma unroll
+                for (int e = 0; e < V; ++e) acc[e] = scaled(alpha, acc[e]);
+#pragma unroll
+                for (int q = 1; q < MAXP; ++q) {
+                  if (q < P) {
+                    Pk::unpack(v[q], f);
+#pragma unroll
+                    for (int e = 0; e < V; ++e) acc[e] = addRn(acc[e], scaled(alpha, f[e]));
+                  }
+                }
+                const uint4 o = Pk::pack(acc);
+                st16(reinterpret_cast<uint4*>(y + own.offset) + i, o);
+                for (int d = 1; d < P; ++d) {
+                  const int j = (r + d) % P;
+                  st16(reinterpret_cast<uint4*>(comm.peers[j] + agOff) + i, o);
+                }
+              },
+              whereCode(kCounterTwoShot, c, 7), sTeamFlag + 1)) {
+        sFail = 1;
+        break;
+      }
+      // Scalar tail (the whole chunk for unaligned buffers).
+      const uint64_t e0 = nv * V;
+      reduceRanks<T, MAXP, U>(
+          tm, own.count - e0, false, P, r, x + own.offset + e0, alpha,
+          [&](int q) { return me + tsRsDataAt(L, c, slot, q) + e0 * sizeof(T); },
+          [&](uint64_t, uint4) {},
+          [&](uint64_t e, float f) {
+            stElem(y + own.offset + e0 + e, f);
+            for (int d = 1; d < P; ++d) {
+              const int j = (r + d) % P;
+              stElem(reinterpret_cast<T*>(comm.peers[j] + agOff) + e0 + e, f);
+            }
+          });
+      tm.sync();
+      if (peerThread) stReleaseSys(flagPtr(comm.peers[k], tsAgFlagAt(L, c, slot, r)), seq0 + t + 1);
+      traceMark(comm, c, kCounterTwoShot, 2, t, tm.lead());
     }
-    traceMark(comm, c, kCounterTwoShot, 5, t);
-    return true;
-  };
-  uint64_t done = 0;
-  for (uint64_t t = 0; t < ntiles; ++t) {
-    traceMark(comm, c, kCounterTwoShot, 0, t);
-    if (!waitAll(false, t, 1)) break;
-    traceMark(comm, c, kCounterTwoShot, 1, t);
-    const uint64_t tile = tileOf(t);
-    const int slot = slotOf(t);
-    // Reduce my chunk in rank order, store it locally and push it to all.
-    const Span own = chunkSpan(pl, tile, r, V);
-    const uint64_t agOff = tsAgDataAt(L, c, slot, r);
-    reduceRanks<T, MAXP, U>(
-        own.count, vec, P, r, x + own.offset, a.scale,
-        [&](int k) { return me + tsRsDataAt(L, c, slot, k); },
-        [&](uint64_t i, uint4 v) {
-          st16(reinterpret_cast<uint4*>(y + own.offset) + i, v);
-          for (int k = 1; k < P; ++k) {
-            const int j = (r + k) % P;
-            st16(reinterpret_cast<uint4*>(comm.peers[j] + agOff) + i, v);
-          }
-        },
-        [&](uint64_t e, float f) {
-          stElem(y + own.offset + e, f);
-          for (int k = 1; k < P; ++k) {
-            const int j = (r + k) % P;
-            stElem(reinterpret_cast<T*>(comm.peers[j] + agOff) + e, f);
-          }
-        });
-    __syncthreads();
-    if (tid < P && tid != r)
-      stReleaseSys(flagPtr(comm.peers[tid], tsAgFlagAt(L, c, slot, r)), seq0 + t + 1);
-    traceMark(comm, c, kCounterTwoShot, 2, t);
-    // The all-gather of the previous tile: its peers finished long ago (they
-    // are reducing tile t now), so this wait rarely stalls.
-    if (t > 0 && !finishAG(t - 1)) break;
-    // Reduce-scatter data for tile t + S - 1 goes into slot (t - 1) % S:
-    // every peer finished reducing tile t - 1 (its all-gather arrived) and
-    // its all-gather slot was just copied out.
-    if (t + kTwoShotSlots - 1 < ntiles) pushRS(t + kTwoShotSlots - 1);
-    done = t;
+  } else {
+    for (uint64_t t = 0; t < ntiles; ++t) {
+      const int slot = slotOf(t);
+      if (peerThread && !waitFlag(comm, flagPtr(me, tsAgFlagAt(L, c, slot, k)), seq0 + t + 1,
+                                  whereCode(kCounterTwoShot, c, 2)))
+        sFail = 1;
+      tm.sync();
+      if (sFail) break;
+      traceMark(comm, c, kCounterTwoShot, 4, t, tm.lead());
+      const uint64_t tile = tileOf(t);
+      for (int d = 1; d < P; ++d) {
+        const int j = (r + P - d) % P;
+        const Span sp = chunkSpan(pl, tile, j, V);
+        T* dst = y + sp.offset;
+        copyOut<T, kLdMailbox, 8>(tm, reinterpret_cast<const T*>(me + tsAgDataAt(L, c, slot, j)),
+                                  sp.count, vec, false, 1.f, 1, [dst](int) { return dst; });
+      }
+      tm.sync();
+      if (tm.lead()) stReleaseCta(&sGathered, t + 1);
+      traceMark(comm, c, kCounterTwoShot, 5, t, tm.lead());
+    }
   }
-  if (ntiles > 0 && done + 1 == ntiles && !sFail && finishAG(ntiles - 1)) done = ntiles;
-  // Every thread has passed the final barrier of the loop (or broke out on
-  // a failure seen by all), so thread 0 can record the new sequence number.
-  if (tid == 0 && !sFail) comm.counters[kCounterTwoShot * kMaxChannels + c] = seq0 + done;
+  __syncthreads();
+  if (threadIdx.x == 0 && !sFail) comm.counters[kCounterTwoShot * kMaxChannels + c] = seq0 + ntiles;
 }
 
 // ---------------------------------------------------------------------------
@@ -354,6 +475,7 @@ __device__ __forceinline__ void oneShotBody(const DevComm& comm, const AllReduce
   constexpr int V = Pack<T>::V;
   constexpr int U = MAXP <= 2 ? 4 : MAXP <= 4 ? 2 : 1;
   const int tid = threadIdx.x, P = comm.nranks, r = comm.rank;
+  const Team cta = wholeCta();
   const MailboxLayout& L = comm.layout;
   const int S = L.osSlots;
   char* const me = comm.peers[r];
@@ -381,7 +503,7 @@ __device__ __forceinline__ void oneShotBody(const DevComm& comm, const AllReduce
     if (sFail) break;
     traceMark(comm, c, kCounterOneShot, 1, t);
     const uint64_t dataOff = osDataAt(L, c, s, r);
-    copyOut<T, kLdInput, 8>(x + sp.offset, sp.count, vec, false, 1.f, P - 1, [&](int d) {
+    copyOut<T, kLdInput, 8>(cta, x + sp.offset, sp.count, vec, false, 1.f, P - 1, [&](int d) {
       return comm.peers[(r + 1 + d) % P] + dataOff;
     });
     __syncthreads();
@@ -395,7 +517,7 @@ __device__ __forceinline__ void oneShotBody(const DevComm& comm, const AllReduce
     if (sFail) break;
     traceMark(comm, c, kCounterOneShot, 3, t);
     reduceRanks<T, MAXP, U>(
-        sp.count, vec, P, r, x + sp.offset, a.scale,
+        cta, sp.count, vec, P, r, x + sp.offset, a.scale,
         [&](int k) { return me + osDataAt(L, c, s, k); },
         [&](uint64_t i, uint4 v) { st16(reinterpret_cast<uint4*>(y + sp.offset) + i, v); },
         [&](uint64_t e, float f) { stElem(y + sp.offset + e, f); });
@@ -452,6 +574,7 @@ __device__ __forceinline__ void ringBody(const DevComm& comm, const AllReduceArg
   using Pk = Pack<T>;
   constexpr int V = Pk::V;
   const int tid = threadIdx.x, P = comm.nranks, r = comm.rank;
+  const Team cta = wholeCta();
   const T* x = static_cast<const T*>(a.send);
   T* y = static_cast<T*>(a.recv);
   const ChunkPlan& pl = a.chunk;
@@ -500,7 +623,7 @@ __device__ __forceinline__ void ringBody(const DevComm& comm, const AllReduceArg
       const Span sp = chunkSpan(pl, tile, ringChunkBehind(r, 1, P), V);
       if (!acquire(false, true, 1)) break;
       char* out = ch.outSlot(ch.sendT);
-      copyOut<T, kLdInput, 8>(x + sp.offset, sp.count, vec, scale, alpha, 1,
+      copyOut<T, kLdInput, 8>(cta, x + sp.offset, sp.count, vec, scale, alpha, 1,
                               [out](int) { return out; });
       finish(false, true);
     }
@@ -512,7 +635,7 @@ __device__ __forceinline__ void ringBody(const DevComm& comm, const AllReduceArg
       const T* in = ch.inSlot(ch.recvT);
       char* out = ch.outSlot(ch.sendT);
       ringHop<T, 2>(
-          sp.count, vec, in, x + sp.offset, alpha,
+          cta, sp.count, vec, in, x + sp.offset, alpha,
           [&](uint64_t i, uint4 v) { st16(reinterpret_cast<uint4*>(out) + i, v); },
           [&](uint64_t e, float f) { stElem(reinterpret_cast<T*>(out) + e, f); });
       finish(true, true);
@@ -526,7 +649,7 @@ __device__ __forceinline__ void ringBody(const DevComm& comm, const AllReduceArg
       char* out = ch.outSlot(ch.sendT);
       T* yo = y + sp.offset;
       ringHop<T, 2>(
-          sp.count, vec, in, x + sp.offset, alpha,
+          cta, sp.count, vec, in, x + sp.offset, alpha,
           [&](uint64_t i, uint4 v) {
             st16(reinterpret_cast<uint4*>(yo) + i, v);
             st16(reinterpret_cast<uint4*>(out) + i, v);
@@ -544,7 +667,7 @@ __device__ __forceinline__ void ringBody(const DevComm& comm, const AllReduceArg
       const T* in = ch.inSlot(ch.recvT);
       char* out = ch.outSlot(ch.sendT);
       T* yo = y + sp.offset;
-      copyOut<T, kLdMailbox, 8>(in, sp.count, vec, false, 1.f, 2, [&](int k) {
+      copyOut<T, kLdMailbox, 8>(cta, in, sp.count, vec, false, 1.f, 2, [&](int k) {
         return k == 0 ? reinterpret_cast<char*>(yo) : out;
       });
       finish(true, true);
@@ -554,7 +677,7 @@ __device__ __forceinline__ void ringBody(const DevComm& comm, const AllReduceArg
       const Span sp = chunkSpan(pl, tile, ringChunkBehind(r, P - 1, P), V);
       if (!acquire(true, false, 5)) break;
       T* yo = y + sp.offset;
-      copyOut<T, kLdMailbox, 8>(ch.inSlot(ch.recvT), sp.count, vec, false, 1.f, 1,
+      copyOut<T, kLdMailbox, 8>(cta, ch.inSlot(ch.recvT), sp.count, vec, false, 1.f, 1,
                                 [yo](int) { return reinterpret_cast<char*>(yo); });
       finish(true, false);
     }
@@ -563,30 +686,30 @@ __device__ __forceinline__ void ringBody(const DevComm& comm, const AllReduceArg
 }
 
 // ---------------------------------------------------------------------------
-// NVLS
+// NVLS with three warp-specialised teams per channel CTA:
+//
+//   copy-in   x tile t -> this rank's input block (slot t%S); publish
+//             "copied in t" to every peer
+//   switch    wait "copied in t" from every rank (own copy-in through a
+//             shared counter); multimem.ld_reduce this rank's share of the
+//             tile in the NVSwitch and multimem.st it to every rank's output
+//             block; publish "stored t"
+//   copy-out  wait "stored t" from every rank; copy the output block to y
+//
+// Flags are one monotone word per (phase, channel, source rank). Block reuse
+// (S = kNvlsSlots): copy-in overwrites input block t%S with tile t only after
+// this CTA's copy-out finished tile t-S, which waited for every rank's
+// "stored t-S", so every switch read of that block is done; a peer's
+// multimem store of tile t into output block t%S follows its wait for this
+// rank's "copied in t", published after the same copy-out.
 // ---------------------------------------------------------------------------
 template <typename T>
-// NVLS, software-pipelined over S = kNvlsSlots input/output blocks:
-//
-//   copy in tiles 0 .. S-2, publish "copied in" for each
-//   for t: wait every rank's "copied in t"; multimem reduce + broadcast my
-//          share of tile t; publish "stored t"
-//          wait every rank's "stored t-1"; copy tile t-1 out      <- deferred
-//          copy in tile t+S-1 (slot of t-1); publish "copied in t+S-1"
-//
-// Flags are one monotone word per (phase, channel, source rank): tiles are
-// copied in and stored in order, so "copied in t" is implied by any later
-// value. Block reuse: tile t+S-1 overwrites the input block of t-1 only after
-// every rank published "stored t-1" (their switch reads of t-1 are done), and
-// this rank publishes "copied in t+S-1" only after it copied tile t-1 out of
-// the shared output block, so no rank's multimem store of tile t+S-1 can
-// overwrite unread data.
 __global__ void __launch_bounds__(kMaxThreads)
     nvlsKernel(const __grid_constant__ DevComm comm, const __grid_constant__ AllReduceArgs a) {
   using Pk = Pack<T>;
   constexpr int V = Pk::V;
   constexpr int S = kNvlsSlots;
-  const int c = blockIdx.x, tid = threadIdx.x, P = comm.nranks, r = comm.rank;
+  const int c = blockIdx.x, P = comm.nranks, r = comm.rank;
   const MailboxLayout& L = comm.layout;
   char* const me = comm.peers[r];
   const T* x = static_cast<const T*>(a.send);
@@ -597,7 +720,11 @@ __global__ void __launch_bounds__(kMaxThreads)
   const bool scale = alpha != 1.0f;
   const uint64_t tb = comm.nvlsTileBytes;
   __shared__ int sFail;
-  if (tid == 0) sFail = 0;
+  __shared__ unsigned long long sIn, sStored, sOut;
+  if (threadIdx.x == 0) {
+    sFail = 0;
+    sIn = sStored = sOut = 0;
+  }
   const uint64_t seq0 = comm.counters[kCounterNvls * kMaxChannels + c];
   __syncthreads();
   const uint64_t ntiles = channelTiles(pl.numTiles, pl.channels, c);
@@ -605,89 +732,104 @@ __global__ void __launch_bounds__(kMaxThreads)
   auto spanOf = [&](uint64_t t) {
     return blockTileSpan(pl, (uint64_t)c + t * (uint64_t)pl.channels);
   };
-
-  auto publish = [&](int phase, uint64_t value) {
+  int role;
+  const Team tm = splitTeams(comm.nvlsSplit, &role);  // copy-in / switch / copy-out
+  const bool peerThread = tm.tid < P && tm.tid != r;
+  const int k = tm.tid;
+  // Publishes phase `phase` of tile t: release to every peer, then (after a
+  // system fence, so the switch sees this rank's data too) the local counter.
+  auto publish = [&](int phase, uint64_t t, unsigned long long* local) {
     fenceProxyAlias();
-    __syncthreads();
-    if (tid < P && tid != r)
-      stReleaseSys(flagPtr(comm.peers[tid], nvlsFlagAt(L, phase, c, r)), value);
+    tm.sync();
+    if (peerThread) stReleaseSys(flagPtr(comm.peers[k], nvlsFlagAt(L, phase, c, r)), seq0 + t + 1);
+    if (tm.lead()) {
+      fenceAcqRelSys();
+      stReleaseCta(local, t + 1);
+    }
   };
-  auto waitAll = [&](int phase, uint64_t value) -> bool {
-    if (tid < P && tid != r &&
-        !waitFlag(comm, flagPtr(me, nvlsFlagAt(L, phase, c, tid)), value,
-                  whereCode(kCounterNvls, c, phase + 1)))
+  // Waits for phase `phase` of tile t on every peer and on this rank.
+  auto waitAll = [&](int phase, uint64_t t, const unsigned long long* local) -> bool {
+    if (peerThread && !waitFlag(comm, flagPtr(me, nvlsFlagAt(L, phase, c, k)), seq0 + t + 1,
+                                whereCode(kCounterNvls, c, phase + 1)))
       sFail = 1;
-    __syncthreads();
+    if (tm.lead() && !waitLocal(comm, local, t + 1, &sFail, whereCode(kCounterNvls, c, phase + 4)))
+      sFail = 1;
+    tm.sync();
     fenceProxyAlias();
     return sFail == 0;
   };
-  auto copyIn = [&](uint64_t t) {
-    const Span sp = spanOf(t);
-    char* dst = comm.nvlsUc + nvlsInAt(tb, c, slotOf(t));
-    copyOut<T, kLdInput, 8>(x + sp.offset, sp.count, vec, false, 1.f, 1,
-                            [dst](int) { return dst; });
-    traceMark(comm, c, kCounterNvls, 1, t);
-    publish(0, seq0 + t + 1);
-  };
-  auto copyOutTile = [&](uint64_t t) -> bool {
-    if (!waitAll(1, seq0 + t + 1)) return false;
-    traceMark(comm, c, kCounterNvls, 4, t);
-    const Span sp = spanOf(t);
-    const T* src = reinterpret_cast<const T*>(comm.nvlsUc + nvlsOutAt(tb, c, slotOf(t)));
-    T* yo = y + sp.offset;
-    copyOut<T, kLdMailbox, 8>(src, sp.count, vec, false, 1.f, 1,
-                              [yo](int) { return reinterpret_cast<char*>(yo); });
-    traceMark(comm, c, kCounterNvls, 5, t);
-    return true;
-  };
 
-  for (uint64_t t = 0; t < ntiles && t + 1 < (uint64_t)S; ++t) copyIn(t);
-  uint64_t done = 0;
-  for (uint64_t t = 0; t < ntiles; ++t) {
-    traceMark(comm, c, kCounterNvls, 0, t);
-    if (!waitAll(0, seq0 + t + 1)) break;
-    traceMark(comm, c, kCounterNvls, 2, t);
-    // Reduce this rank's share of the tile in the switch and broadcast it
-    // (whole vectors; padding past the tile end is reduced but never copied
-    // out).
-    const Span sp = spanOf(t);
-    const int slot = slotOf(t);
-    char* const mcIn = comm.nvlsMc + nvlsInAt(tb, c, slot);
-    char* const mcOut = comm.nvlsMc + nvlsOutAt(tb, c, slot);
-    const Span share = blockShare(divUp(sp.count, V), P, r, 1);
-    const uint64_t NT = blockDim.x;
-    constexpr int UN = 4;  // switch reductions in flight per thread
-    for (uint64_t base = tid; base < share.count; base += NT * UN) {
-      uint4 v[UN];
-#pragma unroll
-      for (int u = 0; u < UN; ++u) {
-        const uint64_t i = share.offset + base + u * NT;
-        if (base + u * NT < share.count) v[u] = Multimem<T>::ldReduce(mcIn + i * 16);
+  if (role == 0) {
+    for (uint64_t t = 0; t < ntiles; ++t) {
+      if (t >= (uint64_t)S) {
+        if (tm.lead() &&
+            !waitLocal(comm, &sOut, t - S + 1, &sFail, whereCode(kCounterNvls, c, 3)))
+          sFail = 1;
+        tm.sync();
+        if (sFail) break;
       }
+      const Span sp = spanOf(t);
+      char* dst = comm.nvlsUc + nvlsInAt(tb, c, slotOf(t));
+      copyOut<T, kLdInput, 8>(tm, x + sp.offset, sp.count, vec, false, 1.f, 1,
+                              [dst](int) { return dst; });
+      publish(0, t, &sIn);
+      traceMark(comm, c, kCounterNvls, 1, t, tm.lead());
+    }
+  } else if (role == 1) {
+    for (uint64_t t = 0; t < ntiles; ++t) {
+      if (!waitAll(0, t, &sIn)) break;
+      traceMark(comm, c, kCounterNvls, 2, t, tm.lead());
+      // This rank's share of the tile, in whole vectors (padding past the
+      // tile end is reduced but never copied out).
+      const Span sp = spanOf(t);
+      const int slot = slotOf(t);
+      char* const mcIn = comm.nvlsMc + nvlsInAt(tb, c, slot);
+      char* const mcOut = comm.nvlsMc + nvlsOutAt(tb, c, slot);
+      const Span share = blockShare(divUp(sp.count, V), P, r, 1);
+      const uint64_t NT = tm.nt;
+      constexpr int UN = 8;  // switch reductions in flight per thread
+      for (uint64_t base = tm.tid; base < share.count; base += NT * UN) {
+        uint4 v[UN];
 #pragma unroll
-      for (int u = 0; u < UN; ++u) {
-        const uint64_t i = share.offset + base + u * NT;
-        if (base + u * NT < share.count) {
-          uint4 w = v[u];
-          if (scale) {
-            float f[V];
-            Pk::unpack(w, f);
+        for (int u = 0; u < UN; ++u) {
+          const uint64_t i = share.offset + base + u * NT;
+          if (base + u * NT < share.count) v[u] = Multimem<T>::ldReduce(mcIn + i * 16);
+        }
 #pragma unroll
-            for (int e = 0; e < V; ++e) f[e] = scaled(alpha, f[e]);
-            w = Pk::pack(f);
+        for (int u = 0; u < UN; ++u) {
+          const uint64_t i = share.offset + base + u * NT;
+          if (base + u * NT < share.count) {
+            uint4 w = v[u];
+            if (scale) {
+              float f[V];
+              Pk::unpack(w, f);
+#pragma unroll
+              for (int e = 0; e < V; ++e) f[e] = scaled(alpha, f[e]);
+              w = Pk::pack(f);
+            }
+            Multimem<T>::st(mcOut + i * 16, w);
           }
-          Multimem<T>::st(mcOut + i * 16, w);
         }
       }
+      publish(1, t, &sStored);
+      traceMark(comm, c, kCounterNvls, 3, t, tm.lead());
     }
-    traceMark(comm, c, kCounterNvls, 3, t);
-    publish(1, seq0 + t + 1);
-    if (t > 0 && !copyOutTile(t - 1)) break;
-    if (t + S - 1 < ntiles) copyIn(t + S - 1);
-    done = t;
+  } else {
+    for (uint64_t t = 0; t < ntiles; ++t) {
+      if (!waitAll(1, t, &sStored)) break;
+      traceMark(comm, c, kCounterNvls, 4, t, tm.lead());
+      const Span sp = spanOf(t);
+      const T* src = reinterpret_cast<const T*>(comm.nvlsUc + nvlsOutAt(tb, c, slotOf(t)));
+      T* yo = y + sp.offset;
+      copyOut<T, kLdMailbox, 8>(tm, src, sp.count, vec, false, 1.f, 1,
+                                [yo](int) { return reinterpret_cast<char*>(yo); });
+      tm.sync();
+      if (tm.lead()) stReleaseCta(&sOut, t + 1);
+      traceMark(comm, c, kCounterNvls, 5, t, tm.lead());
+    }
   }
-  if (ntiles > 0 && done + 1 == ntiles && !sFail && copyOutTile(ntiles - 1)) done = ntiles;
-  if (tid == 0 && !sFail) comm.counters[kCounterNvls * kMaxChannels + c] = seq0 + done;
+  __syncthreads();
+  if (threadIdx.x == 0 && !sFail) comm.counters[kCounterNvls * kMaxChannels + c] = seq0 + ntiles;
 }
 
 // ---------------------------------------------------------------------------
@@ -764,7 +906,12 @@ cudaError_t launchEmulatedTyped(const EmulatedLaunch& e, int channels, int threa
   const void* fn = e.nranks <= 2   ? (const void*)emulatedKernel<T, 2>
                    : e.nranks <= 4 ? (const void*)emulatedKernel<T, 4>
                                    : (const void*)emulatedKernel<T, 8>;
-  return cudaLaunchCooperativeKernel(fn, grid, block, args, 0, stream);
+  const uint32_t smem = twoShotSmemBytes(e.comm[0], 8);
+  cudaError_t err = e.nranks <= 2   ? allowSmem<emulatedKernel<T, 2>>(smem)
+                    : e.nranks <= 4 ? allowSmem<emulatedKernel<T, 4>>(smem)
+                                    : allowSmem<emulatedKernel<T, 8>>(smem);
+  if (err != cudaSuccess) return err;
+  return cudaLaunchCooperativeKernel(fn, grid, block, args, smem, stream);
 }
 
 template <typename T>
@@ -772,10 +919,26 @@ int emulatedMaxCtasTyped(int threads) {
   int perSm = 0, sms = 0, dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 0;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&perSm, emulatedKernel<T, 8>, threads, 0) !=
-      cudaSuccess)
+  DevComm d{};
+  d.tsStages = 2;
+  d.tsPushStage = 32768;
+  d.tsRedStage = 65536;
+  const uint32_t smem = twoShotSmemBytes(d, 8);
+  if (allowSmem<emulatedKernel<T, 8>>(smem) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&perSm, emulatedKernel<T, 8>, threads, smem) !=
+          cudaSuccess)
     return 0;
   return perSm * sms;
+}
+
+template <typename T, int MAXP>
+cudaError_t launchTwoShot(const DevComm& comm, const AllReduceArgs& a, dim3 block,
+                          cudaStream_t stream) {
+  const uint32_t smem = twoShotSmemBytes(comm, MAXP);
+  cudaError_t err = allowSmem<twoShotKernel<T, MAXP>>(smem);
+  if (err != cudaSuccess) return err;
+  twoShotKernel<T, MAXP><<<a.chunk.channels, block, smem, stream>>>(comm, a);
+  return cudaGetLastError();
 }
 
 template <typename T>
@@ -788,14 +951,12 @@ cudaError_t launchTyped(const DevComm& comm, const AllReduceArgs& a, int algo, i
       break;
     case TNCCL_ALGO_TWOSHOT:
       if (comm.nranks <= 2)
-        twoShotKernel<T, 2><<<a.chunk.channels, block, 0, stream>>>(comm, a);
+        return launchTwoShot<T, 2>(comm, a, block, stream);
       else if (comm.nranks <= 4)
-        twoShotKernel<T, 4><<<a.chunk.channels, block, 0, stream>>>(comm, a);
+        return launchTwoShot<T, 4>(comm, a, block, stream);
       else if (comm.nranks <= 8)
-        twoShotKernel<T, 8><<<a.chunk.channels, block, 0, stream>>>(comm, a);
-      else
-        twoShotKernel<T, 16><<<a.chunk.channels, block, 0, stream>>>(comm, a);
-      break;
+        return launchTwoShot<T, 8>(comm, a, block, stream);
+      return launchTwoShot<T, 16>(comm, a, block, stream);
     case TNCCL_ALGO_ONESHOT:
       if (comm.nranks <= 2)
         oneShotKernel<T, 2><<<a.block.channels, block, 0, stream>>>(comm, a);

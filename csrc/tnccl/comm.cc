@@ -147,6 +147,12 @@ void fillDevComm(tncclComm* comm) {
   d.trace = comm->trace;
   d.traceCount = comm->traceCount;
   d.traceEvents = (uint32_t)comm->cfg.traceEvents;
+  d.tsSplit = comm->cfg.tsSplit;
+  d.nvlsSplit = comm->cfg.nvlsSplit;
+  d.acquireMode = comm->cfg.acquireMode;
+  d.tsStages = comm->cfg.tsStages;
+  d.tsPushStage = (uint32_t)comm->cfg.tsPushStage;
+  d.tsRedStage = (uint32_t)comm->cfg.tsRedStage;
 }
 
 void deriveThresholds(tncclComm* comm) {

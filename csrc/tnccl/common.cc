@@ -2,6 +2,7 @@
 
 #include "protocol.h"
 
+#include <stdio.h>
 #include <string.h>
 #include <strings.h>
 #include <unistd.h>
@@ -69,7 +70,7 @@ static int64_t roundTo16(int64_t v) { return v < 16 ? 16 : (v + 15) / 16 * 16; }
 
 Config loadConfig() {
   Config c{};
-  c.channels = clampInt(envInt("TNCCL_NCHANNELS", 64), 1, kMaxChannels);
+  c.channels = clampInt(envInt("TNCCL_NCHANNELS", 128), 1, kMaxChannels);
   c.osChannels = clampInt(envInt("TNCCL_ONESHOT_CHANNELS", 16), 1, kMaxChannels);
   c.ringSlots = clampInt(envInt("TNCCL_SLOTS", 4), 2, 16);
   c.ringChunkBytes = roundTo16(envInt("TNCCL_CHUNK_BYTES", 256 << 10));
@@ -89,13 +90,38 @@ Config loadConfig() {
   if (c.timeoutMs < 1) c.timeoutMs = 1;
   c.bootstrapTimeoutMs = envInt("TNCCL_BOOTSTRAP_TIMEOUT_MS", 30000);
   if (c.bootstrapTimeoutMs < 1) c.bootstrapTimeoutMs = 1;
-  c.threads = clampInt(envInt("TNCCL_NTHREADS", 512), 64, 512) / 32 * 32;
+  c.threads = clampInt(envInt("TNCCL_NTHREADS", 512), 128, 512) / 32 * 32;
   c.useCuMem = (int)envInt("TNCCL_CUMEM_ENABLE", 1);
   c.oneShotMaxBytes = envInt("TNCCL_ONESHOT_MAX_BYTES", 0);
   c.nvlsMinBytes = envInt("TNCCL_NVLS_MIN_BYTES", 0);
   c.traceEvents = envInt("TNCCL_TRACE", 0) ? clampInt(envInt("TNCCL_TRACE_EVENTS", 4096), 16, 1 << 20)
                                             : 0;
+  c.tsSplit = parseSplit(envStr("TNCCL_TWOSHOT_SPLIT", ""), 2 | (4 << 4));
+  c.nvlsSplit = parseSplit(envStr("TNCCL_NVLS_SPLIT", ""), 2 | (4 << 4));
+  c.acquireMode = envInt("TNCCL_ACQUIRE_LOAD", 1) ? 1 : 0;
+  // Staging sizes: the reduce stage is split among up to 16 sources and every
+  // buffer stays 16-byte aligned; the total fits 227 KiB of shared memory.
+  c.tsStages = clampInt(envInt("TNCCL_TWOSHOT_STAGES", 2), 1, 8);
+  c.tsPushStage = (int)(clampInt(envInt("TNCCL_TWOSHOT_PUSH_STAGE", 32 << 10), 1 << 10, 64 << 10) / 16 * 16);
+  c.tsRedStage = (int)(clampInt(envInt("TNCCL_TWOSHOT_REDUCE_STAGE", 64 << 10), 4 << 10, 128 << 10) / 256 * 256);
+  while (c.tsStages > 1 && 128 + (int64_t)c.tsStages * (c.tsPushStage + c.tsRedStage) > 227 * 1024)
+    --c.tsStages;
+  if (128 + (int64_t)c.tsStages * (c.tsPushStage + c.tsRedStage) > 227 * 1024) {
+    c.tsPushStage = 32 << 10;
+    c.tsRedStage = 64 << 10;
+  }
   return c;
+}
+
+int parseSplit(const std::string& s, int dflt) {
+  int a = 0, b = 0;
+  if (s.empty()) return dflt;
+  if (sscanf(s.c_str(), "%d,%d", &a, &b) != 2 || a < 1 || b < 1 || a + b > 7) {
+    TN_WARN("malformed team split '%s' (want a,b in eighths, a + b <= 7); using default",
+            s.c_str());
+    return dflt;
+  }
+  return a | (b << 4);
 }
 
 uint64_t configHash(const Config& c) {
@@ -131,11 +157,13 @@ namespace tnccl {
 
 void adaptConfig(Config& c, int nranks) {
   if (nranks < 1) nranks = 1;
-  // Two-shot: a 256 KiB tile per channel split into one chunk per rank, so
+  // Two-shot: a 512 KiB tile per channel split into one chunk per rank, so
   // the mailbox (channels x slots x tile x 2) does not grow with nranks.
+  // Measured on 2 x B200: 256 KiB chunks reach 590-625 GB/s bus bandwidth
+  // at 256 MiB with 64-128 channels; 64 KiB chunks lose a third.
   if (c.tsChunkBytes <= 16 && envInt("TNCCL_TWOSHOT_CHUNK_BYTES", 0) == 0) {
-    int64_t chunk = (int64_t)(256 << 10) / nranks;
-    chunk = chunk < (16 << 10) ? (16 << 10) : chunk > (128 << 10) ? (128 << 10) : chunk;
+    int64_t chunk = (int64_t)(512 << 10) / nranks;
+    chunk = chunk < (32 << 10) ? (32 << 10) : chunk > (256 << 10) ? (256 << 10) : chunk;
     c.tsChunkBytes = chunk / 16 * 16;
   }
 }

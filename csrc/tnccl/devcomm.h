@@ -43,6 +43,15 @@ struct DevComm {
   uint64_t* trace;
   uint32_t* traceCount;
   uint32_t traceEvents;
+  // Warp split (eighths, a | b << 4) of the two-shot and NVLS teams.
+  int tsSplit;
+  int nvlsSplit;
+  int acquireMode;  // 1: ld.acquire.sys on the flag, 0: fence.acq_rel.sys
+  // Two-shot shared-memory staging: stages per team, push stage bytes,
+  // reduce stage bytes (all sources together).
+  int tsStages;
+  uint32_t tsPushStage;
+  uint32_t tsRedStage;
 };
 
 // Tag of one trace record: algorithm family, phase, tile index (low 16 bits).

@@ -31,6 +31,11 @@ __device__ __forceinline__ uint64_t ldRelaxedSys(const uint64_t* p) {
   asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ uint64_t ldAcquireSys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
 __device__ __forceinline__ void stReleaseSys(uint64_t* p, uint64_t v) {
   asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
@@ -49,6 +54,17 @@ __device__ __forceinline__ uint64_t globalTimerNs() {
 // Where-codes recorded on a failed wait: family, channel, phase.
 __device__ __forceinline__ int whereCode(int family, int channel, int phase) {
   return (family << 24) | (channel << 8) | phase;
+}
+
+// Acquire side of a flag that was seen at or past its target: re-read it
+// with ld.acquire.sys (it is monotone, so the value still satisfies the
+// wait and synchronises with the release that wrote it), or, with
+// acquireMode 0, a fence.acq_rel.sys after the relaxed poll.
+__device__ __forceinline__ void acquireFlag(const DevComm& comm, const uint64_t* flag) {
+  if (comm.acquireMode)
+    (void)ldAcquireSys(flag);
+  else
+    fenceAcqRelSys();
 }
 
 static __device__ __noinline__ void recordFailure(const DevComm& comm, int code, int where,
@@ -76,7 +92,7 @@ static __device__ __noinline__ bool waitSlow(const DevComm& comm, const uint64_t
   for (;;) {
     v = ldRelaxedSys(flag);
     if (v >= target) {
-      fenceAcqRelSys();
+      acquireFlag(comm, flag);
       return true;
     }
     ++polls;
@@ -98,21 +114,233 @@ static __device__ __noinline__ bool waitSlow(const DevComm& comm, const uint64_t
 __device__ __forceinline__ bool waitFlag(const DevComm& comm, const uint64_t* flag,
                                          uint64_t target, int where) {
   if (ldRelaxedSys(flag) >= target) {
-    fenceAcqRelSys();
+    acquireFlag(comm, flag);
     return true;
   }
   return waitSlow(comm, flag, target, where);
 }
 
-// Records a phase boundary of channel c (thread 0 only; no-op when tracing
-// is off).
+// Records a phase boundary of channel c (by one thread: thread 0, or the
+// caller's `lead`; no-op when tracing is off). Several teams of one CTA may
+// record concurrently, so the slot index is taken atomically.
 __device__ __forceinline__ void traceMark(const DevComm& comm, int c, int family, int phase,
-                                          uint64_t tile) {
-  if (comm.trace == nullptr || threadIdx.x != 0) return;
-  const uint32_t i = comm.traceCount[c]++;
+                                          uint64_t tile, bool lead) {
+  if (comm.trace == nullptr || !lead) return;
+  const uint32_t i = atomicAdd(comm.traceCount + c, 1u);
   uint64_t* rec = comm.trace + ((uint64_t)c * comm.traceEvents + i % comm.traceEvents) * 2;
   rec[0] = globalTimerNs();
   rec[1] = traceTag(family, phase, tile);
+}
+
+__device__ __forceinline__ void traceMark(const DevComm& comm, int c, int family, int phase,
+                                          uint64_t tile) {
+  traceMark(comm, c, family, phase, tile, threadIdx.x == 0);
+}
+
+// ---------------------------------------------------------------------------
+// Teams: warp-aligned groups of a CTA that run different roles of one
+// channel concurrently. A team synchronises on its own named barrier
+// (bar.sync id, count); id 0 with the whole CTA is __syncthreads.
+// ---------------------------------------------------------------------------
+struct Team {
+  int tid;  // thread index within the team
+  int nt;   // threads in the team (multiple of 32)
+  int bar;  // named barrier id
+  __device__ __forceinline__ void sync() const {
+    if (bar == 0)
+      __syncthreads();
+    else
+      asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(nt) : "memory");
+  }
+  __device__ __forceinline__ bool lead() const { return tid == 0; }
+};
+
+__device__ __forceinline__ Team wholeCta() {
+  return Team{(int)threadIdx.x, (int)blockDim.x, 0};
+}
+
+// Progress counters between teams of one CTA live in shared memory: the
+// producer team passes its barrier, then its leader publishes with a
+// CTA-scope release; the consumer's leader polls with a CTA-scope acquire
+// and then passes its own team barrier.
+__device__ __forceinline__ void stReleaseCta(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.cta.shared.u64 [%0], %1;" ::"r"((uint32_t)__cvta_generic_to_shared(p)),
+               "l"(v)
+               : "memory");
+}
+__device__ __forceinline__ unsigned long long ldAcquireCta(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.cta.shared.u64 %0, [%1];"
+               : "=l"(v)
+               : "r"((uint32_t)__cvta_generic_to_shared(p))
+               : "memory");
+  return v;
+}
+
+// Bounded wait on a shared-memory progress counter written by another team.
+// Ends early (false) when `fail` (shared) is raised by any team, when an
+// error or abort is recorded in the status block, or on the time/iteration
+// bound (records TNCCL_TIMEOUT).
+static __device__ __noinline__ bool waitLocal(const DevComm& comm, const unsigned long long* ctr,
+                                              uint64_t target, const volatile int* fail,
+                                              int where) {
+  if (ldAcquireCta(ctr) >= target) return true;
+  const uint64_t start = globalTimerNs();
+  const uint64_t maxPolls = comm.timeoutNs / 16 + 4096;
+  uint64_t polls = 0;
+  for (;;) {
+    const unsigned long long v = ldAcquireCta(ctr);
+    if (v >= target) return true;
+    if (*fail) return false;
+    ++polls;
+    if ((polls & 255) == 0) {
+      if (comm.status->abort) {
+        recordFailure(comm, 6, where, target, v);
+        return false;
+      }
+      if (comm.status->error) return false;
+      if (globalTimerNs() - start > comm.timeoutNs || polls > maxPolls) {
+        recordFailure(comm, 5, where, target, v);
+        return false;
+      }
+    }
+    if (polls > 64) __nanosleep(32);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// TMA bulk copies into shared memory (cp.async.bulk, completion counted in
+// bytes on an mbarrier). Only this GPU's own memory is ever a source.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smemAddr(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbarInit(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smemAddr(bar)), "r"(count)
+               : "memory");
+}
+// Makes mbarrier initialisation visible to the async (TMA) proxy.
+__device__ __forceinline__ void fenceMbarInit() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbarArriveExpectTx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smemAddr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulkLoad(void* smemDst, const void* gsrc, uint32_t bytes,
+                                         uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smemAddr(smemDst)),
+      "l"(gsrc), "r"(bytes), "r"(smemAddr(bar))
+      : "memory");
+}
+// Non-blocking probe of phase `parity` (test_wait: the thread is never
+// suspended, so a completed phase is seen at once).
+__device__ __forceinline__ bool mbarTryWait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smemAddr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for phase `parity` of an mbarrier (a TMA copy of local memory
+// that never lands means a broken context; the wait still gives up).
+static __device__ __noinline__ bool mbarWaitSlow(const DevComm& comm, uint64_t* bar,
+                                                 uint32_t parity, int where) {
+  const uint64_t start = globalTimerNs();
+  for (uint64_t polls = 1;; ++polls) {
+    if (mbarTryWait(bar, parity)) return true;
+    if ((polls & 63) == 0 && (globalTimerNs() - start > comm.timeoutNs || polls > (1ull << 32))) {
+      recordFailure(comm, 5, where, parity, 0);
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ bool mbarWait(const DevComm& comm, uint64_t* bar, uint32_t parity,
+                                         int where) {
+  return mbarTryWait(bar, parity) || mbarWaitSlow(comm, bar, parity, where);
+}
+__device__ __forceinline__ uint4 ldShared16(const void* p) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(smemAddr(p)));
+  return v;
+}
+
+// A ring of `nb` shared-memory stages, each holding `nsrc` buffers of
+// `stageBytes`, filled by one leader thread with TMA bulk copies and drained
+// by its team. `used` counts stages consumed so far (identical in every
+// thread of the team), which gives each stage's buffer and mbarrier parity.
+struct StageRing {
+  char* buf;
+  uint64_t* full;  // nb mbarriers (arrival count 1)
+  uint32_t stageBytes;
+  int nb;
+  uint64_t used;
+  int pieces = 1;  // bulk copies per stage and source
+};
+
+// Streams nvec 16-byte vectors of `nsrc` local sources (src(k) -> base
+// address, 16-byte aligned) through the ring and calls f(i, v) with v[k] =
+// vector i of source k. Stages are issued nb ahead. Per stage the leader
+// waits (bounded) for the mbarrier and shares the outcome through
+// `teamFlag` (shared, one per team), so the whole team leaves together if a
+// stage never lands (recorded as TNCCL_TIMEOUT); after its stage the team
+// passes its barrier before the leader refills the buffer.
+template <int MAXSRC, typename SrcF, typename F>
+__device__ __forceinline__ bool stageStream(const DevComm& comm, const Team& tm, StageRing& R,
+                                            int nsrc, uint64_t nvec, SrcF src, F f, int where,
+                                            volatile int* teamFlag) {
+  const uint64_t vb = R.stageBytes / 16;
+  const uint64_t nst = (nvec + vb - 1) / vb;
+  auto issue = [&](uint64_t j) {
+    const uint64_t g = R.used + j;
+    const int b = (int)(g % (uint64_t)R.nb);
+    const uint64_t v0 = j * vb;
+    const uint32_t bytes = (uint32_t)((nvec - v0 < vb ? nvec - v0 : vb) * 16);
+    mbarArriveExpectTx(R.full + b, bytes * (uint32_t)nsrc);
+    const uint32_t piece = (bytes / (uint32_t)R.pieces + 15) / 16 * 16;
+    for (int k = 0; k < nsrc; ++k)
+      for (uint32_t o = 0; o < bytes; o += piece)
+        bulkLoad(R.buf + ((size_t)b * MAXSRC + k) * R.stageBytes + o,
+                 reinterpret_cast<const char*>(src(k)) + v0 * 16 + o,
+                 bytes - o < piece ? bytes - o : piece, R.full + b);
+  };
+  if (tm.lead())
+    for (uint64_t j = 0; j < nst && j < (uint64_t)R.nb; ++j) issue(j);
+  bool ok = true;
+  for (uint64_t j = 0; j < nst; ++j) {
+    const uint64_t g = R.used + j;
+    const int b = (int)(g % (uint64_t)R.nb);
+    const uint32_t parity = (uint32_t)((g / (uint64_t)R.nb) & 1);
+    if (tm.lead()) *teamFlag = mbarWait(comm, R.full + b, parity, where) ? 0 : 1;
+    tm.sync();
+    if (*teamFlag) {
+      ok = false;
+      break;
+    }
+    (void)mbarTryWait(R.full + b, parity);  // completed: acquire in this thread
+    const uint64_t v0 = j * vb;
+    const uint32_t nv = (uint32_t)(nvec - v0 < vb ? nvec - v0 : vb);
+    const char* base = R.buf + (size_t)b * MAXSRC * R.stageBytes;
+    for (uint32_t i = tm.tid; i < nv; i += tm.nt) {
+      uint4 v[MAXSRC];
+#pragma unroll
+      for (int k = 0; k < MAXSRC; ++k)
+        if (k < nsrc) v[k] = ldShared16(base + (size_t)k * R.stageBytes + (size_t)i * 16);
+      f(v0 + i, v);
+    }
+    tm.sync();
+    if (tm.lead() && j + R.nb < nst) issue(j + R.nb);
+  }
+  R.used += nst;
+  return ok;
 }
 
 __device__ __forceinline__ uint64_t* flagPtr(char* base, uint64_t off) {

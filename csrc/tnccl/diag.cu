@@ -8,6 +8,9 @@
 //              st.release.sys flag to the peer (the cost of publishing)
 //   3 local  : copy within this rank's mailbox
 //   4 local->peer copy, 5 two local loads -> one local + one peer store
+//   6 push while warp 0 keeps issuing one ordering operation (chunk picks it)
+//   7 / 8 TMA-staged copy local->peer / local->local (unroll = stages,
+//         chunk = stage bytes); 9 = 7 with every stage split into 8 copies
 // The caller runs the same mode on every rank at the same time; no kernel
 // waits on another rank, so there is nothing to time out.
 #include <cuda_runtime.h>
@@ -32,7 +35,35 @@ __global__ void diagKernel(char* local, char* peer, uint64_t bytes, int mode, ui
   const uint64_t nvec = per / 16;
   const uint64_t NT = blockDim.x;
   uint32_t acc = 0;
-  if (mode == 2) {
+  if (mode == 6) {
+    // Warps 1.. push like mode 0 while warp 0 (lane 0) keeps issuing one
+    // ordering operation every ~500 ns: chunk 0 none, 1 fence.acq_rel.sys,
+    // 2 ld.acquire.sys of a local word, 3 st.release.sys to the peer.
+    __shared__ volatile int sDone;
+    if (threadIdx.x == 0) sDone = 0;
+    __syncthreads();
+    const uint64_t NT2 = NT - 32;
+    if (threadIdx.x >= 32) {
+      for (uint64_t b = threadIdx.x - 32; b < nvec; b += NT2 * U) {
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const uint64_t i = b + u * NT2;
+          if (i < nvec) st16(peer + base + i * 16, make_uint4((uint32_t)i, 1, 2, 3));
+        }
+      }
+      asm volatile("bar.sync 1, %0;" ::"r"((int)NT2) : "memory");
+      if (threadIdx.x == 32) sDone = 1;
+    } else if (threadIdx.x == 0) {
+      uint64_t n = 0;
+      while (!sDone && n < (1u << 24)) {
+        if (chunk == 1) fenceAcqRelSys();
+        if (chunk == 2) acc += (uint32_t)ldAcquireSys(reinterpret_cast<uint64_t*>(local));
+        if (chunk == 3) stReleaseSys(peerFlag + blockIdx.x, ++n);
+        ++n;
+        __nanosleep(500);
+      }
+    }
+  } else if (mode == 2) {
     const uint64_t cvec = chunk / 16;
     uint64_t seq = 0;
     for (uint64_t c0 = 0; c0 < nvec; c0 += cvec) {
@@ -105,6 +136,31 @@ __global__ void diagKernel(char* local, char* peer, uint64_t bytes, int mode, ui
   if (acc == 0x12345678u) *sink = acc;
 }
 
+// Modes 7 / 8: the TMA-staged stream of the collectives (stageStream) with
+// one team of the whole CTA: local -> peer (7) or local -> local (8), with
+// `nb` stages of `stageBytes` in flight.
+__global__ void diagStageKernel(const __grid_constant__ DevComm comm, char* local, char* peer,
+                                uint64_t bytes, int mode, uint32_t stageBytes, int nb,
+                                int pieces) {
+  extern __shared__ __align__(128) char dsmem[];
+  __shared__ int sFlag;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(dsmem);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < nb; ++i) mbarInit(bars + i, 1);
+    fenceMbarInit();
+  }
+  __syncthreads();
+  StageRing ring{dsmem + 128, bars, stageBytes, nb, 0, pieces};
+  const Team tm = wholeCta();
+  const uint64_t per = bytes / gridDim.x / 16 * 16;
+  const char* src = local + per * blockIdx.x;
+  char* dst = (mode == 8 ? local + bytes : peer) + per * blockIdx.x;
+  (void)stageStream<1>(
+      comm, tm, ring, 1, per / 16, [&](int) -> const void* { return src; },
+      [&](uint64_t i, const uint4* v) { st16(reinterpret_cast<uint4*>(dst) + i, v[0]); },
+      whereCode(15, blockIdx.x, 10), &sFlag);
+}
+
 }  // namespace
 }  // namespace tnccl
 
@@ -121,7 +177,7 @@ extern "C" tncclResult tncclDiagBench(tncclComm_t comm, int mode, size_t bytes, 
   const size_t area = (size_t)comm->layout.channels *
                                                      comm->layout.ringSlots *
                                                      comm->layout.ringChunkBytes;
-  const size_t span = bytes * (mode == 5 ? 3 : mode == 3 ? 2 : 1);
+  const size_t span = bytes * (mode == 5 ? 3 : (mode == 3 || mode == 8) ? 2 : 1);
   if (bytes == 0 || span > area) return TNCCL_INVALID_ARGUMENT;
   char* local = comm->local.base + comm->layout.ringDataOff;
   char* peer = comm->dev.peers[next] + comm->layout.ringDataOff;
@@ -134,7 +190,23 @@ extern "C" tncclResult tncclDiagBench(tncclComm_t comm, int mode, size_t bytes, 
   cudaEvent_t e0, e1;
   cudaEventCreate(&e0);
   cudaEventCreate(&e1);
+  // Modes 7 / 8: `unroll` is the number of stages, `chunk` the stage bytes.
+  const uint32_t smem = 128 + (uint32_t)unroll * (uint32_t)chunk;
+  const bool staged = mode == 7 || mode == 8 || mode == 9;
+  if (staged) {
+    if (unroll < 1 || unroll > 8 || chunk < 16 || chunk % 16 || smem > 220 * 1024)
+      return TNCCL_INVALID_ARGUMENT;
+    if (cudaFuncSetAttribute(diagStageKernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
+      return TNCCL_CUDA_ERROR;
+  }
   auto launch = [&]() {
+    if (staged) {
+      diagStageKernel<<<ctas, threads, smem, stream>>>(comm->dev, local, peer, bytes, mode,
+                                                       (uint32_t)chunk, unroll,
+                                                       mode == 9 ? 8 : 1);
+      return;
+    }
     switch (unroll) {
       case 1: diagKernel<1><<<ctas, threads, 0, stream>>>(local, peer, bytes, mode, chunk, flag, sink); break;
       case 2: diagKernel<2><<<ctas, threads, 0, stream>>>(local, peer, bytes, mode, chunk, flag, sink); break;
@@ -144,10 +216,12 @@ extern "C" tncclResult tncclDiagBench(tncclComm_t comm, int mode, size_t bytes, 
     }
   };
   launch();
+  cudaError_t err = cudaGetLastError();
   cudaEventRecord(e0, stream);
   for (int i = 0; i < iters; ++i) launch();
   cudaEventRecord(e1, stream);
-  cudaError_t err = cudaEventSynchronize(e1);
+  if (err == cudaSuccess) err = cudaGetLastError();
+  if (err == cudaSuccess) err = cudaEventSynchronize(e1);
   float ms = 0.f;
   if (err == cudaSuccess) err = cudaEventElapsedTime(&ms, e0, e1);
   cudaEventDestroy(e0);

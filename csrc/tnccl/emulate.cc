@@ -129,6 +129,12 @@ extern "C" tncclResult tncclEmuCreate(tncclEmu_t* out, int nranks) {
     dc.counters = e->counters + (size_t)k * kNumCounterFamilies * kMaxChannels;
     dc.status = e->devStatus;
     dc.timeoutNs = (uint64_t)e->cfg.timeoutMs * 1000000ull;
+    dc.tsSplit = e->cfg.tsSplit;
+    dc.nvlsSplit = e->cfg.nvlsSplit;
+    dc.acquireMode = e->cfg.acquireMode;
+    dc.tsStages = e->cfg.tsStages;
+    dc.tsPushStage = (uint32_t)e->cfg.tsPushStage;
+    dc.tsRedStage = (uint32_t)e->cfg.tsRedStage;
   }
   *out = e;
   return TNCCL_SUCCESS;

@@ -97,7 +97,7 @@ struct World {
   float* data(int r, uint64_t off) { return reinterpret_cast<float*>(base(r) + off); }
 
   void publish(int self, int r, uint64_t off, uint64_t v) {
-    int n = published[(size_t)self]++;
+    int n = __atomic_fetch_add(&published[(size_t)self], 1, __ATOMIC_RELAXED);
     if (self == dropRank && n == dropAt) return;  // injected loss
     __atomic_store_n(flag(r, off), v, __ATOMIC_RELEASE);
   }
@@ -132,9 +132,9 @@ struct Job {
 float rnd(int t, float f) { return oracle::roundTo(t, f); }
 
 bool twoShot(World& w, int r, const Job& j, uint64_t count) {
-  // Same pipeline as twoShotBody: reduce-scatter data is pushed
-  // kTwoShotSlots - 1 tiles ahead, and the all-gather of tile t is finished
-  // after tile t + 1 has been reduced.
+  // Same structure as twoShotBody: per channel, a push, a reduce and a
+  // gather role run concurrently (here: three threads), coupled only by the
+  // peers' flags and by the local "gathered" counter that gates slot reuse.
   const Config& c = w.cfg;
   const int P = c.P;
   const MailboxLayout& L = w.L;
@@ -147,52 +147,79 @@ bool twoShot(World& w, int r, const Job& j, uint64_t count) {
     const uint64_t ntiles = channelTiles(pl.numTiles, pl.channels, ch);
     auto tileOf = [&](uint64_t t) { return (uint64_t)ch + t * (uint64_t)pl.channels; };
     auto slotOf = [&](uint64_t t) { return (int)((seq0 + t) % kTwoShotSlots); };
-    auto pushRS = [&](uint64_t t) {
-      for (int k = 1; k < P; ++k) {
-        const int dst = (r + k) % P;
-        Span sp = chunkSpan(pl, tileOf(t), dst, c.vec);
-        float* out = w.data(dst, tsRsDataAt(L, ch, slotOf(t), r));
-        for (uint64_t e = 0; e < sp.count; ++e) out[e] = x[sp.offset + e];
-      }
-      for (int p = 0; p < P; ++p)
-        if (p != r) w.publish(r, p, tsRsFlagAt(L, ch, slotOf(t), r), seq0 + t + 1);
-    };
-    for (uint64_t t = 0; t < ntiles && t + 1 < (uint64_t)kTwoShotSlots; ++t) pushRS(t);
-    auto finishAG = [&](uint64_t t) -> bool {
-      const int slot = slotOf(t);
-      for (int p = 0; p < P; ++p)
-        if (p != r && !w.wait(r, tsAgFlagAt(L, ch, slot, p), seq0 + t + 1)) return false;
-      for (int k = 1; k < P; ++k) {
-        const int src = (r + P - k) % P;
-        Span sp = chunkSpan(pl, tileOf(t), src, c.vec);
-        const float* in = w.data(r, tsAgDataAt(L, ch, slot, src));
-        for (uint64_t e = 0; e < sp.count; ++e) y[sp.offset + e] = in[e];
-      }
-      return true;
-    };
-    for (uint64_t t = 0; t < ntiles; ++t) {
-      const int slot = slotOf(t);
-      const uint64_t want = seq0 + t + 1;
-      for (int p = 0; p < P; ++p)
-        if (p != r && !w.wait(r, tsRsFlagAt(L, ch, slot, p), want)) return false;
-      Span own = chunkSpan(pl, tileOf(t), r, c.vec);
-      for (uint64_t e = 0; e < own.count; ++e) {
-        float acc = 0;
-        for (int k = 0; k < P; ++k) {
-          float v = k == r ? x[own.offset + e] : w.data(r, tsRsDataAt(L, ch, slot, k))[e];
-          acc = k == 0 ? oracle::mul(j.alpha, v) : oracle::add(acc, oracle::mul(j.alpha, v));
+    std::atomic<uint64_t> gathered{0};
+    std::atomic<int> fail{0};
+    auto push = [&] {
+      for (uint64_t t = 0; t < ntiles && !fail.load(); ++t) {
+        if (t >= (uint64_t)kTwoShotSlots) {
+          auto start = std::chrono::steady_clock::now();
+          while (gathered.load(std::memory_order_acquire) < t - kTwoShotSlots + 1) {
+            if (fail.load() || w.error.load() ||
+                std::chrono::steady_clock::now() - start >
+                    std::chrono::milliseconds(c.timeoutMs)) {
+              fail.store(1);
+              return;
+            }
+            std::this_thread::yield();
+          }
         }
-        acc = rnd(j.dtype, acc);
-        y[own.offset + e] = acc;
+        for (int k = 1; k < P; ++k) {
+          const int dst = (r + k) % P;
+          Span sp = chunkSpan(pl, tileOf(t), dst, c.vec);
+          float* out = w.data(dst, tsRsDataAt(L, ch, slotOf(t), r));
+          for (uint64_t e = 0; e < sp.count; ++e) out[e] = x[sp.offset + e];
+        }
         for (int p = 0; p < P; ++p)
-          if (p != r) w.data(p, tsAgDataAt(L, ch, slot, r))[e] = acc;
+          if (p != r) w.publish(r, p, tsRsFlagAt(L, ch, slotOf(t), r), seq0 + t + 1);
       }
-      for (int p = 0; p < P; ++p)
-        if (p != r) w.publish(r, p, tsAgFlagAt(L, ch, slot, r), want);
-      if (t > 0 && !finishAG(t - 1)) return false;
-      if (t + kTwoShotSlots - 1 < ntiles) pushRS(t + kTwoShotSlots - 1);
-    }
-    if (ntiles > 0 && !finishAG(ntiles - 1)) return false;
+    };
+    auto reduce = [&] {
+      for (uint64_t t = 0; t < ntiles; ++t) {
+        const int slot = slotOf(t);
+        const uint64_t want = seq0 + t + 1;
+        for (int p = 0; p < P; ++p)
+          if (p != r && !w.wait(r, tsRsFlagAt(L, ch, slot, p), want)) {
+            fail.store(1);
+            return;
+          }
+        Span own = chunkSpan(pl, tileOf(t), r, c.vec);
+        for (uint64_t e = 0; e < own.count; ++e) {
+          float acc = 0;
+          for (int k = 0; k < P; ++k) {
+            float v = k == r ? x[own.offset + e] : w.data(r, tsRsDataAt(L, ch, slot, k))[e];
+            acc = k == 0 ? oracle::mul(j.alpha, v) : oracle::add(acc, oracle::mul(j.alpha, v));
+          }
+          acc = rnd(j.dtype, acc);
+          y[own.offset + e] = acc;
+          for (int p = 0; p < P; ++p)
+            if (p != r) w.data(p, tsAgDataAt(L, ch, slot, r))[e] = acc;
+        }
+        for (int p = 0; p < P; ++p)
+          if (p != r) w.publish(r, p, tsAgFlagAt(L, ch, slot, r), want);
+      }
+    };
+    auto gather = [&] {
+      for (uint64_t t = 0; t < ntiles; ++t) {
+        const int slot = slotOf(t);
+        for (int p = 0; p < P; ++p)
+          if (p != r && !w.wait(r, tsAgFlagAt(L, ch, slot, p), seq0 + t + 1)) {
+            fail.store(1);
+            return;
+          }
+        for (int k = 1; k < P; ++k) {
+          const int src = (r + P - k) % P;
+          Span sp = chunkSpan(pl, tileOf(t), src, c.vec);
+          const float* in = w.data(r, tsAgDataAt(L, ch, slot, src));
+          for (uint64_t e = 0; e < sp.count; ++e) y[sp.offset + e] = in[e];
+        }
+        gathered.store(t + 1, std::memory_order_release);
+      }
+    };
+    std::thread tp(push), tr(reduce);
+    gather();
+    tp.join();
+    tr.join();
+    if (fail.load()) return false;
     seq = seq0 + ntiles;
   }
   return true;
