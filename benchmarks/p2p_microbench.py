@@ -40,12 +40,14 @@ def main():
              5: "reduce mix (2 local loads -> local + peer store)",
              6: "push with a concurrent ordering op in warp 0",
              7: "TMA-staged local->peer", 8: "TMA-staged local->local",
-             9: "TMA-staged local->peer, 8 copies per stage"}
+             9: "TMA-staged local->peer, 8 copies per stage",
+             10: "NVLS ld_reduce (share)", 11: "NVLS multimem.st", 12: "NVLS ld_reduce+st (share)"}
     only = [int(m) for m in os.environ.get("P2P_MODES", "0,1,3,2,4,5").split(",")]
     for mode in only:
         for ctas in (1, 8, 32, 64, 128):
             for threads in ((128, 256) if mode in (7, 8, 9) else (256, 512)):
-                for unroll in ((2, 4, 8) if mode not in (2, 7, 8, 9) else
+                for unroll in ((4, 8, 16) if mode >= 10 else
+                               (2, 4, 8) if mode not in (2, 7, 8, 9) else
                                (1,) if mode == 2 else (2, 3)):
                     chunks = ((16 << 10, 64 << 10, 256 << 10) if mode == 2 else
                               (0, 1, 2, 3) if mode == 6 else

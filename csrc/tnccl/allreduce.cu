@@ -43,16 +43,27 @@ constexpr int kLdInput = 0;
 constexpr int kLdMailbox = 1;
 constexpr int kMaxThreads = 512;
 
-// Shared-memory staging of the two-shot push and reduce teams
-// (DevComm::tsStages stages per team; a push stage is tsPushStage bytes, a
-// reduce stage holds MAXP sources of tsRedStage / MAXP bytes each). The
-// first 128 bytes hold the mbarriers (at most kMaxStages per team).
+// Shared-memory staging (TMA bulk copies into a ring of stages per team).
+// Two-shot: DevComm::tsStages stages for the push and the reduce team; a
+// stage of tsPushStage / tsRedStage bytes is split evenly among the team's
+// sources (MAXP - 1 peers' chunks for push, MAXP contributions for reduce).
+// NVLS: nvlsStages stages of nvlsStage bytes for the copy-in team. The
+// gather / copy-out teams load through registers: a CTA's TMA unit is shared
+// by its teams, and on 2 x B200 moving the gather onto it as well cost 15-25%
+// at 4-64 MiB. The first kBarBytes bytes hold the mbarriers, kMaxStages per
+// team.
 constexpr int kMaxStages = 8;
-__host__ __device__ constexpr uint32_t redSourceBytes(uint32_t redStage, int maxp) {
-  return redStage / (uint32_t)maxp / 16 * 16;
+constexpr uint32_t kBarBytes = 256;
+__host__ __device__ constexpr uint32_t perSource(uint32_t stage, int nsrc) {
+  return stage / (uint32_t)nsrc / 16 * 16;
 }
-uint32_t twoShotSmemBytes(const DevComm& d, int maxp) {
-  return 128 + (uint32_t)d.tsStages * (d.tsPushStage + redSourceBytes(d.tsRedStage, maxp) * maxp);
+__host__ __device__ uint32_t twoShotSmemBytes(const DevComm& d, int maxp) {
+  const int np = maxp > 1 ? maxp - 1 : 1;
+  return kBarBytes + (uint32_t)d.tsStages * (perSource(d.tsPushStage, np) * np +
+                                             perSource(d.tsRedStage, maxp) * maxp);
+}
+__host__ __device__ uint32_t nvlsSmemBytes(const DevComm& d) {
+  return kBarBytes + (uint32_t)d.nvlsStages * perSource(d.nvlsStage, 1);
 }
 
 // Opts `Kernel` into `bytes` of dynamic shared memory, once per device.
@@ -273,6 +284,52 @@ __device__ __forceinline__ void ringHop(const Team& tm, uint64_t n, bool vec, co
 // ---------------------------------------------------------------------------
 enum TwoShotRole { kTsPush = 0, kTsReduce = 1, kTsGather = 2 };
 
+// True when the launch provided at least `need` bytes of dynamic shared
+// memory. Otherwise thread 0 records TNCCL_CUDA_ERROR (where-code phase 15)
+// and every thread of the CTA must return before touching the rings.
+__device__ __forceinline__ bool haveSmem(const DevComm& comm, uint32_t need, int family, int c) {
+  uint32_t dyn;
+  asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn));
+  if (need <= dyn) return true;
+  if (threadIdx.x == 0) recordFailure(comm, 4, whereCode(family, c, 15), need, dyn);
+  return false;
+}
+
+// Copies n (<= MAXSRC) local sources to their destinations: source k holds
+// count(k) elements at src(k) (local memory), destination k is dst(k) (local
+// or a peer's mailbox). The vectors that every source has are streamed
+// through the team's TMA stage ring, all sources in one pass; what is left
+// of each source (other chunk lengths, scalar tails, unaligned buffers) goes
+// through registers. Returns false if a stage never landed.
+template <typename T, int MAXSRC, int LD, typename SrcF, typename CountF, typename DstF>
+__device__ __forceinline__ bool stagedCopy(const DevComm& comm, const Team& tm, StageRing& R,
+                                           int n, bool vec, SrcF src, CountF count, DstF dst,
+                                           int where, volatile int* teamFlag) {
+  constexpr int V = Pack<T>::V;
+  uint64_t nv = ~0ull;
+  for (int k = 0; k < n; ++k) {
+    const uint64_t c = count(k) / V;
+    nv = c < nv ? c : nv;
+  }
+  if (!vec || n == 0) nv = 0;
+  if (nv > 0 && !stageStream<MAXSRC>(
+                    comm, tm, R, n, nv, [&](int k) -> const void* { return src(k); },
+                    [&](uint64_t i, const uint4* v) {
+#pragma unroll
+                      for (int k = 0; k < MAXSRC; ++k)
+                        if (k < n) st16(reinterpret_cast<uint4*>(dst(k)) + i, v[k]);
+                    },
+                    where, teamFlag))
+    return false;
+  for (int k = 0; k < n; ++k) {
+    const uint64_t e0 = nv * V;
+    char* d = dst(k) + e0 * sizeof(T);
+    copyOut<T, LD, 8>(tm, src(k) + e0, count(k) - e0, vec, false, 1.f, 1,
+                      [d](int) { return d; });
+  }
+  return true;
+}
+
 // Warp split of a CTA into three teams: split = a | b << 4 gives the first
 // two teams a/8 and b/8 of the warps (at least one each), the third the rest
 // (at least one; the launch has >= 4 warps).
@@ -309,17 +366,22 @@ __device__ __forceinline__ void twoShotBody(const DevComm& comm, const AllReduce
   const bool vec = a.vectorized != 0;
   using Pk = Pack<T>;
   const float alpha = a.scale;
+  if (!haveSmem(comm, twoShotSmemBytes(comm, MAXP), kCounterTwoShot, c)) return;
   __shared__ int sFail;
   __shared__ int sTeamFlag[3];
   __shared__ unsigned long long sGathered;  // tiles the gather team copied out
-  // Dynamic shared memory: the mbarriers of both staged teams, then the
-  // push stages, then the reduce stages.
+  // Dynamic shared memory: the mbarriers of the two staged teams, then the
+  // push and the reduce stage rings.
+  constexpr int NP = MAXP > 1 ? MAXP - 1 : 1;  // peers' chunks per tile
   extern __shared__ __align__(128) char dsmem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(dsmem);
   const int nst = comm.tsStages;
-  StageRing pushRing{dsmem + 128, bars, comm.tsPushStage, nst, 0};
-  StageRing redRing{dsmem + 128 + (size_t)nst * comm.tsPushStage, bars + kMaxStages,
-                    redSourceBytes(comm.tsRedStage, MAXP), nst, 0};
+  const uint32_t pushSrc = perSource(comm.tsPushStage, NP);
+  const uint32_t redSrc = perSource(comm.tsRedStage, MAXP);
+  char* ring0 = dsmem + kBarBytes;
+  char* ring1 = ring0 + (size_t)nst * NP * pushSrc;
+  StageRing pushRing{ring0, bars, pushSrc, nst, 0};
+  StageRing redRing{ring1, bars + kMaxStages, redSrc, nst, 0};
   if (threadIdx.x == 0) {
     sFail = 0;
     sGathered = 0;
@@ -351,23 +413,15 @@ __device__ __forceinline__ void twoShotBody(const DevComm& comm, const AllReduce
       }
       const uint64_t tile = tileOf(t);
       const int slot = slotOf(t);
-      bool ok = true;
-      for (int d = 1; d < P && ok; ++d) {
-        const int j = (r + d) % P;
-        const Span sp = chunkSpan(pl, tile, j, V);
-        char* dst = comm.peers[j] + tsRsDataAt(L, c, slot, r);
-        // 16-byte vectors staged through shared memory by TMA, then the
-        // scalar tail (or everything, for unaligned buffers).
-        const uint64_t nv = vec ? sp.count / V : 0;
-        if (nv > 0)
-          ok = stageStream<1>(
-              comm, tm, pushRing, 1, nv, [&](int) -> const void* { return x + sp.offset; },
-              [&](uint64_t i, const uint4* v) { st16(reinterpret_cast<uint4*>(dst) + i, v[0]); },
-              whereCode(kCounterTwoShot, c, 6), sTeamFlag + 0);
-        char* dtail = dst + nv * 16;
-        copyOut<T, kLdInput, 8>(tm, x + sp.offset + nv * V, sp.count - nv * V, false, false, 1.f,
-                                1, [dtail](int) { return dtail; });
-      }
+      // Chunk j of my input -> rank j's slot, every peer in one staged pass
+      // (source k is peer (r + 1 + k) % P).
+      auto peerOf = [&](int q) { return (r + 1 + q) % P; };
+      const bool ok = stagedCopy<T, NP, kLdInput>(
+          comm, tm, pushRing, P - 1, vec,
+          [&](int q) { return x + chunkSpan(pl, tile, peerOf(q), V).offset; },
+          [&](int q) { return chunkSpan(pl, tile, peerOf(q), V).count; },
+          [&](int q) { return comm.peers[peerOf(q)] + tsRsDataAt(L, c, slot, r); },
+          whereCode(kCounterTwoShot, c, 6), sTeamFlag + 0);
       if (!ok) {
         sFail = 1;
         break;
@@ -449,6 +503,7 @@ __device__ __forceinline__ void twoShotBody(const DevComm& comm, const AllReduce
       if (sFail) break;
       traceMark(comm, c, kCounterTwoShot, 4, t, tm.lead());
       const uint64_t tile = tileOf(t);
+      // Every peer's reduced chunk: all-gather slot -> y (register path).
       for (int d = 1; d < P; ++d) {
         const int j = (r + P - d) % P;
         const Span sp = chunkSpan(pl, tile, j, V);
@@ -688,20 +743,23 @@ __device__ __forceinline__ void ringBody(const DevComm& comm, const AllReduceArg
 // ---------------------------------------------------------------------------
 // NVLS with three warp-specialised teams per channel CTA:
 //
-//   copy-in   x tile t -> this rank's input block (slot t%S); publish
-//             "copied in t" to every peer
-//   switch    wait "copied in t" from every rank (own copy-in through a
-//             shared counter); multimem.ld_reduce this rank's share of the
-//             tile in the NVSwitch and multimem.st it to every rank's output
-//             block; publish "stored t"
-//   copy-out  wait "stored t" from every rank; copy the output block to y
+//   copy-in   x tile t -> this rank's input block (slot t%S, TMA-staged);
+//             count "copied in" on every rank
+//   switch    wait until all P ranks copied tile t in; multimem.ld_reduce
+//             this rank's share of the tile in the NVSwitch and multimem.st
+//             it to every rank's output block; count "stored"
+//   copy-out  wait until all P ranks stored their share; copy the output
+//             block to y
 //
-// Flags are one monotone word per (phase, channel, source rank). Block reuse
-// (S = kNvlsSlots): copy-in overwrites input block t%S with tile t only after
-// this CTA's copy-out finished tile t-S, which waited for every rank's
-// "stored t-S", so every switch read of that block is done; a peer's
-// multimem store of tile t into output block t%S follows its wait for this
-// rank's "copied in t", published after the same copy-out.
+// The barriers are 64-bit counters per phase ("copied in", "stored"),
+// channel and slot in the multicast region: a team leader adds 1 to every
+// rank's copy with one multimem.red.release, and a wait polls the local copy
+// until it reaches P x (uses of the slot so far). Block reuse (S = kNvlsSlots): copy-in overwrites input
+// block t%S with tile t only after this CTA's copy-out finished tile t-S,
+// which waited until every rank stored t-S, so every switch read of that
+// block is done; a peer's multimem store of tile t into output block t%S
+// follows its wait for this rank's "copied in t", counted after the same
+// copy-out.
 // ---------------------------------------------------------------------------
 template <typename T>
 __global__ void __launch_bounds__(kMaxThreads)
@@ -710,8 +768,6 @@ __global__ void __launch_bounds__(kMaxThreads)
   constexpr int V = Pk::V;
   constexpr int S = kNvlsSlots;
   const int c = blockIdx.x, P = comm.nranks, r = comm.rank;
-  const MailboxLayout& L = comm.layout;
-  char* const me = comm.peers[r];
   const T* x = static_cast<const T*>(a.send);
   T* y = static_cast<T*>(a.recv);
   const BlockPlan& pl = a.block;
@@ -719,11 +775,21 @@ __global__ void __launch_bounds__(kMaxThreads)
   const float alpha = a.scale;
   const bool scale = alpha != 1.0f;
   const uint64_t tb = comm.nvlsTileBytes;
+  if (!haveSmem(comm, nvlsSmemBytes(comm), kCounterNvls, c)) return;
   __shared__ int sFail;
-  __shared__ unsigned long long sIn, sStored, sOut;
+  __shared__ int sTeamFlag[3];
+  __shared__ unsigned long long sOut;  // tiles this CTA copied out
+  // Dynamic shared memory: mbarriers, then the copy-in ring.
+  extern __shared__ __align__(128) char dsmem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(dsmem);
+  const int nst = comm.nvlsStages;
+  const uint32_t stB = perSource(comm.nvlsStage, 1);
+  StageRing inRing{dsmem + kBarBytes, bars, stB, nst, 0};
   if (threadIdx.x == 0) {
     sFail = 0;
-    sIn = sStored = sOut = 0;
+    sOut = 0;
+    for (int i = 0; i < nst; ++i) mbarInit(bars + i, 1);
+    fenceMbarInit();
   }
   const uint64_t seq0 = comm.counters[kCounterNvls * kMaxChannels + c];
   __syncthreads();
@@ -734,25 +800,22 @@ __global__ void __launch_bounds__(kMaxThreads)
   };
   int role;
   const Team tm = splitTeams(comm.nvlsSplit, &role);  // copy-in / switch / copy-out
-  const bool peerThread = tm.tid < P && tm.tid != r;
-  const int k = tm.tid;
-  // Publishes phase `phase` of tile t: release to every peer, then (after a
-  // system fence, so the switch sees this rank's data too) the local counter.
-  auto publish = [&](int phase, uint64_t t, unsigned long long* local) {
+  auto counter = [&](char* base, int phase, uint64_t t) {
+    return reinterpret_cast<uint64_t*>(
+        base + nvlsCounterAt(tb, comm.nvlsChannels, phase, c, slotOf(t)));
+  };
+  // Counts phase `phase` of tile t on every rank.
+  auto publish = [&](int phase, uint64_t t) {
     fenceProxyAlias();
     tm.sync();
-    if (peerThread) stReleaseSys(flagPtr(comm.peers[k], nvlsFlagAt(L, phase, c, r)), seq0 + t + 1);
-    if (tm.lead()) {
-      fenceAcqRelSys();
-      stReleaseCta(local, t + 1);
-    }
+    if (tm.lead()) multimemAddRelease(counter(comm.nvlsMc, phase, t), 1);
   };
-  // Waits for phase `phase` of tile t on every peer and on this rank.
-  auto waitAll = [&](int phase, uint64_t t, const unsigned long long* local) -> bool {
-    if (peerThread && !waitFlag(comm, flagPtr(me, nvlsFlagAt(L, phase, c, k)), seq0 + t + 1,
-                                whereCode(kCounterNvls, c, phase + 1)))
-      sFail = 1;
-    if (tm.lead() && !waitLocal(comm, local, t + 1, &sFail, whereCode(kCounterNvls, c, phase + 4)))
+  // Waits until every rank counted phase `phase` of tile t: its slot's
+  // counter reaches P x (uses of the slot up to tile t).
+  auto waitAll = [&](int phase, uint64_t t) -> bool {
+    const uint64_t uses = (seq0 + t) / S + 1;
+    if (tm.lead() && !waitFlag(comm, counter(comm.nvlsUc, phase, t), (uint64_t)P * uses,
+                               whereCode(kCounterNvls, c, phase + 1)))
       sFail = 1;
     tm.sync();
     fenceProxyAlias();
@@ -770,14 +833,19 @@ __global__ void __launch_bounds__(kMaxThreads)
       }
       const Span sp = spanOf(t);
       char* dst = comm.nvlsUc + nvlsInAt(tb, c, slotOf(t));
-      copyOut<T, kLdInput, 8>(tm, x + sp.offset, sp.count, vec, false, 1.f, 1,
-                              [dst](int) { return dst; });
-      publish(0, t, &sIn);
+      if (!stagedCopy<T, 1, kLdInput>(
+              comm, tm, inRing, 1, vec, [&](int) { return x + sp.offset; },
+              [&](int) { return sp.count; }, [&](int) { return dst; },
+              whereCode(kCounterNvls, c, 7), sTeamFlag + 0)) {
+        sFail = 1;
+        break;
+      }
+      publish(0, t);
       traceMark(comm, c, kCounterNvls, 1, t, tm.lead());
     }
   } else if (role == 1) {
     for (uint64_t t = 0; t < ntiles; ++t) {
-      if (!waitAll(0, t, &sIn)) break;
+      if (!waitAll(0, t)) break;
       traceMark(comm, c, kCounterNvls, 2, t, tm.lead());
       // This rank's share of the tile, in whole vectors (padding past the
       // tile end is reduced but never copied out).
@@ -811,12 +879,12 @@ __global__ void __launch_bounds__(kMaxThreads)
           }
         }
       }
-      publish(1, t, &sStored);
+      publish(1, t);
       traceMark(comm, c, kCounterNvls, 3, t, tm.lead());
     }
   } else {
     for (uint64_t t = 0; t < ntiles; ++t) {
-      if (!waitAll(1, t, &sStored)) break;
+      if (!waitAll(1, t)) break;
       traceMark(comm, c, kCounterNvls, 4, t, tm.lead());
       const Span sp = spanOf(t);
       const T* src = reinterpret_cast<const T*>(comm.nvlsUc + nvlsOutAt(tb, c, slotOf(t)));
@@ -906,7 +974,8 @@ cudaError_t launchEmulatedTyped(const EmulatedLaunch& e, int channels, int threa
   const void* fn = e.nranks <= 2   ? (const void*)emulatedKernel<T, 2>
                    : e.nranks <= 4 ? (const void*)emulatedKernel<T, 4>
                                    : (const void*)emulatedKernel<T, 8>;
-  const uint32_t smem = twoShotSmemBytes(e.comm[0], 8);
+  // Dynamic shared memory of the two-shot body for this kernel's MAXP.
+  const uint32_t smem = twoShotSmemBytes(e.comm[0], e.nranks <= 2 ? 2 : e.nranks <= 4 ? 4 : 8);
   cudaError_t err = e.nranks <= 2   ? allowSmem<emulatedKernel<T, 2>>(smem)
                     : e.nranks <= 4 ? allowSmem<emulatedKernel<T, 4>>(smem)
                                     : allowSmem<emulatedKernel<T, 8>>(smem);
@@ -923,7 +992,7 @@ int emulatedMaxCtasTyped(int threads) {
   d.tsStages = 2;
   d.tsPushStage = 32768;
   d.tsRedStage = 65536;
-  const uint32_t smem = twoShotSmemBytes(d, 8);
+  const uint32_t smem = twoShotSmemBytes(d, 2);  // the largest layout
   if (allowSmem<emulatedKernel<T, 8>>(smem) != cudaSuccess ||
       cudaOccupancyMaxActiveBlocksPerMultiprocessor(&perSm, emulatedKernel<T, 8>, threads, smem) !=
           cudaSuccess)
@@ -967,9 +1036,13 @@ cudaError_t launchTyped(const DevComm& comm, const AllReduceArgs& a, int algo, i
       else
         oneShotKernel<T, 16><<<a.block.channels, block, 0, stream>>>(comm, a);
       break;
-    case TNCCL_ALGO_NVLS:
-      nvlsKernel<T><<<a.block.channels, block, 0, stream>>>(comm, a);
+    case TNCCL_ALGO_NVLS: {
+      const uint32_t smem = nvlsSmemBytes(comm);
+      cudaError_t err = allowSmem<nvlsKernel<T>>(smem);
+      if (err != cudaSuccess) return err;
+      nvlsKernel<T><<<a.block.channels, block, smem, stream>>>(comm, a);
       break;
+    }
     default:
       return cudaErrorInvalidValue;
   }

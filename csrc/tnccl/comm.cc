@@ -153,14 +153,19 @@ void fillDevComm(tncclComm* comm) {
   d.tsStages = comm->cfg.tsStages;
   d.tsPushStage = (uint32_t)comm->cfg.tsPushStage;
   d.tsRedStage = (uint32_t)comm->cfg.tsRedStage;
+  d.nvlsStages = comm->cfg.nvlsStages;
+  d.nvlsStage = (uint32_t)comm->cfg.nvlsStage;
 }
 
 void deriveThresholds(tncclComm* comm) {
   const int P = comm->nranks;
-  // Defaults from the measured sweep on 8x B200 (benchmarks/allreduce_sweep.py);
+  // Defaults from the measured sweeps on 2 and 4 B200 (benchmarks/
+  // allreduce_sweep.py): one-shot wins up to 512 KiB, the warp-specialised
+  // two-shot above (it also beats the NVLS kernel at every size measured, so
+  // AUTO picks NVLS only when TNCCL_NVLS_MIN_BYTES asks for it).
   // TNCCL_ONESHOT_MAX_BYTES / TNCCL_NVLS_MIN_BYTES override them.
-  uint64_t os = P <= 2 ? (512u << 10) : P <= 4 ? (256u << 10) : (128u << 10);
-  uint64_t nv = P <= 2 ? (64ull << 20) : (4ull << 20);
+  uint64_t os = P <= 4 ? (512u << 10) : (256u << 10);
+  uint64_t nv = ~0ull;
   if (comm->cfg.oneShotMaxBytes > 0) os = (uint64_t)comm->cfg.oneShotMaxBytes;
   if (comm->cfg.nvlsMinBytes > 0) nv = (uint64_t)comm->cfg.nvlsMinBytes;
   comm->oneShotMaxBytes = os;
@@ -224,7 +229,6 @@ extern "C" tncclResult tncclCommInitRank(tncclComm_t* out, int nranks, tncclUniq
   lc.tsChunkBytes = (uint64_t)comm->cfg.tsChunkBytes;
   lc.osSlots = comm->cfg.osSlots;
   lc.osTileBytes = (uint64_t)comm->cfg.osTileBytes;
-  lc.nvlsChannels = comm->cfg.nvlsChannels;
   comm->layout = makeLayout(lc);
 
   PeerMeta me{};

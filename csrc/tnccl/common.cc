@@ -78,7 +78,7 @@ Config loadConfig() {
   c.osSlots = clampInt(envInt("TNCCL_ONESHOT_SLOTS", 2), 1, 8);
   c.osTileBytes = roundTo16(envInt("TNCCL_ONESHOT_TILE_BYTES", 32 << 10));
   c.nvlsChannels = clampInt(envInt("TNCCL_NVLS_CHANNELS", 64), 1, kMaxChannels);
-  c.nvlsTileBytes = roundTo16(envInt("TNCCL_NVLS_TILE_BYTES", 128 << 10));
+  c.nvlsTileBytes = roundTo16(envInt("TNCCL_NVLS_TILE_BYTES", 512 << 10));
   c.nvlsEnable = (int)envInt("TNCCL_NVLS_ENABLE", 1);
   int algo = parseAlgo(envStr("TNCCL_ALGO", "auto"));
   if (algo < 0) {
@@ -97,19 +97,21 @@ Config loadConfig() {
   c.traceEvents = envInt("TNCCL_TRACE", 0) ? clampInt(envInt("TNCCL_TRACE_EVENTS", 4096), 16, 1 << 20)
                                             : 0;
   c.tsSplit = parseSplit(envStr("TNCCL_TWOSHOT_SPLIT", ""), 2 | (4 << 4));
-  c.nvlsSplit = parseSplit(envStr("TNCCL_NVLS_SPLIT", ""), 2 | (4 << 4));
+  c.nvlsSplit = parseSplit(envStr("TNCCL_NVLS_SPLIT", ""), 1 | (4 << 4));
   c.acquireMode = envInt("TNCCL_ACQUIRE_LOAD", 1) ? 1 : 0;
-  // Staging sizes: the reduce stage is split among up to 16 sources and every
-  // buffer stays 16-byte aligned; the total fits 227 KiB of shared memory.
+  // Staging sizes: a stage is split among up to 16 sources and every buffer
+  // stays 16-byte aligned; 256 bytes of mbarriers plus all rings fit the
+  // 227 KiB of shared memory a CTA can have (fewer stages otherwise).
+  const int64_t kSmem = 227 * 1024 - 256;
   c.tsStages = clampInt(envInt("TNCCL_TWOSHOT_STAGES", 2), 1, 8);
-  c.tsPushStage = (int)(clampInt(envInt("TNCCL_TWOSHOT_PUSH_STAGE", 32 << 10), 1 << 10, 64 << 10) / 16 * 16);
-  c.tsRedStage = (int)(clampInt(envInt("TNCCL_TWOSHOT_REDUCE_STAGE", 64 << 10), 4 << 10, 128 << 10) / 256 * 256);
-  while (c.tsStages > 1 && 128 + (int64_t)c.tsStages * (c.tsPushStage + c.tsRedStage) > 227 * 1024)
-    --c.tsStages;
-  if (128 + (int64_t)c.tsStages * (c.tsPushStage + c.tsRedStage) > 227 * 1024) {
-    c.tsPushStage = 32 << 10;
-    c.tsRedStage = 64 << 10;
-  }
+  c.tsPushStage = clampInt(envInt("TNCCL_TWOSHOT_PUSH_STAGE", 32 << 10), 4 << 10, 96 << 10) / 256 * 256;
+  c.tsRedStage = clampInt(envInt("TNCCL_TWOSHOT_REDUCE_STAGE", 64 << 10), 4 << 10, 128 << 10) / 256 * 256;
+  auto tsBytes = [&c]() { return (int64_t)c.tsStages * (c.tsPushStage + c.tsRedStage); };
+  while (c.tsStages > 1 && tsBytes() > kSmem) --c.tsStages;
+  if (tsBytes() > kSmem) c.tsPushStage = c.tsRedStage = 32 << 10;
+  c.nvlsStages = clampInt(envInt("TNCCL_NVLS_STAGES", 2), 1, 8);
+  c.nvlsStage = clampInt(envInt("TNCCL_NVLS_STAGE", 48 << 10), 4 << 10, 96 << 10) / 256 * 256;
+  while (c.nvlsStages > 1 && (int64_t)c.nvlsStages * c.nvlsStage > kSmem) --c.nvlsStages;
   return c;
 }
 

@@ -53,11 +53,13 @@ struct Config {
   // for the first two teams (packed a | b << 4; the third team gets the
   // rest). Local to a rank: it does not change the protocol.
   int tsSplit;               // TNCCL_TWOSHOT_SPLIT "push,reduce" (default 2,4)
-  int nvlsSplit;             // TNCCL_NVLS_SPLIT "copy-in,switch" (default 2,4)
+  int nvlsSplit;             // TNCCL_NVLS_SPLIT "copy-in,switch" (default 1,4)
   int acquireMode;           // TNCCL_ACQUIRE_LOAD (1: ld.acquire.sys, 0: fence)
   int tsStages;              // TNCCL_TWOSHOT_STAGES (1..8, default 2)
   int tsPushStage;           // TNCCL_TWOSHOT_PUSH_STAGE bytes (default 32 KiB)
   int tsRedStage;            // TNCCL_TWOSHOT_REDUCE_STAGE bytes (default 64 KiB)
+  int nvlsStages;            // TNCCL_NVLS_STAGES (1..8, default 2)
+  int nvlsStage;             // TNCCL_NVLS_STAGE bytes (default 48 KiB)
 };
 
 // Parses "a,b" (eighths, each 1..6, a + b <= 7) into a | b << 4.

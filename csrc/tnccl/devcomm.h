@@ -52,6 +52,9 @@ struct DevComm {
   int tsStages;
   uint32_t tsPushStage;
   uint32_t tsRedStage;
+  // NVLS copy-in / copy-out staging: stages per team, bytes per stage.
+  int nvlsStages;
+  uint32_t nvlsStage;
 };
 
 // Tag of one trace record: algorithm family, phase, tile index (low 16 bits).

@@ -451,6 +451,13 @@ __device__ __forceinline__ float addRn(float a, float b) { return __fadd_rn(a, b
 // ---------------------------------------------------------------------------
 // NVLS multimem (NVSwitch reduce / multicast)
 // ---------------------------------------------------------------------------
+// Adds v to a 64-bit counter on every GPU of the multicast object, with
+// release semantics (orders this thread's earlier accesses, and those it
+// observed through bar.sync, before the add on every copy).
+__device__ __forceinline__ void multimemAddRelease(uint64_t* mc, uint64_t v) {
+  asm volatile("multimem.red.release.sys.global.add.u64 [%0], %1;" ::"l"(mc), "l"(v) : "memory");
+}
+
 template <typename T>
 struct Multimem;
 

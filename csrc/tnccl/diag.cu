@@ -11,6 +11,8 @@
 //   6 push while warp 0 keeps issuing one ordering operation (chunk picks it)
 //   7 / 8 TMA-staged copy local->peer / local->local (unroll = stages,
 //         chunk = stage bytes); 9 = 7 with every stage split into 8 copies
+//   10 / 11 / 12 NVLS: multimem.ld_reduce of this rank's share / multimem.st
+//         of the whole block / both (bytes <= the NVLS region)
 // The caller runs the same mode on every rank at the same time; no kernel
 // waits on another rank, so there is nothing to time out.
 #include <cuda_runtime.h>
@@ -161,6 +163,44 @@ __global__ void diagStageKernel(const __grid_constant__ DevComm comm, char* loca
       whereCode(15, blockIdx.x, 10), &sFlag);
 }
 
+// Modes 10-12: NVLS throughput over the multicast region: 10 streams
+// multimem.ld_reduce (fp32 add), 11 streams multimem.st, 12 does both (the
+// switch step of the NVLS all-reduce) on this rank's 1/P share. U operations
+// in flight per thread.
+template <int U>
+__global__ void diagNvlsKernel(char* mc, uint64_t bytes, int mode, int nranks, int rank,
+                               unsigned* sink) {
+  uint64_t per = bytes / gridDim.x / 16 * 16;
+  uint64_t base = per * blockIdx.x;
+  if (mode != 11) {  // this rank's share of the CTA's block
+    const uint64_t share = per / (uint64_t)nranks / 16 * 16;
+    base += share * (uint64_t)rank;
+    per = share;
+  }
+  const uint64_t nvec = per / 16, NT = blockDim.x;
+  uint32_t acc = 0;
+  for (uint64_t b = threadIdx.x; b < nvec; b += NT * U) {
+    uint4 v[U];
+    if (mode != 11) {
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (b + u * NT < nvec) v[u] = Multimem<float>::ldReduce(mc + base + (b + u * NT) * 16);
+    } else {
+#pragma unroll
+      for (int u = 0; u < U; ++u) v[u] = make_uint4((uint32_t)(b + u), 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (b + u * NT >= nvec) continue;
+      if (mode == 10)
+        acc += v[u].x ^ v[u].w;
+      else
+        Multimem<float>::st(mc + base + (b + u * NT) * 16, v[u]);
+    }
+  }
+  if (acc == 0x12345678u) *sink = acc;
+}
+
 }  // namespace
 }  // namespace tnccl
 
@@ -193,6 +233,9 @@ extern "C" tncclResult tncclDiagBench(tncclComm_t comm, int mode, size_t bytes, 
   // Modes 7 / 8: `unroll` is the number of stages, `chunk` the stage bytes.
   const uint32_t smem = 128 + (uint32_t)unroll * (uint32_t)chunk;
   const bool staged = mode == 7 || mode == 8 || mode == 9;
+  const bool nvls = mode >= 10 && mode <= 12;
+  if (nvls && (!comm->nvls.enabled || bytes > comm->nvls.bytes)) return TNCCL_INVALID_ARGUMENT;
+  char* mc = reinterpret_cast<char*>(comm->nvls.mcVa);
   if (staged) {
     if (unroll < 1 || unroll > 8 || chunk < 16 || chunk % 16 || smem > 220 * 1024)
       return TNCCL_INVALID_ARGUMENT;
@@ -201,6 +244,15 @@ extern "C" tncclResult tncclDiagBench(tncclComm_t comm, int mode, size_t bytes, 
       return TNCCL_CUDA_ERROR;
   }
   auto launch = [&]() {
+    if (nvls) {
+      switch (unroll) {
+        case 2: diagNvlsKernel<2><<<ctas, threads, 0, stream>>>(mc, bytes, mode, comm->nranks, comm->rank, sink); break;
+        case 8: diagNvlsKernel<8><<<ctas, threads, 0, stream>>>(mc, bytes, mode, comm->nranks, comm->rank, sink); break;
+        case 16: diagNvlsKernel<16><<<ctas, threads, 0, stream>>>(mc, bytes, mode, comm->nranks, comm->rank, sink); break;
+        default: diagNvlsKernel<4><<<ctas, threads, 0, stream>>>(mc, bytes, mode, comm->nranks, comm->rank, sink); break;
+      }
+      return;
+    }
     if (staged) {
       diagStageKernel<<<ctas, threads, smem, stream>>>(comm->dev, local, peer, bytes, mode,
                                                        (uint32_t)chunk, unroll,

@@ -83,7 +83,6 @@ extern "C" tncclResult tncclEmuCreate(tncclEmu_t* out, int nranks) {
   lc.tsChunkBytes = (uint64_t)e->cfg.tsChunkBytes;
   lc.osSlots = e->cfg.osSlots;
   lc.osTileBytes = (uint64_t)e->cfg.osTileBytes;
-  lc.nvlsChannels = 1;
   e->layout = makeLayout(lc);
   tncclResult r = TNCCL_SUCCESS;
   e->mailbox.assign((size_t)nranks, nullptr);
@@ -135,6 +134,8 @@ extern "C" tncclResult tncclEmuCreate(tncclEmu_t* out, int nranks) {
     dc.tsStages = e->cfg.tsStages;
     dc.tsPushStage = (uint32_t)e->cfg.tsPushStage;
     dc.tsRedStage = (uint32_t)e->cfg.tsRedStage;
+    dc.nvlsStages = e->cfg.nvlsStages;
+    dc.nvlsStage = (uint32_t)e->cfg.nvlsStage;
   }
   *out = e;
   return TNCCL_SUCCESS;

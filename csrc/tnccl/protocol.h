@@ -201,10 +201,6 @@ struct MailboxLayout {
   uint64_t osTileBytes;
   uint64_t osDataOff, osFlagOff, osAckOff;
 
-  // NVLS barrier words (unicast): two phases x channels x P sources.
-  int nvlsChannels;
-  uint64_t nvlsFlagOff;
-
   uint64_t totalBytes;
 };
 
@@ -217,7 +213,6 @@ struct LayoutConfig {
   uint64_t tsChunkBytes;
   int osSlots;
   uint64_t osTileBytes;
-  int nvlsChannels;
 };
 
 TN_HD uint64_t alignUp(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
@@ -234,7 +229,6 @@ inline MailboxLayout makeLayout(const LayoutConfig& c) {
   L.tsChunkBytes = c.tsChunkBytes;
   L.osSlots = c.osSlots;
   L.osTileBytes = c.osTileBytes;
-  L.nvlsChannels = c.nvlsChannels;
 
   uint64_t off = 0;
   L.ringDataOff = off;
@@ -261,8 +255,6 @@ inline MailboxLayout makeLayout(const LayoutConfig& c) {
   off = alignUp(off + (uint64_t)c.osChannels * (uint64_t)c.osSlots * P * 8, 128);
   L.osAckOff = off;
   off = alignUp(off + (uint64_t)c.osChannels * (uint64_t)c.osSlots * P * 8, 128);
-  L.nvlsFlagOff = off;
-  off = alignUp(off + 2ull * (uint64_t)c.nvlsChannels * P * 8, 128);
   L.totalBytes = alignUp(off, 4096);
   return L;
 }
@@ -303,21 +295,28 @@ TN_HD uint64_t osAckAt(const MailboxLayout& L, int c, int s, int consumer) {
   return L.osAckOff +
          (((uint64_t)c * L.osSlots + s) * L.nranks + consumer) * 8;
 }
-TN_HD uint64_t nvlsFlagAt(const MailboxLayout& L, int phase, int c, int src) {
-  return L.nvlsFlagOff +
-         (((uint64_t)phase * L.nvlsChannels + c) * L.nranks + src) * 8;
-}
-
 // NVLS multicast region: per channel kNvlsSlots pairs of an input block and
-// an output block.
+// an output block, then the barrier counters: one 64-bit word per phase
+// ("copied in", "stored"), channel and slot that every rank increments with
+// a multicast add (multimem.red) once per use of the slot, so each rank's
+// copy counts all ranks. A rank cannot count use k + 1 of a slot before
+// every rank counted use k (the slot is reused only after all ranks stored
+// it), so a count of P * k means every rank finished use k.
 TN_HD uint64_t nvlsInAt(uint64_t tileBytes, int c, int slot) {
   return ((uint64_t)c * kNvlsSlots + (uint64_t)slot) * 2 * tileBytes;
 }
 TN_HD uint64_t nvlsOutAt(uint64_t tileBytes, int c, int slot) {
   return nvlsInAt(tileBytes, c, slot) + tileBytes;
 }
-TN_HD uint64_t nvlsRegionBytes(uint64_t tileBytes, int channels) {
+TN_HD uint64_t nvlsDataBytes(uint64_t tileBytes, int channels) {
   return (uint64_t)channels * kNvlsSlots * 2 * tileBytes;
+}
+TN_HD uint64_t nvlsCounterAt(uint64_t tileBytes, int channels, int phase, int c, int slot) {
+  return nvlsDataBytes(tileBytes, channels) +
+         (((uint64_t)phase * kMaxChannels + c) * kNvlsSlots + slot) * 8;
+}
+TN_HD uint64_t nvlsRegionBytes(uint64_t tileBytes, int channels) {
+  return nvlsDataBytes(tileBytes, channels) + alignUp(2ull * kMaxChannels * kNvlsSlots * 8, 4096);
 }
 
 }  // namespace tnccl

@@ -312,8 +312,11 @@ tncclResult setupNvls(tncclComm* comm) {
   if (st == TNCCL_SUCCESS &&
       !mapHandle(api, n.mc, n.bytes, gran, comm->device, &n.mcVa, &n.mcReserved, &n.mcMapped))
     st = TNCCL_UNSUPPORTED;
+  // Zero the region (its barrier counters start at 0) and wait for it: no
+  // rank may add to a counter before every rank finished zeroing its copy.
   if (st == TNCCL_SUCCESS &&
-      cudaMemset(reinterpret_cast<void*>(n.ucVa), 0, n.bytes) != cudaSuccess)
+      (cudaMemset(reinterpret_cast<void*>(n.ucVa), 0, n.bytes) != cudaSuccess ||
+       cudaDeviceSynchronize() != cudaSuccess))
     st = TNCCL_UNSUPPORTED;
   if ((r = agree(st)) != TNCCL_SUCCESS) {
     // Nobody has used the object yet; unmap and unbind in step on all ranks.

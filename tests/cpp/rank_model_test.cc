@@ -82,7 +82,6 @@ struct World {
     lc.tsChunkBytes = c.tsChunkElems * 4;
     lc.osSlots = c.osSlots;
     lc.osTileBytes = c.osTileElems * 4;
-    lc.nvlsChannels = 1;
     L = makeLayout(lc);
     mem.assign((size_t)c.P, std::vector<uint64_t>(L.totalBytes / 8, 0));
     counters.assign((size_t)c.P, std::vector<uint64_t>(kNumCounterFamilies * kMaxChannels, 0));
