@@ -246,14 +246,44 @@ def main():
 
     e2e = None
     if not args.no_e2e:
-        idx_dev = torch.empty((B, T + 1), dtype=torch.int64, device=dev)
+        # Every step copies its token batch host -> device (pinned, on a copy
+        # stream, double-buffered) and reads its loss device -> host (into
+        # pinned memory); the host reads step i's loss after launching step
+        # i + 1, so the device never waits for the host.
+        bufs = [torch.empty((B, T + 1), dtype=torch.int64, device=dev) for _ in range(2)]
+        ready = [torch.cuda.Event() for _ in range(2)]
+        done = [torch.cuda.Event() for _ in range(2)]
+        loss_host = torch.empty(args.steps, dtype=torch.float32).pin_memory()
+        loss_ev = [torch.cuda.Event() for _ in range(args.steps)]
+        copy_stream = torch.cuda.Stream(dev)
+        losses = []
+
+        def fetch(i):
+            j = i % 2
+            if i >= 2:
+                copy_stream.wait_event(done[j])  # step i - 2 finished reading bufs[j]
+            with torch.cuda.stream(copy_stream):
+                bufs[j].copy_(host[i % pool], non_blocking=True)
+                ready[j].record(copy_stream)
+
         torch.cuda.synchronize()
         dist.barrier()
         t0 = time.perf_counter()
+        fetch(0)
         for i in range(args.steps):
-            idx_dev.copy_(host[i % pool], non_blocking=True)
-            l = step(idx_dev[:, :T], idx_dev[:, 1:])
-            float(l.item())  # device -> host read of the step's loss
+            if i + 1 < args.steps:
+                fetch(i + 1)
+            j = i % 2
+            stream.wait_event(ready[j])
+            l = step(bufs[j][:, :T], bufs[j][:, 1:])
+            done[j].record(stream)
+            loss_host[i].copy_(l.float(), non_blocking=True)  # device -> host
+            loss_ev[i].record(stream)
+            if i >= 1:
+                loss_ev[i - 1].synchronize()
+                losses.append(float(loss_host[i - 1]))
+        loss_ev[args.steps - 1].synchronize()
+        losses.append(float(loss_host[args.steps - 1]))
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0
         wall_max = max_over_ranks(wall, dev)

@@ -92,6 +92,12 @@ extern "C" tncclResult tncclCommGetInfo(tncclComm_t comm, tncclCommInfo* info) {
   return TNCCL_SUCCESS;
 }
 
+extern "C" tncclResult tncclCommSetMaxChannels(tncclComm_t comm, int maxChannels) {
+  if (comm == nullptr || maxChannels < 0) return TNCCL_INVALID_ARGUMENT;
+  comm->maxChannels = maxChannels;
+  return TNCCL_SUCCESS;
+}
+
 extern "C" tncclResult tncclCommGetAsyncError(tncclComm_t comm, tncclResult* asyncError) {
   if (comm == nullptr || asyncError == nullptr) return TNCCL_INVALID_ARGUMENT;
   const int e = comm->hostStatus ? comm->hostStatus->error : 0;

@@ -159,12 +159,12 @@ void fillDevComm(tncclComm* comm) {
 
 void deriveThresholds(tncclComm* comm) {
   const int P = comm->nranks;
-  // Defaults from the measured sweeps on 2 and 4 B200 (benchmarks/
+  // Defaults from the measured sweeps on 2, 4 and 8 B200 (benchmarks/
   // allreduce_sweep.py): one-shot wins up to 512 KiB, the warp-specialised
   // two-shot above (it also beats the NVLS kernel at every size measured, so
   // AUTO picks NVLS only when TNCCL_NVLS_MIN_BYTES asks for it).
   // TNCCL_ONESHOT_MAX_BYTES / TNCCL_NVLS_MIN_BYTES override them.
-  uint64_t os = P <= 4 ? (512u << 10) : (256u << 10);
+  uint64_t os = 512u << 10;
   uint64_t nv = ~0ull;
   if (comm->cfg.oneShotMaxBytes > 0) os = (uint64_t)comm->cfg.oneShotMaxBytes;
   if (comm->cfg.nvlsMinBytes > 0) nv = (uint64_t)comm->cfg.nvlsMinBytes;

@@ -98,6 +98,7 @@ struct tncclComm {
   bool aborted = false;
   uint64_t oneShotMaxBytes = 0;
   uint64_t nvlsMinBytes = 0;
+  int maxChannels = 0;  // tncclCommSetMaxChannels cap (0: none)
 };
 
 namespace tnccl {

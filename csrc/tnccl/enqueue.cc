@@ -127,21 +127,24 @@ extern "C" tncclResult tncclAllReduceEx(const void* send, void* recv, size_t cou
   a.vectorized = vectorized;
   const uint64_t V = kVectorBytes / es;
   const Config& cfg = comm->cfg;
+  auto cap = [comm](int channels) {
+    return comm->maxChannels > 0 && comm->maxChannels < channels ? comm->maxChannels : channels;
+  };
   switch (chosen) {
     case TNCCL_ALGO_RING:
-      a.chunk = makeChunkPlan(count, comm->nranks, cfg.channels,
+      a.chunk = makeChunkPlan(count, comm->nranks, cap(cfg.channels),
                               (uint64_t)cfg.ringChunkBytes / es, kRingMinChunkBytes / es, V);
       break;
     case TNCCL_ALGO_TWOSHOT:
-      a.chunk = makeChunkPlan(count, comm->nranks, cfg.channels,
+      a.chunk = makeChunkPlan(count, comm->nranks, cap(cfg.channels),
                               (uint64_t)cfg.tsChunkBytes / es, kTwoShotMinChunkBytes / es, V);
       break;
     case TNCCL_ALGO_ONESHOT:
-      a.block = makeBlockPlan(count, cfg.osChannels, (uint64_t)cfg.osTileBytes / es,
+      a.block = makeBlockPlan(count, cap(cfg.osChannels), (uint64_t)cfg.osTileBytes / es,
                               kOneShotMinTileBytes / es, V);
       break;
     case TNCCL_ALGO_NVLS:
-      a.block = makeBlockPlan(count, comm->nvls.channels, comm->nvls.tileBytes / es,
+      a.block = makeBlockPlan(count, cap(comm->nvls.channels), comm->nvls.tileBytes / es,
                               kNvlsMinTileBytes / es, V);
       break;
     default:

@@ -111,6 +111,11 @@ class Communicator {
     return tncclAlgoName(a);
   }
 
+  void setMaxChannels(int n) {
+    live();
+    check(tncclCommSetMaxChannels(comm_, n), "tncclCommSetMaxChannels");
+  }
+
   int asyncError() {
     live();
     tncclResult r;
@@ -262,6 +267,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
            py::arg("count"), py::arg("dtype"), py::arg("op") = "sum", py::arg("scale") = 1.0,
            py::arg("algo") = "auto", py::arg("stream") = 0)
       .def("select_algo", &Communicator::selectAlgo)
+      .def("set_max_channels", &Communicator::setMaxChannels, py::arg("max_channels"))
       .def("async_error", &Communicator::asyncError)
       .def("abort", &Communicator::abort)
       .def("destroy", &Communicator::destroy)

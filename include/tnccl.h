@@ -154,6 +154,14 @@ tncclResult tncclCommCount(tncclComm_t comm, int* nranks);
 tncclResult tncclCommUserRank(tncclComm_t comm, int* rank);
 tncclResult tncclCommCuDevice(tncclComm_t comm, int* device);
 
+/* Caps the CTAs (channels) of every later ring / two-shot / one-shot / NVLS
+ * launch on this communicator at maxChannels (clamped to 1 .. the configured
+ * count; 0 restores the configured count). A collective that overlaps with
+ * compute (the DDP hook) leaves the other SMs to the compute kernels. Local
+ * to the rank and stream-ordered like any launch parameter; ranks should use
+ * the same cap. */
+tncclResult tncclCommSetMaxChannels(tncclComm_t comm, int maxChannels);
+
 /* The algorithm TNCCL_ALGO_AUTO would use for this message. */
 tncclResult tncclCommSelectAlgo(tncclComm_t comm, size_t count,
                                 tncclDataType_t dtype, tncclAlgo_t* algo);

@@ -72,6 +72,11 @@ class Communicator:
             stream = torch.cuda.current_stream(self.device).cuda_stream
         self._c.all_reduce_ptr(send, recv, count, code, op, float(scale), algo, stream)
 
+    def set_max_channels(self, max_channels: int) -> None:
+        """Caps the CTAs of later collectives (0 restores the configured count);
+        a collective that overlaps with compute leaves the other SMs to it."""
+        self._c.set_max_channels(int(max_channels))
+
     def select_algo(self, numel: int, dtype: torch.dtype) -> str:
         return self._c.select_algo(numel, dtype)
 

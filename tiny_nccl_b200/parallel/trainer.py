@@ -4,6 +4,8 @@ kernel, overlapped with backward) and the fused AdamW kernel.
 """
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.distributed as dist
 from torch.nn.parallel import DistributedDataParallel as DDP
@@ -17,10 +19,15 @@ class DataParallelTrainer:
     def __init__(self, model: torch.nn.Module, comm: Communicator, lr: float = 6e-4,
                  weight_decay: float = 0.1, betas=(0.9, 0.95), bucket_cap_mb: int = 25,
                  algo: str = "auto", wire_dtype: torch.dtype | None = None,
-                 amp_dtype: torch.dtype = torch.bfloat16):
+                 amp_dtype: torch.dtype = torch.bfloat16, max_channels: int | None = None):
         if not dist.is_initialized():
             raise RuntimeError("DataParallelTrainer needs torch.distributed initialised")
         self.comm = comm
+        # Gradient all-reduces run concurrently with backward kernels: cap
+        # their CTAs so compute keeps most SMs (TNCCL_DDP_CHANNELS, default 32).
+        if max_channels is None:
+            max_channels = int(os.environ.get("TNCCL_DDP_CHANNELS", "32"))
+        comm.set_max_channels(max_channels)
         self.model = model
         self.amp_dtype = amp_dtype
         dev = comm.device
