@@ -23,14 +23,50 @@ import torch.distributed as dist
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 NAMES = {
-    2: {0: "tile start", 1: "RS arrived", 2: "reduced+AG published", 3: "next RS pushed",
+    2: {0: "pushed+published", 1: "RS arrived", 2: "reduced+AG published",
         4: "AG arrived", 5: "copied out"},
     1: {0: "tile start", 1: "slot free", 2: "pushed+published", 3: "peers arrived",
         4: "reduced+acked"},
-    3: {0: "tile start", 1: "copied in", 2: "barrier 1", 3: "switch reduce+store",
-        4: "barrier 2", 5: "copied out"},
+    3: {1: "copied in", 2: "all copied in", 3: "switch reduce+store counted",
+        4: "all stored", 5: "copied out"},
 }
 FAMILY = {"ring": 0, "oneshot": 1, "twoshot": 2, "nvls": 3}
+
+# Warp-specialised kernels: each team marks its own phases. (start mark,
+# end mark) pairs give a team's busy time per tile; (end of tile t-1, start
+# of tile t) its wait. The push / copy-in team marks once per tile (period).
+TEAMS = {
+    2: {"push": (None, 0), "reduce": (1, 2), "gather": (4, 5)},
+    3: {"copy-in": (None, 1), "switch": (2, 3), "copy-out": (4, 5)},
+}
+
+
+def team_stats(raw: dict, fam: int) -> dict:
+    """Mean busy / wait / period per team over every channel's last call."""
+    out = {}
+    acc = {}
+    for ev in raw.values():
+        ts = [e[0] for e in ev]
+        if len(ts) < 2:
+            continue
+        gap, i = max((ts[k + 1] - ts[k], k) for k in range(len(ts) - 1))
+        last = ev[i + 1:] if gap > 50_000 else ev  # keep the final call
+        by = collections.defaultdict(dict)
+        for t, p, tile in last:
+            by[p][tile] = t
+        for team, (s, e) in TEAMS.get(fam, {}).items():
+            for tile in by[e]:
+                if s is None:
+                    if tile - 1 in by[e]:
+                        acc.setdefault((team, "period"), []).append(by[e][tile] - by[e][tile - 1])
+                    continue
+                if tile in by[s]:
+                    acc.setdefault((team, "busy"), []).append(by[e][tile] - by[s][tile])
+                if tile in by[s] and tile - 1 in by[e]:
+                    acc.setdefault((team, "wait"), []).append(by[s][tile] - by[e][tile - 1])
+    for (team, kind), v in acc.items():
+        out[f"{team} {kind}"] = {"mean_us": sum(v) / len(v) / 1e3, "n": len(v)}
+    return out
 
 
 def main():
@@ -77,6 +113,7 @@ def main():
     summary = {f"{NAMES.get(fam, {}).get(a, a)} -> {NAMES.get(fam, {}).get(b, b)}":
                {"mean_us": sum(v) / len(v) / 1e3, "n": len(v)} for (a, b), v in sorted(deltas.items())}
     rec = {"rank": rank, "algo": args.algo, "bytes": size, "phases": summary,
+           "teams": team_stats(raw, fam),
            "channel_span_us_mean": sum(spans) / max(1, len(spans)) / 1e3}
     if args.dump:
         with open(f"{args.dump}.rank{rank}.json", "w") as f:

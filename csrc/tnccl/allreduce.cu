@@ -300,7 +300,8 @@ __device__ __forceinline__ bool haveSmem(const DevComm& comm, uint32_t need, int
 // or a peer's mailbox). The vectors that every source has are streamed
 // through the team's TMA stage ring, all sources in one pass; what is left
 // of each source (other chunk lengths, scalar tails, unaligned buffers) goes
-// through registers. Returns false if a stage never landed.
+// through registers; so does everything when the shortest source is below
+// DevComm::stageMinBytes. Returns false if a stage never landed.
 template <typename T, int MAXSRC, int LD, typename SrcF, typename CountF, typename DstF>
 __device__ __forceinline__ bool stagedCopy(const DevComm& comm, const Team& tm, StageRing& R,
                                            int n, bool vec, SrcF src, CountF count, DstF dst,
@@ -311,7 +312,7 @@ __device__ __forceinline__ bool stagedCopy(const DevComm& comm, const Team& tm, 
     const uint64_t c = count(k) / V;
     nv = c < nv ? c : nv;
   }
-  if (!vec || n == 0) nv = 0;
+  if (!vec || n == 0 || nv * 16 < comm.stageMinBytes) nv = 0;
   if (nv > 0 && !stageStream<MAXSRC>(
                     comm, tm, R, n, nv, [&](int k) -> const void* { return src(k); },
                     [&](uint64_t i, const uint4* v) {
@@ -444,7 +445,11 @@ __device__ __forceinline__ void twoShotBody(const DevComm& comm, const AllReduce
       // Vector part: every rank's contribution staged through shared memory
       // by TMA (own input from x, the others from the reduce-scatter slots),
       // summed in rank order in fp32, stored to y and pushed to every peer.
-      const uint64_t nv = vec ? own.count / V : 0;
+      // Short chunks skip the staging (one TMA round trip and two team
+      // barriers per stage cost more than they hide) and reduce through
+      // registers below.
+      const uint64_t nv =
+          vec && own.count * sizeof(T) >= comm.stageMinBytes ? own.count / V : 0;
       if (nv > 0 &&
           !stageStream<MAXP>(
               comm, tm, redRing, P, nv,
@@ -476,12 +481,19 @@ __device__ __forceinline__ void twoShotBody(const DevComm& comm, const AllReduce
         sFail = 1;
         break;
       }
-      // Scalar tail (the whole chunk for unaligned buffers).
+      // The rest: scalar tail, or the whole chunk when it is short (vectors)
+      // or the buffers are unaligned (scalars).
       const uint64_t e0 = nv * V;
       reduceRanks<T, MAXP, U>(
-          tm, own.count - e0, false, P, r, x + own.offset + e0, alpha,
+          tm, own.count - e0, vec && nv == 0, P, r, x + own.offset + e0, alpha,
           [&](int q) { return me + tsRsDataAt(L, c, slot, q) + e0 * sizeof(T); },
-          [&](uint64_t, uint4) {},
+          [&](uint64_t i, uint4 v) {
+            st16(reinterpret_cast<uint4*>(y + own.offset + e0) + i, v);
+            for (int d = 1; d < P; ++d) {
+              const int j = (r + d) % P;
+              st16(reinterpret_cast<uint4*>(comm.peers[j] + agOff + e0 * sizeof(T)) + i, v);
+            }
+          },
           [&](uint64_t e, float f) {
             stElem(y + own.offset + e0 + e, f);
             for (int d = 1; d < P; ++d) {

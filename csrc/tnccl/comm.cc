@@ -155,6 +155,7 @@ void fillDevComm(tncclComm* comm) {
   d.tsRedStage = (uint32_t)comm->cfg.tsRedStage;
   d.nvlsStages = comm->cfg.nvlsStages;
   d.nvlsStage = (uint32_t)comm->cfg.nvlsStage;
+  d.stageMinBytes = (uint32_t)comm->cfg.stageMinBytes;
 }
 
 void deriveThresholds(tncclComm* comm) {

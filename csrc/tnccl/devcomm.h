@@ -55,6 +55,8 @@ struct DevComm {
   // NVLS copy-in / copy-out staging: stages per team, bytes per stage.
   int nvlsStages;
   uint32_t nvlsStage;
+  // Copies of fewer bytes per source than this go through registers.
+  uint32_t stageMinBytes;
 };
 
 // Tag of one trace record: algorithm family, phase, tile index (low 16 bits).

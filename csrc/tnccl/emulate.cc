@@ -136,6 +136,7 @@ extern "C" tncclResult tncclEmuCreate(tncclEmu_t* out, int nranks) {
     dc.tsRedStage = (uint32_t)e->cfg.tsRedStage;
     dc.nvlsStages = e->cfg.nvlsStages;
     dc.nvlsStage = (uint32_t)e->cfg.nvlsStage;
+    dc.stageMinBytes = (uint32_t)e->cfg.stageMinBytes;
   }
   *out = e;
   return TNCCL_SUCCESS;

@@ -113,3 +113,38 @@ def test_emulated_in_place_and_sequence(emulators):
         for x in xs:
             assert bool(torch.all(x == want)), (it, algo)
     assert emu.async_error() == 0
+
+
+@pytest.mark.parametrize("P", [2, 4])
+@pytest.mark.parametrize("stage_min", [0, 1 << 30])
+def test_emulated_twoshot_staging_paths(built, P, stage_min):
+    """Two-shot with every copy staged through shared memory by TMA
+    (TNCCL_STAGE_MIN_BYTES=0) and with none staged, bit for bit against the
+    oracle, whichever is the default for this rank count."""
+    import tiny_nccl_b200 as tn
+    old = os.environ.get("TNCCL_STAGE_MIN_BYTES")
+    os.environ["TNCCL_STAGE_MIN_BYTES"] = str(stage_min)
+    os.environ["TNCCL_NCHANNELS"] = str(CHANNELS)
+    try:
+        emu = tn.load().Emulator(P)
+    finally:
+        if old is None:
+            del os.environ["TNCCL_STAGE_MIN_BYTES"]
+        else:
+            os.environ["TNCCL_STAGE_MIN_BYTES"] = old
+    try:
+        g = torch.Generator(device="cuda")
+        for count in (4097, 1_000_003, 3_000_000):
+            for dtype in (torch.float32, torch.bfloat16):
+                g.manual_seed(count + P)
+                xs = [(torch.rand(count, device="cuda", generator=g) * 2 - 1).to(dtype)
+                      for _ in range(P)]
+                ys = [torch.empty_like(x) for x in xs]
+                emu.all_reduce(xs, ys, algo="twoshot")
+                torch.cuda.synchronize()
+                assert emu.async_error() == 0
+                want = oracle(xs, "twoshot", 1.0, dtype)
+                for y in ys:
+                    assert bool(torch.equal(y, want)), (P, stage_min, count, dtype)
+    finally:
+        emu.destroy()
