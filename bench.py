@@ -17,6 +17,8 @@ Weak scaling: every GPU processes 8 x 1024 tokens per step.
   baseline/build_reference.sh) all-reduces the gradient buckets through its
   public tncclAllReduceSumF32, inside stock PyTorch: Hugging Face GPT2LMHeadModel,
   torch.optim.AdamW, DistributedDataParallel.
+--impl nccl-ddp: the NCCL-DDP baseline, the same stock PyTorch stack with
+  DDP's own NCCL all-reduce.
 
 Timing: W untimed warm-up steps; then K steps bracketed by a barrier and
 torch.cuda.synchronize(), timed with CUDA events on the training stream; the
@@ -158,6 +160,35 @@ def build_reference_trainer(args, rank, world, dev):
     return step, launches, ref.destroy
 
 
+def build_nccl_ddp_trainer(args, rank, world, dev):
+    """The NCCL-DDP baseline: stock PyTorch GPT-2 (Hugging Face), stock DDP
+    (NCCL all-reduce of fp32 gradient buckets), torch fused AdamW."""
+    from torch.nn.parallel import DistributedDataParallel as DDP
+    from transformers import GPT2Config as HFConfig, GPT2LMHeadModel
+
+    cfg = HFConfig(n_layer=12, n_head=12, n_embd=768, vocab_size=50257, n_positions=1024,
+                   resid_pdrop=0.0, embd_pdrop=0.0, attn_pdrop=0.0)
+    torch.manual_seed(1234)
+    model = GPT2LMHeadModel(cfg).to(dev)
+    ddp = DDP(model, device_ids=[dev.index], bucket_cap_mb=25, gradient_as_bucket_view=True,
+              static_graph=True, broadcast_buffers=False)
+    decay = [p for p in model.parameters() if p.dim() >= 2]
+    no_decay = [p for p in model.parameters() if p.dim() < 2]
+    opt = torch.optim.AdamW([{"params": decay, "weight_decay": 0.1},
+                             {"params": no_decay, "weight_decay": 0.0}], lr=6e-4,
+                            betas=(0.9, 0.95), fused=True)
+
+    def step(idx, tgt):
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            out = ddp(input_ids=idx, labels=idx)
+        out.loss.backward()
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+        return out.loss.detach()
+
+    return step, (lambda: 0), (lambda: None)
+
+
 def build_tnccl_trainer(args, rank, world, dev):
     import tiny_nccl_b200 as tn
     from tiny_nccl_b200.models import GPT2, GPT2Config
@@ -183,7 +214,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", default="tnccl", choices=["tnccl", "reference"])
+    ap.add_argument("--impl", default="tnccl", choices=["tnccl", "reference", "nccl-ddp"])
     ap.add_argument("--batch", type=int, default=8)
     ap.add_argument("--seq", type=int, default=1024)
     ap.add_argument("--algo", default="auto")
@@ -205,6 +236,8 @@ def main():
     B, T = args.batch, args.seq
     if args.impl == "reference":
         step, launches, close = build_reference_trainer(args, rank, world, dev)
+    elif args.impl == "nccl-ddp":
+        step, launches, close = build_nccl_ddp_trainer(args, rank, world, dev)
     else:
         step, launches, close = build_tnccl_trainer(args, rank, world, dev)
 

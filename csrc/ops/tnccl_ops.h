@@ -40,6 +40,17 @@ int tnops_ln_partial_rows(void);
 int tnops_cross_entropy_fwd_bwd(uint16_t* logits, const int64_t* target, float* loss, int rows,
                                 int V, int ld, int valid, cudaStream_t stream);
 
+// Bias gradient of a linear layer: db[n] = sum_m g[m, n] (g bf16 [M, N],
+// db fp32 [N], N a multiple of 8), deterministic two-pass column sum through
+// `partial` (tnops_colsum_parts(M, N) * N floats).
+int tnops_bias_grad(const uint16_t* g, float* db, float* partial, int M, int N,
+                    cudaStream_t stream);
+// Fused tanh-GELU backward and bias gradient of the linear layer feeding the
+// GELU: gpre = bf16(gy * gelu'(pre)), db[n] = sum_m gpre[m, n].
+int tnops_gelu_bwd_bias(const uint16_t* gy, const uint16_t* pre, uint16_t* gpre, float* db,
+                        float* partial, int M, int N, cudaStream_t stream);
+int tnops_colsum_parts(int M, int N);
+
 // Multiplies a bf16 tensor by the fp32 scalar *scale (device memory); no-op
 // on the device when *scale == 1.
 int tnops_scale_bf16(uint16_t* x, size_t n, const float* scale, cudaStream_t stream);

@@ -99,6 +99,36 @@ at::Tensor crossEntropy(at::Tensor logits, const at::Tensor& target, int64_t val
   return loss;
 }
 
+// g bf16 [M, N] -> db fp32 [N] (column sums)
+at::Tensor biasGrad(const at::Tensor& g) {
+  need(g, at::kBFloat16, "grad");
+  TORCH_CHECK(g.dim() == 2 && g.size(1) % 8 == 0, "bias_grad: want [M, N] with N % 8 == 0");
+  c10::cuda::CUDAGuard guard(g.device());
+  const int M = (int)g.size(0), N = (int)g.size(1);
+  auto db = at::empty({N}, g.options().dtype(at::kFloat));
+  auto part = at::empty({(int64_t)tnops_colsum_parts(M, N) * N}, g.options().dtype(at::kFloat));
+  ok(tnops_bias_grad(bf(g), db.data_ptr<float>(), part.data_ptr<float>(), M, N, streamOf(g)),
+     "tnops_bias_grad");
+  return db;
+}
+
+// gy, pre bf16 [M, N] -> (gpre bf16 [M, N], db fp32 [N])
+std::vector<at::Tensor> geluBwdBias(const at::Tensor& gy, const at::Tensor& pre) {
+  need(gy, at::kBFloat16, "grad_y");
+  need(pre, at::kBFloat16, "pre");
+  TORCH_CHECK(gy.dim() == 2 && gy.sizes() == pre.sizes() && gy.size(1) % 8 == 0,
+              "gelu_bwd_bias: want equal [M, N] with N % 8 == 0");
+  c10::cuda::CUDAGuard guard(gy.device());
+  const int M = (int)gy.size(0), N = (int)gy.size(1);
+  auto gpre = at::empty_like(gy);
+  auto db = at::empty({N}, gy.options().dtype(at::kFloat));
+  auto part = at::empty({(int64_t)tnops_colsum_parts(M, N) * N}, gy.options().dtype(at::kFloat));
+  ok(tnops_gelu_bwd_bias(bf(gy), bf(pre), bf(gpre), db.data_ptr<float>(), part.data_ptr<float>(),
+                         M, N, streamOf(gy)),
+     "tnops_gelu_bwd_bias");
+  return {gpre, db};
+}
+
 void scaleBf16(at::Tensor x, const at::Tensor& scale) {
   need(x, at::kBFloat16, "x");
   need(scale, at::kFloat, "scale");
@@ -149,6 +179,8 @@ void registerOps(py::module_& m) {
           py::arg("weight"), py::arg("mean"), py::arg("rstd"), py::arg("want_bf16"));
   ops.def("cross_entropy_fwd_bwd", &crossEntropy, py::arg("logits"), py::arg("target"),
           py::arg("valid"), py::arg("classes") = 0);
+  ops.def("bias_grad", &biasGrad, py::arg("grad"));
+  ops.def("gelu_bwd_bias", &geluBwdBias, py::arg("grad_y"), py::arg("pre"));
   ops.def("scale_bf16_", &scaleBf16);
   ops.def("adamw", &adamw);
   ops.def("launch_count", []() { return tnops_launch_count(); });

@@ -94,3 +94,75 @@ def test_adamw_matches_torch(ops):
         opt_b.step()
     for x, y in zip(a, b):
         torch.testing.assert_close(x, y, atol=1e-6, rtol=1e-5)
+
+
+@pytest.mark.parametrize("M,N", [(8192, 768), (1000, 3072), (37, 2304), (5, 8)])
+def test_bias_grad(ops, M, N):
+    """Column sums of a bf16 gradient (the bias gradient) vs fp32 torch."""
+    from tiny_nccl_b200._native import load
+    torch.manual_seed(M + N)
+    g = torch.randn(M, N, device="cuda").to(torch.bfloat16)
+    db = load().ops.bias_grad(g)
+    ref = g.float().sum(0)
+    assert db.dtype == torch.float32
+    torch.testing.assert_close(db, ref, rtol=1e-5, atol=1e-4)
+    # deterministic: the same bits on a second call
+    assert torch.equal(db, load().ops.bias_grad(g))
+
+
+def _gelu_tanh_grad64(x):
+    k0, k1 = (2.0 / torch.pi) ** 0.5, 0.044715
+    t = torch.tanh(k0 * (x + k1 * x ** 3))
+    return 0.5 * (1 + t) + 0.5 * x * (1 - t * t) * k0 * (1 + 3 * k1 * x * x)
+
+
+@pytest.mark.parametrize("M,N", [(4096, 3072), (129, 64)])
+def test_gelu_bwd_bias(ops, M, N):
+    """Fused tanh-GELU backward + bias gradient vs an fp64 reference of the
+    same formula: the bf16 gradient within one rounding, the bias gradient
+    as the fp32 column sum of the kernel's own bf16 gradient."""
+    from tiny_nccl_b200._native import load
+    torch.manual_seed(N)
+    gy = torch.randn(M, N, device="cuda").to(torch.bfloat16)
+    pre = (2 * torch.randn(M, N, device="cuda")).to(torch.bfloat16)
+    gpre, db = load().ops.gelu_bwd_bias(gy, pre)
+    ref = (gy.double() * _gelu_tanh_grad64(pre.double())).to(torch.bfloat16)
+    # One bf16 rounding of the product, plus the fp32 evaluation error of
+    # gelu' (absolute, scaled by |gy|) where the derivative nearly cancels.
+    diff = (gpre.float() - ref.float()).abs()
+    bound = ref.float().abs() * 2.0 ** -7 + gy.float().abs() * 1e-5 + 1e-30
+    assert bool((diff <= bound).all()), float((diff / bound).max())
+    torch.testing.assert_close(db, gpre.float().sum(0), rtol=1e-5, atol=1e-4)
+
+
+def test_linear_autograd_matches_torch(ops):
+    """ops.linear / ops.linear_gelu (custom backward: fp32 weight gradient
+    from the GEMM, fused bias / GELU gradients) vs autocast nn.functional."""
+    torch.manual_seed(3)
+    x = torch.randn(4, 256, 768, device="cuda")
+    lin = torch.nn.Linear(768, 3072).cuda()
+    lin2 = torch.nn.Linear(3072, 768).cuda()
+    gy = torch.randn(4, 256, 768, device="cuda")
+
+    def run(fused):
+        for p in (*lin.parameters(), *lin2.parameters()):
+            p.grad = None
+        xi = x.clone().requires_grad_()
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            if fused:
+                h = ops.linear_gelu(xi, lin.weight, lin.bias)
+                y = ops.linear(h, lin2.weight, lin2.bias)
+            else:
+                h = torch.nn.functional.gelu(lin(xi), approximate="tanh")
+                y = lin2(h)
+        (y.float() * gy).sum().backward()
+        return y.float(), xi.grad, [p.grad.clone() for p in (*lin.parameters(), *lin2.parameters())]
+
+    yf, gxf, gpf = run(True)
+    yt, gxt, gpt = run(False)
+    torch.testing.assert_close(yf, yt, rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(gxf, gxt, rtol=5e-2, atol=5e-2)
+    for a, b in zip(gpf, gpt):
+        assert a.dtype == torch.float32
+        rel = (a - b).norm() / b.norm()
+        assert rel < 2e-2, float(rel)

@@ -71,9 +71,9 @@ class Block(nn.Module):
         self.mlp_fc = nn.Linear(d, 4 * d)
         self.mlp_proj = nn.Linear(4 * d, d)
 
-    def attention(self, h: torch.Tensor) -> torch.Tensor:
+    def attention(self, h: torch.Tensor, ops=None) -> torch.Tensor:
         B, T, C = h.shape
-        qkv = self.attn_qkv(h)
+        qkv = ops.linear(h, self.attn_qkv.weight, self.attn_qkv.bias) if ops else self.attn_qkv(h)
         q, k, v = qkv.split(C, dim=2)
         hd = C // self.n_head
         q = q.view(B, T, self.n_head, hd).transpose(1, 2)
@@ -81,6 +81,8 @@ class Block(nn.Module):
         v = v.view(B, T, self.n_head, hd).transpose(1, 2)
         y = F.scaled_dot_product_attention(q, k, v, is_causal=True)
         y = y.transpose(1, 2).contiguous().view(B, T, C)
+        if ops:
+            return ops.linear(y, self.attn_proj.weight, self.attn_proj.bias)
         return self.attn_proj(y)
 
     def forward_torch(self, x: torch.Tensor) -> torch.Tensor:
@@ -89,7 +91,8 @@ class Block(nn.Module):
         return x + self.mlp_proj(h)
 
     def mlp_fused(self, h: torch.Tensor, ops) -> torch.Tensor:
-        return self.mlp_proj(ops.linear_gelu(h, self.mlp_fc.weight, self.mlp_fc.bias))
+        g = ops.linear_gelu(h, self.mlp_fc.weight, self.mlp_fc.bias)
+        return ops.linear(g, self.mlp_proj.weight, self.mlp_proj.bias)
 
 
 class GPT2(nn.Module):
@@ -158,7 +161,7 @@ class GPT2(nn.Module):
         h = ops.layer_norm(x, first.weight, first.bias)
         L = len(self.blocks)
         for i, blk in enumerate(self.blocks):
-            a = blk.attention(h.view(B, T, C))
+            a = blk.attention(h.view(B, T, C), ops)
             x, h = ops.add_layer_norm(x, a.reshape(B * T, C), blk.ln_2.weight, blk.ln_2.bias)
             m = blk.mlp_fused(h, ops)
             nxt = self.blocks[i + 1].ln_1 if i + 1 < L else self.ln_f

@@ -95,10 +95,69 @@ def cross_entropy(logits: torch.Tensor, target: torch.Tensor,
     return _CrossEntropy.apply(logits.contiguous(), target.contiguous(), int(classes))
 
 
+def _wgrad(gy: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+    """dW = gy^T x with bf16 operands and the fp32 result written by the GEMM
+    itself (no bf16 rounding, no separate cast to the fp32 parameter)."""
+    return torch.mm(gy.t(), x, out_dtype=torch.float32)
+
+
+class _LinearBias(torch.autograd.Function):
+    """y = x W^T + b in bf16 (cuBLAS GEMM with bias epilogue) for fp32
+    parameters. Backward: dX and dW on cuBLAS (dW written in fp32), db by the
+    deterministic column-sum kernel."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias):
+        w16 = weight.to(torch.bfloat16)
+        with torch.autocast("cuda", enabled=False):
+            y = torch.addmm(bias.to(torch.bfloat16), x, w16.t())
+        ctx.save_for_backward(x, w16)
+        return y
+
+    @staticmethod
+    def backward(ctx, gy):
+        x, w16 = ctx.saved_tensors
+        gy = gy.contiguous()
+        return gy @ w16, _wgrad(gy, x), _ops().bias_grad(gy)
+
+
+class _LinearGelu(torch.autograd.Function):
+    """y = GELU_tanh(x W^T + b). Backward: one kernel computes the GELU
+    gradient and the bias gradient (column sums of that gradient); dX and dW
+    on cuBLAS."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias):
+        w16 = weight.to(torch.bfloat16)
+        with torch.autocast("cuda", enabled=False):
+            pre = torch.addmm(bias.to(torch.bfloat16), x, w16.t())
+            y = torch.nn.functional.gelu(pre, approximate="tanh")
+        ctx.save_for_backward(x, w16, pre)
+        return y
+
+    @staticmethod
+    def backward(ctx, gy):
+        x, w16, pre = ctx.saved_tensors
+        gpre, db = _ops().gelu_bwd_bias(gy.contiguous(), pre)
+        return gpre @ w16, _wgrad(gpre, x), db
+
+
+def _rows(x: torch.Tensor) -> torch.Tensor:
+    x = x.reshape(-1, x.shape[-1])
+    return (x if x.dtype == torch.bfloat16 else x.to(torch.bfloat16)).contiguous()
+
+
+def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
+    """bf16 x W^T + b over the last dimension of x (fp32 weight and bias)."""
+    y = _LinearBias.apply(_rows(x), weight, bias)
+    return y.view(*x.shape[:-1], weight.shape[0])
+
+
 def linear_gelu(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
-    """GELU(tanh)(x W^T + b): cuBLAS GEMM with fused bias, tanh-GELU kernel."""
-    return torch.nn.functional.gelu(torch.nn.functional.linear(x, weight, bias),
-                                    approximate="tanh")
+    """GELU(tanh)(x W^T + b) in bf16; the backward fuses the GELU gradient
+    with the bias gradient."""
+    y = _LinearGelu.apply(_rows(x), weight, bias)
+    return y.view(*x.shape[:-1], weight.shape[0])
 
 
 def launch_count() -> int:
