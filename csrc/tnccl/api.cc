@@ -92,6 +92,13 @@ extern "C" tncclResult tncclCommGetInfo(tncclComm_t comm, tncclCommInfo* info) {
   return TNCCL_SUCCESS;
 }
 
+extern "C" tncclResult tncclCommValidate(tncclComm_t comm, int* corrupted) {
+  if (comm == nullptr || corrupted == nullptr) return TNCCL_INVALID_ARGUMENT;
+  if (comm->streamBound && cudaStreamSynchronize(comm->boundStream) != cudaSuccess)
+    return TNCCL_CUDA_ERROR;
+  return countBadCanaries(comm, corrupted);
+}
+
 extern "C" tncclResult tncclCommSetMaxChannels(tncclComm_t comm, int maxChannels) {
   if (comm == nullptr || maxChannels < 0) return TNCCL_INVALID_ARGUMENT;
   comm->maxChannels = maxChannels;

@@ -82,8 +82,34 @@ tncclResult initMailboxContents(tncclComm* comm) {
   if (cudaMemcpy(comm->local.base + L.ringCreditOff, credits.data(),
                  credits.size() * sizeof(uint64_t), cudaMemcpyHostToDevice) != cudaSuccess)
     return TNCCL_CUDA_ERROR;
+  for (int k = 0; k < kNumCanaries; ++k)
+    if (cudaMemset(comm->local.base + L.canaryOff[k], kCanaryByte, kCanaryBytes) != cudaSuccess)
+      return TNCCL_CUDA_ERROR;
   return cudaDeviceSynchronize() == cudaSuccess ? TNCCL_SUCCESS : TNCCL_CUDA_ERROR;
 }
+
+}  // namespace
+
+// Counts the canary regions of this rank's mailbox that no longer hold
+// kCanaryByte (the caller has synchronised the bound stream).
+tncclResult countBadCanaries(tncclComm* comm, int* corrupted) {
+  *corrupted = 0;
+  if (comm->local.base == nullptr) return TNCCL_SUCCESS;
+  unsigned char buf[kCanaryBytes];
+  for (int k = 0; k < kNumCanaries; ++k) {
+    if (cudaMemcpy(buf, comm->local.base + comm->layout.canaryOff[k], kCanaryBytes,
+                   cudaMemcpyDeviceToHost) != cudaSuccess)
+      return TNCCL_CUDA_ERROR;
+    for (uint64_t i = 0; i < kCanaryBytes; ++i)
+      if (buf[i] != kCanaryByte) {
+        ++*corrupted;
+        break;
+      }
+  }
+  return TNCCL_SUCCESS;
+}
+
+namespace {
 
 tncclResult allocDeviceState(tncclComm* comm) {
   void* h = nullptr;
@@ -359,6 +385,10 @@ extern "C" tncclResult tncclCommDestroy(tncclComm_t comm) {
     delete comm;
     return TNCCL_SUCCESS;
   }
+  int corrupted = 0;
+  if (countBadCanaries(comm, &corrupted) == TNCCL_SUCCESS && corrupted > 0)
+    TN_WARN("rank %d: %d mailbox canary region(s) overwritten; a kernel wrote past an area",
+            comm->rank, corrupted);
   tncclResult b1 = bootstrapBarrier(&comm->bootstrap);  // every kernel has finished
   if (b1 != TNCCL_SUCCESS) result = b1;
   nvlsUnmap(comm, &result);

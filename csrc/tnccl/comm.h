@@ -117,6 +117,9 @@ void nvlsRelease(tncclComm* comm, tncclResult* result);
 // enqueue.cc
 tncclAlgo_t selectAlgo(const tncclComm* comm, uint64_t bytes);
 
+// comm.cc: mailbox canary regions that were overwritten.
+tncclResult countBadCanaries(tncclComm* comm, int* corrupted);
+
 // Launch counter shared by every kernel launch in the library.
 extern std::atomic<unsigned long long> gLaunchCount;
 

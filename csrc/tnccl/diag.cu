@@ -309,6 +309,15 @@ extern "C" tncclResult tncclDiagWaitTimeout(tncclComm_t comm, int timeoutMs, cud
   return cudaGetLastError() == cudaSuccess ? TNCCL_SUCCESS : TNCCL_CUDA_ERROR;
 }
 
+extern "C" tncclResult tncclDiagCorruptCanary(tncclComm_t comm, int which) {
+  if (comm == nullptr || which < 0 || which >= kNumCanaries || comm->local.base == nullptr)
+    return TNCCL_INVALID_ARGUMENT;
+  if (cudaMemset(comm->local.base + comm->layout.canaryOff[which], 0, 8) != cudaSuccess ||
+      cudaDeviceSynchronize() != cudaSuccess)
+    return TNCCL_CUDA_ERROR;
+  return TNCCL_SUCCESS;
+}
+
 extern "C" tncclResult tncclCommTraceRead(tncclComm_t comm, int channel, unsigned long long* out,
                                           size_t maxRecords, size_t* n) {
   if (comm == nullptr || n == nullptr || channel < 0 || channel >= kMaxChannels)

@@ -30,6 +30,10 @@ extern "C" {
 // reports TNCCL_TIMEOUT and the communicator refuses further collectives.
 tncclResult tncclDiagWaitTimeout(tncclComm_t comm, int timeoutMs, cudaStream_t stream);
 
+// Overwrites guard line `which` (0 .. 4) of this rank's mailbox from the host
+// (cudaMemset), so a test can check that tncclCommValidate notices.
+tncclResult tncclDiagCorruptCanary(tncclComm_t comm, int which);
+
 #ifdef __cplusplus
 }
 #endif

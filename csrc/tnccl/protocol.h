@@ -201,8 +201,18 @@ struct MailboxLayout {
   uint64_t osTileBytes;
   uint64_t osDataOff, osFlagOff, osAckOff;
 
+  // Canary lines after every data area and after the flag block: filled
+  // with kCanaryByte at init and checked by tncclCommValidate / destroy, so
+  // a write past the end of an area shows up (kNumCanaries regions of
+  // kCanaryBytes).
+  uint64_t canaryOff[5];
+
   uint64_t totalBytes;
 };
+
+constexpr int kNumCanaries = 5;
+constexpr uint64_t kCanaryBytes = 128;
+constexpr unsigned char kCanaryByte = 0xA5;
 
 struct LayoutConfig {
   int nranks;
@@ -233,15 +243,20 @@ inline MailboxLayout makeLayout(const LayoutConfig& c) {
   uint64_t off = 0;
   L.ringDataOff = off;
   off += C * (uint64_t)c.ringSlots * c.ringChunkBytes;
-  off = alignUp(off, 4096);
+  L.canaryOff[0] = off;
+  off = alignUp(off + kCanaryBytes, 4096);
   L.tsRsDataOff = off;
   off += C * kTwoShotSlots * P * c.tsChunkBytes;
+  L.canaryOff[1] = off;
+  off = alignUp(off + kCanaryBytes, 128);
   L.tsAgDataOff = off;
   off += C * kTwoShotSlots * P * c.tsChunkBytes;
-  off = alignUp(off, 4096);
+  L.canaryOff[2] = off;
+  off = alignUp(off + kCanaryBytes, 4096);
   L.osDataOff = off;
   off += (uint64_t)c.osChannels * (uint64_t)c.osSlots * P * c.osTileBytes;
-  off = alignUp(off, 4096);
+  L.canaryOff[3] = off;
+  off = alignUp(off + kCanaryBytes, 4096);
   // Flag words. Each group starts on its own 128-byte line.
   L.ringReadyOff = off;
   off = alignUp(off + C * (uint64_t)c.ringSlots * 8, 128);
@@ -255,6 +270,8 @@ inline MailboxLayout makeLayout(const LayoutConfig& c) {
   off = alignUp(off + (uint64_t)c.osChannels * (uint64_t)c.osSlots * P * 8, 128);
   L.osAckOff = off;
   off = alignUp(off + (uint64_t)c.osChannels * (uint64_t)c.osSlots * P * 8, 128);
+  L.canaryOff[4] = off;
+  off += kCanaryBytes;
   L.totalBytes = alignUp(off, 4096);
   return L;
 }

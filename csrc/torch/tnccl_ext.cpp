@@ -111,6 +111,18 @@ class Communicator {
     return tncclAlgoName(a);
   }
 
+  int validate() {
+    live();
+    int bad = 0;
+    check(tncclCommValidate(comm_, &bad), "tncclCommValidate");
+    return bad;
+  }
+
+  void diagCorruptCanary(int which) {
+    live();
+    check(tncclDiagCorruptCanary(comm_, which), "tncclDiagCorruptCanary");
+  }
+
   void setMaxChannels(int n) {
     live();
     check(tncclCommSetMaxChannels(comm_, n), "tncclCommSetMaxChannels");
@@ -268,6 +280,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
            py::arg("algo") = "auto", py::arg("stream") = 0)
       .def("select_algo", &Communicator::selectAlgo)
       .def("set_max_channels", &Communicator::setMaxChannels, py::arg("max_channels"))
+      .def("validate", &Communicator::validate)
+      .def("diag_corrupt_canary", &Communicator::diagCorruptCanary, py::arg("which"))
       .def("async_error", &Communicator::asyncError)
       .def("abort", &Communicator::abort)
       .def("destroy", &Communicator::destroy)

@@ -162,6 +162,11 @@ tncclResult tncclCommCuDevice(tncclComm_t comm, int* device);
  * the same cap. */
 tncclResult tncclCommSetMaxChannels(tncclComm_t comm, int maxChannels);
 
+/* Waits for the bound stream, then checks the guard lines placed after every
+ * mailbox area of this rank (filled with a pattern at init). *corrupted is
+ * the number of guard lines that were overwritten (0 = intact). Local. */
+tncclResult tncclCommValidate(tncclComm_t comm, int* corrupted);
+
 /* The algorithm TNCCL_ALGO_AUTO would use for this message. */
 tncclResult tncclCommSelectAlgo(tncclComm_t comm, size_t count,
                                 tncclDataType_t dtype, tncclAlgo_t* algo);

@@ -26,6 +26,20 @@ def test_cuda_graph_capture_replay(built):
 
 
 @pytest.mark.gpu
+def test_trainer_checkpoint_resume(built):
+    n = 2 if gpu_count() >= 2 else 1
+    r = torchrun(n, ["tests/workers/checkpoint_worker.py"], timeout=600)
+    assert r.returncode == 0 and "PASS" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(gpu_count() < 2, reason="needs 2 GPUs")
+def test_mailbox_guard_lines(built):
+    r = torchrun(2, ["tests/workers/canary_worker.py"], timeout=600)
+    assert r.returncode == 0 and "PASS" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
+
+
+@pytest.mark.gpu
 @pytest.mark.skipif(gpu_count() < 2, reason="needs 2 GPUs")
 def test_bounded_wait_timeout_two_ranks(built):
     env = {"TNCCL_TIMEOUT_MS": "1500", "TNCCL_NVLS_ENABLE": "0", "NCCL_NVLS_ENABLE": "0"}

@@ -72,6 +72,11 @@ class Communicator:
             stream = torch.cuda.current_stream(self.device).cuda_stream
         self._c.all_reduce_ptr(send, recv, count, code, op, float(scale), algo, stream)
 
+    def validate(self) -> int:
+        """Waits for the bound stream and returns how many of this rank's
+        mailbox guard lines were overwritten (0 = intact)."""
+        return self._c.validate()
+
     def set_max_channels(self, max_channels: int) -> None:
         """Caps the CTAs of later collectives (0 restores the configured count);
         a collective that overlaps with compute leaves the other SMs to it."""
