@@ -71,7 +71,7 @@ static int64_t roundTo16(int64_t v) { return v < 16 ? 16 : (v + 15) / 16 * 16; }
 Config loadConfig() {
   Config c{};
   c.channels = clampInt(envInt("TNCCL_NCHANNELS", 128), 1, kMaxChannels);
-  c.osChannels = clampInt(envInt("TNCCL_ONESHOT_CHANNELS", 16), 1, kMaxChannels);
+  c.osChannels = clampInt(envInt("TNCCL_ONESHOT_CHANNELS", 64), 1, kMaxChannels);
   c.ringSlots = clampInt(envInt("TNCCL_SLOTS", 4), 2, 16);
   c.ringChunkBytes = roundTo16(envInt("TNCCL_CHUNK_BYTES", 256 << 10));
   c.tsChunkBytes = roundTo16(envInt("TNCCL_TWOSHOT_CHUNK_BYTES", 0));  // 0: by nranks

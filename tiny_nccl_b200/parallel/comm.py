@@ -77,6 +77,14 @@ class Communicator:
         mailbox guard lines were overwritten (0 = intact)."""
         return self._c.validate()
 
+    def side_stream(self) -> torch.cuda.Stream:
+        """A stream of this communicator's device, created once and shared by
+        the components (DDP hooks, trainers) that enqueue on it; the
+        communicator binds to the first stream a collective runs on."""
+        if getattr(self, "_side", None) is None:
+            self._side = torch.cuda.Stream(device=self.device)
+        return self._side
+
     def set_max_channels(self, max_channels: int) -> None:
         """Caps the CTAs of later collectives (0 restores the configured count);
         a collective that overlaps with compute leaves the other SMs to it."""

@@ -21,7 +21,9 @@ class TncclHookState:
     def __init__(self, comm: Communicator, stream: torch.cuda.Stream | None = None,
                  algo: str = "auto", wire_dtype: torch.dtype | None = None):
         self.comm = comm
-        self.stream = stream if stream is not None else torch.cuda.Stream(device=comm.device)
+        # Collectives of a communicator run on the one stream it is bound to,
+        # so every hook on the same communicator shares its side stream.
+        self.stream = stream if stream is not None else comm.side_stream()
         self.algo = algo
         self.wire_dtype = wire_dtype
         self.buckets = 0
