@@ -1,7 +1,9 @@
 // rank_model_test.cc - threaded CPU model of the device protocols.
 //
-// One std::thread per rank runs the ring, one-shot and two-shot algorithms of
-// csrc/tnccl/allreduce.cu step for step on host memory: the same protocol.h
+// One std::thread per rank runs the ring, one-shot, two-shot and NVLS
+// algorithms of csrc/tnccl/allreduce.cu step for step on host memory (the
+// warp-specialised teams of two-shot and NVLS as threads of their own, the
+// NVLS multicast region as one copy per rank): the same protocol.h
 // partition and mailbox layout, 64-bit sequence words written with release
 // stores and polled with acquire loads, per-channel sequence counters that
 // persist across collectives, and bounded waits. Channels of one rank run one
@@ -26,6 +28,7 @@
 #include <atomic>
 #include <chrono>
 #include <functional>
+#include <memory>
 #include <thread>
 #include <vector>
 
@@ -43,7 +46,7 @@ void report(const char* what, bool ok) {
   if (!ok) ++gFailed;
 }
 
-enum Algo { kRing = 1, kOneShot = 2, kTwoShot = 3 };
+enum Algo { kRing = 1, kOneShot = 2, kTwoShot = 3, kNvls = 4 };
 
 struct Config {
   int P = 4;
@@ -54,6 +57,8 @@ struct Config {
   uint64_t tsChunkElems = 8192;
   int osSlots = 2;
   uint64_t osTileElems = 8192;
+  int nvlsChannels = 2;
+  uint64_t nvlsTileElems = 8192;
   uint64_t vec = 4;         // element granularity of chunk boundaries
   uint64_t minChunk = 4;
   int timeoutMs = 2000;
@@ -86,9 +91,48 @@ struct World {
     mem.assign((size_t)c.P, std::vector<uint64_t>(L.totalBytes / 8, 0));
     counters.assign((size_t)c.P, std::vector<uint64_t>(kNumCounterFamilies * kMaxChannels, 0));
     published.assign((size_t)c.P, 0);
+    mc.assign((size_t)c.P, std::vector<float>((size_t)c.nvlsChannels * kNvlsSlots * 2 *
+                                                  c.nvlsTileElems, 0.f));
+    const size_t ncount = (size_t)c.P * 2 * c.nvlsChannels * kNvlsSlots;
+    mcCount.reset(new std::atomic<uint64_t>[ncount]);
+    for (size_t i = 0; i < ncount; ++i) mcCount[i].store(0);
     for (int r = 0; r < c.P; ++r)
       for (int ch = 0; ch < c.channels; ++ch)
         for (int s = 0; s < c.ringSlots; ++s) *flag(r, ringCreditAt(L, ch, s)) = (uint64_t)s;
+  }
+
+  // NVLS: each rank's copy of the multicast region (input / output block per
+  // channel and slot) and of the barrier counters; a multicast store or add
+  // updates every rank's copy, a multicast reduce reads every rank's copy.
+  std::vector<std::vector<float>> mc;
+  std::unique_ptr<std::atomic<uint64_t>[]> mcCount;
+  float* mcIn(int r, int c, int s) {
+    return mc[(size_t)r].data() + ((size_t)c * kNvlsSlots + s) * 2 * cfg.nvlsTileElems;
+  }
+  float* mcOut(int r, int c, int s) { return mcIn(r, c, s) + cfg.nvlsTileElems; }
+  std::atomic<uint64_t>& mcCounter(int r, int phase, int c, int s) {
+    return mcCount[(((size_t)r * 2 + phase) * cfg.nvlsChannels + c) * kNvlsSlots + s];
+  }
+  // multimem.red.release: +1 on every rank's copy.
+  void mcAdd(int self, int phase, int c, int s) {
+    int n = __atomic_fetch_add(&published[(size_t)self], 1, __ATOMIC_RELAXED);
+    if (self == dropRank && n == dropAt) return;  // injected loss
+    for (int q = 0; q < cfg.P; ++q) mcCounter(q, phase, c, s).fetch_add(1, std::memory_order_release);
+  }
+  bool mcWait(int r, int phase, int c, int s, uint64_t want) {
+    auto start = std::chrono::steady_clock::now();
+    uint64_t spins = 0;
+    while (mcCounter(r, phase, c, s).load(std::memory_order_acquire) < want) {
+      if ((++spins & 1023) == 0) {
+        if (error.load()) return false;
+        if (std::chrono::steady_clock::now() - start > std::chrono::milliseconds(cfg.timeoutMs)) {
+          error.store(5);
+          return false;
+        }
+        std::this_thread::yield();
+      }
+    }
+    return true;
   }
 
   char* base(int r) { return reinterpret_cast<char*>(mem[(size_t)r].data()); }
@@ -267,6 +311,88 @@ bool oneShot(World& w, int r, const Job& j, uint64_t count) {
   return true;
 }
 
+bool nvls(World& w, int r, const Job& j, uint64_t count) {
+  // Same structure as nvlsKernel: per channel a copy-in, a switch and a
+  // copy-out role (three threads) coupled by the per-slot multicast counters
+  // (P x uses of the slot) and the local "copied out" counter. The switch
+  // sums every rank's input copy in rank order (the real switch's order is
+  // its own; the model checks the protocol, not the switch arithmetic).
+  const Config& c = w.cfg;
+  const int P = c.P;
+  constexpr int S = kNvlsSlots;
+  BlockPlan pl = makeBlockPlan(count, c.nvlsChannels, c.nvlsTileElems, c.minChunk, c.vec);
+  const std::vector<float>& x = (*j.x)[(size_t)r];
+  std::vector<float>& y = (*j.y)[(size_t)r];
+  for (int ch = 0; ch < pl.channels; ++ch) {
+    uint64_t& seq = w.counters[(size_t)r][kCounterNvls * kMaxChannels + ch];
+    const uint64_t seq0 = seq;
+    const uint64_t ntiles = channelTiles(pl.numTiles, pl.channels, ch);
+    auto spanOf = [&](uint64_t t) { return blockTileSpan(pl, (uint64_t)ch + t * pl.channels); };
+    auto slotOf = [&](uint64_t t) { return (int)((seq0 + t) % S); };
+    auto usesOf = [&](uint64_t t) { return (seq0 + t) / S + 1; };
+    std::atomic<uint64_t> copiedOut{0};
+    std::atomic<int> fail{0};
+    auto copyIn = [&] {
+      for (uint64_t t = 0; t < ntiles && !fail.load(); ++t) {
+        if (t >= (uint64_t)S) {
+          auto start = std::chrono::steady_clock::now();
+          while (copiedOut.load(std::memory_order_acquire) < t - S + 1) {
+            if (fail.load() || w.error.load() ||
+                std::chrono::steady_clock::now() - start > std::chrono::milliseconds(c.timeoutMs)) {
+              fail.store(1);
+              return;
+            }
+            std::this_thread::yield();
+          }
+        }
+        const Span sp = spanOf(t);
+        float* in = w.mcIn(r, ch, slotOf(t));
+        for (uint64_t e = 0; e < sp.count; ++e) in[e] = x[sp.offset + e];
+        w.mcAdd(r, 0, ch, slotOf(t));
+      }
+    };
+    auto sw = [&] {
+      for (uint64_t t = 0; t < ntiles; ++t) {
+        const int s = slotOf(t);
+        if (!w.mcWait(r, 0, ch, s, (uint64_t)P * usesOf(t))) {
+          fail.store(1);
+          return;
+        }
+        const Span sp = spanOf(t);
+        const Span share = blockShare(divUp(sp.count, c.vec), P, r, 1);
+        for (uint64_t e = share.offset * c.vec;
+             e < (share.offset + share.count) * c.vec && e < sp.count; ++e) {
+          float acc = w.mcIn(0, ch, s)[e];
+          for (int q = 1; q < P; ++q) acc = oracle::add(acc, w.mcIn(q, ch, s)[e]);
+          const float v = rnd(j.dtype, oracle::mul(j.alpha, acc));
+          for (int q = 0; q < P; ++q) w.mcOut(q, ch, s)[e] = v;  // multicast store
+        }
+        w.mcAdd(r, 1, ch, s);
+      }
+    };
+    auto copyOut = [&] {
+      for (uint64_t t = 0; t < ntiles; ++t) {
+        const int s = slotOf(t);
+        if (!w.mcWait(r, 1, ch, s, (uint64_t)P * usesOf(t))) {
+          fail.store(1);
+          return;
+        }
+        const Span sp = spanOf(t);
+        const float* out = w.mcOut(r, ch, s);
+        for (uint64_t e = 0; e < sp.count; ++e) y[sp.offset + e] = out[e];
+        copiedOut.store(t + 1, std::memory_order_release);
+      }
+    };
+    std::thread ti(copyIn), ts(sw);
+    copyOut();
+    ti.join();
+    ts.join();
+    if (fail.load()) return false;
+    seq = seq0 + ntiles;
+  }
+  return true;
+}
+
 bool ring(World& w, int r, const Job& j, uint64_t count) {
   const Config& c = w.cfg;
   const int P = c.P;
@@ -359,8 +485,9 @@ bool collective(World& w, Algo a, const Job& j, uint64_t count) {
           (*j.y)[0][e] = rnd(j.dtype, oracle::mul(j.alpha, (*j.x)[0][e]));
         return;
       }
-      bool res = a == kRing ? ring(w, r, j, count)
+      bool res = a == kRing      ? ring(w, r, j, count)
                  : a == kOneShot ? oneShot(w, r, j, count)
+                 : a == kNvls    ? nvls(w, r, j, count)
                                  : twoShot(w, r, j, count);
       ok[(size_t)r] = res ? 1 : 0;
     });
@@ -395,6 +522,14 @@ bool checkOne(World& w, Algo a, int dtype, uint64_t count, bool inPlace, bool av
     ChunkPlan pl = makeChunkPlan(count, P, w.cfg.channels, w.cfg.ringChunkElems, w.cfg.minChunk,
                                  w.cfg.vec);
     oracle::ring(dtype, x, alpha, pl, w.cfg.vec, want);
+  } else if (a == kNvls) {
+    // The switch sums first and the pre-scale applies to the sum.
+    want.resize(count);
+    for (uint64_t e = 0; e < count; ++e) {
+      float acc = x[0][e];
+      for (int k = 1; k < P; ++k) acc = oracle::add(acc, x[(size_t)k][e]);
+      want[e] = rnd(dtype, oracle::mul(alpha, acc));
+    }
   } else {
     oracle::canonical(dtype, x, alpha, want);
   }
@@ -408,10 +543,12 @@ bool checkOne(World& w, Algo a, int dtype, uint64_t count, bool inPlace, bool av
   return true;
 }
 
-const char* algoName(Algo a) { return a == kRing ? "ring" : a == kOneShot ? "oneshot" : "twoshot"; }
+const char* algoName(Algo a) {
+  return a == kRing ? "ring" : a == kOneShot ? "oneshot" : a == kNvls ? "nvls" : "twoshot";
+}
 
 void referenceMatrix() {
-  for (Algo a : {kRing, kOneShot, kTwoShot}) {
+  for (Algo a : {kRing, kOneShot, kTwoShot, kNvls}) {
     bool ok = true;
     for (int P : {1, 2, 3, 4, 7}) {
       Config c;
@@ -421,6 +558,7 @@ void referenceMatrix() {
       c.ringChunkElems = 7;  // tiny chunks force many tiles (as tiny-nccl's test)
       c.tsChunkElems = 7;
       c.osTileElems = 7;
+      c.nvlsTileElems = 7;
       c.vec = 1;
       c.minChunk = 1;
       World w(c);
@@ -440,7 +578,7 @@ void baselineConfig1() {
   c.ringSlots = 8;
   c.ringChunkElems = 16384;  // 64 KiB of fp32 per slot
   c.channels = 4;
-  for (Algo a : {kRing, kTwoShot, kOneShot}) {
+  for (Algo a : {kRing, kTwoShot, kOneShot, kNvls}) {
     for (int t : {oracle::kF32, oracle::kBF16}) {
       World w(c);
       bool ok = true;
@@ -463,12 +601,13 @@ void sequenceContinuity() {
   c.ringChunkElems = 64;
   c.tsChunkElems = 64;
   c.osTileElems = 64;
+  c.nvlsTileElems = 64;
   World w(c);
   bool ok = true;
   uint64_t seed = 5;
   // 200 collectives of varying size and algorithm on the same mailboxes.
   for (int i = 0; i < 200 && ok; ++i) {
-    Algo a = (Algo)(1 + i % 3);
+    Algo a = (Algo)(1 + i % 4);
     uint64_t n = (uint64_t)((i * 37) % 900);
     ok = checkOne(w, a, i % 2 ? oracle::kBF16 : oracle::kF32, n, i % 5 == 0, i % 7 == 0, seed++);
   }
@@ -493,7 +632,7 @@ void ticketReplay() {
 }
 
 void faultInjection() {
-  for (Algo a : {kRing, kOneShot, kTwoShot}) {
+  for (Algo a : {kRing, kOneShot, kTwoShot, kNvls}) {
     Config c;
     c.P = 4;
     c.timeoutMs = 200;
