@@ -93,6 +93,12 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
   }
 }
 
+// One warp per row. Every load of a row (gy, x_out, the residual gradient)
+// is issued before any of it is used; the per-column dw / db accumulators of
+// each warp live in shared memory (one row of C floats per warp and
+// quantity), which leaves the registers to the loads in flight. Summation
+// order per column: the rows of each warp in row order, then the 8 warps in
+// warp order (here), then the CTAs in order (reducePartials).
 template <int K>
 __global__ void __launch_bounds__(kWarpsPerBlock * 32, 2)
     lnBwdKernel(const uint16_t* __restrict__ gy, const float* __restrict__ gres,
@@ -100,16 +106,20 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, 2)
                 const float* __restrict__ mean, const float* __restrict__ rstd,
                 float* __restrict__ dx, uint16_t* __restrict__ dxb, float* __restrict__ partial,
                 int rows, int C) {
-  __shared__ float sAcc[kWarpsPerBlock][128 * K];
+  extern __shared__ __align__(16) float sAcc[];  // [dw | db][warp][C]
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int C4 = C >> 2;
   const float invC = 1.0f / (float)C;
-  float4 dwAcc[K], dbAcc[K];
+  float4* myDw = reinterpret_cast<float4*>(sAcc + (size_t)warp * C);
+  float4* myDb = reinterpret_cast<float4*>(sAcc + (size_t)(kWarpsPerBlock + warp) * C);
 #pragma unroll
   for (int k = 0; k < K; ++k) {
-    dwAcc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-    dbAcc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int i = lane + 32 * k;
+    if (i < C4) {
+      myDw[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      myDb[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
   }
   const float4* w4 = reinterpret_cast<const float4*>(w);
   const int stride = gridDim.x * kWarpsPerBlock;
@@ -118,32 +128,45 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, 2)
     const float mu = mean[row], rs = rstd[row];
     const uint2* gr = reinterpret_cast<const uint2*>(gy + base);
     const float4* xr = reinterpret_cast<const float4*>(xo + base);
+    const float4* rr = gres ? reinterpret_cast<const float4*>(gres + base) : nullptr;
+    uint2 graw[K];
+    float4 xv[K], res[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const int i = lane + 32 * k;
+      if (i < C4) {
+        graw[k] = __ldcs(gr + i);
+        xv[k] = __ldcs(xr + i);
+        res[k] = rr ? __ldcs(rr + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
     float4 g[K], xh[K];
     float s1 = 0.f, s2 = 0.f;
 #pragma unroll
     for (int k = 0; k < K; ++k) {
       const int i = lane + 32 * k;
       if (i < C4) {
-        g[k] = bf4(gr[i]);
-        const float4 xv = xr[i];
-        xh[k] = make_float4((xv.x - mu) * rs, (xv.y - mu) * rs, (xv.z - mu) * rs,
-                            (xv.w - mu) * rs);
+        g[k] = bf4(graw[k]);
+        xh[k] = make_float4((xv[k].x - mu) * rs, (xv[k].y - mu) * rs, (xv[k].z - mu) * rs,
+                            (xv[k].w - mu) * rs);
         const float4 ww = w4[i];
         const float4 gw = make_float4(g[k].x * ww.x, g[k].y * ww.y, g[k].z * ww.z, g[k].w * ww.w);
         s1 += (gw.x + gw.y) + (gw.z + gw.w);
         s2 += (gw.x * xh[k].x + gw.y * xh[k].y) + (gw.z * xh[k].z + gw.w * xh[k].w);
-        dwAcc[k].x += g[k].x * xh[k].x;
-        dwAcc[k].y += g[k].y * xh[k].y;
-        dwAcc[k].z += g[k].z * xh[k].z;
-        dwAcc[k].w += g[k].w * xh[k].w;
-        dbAcc[k].x += g[k].x;
-        dbAcc[k].y += g[k].y;
-        dbAcc[k].z += g[k].z;
-        dbAcc[k].w += g[k].w;
+        float4 a = myDw[i], d = myDb[i];
+        a.x += g[k].x * xh[k].x;
+        a.y += g[k].y * xh[k].y;
+        a.z += g[k].z * xh[k].z;
+        a.w += g[k].w * xh[k].w;
+        d.x += g[k].x;
+        d.y += g[k].y;
+        d.z += g[k].z;
+        d.w += g[k].w;
+        myDw[i] = a;
+        myDb[i] = d;
       }
     }
     const float m1 = warpSum(s1) * invC, m2 = warpSum(s2) * invC;
-    const float4* rr = gres ? reinterpret_cast<const float4*>(gres + base) : nullptr;
     float4* dr = reinterpret_cast<float4*>(dx + base);
     uint2* dbr = dxb ? reinterpret_cast<uint2*>(dxb + base) : nullptr;
 #pragma unroll
@@ -152,39 +175,24 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, 2)
       if (i < C4) {
         const float4 ww = w4[i];
         float4 o;
-        o.x = rs * (g[k].x * ww.x - m1 - xh[k].x * m2);
-        o.y = rs * (g[k].y * ww.y - m1 - xh[k].y * m2);
-        o.z = rs * (g[k].z * ww.z - m1 - xh[k].z * m2);
-        o.w = rs * (g[k].w * ww.w - m1 - xh[k].w * m2);
-        if (rr) {
-          const float4 r = rr[i];
-          o.x += r.x;
-          o.y += r.y;
-          o.z += r.z;
-          o.w += r.w;
-        }
+        o.x = rs * (g[k].x * ww.x - m1 - xh[k].x * m2) + res[k].x;
+        o.y = rs * (g[k].y * ww.y - m1 - xh[k].y * m2) + res[k].y;
+        o.z = rs * (g[k].z * ww.z - m1 - xh[k].z * m2) + res[k].z;
+        o.w = rs * (g[k].w * ww.w - m1 - xh[k].w * m2) + res[k].w;
         dr[i] = o;
         if (dbr) dbr[i] = tobf4(o);
       }
     }
   }
-  // Combine the warps of this CTA, then write one partial row: dw first,
-  // then db, reusing one shared buffer.
+  // Combine the warps of this CTA into one partial row of [dw | db].
+  __syncthreads();
+  for (int c = threadIdx.x; c < 2 * C; c += blockDim.x) {
+    const int q = c / C, col = c - q * C;
+    const float* src = sAcc + (size_t)q * kWarpsPerBlock * C + col;
+    float a = 0.f;
 #pragma unroll
-  for (int pass = 0; pass < 2; ++pass) {
-#pragma unroll
-    for (int k = 0; k < K; ++k) {
-      const int i = lane + 32 * k;
-      if (i < C4) reinterpret_cast<float4*>(sAcc[warp])[i] = pass == 0 ? dwAcc[k] : dbAcc[k];
-    }
-    __syncthreads();
-    for (int c = threadIdx.x; c < C; c += blockDim.x) {
-      float a = 0.f;
-#pragma unroll
-      for (int wv = 0; wv < kWarpsPerBlock; ++wv) a += sAcc[wv][c];
-      partial[(size_t)blockIdx.x * 2 * C + (size_t)pass * C + c] = a;
-    }
-    __syncthreads();
+    for (int wv = 0; wv < kWarpsPerBlock; ++wv) a += src[(size_t)wv * C];
+    partial[(size_t)blockIdx.x * 2 * C + c] = a;
   }
 }
 
@@ -227,8 +235,12 @@ cudaError_t bwdK(const uint16_t* gy, const float* gres, const float* xo, const f
                  int rows, int C, cudaStream_t st) {
   int blocks = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock;
   if (blocks > kPartialRows) blocks = kPartialRows;
-  lnBwdKernel<K><<<blocks, kWarpsPerBlock * 32, 0, st>>>(gy, gres, xo, w, m, r, dx, dxb, partial,
-                                                        rows, C);
+  const int smem = 2 * kWarpsPerBlock * C * (int)sizeof(float);  // dw and db rows per warp
+  cudaError_t e = cudaFuncSetAttribute(lnBwdKernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       smem);
+  if (e != cudaSuccess) return e;
+  lnBwdKernel<K><<<blocks, kWarpsPerBlock * 32, smem, st>>>(gy, gres, xo, w, m, r, dx, dxb,
+                                                           partial, rows, C);
   return cudaGetLastError();
 }
 

@@ -189,12 +189,12 @@ void deriveThresholds(tncclComm* comm) {
   // Defaults from the measured sweeps on 2, 4 and 8 B200 (benchmarks/
   // allreduce_sweep.py, tune_allreduce.py): one-shot (64 channels) moves
   // (P-1) x the message per link direction but needs one flag round trip
-  // instead of two, so it wins up to 2 MiB on 2 GPUs (112 vs 104 GB/s),
-  // up to 1 MiB on 4 and up to 512 KiB on 8; the warp-specialised two-shot
-  // above (it also beats the NVLS kernel at every size measured, so AUTO
-  // picks NVLS only when TNCCL_NVLS_MIN_BYTES asks for it).
-  // TNCCL_ONESHOT_MAX_BYTES / TNCCL_NVLS_MIN_BYTES override them.
-  uint64_t os = P <= 2 ? (2u << 20) : P <= 4 ? (1u << 20) : (512u << 10);
+  // instead of two, so it wins up to 2 MiB on 2 GPUs (112 vs 104 GB/s) and
+  // up to 1 MiB on 4 and 8 (61 vs 56 GB/s at 1 MiB on 8); the
+  // warp-specialised two-shot above (it also beats the NVLS kernel at every
+  // size measured, so AUTO picks NVLS only when TNCCL_NVLS_MIN_BYTES asks
+  // for it). TNCCL_ONESHOT_MAX_BYTES / TNCCL_NVLS_MIN_BYTES override them.
+  uint64_t os = P <= 2 ? (2u << 20) : (1u << 20);
   uint64_t nv = ~0ull;
   if (comm->cfg.oneShotMaxBytes > 0) os = (uint64_t)comm->cfg.oneShotMaxBytes;
   if (comm->cfg.nvlsMinBytes > 0) nv = (uint64_t)comm->cfg.nvlsMinBytes;

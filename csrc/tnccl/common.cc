@@ -112,7 +112,12 @@ Config loadConfig() {
   c.nvlsStages = clampInt(envInt("TNCCL_NVLS_STAGES", 2), 1, 8);
   c.nvlsStage = clampInt(envInt("TNCCL_NVLS_STAGE", 48 << 10), 4 << 10, 96 << 10) / 256 * 256;
   while (c.nvlsStages > 1 && (int64_t)c.nvlsStages * c.nvlsStage > kSmem) --c.nvlsStages;
-  c.stageMinBytes = clampInt(envInt("TNCCL_STAGE_MIN_BYTES", -1), -1, 1 << 30);  // -1: by nranks
+  // TMA staging of the two-shot push / reduce and NVLS copy-in loads is
+  // opt-in (TNCCL_STAGE_MIN_BYTES): the register path was as fast or faster
+  // at every size measured, on 4 x B200 (648 vs 631 GB/s at 256 MiB) and on
+  // 8 (618 vs 367 at 256 MiB, 654 vs 484 at 1 GiB): a bulk-copy stage has a
+  // fixed cost that short per-peer pieces do not amortise.
+  c.stageMinBytes = clampInt(envInt("TNCCL_STAGE_MIN_BYTES", 1 << 30), 0, 1 << 30);
   return c;
 }
 
@@ -169,11 +174,6 @@ void adaptConfig(Config& c, int nranks) {
     chunk = chunk < (32 << 10) ? (32 << 10) : chunk > (256 << 10) ? (256 << 10) : chunk;
     c.tsChunkBytes = chunk / 16 * 16;
   }
-  // TMA staging of the two-shot push / reduce copies: on 4 x B200 the
-  // register path was as fast or faster at every size (648 vs 631 GB/s at
-  // 256 MiB, 128 channels), so up to 4 ranks nothing is staged; with more
-  // ranks the reduce reads more sources than registers keep in flight.
-  if (c.stageMinBytes < 0) c.stageMinBytes = nranks <= 4 ? (1 << 30) : (16 << 10);
 }
 
 }  // namespace tnccl

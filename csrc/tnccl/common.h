@@ -60,7 +60,7 @@ struct Config {
   int tsRedStage;            // TNCCL_TWOSHOT_REDUCE_STAGE bytes (default 64 KiB)
   int nvlsStages;            // TNCCL_NVLS_STAGES (1..8, default 2)
   int nvlsStage;             // TNCCL_NVLS_STAGE bytes (default 48 KiB)
-  int stageMinBytes;         // TNCCL_STAGE_MIN_BYTES (default by nranks)
+  int stageMinBytes;         // TNCCL_STAGE_MIN_BYTES (default 1 GiB: staging off)
 };
 
 // Parses "a,b" (eighths, each 1..6, a + b <= 7) into a | b << 4.

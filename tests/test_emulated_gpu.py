@@ -115,12 +115,12 @@ def test_emulated_in_place_and_sequence(emulators):
     assert emu.async_error() == 0
 
 
-@pytest.mark.parametrize("P", [2, 4])
+@pytest.mark.parametrize("P", [2, 4, 8])
 @pytest.mark.parametrize("stage_min", [0, 1 << 30])
 def test_emulated_twoshot_staging_paths(built, P, stage_min):
     """Two-shot with every copy staged through shared memory by TMA
-    (TNCCL_STAGE_MIN_BYTES=0) and with none staged, bit for bit against the
-    oracle, whichever is the default for this rank count."""
+    (TNCCL_STAGE_MIN_BYTES=0, opt-in) and with none staged (the default),
+    bit for bit against the oracle."""
     import tiny_nccl_b200 as tn
     old = os.environ.get("TNCCL_STAGE_MIN_BYTES")
     os.environ["TNCCL_STAGE_MIN_BYTES"] = str(stage_min)
