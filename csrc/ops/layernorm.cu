@@ -236,9 +236,18 @@ cudaError_t bwdK(const uint16_t* gy, const float* gres, const float* xo, const f
   int blocks = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock;
   if (blocks > kPartialRows) blocks = kPartialRows;
   const int smem = 2 * kWarpsPerBlock * C * (int)sizeof(float);  // dw and db rows per warp
-  cudaError_t e = cudaFuncSetAttribute(lnBwdKernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       smem);
+  // Opt in to the shared memory once per device (bit d of `done`).
+  static std::atomic<uint64_t> done{0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
+  const uint64_t bit = dev < 64 ? (1ull << dev) : 0;
+  if (!(done.load(std::memory_order_acquire) & bit)) {
+    e = cudaFuncSetAttribute(lnBwdKernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             2 * kWarpsPerBlock * 128 * K * (int)sizeof(float));
+    if (e != cudaSuccess) return e;
+    done.fetch_or(bit, std::memory_order_acq_rel);
+  }
   lnBwdKernel<K><<<blocks, kWarpsPerBlock * 32, smem, st>>>(gy, gres, xo, w, m, r, dx, dxb,
                                                            partial, rows, C);
   return cudaGetLastError();
