@@ -14,12 +14,16 @@
 //            reduces all P contributions locally in rank order 0..P-1.
 //   two-shot reduce-scatter by pushing chunk j to rank j, which reduces in
 //            rank order 0..P-1, then all-gather by pushing the reduced chunk
-//            to every peer. Each rank both sends to and receives from every
+//            to every peer; three warp-specialised teams (push, reduce,
+//            gather) per CTA run the phases of successive tiles
+//            concurrently. Each rank both sends to and receives from every
 //            peer in both phases, which doubles as flow control: no credit
 //            words are needed (see the slot-reuse argument below).
-//   NVLS     copy the tile into the multicast-bound buffer, barrier, reduce
-//            this rank's share in the NVSwitch (multimem.ld_reduce), broadcast
-//            it with multimem.st, barrier, copy the tile out.
+//   NVLS     teams copy the tile into the multicast-bound buffer, reduce this
+//            rank's share in the NVSwitch (multimem.ld_reduce) and broadcast
+//            it with multimem.st, and copy the result out; the barriers
+//            between them are per-slot counters that every rank increments
+//            on every GPU with one multimem.red.
 //
 // Every wait is bounded (device.cuh); a CTA whose wait fails stops, leaves
 // its sequence number untouched and the host sees the recorded error.

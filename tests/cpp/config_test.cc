@@ -1,0 +1,213 @@
+// config_test.cc - host-side configuration and partition invariants, no GPU.
+//
+//  * loadConfig: defaults, environment overrides, clamping of out-of-range
+//    values, the team-split parser and its fallback on malformed input;
+//  * adaptConfig: the two-shot chunk per rank count (512 KiB tile, chunk
+//    clamped to 32..256 KiB) and that an explicit TNCCL_TWOSHOT_CHUNK_BYTES
+//    wins;
+//  * configHash: equal for equal protocol fields, different when a field that
+//    changes the mailbox layout differs, unchanged by rank-local knobs;
+//  * makeLayout: areas and flag groups do not overlap, the canary lines sit
+//    between them, alignment, and the total size;
+//  * makeChunkPlan / chunkSpan and makeBlockPlan / blockTileSpan / blockShare:
+//    every element is covered exactly once, chunk boundaries fall on vector
+//    boundaries, for many counts, rank counts and channel counts.
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <algorithm>
+#include <string>
+#include <utility>
+#include <vector>
+
+#include "common.h"
+#include "protocol.h"
+
+using namespace tnccl;
+
+namespace {
+
+int gFailed = 0;
+void check(bool ok, const char* what) {
+  printf("%-60s %s\n", what, ok ? "ok" : "FAILED");
+  if (!ok) ++gFailed;
+}
+
+void clearEnv() {
+  for (const char* v :
+       {"TNCCL_NCHANNELS", "TNCCL_ONESHOT_CHANNELS", "TNCCL_TWOSHOT_CHUNK_BYTES",
+        "TNCCL_NTHREADS", "TNCCL_TWOSHOT_SPLIT", "TNCCL_NVLS_SPLIT", "TNCCL_TWOSHOT_STAGES",
+        "TNCCL_TWOSHOT_PUSH_STAGE", "TNCCL_TWOSHOT_REDUCE_STAGE", "TNCCL_STAGE_MIN_BYTES",
+        "TNCCL_ALGO", "TNCCL_TIMEOUT_MS", "TNCCL_ACQUIRE_LOAD", "TNCCL_NVLS_STAGE"})
+    unsetenv(v);
+}
+
+void defaultsAndOverrides() {
+  clearEnv();
+  setenv("TNCCL_DEBUG", "NONE", 1);  // the malformed-value cases below warn
+  Config c = loadConfig();
+  check(c.channels == 128 && c.osChannels == 64 && c.threads == 512, "defaults: channels, threads");
+  check(c.tsSplit == (2 | (4 << 4)) && c.nvlsSplit == (1 | (4 << 4)), "defaults: team splits");
+  check(c.stageMinBytes == (1 << 30) && c.acquireMode == 1, "defaults: staging off, ld.acquire");
+  check(c.forcedAlgo == TNCCL_ALGO_AUTO && c.timeoutMs == 30000, "defaults: algorithm, timeout");
+
+  setenv("TNCCL_NCHANNELS", "100000", 1);
+  setenv("TNCCL_NTHREADS", "40", 1);
+  setenv("TNCCL_TWOSHOT_SPLIT", "3,2", 1);
+  setenv("TNCCL_ALGO", "twoshot", 1);
+  setenv("TNCCL_TIMEOUT_MS", "0", 1);
+  c = loadConfig();
+  check(c.channels == kMaxChannels, "TNCCL_NCHANNELS clamped to kMaxChannels");
+  check(c.threads == 128, "TNCCL_NTHREADS clamped to 128 (three teams need 4 warps)");
+  check(c.tsSplit == (3 | (2 << 4)), "TNCCL_TWOSHOT_SPLIT=3,2 parsed");
+  check(c.forcedAlgo == TNCCL_ALGO_TWOSHOT && c.timeoutMs == 1, "algorithm and timeout floor");
+
+  setenv("TNCCL_TWOSHOT_SPLIT", "6,6", 1);  // 12 eighths: rejected
+  setenv("TNCCL_NVLS_SPLIT", "garbage", 1);
+  c = loadConfig();
+  check(c.tsSplit == (2 | (4 << 4)) && c.nvlsSplit == (1 | (4 << 4)),
+        "malformed splits fall back to the defaults");
+  check(parseSplit("", 7) == 7 && parseSplit("1,1", 0) == (1 | (1 << 4)) &&
+            parseSplit("0,3", 9) == 9 && parseSplit("4,4", 9) == 9,
+        "parseSplit bounds");
+
+  setenv("TNCCL_TWOSHOT_STAGES", "8", 1);
+  setenv("TNCCL_TWOSHOT_PUSH_STAGE", "98304", 1);
+  setenv("TNCCL_TWOSHOT_REDUCE_STAGE", "98304", 1);
+  c = loadConfig();
+  check((int64_t)c.tsStages * (c.tsPushStage + c.tsRedStage) <= 227 * 1024 - 256,
+        "staging rings fit 227 KiB of shared memory");
+  clearEnv();
+}
+
+void adaptChunks() {
+  clearEnv();
+  bool ok = true;
+  for (int P = 1; P <= 16; ++P) {
+    Config c = loadConfig();
+    adaptConfig(c, P);
+    int64_t want = (512 << 10) / P;
+    want = std::min<int64_t>(std::max<int64_t>(want, 32 << 10), 256 << 10) / 16 * 16;
+    ok = ok && c.tsChunkBytes == want;
+  }
+  check(ok, "two-shot chunk = 512 KiB / P clamped to 32..256 KiB");
+  setenv("TNCCL_TWOSHOT_CHUNK_BYTES", "65536", 1);
+  Config c = loadConfig();
+  adaptConfig(c, 2);
+  check(c.tsChunkBytes == 65536, "TNCCL_TWOSHOT_CHUNK_BYTES overrides the rank-count rule");
+  clearEnv();
+}
+
+void hashes() {
+  clearEnv();
+  Config a = loadConfig(), b = loadConfig();
+  check(configHash(a) == configHash(b), "configHash equal for equal configs");
+  b.channels = a.channels - 1;
+  check(configHash(a) != configHash(b), "configHash differs when the layout differs");
+  b = a;
+  b.threads = 256;
+  b.tsSplit = 3 | (3 << 4);
+  b.timeoutMs = 5;
+  check(configHash(a) == configHash(b), "configHash ignores rank-local knobs");
+}
+
+void layouts() {
+  bool ok = true;
+  for (int P : {2, 3, 4, 8, 16}) {
+    LayoutConfig lc{};
+    lc.nranks = P;
+    lc.channels = 96;
+    lc.osChannels = 64;
+    lc.ringSlots = 4;
+    lc.ringChunkBytes = 256 << 10;
+    lc.tsChunkBytes = (512 << 10) / P;
+    lc.osSlots = 2;
+    lc.osTileBytes = 32 << 10;
+    const MailboxLayout L = makeLayout(lc);
+    const uint64_t C = 96;
+    std::vector<std::pair<uint64_t, uint64_t>> areas = {
+        {L.ringDataOff, C * 4 * lc.ringChunkBytes},
+        {L.tsRsDataOff, C * kTwoShotSlots * P * lc.tsChunkBytes},
+        {L.tsAgDataOff, C * kTwoShotSlots * P * lc.tsChunkBytes},
+        {L.osDataOff, 64ull * 2 * P * lc.osTileBytes},
+        {L.ringReadyOff, C * 4 * 8},
+        {L.ringCreditOff, C * 4 * 8},
+        {L.tsRsFlagOff, C * kTwoShotSlots * P * 8},
+        {L.tsAgFlagOff, C * kTwoShotSlots * P * 8},
+        {L.osFlagOff, 64ull * 2 * P * 8},
+        {L.osAckOff, 64ull * 2 * P * 8},
+    };
+    for (int k = 0; k < kNumCanaries; ++k) areas.push_back({L.canaryOff[k], kCanaryBytes});
+    std::sort(areas.begin(), areas.end());
+    for (size_t i = 0; i + 1 < areas.size(); ++i)
+      ok = ok && areas[i].first + areas[i].second <= areas[i + 1].first;
+    ok = ok && areas.back().first + areas.back().second <= L.totalBytes;
+    ok = ok && L.totalBytes % 4096 == 0 && L.tsRsDataOff % 4096 == 0 && L.osDataOff % 4096 == 0;
+    // The canary after an area starts exactly where the area ends.
+    ok = ok && L.canaryOff[0] == L.ringDataOff + C * 4 * lc.ringChunkBytes;
+    ok = ok && L.canaryOff[1] == L.tsRsDataOff + C * kTwoShotSlots * P * lc.tsChunkBytes;
+    ok = ok && L.canaryOff[2] == L.tsAgDataOff + C * kTwoShotSlots * P * lc.tsChunkBytes;
+  }
+  check(ok, "mailbox areas, flags and canaries do not overlap");
+  const uint64_t tb = 512 << 10;
+  check(nvlsCounterAt(tb, 64, 1, 127, kNvlsSlots - 1) + 8 <= nvlsRegionBytes(tb, 64) &&
+            nvlsCounterAt(tb, 64, 0, 0, 0) == nvlsDataBytes(tb, 64),
+        "NVLS counters follow the data blocks inside the region");
+}
+
+void plans() {
+  bool ok = true;
+  uint64_t seed = 12345;
+  auto rnd = [&seed]() {
+    seed = seed * 6364136223846793005ull + 1442695040888963407ull;
+    return seed >> 33;
+  };
+  for (int it = 0; it < 400 && ok; ++it) {
+    const uint64_t V = (it % 2) ? 4 : 8;
+    const uint64_t count = (it < 20) ? (uint64_t)it : rnd() % 3000000;
+    const int P = 2 + (int)(rnd() % 15);
+    const int channels = 1 + (int)(rnd() % 128);
+    const uint64_t maxChunk = 16 * (1 + rnd() % 4096);
+    ChunkPlan cp = makeChunkPlan(count, P, channels, maxChunk, 16, V);
+    std::vector<unsigned char> seen(count, 0);
+    for (uint64_t t = 0; t < cp.numTiles; ++t)
+      for (int j = 0; j < P; ++j) {
+        const Span s = chunkSpan(cp, t, j, V);
+        ok = ok && (s.count == 0 || s.offset % V == 0) && s.offset + s.count <= count;
+        for (uint64_t e = s.offset; e < s.offset + s.count && ok; ++e) ok = ++seen[e] == 1;
+      }
+    for (uint64_t e = 0; e < count && ok; ++e) ok = seen[e] == 1;
+    ok = ok && cp.channels >= 1 && cp.channels <= channels;
+
+    BlockPlan bp = makeBlockPlan(count, channels, maxChunk, 16, V);
+    std::fill(seen.begin(), seen.end(), 0);
+    for (uint64_t t = 0; t < bp.numTiles; ++t) {
+      const Span s = blockTileSpan(bp, t);
+      for (uint64_t e = s.offset; e < s.offset + s.count && ok; ++e) ok = ++seen[e] == 1;
+      // NVLS shares: every vector of the tile belongs to exactly one rank.
+      const uint64_t nv = divUp(s.count, V);
+      uint64_t covered = 0;
+      for (int r = 0; r < P; ++r) {
+        const Span sh = blockShare(nv, P, r, 1);
+        ok = ok && sh.offset == covered;
+        covered += sh.count;
+      }
+      ok = ok && covered == nv;
+    }
+    for (uint64_t e = 0; e < count && ok; ++e) ok = seen[e] == 1;
+  }
+  check(ok, "chunk / block / share plans cover every element once");
+}
+
+}  // namespace
+
+int main() {
+  defaultsAndOverrides();
+  adaptChunks();
+  hashes();
+  layouts();
+  plans();
+  printf("config_test: %s\n", gFailed ? "FAIL" : "PASS");
+  return gFailed ? 1 : 0;
+}

@@ -61,6 +61,12 @@ def test_rank_model(built):
         assert line in r.stdout
 
 
+def test_config_and_partitions(built):
+    r = run([os.path.join(ROOT, "build", "bin", "config_test")], timeout=120)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "config_test: PASS" in r.stdout
+
+
 @pytest.mark.skipif(__import__("conftest").gpu_count() > 0, reason="CPU-only behaviour")
 def test_init_without_gpu_fails_cleanly(built):
     import tiny_nccl_b200 as tn

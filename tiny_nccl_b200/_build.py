@@ -159,6 +159,8 @@ PROGRAMS = {
     "allreduce_gpu_test": ROOT / "tests" / "cpp" / "allreduce_gpu_test.cc",
     "bootstrap_test": ROOT / "tests" / "cpp" / "bootstrap_test.cc",
     "rank_model_test": ROOT / "tests" / "cpp" / "rank_model_test.cc",
+    # host configuration / partition checks, built with the library's config code
+    "config_test": (ROOT / "tests" / "cpp" / "config_test.cc", TNCCL_SRC / "common.cc"),
 }
 
 
@@ -167,20 +169,24 @@ def build_programs() -> list[Path]:
     lib = build_tnccl()
     BIN.mkdir(parents=True, exist_ok=True)
     outs = []
-    for name, src in PROGRAMS.items():
-        if not src.exists():
+    for name, entry in PROGRAMS.items():
+        srcs = list(entry) if isinstance(entry, tuple) else [entry]
+        if not srcs[0].exists():
             continue
         out = BIN / name
         stamp = BIN / (name + ".stamp")
-        deps = [src] + _headers(ROOT / "tests" / "cpp") + _headers(TNCCL_SRC) + \
+        deps = srcs + _headers(ROOT / "tests" / "cpp") + _headers(TNCCL_SRC) + \
             [ROOT / "include" / "tnccl.h"]
         key = _hash(deps, "prog " + " ".join(CXXFLAGS) + str(lib.stat().st_size))
         if not (out.exists() and stamp.exists() and stamp.read_text() == key):
-            obj = OBJ / "bin" / (name + ".o")
-            obj.parent.mkdir(parents=True, exist_ok=True)
-            _run(["g++", *CXXFLAGS, "-O2", *INCLUDES, f"-I{ROOT / 'tests' / 'cpp'}", "-c",
-                  str(src), "-o", str(obj)])
-            _run([NVCC, *ARCH, "-o", str(out), str(obj), f"-L{LIB}", "-ltnccl",
+            objs = []
+            for k, src in enumerate(srcs):
+                obj = OBJ / "bin" / f"{name}.{k}.o"
+                obj.parent.mkdir(parents=True, exist_ok=True)
+                _run(["g++", *CXXFLAGS, "-O2", *INCLUDES, f"-I{ROOT / 'tests' / 'cpp'}", "-c",
+                      str(src), "-o", str(obj)])
+                objs.append(str(obj))
+            _run([NVCC, *ARCH, "-o", str(out), *objs, f"-L{LIB}", "-ltnccl",
                   "-Xlinker", f"-rpath,{LIB}", "-Xlinker", "-rpath,$ORIGIN/../../tiny_nccl_b200/lib",
                   "-lpthread"])
             stamp.write_text(key)
