@@ -10,7 +10,9 @@
 // whether it happened to be bit-exact.
 //
 // "stress" is BASELINE config 2: count = 1,048,576 fp32, 100 iterations with
-// fresh inputs on one bound stream, every iteration checked.
+// fresh inputs on one bound stream, every iteration checked. The other modes
+// end by checking that device memory did not grow across collectives of 4 to
+// 64 MiB and that the mailbox guard lines are intact.
 #include <cuda_runtime_api.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -194,6 +196,36 @@ int runRank(int rank, int P, const std::string& mode, const std::vector<tncclAlg
     // AUTO across sizes, then count = 0 between non-empty collectives.
     for (size_t n : {(size_t)0, (size_t)4096, (size_t)0, (size_t)3 << 20, (size_t)0})
       if (!hard) hard = !R.run(Case{TNCCL_ALGO_AUTO, 0, n, false, false, 0}, seed++);
+  }
+  if (!hard && mode != "stress") {
+    // Communication memory is constant: no device allocation grows with the
+    // message (the buffers of this test are freed around the measurement),
+    // and the guard lines after every mailbox area are intact.
+    auto dropBuffers = [&R]() {
+      cudaFree(R.dsend);
+      cudaFree(R.drecv);
+      R.dsend = R.drecv = nullptr;
+      R.cap = 0;
+      cudaDeviceSynchronize();
+    };
+    dropBuffers();
+    size_t free0 = 0, free1 = 0, total = 0;
+    cudaMemGetInfo(&free0, &total);
+    for (size_t n : {(size_t)1 << 20, (size_t)4 << 20, (size_t)16 << 20})
+      if (!hard) hard = !R.run(Case{TNCCL_ALGO_AUTO, 0, n, false, false, 0}, seed++);
+    dropBuffers();
+    cudaMemGetInfo(&free1, &total);
+    const long long grew = (long long)free0 - (long long)free1;
+    if (grew > (32ll << 20)) {
+      fprintf(stderr, "rank %d: device memory grew by %lld bytes across collectives\n", rank,
+              grew);
+      hard = true;
+    }
+    int corrupted = 0;
+    if (tncclCommValidate(R.comm, &corrupted) != TNCCL_SUCCESS || corrupted != 0) {
+      fprintf(stderr, "rank %d: %d mailbox guard line(s) overwritten\n", rank, corrupted);
+      hard = true;
+    }
   }
   printf("rank %d: nvls=%d passed=%d failed=%d nvls_inexact=%d hard=%d\n", rank,
          R.info.nvlsEnabled, R.passes, R.failures, R.nvlsInexact, (int)hard);
