@@ -5,7 +5,7 @@ import os
 import pytest
 import torch
 
-from conftest import ROOT, gpu_count, run, torchrun
+from conftest import ROOT, gpu_count, run
 
 pytestmark = pytest.mark.gpu
 
