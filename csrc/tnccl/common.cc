@@ -7,6 +7,7 @@
 #include <strings.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <mutex>
 
 namespace tnccl {
@@ -118,6 +119,7 @@ Config loadConfig() {
   // 8 (618 vs 367 at 256 MiB, 654 vs 484 at 1 GiB): a bulk-copy stage has a
   // fixed cost that short per-peer pieces do not amortise.
   c.stageMinBytes = clampInt(envInt("TNCCL_STAGE_MIN_BYTES", 1 << 30), 0, 1 << 30);
+  c.tuning = loadTuningTable();
   return c;
 }
 
@@ -156,6 +158,12 @@ uint64_t configHash(const Config& c) {
   mix(c.useCuMem);
   mix(c.oneShotMaxBytes);
   mix(c.nvlsMinBytes);
+  // Every rank must pick the same algorithm for a message.
+  for (const TuningEntry& e : c.tuning.entries) {
+    mix(e.nranks);
+    mix((int64_t)e.maxBytes);
+    mix(e.algo);
+  }
   return h;
 }
 
@@ -174,6 +182,70 @@ void adaptConfig(Config& c, int nranks) {
     chunk = chunk < (32 << 10) ? (32 << 10) : chunk > (256 << 10) ? (256 << 10) : chunk;
     c.tsChunkBytes = chunk / 16 * 16;
   }
+}
+
+bool parseTuningTable(const std::string& text, TuningTable* out, std::string* error) {
+  out->entries.clear();
+  size_t pos = 0;
+  int lineNo = 0;
+  while (pos <= text.size()) {
+    size_t end = text.find('\n', pos);
+    if (end == std::string::npos) end = text.size();
+    std::string line = text.substr(pos, end - pos);
+    pos = end + 1;
+    ++lineNo;
+    const size_t hash = line.find('#');
+    if (hash != std::string::npos) line.resize(hash);
+    if (line.find_first_not_of(" \t\r") == std::string::npos) continue;
+    int nranks = 0;
+    unsigned long long maxBytes = 0;
+    char algoName[32] = {0};
+    char extra[2] = {0};
+    if (sscanf(line.c_str(), "%d %llu %31s %1s", &nranks, &maxBytes, algoName, extra) != 3 ||
+        nranks < 1 || nranks > kMaxRanks) {
+      if (error) *error = "line " + std::to_string(lineNo) + ": want <nranks> <max_bytes> <algo>";
+      return false;
+    }
+    const int algo = parseAlgo(algoName);
+    if (algo <= TNCCL_ALGO_AUTO) {
+      if (error) *error = "line " + std::to_string(lineNo) + ": unknown algorithm " + algoName;
+      return false;
+    }
+    out->entries.push_back(TuningEntry{nranks, (uint64_t)maxBytes, algo});
+  }
+  std::sort(out->entries.begin(), out->entries.end(),
+            [](const TuningEntry& a, const TuningEntry& b) {
+              return a.nranks != b.nranks ? a.nranks < b.nranks : a.maxBytes < b.maxBytes;
+            });
+  return true;
+}
+
+TuningTable loadTuningTable() {
+  TuningTable t;
+  const std::string path = envStr("TNCCL_TUNING_FILE", "");
+  if (path.empty()) return t;
+  FILE* f = fopen(path.c_str(), "r");
+  if (f == nullptr) {
+    TN_WARN("TNCCL_TUNING_FILE %s cannot be read; using the built-in thresholds", path.c_str());
+    return t;
+  }
+  std::string text;
+  char buf[4096];
+  size_t n;
+  while ((n = fread(buf, 1, sizeof(buf), f)) > 0) text.append(buf, n);
+  fclose(f);
+  std::string err;
+  if (!parseTuningTable(text, &t, &err)) {
+    TN_WARN("TNCCL_TUNING_FILE %s: %s; using the built-in thresholds", path.c_str(), err.c_str());
+    t.entries.clear();
+  }
+  return t;
+}
+
+int tunedAlgo(const TuningTable& t, int nranks, uint64_t bytes) {
+  for (const TuningEntry& e : t.entries)
+    if (e.nranks == nranks && bytes <= e.maxBytes) return e.algo;
+  return -1;
 }
 
 }  // namespace tnccl

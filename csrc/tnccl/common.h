@@ -8,6 +8,7 @@
 #include <stdlib.h>
 
 #include <string>
+#include <vector>
 
 #include "tnccl.h"
 
@@ -26,6 +27,25 @@ void logf(int level, const char* fmt, ...) __attribute__((format(printf, 2, 3)))
 // the default with a warning.
 int64_t envInt(const char* name, int64_t dflt);
 std::string envStr(const char* name, const char* dflt);
+
+// AUTO tuning table (TNCCL_TUNING_FILE): text lines "<nranks> <max_bytes>
+// <algo>", '#' starts a comment. For a communicator of nranks ranks, a
+// message of b bytes uses the algorithm of the line with the smallest
+// max_bytes >= b among that rank count's lines; sizes above every line keep
+// the built-in rule. benchmarks/make_tuning_table.py writes such a file from
+// a measured sweep.
+struct TuningEntry {
+  int nranks;
+  uint64_t maxBytes;
+  int algo;
+};
+struct TuningTable {
+  std::vector<TuningEntry> entries;  // sorted by (nranks, maxBytes)
+};
+// Parses `text`; false (and *error set) on a malformed line.
+bool parseTuningTable(const std::string& text, TuningTable* out, std::string* error);
+// The table's algorithm for (nranks, bytes), or -1 when no line applies.
+int tunedAlgo(const TuningTable& t, int nranks, uint64_t bytes);
 
 // Tunables read once per communicator. They must be equal on every rank; the
 // bootstrap hello carries their hash and rank 0 rejects a mismatch.
@@ -61,7 +81,12 @@ struct Config {
   int nvlsStages;            // TNCCL_NVLS_STAGES (1..8, default 2)
   int nvlsStage;             // TNCCL_NVLS_STAGE bytes (default 48 KiB)
   int stageMinBytes;         // TNCCL_STAGE_MIN_BYTES (default 1 GiB: staging off)
+  TuningTable tuning;        // TNCCL_TUNING_FILE (empty: built-in AUTO rule)
 };
+
+// Loads TNCCL_TUNING_FILE when set (a missing or malformed file warns and
+// yields an empty table).
+TuningTable loadTuningTable();
 
 // Parses "a,b" (eighths, each 1..6, a + b <= 7) into a | b << 4.
 int parseSplit(const std::string& s, int dflt);
@@ -73,5 +98,7 @@ void adaptConfig(Config& c, int nranks);
 uint64_t configHash(const Config& c);
 
 int parseAlgo(const std::string& s);
+
+
 
 }  // namespace tnccl

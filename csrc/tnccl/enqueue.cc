@@ -55,6 +55,8 @@ tncclAlgo_t selectAlgo(const tncclComm* comm, uint64_t bytes) {
     if (comm->cfg.forcedAlgo == TNCCL_ALGO_NVLS && !comm->nvls.enabled) return TNCCL_ALGO_TWOSHOT;
     return (tncclAlgo_t)comm->cfg.forcedAlgo;
   }
+  const int tuned = tunedAlgo(comm->cfg.tuning, comm->nranks, bytes);
+  if (tuned > 0 && (tuned != TNCCL_ALGO_NVLS || comm->nvls.enabled)) return (tncclAlgo_t)tuned;
   if (bytes <= comm->oneShotMaxBytes) return TNCCL_ALGO_ONESHOT;
   if (comm->nvls.enabled && bytes >= comm->nvlsMinBytes) return TNCCL_ALGO_NVLS;
   return TNCCL_ALGO_TWOSHOT;

@@ -7,6 +7,8 @@
 //    wins;
 //  * configHash: equal for equal protocol fields, different when a field that
 //    changes the mailbox layout differs, unchanged by rank-local knobs;
+//  * TNCCL_TUNING_FILE: parsing, rejection of malformed lines, lookup, and
+//    that the table is part of the configuration hash;
 //  * makeLayout: areas and flag groups do not overlap, the canary lines sit
 //    between them, alignment, and the total size;
 //  * makeChunkPlan / chunkSpan and makeBlockPlan / blockTileSpan / blockShare:
@@ -112,6 +114,46 @@ void hashes() {
   check(configHash(a) == configHash(b), "configHash ignores rank-local knobs");
 }
 
+void tuningTables() {
+  TuningTable t;
+  std::string err;
+  const char* text =
+      "# measured on 8 x B200\n"
+      "8 1048576 oneshot\n"
+      "8 268435456 twoshot   # mid sizes\n"
+      "\n"
+      "2 2097152 oneshot\n"
+      "8 524288 oneshot\n";
+  check(parseTuningTable(text, &t, &err) && t.entries.size() == 4, "tuning table parses");
+  check(tunedAlgo(t, 8, 1) == TNCCL_ALGO_ONESHOT && tunedAlgo(t, 8, 1048577) == TNCCL_ALGO_TWOSHOT &&
+            tunedAlgo(t, 8, 268435457) == -1 && tunedAlgo(t, 4, 100) == -1 &&
+            tunedAlgo(t, 2, 2097152) == TNCCL_ALGO_ONESHOT,
+        "tuning lookup: smallest max_bytes >= size, per rank count");
+  check(!parseTuningTable("8 1024\n", &t, &err) && err.find("line 1") != std::string::npos,
+        "tuning: missing field rejected with its line number");
+  check(!parseTuningTable("4 1024 fastest\n", &t, &err) && !parseTuningTable("0 1 ring\n", &t, &err) &&
+            !parseTuningTable("4 1024 auto\n", &t, &err) &&
+            !parseTuningTable("4 1024 ring extra\n", &t, &err),
+        "tuning: bad algorithm / rank count / trailing field rejected");
+
+  clearEnv();
+  Config a = loadConfig();
+  const std::string path = "/tmp/tnccl_config_test_tuning.txt";
+  FILE* f = fopen(path.c_str(), "w");
+  fputs("2 4096 ring\n", f);
+  fclose(f);
+  setenv("TNCCL_TUNING_FILE", path.c_str(), 1);
+  Config b = loadConfig();
+  check(b.tuning.entries.size() == 1 && tunedAlgo(b.tuning, 2, 4096) == TNCCL_ALGO_RING,
+        "TNCCL_TUNING_FILE loaded");
+  check(configHash(a) != configHash(b), "configHash covers the tuning table");
+  setenv("TNCCL_TUNING_FILE", "/nonexistent/tnccl.txt", 1);
+  Config c = loadConfig();
+  check(c.tuning.entries.empty(), "unreadable tuning file ignored");
+  unsetenv("TNCCL_TUNING_FILE");
+  remove(path.c_str());
+}
+
 void layouts() {
   bool ok = true;
   for (int P : {2, 3, 4, 8, 16}) {
@@ -206,6 +248,7 @@ int main() {
   defaultsAndOverrides();
   adaptChunks();
   hashes();
+  tuningTables();
   layouts();
   plans();
   printf("config_test: %s\n", gFailed ? "FAIL" : "PASS");

@@ -72,3 +72,28 @@ def test_init_without_gpu_fails_cleanly(built):
     import tiny_nccl_b200 as tn
     with pytest.raises(RuntimeError, match="CUDA error"):
         tn.Communicator(tn.get_unique_id(), 1, 0)
+
+
+def test_make_tuning_table(tmp_path):
+    """benchmarks/make_tuning_table.py: fastest algorithm per size, merged
+    into runs per rank count, last run unbounded."""
+    import json
+    import subprocess
+    import sys
+    recs = []
+    for n, algo_bw in ((2, {1024: {"oneshot": 1.0, "twoshot": 0.5},
+                            1 << 20: {"oneshot": 50.0, "twoshot": 40.0},
+                            1 << 24: {"oneshot": 30.0, "twoshot": 300.0, "nccl": 400.0}}),
+                       (8, {1024: {"oneshot": 1.0, "ring": 2.0}})):
+        for size, d in algo_bw.items():
+            for impl, bw in d.items():
+                recs.append({"impl": impl, "n_gpus": n, "bytes": size, "busbw_gbs": bw})
+    src = tmp_path / "sweep.jsonl"
+    src.write_text("\n".join(json.dumps(r) for r in recs))
+    out = tmp_path / "tuning.txt"
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "benchmarks", "make_tuning_table.py"),
+                        str(src), "-o", str(out)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    lines = [l for l in out.read_text().splitlines() if not l.startswith("#")]
+    assert lines == [f"2 {1 << 20} oneshot", f"2 {(1 << 64) - 1} twoshot",
+                     f"8 {(1 << 64) - 1} ring"], lines
