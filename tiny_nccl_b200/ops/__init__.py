@@ -1,5 +1,6 @@
-"""Fused sm_100a model kernels (LayerNorm, cross-entropy, AdamW) and the
-functional all-reduce."""
+"""Fused sm_100a model kernels: residual-add + LayerNorm, softmax
+cross-entropy, multi-tensor AdamW, and the bias / GELU-backward gradients
+behind the autograd linears."""
 from .fused import (add_layer_norm, cross_entropy, launch_count, layer_norm, linear,
                     linear_gelu)
 from .optim import AdamW, gpt2_param_groups
