@@ -340,10 +340,8 @@ __device__ __forceinline__ bool stagedCopy(const DevComm& comm, const Team& tm, 
 // (at least one; the launch has >= 4 warps).
 __device__ __forceinline__ Team splitTeams(int split, int* role) {
   const int nw = blockDim.x / 32, w = threadIdx.x / 32;
-  int nPush = nw * (split & 15) / 8, nRed = nw * ((split >> 4) & 15) / 8;
-  nPush = nPush < 1 ? 1 : nPush;
-  nRed = nRed < 1 ? 1 : nRed;
-  if (nPush + nRed > nw - 1) nRed = nw - 1 - nPush;
+  const TeamWarps tw = teamWarps(nw, split);
+  const int nPush = tw.first, nRed = tw.second;
   if (w < nPush) {
     *role = kTsPush;
     return Team{(int)threadIdx.x, nPush * 32, 1};

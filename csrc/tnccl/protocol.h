@@ -227,6 +227,19 @@ struct LayoutConfig {
 
 TN_HD uint64_t alignUp(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
 
+// Warp counts of the three teams of a warp-specialised CTA of nw >= 3 warps:
+// split = a | b << 4 asks for a/8 and b/8 of the warps for the first two
+// teams; every team gets at least one warp and the third the rest.
+struct TeamWarps {
+  int first, second, third;
+};
+TN_HD TeamWarps teamWarps(int nw, int split) {
+  int a = nw * (split & 15) / 8, b = nw * ((split >> 4) & 15) / 8;
+  a = a < 1 ? 1 : a > nw - 2 ? nw - 2 : a;
+  b = b < 1 ? 1 : b > nw - 1 - a ? nw - 1 - a : b;
+  return TeamWarps{a, b, nw - a - b};
+}
+
 inline MailboxLayout makeLayout(const LayoutConfig& c) {
   MailboxLayout L{};
   const uint64_t P = (uint64_t)c.nranks;

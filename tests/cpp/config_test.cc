@@ -154,6 +154,20 @@ void tuningTables() {
   remove(path.c_str());
 }
 
+void teamSplits() {
+  bool ok = true;
+  for (int nw = 3; nw <= 32; ++nw)
+    for (int a = 0; a < 16; ++a)
+      for (int b = 0; b < 16; ++b) {
+        const TeamWarps t = teamWarps(nw, a | (b << 4));
+        ok = ok && t.first >= 1 && t.second >= 1 && t.third >= 1 &&
+             t.first + t.second + t.third == nw;
+      }
+  const TeamWarps d = teamWarps(16, 2 | (4 << 4));
+  check(ok && d.first == 4 && d.second == 8 && d.third == 4,
+        "team split: every team >= 1 warp for any split, 16 warps 2,4 -> 4/8/4");
+}
+
 void layouts() {
   bool ok = true;
   for (int P : {2, 3, 4, 8, 16}) {
@@ -249,6 +263,7 @@ int main() {
   adaptChunks();
   hashes();
   tuningTables();
+  teamSplits();
   layouts();
   plans();
   printf("config_test: %s\n", gFailed ? "FAIL" : "PASS");
