@@ -614,6 +614,46 @@ void sequenceContinuity() {
   report("200 mixed collectives on one mailbox set", ok);
 }
 
+// Randomised configurations: rank count, channel count, chunk / tile sizes
+// small enough that every slot ring wraps many times, and random counts,
+// algorithms, dtypes, in-place and pre-scale, three collectives per world.
+void randomized() {
+  uint64_t s = 0x9e3779b97f4a7c15ull;
+  auto rnd = [&s](uint64_t n) {
+    s ^= s << 13;
+    s ^= s >> 7;
+    s ^= s << 17;
+    return s % n;
+  };
+  bool ok = true;
+  int worlds = 0;
+  for (; worlds < 60 && ok; ++worlds) {
+    Config c;
+    c.P = 2 + (int)rnd(7);
+    c.channels = 1 + (int)rnd(4);
+    c.osChannels = 1 + (int)rnd(4);
+    c.nvlsChannels = 1 + (int)rnd(3);
+    c.ringSlots = 2 + (int)rnd(4);
+    c.ringChunkElems = 4 * (1 + rnd(32));
+    c.tsChunkElems = 4 * (1 + rnd(32));
+    c.osSlots = 1 + (int)rnd(3);
+    c.osTileElems = 4 * (1 + rnd(32));
+    c.nvlsTileElems = 4 * (1 + rnd(32));
+    World w(c);
+    for (int k = 0; k < 3 && ok; ++k) {
+      const Algo a = (Algo)(1 + rnd(4));
+      const uint64_t n = rnd(5) == 0 ? rnd(8) : rnd(20000);
+      ok = checkOne(w, a, rnd(2) ? oracle::kBF16 : oracle::kF32, n, rnd(2) == 0, rnd(3) == 0,
+                    1000 + (uint64_t)worlds * 3 + (uint64_t)k);
+      if (!ok) printf("  world %d: P=%d algo=%s count=%llu\n", worlds, c.P, algoName(a),
+                      (unsigned long long)n);
+    }
+  }
+  char name[96];
+  snprintf(name, sizeof(name), "randomised configurations (%d worlds x 3)", worlds);
+  report(name, ok);
+}
+
 void ticketReplay() {
   // tiny-nccl tests/ring_model_test.cc:149-159: credit == t before send,
   // ready = t + 1 on publish, credit = t + S on release.
@@ -661,6 +701,7 @@ int main() {
   referenceMatrix();
   baselineConfig1();
   sequenceContinuity();
+  randomized();
   ticketReplay();
   faultInjection();
   printf("rank_model_test: %s\n", gFailed ? "FAIL" : "PASS");
