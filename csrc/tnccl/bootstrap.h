@@ -2,11 +2,13 @@
 // all-gather, barrier and file-descriptor passing.
 //
 // Behaviour kept from tiny-nccl (src/bootstrap.cc): the unique id names a
-// Unix-socket path; rank 0 binds it (mode 0600), accepts nranks-1 peers and
-// validates their hello (matching nranks, rank in range, no duplicate); peers
-// retry connect until the deadline; every operation has a deadline; all-gather
-// is gather-to-root then broadcast; barrier is collect-then-release; rank 0
-// unlinks the path only if it bound it.
+// Unix-socket path (tncclGetUniqueId :325, path decoding :221); rank 0 binds
+// it (mode 0600), accepts nranks-1 peers and validates their hello (matching
+// nranks, rank in range, no duplicate; bootstrapOpen :354); peers retry
+// connect until the deadline (:264); every operation has a deadline
+// (:73-114); all-gather is gather-to-root then broadcast (:459); barrier is
+// collect-then-release (:502); rank 0 unlinks the path only if it bound it
+// (:532).
 //
 // Added here: every frame carries a per-communicator operation number so that
 // ranks that drift out of step fail with an error instead of mis-pairing
