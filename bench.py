@@ -209,6 +209,28 @@ def build_tnccl_trainer(args, rank, world, dev):
     return trainer.step, launches, close
 
 
+def make_record(impl, world, B, T, steps, warmup, ms_max, clocks, launches, e2e, loss):
+    """The one JSON line bench.py prints (rank 0): whole-job tokens/s from the
+    device step time (max over ranks), plus the end-to-end number, clocks and
+    the kernel-launch count of this repository's kernels."""
+    from tiny_nccl_b200.models import GPT2Config
+    tokens_per_s = world * B * T / (ms_max * 1e-3)
+    flops = GPT2Config().flops_per_token(T) * tokens_per_s / world
+    return {"metric": METRIC, "value": tokens_per_s, "unit": "tokens/s", "n_gpus": world,
+            "steps": steps, "warmup": warmup, "ms_per_step": ms_max,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic token ids Uniform[0,50257) seeded per rank; "
+                                     "random-init weights",
+            "impl": impl,
+            "config": {"model": "GPT-2 small (124M): 12 layers, d_model 768, 12 heads, vocab 50257",
+                       "global_batch": B * world, "micro_batch_per_gpu": B, "seq_len": T,
+                       "parallelism": f"dp{world}", "optimizer": "AdamW", "amp": "bf16 autocast",
+                       "l2": "no flush: one step touches several GB (activations, 124M-param "
+                             "weights/grads/optimizer state), far above the 126 MB L2"},
+            "clocks": clocks, "gpu_launches": launches, "e2e": e2e,
+            "model_tflops_per_gpu": flops / 1e12, "loss": loss}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -324,23 +346,9 @@ def main():
                "h2d_bytes_per_step": B * (T + 1) * 8, "d2h_bytes_per_step": 4,
                "ms_per_step": wall_max * 1e3 / args.steps, "timing": "host wall clock, max over ranks"}
 
-    tokens_per_s = world * B * T / (ms_max * 1e-3)
     if rank == 0:
-        from tiny_nccl_b200.models import GPT2Config
-        flops = GPT2Config().flops_per_token(T) * tokens_per_s / world
-        rec = {"metric": METRIC, "value": tokens_per_s, "unit": "tokens/s", "n_gpus": world,
-               "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
-               "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-               "dtype": "bf16", "data": "synthetic token ids Uniform[0,50257) seeded per rank; "
-                                        "random-init weights",
-               "impl": args.impl,
-               "config": {"model": "GPT-2 small (124M): 12 layers, d_model 768, 12 heads, vocab 50257",
-                          "global_batch": B * world, "micro_batch_per_gpu": B, "seq_len": T,
-                          "parallelism": f"dp{world}", "optimizer": "AdamW", "amp": "bf16 autocast",
-                          "l2": "no flush: one step touches several GB (activations, 124M-param "
-                                "weights/grads/optimizer state), far above the 126 MB L2"},
-               "clocks": clocks, "gpu_launches": int(l1 - l0), "e2e": e2e,
-               "model_tflops_per_gpu": flops / 1e12, "loss": last_loss}
+        rec = make_record(args.impl, world, B, T, args.steps, args.warmup, ms_max, clocks,
+                          int(l1 - l0), e2e, last_loss)
         print(json.dumps(rec), flush=True)
     close()
     dist.barrier()

@@ -97,3 +97,25 @@ def test_make_tuning_table(tmp_path):
     lines = [l for l in out.read_text().splitlines() if not l.startswith("#")]
     assert lines == [f"2 {1 << 20} oneshot", f"2 {(1 << 64) - 1} twoshot",
                      f"8 {(1 << 64) - 1} ring"], lines
+
+
+def test_bench_record_contract():
+    """The JSON line of bench.py carries every key the benchmark contract
+    names, with whole-job tokens/s derived from the device step time."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("bench", os.path.join(ROOT, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    e2e = {"value": 1.0, "unit": "tokens/s", "h2d_bytes_per_step": 65600, "d2h_bytes_per_step": 4}
+    clocks = {"sm_mhz": 1965.0, "sm_max_mhz": 1965.0, "reasons": []}
+    rec = bench.make_record("tnccl", 8, 8, 1024, 20, 5, 16.0, clocks, 1234, e2e, 10.9)
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step",
+                "higher_is_better", "scaling", "vs_baseline", "dtype", "data", "config",
+                "clocks", "e2e", "gpu_launches"):
+        assert key in rec, key
+    for key in ("model", "global_batch", "seq_len", "parallelism"):
+        assert key in rec["config"], key
+    assert rec["value"] == 8 * 8 * 1024 / 16.0e-3
+    assert rec["config"]["global_batch"] == 64 and rec["config"]["parallelism"] == "dp8"
+    assert rec["scaling"] == "weak" and rec["higher_is_better"] is True
+    assert rec["dtype"] == "bf16" and rec["gpu_launches"] == 1234
