@@ -20,7 +20,9 @@ Weak scaling: every GPU processes 8 x 1024 tokens per step.
 --impl nccl-ddp: the NCCL-DDP baseline, the same stock PyTorch stack with
   DDP's own NCCL all-reduce.
 
-Timing: W untimed warm-up steps; then K steps bracketed by a barrier and
+Timing: W untimed warm-up steps (continued until at least --min-warmup-s
+seconds of warm-up; the JSON reports the count as warmup_steps_run); then K
+steps bracketed by a barrier and
 torch.cuda.synchronize(), timed with CUDA events on the training stream; the
 step time is the max over ranks. A second timed loop of K steps measures the
 same metric end to end (pinned-host token copy in, loss read back each step).
@@ -241,6 +243,8 @@ def main():
     ap.add_argument("--seq", type=int, default=1024)
     ap.add_argument("--algo", default="auto")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--min-warmup-s", type=float, default=1.0,
+                    help="untimed warm-up continues past --warmup steps until this long")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -275,8 +279,26 @@ def main():
         b = dev_batches[i % pool]
         return step(b[:, :T], b[:, 1:])
 
-    for i in range(args.warmup):
-        run(i)
+    # Warm-up: the requested W steps, continued (untimed) until at least
+    # --min-warmup-s seconds have passed after the first step (which loads
+    # kernels and builds plans). A cold process can step ~30 % slower for its
+    # next ~0.5 s (per-step times on one B200: 20 ms for steps 2-20, 14.5 ms
+    # from step 21 on). Rank 0 decides when to stop, so every rank runs the
+    # same number of steps (their DDP collectives stay in step).
+    run(0)
+    torch.cuda.synchronize()
+    t_warm = time.perf_counter()
+    warm = 1
+    while True:
+        if warm >= args.warmup:
+            torch.cuda.synchronize()
+            more = time.perf_counter() - t_warm < args.min_warmup_s and warm < 500
+            flag = torch.tensor([1.0 if more else 0.0], device=dev)
+            dist.broadcast(flag, 0)
+            if flag.item() == 0.0:
+                break
+        run(warm)
+        warm += 1
     torch.cuda.synchronize()
     dist.barrier()
 
@@ -349,6 +371,7 @@ def main():
     if rank == 0:
         rec = make_record(args.impl, world, B, T, args.steps, args.warmup, ms_max, clocks,
                           int(l1 - l0), e2e, last_loss)
+        rec["warmup_steps_run"] = warm
         print(json.dumps(rec), flush=True)
     close()
     dist.barrier()
