@@ -119,3 +119,22 @@ def test_bench_record_contract():
     assert rec["config"]["global_batch"] == 64 and rec["config"]["parallelism"] == "dp8"
     assert rec["scaling"] == "weak" and rec["higher_is_better"] is True
     assert rec["dtype"] == "bf16" and rec["gpu_launches"] == 1234
+
+
+def test_clock_summary_parsing():
+    """The clock record bench.py attaches: median SM clock under load, max
+    clock, and every throttle reason seen while loaded."""
+    from tiny_nccl_b200.utils.clocks import summarize
+    na, act = "Not Active", "Active"
+    rows = [
+        f"0, 1965, 1965, 120.5, 0x0, {na}, {na}, {na}, {na}",   # idle, below the load cut
+        f"0, 1965, 1965, 650.0, 0x0, {na}, {na}, {na}, {na}",
+        f"0, 1800, 1965, 980.0, 0x4, {na}, {na}, {na}, {act}",
+        f"0, 1700, 1965, 990.0, 0x4, {na}, {na}, {na}, {act}",
+        "garbage line",
+    ]
+    s = summarize("\n".join(rows))
+    assert s["sm_mhz"] == 1800 and s["sm_max_mhz"] == 1965
+    assert s["reasons"] == ["sw_power_cap"]
+    assert s["samples"] == 4 and s["samples_under_load"] == 3 and s["power_w_max"] == 990.0
+    assert summarize("")["available"] is False
