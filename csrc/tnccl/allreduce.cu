@@ -61,12 +61,19 @@ constexpr uint32_t kBarBytes = 256;
 __host__ __device__ constexpr uint32_t perSource(uint32_t stage, int nsrc) {
   return stage / (uint32_t)nsrc / 16 * 16;
 }
+// The rings are reserved only when staging can happen: a staged copy moves at
+// least stageMinBytes per source, and no source of a tile exceeds the two-shot
+// chunk / the NVLS tile. With staging off (the default) a launch asks for the
+// mbarrier bytes only, so it does not change the SM's shared-memory carve-out
+// under the compute kernels it overlaps with.
 __host__ __device__ uint32_t twoShotSmemBytes(const DevComm& d, int maxp) {
+  if (d.stageMinBytes > d.layout.tsChunkBytes) return kBarBytes;
   const int np = maxp > 1 ? maxp - 1 : 1;
   return kBarBytes + (uint32_t)d.tsStages * (perSource(d.tsPushStage, np) * np +
                                              perSource(d.tsRedStage, maxp) * maxp);
 }
 __host__ __device__ uint32_t nvlsSmemBytes(const DevComm& d) {
+  if (d.stageMinBytes > d.nvlsTileBytes) return kBarBytes;
   return kBarBytes + (uint32_t)d.nvlsStages * perSource(d.nvlsStage, 1);
 }
 
