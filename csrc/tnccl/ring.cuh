@@ -1,0 +1,169 @@
+// ring.cuh - the multi-channel ring all-reduce body (included by
+// allreduce.cu).
+#pragma once
+
+#include "kernel_common.cuh"
+
+namespace tnccl {
+namespace {
+
+using namespace dev;
+
+// ---------------------------------------------------------------------------
+// Ring (per-channel FIFO with ready words in the consumer and credit words in
+// the producer, both polled locally).
+// ---------------------------------------------------------------------------
+template <typename T>
+struct RingChannel {
+  const DevComm* comm;
+  int c, S, next, prev;
+  char* me;
+  uint64_t sendT, recvT;
+
+  __device__ char* outSlot(uint64_t t) const {
+    return comm->peers[next] + ringDataAt(comm->layout, c, (int)(t % (uint64_t)S));
+  }
+  __device__ const T* inSlot(uint64_t t) const {
+    return reinterpret_cast<const T*>(me + ringDataAt(comm->layout, c, (int)(t % (uint64_t)S)));
+  }
+  // Thread 0 waits; the caller passes bar.sync before using the slots.
+  __device__ bool waitSend(int phase) const {
+    return waitFlag(*comm, flagPtr(me, ringCreditAt(comm->layout, c, (int)(sendT % (uint64_t)S))),
+                    sendT, whereCode(kCounterRing, c, phase));
+  }
+  __device__ bool waitRecv(int phase) const {
+    return waitFlag(*comm, flagPtr(me, ringReadyAt(comm->layout, c, (int)(recvT % (uint64_t)S))),
+                    recvT + 1, whereCode(kCounterRing, c, phase));
+  }
+  // Called by thread 0 after bar.sync.
+  __device__ void publishSend() {
+    stReleaseSys(flagPtr(comm->peers[next], ringReadyAt(comm->layout, c, (int)(sendT % (uint64_t)S))),
+                 sendT + 1);
+    ++sendT;
+  }
+  __device__ void releaseRecv() {
+    stReleaseSys(flagPtr(comm->peers[prev], ringCreditAt(comm->layout, c, (int)(recvT % (uint64_t)S))),
+                 recvT + (uint64_t)S);
+    ++recvT;
+  }
+};
+
+template <typename T>
+__device__ __forceinline__ void ringBody(const DevComm& comm, const AllReduceArgs& a,
+                                         const int c) {
+  using Pk = Pack<T>;
+  constexpr int V = Pk::V;
+  const int tid = threadIdx.x, P = comm.nranks, r = comm.rank;
+  const Team cta = wholeCta();
+  const T* x = static_cast<const T*>(a.send);
+  T* y = static_cast<T*>(a.recv);
+  const ChunkPlan& pl = a.chunk;
+  const bool vec = a.vectorized != 0;
+  const float alpha = a.scale;
+  const bool scale = alpha != 1.0f;
+  __shared__ int sFail;
+  if (tid == 0) sFail = 0;
+  RingChannel<T> ch;
+  ch.comm = &comm;
+  ch.c = c;
+  ch.S = comm.layout.ringSlots;
+  ch.next = (r + 1) % P;
+  ch.prev = (r + P - 1) % P;
+  ch.me = comm.peers[r];
+  ch.sendT = ch.recvT = comm.counters[kCounterRing * kMaxChannels + c];
+  __syncthreads();
+
+  // Wait helpers: `needRecv` / `needSend` select which FIFO ends to acquire.
+  auto acquire = [&](bool needRecv, bool needSend, int phase) -> bool {
+    if (tid == 0) {
+      bool ok = true;
+      if (needRecv) ok = ch.waitRecv(phase);
+      if (ok && needSend) ok = ch.waitSend(phase);
+      if (!ok) sFail = 1;
+    }
+    __syncthreads();
+    return sFail == 0;
+  };
+  auto finish = [&](bool recvDone, bool sendDone) {
+    __syncthreads();
+    if (tid == 0) {
+      if (recvDone) ch.releaseRecv();
+      if (sendDone) ch.publishSend();
+    } else {
+      if (recvDone) ++ch.recvT;
+      if (sendDone) ++ch.sendT;
+    }
+  };
+
+  const uint64_t ntiles = channelTiles(pl.numTiles, pl.channels, c);
+  for (uint64_t t = 0; t < ntiles && !sFail; ++t) {
+    const uint64_t tile = (uint64_t)c + t * (uint64_t)pl.channels;
+    // Reduce-scatter: send chunk r-1.
+    {
+      const Span sp = chunkSpan(pl, tile, ringChunkBehind(r, 1, P), V);
+      if (!acquire(false, true, 1)) break;
+      char* out = ch.outSlot(ch.sendT);
+      copyOut<T, kLdInput, 8>(cta, x + sp.offset, sp.count, vec, scale, alpha, 1,
+                              [out](int) { return out; });
+      finish(false, true);
+    }
+    // recv + reduce + send for distances 2..P-1.
+    bool ok = true;
+    for (int d = 2; d < P && ok; ++d) {
+      const Span sp = chunkSpan(pl, tile, ringChunkBehind(r, d, P), V);
+      if (!(ok = acquire(true, true, 2))) break;
+      const T* in = ch.inSlot(ch.recvT);
+      char* out = ch.outSlot(ch.sendT);
+      ringHop<T, 2>(
+          cta, sp.count, vec, in, x + sp.offset, alpha,
+          [&](uint64_t i, uint4 v) { st16(reinterpret_cast<uint4*>(out) + i, v); },
+          [&](uint64_t e, float f) { stElem(reinterpret_cast<T*>(out) + e, f); });
+      finish(true, true);
+    }
+    if (!ok) break;
+    // Final reduce-scatter step: y[chunk r] = in + a*x, stored and forwarded.
+    {
+      const Span sp = chunkSpan(pl, tile, r, V);
+      if (!acquire(true, true, 3)) break;
+      const T* in = ch.inSlot(ch.recvT);
+      char* out = ch.outSlot(ch.sendT);
+      T* yo = y + sp.offset;
+      ringHop<T, 2>(
+          cta, sp.count, vec, in, x + sp.offset, alpha,
+          [&](uint64_t i, uint4 v) {
+            st16(reinterpret_cast<uint4*>(yo) + i, v);
+            st16(reinterpret_cast<uint4*>(out) + i, v);
+          },
+          [&](uint64_t e, float f) {
+            stElem(yo + e, f);
+            stElem(reinterpret_cast<T*>(out) + e, f);
+          });
+      finish(true, true);
+    }
+    // All-gather: recv + store + forward for distances 1..P-2, then store.
+    for (int d = 1; d < P - 1 && ok; ++d) {
+      const Span sp = chunkSpan(pl, tile, ringChunkBehind(r, d, P), V);
+      if (!(ok = acquire(true, true, 4))) break;
+      const T* in = ch.inSlot(ch.recvT);
+      char* out = ch.outSlot(ch.sendT);
+      T* yo = y + sp.offset;
+      copyOut<T, kLdMailbox, 8>(cta, in, sp.count, vec, false, 1.f, 2, [&](int k) {
+        return k == 0 ? reinterpret_cast<char*>(yo) : out;
+      });
+      finish(true, true);
+    }
+    if (!ok) break;
+    {
+      const Span sp = chunkSpan(pl, tile, ringChunkBehind(r, P - 1, P), V);
+      if (!acquire(true, false, 5)) break;
+      T* yo = y + sp.offset;
+      copyOut<T, kLdMailbox, 8>(cta, ch.inSlot(ch.recvT), sp.count, vec, false, 1.f, 1,
+                                [yo](int) { return reinterpret_cast<char*>(yo); });
+      finish(true, false);
+    }
+  }
+  if (tid == 0 && !sFail) comm.counters[kCounterRing * kMaxChannels + c] = ch.sendT;
+}
+
+}  // namespace
+}  // namespace tnccl
