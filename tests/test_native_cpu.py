@@ -138,3 +138,31 @@ def test_clock_summary_parsing():
     assert s["reasons"] == ["sw_power_cap"]
     assert s["samples"] == 4 and s["samples_under_load"] == 3 and s["power_w_max"] == 990.0
     assert summarize("")["available"] is False
+
+
+def test_store_keys_change_per_communicator(monkeypatch):
+    """init_from_store: a default key is new for every communicator, so a
+    second communicator never reads the first one's id from the store."""
+    from tiny_nccl_b200.parallel import comm as C
+
+    made = []
+
+    class FakeComm:
+        def __init__(self, uid, nranks, rank, device=None):
+            made.append((uid, nranks, rank))
+
+    class Store(dict):
+        def set(self, k, v):
+            self[k] = v
+
+        def get(self, k):
+            return self[k]
+
+    ids = iter([b"first", b"second"])
+    monkeypatch.setattr(C, "Communicator", FakeComm)
+    monkeypatch.setattr(C, "get_unique_id", lambda: next(ids))
+    store = Store()
+    C.init_from_store(store, 0, 2)
+    C.init_from_store(store, 0, 2)
+    assert len(store) == 2 and sorted(store.values()) == [b"first", b"second"]
+    assert C._store_key("explicit") == "explicit"

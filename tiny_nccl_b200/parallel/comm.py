@@ -36,6 +36,7 @@ class Communicator:
         if device is not None:
             torch.cuda.set_device(device)
         self._c = load().Communicator(unique_id, nranks, rank)
+        self._side = None
 
     # -- properties -----------------------------------------------------------
     @property
@@ -81,7 +82,7 @@ class Communicator:
         """A stream of this communicator's device, created once and shared by
         the components (DDP hooks, trainers) that enqueue on it; the
         communicator binds to the first stream a collective runs on."""
-        if getattr(self, "_side", None) is None:
+        if self._side is None:
             self._side = torch.cuda.Stream(device=self.device)
         return self._side
 
@@ -114,10 +115,24 @@ class Communicator:
         return self._c.alive
 
 
-def init_from_store(store, rank: int, world_size: int, key: str = "tnccl/uid",
+_created = 0  # communicators created through a store by this process
+
+
+def _store_key(key: str | None) -> str:
+    """The store key of the next communicator: the caller's, or a default
+    that changes with every communicator this process creates, so a later
+    communicator never picks up an earlier id left in the store (every rank
+    creates its communicators in the same order, so the keys agree)."""
+    global _created
+    _created += 1
+    return key if key is not None else f"tnccl/uid/{_created}"
+
+
+def init_from_store(store, rank: int, world_size: int, key: str | None = None,
                     device: int | None = None) -> Communicator:
     """Creates a communicator, sharing the unique id through ``store``
     (anything with ``set(key, bytes)`` and a blocking ``get(key)``)."""
+    key = _store_key(key)
     if rank == 0:
         uid = get_unique_id()
         store.set(key, uid)
@@ -126,7 +141,8 @@ def init_from_store(store, rank: int, world_size: int, key: str = "tnccl/uid",
     return Communicator(uid, world_size, rank, device=device)
 
 
-def init_from_torch_distributed(key: str = "tnccl/uid", device: int | None = None) -> Communicator:
+def init_from_torch_distributed(key: str | None = None,
+                                device: int | None = None) -> Communicator:
     """Creates a communicator over the ranks of the default process group."""
     import torch.distributed as dist
 
