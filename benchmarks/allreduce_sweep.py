@@ -91,6 +91,9 @@ def main():
     ap.add_argument("--impls", default="oneshot,twoshot,ring,nvls,auto,nccl")
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--iters", type=int, default=100)
+    ap.add_argument("--ref-max-bytes", default="1G",
+                    help="largest size run for the reference ring (~2 GB/s: 4 GiB takes seconds "
+                         "per call)")
     ap.add_argument("--max-seconds-per-point", type=float, default=1.5,
                     help="caps K for large sizes (time-bounded sweeps)")
     ap.add_argument("--out", default="")
@@ -141,6 +144,9 @@ def main():
         x = src[:n]
         y = dst[:n]
         for impl in impls:
+            if impl == "ref" and size > parse_size(args.ref_max_bytes):
+                continue
+
             def op():
                 if impl == "nccl":
                     dist.all_reduce(y)  # in place, like NCCL's own bench
