@@ -6,21 +6,18 @@
 #include "bootstrap.h"
 
 #include <errno.h>
-#include <fcntl.h>
 #include <poll.h>
 #include <stdio.h>
 #include <string.h>
-#include <sys/random.h>
 #include <sys/socket.h>
 #include <sys/stat.h>
 #include <sys/un.h>
 #include <unistd.h>
 
 #include <algorithm>
-#include <chrono>
-#include <climits>
 
 #include "common.h"
+#include "sockio.h"
 
 namespace tnccl {
 namespace {
@@ -68,84 +65,6 @@ struct Hello {
   int32_t pad;
   uint64_t configHash;
 };
-
-using Clock = std::chrono::steady_clock;
-using Deadline = Clock::time_point;
-
-Deadline deadlineIn(int ms) { return Clock::now() + std::chrono::milliseconds(ms); }
-
-int msLeft(Deadline d) {
-  auto now = Clock::now();
-  if (now >= d) return 0;
-  auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(d - now).count();
-  return (int)std::min<int64_t>(ms + 1, INT_MAX);
-}
-
-// Outcome of a socket step: ok, timed out, or failed otherwise.
-enum class Io { kOk, kTimeout, kError };
-
-Io waitFd(int fd, short events, Deadline d) {
-  for (;;) {
-    int left = msLeft(d);
-    if (left == 0) return Io::kTimeout;
-    pollfd p{fd, events, 0};
-    int rc = poll(&p, 1, left);
-    if (rc > 0) {
-      if (p.revents & POLLNVAL) return Io::kError;
-      if (p.revents & events) return Io::kOk;
-      if (p.revents & (POLLERR | POLLHUP)) return Io::kError;
-      continue;
-    }
-    if (rc == 0) return Io::kTimeout;
-    if (errno != EINTR) return Io::kError;
-  }
-}
-
-Io readAll(int fd, void* buf, size_t n, Deadline d) {
-  auto* p = static_cast<unsigned char*>(buf);
-  size_t done = 0;
-  while (done < n) {
-    ssize_t rc = recv(fd, p + done, n - done, 0);
-    if (rc > 0) {
-      done += (size_t)rc;
-      continue;
-    }
-    if (rc == 0) return Io::kError;  // peer closed
-    if (errno == EINTR) continue;
-    if (errno == EAGAIN || errno == EWOULDBLOCK) {
-      Io w = waitFd(fd, POLLIN, d);
-      if (w != Io::kOk) return w;
-      continue;
-    }
-    return Io::kError;
-  }
-  return Io::kOk;
-}
-
-Io writeAll(int fd, const void* buf, size_t n, Deadline d) {
-  auto* p = static_cast<const unsigned char*>(buf);
-  size_t done = 0;
-  while (done < n) {
-    ssize_t rc = send(fd, p + done, n - done, MSG_NOSIGNAL);
-    if (rc > 0) {
-      done += (size_t)rc;
-      continue;
-    }
-    if (rc < 0 && errno == EINTR) continue;
-    if (rc < 0 && (errno == EAGAIN || errno == EWOULDBLOCK)) {
-      Io w = waitFd(fd, POLLOUT, d);
-      if (w != Io::kOk) return w;
-      continue;
-    }
-    return Io::kError;
-  }
-  return Io::kOk;
-}
-
-tncclResult toResult(Io io) {
-  return io == Io::kOk ? TNCCL_SUCCESS
-                       : io == Io::kTimeout ? TNCCL_TIMEOUT : TNCCL_SYSTEM_ERROR;
-}
 
 Io sendFrame(int fd, uint16_t type, uint32_t op, uint32_t status,
              const void* payload, size_t bytes, Deadline d) {
@@ -275,37 +194,6 @@ Io recvFrameFds(int fd, uint16_t type, uint32_t op, void* payload, size_t bytes,
   return readAll(fd, p + done, bytes - done, d);
 }
 
-bool randomBytes(void* buf, size_t n) {
-  auto* p = static_cast<unsigned char*>(buf);
-  size_t done = 0;
-  while (done < n) {
-    ssize_t rc = getrandom(p + done, n - done, 0);
-    if (rc > 0) {
-      done += (size_t)rc;
-    } else if (rc < 0 && errno == EINTR) {
-      continue;
-    } else {
-      break;
-    }
-  }
-  if (done == n) return true;
-  int fd = open("/dev/urandom", O_RDONLY | O_CLOEXEC);
-  if (fd < 0) return false;
-  while (done < n) {
-    ssize_t rc = read(fd, p + done, n - done);
-    if (rc > 0) {
-      done += (size_t)rc;
-    } else if (rc < 0 && errno == EINTR) {
-      continue;
-    } else {
-      close(fd);
-      return false;
-    }
-  }
-  close(fd);
-  return true;
-}
-
 sockaddr_un addressOf(const char* path, socklen_t* len) {
   sockaddr_un a{};
   a.sun_family = AF_UNIX;
@@ -348,24 +236,6 @@ int connectHub(const char* path, Deadline d, Io* why) {
   }
   *why = Io::kTimeout;
   return -1;
-}
-
-int acceptOne(int listenFd, Deadline d, Io* why) {
-  for (;;) {
-    int fd = accept4(listenFd, nullptr, nullptr, SOCK_NONBLOCK | SOCK_CLOEXEC);
-    if (fd >= 0) return fd;
-    if (errno == EINTR) continue;
-    if (errno == EAGAIN || errno == EWOULDBLOCK) {
-      Io w = waitFd(listenFd, POLLIN, d);
-      if (w != Io::kOk) {
-        *why = w;
-        return -1;
-      }
-      continue;
-    }
-    *why = Io::kError;
-    return -1;
-  }
 }
 
 bool allowedPathChar(unsigned char ch) {

@@ -349,4 +349,73 @@ TN_HD uint64_t nvlsRegionBytes(uint64_t tileBytes, int channels) {
   return nvlsDataBytes(tileBytes, channels) + alignUp(2ull * kMaxChannels * kNvlsSlots * 8, 4096);
 }
 
+// ---------------------------------------------------------------------------
+// One ring edge's FIFO as the ring kernel and the socket proxy see it: per
+// channel c and slot s (index c * slots + s) a payload of chunkBytes, a ready
+// word (ticket + 1 once the payload of that ticket is written) and a credit
+// word (the first ticket that may use the slot; slot s starts at s). For an
+// NVLink edge the payload and ready words live in the consumer's mailbox and
+// the credits in the producer's, so both ends poll local memory. For a socket
+// edge all of them live in one host-mapped buffer per direction (layout:
+// makeNetFifoLayout) that the rank's kernel shares with its proxy thread,
+// plus a payload-size word per slot, since a frame carries exactly the bytes
+// the kernel wrote.
+// ---------------------------------------------------------------------------
+struct RingFifo {
+  char* data;
+  uint64_t* ready;
+  uint64_t* credit;
+  uint64_t* bytes;  // payload bytes per slot (socket edges; null for NVLink)
+  uint64_t chunkBytes;
+  int slots;
+};
+
+TN_HD uint64_t ringFifoIndex(const RingFifo& f, int c, uint64_t ticket) {
+  return (uint64_t)c * (uint64_t)f.slots + ticket % (uint64_t)f.slots;
+}
+TN_HD char* ringFifoData(const RingFifo& f, int c, uint64_t ticket) {
+  return f.data + ringFifoIndex(f, c, ticket) * f.chunkBytes;
+}
+
+// The FIFO of the NVLink edge producer -> consumer, from the two mailboxes.
+TN_HD RingFifo nvlinkRingFifo(char* consumer, char* producer, const MailboxLayout& L) {
+  return RingFifo{consumer + L.ringDataOff,
+                  reinterpret_cast<uint64_t*>(consumer + L.ringReadyOff),
+                  reinterpret_cast<uint64_t*>(producer + L.ringCreditOff), nullptr,
+                  L.ringChunkBytes, L.ringSlots};
+}
+
+struct NetFifoLayout {
+  int channels;
+  int slots;
+  uint64_t chunkBytes;
+  uint64_t readyOff, creditOff, bytesOff;
+  uint64_t totalBytes;
+};
+
+TN_HD NetFifoLayout makeNetFifoLayout(int channels, int slots, uint64_t chunkBytes) {
+  NetFifoLayout L{};
+  const uint64_t n = (uint64_t)channels * (uint64_t)slots;
+  L.channels = channels;
+  L.slots = slots;
+  L.chunkBytes = chunkBytes;
+  L.readyOff = alignUp(n * chunkBytes, 128);
+  L.creditOff = alignUp(L.readyOff + n * 8, 128);
+  L.bytesOff = alignUp(L.creditOff + n * 8, 128);
+  L.totalBytes = alignUp(L.bytesOff + n * 8, 4096);
+  return L;
+}
+
+TN_HD RingFifo netRingFifo(char* base, const NetFifoLayout& L) {
+  return RingFifo{base, reinterpret_cast<uint64_t*>(base + L.readyOff),
+                  reinterpret_cast<uint64_t*>(base + L.creditOff),
+                  reinterpret_cast<uint64_t*>(base + L.bytesOff), L.chunkBytes, L.slots};
+}
+
+// Socket frame: ticket (8 bytes) and payload bytes (4 bytes), big-endian,
+// then the payload. The close frame (ticket kNetCloseTicket, no payload) ends
+// a connection cleanly; a connection that ends without it is a failure.
+constexpr uint32_t kNetFrameHeaderBytes = 12;
+constexpr uint64_t kNetCloseTicket = ~0ull;
+
 }  // namespace tnccl

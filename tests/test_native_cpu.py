@@ -61,6 +61,15 @@ def test_rank_model(built):
         assert line in r.stdout
 
 
+def test_socket_ring_edges(built):
+    """Socket data plane (TCP ring edges + proxy thread) on host threads:
+    stream integrity under back-pressure, ring all-reduce over mixed NVLink /
+    socket edges vs the ring oracle, and the host-made failure paths."""
+    r = run([os.path.join(ROOT, "build", "bin", "net_proxy_test")], timeout=300)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "net_proxy_test: PASS" in r.stdout
+
+
 def test_config_and_partitions(built):
     r = run([os.path.join(ROOT, "build", "bin", "config_test")], timeout=120)
     assert r.returncode == 0, r.stdout + r.stderr

@@ -35,9 +35,32 @@ def test_rank_model_under_tsan():
 @pytest.mark.skipif(shutil.which("g++") is None, reason="needs g++")
 def test_bootstrap_under_asan_ubsan():
     exe = _build("bootstrap_asan", ["tests/cpp/bootstrap_test.cc", "csrc/tnccl/bootstrap.cc",
-                                    "csrc/tnccl/common.cc"],
+                                    "csrc/tnccl/common.cc", "csrc/tnccl/sockio.cc"],
                  ["-fsanitize=address,undefined", "-fno-omit-frame-pointer",
                   "-fno-sanitize-recover=undefined"])
     env = dict(os.environ, ASAN_OPTIONS="detect_leaks=1:abort_on_error=1")
     r = subprocess.run([exe], capture_output=True, text=True, timeout=300, env=env)
     assert r.returncode == 0 and "bootstrap_test: PASS" in r.stdout, r.stdout[-2000:] + r.stderr[-4000:]
+
+
+_NET_SRCS = ["tests/cpp/net_proxy_test.cc", "csrc/tnccl/net.cc", "csrc/tnccl/sockio.cc",
+             "csrc/tnccl/bootstrap.cc", "csrc/tnccl/common.cc"]
+
+
+@pytest.mark.skipif(shutil.which("g++") is None, reason="needs g++")
+def test_socket_proxy_under_tsan():
+    exe = _build("net_proxy_tsan", _NET_SRCS, ["-fsanitize=thread"])
+    env = dict(os.environ, TSAN_OPTIONS="halt_on_error=1 second_deadlock_stack=1")
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=600, env=env)
+    assert r.returncode == 0 and "net_proxy_test: PASS" in r.stdout, r.stdout[-2000:] + r.stderr[-4000:]
+    assert "WARNING: ThreadSanitizer" not in r.stderr, r.stderr[-4000:]
+
+
+@pytest.mark.skipif(shutil.which("g++") is None, reason="needs g++")
+def test_socket_proxy_under_asan_ubsan():
+    exe = _build("net_proxy_asan", _NET_SRCS,
+                 ["-fsanitize=address,undefined", "-fno-omit-frame-pointer",
+                  "-fno-sanitize-recover=undefined"])
+    env = dict(os.environ, ASAN_OPTIONS="detect_leaks=1:abort_on_error=1")
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=300, env=env)
+    assert r.returncode == 0 and "net_proxy_test: PASS" in r.stdout, r.stdout[-2000:] + r.stderr[-4000:]

@@ -159,6 +159,8 @@ PROGRAMS = {
     "allreduce_gpu_test": ROOT / "tests" / "cpp" / "allreduce_gpu_test.cc",
     "bootstrap_test": ROOT / "tests" / "cpp" / "bootstrap_test.cc",
     "rank_model_test": ROOT / "tests" / "cpp" / "rank_model_test.cc",
+    # socket ring edges: connection set-up, proxy thread, ring over sockets
+    "net_proxy_test": ROOT / "tests" / "cpp" / "net_proxy_test.cc",
     # host configuration / partition checks, built with the library's config code
     "config_test": (ROOT / "tests" / "cpp" / "config_test.cc", TNCCL_SRC / "common.cc"),
 }
