@@ -90,10 +90,13 @@ __global__ void __launch_bounds__(kMaxThreads)
   oneShotBody<T, MAXP>(comm, a, blockIdx.x);
 }
 
-template <typename T>
+// NET: the communicator has socket ring edges (TNCCL_NET), so either edge of
+// this rank may be a host-mapped FIFO; the NVLink-only ring is compiled
+// without those branches.
+template <typename T, bool NET>
 __global__ void __launch_bounds__(kMaxThreads)
     ringKernel(const __grid_constant__ DevComm comm, const __grid_constant__ AllReduceArgs a) {
-  ringBody<T>(comm, a, blockIdx.x);
+  ringBody<T, NET>(comm, a, blockIdx.x);
 }
 
 // Single-GPU emulation of `nranks` ranks: blockIdx.y selects the emulated
@@ -112,7 +115,7 @@ __global__ void __launch_bounds__(kMaxThreads)
       oneShotBody<T, MAXP>(e.comm[r], e.args[r], blockIdx.x);
       break;
     default:
-      ringBody<T>(e.comm[r], e.args[r], blockIdx.x);
+      ringBody<T, false>(e.comm[r], e.args[r], blockIdx.x);
       break;
   }
 }
@@ -168,7 +171,10 @@ cudaError_t launchTyped(const DevComm& comm, const AllReduceArgs& a, int algo, i
   const dim3 block((unsigned)threads);
   switch (algo) {
     case TNCCL_ALGO_RING:
-      ringKernel<T><<<a.chunk.channels, block, 0, stream>>>(comm, a);
+      if (comm.netSend || comm.netRecv)
+        ringKernel<T, true><<<a.chunk.channels, block, 0, stream>>>(comm, a);
+      else
+        ringKernel<T, false><<<a.chunk.channels, block, 0, stream>>>(comm, a);
       break;
     case TNCCL_ALGO_TWOSHOT:
       if (comm.nranks <= 2)

@@ -91,6 +91,9 @@ extern "C" tncclResult tncclCommGetInfo(tncclComm_t comm, tncclCommInfo* info) {
   info->ringMinChunkBytes = kRingMinChunkBytes;
   info->oneShotChannels = comm->cfg.osChannels;
   info->nvlsChannels = comm->nvls.enabled ? comm->nvls.channels : 0;
+  info->netSendSocket = comm->net.send ? 1 : 0;
+  info->netRecvSocket = comm->net.recv ? 1 : 0;
+  info->netChannels = comm->net.any ? comm->net.layout.channels : 0;
   return TNCCL_SUCCESS;
 }
 

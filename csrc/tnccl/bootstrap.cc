@@ -1,13 +1,17 @@
-// bootstrap.cc - AF_UNIX star rendezvous (see bootstrap.h for the contract).
+// bootstrap.cc - AF_UNIX or TCP star rendezvous (see bootstrap.h for the
+// contract).
 #ifndef _GNU_SOURCE
 #define _GNU_SOURCE
 #endif
 
 #include "bootstrap.h"
 
+#include <arpa/inet.h>
 #include <errno.h>
+#include <netinet/in.h>
 #include <poll.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 #include <sys/socket.h>
 #include <sys/stat.h>
@@ -15,6 +19,7 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <string>
 
 #include "common.h"
 #include "sockio.h"
@@ -22,9 +27,10 @@
 namespace tnccl {
 namespace {
 
-constexpr uint64_t kIdMagic = 0x3230304242434e54ull;   // "TNCBB002" little-endian
-constexpr uint32_t kFrameMagic = 0x544e4246u;          // "FBNT"
-constexpr uint16_t kWireVersion = 2;
+constexpr uint64_t kIdMagic = 0x3230304242434e54ull;     // "TNCBB002" little-endian
+constexpr uint64_t kTcpIdMagic = 0x3330305442434e54ull;  // "TNCBT003" little-endian
+constexpr uint32_t kFrameMagic = 0x544e4246u;            // "FBNT"
+constexpr uint16_t kWireVersion = 3;
 constexpr size_t kMaxGatherBytes = 1u << 20;           // per rank
 constexpr char kBaseName[] = "tnccl-b200-";
 
@@ -49,6 +55,17 @@ struct IdPayload {
 };
 static_assert(sizeof(IdPayload) == sizeof(tncclUniqueId), "id layout");
 
+struct TcpIdPayload {
+  uint64_t magic;
+  uint32_t version;
+  uint32_t ipv4;  // network byte order
+  uint32_t port;
+  uint32_t pad;
+  uint64_t nonce;  // random, never 0
+  char reserved[96];
+};
+static_assert(sizeof(TcpIdPayload) == sizeof(tncclUniqueId), "tcp id layout");
+
 struct FrameHeader {
   uint32_t magic;
   uint16_t version;
@@ -64,6 +81,7 @@ struct Hello {
   int32_t pid;
   int32_t pad;
   uint64_t configHash;
+  uint64_t nonce;  // TCP ids: the communicator nonce (0 for AF_UNIX)
 };
 
 Io sendFrame(int fd, uint16_t type, uint32_t op, uint32_t status,
@@ -246,8 +264,47 @@ bool allowedPathChar(unsigned char ch) {
 
 }  // namespace
 
+tncclResult bootstrapNewTcpId(tncclUniqueId* id, const char* addr, int port) {
+  if (id == nullptr || port <= 0 || port > 65535) return TNCCL_INVALID_ARGUMENT;
+  TcpIdPayload p{};
+  if (!parseIpv4(addr, &p.ipv4)) return TNCCL_INVALID_ARGUMENT;
+  p.magic = kTcpIdMagic;
+  p.version = kWireVersion;
+  p.port = (uint32_t)port;
+  do {
+    if (!randomBytes(&p.nonce, sizeof(p.nonce))) return TNCCL_SYSTEM_ERROR;
+  } while (p.nonce == 0);
+  memcpy(id->bytes, &p, sizeof(p));
+  return TNCCL_SUCCESS;
+}
+
+bool bootstrapDecodeTcpId(const tncclUniqueId& id, uint32_t* ipv4, int* port, uint64_t* nonce) {
+  TcpIdPayload p{};
+  memcpy(&p, id.bytes, sizeof(p));
+  if (p.magic != kTcpIdMagic || p.version != kWireVersion || p.port == 0 || p.port > 65535 ||
+      p.nonce == 0 || p.ipv4 == 0)
+    return false;
+  *ipv4 = p.ipv4;
+  *port = (int)p.port;
+  *nonce = p.nonce;
+  return true;
+}
+
 tncclResult bootstrapNewId(tncclUniqueId* id) {
   if (id == nullptr) return TNCCL_INVALID_ARGUMENT;
+  const std::string tcp = envStr("TNCCL_BOOTSTRAP_ADDR", "");
+  if (!tcp.empty()) {
+    const size_t colon = tcp.rfind(':');
+    if (colon == std::string::npos) {
+      TN_WARN("TNCCL_BOOTSTRAP_ADDR must be <ipv4>:<port>, got '%s'", tcp.c_str());
+      return TNCCL_INVALID_ARGUMENT;
+    }
+    const std::string host = tcp.substr(0, colon);
+    char* end = nullptr;
+    const long port = strtol(tcp.c_str() + colon + 1, &end, 10);
+    if (end == tcp.c_str() + colon + 1 || *end != '\0') return TNCCL_INVALID_ARGUMENT;
+    return bootstrapNewTcpId(id, host.c_str(), (int)port);
+  }
   unsigned char rnd[16];
   if (!randomBytes(rnd, sizeof(rnd))) return TNCCL_SYSTEM_ERROR;
   char hex[33];
@@ -301,34 +358,55 @@ tncclResult bootstrapOpen(Bootstrap* b, const tncclUniqueId& id, int nranks,
       rank < 0 || rank >= nranks) {
     return TNCCL_INVALID_ARGUMENT;
   }
-  char path[108];
-  if (!bootstrapDecodeId(id, path)) return TNCCL_INVALID_ARGUMENT;
+  char path[108] = {};
+  uint32_t ip = 0;
+  int port = 0;
+  uint64_t nonce = 0;
+  const bool tcp = bootstrapDecodeTcpId(id, &ip, &port, &nonce);
+  if (!tcp && !bootstrapDecodeId(id, path)) return TNCCL_INVALID_ARGUMENT;
   b->rank = rank;
   b->nranks = nranks;
   b->timeoutMs = timeoutMs;
   b->opSeq = 0;
+  b->tcp = tcp;
+  b->nonce = nonce;
+  b->hubIpv4 = ip;
   Deadline d = deadlineIn(timeoutMs);
 
   if (rank == 0) {
     b->peerFds.assign((size_t)nranks, -1);
-    b->listenFd = newSocket();
-    if (b->listenFd < 0) {
-      bootstrapClose(b);
-      return TNCCL_SYSTEM_ERROR;
-    }
-    b->active = true;
-    socklen_t len;
-    sockaddr_un a = addressOf(path, &len);
-    if (bind(b->listenFd, reinterpret_cast<sockaddr*>(&a), len) != 0) {
-      TN_WARN("bootstrap: bind(%s) failed: %s", path, strerror(errno));
-      bootstrapClose(b);  // path not owned: never unlink another rendezvous
-      return TNCCL_SYSTEM_ERROR;
-    }
-    strncpy(b->path, path, sizeof(b->path) - 1);
-    b->ownsPath = true;
-    if (chmod(path, S_IRUSR | S_IWUSR) != 0 || listen(b->listenFd, nranks) != 0) {
-      bootstrapClose(b);
-      return TNCCL_SYSTEM_ERROR;
+    if (tcp) {
+      char addr[INET_ADDRSTRLEN] = {};
+      in_addr ia{};
+      ia.s_addr = ip;
+      inet_ntop(AF_INET, &ia, addr, sizeof(addr));
+      b->listenFd = tcpListen(addr, port, nranks, nullptr);
+      if (b->listenFd < 0) {
+        TN_WARN("bootstrap: cannot listen on %s:%d: %s", addr, port, strerror(errno));
+        bootstrapClose(b);
+        return TNCCL_SYSTEM_ERROR;
+      }
+      b->active = true;
+    } else {
+      b->listenFd = newSocket();
+      if (b->listenFd < 0) {
+        bootstrapClose(b);
+        return TNCCL_SYSTEM_ERROR;
+      }
+      b->active = true;
+      socklen_t len;
+      sockaddr_un a = addressOf(path, &len);
+      if (bind(b->listenFd, reinterpret_cast<sockaddr*>(&a), len) != 0) {
+        TN_WARN("bootstrap: bind(%s) failed: %s", path, strerror(errno));
+        bootstrapClose(b);  // path not owned: never unlink another rendezvous
+        return TNCCL_SYSTEM_ERROR;
+      }
+      strncpy(b->path, path, sizeof(b->path) - 1);
+      b->ownsPath = true;
+      if (chmod(path, S_IRUSR | S_IWUSR) != 0 || listen(b->listenFd, nranks) != 0) {
+        bootstrapClose(b);
+        return TNCCL_SYSTEM_ERROR;
+      }
     }
     for (int joined = 1; joined < nranks; ++joined) {
       Io why = Io::kOk;
@@ -350,6 +428,9 @@ tncclResult bootstrapOpen(Bootstrap* b, const tncclUniqueId& id, int nranks,
       if (h.nranks != nranks || h.rank <= 0 || h.rank >= nranks ||
           b->peerFds[(size_t)h.rank] != -1) {
         st = TNCCL_INVALID_ARGUMENT;
+      } else if (h.nonce != nonce) {
+        TN_WARN("bootstrap: a rank of another communicator joined (nonce mismatch)");
+        st = TNCCL_INVALID_ARGUMENT;
       } else if (h.configHash != configHash) {
         TN_WARN("bootstrap: rank %d has a different TNCCL_* configuration", h.rank);
         st = TNCCL_INVALID_ARGUMENT;
@@ -368,13 +449,13 @@ tncclResult bootstrapOpen(Bootstrap* b, const tncclUniqueId& id, int nranks,
   }
 
   Io why = Io::kOk;
-  b->hubFd = connectHub(path, d, &why);
+  b->hubFd = tcp ? tcpConnect(ip, port, d, &why) : connectHub(path, d, &why);
   if (b->hubFd < 0) {
     bootstrapClose(b);
     return toResult(why);
   }
   b->active = true;
-  Hello h{rank, nranks, (int32_t)getpid(), 0, configHash};
+  Hello h{rank, nranks, (int32_t)getpid(), 0, configHash, nonce};
   uint32_t st = 0;
   Io io = sendFrame(b->hubFd, kHello, 0, 0, &h, sizeof(h), d);
   if (io == Io::kOk) io = recvFrame(b->hubFd, kHelloAck, 0, nullptr, 0, &st, d);
@@ -439,6 +520,7 @@ tncclResult bootstrapBarrier(Bootstrap* b) {
 
 tncclResult bootstrapAllGatherFds(Bootstrap* b, int myFd, int* fds) {
   if (b == nullptr || !b->active || fds == nullptr) return TNCCL_INVALID_ARGUMENT;
+  if (b->tcp) return TNCCL_UNSUPPORTED;  // same answer on every rank, no message
   const uint32_t op = ++b->opSeq;
   const int P = b->nranks;
   Deadline d = deadlineIn(b->timeoutMs);
@@ -510,6 +592,7 @@ tncclResult bootstrapAllGatherFds(Bootstrap* b, int myFd, int* fds) {
 
 tncclResult bootstrapBroadcastFd(Bootstrap* b, int fd, int* out) {
   if (b == nullptr || !b->active || out == nullptr) return TNCCL_INVALID_ARGUMENT;
+  if (b->tcp) return TNCCL_UNSUPPORTED;
   const uint32_t op = ++b->opSeq;
   Deadline d = deadlineIn(b->timeoutMs);
   *out = -1;
@@ -556,6 +639,9 @@ void bootstrapClose(Bootstrap* b) {
   b->rank = -1;
   b->nranks = 0;
   b->active = false;
+  b->tcp = false;
+  b->nonce = 0;
+  b->hubIpv4 = 0;
 }
 
 }  // namespace tnccl

@@ -15,6 +15,15 @@
 // messages; the hello carries a configuration hash; SCM_RIGHTS passing of
 // POSIX file descriptors (cuMem / multicast handles) as an all-gather and a
 // broadcast from rank 0; deadline expiry returns TNCCL_TIMEOUT.
+//
+// TCP rendezvous for ranks on several hosts (tiny-nccl's socket design,
+// docs/design-v0.2.md:78, leaves its encoding open): when
+// TNCCL_BOOTSTRAP_ADDR=<ipv4>:<port> is set where the id is created, the id
+// carries that address and a random 64-bit communicator nonce instead of a
+// socket path; rank 0 listens there, the others connect with retry, and the
+// hello must carry the same nonce. Frames, all-gather and barrier are the
+// same over both socket kinds; descriptor passing needs AF_UNIX and returns
+// TNCCL_UNSUPPORTED on a TCP bootstrap.
 #pragma once
 
 #include <stddef.h>
@@ -41,13 +50,22 @@ struct Bootstrap {
   bool active = false;
   uint32_t opSeq = 0;         // bootstrap collectives issued so far
   int timeoutMs = 30000;
+  bool tcp = false;           // TCP rendezvous (no descriptor passing)
+  uint64_t nonce = 0;         // communicator nonce of a TCP id (0 for AF_UNIX)
+  uint32_t hubIpv4 = 0;       // TCP: rank 0's address (network byte order)
 };
 
-// Encodes a fresh rendezvous path into id (random 128-bit suffix).
+// Encodes a fresh rendezvous into id: a TCP id when TNCCL_BOOTSTRAP_ADDR is
+// set, else an AF_UNIX path with a random 128-bit suffix.
 tncclResult bootstrapNewId(tncclUniqueId* id);
+// A TCP id for rank 0 at addr:port (dotted quad, port 1..65535).
+tncclResult bootstrapNewTcpId(tncclUniqueId* id, const char* addr, int port);
 
-// Validates id and returns the socket path it names.
+// Validates an AF_UNIX id and returns the socket path it names.
 bool bootstrapDecodeId(const tncclUniqueId& id, char (&path)[108]);
+// Validates a TCP id and returns rank 0's address (network byte order), port
+// and the communicator nonce.
+bool bootstrapDecodeTcpId(const tncclUniqueId& id, uint32_t* ipv4, int* port, uint64_t* nonce);
 
 tncclResult bootstrapOpen(Bootstrap* b, const tncclUniqueId& id, int nranks,
                           int rank, uint64_t configHash, int timeoutMs);
@@ -56,7 +74,8 @@ tncclResult bootstrapAllGather(Bootstrap* b, const void* send, void* recv,
 tncclResult bootstrapBarrier(Bootstrap* b);
 
 // Every rank contributes one descriptor (or -1 when it has none, which makes
-// the collective fail on every rank). On success fds[r] holds a descriptor
+// the collective fail on every rank). TNCCL_UNSUPPORTED on every rank of a
+// TCP bootstrap (the same for bootstrapBroadcastFd). On success fds[r] holds a descriptor
 // for rank r's object, owned by the caller (fds[rank] is a duplicate of the
 // caller's own descriptor).
 tncclResult bootstrapAllGatherFds(Bootstrap* b, int myFd, int* fds);

@@ -13,7 +13,9 @@
 // P2P access and native peer atomics; devices are compared by UUID rather
 // than by per-process ordinal; an NVLS multicast object is created when every
 // rank supports it; the host-mapped status block and the device-resident FIFO
-// counters are allocated here.
+// counters are allocated here. Ranks on other hosts (compared by host
+// identity) are not mapped: the ring edges that reach them are socket edges
+// (net_setup.cc), and such a communicator runs the ring only.
 #include <string.h>
 #include <unistd.h>
 
@@ -23,6 +25,7 @@
 
 #include "comm.h"
 #include "driver.h"
+#include "sockio.h"
 
 namespace tnccl {
 namespace {
@@ -182,6 +185,9 @@ void fillDevComm(tncclComm* comm) {
   d.nvlsStages = comm->cfg.nvlsStages;
   d.nvlsStage = (uint32_t)comm->cfg.nvlsStage;
   d.stageMinBytes = (uint32_t)comm->cfg.stageMinBytes;
+  d.netSend = comm->net.sendDev;
+  d.netRecv = comm->net.recvDev;
+  d.netLayout = comm->net.layout;
 }
 
 void deriveThresholds(tncclComm* comm) {
@@ -206,6 +212,8 @@ void deriveThresholds(tncclComm* comm) {
 // close our imports and the control connection, keep the export alive.
 void abandonPublished(tncclComm* comm) {
   tncclResult ignored = TNCCL_SUCCESS;
+  netStopProxy(comm, false, &ignored);
+  netRelease(comm, true);  // host FIFOs: no kernel has run
   closePeerMailboxes(comm, &ignored);
   bootstrapClose(&comm->bootstrap);
 }
@@ -263,6 +271,8 @@ extern "C" tncclResult tncclCommInitRank(tncclComm_t* out, int nranks, tncclUniq
 
   PeerMeta me{};
   me.device = comm->device;
+  me.hostId = hostIdentity();
+  if (rank == 0 && !randomBytes(&me.nonce, sizeof(me.nonce))) me.status = TNCCL_SYSTEM_ERROR;
   cudaDeviceProp prop{};
   if (cudaGetDeviceProperties(&prop, comm->device) == cudaSuccess) {
     memcpy(me.uuid, &prop.uuid, sizeof(me.uuid));
@@ -271,8 +281,11 @@ extern "C" tncclResult tncclCommInitRank(tncclComm_t* out, int nranks, tncclUniq
   }
   if (cudaDeviceGetPCIBusId(me.busId, sizeof(me.busId), comm->device) != cudaSuccess)
     me.status = TNCCL_CUDA_ERROR;
+  // A TCP bootstrap cannot pass descriptors: mailboxes are shared as cudaIpc
+  // handles inside PeerMeta instead.
   if (me.status == TNCCL_SUCCESS)
-    me.status = allocLocalMailbox(comm.get(), comm->layout.totalBytes, comm->cfg.useCuMem != 0);
+    me.status = allocLocalMailbox(comm.get(), comm->layout.totalBytes,
+                                  comm->cfg.useCuMem != 0 && !comm->bootstrap.tcp);
   if (me.status == TNCCL_SUCCESS) me.status = initMailboxContents(comm.get());
   me.ipcMode = comm->ipcMode;
   me.mailboxBytes = comm->local.bytes;
@@ -289,8 +302,31 @@ extern "C" tncclResult tncclCommInitRank(tncclComm_t* out, int nranks, tncclUniq
   if (status == TNCCL_SUCCESS && !devicesUnique(metas)) status = TNCCL_UNSUPPORTED;
   for (const PeerMeta& m : metas)
     if (status == TNCCL_SUCCESS && m.ipcMode != metas[0].ipcMode) status = TNCCL_UNSUPPORTED;
+
+  // Locality. Peers on this host are mapped; a ring edge between hosts (every
+  // ring edge with TNCCL_NET=force) is a socket edge. All inputs are
+  // all-gathered or hashed into the configuration, so every rank decides
+  // alike.
+  std::vector<char> local((size_t)nranks);
+  comm->allPeersMapped = true;
+  for (int p = 0; p < nranks; ++p) {
+    local[(size_t)p] = metas[(size_t)p].hostId == metas[(size_t)rank].hostId;
+    comm->allPeersMapped = comm->allPeersMapped && local[(size_t)p];
+  }
+  const int netMode = comm->cfg.netMode;
+  auto socketEdge = [&](int a) {
+    const int b = (a + 1) % nranks;
+    return netMode == 2 || (netMode == 1 && metas[(size_t)a].hostId != metas[(size_t)b].hostId);
+  };
+  for (int q = 0; q < nranks; ++q) comm->net.any = comm->net.any || socketEdge(q);
+  comm->net.send = socketEdge(rank);
+  comm->net.recv = socketEdge((rank + nranks - 1) % nranks);
+  if (status == TNCCL_SUCCESS && !comm->allPeersMapped && netMode == 0) {
+    TN_WARN("rank %d: ranks on several hosts need socket edges (TNCCL_NET=auto)", rank);
+    status = TNCCL_UNSUPPORTED;
+  }
   for (int p = 0; p < nranks && status == TNCCL_SUCCESS; ++p)
-    if (p != rank) status = checkPeer(comm.get(), metas[(size_t)p]);
+    if (p != rank && local[(size_t)p]) status = checkPeer(comm.get(), metas[(size_t)p]);
 
   // Every rank takes part in the descriptor all-gather (cuMem mode) even
   // after a local failure, so the collective sequence stays aligned.
@@ -305,11 +341,12 @@ extern "C" tncclResult tncclCommInitRank(tncclComm_t* out, int nranks, tncclUniq
     }
   }
   for (int p = 0; p < nranks && status == TNCCL_SUCCESS; ++p) {
-    if (p == rank) continue;
+    if (p == rank || !local[(size_t)p]) continue;
     status = importPeerMailbox(comm.get(), p, fds[(size_t)p], metas[(size_t)p]);
   }
   for (int fd : fds)
     if (fd >= 0) close(fd);
+  if (status == TNCCL_SUCCESS && comm->net.any) status = netAllocFifos(comm.get());
 
   // Connection status round, then the ready barrier (tiny-nccl
   // src/comm.cc:173-196).
@@ -323,8 +360,9 @@ extern "C" tncclResult tncclCommInitRank(tncclComm_t* out, int nranks, tncclUniq
   }
   status = firstFailure(conns);
 
-  // NVLS only when every rank is connected and capable.
-  bool allNvls = status == TNCCL_SUCCESS;
+  // NVLS only when every rank is connected, on this host and capable (the
+  // multicast handle travels as a descriptor, so not over a TCP bootstrap).
+  bool allNvls = status == TNCCL_SUCCESS && comm->allPeersMapped && !comm->bootstrap.tcp;
   for (const PeerMeta& m : metas) allNvls = allNvls && m.nvlsCapable;
   if (allNvls) {
     r = setupNvls(comm.get());
@@ -335,6 +373,13 @@ extern "C" tncclResult tncclCommInitRank(tncclComm_t* out, int nranks, tncclUniq
     if (r == TNCCL_UNSUPPORTED) TN_INFO("rank %d: NVLS unavailable; using P2P algorithms", rank);
   }
 
+  // Socket edges: connections and proxy (collective; `status` is the same on
+  // every rank here).
+  if (status == TNCCL_SUCCESS && comm->net.any) {
+    r = netStart(comm.get(), metas[0].nonce);
+    if (r != TNCCL_SUCCESS) status = r;
+  }
+
   r = bootstrapBarrier(&comm->bootstrap);
   if (r != TNCCL_SUCCESS) {
     abandonPublished(comm.get());
@@ -342,6 +387,8 @@ extern "C" tncclResult tncclCommInitRank(tncclComm_t* out, int nranks, tncclUniq
   }
   if (status != TNCCL_SUCCESS) {
     tncclResult ignored = TNCCL_SUCCESS;
+    netStopProxy(comm.get(), false, &ignored);
+    netRelease(comm.get(), true);  // host FIFOs: no kernel has run
     nvlsUnmap(comm.get(), &ignored);
     closePeerMailboxes(comm.get(), &ignored);
     tncclResult cleanup = bootstrapBarrier(&comm->bootstrap);
@@ -354,9 +401,9 @@ extern "C" tncclResult tncclCommInitRank(tncclComm_t* out, int nranks, tncclUniq
     return cleanup == TNCCL_SUCCESS ? status : cleanup;
   }
   fillDevComm(comm.get());
-  TN_INFO("rank %d/%d: device %d, ipc %s, mailbox %zu bytes, NVLS %s", rank, nranks,
-          comm->device, comm->ipcMode == kIpcCuMem ? "cuMem" : "legacy", comm->local.bytes,
-          comm->nvls.enabled ? "on" : "off");
+  TN_INFO("rank %d/%d: device %d, ipc %s, mailbox %zu bytes, NVLS %s, socket edges %s", rank,
+          nranks, comm->device, comm->ipcMode == kIpcCuMem ? "cuMem" : "legacy",
+          comm->local.bytes, comm->nvls.enabled ? "on" : "off", comm->net.any ? "yes" : "no");
   *out = comm.release();
   return TNCCL_SUCCESS;
 }
@@ -377,7 +424,11 @@ extern "C" tncclResult tncclCommDestroy(tncclComm_t comm) {
   tncclResult result = TNCCL_SUCCESS;
   if (comm->streamBound && cudaStreamSynchronize(comm->boundStream) != cudaSuccess) {
     // A kernel may still own the mappings: break the control connection so
-    // peers take their bounded error paths; retain device memory.
+    // peers take their bounded error paths; retain device memory and the
+    // socket FIFOs.
+    tncclResult ignored = TNCCL_SUCCESS;
+    netStopProxy(comm, false, &ignored);
+    netRelease(comm, false);
     bootstrapClose(&comm->bootstrap);
     delete comm;
     return TNCCL_CUDA_ERROR;
@@ -394,10 +445,14 @@ extern "C" tncclResult tncclCommDestroy(tncclComm_t comm) {
             comm->rank, corrupted);
   tncclResult b1 = bootstrapBarrier(&comm->bootstrap);  // every kernel has finished
   if (b1 != TNCCL_SUCCESS) result = b1;
+  netStopProxy(comm, b1 == TNCCL_SUCCESS, &result);  // no frame is in flight any more
   nvlsUnmap(comm, &result);
   closePeerMailboxes(comm, &result);
   tncclResult b2 = bootstrapBarrier(&comm->bootstrap);  // every importer has closed
   if (b2 != TNCCL_SUCCESS && result == TNCCL_SUCCESS) result = b2;
+  // This rank's stream is idle and its proxy stopped: nothing touches its
+  // socket FIFOs whatever the barriers returned.
+  netRelease(comm, true);
   if (b1 == TNCCL_SUCCESS && b2 == TNCCL_SUCCESS) {
     nvlsRelease(comm, &result);
     freeLocalMailbox(comm, &result);

@@ -9,6 +9,7 @@
 #include "bootstrap.h"
 #include "common.h"
 #include "devcomm.h"
+#include "net.h"
 #include "tnccl.h"
 
 namespace tnccl {
@@ -70,6 +71,22 @@ struct PeerMeta {
   char uuid[16];
   char busId[32];
   cudaIpcMemHandle_t ipcHandle;
+  uint64_t hostId;      // ranks with equal ids share a host (NVLink / IPC reach)
+  uint64_t nonce;       // rank 0's random communicator nonce (socket hellos)
+};
+
+// This rank's socket ring edges (TNCCL_NET) and their proxy.
+struct NetState {
+  bool any = false;   // some ring edge of the communicator is a socket edge
+  bool send = false;  // this rank's edge to rank + 1
+  bool recv = false;  // this rank's edge from rank - 1
+  NetFifoLayout layout{};
+  char* sendHost = nullptr;  // cudaHostAlloc'd FIFOs (host views)
+  char* recvHost = nullptr;
+  char* sendDev = nullptr;   // their device views
+  char* recvDev = nullptr;
+  NetRing ring;
+  NetProxy* proxy = nullptr;
 };
 
 }  // namespace tnccl
@@ -86,6 +103,8 @@ struct tncclComm {
   tnccl::LocalMailbox local;
   tnccl::PeerMailbox peers[tnccl::kMaxRanks];
   tnccl::NvlsState nvls;
+  tnccl::NetState net;
+  bool allPeersMapped = true;  // every peer is on this host and mapped
   tnccl::DevComm dev{};
   uint64_t* counters = nullptr;
   uint64_t* diagWord = nullptr;  // device word that nothing writes (self tests)
@@ -119,6 +138,24 @@ tncclAlgo_t selectAlgo(const tncclComm* comm, uint64_t bytes);
 
 // comm.cc: mailbox canary regions that were overwritten.
 tncclResult countBadCanaries(tncclComm* comm, int* corrupted);
+
+// net_setup.cc: socket ring edges of a communicator.
+// Hash of this host's identity (hostname and kernel boot id; TNCCL_HOST_ID
+// overrides it, which lets one machine act as several hosts).
+uint64_t hostIdentity();
+// Sets the socket FIFO layout (every rank of a communicator with socket
+// edges: it caps the ring's channels) and allocates and initialises the
+// host-mapped FIFOs of this rank's own socket edges (local; before the
+// connection status round).
+tncclResult netAllocFifos(tncclComm* comm);
+// Connects the socket edges (collective) and starts the proxy.
+tncclResult netStart(tncclComm* comm, uint64_t nonce);
+// Stops and joins the proxy (close frames first when `graceful`; a proxy
+// failure then lands in *result).
+void netStopProxy(tncclComm* comm, bool graceful, tncclResult* result);
+// Closes the connections; frees the FIFOs when `freeFifos` (no kernel of
+// this rank can touch them any more).
+void netRelease(tncclComm* comm, bool freeFifos);
 
 // Launch counter shared by every kernel launch in the library.
 extern std::atomic<unsigned long long> gLaunchCount;

@@ -63,6 +63,13 @@ int parseAlgo(const std::string& s) {
   return -1;
 }
 
+int parseNetMode(const std::string& s) {
+  if (s.empty() || strcasecmp(s.c_str(), "auto") == 0 || s == "1") return 1;
+  if (strcasecmp(s.c_str(), "off") == 0 || s == "0") return 0;
+  if (strcasecmp(s.c_str(), "force") == 0 || s == "2") return 2;
+  return -1;
+}
+
 static int clampInt(int64_t v, int lo, int hi) {
   return (int)(v < lo ? lo : v > hi ? hi : v);
 }
@@ -120,6 +127,15 @@ Config loadConfig() {
   // fixed cost that short per-peer pieces do not amortise.
   c.stageMinBytes = clampInt(envInt("TNCCL_STAGE_MIN_BYTES", 1 << 30), 0, 1 << 30);
   c.tuning = loadTuningTable();
+  c.netMode = parseNetMode(envStr("TNCCL_NET", "auto"));
+  if (c.netMode < 0) {
+    TN_WARN("unknown TNCCL_NET (want off, auto or force); using auto");
+    c.netMode = 1;
+  }
+  c.netChannels = clampInt(envInt("TNCCL_NET_CHANNELS", 2), 1, 8);
+  c.netIf = envStr("TNCCL_NET_IF", "");
+  c.netSockBuf = clampInt(envInt("TNCCL_NET_SOCKBUF", 0), 0, 1 << 30);
+  c.netSpinUs = clampInt(envInt("TNCCL_NET_SPIN_US", 200), 0, 1000000);
   return c;
 }
 
@@ -158,6 +174,9 @@ uint64_t configHash(const Config& c) {
   mix(c.useCuMem);
   mix(c.oneShotMaxBytes);
   mix(c.nvlsMinBytes);
+  // Which ring edges are socket edges, and the ring channels they carry.
+  mix(c.netMode);
+  mix(c.netChannels);
   // Every rank must pick the same algorithm for a message.
   for (const TuningEntry& e : c.tuning.entries) {
     mix(e.nranks);

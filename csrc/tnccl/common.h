@@ -82,6 +82,13 @@ struct Config {
   int nvlsStage;             // TNCCL_NVLS_STAGE bytes (default 48 KiB)
   int stageMinBytes;         // TNCCL_STAGE_MIN_BYTES (default 1 GiB: staging off)
   TuningTable tuning;        // TNCCL_TUNING_FILE (empty: built-in AUTO rule)
+  // Socket ring edges (net.h). TNCCL_NET: "off", "auto" (edges between
+  // ranks on different hosts) or "force" (every ring edge, also on one host).
+  int netMode;               // 0 off, 1 auto, 2 force
+  int netChannels;           // TNCCL_NET_CHANNELS: ring channels of a socket edge (1..8)
+  std::string netIf;         // TNCCL_NET_IF: IPv4 address to listen on ("": derived)
+  int netSockBuf;            // TNCCL_NET_SOCKBUF: SO_SNDBUF / SO_RCVBUF (0: system)
+  int netSpinUs;             // TNCCL_NET_SPIN_US: proxy busy-poll window
 };
 
 // Loads TNCCL_TUNING_FILE when set (a missing or malformed file warns and
@@ -98,7 +105,7 @@ void adaptConfig(Config& c, int nranks);
 uint64_t configHash(const Config& c);
 
 int parseAlgo(const std::string& s);
-
-
+// "off" / "auto" / "force" (or 0 / 1 / 2); -1 when malformed.
+int parseNetMode(const std::string& s);
 
 }  // namespace tnccl

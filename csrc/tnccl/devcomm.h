@@ -57,6 +57,12 @@ struct DevComm {
   uint32_t nvlsStage;
   // Copies of fewer bytes per source than this go through registers.
   uint32_t stageMinBytes;
+  // Socket ring edges (TNCCL_NET): device views of the host-mapped FIFOs
+  // this rank's ring kernel shares with its proxy thread (layout netLayout);
+  // null where the edge to rank + 1 / from rank - 1 is an NVLink edge.
+  char* netSend;
+  char* netRecv;
+  NetFifoLayout netLayout;
 };
 
 // Tag of one trace record: algorithm family, phase, tile index (low 16 bits).

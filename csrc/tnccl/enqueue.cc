@@ -51,6 +51,10 @@ void bindStream(tncclComm* comm, cudaStream_t stream) {
 }  // namespace
 
 tncclAlgo_t selectAlgo(const tncclComm* comm, uint64_t bytes) {
+  // With socket edges only the ring carries data between every neighbour;
+  // on one host (TNCCL_NET=force) a forced algorithm still runs over NVLink.
+  if (comm->net.any && (!comm->allPeersMapped || comm->cfg.forcedAlgo == TNCCL_ALGO_AUTO))
+    return TNCCL_ALGO_RING;
   if (comm->cfg.forcedAlgo != TNCCL_ALGO_AUTO) {
     if (comm->cfg.forcedAlgo == TNCCL_ALGO_NVLS && !comm->nvls.enabled) return TNCCL_ALGO_TWOSHOT;
     return (tncclAlgo_t)comm->cfg.forcedAlgo;
@@ -119,6 +123,8 @@ extern "C" tncclResult tncclAllReduceEx(const void* send, void* recv, size_t cou
 
   tncclAlgo_t chosen = algo == TNCCL_ALGO_AUTO ? selectAlgo(comm, bytes) : algo;
   if (chosen == TNCCL_ALGO_NVLS && !comm->nvls.enabled) return TNCCL_UNSUPPORTED;
+  // The all-peer algorithms need every peer mapped.
+  if (chosen != TNCCL_ALGO_RING && !comm->allPeersMapped) return TNCCL_UNSUPPORTED;
 
   AllReduceArgs a{};
   a.send = send;
@@ -133,10 +139,14 @@ extern "C" tncclResult tncclAllReduceEx(const void* send, void* recv, size_t cou
     return comm->maxChannels > 0 && comm->maxChannels < channels ? comm->maxChannels : channels;
   };
   switch (chosen) {
-    case TNCCL_ALGO_RING:
-      a.chunk = makeChunkPlan(count, comm->nranks, cap(cfg.channels),
-                              (uint64_t)cfg.ringChunkBytes / es, kRingMinChunkBytes / es, V);
+    case TNCCL_ALGO_RING: {
+      // Socket edges carry the first net.layout.channels channels only.
+      int ch = cap(cfg.channels);
+      if (comm->net.any && ch > comm->net.layout.channels) ch = comm->net.layout.channels;
+      a.chunk = makeChunkPlan(count, comm->nranks, ch, (uint64_t)cfg.ringChunkBytes / es,
+                              kRingMinChunkBytes / es, V);
       break;
+    }
     case TNCCL_ALGO_TWOSHOT:
       a.chunk = makeChunkPlan(count, comm->nranks, cap(cfg.channels),
                               (uint64_t)cfg.tsChunkBytes / es, kTwoShotMinChunkBytes / es, V);

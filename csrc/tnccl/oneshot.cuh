@@ -15,7 +15,6 @@ using namespace dev;
 template <typename T, int MAXP>
 __device__ __forceinline__ void oneShotBody(const DevComm& comm, const AllReduceArgs& a,
                                             const int c) {
-  constexpr int V = Pack<T>::V;
   constexpr int U = MAXP <= 2 ? 4 : MAXP <= 4 ? 2 : 1;
   const int tid = threadIdx.x, P = comm.nranks, r = comm.rank;
   const Team cta = wholeCta();

@@ -11,44 +11,59 @@ using namespace dev;
 
 // ---------------------------------------------------------------------------
 // Ring (per-channel FIFO with ready words in the consumer and credit words in
-// the producer, both polled locally).
+// the producer, both polled locally). Each edge is a RingFifo: over NVLink
+// it is made of the two mailboxes; a socket edge (TNCCL_NET) is a host-mapped
+// FIFO that the rank's proxy thread moves over TCP, where the producer also
+// writes each slot's payload size.
 // ---------------------------------------------------------------------------
-template <typename T>
+template <typename T, bool NET>
 struct RingChannel {
   const DevComm* comm;
-  int c, S, next, prev;
+  int c, next, prev;
   char* me;
   uint64_t sendT, recvT;
 
-  __device__ char* outSlot(uint64_t t) const {
-    return comm->peers[next] + ringDataAt(comm->layout, c, (int)(t % (uint64_t)S));
+  // The two edges, rebuilt from the launch parameters at each use (cheaper in
+  // registers than keeping them). NET = false compiles the NVLink-only ring.
+  __device__ RingFifo out() const {
+    return NET && comm->netSend ? netRingFifo(comm->netSend, comm->netLayout)
+                                : nvlinkRingFifo(comm->peers[next], me, comm->layout);
   }
+  __device__ RingFifo in() const {
+    return NET && comm->netRecv ? netRingFifo(comm->netRecv, comm->netLayout)
+                                : nvlinkRingFifo(me, comm->peers[prev], comm->layout);
+  }
+  __device__ char* outSlot(uint64_t t) const { return ringFifoData(out(), c, t); }
   __device__ const T* inSlot(uint64_t t) const {
-    return reinterpret_cast<const T*>(me + ringDataAt(comm->layout, c, (int)(t % (uint64_t)S)));
+    return reinterpret_cast<const T*>(ringFifoData(in(), c, t));
   }
   // Thread 0 waits; the caller passes bar.sync before using the slots.
   __device__ bool waitSend(int phase) const {
-    return waitFlag(*comm, flagPtr(me, ringCreditAt(comm->layout, c, (int)(sendT % (uint64_t)S))),
-                    sendT, whereCode(kCounterRing, c, phase));
+    const RingFifo f = out();
+    return waitFlag(*comm, f.credit + ringFifoIndex(f, c, sendT), sendT,
+                    whereCode(kCounterRing, c, phase));
   }
   __device__ bool waitRecv(int phase) const {
-    return waitFlag(*comm, flagPtr(me, ringReadyAt(comm->layout, c, (int)(recvT % (uint64_t)S))),
-                    recvT + 1, whereCode(kCounterRing, c, phase));
+    const RingFifo f = in();
+    return waitFlag(*comm, f.ready + ringFifoIndex(f, c, recvT), recvT + 1,
+                    whereCode(kCounterRing, c, phase));
   }
   // Called by thread 0 after bar.sync.
-  __device__ void publishSend() {
-    stReleaseSys(flagPtr(comm->peers[next], ringReadyAt(comm->layout, c, (int)(sendT % (uint64_t)S))),
-                 sendT + 1);
+  __device__ void publishSend(uint64_t bytes) {
+    const RingFifo f = out();
+    const uint64_t i = ringFifoIndex(f, c, sendT);
+    if (NET && f.bytes) f.bytes[i] = bytes;  // ordered by the release below
+    stReleaseSys(f.ready + i, sendT + 1);
     ++sendT;
   }
   __device__ void releaseRecv() {
-    stReleaseSys(flagPtr(comm->peers[prev], ringCreditAt(comm->layout, c, (int)(recvT % (uint64_t)S))),
-                 recvT + (uint64_t)S);
+    const RingFifo f = in();
+    stReleaseSys(f.credit + ringFifoIndex(f, c, recvT), recvT + (uint64_t)f.slots);
     ++recvT;
   }
 };
 
-template <typename T>
+template <typename T, bool NET>
 __device__ __forceinline__ void ringBody(const DevComm& comm, const AllReduceArgs& a,
                                          const int c) {
   using Pk = Pack<T>;
@@ -63,14 +78,19 @@ __device__ __forceinline__ void ringBody(const DevComm& comm, const AllReduceArg
   const bool scale = alpha != 1.0f;
   __shared__ int sFail;
   if (tid == 0) sFail = 0;
-  RingChannel<T> ch;
+  RingChannel<T, NET> ch;
   ch.comm = &comm;
   ch.c = c;
-  ch.S = comm.layout.ringSlots;
   ch.next = (r + 1) % P;
   ch.prev = (r + P - 1) % P;
   ch.me = comm.peers[r];
   ch.sendT = ch.recvT = comm.counters[kCounterRing * kMaxChannels + c];
+  // A socket edge provisions netLayout.channels channels (the host caps the
+  // plan to them); a launch beyond them would write outside its FIFO.
+  if (NET && tid == 0 && (comm.netSend || comm.netRecv) && c >= comm.netLayout.channels) {
+    recordFailure(comm, 1 /* TNCCL_INVALID_ARGUMENT */, whereCode(kCounterRing, c, 0), 0, 0);
+    sFail = 1;
+  }
   __syncthreads();
 
   // Wait helpers: `needRecv` / `needSend` select which FIFO ends to acquire.
@@ -84,11 +104,13 @@ __device__ __forceinline__ void ringBody(const DevComm& comm, const AllReduceArg
     __syncthreads();
     return sFail == 0;
   };
-  auto finish = [&](bool recvDone, bool sendDone) {
+  // sendElems: elements of T in the slot just written (socket edges carry
+  // exactly those bytes).
+  auto finish = [&](bool recvDone, bool sendDone, uint64_t sendElems) {
     __syncthreads();
     if (tid == 0) {
       if (recvDone) ch.releaseRecv();
-      if (sendDone) ch.publishSend();
+      if (sendDone) ch.publishSend(sendElems * sizeof(T));
     } else {
       if (recvDone) ++ch.recvT;
       if (sendDone) ++ch.sendT;
@@ -105,7 +127,7 @@ __device__ __forceinline__ void ringBody(const DevComm& comm, const AllReduceArg
       char* out = ch.outSlot(ch.sendT);
       copyOut<T, kLdInput, 8>(cta, x + sp.offset, sp.count, vec, scale, alpha, 1,
                               [out](int) { return out; });
-      finish(false, true);
+      finish(false, true, sp.count);
     }
     // recv + reduce + send for distances 2..P-1.
     bool ok = true;
@@ -118,7 +140,7 @@ __device__ __forceinline__ void ringBody(const DevComm& comm, const AllReduceArg
           cta, sp.count, vec, in, x + sp.offset, alpha,
           [&](uint64_t i, uint4 v) { st16(reinterpret_cast<uint4*>(out) + i, v); },
           [&](uint64_t e, float f) { stElem(reinterpret_cast<T*>(out) + e, f); });
-      finish(true, true);
+      finish(true, true, sp.count);
     }
     if (!ok) break;
     // Final reduce-scatter step: y[chunk r] = in + a*x, stored and forwarded.
@@ -138,7 +160,7 @@ __device__ __forceinline__ void ringBody(const DevComm& comm, const AllReduceArg
             stElem(yo + e, f);
             stElem(reinterpret_cast<T*>(out) + e, f);
           });
-      finish(true, true);
+      finish(true, true, sp.count);
     }
     // All-gather: recv + store + forward for distances 1..P-2, then store.
     for (int d = 1; d < P - 1 && ok; ++d) {
@@ -150,7 +172,7 @@ __device__ __forceinline__ void ringBody(const DevComm& comm, const AllReduceArg
       copyOut<T, kLdMailbox, 8>(cta, in, sp.count, vec, false, 1.f, 2, [&](int k) {
         return k == 0 ? reinterpret_cast<char*>(yo) : out;
       });
-      finish(true, true);
+      finish(true, true, sp.count);
     }
     if (!ok) break;
     {
@@ -159,7 +181,7 @@ __device__ __forceinline__ void ringBody(const DevComm& comm, const AllReduceArg
       T* yo = y + sp.offset;
       copyOut<T, kLdMailbox, 8>(cta, ch.inSlot(ch.recvT), sp.count, vec, false, 1.f, 1,
                                 [yo](int) { return reinterpret_cast<char*>(yo); });
-      finish(true, false);
+      finish(true, false, 0);
     }
   }
   if (tid == 0 && !sFail) comm.counters[kCounterRing * kMaxChannels + c] = ch.sendT;

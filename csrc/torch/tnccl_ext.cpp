@@ -164,6 +164,9 @@ class Communicator {
     d["nvls_bytes"] = (uint64_t)info_.nvlsBytes;
     d["oneshot_max_bytes"] = (uint64_t)info_.sizeThresholds[0];
     d["nvls_min_bytes"] = (uint64_t)info_.sizeThresholds[1];
+    d["socket_send_edge"] = (bool)info_.netSendSocket;
+    d["socket_recv_edge"] = (bool)info_.netRecvSocket;
+    d["socket_channels"] = info_.netChannels;
     return d;
   }
 

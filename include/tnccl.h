@@ -8,7 +8,9 @@
  * change).
  *
  * Contract (same as tiny-nccl unless stated):
- *  - One process per GPU, one rank per process, all ranks on one host.
+ *  - One process per GPU, one rank per process. Ranks on several hosts
+ *    (TNCCL_BOOTSTRAP_ADDR for the rendezvous) are linked by socket ring edges
+ *    (TNCCL_NET); such a communicator runs the ring algorithm only.
  *  - tncclCommInitRank and tncclCommDestroy are blocking collectives when
  *    nranks > 1: every rank calls them, in the same order.
  *  - The communicator captures the CUDA device that is current at init and is
@@ -147,6 +149,9 @@ typedef struct {
   size_t ringMinChunkBytes; /* smallest ring chunk the planner uses */
   int oneShotChannels;
   int nvlsChannels;
+  int netSendSocket;        /* 1: this rank's ring edge to rank + 1 is a socket edge */
+  int netRecvSocket;        /* 1: its ring edge from rank - 1 is a socket edge */
+  int netChannels;          /* ring channels when the communicator has socket edges */
 } tncclCommInfo;
 
 tncclResult tncclCommGetInfo(tncclComm_t comm, tncclCommInfo* info);

@@ -1,9 +1,9 @@
-// bootstrap_test.cc - CPU-only tests of the AF_UNIX control plane with
-// forked ranks (no GPU): id codec, rendezvous, all-gather, barrier,
+// bootstrap_test.cc - CPU-only tests of the AF_UNIX and TCP control plane
+// with forked ranks (no GPU): id codecs, rendezvous, all-gather, barrier,
 // descriptor passing, and the failure paths (bad id, nranks mismatch,
 // duplicate rank, missing rank, peer death, configuration mismatch, ranks
-// out of step). Every failure is made on the host; every wait is bounded by
-// the bootstrap deadline.
+// out of step, a TCP rank of another communicator). Every failure is made on
+// the host; every wait is bounded by the bootstrap deadline.
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
@@ -16,6 +16,7 @@
 #include <vector>
 
 #include "bootstrap.h"
+#include "sockio.h"
 
 using namespace tnccl;
 
@@ -217,6 +218,89 @@ void testOutOfStep() {
   report("ranks out of step", codes[0] != 0 && codes[1] != 0);
 }
 
+// ---- TCP rendezvous --------------------------------------------------------
+
+int freePort() {
+  int port = 0;
+  int fd = tcpListen("127.0.0.1", 0, 1, &port);
+  if (fd >= 0) close(fd);
+  return port;
+}
+
+void testTcpIdCodec() {
+  tncclUniqueId id{};
+  bool ok = bootstrapNewTcpId(&id, "127.0.0.1", 29500) == TNCCL_SUCCESS;
+  uint32_t ip = 0;
+  int port = 0;
+  uint64_t nonce = 0, nonce2 = 0;
+  char path[108];
+  ok = ok && bootstrapDecodeTcpId(id, &ip, &port, &nonce) && port == 29500 && nonce != 0;
+  ok = ok && !bootstrapDecodeId(id, path);  // not an AF_UNIX id
+  tncclUniqueId id2{};
+  ok = ok && bootstrapNewTcpId(&id2, "127.0.0.1", 29500) == TNCCL_SUCCESS &&
+       bootstrapDecodeTcpId(id2, &ip, &port, &nonce2) && nonce2 != nonce;
+  tncclUniqueId un{};
+  ok = ok && bootstrapNewId(&un) == TNCCL_SUCCESS && !bootstrapDecodeTcpId(un, &ip, &port, &nonce);
+  ok = ok && bootstrapNewTcpId(&id, "not-an-address", 29500) == TNCCL_INVALID_ARGUMENT;
+  ok = ok && bootstrapNewTcpId(&id, "127.0.0.1", 0) == TNCCL_INVALID_ARGUMENT;
+  ok = ok && bootstrapNewTcpId(&id, "127.0.0.1", 70000) == TNCCL_INVALID_ARGUMENT;
+  // Through the environment, as tncclGetUniqueId does.
+  setenv("TNCCL_BOOTSTRAP_ADDR", "127.0.0.1:29501", 1);
+  ok = ok && bootstrapNewId(&id) == TNCCL_SUCCESS && bootstrapDecodeTcpId(id, &ip, &port, &nonce) &&
+       port == 29501;
+  setenv("TNCCL_BOOTSTRAP_ADDR", "127.0.0.1", 1);  // no port
+  ok = ok && bootstrapNewId(&id) == TNCCL_INVALID_ARGUMENT;
+  unsetenv("TNCCL_BOOTSTRAP_ADDR");
+  report("tcp id codec", ok);
+}
+
+void testTcpRendezvous(int P) {
+  tncclUniqueId id{};
+  bootstrapNewTcpId(&id, "127.0.0.1", freePort());
+  auto codes = forkRanks(P, [&](int r) -> int {
+    Bootstrap b;
+    if (bootstrapOpen(&b, id, P, r, 42, 5000) != TNCCL_SUCCESS) return 10;
+    if (!b.tcp) return 11;
+    int64_t mine[2] = {r, 5 * r + 3};
+    std::vector<int64_t> all((size_t)P * 2);
+    if (bootstrapAllGather(&b, mine, all.data(), sizeof(mine)) != TNCCL_SUCCESS) return 12;
+    for (int p = 0; p < P; ++p)
+      if (all[(size_t)p * 2] != p || all[(size_t)p * 2 + 1] != 5 * p + 3) return 13;
+    if (bootstrapBarrier(&b) != TNCCL_SUCCESS) return 14;
+    // Descriptor passing needs AF_UNIX: every rank gets the same answer and
+    // the collective sequence stays aligned.
+    std::vector<int> fds((size_t)P, -1);
+    if (bootstrapAllGatherFds(&b, 0, fds.data()) != TNCCL_UNSUPPORTED) return 15;
+    int got = -1;
+    if (bootstrapBroadcastFd(&b, 0, &got) != TNCCL_UNSUPPORTED) return 16;
+    if (bootstrapAllGather(&b, mine, all.data(), sizeof(mine)) != TNCCL_SUCCESS) return 17;
+    if (bootstrapBarrier(&b) != TNCCL_SUCCESS) return 18;
+    bootstrapClose(&b);
+    return 0;
+  });
+  bool ok = true;
+  for (int c : codes) ok = ok && c == 0;
+  char name[64];
+  snprintf(name, sizeof(name), "tcp rendezvous P=%d", P);
+  report(name, ok);
+  if (!ok)
+    for (size_t i = 0; i < codes.size(); ++i) printf("  rank %zu exit %d\n", i, codes[i]);
+}
+
+void testTcpNonceMismatch() {
+  // Two ids for the same address: a rank holding the other id is refused.
+  const int port = freePort();
+  tncclUniqueId a{}, b2{};
+  bootstrapNewTcpId(&a, "127.0.0.1", port);
+  bootstrapNewTcpId(&b2, "127.0.0.1", port);
+  auto codes = forkRanks(2, [&](int r) -> int {
+    Bootstrap b;
+    return (int)bootstrapOpen(&b, r == 0 ? a : b2, 2, r, 1, 3000);
+  });
+  report("tcp nonce mismatch", codes[0] == TNCCL_INVALID_ARGUMENT &&
+                                   codes[1] == TNCCL_INVALID_ARGUMENT);
+}
+
 }  // namespace
 
 int main() {
@@ -229,6 +313,9 @@ int main() {
   testMissingRank();
   testPeerDeath();
   testOutOfStep();
+  testTcpIdCodec();
+  for (int P : {2, 4}) testTcpRendezvous(P);
+  testTcpNonceMismatch();
   printf("bootstrap_test: %s\n", gFailed ? "FAIL" : "PASS");
   return gFailed ? 1 : 0;
 }
