@@ -8,6 +8,10 @@ using namespace tnccl;
 
 extern "C" tncclResult tncclGetUniqueId(tncclUniqueId* id) { return bootstrapNewId(id); }
 
+extern "C" tncclResult tncclGetUniqueIdTcp(tncclUniqueId* id, const char* ipv4, int port) {
+  return bootstrapNewTcpId(id, ipv4, port);
+}
+
 extern "C" const char* tncclGetErrorString(tncclResult result) {
   switch (result) {
     case TNCCL_SUCCESS:

@@ -266,6 +266,12 @@ py::bytes getUniqueId() {
   return py::bytes(reinterpret_cast<const char*>(id.bytes), sizeof(id.bytes));
 }
 
+py::bytes getUniqueIdTcp(const std::string& ipv4, int port) {
+  tncclUniqueId id;
+  check(tncclGetUniqueIdTcp(&id, ipv4.c_str(), port), "tncclGetUniqueIdTcp");
+  return py::bytes(reinterpret_cast<const char*>(id.bytes), sizeof(id.bytes));
+}
+
 }  // namespace
 
 void registerOps(py::module_& m);  // ops_ext.cpp
@@ -303,6 +309,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("async_error", &Emulator::asyncError)
       .def("destroy", &Emulator::destroy);
   m.def("get_unique_id", &getUniqueId);
+  m.def("get_unique_id_tcp", &getUniqueIdTcp);
   m.def("launch_count", []() { return tncclGetLaunchCount(); });
   m.def("error_string", [](int r) { return std::string(tncclGetErrorString((tncclResult)r)); });
   m.def("version", []() {

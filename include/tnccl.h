@@ -185,6 +185,12 @@ tncclResult tncclCommGetAsyncError(tncclComm_t comm, tncclResult* asyncError);
  * valid afterwards. Local only: it does not notify peers. */
 tncclResult tncclCommAbort(tncclComm_t comm);
 
+/* A unique id for a TCP rendezvous: rank 0 listens on ipv4:port (dotted
+ * quad; the address must be rank 0's), the other ranks connect there. Needed
+ * when ranks run on several hosts; tncclGetUniqueId does the same when
+ * TNCCL_BOOTSTRAP_ADDR=<ipv4>:<port> is set. */
+tncclResult tncclGetUniqueIdTcp(tncclUniqueId* id, const char* ipv4, int port);
+
 const char* tncclAlgoName(tncclAlgo_t algo);
 tncclResult tncclGetVersion(int* version);
 

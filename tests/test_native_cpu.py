@@ -20,7 +20,7 @@ def test_c_abi_surface(built):
     names = ["tncclGetUniqueId", "tncclCommInitRank", "tncclAllReduceSumF32", "tncclCommDestroy",
              "tncclGetErrorString", "tncclAllReduce", "tncclAllReduceEx", "tncclCommGetInfo",
              "tncclCommGetAsyncError", "tncclCommAbort", "tncclCommSelectAlgo", "tncclGetVersion",
-             "tncclGetLaunchCount"]
+             "tncclGetLaunchCount", "tncclGetUniqueIdTcp"]
     for n in names:
         assert hasattr(lib, n), n
     lib.tncclGetErrorString.restype = ctypes.c_char_p
@@ -44,6 +44,13 @@ def test_c_abi_surface(built):
     assert lib.tncclCommDestroy(None) == 1
     assert lib.tncclAllReduceSumF32(None, None, 0, None, None) == 1
     assert lib.tncclGetUniqueId(None) == 1
+    # TCP rendezvous ids: address and port are validated.
+    lib.tncclGetUniqueIdTcp.argtypes = [ctypes.POINTER(Uid), ctypes.c_char_p, ctypes.c_int]
+    tcp = Uid()
+    assert lib.tncclGetUniqueIdTcp(ctypes.byref(tcp), b"127.0.0.1", 29500) == 0
+    assert bytes(tcp.bytes[:8]) == b"TNCBT003"
+    assert lib.tncclGetUniqueIdTcp(ctypes.byref(tcp), b"localhost", 29500) == 1
+    assert lib.tncclGetUniqueIdTcp(ctypes.byref(tcp), b"127.0.0.1", 0) == 1
 
 
 def test_bootstrap_forked_ranks(built):
@@ -169,9 +176,30 @@ def test_store_keys_change_per_communicator(monkeypatch):
 
     ids = iter([b"first", b"second"])
     monkeypatch.setattr(C, "Communicator", FakeComm)
-    monkeypatch.setattr(C, "get_unique_id", lambda: next(ids))
+    monkeypatch.setattr(C, "get_unique_id", lambda bootstrap_addr=None: next(ids))
     store = Store()
     C.init_from_store(store, 0, 2)
     C.init_from_store(store, 0, 2)
     assert len(store) == 2 and sorted(store.values()) == [b"first", b"second"]
     assert C._store_key("explicit") == "explicit"
+
+
+def test_tcp_rendezvous_ids_and_default_address(built):
+    import tiny_nccl_b200 as tn
+
+    a, b = tn.get_unique_id("127.0.0.1:29500"), tn.get_unique_id("127.0.0.1:29500")
+    assert len(a) == 128 and a[:8] == b"TNCBT003" and a != b  # fresh nonce each time
+    assert tn.get_unique_id()[:8] == b"TNCBB002"  # AF_UNIX path id
+    for bad in ("127.0.0.1", "127.0.0.1:0", ":29500", "127.0.0.1:x"):
+        with pytest.raises(ValueError):
+            tn.get_unique_id(bad)
+    with pytest.raises(RuntimeError):
+        tn.get_unique_id("not-an-ip:29500")
+    one_host = {"WORLD_SIZE": "8", "LOCAL_WORLD_SIZE": "8", "MASTER_ADDR": "127.0.0.1",
+                "MASTER_PORT": "29400"}
+    assert tn.default_bootstrap_addr(one_host) is None
+    two_hosts = dict(one_host, LOCAL_WORLD_SIZE="4")
+    assert tn.default_bootstrap_addr(two_hosts) == "127.0.0.1:29401"
+    assert tn.default_bootstrap_addr(dict(two_hosts, TNCCL_BOOTSTRAP_PORT="31000")) == \
+        "127.0.0.1:31000"
+    assert tn.default_bootstrap_addr({"WORLD_SIZE": "1"}) is None

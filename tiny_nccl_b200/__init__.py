@@ -6,8 +6,9 @@
 * ``tiny_nccl_b200.utils``    - device timing and clock sampling.
 """
 from ._native import library_path, load
-from .parallel import (Communicator, TncclHookState, get_unique_id, init_from_store,
-                       init_from_torch_distributed, register_tnccl_hook, tnccl_allreduce_hook)
+from .parallel import (Communicator, TncclHookState, default_bootstrap_addr, get_unique_id,
+                       init_from_store, init_from_torch_distributed, register_tnccl_hook,
+                       tnccl_allreduce_hook)
 
 __version__ = "1.0.0"
 
@@ -18,7 +19,7 @@ def launch_count() -> int:
 
 
 __all__ = [
-    "Communicator", "get_unique_id", "init_from_store", "init_from_torch_distributed",
-    "TncclHookState", "register_tnccl_hook", "tnccl_allreduce_hook", "launch_count", "load",
+    "Communicator", "default_bootstrap_addr", "get_unique_id", "init_from_store",
+    "init_from_torch_distributed", "TncclHookState", "register_tnccl_hook", "tnccl_allreduce_hook", "launch_count", "load",
     "library_path", "__version__",
 ]

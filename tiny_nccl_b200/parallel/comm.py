@@ -8,9 +8,14 @@ over NVLink through the library's mailboxes.
 
 Mirrors tiny-nccl's ``tncclGetUniqueId`` / ``tncclCommInitRank`` /
 ``tncclAllReduceSumF32`` / ``tncclCommDestroy`` (include/tnccl.h:25-51) with
-dtype, pre-scale and algorithm choice added.
+dtype, pre-scale and algorithm choice added. Ranks on several hosts meet
+through a TCP rendezvous (``bootstrap_addr``) and are linked by socket ring
+edges (``TNCCL_NET``).
 """
 from __future__ import annotations
+
+import os
+import socket
 
 import torch
 
@@ -19,9 +24,39 @@ from .._native import load
 ALGOS = ("auto", "ring", "oneshot", "twoshot", "nvls")
 
 
-def get_unique_id() -> bytes:
-    """128-byte rendezvous id (same role as tncclGetUniqueId)."""
-    return load().get_unique_id()
+def _split_addr(addr: str) -> tuple[str, int]:
+    host, sep, port = addr.rpartition(":")
+    if not sep or not host or not port.isdigit() or not 0 < int(port) < 65536:
+        raise ValueError(f"bootstrap address must be <ipv4>:<port>, got {addr!r}")
+    return host, int(port)
+
+
+def get_unique_id(bootstrap_addr: str | None = None) -> bytes:
+    """128-byte rendezvous id (same role as tncclGetUniqueId).
+
+    With ``bootstrap_addr="<ipv4>:<port>"`` the id names a TCP rendezvous
+    where rank 0 listens at that address (ranks on several hosts,
+    tncclGetUniqueIdTcp); otherwise an AF_UNIX path on this host.
+    """
+    if bootstrap_addr is None:
+        return load().get_unique_id()
+    host, port = _split_addr(bootstrap_addr)
+    return load().get_unique_id_tcp(host, port)
+
+
+def default_bootstrap_addr(env=None) -> str | None:
+    """Rank 0's TCP rendezvous address for a job whose ranks span several
+    hosts (torchrun's ``LOCAL_WORLD_SIZE < WORLD_SIZE``): ``MASTER_ADDR``
+    resolved to IPv4 and ``MASTER_PORT + 1`` (``TNCCL_BOOTSTRAP_PORT``
+    overrides the port). None when every rank is on one host, where the
+    AF_UNIX rendezvous is used."""
+    env = os.environ if env is None else env
+    world = int(env.get("WORLD_SIZE", "1"))
+    local = int(env.get("LOCAL_WORLD_SIZE", str(world)))
+    if local >= world or "MASTER_ADDR" not in env:
+        return None
+    port = int(env.get("TNCCL_BOOTSTRAP_PORT", int(env.get("MASTER_PORT", "29500")) + 1))
+    return f"{socket.gethostbyname(env['MASTER_ADDR'])}:{port}"
 
 
 class Communicator:
@@ -129,24 +164,32 @@ def _store_key(key: str | None) -> str:
 
 
 def init_from_store(store, rank: int, world_size: int, key: str | None = None,
-                    device: int | None = None) -> Communicator:
+                    device: int | None = None,
+                    bootstrap_addr: str | None = None) -> Communicator:
     """Creates a communicator, sharing the unique id through ``store``
-    (anything with ``set(key, bytes)`` and a blocking ``get(key)``)."""
+    (anything with ``set(key, bytes)`` and a blocking ``get(key)``).
+    ``bootstrap_addr`` (rank 0's ``<ipv4>:<port>``) selects a TCP
+    rendezvous, needed when the ranks span several hosts."""
     key = _store_key(key)
     if rank == 0:
-        uid = get_unique_id()
+        uid = get_unique_id(bootstrap_addr)
         store.set(key, uid)
     else:
         uid = bytes(store.get(key))
     return Communicator(uid, world_size, rank, device=device)
 
 
-def init_from_torch_distributed(key: str | None = None,
-                                device: int | None = None) -> Communicator:
-    """Creates a communicator over the ranks of the default process group."""
+def init_from_torch_distributed(key: str | None = None, device: int | None = None,
+                                bootstrap_addr: str | None = None) -> Communicator:
+    """Creates a communicator over the ranks of the default process group.
+    Across hosts the rendezvous is TCP at ``bootstrap_addr``, by default
+    :func:`default_bootstrap_addr` (``MASTER_ADDR``, ``MASTER_PORT + 1``)."""
     import torch.distributed as dist
 
     if not dist.is_initialized():
         raise RuntimeError("torch.distributed is not initialized")
     store = dist.distributed_c10d._get_default_store()
-    return init_from_store(store, dist.get_rank(), dist.get_world_size(), key=key, device=device)
+    if bootstrap_addr is None and dist.get_rank() == 0:
+        bootstrap_addr = default_bootstrap_addr()
+    return init_from_store(store, dist.get_rank(), dist.get_world_size(), key=key, device=device,
+                           bootstrap_addr=bootstrap_addr)
