@@ -67,6 +67,15 @@ __device__ __forceinline__ void acquireFlag(const DevComm& comm, const uint64_t*
     fenceAcqRelSys();
 }
 
+// Debug protocol checks (-DTNCCL_DEVICE_CHECKS=1; off by default): plan
+// capacities at kernel entry and exact sequence numbers on the ring's FIFO
+// words. A failed check records TNCCL_SYSTEM_ERROR with this bit set in the
+// where-code phase.
+#ifndef TNCCL_DEVICE_CHECKS
+#define TNCCL_DEVICE_CHECKS 0
+#endif
+constexpr int kCheckPhase = 0x80;
+
 static __device__ __noinline__ void recordFailure(const DevComm& comm, int code, int where,
                                            uint64_t expected, uint64_t observed) {
   DevStatus* s = comm.status;

@@ -260,6 +260,26 @@ __device__ __forceinline__ bool haveSmem(const DevComm& comm, uint32_t need, int
   return false;
 }
 
+// Debug builds (-DTNCCL_DEVICE_CHECKS=1) check every launch's plan against the
+// mailbox capacities at kernel entry: a chunk or tile must fit its slot and
+// the channel must be provisioned. On failure thread 0 records
+// TNCCL_SYSTEM_ERROR with the check bit in the where-code phase
+// (kCheckPhase; expected = capacity, observed = need) and every thread of the
+// CTA returns; the other CTAs' waits see the error. Release builds compile
+// the check away.
+__device__ __forceinline__ bool planFits(const DevComm& comm, uint64_t needBytes,
+                                         uint64_t slotBytes, int channel, int channels,
+                                         int family) {
+#if TNCCL_DEVICE_CHECKS
+  if (needBytes <= slotBytes && channel < channels) return true;
+  if (threadIdx.x == 0)
+    recordFailure(comm, 3, whereCode(family, channel, kCheckPhase), slotBytes, needBytes);
+  return false;
+#else
+  return true;
+#endif
+}
+
 // Copies n (<= MAXSRC) local sources to their destinations: source k holds
 // count(k) elements at src(k) (local memory), destination k is dst(k) (local
 // or a peer's mailbox). The vectors that every source has are streamed

@@ -45,6 +45,7 @@ __global__ void __launch_bounds__(kMaxThreads)
   const bool scale = alpha != 1.0f;
   const uint64_t tb = comm.nvlsTileBytes;
   if (!haveSmem(comm, nvlsSmemBytes(comm), kCounterNvls, c)) return;
+  if (!planFits(comm, pl.tileElems * sizeof(T), tb, c, comm.nvlsChannels, kCounterNvls)) return;
   __shared__ int sFail;
   __shared__ int sTeamFlag[3];
   __shared__ unsigned long long sOut;  // tiles this CTA copied out

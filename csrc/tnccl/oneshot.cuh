@@ -25,6 +25,9 @@ __device__ __forceinline__ void oneShotBody(const DevComm& comm, const AllReduce
   T* y = static_cast<T*>(a.recv);
   const BlockPlan& pl = a.block;
   const bool vec = a.vectorized != 0;
+  if (!planFits(comm, pl.tileElems * sizeof(T), L.osTileBytes, c, L.osChannels,
+                kCounterOneShot))
+    return;
   __shared__ int sFail;
   if (tid == 0) sFail = 0;
   uint64_t seq = comm.counters[kCounterOneShot * kMaxChannels + c];

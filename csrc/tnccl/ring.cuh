@@ -40,13 +40,25 @@ struct RingChannel {
   // Thread 0 waits; the caller passes bar.sync before using the slots.
   __device__ bool waitSend(int phase) const {
     const RingFifo f = out();
-    return waitFlag(*comm, f.credit + ringFifoIndex(f, c, sendT), sendT,
-                    whereCode(kCounterRing, c, phase));
+    return waitExact(f.credit + ringFifoIndex(f, c, sendT), sendT, phase);
   }
   __device__ bool waitRecv(int phase) const {
     const RingFifo f = in();
-    return waitFlag(*comm, f.ready + ringFifoIndex(f, c, recvT), recvT + 1,
-                    whereCode(kCounterRing, c, phase));
+    return waitExact(f.ready + ringFifoIndex(f, c, recvT), recvT + 1, phase);
+  }
+  // A ring FIFO word never runs ahead of its waiter: a credit cannot pass
+  // ticket t before t was sent, a ready word cannot pass t + 1 before t was
+  // credited back. Debug builds check the word equals the target exactly.
+  __device__ bool waitExact(const uint64_t* w, uint64_t target, int phase) const {
+    if (!waitFlag(*comm, w, target, whereCode(kCounterRing, c, phase))) return false;
+#if TNCCL_DEVICE_CHECKS
+    const uint64_t v = ldAcquireSys(w);
+    if (v != target) {
+      recordFailure(*comm, 3, whereCode(kCounterRing, c, phase | kCheckPhase), target, v);
+      return false;
+    }
+#endif
+    return true;
   }
   // Called by thread 0 after bar.sync.
   __device__ void publishSend(uint64_t bytes) {
@@ -90,6 +102,12 @@ __device__ __forceinline__ void ringBody(const DevComm& comm, const AllReduceArg
   if (NET && tid == 0 && (comm.netSend || comm.netRecv) && c >= comm.netLayout.channels) {
     recordFailure(comm, 1 /* TNCCL_INVALID_ARGUMENT */, whereCode(kCounterRing, c, 0), 0, 0);
     sFail = 1;
+  }
+  {
+    const uint64_t cap = minU64(ch.out().chunkBytes, ch.in().chunkBytes);
+    if (!planFits(comm, pl.chunkElems * sizeof(T), cap, c, comm.layout.channels, kCounterRing) &&
+        tid == 0)
+      sFail = 1;
   }
   __syncthreads();
 

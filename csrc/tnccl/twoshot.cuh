@@ -47,6 +47,8 @@ __device__ __forceinline__ void twoShotBody(const DevComm& comm, const AllReduce
   using Pk = Pack<T>;
   const float alpha = a.scale;
   if (!haveSmem(comm, twoShotSmemBytes(comm, MAXP), kCounterTwoShot, c)) return;
+  if (!planFits(comm, pl.chunkElems * sizeof(T), L.tsChunkBytes, c, L.channels, kCounterTwoShot))
+    return;
   __shared__ int sFail;
   __shared__ int sTeamFlag[3];
   __shared__ unsigned long long sGathered;  // tiles the gather team copied out

@@ -203,3 +203,19 @@ def test_tcp_rendezvous_ids_and_default_address(built):
     assert tn.default_bootstrap_addr(dict(two_hosts, TNCCL_BOOTSTRAP_PORT="31000")) == \
         "127.0.0.1:31000"
     assert tn.default_bootstrap_addr({"WORLD_SIZE": "1"}) is None
+
+
+def test_kernels_compile_with_device_checks(tmp_path):
+    """The debug build (TNCCL_DEVICE_CHECKS=1: plan capacities and exact ring
+    sequence numbers checked in the kernels) compiles for sm_100a."""
+    import shutil
+
+    nvcc = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "bin", "nvcc")
+    if not os.path.exists(nvcc) and shutil.which("nvcc") is None:
+        pytest.skip("needs nvcc")
+    cmd = [nvcc if os.path.exists(nvcc) else "nvcc", "-gencode", "arch=compute_100a,code=sm_100a",
+           "-O3", "-std=c++17", "--expt-relaxed-constexpr", "-diag-suppress", "177",
+           "-DTNCCL_DEVICE_CHECKS=1", f"-I{ROOT}/include", f"-I{ROOT}/csrc/tnccl", "-c",
+           os.path.join(ROOT, "csrc", "tnccl", "allreduce.cu"), "-o", str(tmp_path / "ar.o")]
+    r = run(cmd, timeout=900)
+    assert r.returncode == 0, r.stderr[-3000:]

@@ -35,6 +35,10 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CXXFLAGS = ["-O2", "-std=c++17", "-fPIC", "-Wall", "-Wextra", "-Wno-unused-parameter"]
 NVCCFLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC",
                     "--expt-relaxed-constexpr", "-diag-suppress", "177"]
+# TNCCL_DEVICE_CHECKS=1 at build time compiles the kernels' debug protocol
+# checks in (plan capacities, exact ring sequence numbers; device.cuh).
+if os.environ.get("TNCCL_DEVICE_CHECKS") == "1":
+    NVCCFLAGS.append("-DTNCCL_DEVICE_CHECKS=1")
 
 TNCCL_SRC = ROOT / "csrc" / "tnccl"
 OPS_SRC = ROOT / "csrc" / "ops"
