@@ -218,6 +218,47 @@ void testOutOfStep() {
   report("ranks out of step", codes[0] != 0 && codes[1] != 0);
 }
 
+// The largest all-gather (1 MiB per rank) moves far more than a socket
+// buffer holds, so every frame goes through partial reads and writes.
+void testLargeGather(bool tcp) {
+  const int P = 4;
+  const size_t n = (1u << 20) / sizeof(uint32_t);
+  tncclUniqueId id{};
+  if (tcp) {
+    int port = 0;
+    int fd = tcpListen("127.0.0.1", 0, 1, &port);
+    if (fd >= 0) close(fd);
+    bootstrapNewTcpId(&id, "127.0.0.1", port);
+  } else {
+    bootstrapNewId(&id);
+  }
+  auto codes = forkRanks(P, [&](int r) -> int {
+    Bootstrap b;
+    if (bootstrapOpen(&b, id, P, r, 7, 10000) != TNCCL_SUCCESS) return 10;
+    std::vector<uint32_t> mine(n), all(n * P);
+    for (size_t i = 0; i < n; ++i) mine[i] = (uint32_t)(r * 2654435761u + i * 40503u);
+    for (int rep = 0; rep < 2; ++rep) {
+      if (bootstrapAllGather(&b, mine.data(), all.data(), n * sizeof(uint32_t)) != TNCCL_SUCCESS)
+        return 11;
+      for (int p = 0; p < P; ++p)
+        for (size_t i = 0; i < n; i += 997)
+          if (all[(size_t)p * n + i] != (uint32_t)(p * 2654435761u + i * 40503u)) return 12;
+    }
+    // One byte more than the limit is refused on every rank, before any I/O.
+    std::vector<char> big((1u << 20) + 1), bigAll(big.size() * P);
+    if (bootstrapAllGather(&b, big.data(), bigAll.data(), big.size()) != TNCCL_INVALID_ARGUMENT)
+      return 13;
+    if (bootstrapBarrier(&b) != TNCCL_SUCCESS) return 14;
+    bootstrapClose(&b);
+    return 0;
+  });
+  bool ok = true;
+  for (int c : codes) ok = ok && c == 0;
+  report(tcp ? "tcp all-gather 1 MiB/rank" : "all-gather 1 MiB/rank", ok);
+  if (!ok)
+    for (size_t i = 0; i < codes.size(); ++i) printf("  rank %zu exit %d\n", i, codes[i]);
+}
+
 // ---- TCP rendezvous --------------------------------------------------------
 
 int freePort() {
@@ -316,6 +357,8 @@ int main() {
   testTcpIdCodec();
   for (int P : {2, 4}) testTcpRendezvous(P);
   testTcpNonceMismatch();
+  testLargeGather(false);
+  testLargeGather(true);
   printf("bootstrap_test: %s\n", gFailed ? "FAIL" : "PASS");
   return gFailed ? 1 : 0;
 }
