@@ -25,6 +25,7 @@
 
 #include "comm.h"
 #include "driver.h"
+#include "nvtx.h"
 #include "sockio.h"
 
 namespace tnccl {
@@ -227,6 +228,7 @@ extern "C" tncclResult tncclCommInitRank(tncclComm_t* out, int nranks, tncclUniq
                                          int rank) {
   if (out == nullptr || nranks <= 0 || rank < 0 || rank >= nranks) return TNCCL_INVALID_ARGUMENT;
   *out = nullptr;
+  NvtxRange range("tncclCommInitRank %d/%d", rank, nranks);
   if (nranks > kMaxRanks) return TNCCL_UNSUPPORTED;
   std::unique_ptr<tncclComm> comm(new (std::nothrow) tncclComm);
   if (!comm) return TNCCL_SYSTEM_ERROR;
@@ -410,6 +412,7 @@ extern "C" tncclResult tncclCommInitRank(tncclComm_t* out, int nranks, tncclUniq
 
 extern "C" tncclResult tncclCommDestroy(tncclComm_t comm) {
   if (comm == nullptr) return TNCCL_INVALID_ARGUMENT;
+  NvtxRange range("tncclCommDestroy %d/%d", comm->rank, comm->nranks);
   int original = -1;
   if (cudaGetDevice(&original) != cudaSuccess) {
     bootstrapClose(&comm->bootstrap);

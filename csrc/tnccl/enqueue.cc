@@ -13,6 +13,7 @@
 
 #include "comm.h"
 #include "launch.h"
+#include "nvtx.h"
 
 namespace tnccl {
 
@@ -165,6 +166,7 @@ extern "C" tncclResult tncclAllReduceEx(const void* send, void* recv, size_t cou
   if (cudaGetLastError() != cudaSuccess) return TNCCL_CUDA_ERROR;
   TN_TRACE("rank %d: allreduce %zu x %zu B algo %s", comm->rank, count, es,
            tncclAlgoName(chosen));
+  NvtxRange range("tncclAllReduce %s %zu B rank %d", tncclAlgoName(chosen), bytes, comm->rank);
   if (launchAllReduceKernel(comm->dev, a, (int)chosen, cfg.threads, stream) != cudaSuccess)
     return TNCCL_CUDA_ERROR;
   gLaunchCount.fetch_add(1, std::memory_order_relaxed);
