@@ -41,7 +41,8 @@ void clearEnv() {
        {"TNCCL_NCHANNELS", "TNCCL_ONESHOT_CHANNELS", "TNCCL_TWOSHOT_CHUNK_BYTES",
         "TNCCL_NTHREADS", "TNCCL_TWOSHOT_SPLIT", "TNCCL_NVLS_SPLIT", "TNCCL_TWOSHOT_STAGES",
         "TNCCL_TWOSHOT_PUSH_STAGE", "TNCCL_TWOSHOT_REDUCE_STAGE", "TNCCL_STAGE_MIN_BYTES",
-        "TNCCL_ALGO", "TNCCL_TIMEOUT_MS", "TNCCL_ACQUIRE_LOAD", "TNCCL_NVLS_STAGE"})
+        "TNCCL_ALGO", "TNCCL_TIMEOUT_MS", "TNCCL_ACQUIRE_LOAD", "TNCCL_NVLS_STAGE", "TNCCL_NET",
+        "TNCCL_NET_CHANNELS", "TNCCL_NET_IF", "TNCCL_NET_SOCKBUF", "TNCCL_NET_SPIN_US"})
     unsetenv(v);
 }
 
@@ -80,6 +81,39 @@ void defaultsAndOverrides() {
   c = loadConfig();
   check((int64_t)c.tsStages * (c.tsPushStage + c.tsRedStage) <= 227 * 1024 - 256,
         "staging rings fit 227 KiB of shared memory");
+  clearEnv();
+}
+
+void netKnobs() {
+  clearEnv();
+  Config c = loadConfig();
+  check(c.netMode == 1 && c.netChannels == 2 && c.netIf.empty() && c.netSockBuf == 0 &&
+            c.netSpinUs == 200,
+        "socket-edge defaults: auto, 2 channels, derived address");
+  check(parseNetMode("off") == 0 && parseNetMode("AUTO") == 1 && parseNetMode("force") == 2 &&
+            parseNetMode("0") == 0 && parseNetMode("2") == 2 && parseNetMode("") == 1 &&
+            parseNetMode("sometimes") == -1,
+        "parseNetMode");
+  setenv("TNCCL_NET", "force", 1);
+  setenv("TNCCL_NET_CHANNELS", "64", 1);
+  setenv("TNCCL_NET_IF", "10.0.0.7", 1);
+  c = loadConfig();
+  check(c.netMode == 2 && c.netChannels == 8 && c.netIf == "10.0.0.7",
+        "TNCCL_NET=force, channels clamped to 8, TNCCL_NET_IF");
+  setenv("TNCCL_NET", "sometimes", 1);
+  c = loadConfig();
+  check(c.netMode == 1, "malformed TNCCL_NET falls back to auto");
+  Config a = loadConfig(), b = a;
+  b.netMode = 2;
+  check(configHash(a) != configHash(b), "configHash covers the socket-edge mode");
+  b = a;
+  b.netChannels = a.netChannels + 1;
+  check(configHash(a) != configHash(b), "configHash covers the socket-edge channels");
+  b = a;
+  b.netIf = "192.168.0.1";
+  b.netSpinUs = 5;
+  b.netSockBuf = 4096;
+  check(configHash(a) == configHash(b), "configHash ignores per-rank socket knobs");
   clearEnv();
 }
 
@@ -260,6 +294,7 @@ void plans() {
 
 int main() {
   defaultsAndOverrides();
+  netKnobs();
   adaptChunks();
   hashes();
   tuningTables();
