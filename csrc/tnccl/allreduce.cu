@@ -120,12 +120,25 @@ __global__ void __launch_bounds__(kMaxThreads)
   }
 }
 
+// Emulated ranks joined by socket edges (the emulator with TNCCL_NET=force):
+// the ring over host-mapped FIFOs that in-process proxy threads move over
+// loopback TCP. Also cooperative: rank k's CTAs wait for data that rank k-1's
+// CTAs produce.
+template <typename T>
+__global__ void __launch_bounds__(kMaxThreads)
+    emulatedNetRingKernel(const __grid_constant__ EmulatedLaunch e) {
+  ringBody<T, true>(e.comm[blockIdx.y], e.args[blockIdx.y], blockIdx.x);
+}
+
 template <typename T>
 cudaError_t launchEmulatedTyped(const EmulatedLaunch& e, int channels, int threads,
                                 cudaStream_t stream) {
   const dim3 grid((unsigned)channels, (unsigned)e.nranks);
   const dim3 block((unsigned)threads);
   void* args[] = {const_cast<EmulatedLaunch*>(&e)};
+  if (e.algo == TNCCL_ALGO_RING && (e.comm[0].netSend || e.comm[0].netRecv))
+    return cudaLaunchCooperativeKernel((const void*)emulatedNetRingKernel<T>, grid, block, args,
+                                       0, stream);
   const void* fn = e.nranks <= 2   ? (const void*)emulatedKernel<T, 2>
                    : e.nranks <= 4 ? (const void*)emulatedKernel<T, 4>
                                    : (const void*)emulatedKernel<T, 8>;

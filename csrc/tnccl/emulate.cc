@@ -11,7 +11,14 @@
 // peer over NVLink). It serves single-GPU tests of the multi-rank algorithms
 // and ncu profiles of their kernels. NVLS needs a multicast object spanning
 // several GPUs and is not emulated.
+//
+// With TNCCL_NET=force the virtual ranks' ring edges are socket edges: each
+// virtual rank gets host-mapped send / receive FIFOs and a proxy thread, and
+// the edges are loopback TCP connections inside this process; the ring then
+// runs through the same socket path (ringBody<T, true>) as ranks on
+// different hosts.
 #include <string.h>
+#include <unistd.h>
 
 #include <algorithm>
 #include <new>
@@ -20,6 +27,8 @@
 #include "comm.h"
 #include "diag.h"
 #include "launch.h"
+#include "net.h"
+#include "sockio.h"
 
 struct tncclEmu {
   int nranks = 0;
@@ -31,6 +40,12 @@ struct tncclEmu {
   tnccl::DevStatus* hostStatus = nullptr;
   tnccl::DevStatus* devStatus = nullptr;
   tnccl::DevComm dev[tnccl::kMaxEmulatedRanks];
+  // socket edges (TNCCL_NET=force)
+  bool net = false;
+  tnccl::NetFifoLayout netLayout{};
+  std::vector<char*> netSend, netRecv;  // host FIFOs per virtual rank
+  std::vector<tnccl::NetRing> rings;
+  std::vector<tnccl::NetProxy*> proxies;
 };
 
 using namespace tnccl;
@@ -38,6 +53,18 @@ using namespace tnccl;
 namespace {
 
 void freeEmu(tncclEmu* e) {
+  for (tnccl::NetProxy*& p : e->proxies) {
+    if (p) netProxyStop(p, false);
+    delete p;
+    p = nullptr;
+  }
+  for (tnccl::NetRing& r : e->rings) netCloseRing(&r);
+  for (char* f : e->netSend)
+    if (f) cudaFreeHost(f);
+  for (char* f : e->netRecv)
+    if (f) cudaFreeHost(f);
+  e->netSend.clear();
+  e->netRecv.clear();
   for (char* m : e->mailbox)
     if (m) cudaFree(m);
   e->mailbox.clear();
@@ -49,6 +76,82 @@ void freeEmu(tncclEmu* e) {
 
 size_t elemSize(tncclDataType_t t) {
   return t == tncclFloat32 ? 4 : (t == tncclBfloat16 || t == tncclFloat16) ? 2 : 0;
+}
+
+void emuNetFailure(void* arg, tncclResult code) {
+  auto* e = static_cast<tncclEmu*>(arg);
+  auto* err = const_cast<int32_t*>(&e->hostStatus->error);
+  int32_t expected = 0;
+  __atomic_compare_exchange_n(err, &expected, (int32_t)code, false, __ATOMIC_SEQ_CST,
+                              __ATOMIC_SEQ_CST);
+}
+
+// Socket edges between the virtual ranks: FIFOs, loopback connections (edge
+// k -> k+1 is connected, accepted and acknowledged in turn; the listen
+// backlog holds the connections meanwhile) and one proxy per virtual rank.
+tncclResult setupEmuNet(tncclEmu* e) {
+  const int P = e->nranks;
+  NetOptions o;
+  o.channels = e->cfg.netChannels;
+  o.sndBuf = o.rcvBuf = e->cfg.netSockBuf;
+  o.spinUs = e->cfg.netSpinUs;
+  o.timeoutMs = (int)e->cfg.bootstrapTimeoutMs;
+  const NetFifoLayout L =
+      makeNetFifoLayout(o.channels, e->cfg.ringSlots, (uint64_t)e->cfg.ringChunkBytes);
+  e->netLayout = L;
+  e->netSend.assign((size_t)P, nullptr);
+  e->netRecv.assign((size_t)P, nullptr);
+  e->rings.assign((size_t)P, NetRing{});
+  e->proxies.assign((size_t)P, nullptr);
+  auto alloc = [&](char** host, char** dev) -> bool {
+    void* h = nullptr;
+    void* d = nullptr;
+    if (cudaHostAlloc(&h, L.totalBytes, cudaHostAllocMapped | cudaHostAllocPortable) !=
+        cudaSuccess)
+      return false;
+    *host = static_cast<char*>(h);
+    netFifoInit(*host, L);
+    if (cudaHostGetDevicePointer(&d, h, 0) != cudaSuccess) return false;
+    *dev = static_cast<char*>(d);
+    return true;
+  };
+  uint64_t nonce = 0;
+  if (!randomBytes(&nonce, sizeof(nonce))) return TNCCL_SYSTEM_ERROR;
+  uint32_t ip = 0;
+  parseIpv4("127.0.0.1", &ip);
+  for (int k = 0; k < P; ++k) {
+    char* sendDev = nullptr;
+    char* recvDev = nullptr;
+    if (!alloc(&e->netSend[(size_t)k], &sendDev) || !alloc(&e->netRecv[(size_t)k], &recvDev))
+      return TNCCL_CUDA_ERROR;
+    e->dev[k].netSend = sendDev;
+    e->dev[k].netRecv = recvDev;
+    e->dev[k].netLayout = L;
+  }
+  for (int k = 0; k < P; ++k) {
+    const int next = (k + 1) % P;
+    int port = 0;
+    const int lfd = tcpListen("127.0.0.1", 0, o.channels + 4, &port);
+    if (lfd < 0) return TNCCL_SYSTEM_ERROR;
+    NetHello h{kNetHelloMagic, kNetVersion, 0, k, next, nonce, L.chunkBytes, L.slots,
+               o.channels};
+    tncclResult r = netConnectEdge(ip, port, h, o, e->rings[(size_t)k].sendFds, o.timeoutMs);
+    if (r == TNCCL_SUCCESS)
+      r = netAcceptEdge(lfd, h, o, e->rings[(size_t)next].recvFds, o.timeoutMs);
+    if (r == TNCCL_SUCCESS) r = netWaitAcks(e->rings[(size_t)k].sendFds, o.channels, o.timeoutMs);
+    close(lfd);
+    if (r != TNCCL_SUCCESS) return r;
+  }
+  for (int k = 0; k < P; ++k) {
+    e->rings[(size_t)k].channels = o.channels;
+    e->proxies[(size_t)k] = new (std::nothrow) NetProxy;
+    if (e->proxies[(size_t)k] == nullptr) return TNCCL_SYSTEM_ERROR;
+    tncclResult r = netProxyStart(e->proxies[(size_t)k], o, L, e->netSend[(size_t)k],
+                                  e->netRecv[(size_t)k], &e->rings[(size_t)k], emuNetFailure, e);
+    if (r != TNCCL_SUCCESS) return r;
+  }
+  e->net = true;
+  return TNCCL_SUCCESS;
 }
 
 }  // namespace
@@ -138,6 +241,14 @@ extern "C" tncclResult tncclEmuCreate(tncclEmu_t* out, int nranks) {
     dc.nvlsStage = (uint32_t)e->cfg.nvlsStage;
     dc.stageMinBytes = (uint32_t)e->cfg.stageMinBytes;
   }
+  if (e->cfg.netMode == 2) {
+    r = setupEmuNet(e);
+    if (r != TNCCL_SUCCESS) {
+      freeEmu(e);
+      delete e;
+      return r;
+    }
+  }
   *out = e;
   return TNCCL_SUCCESS;
 }
@@ -183,7 +294,11 @@ extern "C" tncclResult tncclEmuAllReduce(tncclEmu_t e, const void* const* send,
                                                                    : e->cfg.tsChunkBytes) / es;
       const uint64_t minChunk =
           (algo == TNCCL_ALGO_RING ? kRingMinChunkBytes : kTwoShotMinChunkBytes) / es;
-      a.chunk = makeChunkPlan(count, P, e->cfg.channels, maxChunk, minChunk, V);
+      // Socket edges carry the first netLayout.channels ring channels only.
+      const int ch = algo == TNCCL_ALGO_RING && e->net
+                         ? std::min(e->cfg.channels, e->netLayout.channels)
+                         : e->cfg.channels;
+      a.chunk = makeChunkPlan(count, P, ch, maxChunk, minChunk, V);
       channels = a.chunk.channels;
     }
     L.comm[k] = e->dev[k];

@@ -24,11 +24,11 @@ def _round_up(a, b):
     return _div_up(a, b) * b
 
 
-def ring_chunk_index(count, P, es):
+def ring_chunk_index(count, P, es, channels=CHANNELS):
     """Chunk (segment) owning each element under the ring's chunk plan
     (protocol.h makeChunkPlan / chunkSpan)."""
     V = 16 // es
-    want = _round_up(_div_up(count, P * CHANNELS), V)
+    want = _round_up(_div_up(count, P * channels), V)
     want = max(want, RING_MIN_CHUNK // es)
     want = min(want, RING_CHUNK // es)
     tile_elems = want * P
@@ -50,7 +50,7 @@ def _round_up_t(a, b):
     return _div_up_t(a, b) * b
 
 
-def oracle(xs, algo, alpha, dtype):
+def oracle(xs, algo, alpha, dtype, channels=CHANNELS):
     P = len(xs)
     f = [x.float() for x in xs]
     a = torch.tensor(alpha, dtype=torch.float32, device="cuda")
@@ -60,7 +60,7 @@ def oracle(xs, algo, alpha, dtype):
             acc = acc + f[k] * a
         return acc.to(dtype)
     es = xs[0].element_size()
-    j = ring_chunk_index(xs[0].numel(), P, es)
+    j = ring_chunk_index(xs[0].numel(), P, es, channels)
     stack = torch.stack(f)  # [P, n]
     cols = torch.arange(xs[0].numel(), device="cuda")
     acc = (stack[(j + 1) % P, cols] * a).to(dtype).float()
@@ -146,5 +146,52 @@ def test_emulated_twoshot_staging_paths(built, P, stage_min):
                 want = oracle(xs, "twoshot", 1.0, dtype)
                 for y in ys:
                     assert bool(torch.equal(y, want)), (P, stage_min, count, dtype)
+    finally:
+        emu.destroy()
+
+
+@pytest.mark.skipif(os.environ.get("TNCCL_TEST_SOCKET_EDGES") != "1",
+                    reason="socket-edge GPU path not yet run on a GPU; "
+                           "set TNCCL_TEST_SOCKET_EDGES=1")
+@pytest.mark.parametrize("P", [2, 4])
+def test_emulated_socket_ring(built, P):
+    """The ring over socket edges on one GPU: emulated ranks joined by
+    host-mapped FIFOs, in-process proxy threads and loopback TCP
+    (TNCCL_NET=force, 2 channels), bit for bit against the ring oracle, then
+    30 collectives in a row on the same FIFOs."""
+    import tiny_nccl_b200 as tn
+    env = {"TNCCL_NET": "force", "TNCCL_NET_CHANNELS": "2", "TNCCL_NCHANNELS": str(CHANNELS)}
+    old = {k: os.environ.get(k) for k in env}
+    os.environ.update(env)
+    try:
+        emu = tn.load().Emulator(P)
+    finally:
+        for k, v in old.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
+    try:
+        g = torch.Generator(device="cuda")
+        for count in (1, 4097, 1_000_003):
+            for dtype in (torch.float32, torch.bfloat16):
+                g.manual_seed(count + P)
+                xs = [(torch.rand(count, device="cuda", generator=g) * 2 - 1).to(dtype)
+                      for _ in range(P)]
+                ys = [torch.full_like(x, float("nan")) for x in xs]
+                emu.all_reduce(xs, ys, algo="ring")
+                torch.cuda.synchronize()
+                assert emu.async_error() == 0
+                want = oracle(xs, "ring", 1.0, dtype, channels=2)
+                for y in ys:
+                    assert bool(torch.equal(y, want)), (P, count, dtype)
+        for it in range(30):
+            n = 1 + (it * 7919) % 100_000
+            xs = [torch.full((n,), float(r + it), device="cuda") for r in range(P)]
+            emu.all_reduce(xs, xs, algo="ring")
+            torch.cuda.synchronize()
+            want = float(sum(r + it for r in range(P)))
+            assert all(bool(torch.all(x == want)) for x in xs), it
+        assert emu.async_error() == 0
     finally:
         emu.destroy()
