@@ -2,7 +2,10 @@
 for ncu captures and CUDA-event timing of the kernel alone.
 
     python benchmarks/ops_kernels.py --kernel ln_bwd --iters 20
-Kernels: ln_fwd, ln_bwd, cross_entropy, adamw.
+Kernels: ln_fwd, ln_bwd, cross_entropy, adamw, gemm_gelu (the tcgen05 GEMM of
+the MLP's first layer with its bias + GELU epilogue, M = rows, N = 3072,
+K = 768; reported in TFLOP/s) and gemm_gelu_ref (cuBLAS addmm + GELU on the
+same shapes, for comparison).
 """
 import argparse
 import os
@@ -59,6 +62,17 @@ def main():
             step[0] += 1
             ops.adamw(ps, gs, ms, vs, wd, 6e-4, 0.9, 0.95, 1e-8, step[0], 1.0)
         nbytes = sum(p.numel() for p in ps) * 4 * 7
+    elif args.kernel in ("gemm_gelu", "gemm_gelu_ref"):
+        x = (torch.randn(rows, C, device=dev) * 0.5).to(torch.bfloat16)
+        w = (torch.randn(4 * C, C, device=dev) * 0.02).to(torch.bfloat16)
+        b = (torch.randn(4 * C, device=dev) * 0.02).to(torch.bfloat16)
+        if args.kernel == "gemm_gelu":
+            fn = lambda: ops.gemm_bias_act(x, w, b, True)  # noqa: E731
+        else:
+            fn = lambda: torch.nn.functional.gelu(torch.addmm(b, x, w.t()),  # noqa: E731
+                                                  approximate="tanh")
+        flops = 2.0 * rows * 4 * C * C
+        nbytes = None
     else:
         raise SystemExit(f"unknown kernel {args.kernel}")
     fn()
@@ -70,7 +84,12 @@ def main():
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.iters
-    print(f"{args.kernel}: {ms * 1e3:.1f} us/launch, {nbytes / ms / 1e6:.0f} GB/s algorithmic")
+    if nbytes is None:
+        print(f"{args.kernel}: {ms * 1e3:.1f} us/launch, {flops / ms / 1e9:.0f} TFLOP/s")
+        if args.kernel == "gemm_gelu":
+            assert ops.tcgen05_status(True) == 0, "a tcgen05 GEMM wait timed out"
+    else:
+        print(f"{args.kernel}: {ms * 1e3:.1f} us/launch, {nbytes / ms / 1e6:.0f} GB/s algorithmic")
 
 
 if __name__ == "__main__":

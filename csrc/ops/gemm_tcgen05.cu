@@ -1,0 +1,383 @@
+// gemm_tcgen05.cu - bf16 GEMM with a fused bias (+ tanh-GELU) epilogue on the
+// 5th-generation tensor cores: tcgen05.mma with the fp32 accumulator in TMEM,
+// operands staged by TMA (cp.async.bulk.tensor, 128-byte swizzle) through a
+// 4-stage shared-memory ring.
+//
+//   pre = bf16(x w^T + bias)         x [M, K], w [N, K] (nn.Linear layout)
+//   act = bf16(gelu_tanh(pre))       (GELU variant; gelu of the rounded pre,
+//                                     as when pre is materialised first)
+//
+// One CTA computes one 128 x 256 output tile with three warp roles:
+//   warp 0     one thread issues the TMA loads of each 64-wide K block (A:
+//              128 x 64, B: 256 x 64) into the next free stage;
+//   warp 1     allocates 256 TMEM columns, and one thread issues four
+//              tcgen05.mma 128x256x16 per K block, then tcgen05.commit to the
+//              stage's "empty" barrier (the stage is free once those MMAs have
+//              read it) and, after the last block, to the accumulator barrier;
+//   warps 2-5  wait for the accumulator, read it with tcgen05.ld (warp w owns
+//              TMEM lanes 32 (w % 4) .. +31, i.e. those output rows), add the
+//              bias, apply GELU, round to bf16 and store.
+// Operands are K-major in shared memory, rows of 128 bytes in 8-row swizzle
+// atoms of 1024 bytes: the UMMA descriptor holds the start address, a
+// leading offset of 16 bytes and an 8-row stride of 1024 bytes, layout
+// SWIZZLE_128B, version 1; successive K = 16 slices start 32 bytes further.
+//
+// Every mbarrier wait is bounded (globaltimer). On expiry the CTA records a
+// code in gTcgen05Status, the other roles stop at their next wait, the
+// producer waits (bounded) for the TMA loads it issued, the MMA thread
+// commits and waits (bounded) for the MMAs it issued, and the TMEM columns
+// are freed before the CTA returns. No load uses cluster multicast; the
+// kernel reads this GPU's memory only.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <atomic>
+
+#include "common.cuh"
+#include "tnccl_ops.h"
+
+namespace tnops {
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBN = 256;
+constexpr int kBK = 64;  // bf16: 128 bytes, one swizzle row
+constexpr int kStages = 4;
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kStageA = kBM * kBK * 2;  // 16 KiB
+constexpr uint32_t kStageB = kBN * kBK * 2;  // 32 KiB
+constexpr uint32_t kSmemBytes = kStages * (kStageA + kStageB) + 1024;  // + alignment slack
+constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s per wait
+
+__device__ unsigned int gTcgen05Status;  // first failure code (0: none)
+
+__device__ __forceinline__ uint32_t smemAddr(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ uint64_t globalTimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbarInit(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smemAddr(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbarExpectTx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smemAddr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbarTryWait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smemAddr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Waits until the phase of `parity` completed. Gives up when *abort is set
+// (unless ignoreAbort) or after kWaitNs; on a timeout records `code`.
+__device__ __forceinline__ bool mbarWait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                         unsigned code, bool ignoreAbort = false) {
+  if (mbarTryWait(bar, parity)) return true;
+  const uint64_t t0 = globalTimer();
+  for (uint32_t it = 1;; ++it) {
+    if (mbarTryWait(bar, parity)) return true;
+    if ((it & 63) == 0) {
+      if (!ignoreAbort && *abort) return false;
+      if (globalTimer() - t0 > kWaitNs) {
+        atomicCAS(&gTcgen05Status, 0u, code);
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+__device__ __forceinline__ void tmaLoad2d(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smemAddr(bar))
+      : "memory");
+}
+__device__ __forceinline__ void fenceBeforeSync() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fenceAfterSync() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// K-major operand tile in shared memory, 128-byte swizzle (see the header).
+__device__ __forceinline__ uint64_t smemDesc(uint32_t addr) {
+  uint64_t d = (uint64_t)((addr & 0x3FFFFu) >> 4);  // start address, bits [0,14)
+  d |= (uint64_t)1 << 16;                           // leading byte offset 16 B, bits [16,30)
+  d |= (uint64_t)(1024 >> 4) << 32;                 // 8-row stride 1024 B, bits [32,46)
+  d |= (uint64_t)1 << 46;                           // descriptor version 1, bits [46,48)
+  d |= (uint64_t)2 << 61;                           // SWIZZLE_128B, bits [61,64)
+  return d;
+}
+// Instruction descriptor of kind::f16: bf16 x bf16 -> f32, both K-major,
+// M = 128, N = 256, dense.
+constexpr uint32_t instrDesc() {
+  return (1u << 4)                       // D format f32, bits [4,6)
+         | (1u << 7)                     // A format bf16, bits [7,10)
+         | (1u << 10)                    // B format bf16, bits [10,13)
+         | ((uint32_t)(kBN >> 3) << 17)  // N >> 3, bits [17,23)
+         | ((uint32_t)(kBM >> 4) << 24); // M >> 4, bits [24,29)
+}
+__device__ __forceinline__ void mma(uint32_t tmemD, uint64_t a, uint64_t b, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmemD),
+      "l"(a), "l"(b), "r"(instrDesc()), "r"(accumulate)
+      : "memory");
+}
+// Arrives on `bar` once every tcgen05.mma this thread issued before has completed.
+__device__ __forceinline__ void commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smemAddr(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tmemLoad32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ float geluTanh(float x) {
+  const float k0 = 0.7978845608028654f;  // sqrt(2 / pi)
+  const float k1 = 0.044715f;
+  return 0.5f * x * (1.0f + tanhf(k0 * (x + k1 * x * x * x)));
+}
+
+template <bool GELU>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemmBiasActKernel(const __grid_constant__ CUtensorMap mapA,
+                      const __grid_constant__ CUtensorMap mapB, const uint16_t* __restrict__ bias,
+                      uint16_t* __restrict__ pre, uint16_t* __restrict__ act, int M, int N, int K) {
+  __shared__ __align__(8) uint64_t sFull[kStages];
+  __shared__ __align__(8) uint64_t sEmpty[kStages];
+  __shared__ __align__(8) uint64_t sAccum;
+  __shared__ uint32_t sTmem;
+  __shared__ int sAbort;
+  extern __shared__ uint8_t dsmem[];
+  // Stage buffers start on a 1024-byte boundary (swizzle atoms).
+  const uint32_t base = (smemAddr(dsmem) + 1023u) & ~1023u;
+  const uint32_t stageA0 = base, stageB0 = base + kStages * kStageA;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * kBN, m0 = blockIdx.y * kBM;
+  const int kBlocks = (K + kBK - 1) / kBK;
+  volatile int* abort = &sAbort;
+
+  if (threadIdx.x == 0) {
+    sAbort = 0;
+    for (int s = 0; s < kStages; ++s) {
+      mbarInit(&sFull[s], 1);
+      mbarInit(&sEmpty[s], 1);
+    }
+    mbarInit(&sAccum, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smemAddr(&sTmem)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  fenceBeforeSync();
+  __syncthreads();
+  fenceAfterSync();
+  const uint32_t tmem = sTmem;
+
+  if (warp == 0 && lane == 0) {
+    // Producer.
+    int issued = 0;
+    for (int kb = 0; kb < kBlocks; ++kb) {
+      const int s = kb % kStages;
+      const uint32_t round = (uint32_t)(kb / kStages);
+      // A fresh barrier counts as having completed the phase before its first.
+      if (!mbarWait(&sEmpty[s], (round & 1u) ^ 1u, abort, 1)) break;
+      mbarExpectTx(&sFull[s], kStageA + kStageB);
+      tmaLoad2d(stageA0 + s * kStageA, &mapA, kb * kBK, m0, &sFull[s]);
+      tmaLoad2d(stageB0 + s * kStageB, &mapB, kb * kBK, n0, &sFull[s]);
+      issued = kb + 1;
+    }
+    if (*abort) {
+      // No TMA write may land after the CTA is gone.
+      for (int kb = issued > kStages ? issued - kStages : 0; kb < issued; ++kb)
+        mbarWait(&sFull[kb % kStages], (uint32_t)(kb / kStages) & 1u, abort, 4, true);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // MMA issuer.
+    for (int kb = 0; kb < kBlocks; ++kb) {
+      const int s = kb % kStages;
+      if (!mbarWait(&sFull[s], (uint32_t)(kb / kStages) & 1u, abort, 2)) break;
+      fenceAfterSync();
+      const uint32_t a = stageA0 + s * kStageA, b = stageB0 + s * kStageB;
+#pragma unroll
+      for (int k = 0; k < kBK / 16; ++k)
+        mma(tmem, smemDesc(a + k * 32), smemDesc(b + k * 32), (kb | k) != 0 ? 1u : 0u);
+      commit(&sEmpty[s]);
+    }
+    commit(&sAccum);  // also after an abort: the MMAs issued so far
+    if (*abort) mbarWait(&sAccum, 0, abort, 5, true);
+  } else if (warp >= 2) {
+    // Epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 = tile rows.
+    const int quarter = warp & 3;
+    const int row = m0 + quarter * 32 + lane;
+    // tcgen05.ld is warp-collective: the whole warp proceeds only if every
+    // lane saw the accumulator complete.
+    const bool ready = mbarWait(&sAccum, 0, abort, 3);
+    if (__all_sync(0xffffffffu, ready)) {
+      fenceAfterSync();
+#pragma unroll 1
+      for (int c = 0; c < kBN; c += 32) {
+        float v[32];
+        tmemLoad32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c, v);
+        const int col0 = n0 + c;
+        if (row >= M || col0 >= N) continue;
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          const int col = col0 + g * 8;
+          if (col >= N) break;  // N % 8 == 0: a vector is all in or all out
+          uint32_t pw[4], aw[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            float x0 = v[g * 8 + 2 * i], x1 = v[g * 8 + 2 * i + 1];
+            if (bias) {
+              x0 += bf2f(bias[col + 2 * i]);
+              x1 += bf2f(bias[col + 2 * i + 1]);
+            }
+            const uint16_t p0 = f2bf(x0), p1 = f2bf(x1);
+            pw[i] = (uint32_t)p0 | ((uint32_t)p1 << 16);
+            if (GELU) {
+              const uint16_t a0 = f2bf(geluTanh(bf2f(p0))), a1 = f2bf(geluTanh(bf2f(p1)));
+              aw[i] = (uint32_t)a0 | ((uint32_t)a1 << 16);
+            }
+          }
+          const size_t off = (size_t)row * N + col;
+          if (pre) *reinterpret_cast<uint4*>(pre + off) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
+          if (GELU) *reinterpret_cast<uint4*>(act + off) = make_uint4(aw[0], aw[1], aw[2], aw[3]);
+        }
+      }
+    }
+  }
+  fenceBeforeSync();
+  __syncthreads();
+  if (warp == 1) {
+    fenceAfterSync();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encodeTiled() {
+  static EncodeTiledFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+// [rows, K] row-major bf16, box {64, boxRows}, 128-byte swizzle, zero fill.
+bool makeMap(CUtensorMap* map, const void* base, int rows, int K, int boxRows) {
+  EncodeTiledFn fn = encodeTiled();
+  if (fn == nullptr) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)boxRows};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <bool GELU>
+int launchGemm(const void* x, const void* w, const void* bias, void* pre, void* act, int M, int N,
+               int K, cudaStream_t stream) {
+  // Opt in to the shared memory once per device (bit d of `done`).
+  static std::atomic<uint64_t> done{0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 3;
+  const uint64_t bit = dev < 64 ? (1ull << dev) : 0;
+  if (!(done.load(std::memory_order_acquire) & bit)) {
+    if (cudaFuncSetAttribute(gemmBiasActKernel<GELU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kSmemBytes) != cudaSuccess)
+      return 3;
+    done.fetch_or(bit, std::memory_order_acq_rel);
+  }
+  CUtensorMap mapA, mapB;
+  if (!makeMap(&mapA, x, M, K, kBM) || !makeMap(&mapB, w, N, K, kBN)) return 4;
+  const dim3 grid((unsigned)((N + kBN - 1) / kBN), (unsigned)((M + kBM - 1) / kBM));
+  gemmBiasActKernel<GELU><<<grid, kThreads, kSmemBytes, stream>>>(
+      mapA, mapB, static_cast<const uint16_t*>(bias), static_cast<uint16_t*>(pre),
+      static_cast<uint16_t*>(act), M, N, K);
+  gLaunches.fetch_add(1, std::memory_order_relaxed);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+}  // namespace tnops
+
+using namespace tnops;
+
+// pre = bf16(x w^T + bias) and, with gelu, act = bf16(gelu_tanh(pre)); bias
+// and pre may be null (not both outputs). Requirements: K % 8 == 0 (TMA row
+// pitch), N % 8 == 0, 16-byte aligned x, w, pre, act. Returns 0 on launch.
+extern "C" int tnops_gemm_bias_act(const void* x, const void* w, const void* bias, void* pre,
+                                   void* act, int M, int N, int K, int gelu,
+                                   cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0 || K % 8 != 0 || N % 8 != 0 || !aligned16(x) ||
+      !aligned16(w) || (pre && !aligned16(pre)) || (act && !aligned16(act)) ||
+      (gelu && act == nullptr) || (!gelu && pre == nullptr))
+    return 1;
+  return gelu ? launchGemm<true>(x, w, bias, pre, act, M, N, K, stream)
+              : launchGemm<false>(x, w, bias, pre, act, M, N, K, stream);
+}
+
+// First failure code a tcgen05 GEMM recorded (1-3: a wait of the producer,
+// MMA issuer or epilogue timed out; 4-5: a drain after that timed out), 0 if
+// none; `reset` clears it. Synchronises the device.
+extern "C" unsigned tnops_tcgen05_status(int reset) {
+  unsigned v = 0;
+  cudaMemcpyFromSymbol(&v, gTcgen05Status, sizeof(v));
+  if (reset) {
+    const unsigned z = 0;
+    cudaMemcpyToSymbol(gTcgen05Status, &z, sizeof(z));
+  }
+  return v;
+}

@@ -71,6 +71,17 @@ typedef struct {
 int tnops_adamw(const tnops_adamw_list* list, float lr, float beta1, float beta2, float eps,
                 int64_t step, float grad_scale, cudaStream_t stream);
 
+// bf16 GEMM on the tcgen05 tensor cores with a fused epilogue:
+// pre = bf16(x w^T + bias), and with `gelu` act = bf16(gelu_tanh(pre)).
+// x [M, K], w [N, K] (nn.Linear layout), bias [N] (may be null), pre / act
+// [M, N] (pre may be null with gelu). K % 8 == 0, N % 8 == 0, x, w, pre,
+// act 16-byte aligned; 1 (invalid argument) otherwise.
+int tnops_gemm_bias_act(const void* x, const void* w, const void* bias, void* pre, void* act,
+                        int M, int N, int K, int gelu, cudaStream_t stream);
+// First failure code recorded by a tcgen05 GEMM (a bounded wait that expired),
+// 0 if none; `reset` clears it. Synchronises the device.
+unsigned tnops_tcgen05_status(int reset);
+
 // Number of kernels the ops library launched in this process.
 unsigned long long tnops_launch_count(void);
 

@@ -112,6 +112,32 @@ at::Tensor biasGrad(const at::Tensor& g) {
   return db;
 }
 
+// x bf16 [M, K], w bf16 [N, K], bias bf16 [N] or None -> [pre] or, with gelu,
+// [pre, act] (bf16 [M, N]) from the tcgen05 GEMM with the fused epilogue.
+std::vector<at::Tensor> gemmBiasAct(const at::Tensor& x, const at::Tensor& w,
+                                    const c10::optional<at::Tensor>& bias, bool gelu) {
+  need(x, at::kBFloat16, "x");
+  need(w, at::kBFloat16, "weight");
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1),
+              "gemm_bias_act: want x [M, K] and weight [N, K]");
+  TORCH_CHECK(x.size(1) % 8 == 0 && w.size(0) % 8 == 0,
+              "gemm_bias_act: K and N must be multiples of 8");
+  if (bias) {
+    need(*bias, at::kBFloat16, "bias");
+    TORCH_CHECK(bias->numel() == w.size(0), "gemm_bias_act: bias must have N elements");
+  }
+  c10::cuda::CUDAGuard guard(x.device());
+  const int M = (int)x.size(0), N = (int)w.size(0), K = (int)x.size(1);
+  auto pre = at::empty({M, N}, x.options());
+  at::Tensor act = gelu ? at::empty({M, N}, x.options()) : at::Tensor();
+  const int rc = tnops_gemm_bias_act(x.data_ptr(), w.data_ptr(), bias ? bias->data_ptr() : nullptr,
+                                     pre.data_ptr(), gelu ? act.data_ptr() : nullptr, M, N, K,
+                                     gelu ? 1 : 0, streamOf(x));
+  TORCH_CHECK(rc == 0, "tnops_gemm_bias_act failed (code ", rc, ")");
+  if (gelu) return {pre, act};
+  return {pre};
+}
+
 // gy, pre bf16 [M, N] -> (gpre bf16 [M, N], db fp32 [N])
 std::vector<at::Tensor> geluBwdBias(const at::Tensor& gy, const at::Tensor& pre) {
   need(gy, at::kBFloat16, "grad_y");
@@ -181,6 +207,10 @@ void registerOps(py::module_& m) {
           py::arg("valid"), py::arg("classes") = 0);
   ops.def("bias_grad", &biasGrad, py::arg("grad"));
   ops.def("gelu_bwd_bias", &geluBwdBias, py::arg("grad_y"), py::arg("pre"));
+  ops.def("gemm_bias_act", &gemmBiasAct, py::arg("x"), py::arg("weight"), py::arg("bias"),
+          py::arg("gelu"));
+  ops.def("tcgen05_status", [](bool reset) { return tnops_tcgen05_status(reset ? 1 : 0); },
+          py::arg("reset") = false);
   ops.def("scale_bf16_", &scaleBf16);
   ops.def("adamw", &adamw);
   ops.def("launch_count", []() { return tnops_launch_count(); });
