@@ -219,3 +219,23 @@ def test_kernels_compile_with_device_checks(tmp_path):
            os.path.join(ROOT, "csrc", "tnccl", "allreduce.cu"), "-o", str(tmp_path / "ar.o")]
     r = run(cmd, timeout=900)
     assert r.returncode == 0, r.stderr[-3000:]
+
+
+def test_tcgen05_gemm_rejects_bad_arguments_before_device_work(built):
+    """The tcgen05 GEMM launcher validates shapes and alignment on the host
+    and returns 1 (invalid argument) without touching the device."""
+    lib = ctypes.CDLL(os.path.join(ROOT, "tiny_nccl_b200", "lib", "libtnccl_ops.so"))
+    f = lib.tnops_gemm_bias_act
+    f.argtypes = [ctypes.c_void_p] * 5 + [ctypes.c_int] * 4 + [ctypes.c_void_p]
+    f.restype = ctypes.c_int
+    p = 1 << 20  # aligned address; never dereferenced on these paths
+    cases = [
+        (p, p, 0, p, p, 128, 256, 60, 1),     # K % 8 != 0
+        (p, p, 0, p, p, 128, 250, 64, 1),     # N % 8 != 0
+        (p + 8, p, 0, p, p, 128, 256, 64, 1),  # x not 16-byte aligned
+        (p, p, 0, p, 0, 128, 256, 64, 1),     # GELU without an act output
+        (p, p, 0, 0, p, 128, 256, 64, 0),     # no GELU and no pre output
+        (p, p, 0, p, p, 0, 256, 64, 1),       # empty M
+    ]
+    for x, w, b, pre, act, M, N, K, gelu in cases:
+        assert f(x, w, b or None, pre or None, act or None, M, N, K, gelu, None) == 1
