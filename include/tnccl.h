@@ -1,6 +1,7 @@
 /*
- * tnccl.h - public C API of tnccl-b200, a single-node collective library for
- * NVIDIA B200 (sm_100a) GPUs connected by NVLink 5 / NVSwitch.
+ * tnccl.h - public C API of tnccl-b200, a collective library for NVIDIA B200
+ * (sm_100a) GPUs: NVLink 5 / NVSwitch within a node, TCP socket ring edges
+ * between nodes.
  *
  * The first five entry points and the first five result codes keep the names,
  * values and semantics of tiny-nccl's include/tnccl.h:11-51. Everything after
