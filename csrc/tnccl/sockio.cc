@@ -176,6 +176,13 @@ int tcpListen(const char* addr, int port, int backlog, int* boundPort) {
 void tcpTune(int fd, int sndBuf, int rcvBuf) {
   int one = 1;
   setsockopt(fd, IPPROTO_TCP, TCP_NODELAY, &one, sizeof(one));
+  // A peer host that vanishes without closing its connections shows up as a
+  // socket error after ~20 s of silence (10 s idle, then 5 probes 2 s apart).
+  int idle = 10, intvl = 2, cnt = 5;
+  setsockopt(fd, SOL_SOCKET, SO_KEEPALIVE, &one, sizeof(one));
+  setsockopt(fd, IPPROTO_TCP, TCP_KEEPIDLE, &idle, sizeof(idle));
+  setsockopt(fd, IPPROTO_TCP, TCP_KEEPINTVL, &intvl, sizeof(intvl));
+  setsockopt(fd, IPPROTO_TCP, TCP_KEEPCNT, &cnt, sizeof(cnt));
   if (sndBuf > 0) setsockopt(fd, SOL_SOCKET, SO_SNDBUF, &sndBuf, sizeof(sndBuf));
   if (rcvBuf > 0) setsockopt(fd, SOL_SOCKET, SO_RCVBUF, &rcvBuf, sizeof(rcvBuf));
 }

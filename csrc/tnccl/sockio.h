@@ -47,7 +47,8 @@ int acceptOne(int listenFd, Deadline d, Io* why);
 bool parseIpv4(const char* addr, uint32_t* out);
 int tcpListen(const char* addr, int port, int backlog, int* boundPort);
 int tcpConnect(uint32_t ipv4, int port, Deadline d, Io* why);
-// TCP_NODELAY and, when > 0, SO_SNDBUF / SO_RCVBUF on a connected socket.
+// TCP_NODELAY, keepalive probes (a silent dead peer fails the socket after
+// ~20 s) and, when > 0, SO_SNDBUF / SO_RCVBUF on a connected socket.
 void tcpTune(int fd, int sndBuf, int rcvBuf);
 
 }  // namespace tnccl
