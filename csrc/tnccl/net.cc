@@ -61,36 +61,38 @@ bool stepSend(NetProxy* p, int c) {
     netEncodeHeader(s.hdr, s.ticket, (uint32_t)n);
     s.bytes = n;
     s.off = 0;
+    s.partial = false;
     s.phase = 1;
   }
   const uint64_t total = H + s.bytes;
-  bool moved = false, partial = false;
+  bool moved = false;
   while (s.off < total) {
     iovec iov[2];
     int k = 0;
     if (s.off < H) iov[k++] = iovec{s.hdr + s.off, (size_t)(H - s.off)};
     const uint64_t poff = s.off > H ? s.off - H : 0;
-    if (s.bytes > poff) iov[k++] = iovec{ringFifoData(f, c, s.ticket) + poff, (size_t)(s.bytes - poff)};
+    if (s.bytes > poff)
+      iov[k++] = iovec{ringFifoData(f, c, s.ticket) + poff, (size_t)(s.bytes - poff)};
     msghdr m{};
     m.msg_iov = iov;
     m.msg_iovlen = (size_t)k;
     ssize_t rc = sendmsg(fd, &m, MSG_NOSIGNAL | MSG_DONTWAIT);
     if (rc > 0) {
-      if ((uint64_t)rc < total - s.off) partial = true;
+      if ((uint64_t)rc < total - s.off) s.partial = true;
       s.off += (uint64_t)rc;
       moved = true;
       continue;
     }
     if (rc < 0 && errno == EINTR) continue;
     if (rc < 0 && (errno == EAGAIN || errno == EWOULDBLOCK)) {
-      partial = true;
+      s.partial = true;
       break;
     }
     fail(p, TNCCL_SYSTEM_ERROR, c, "send failed (errno, ticket)", (uint64_t)errno, s.ticket);
     return moved;
   }
-  if (partial) p->partialWrites.fetch_add(1, std::memory_order_relaxed);
   if (s.off < total) return moved;
+  if (s.partial) p->partialWrites.fetch_add(1, std::memory_order_relaxed);
   stRelease(f.credit + i, s.ticket + (uint64_t)f.slots);
   p->framesSent.fetch_add(1, std::memory_order_relaxed);
   p->bytesSent.fetch_add(s.bytes, std::memory_order_relaxed);

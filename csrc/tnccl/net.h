@@ -144,7 +144,7 @@ struct NetProxy {
   // statistics (read by tests and tncclCommGetInfo-style queries)
   std::atomic<uint64_t> framesSent{0}, framesReceived{0};
   std::atomic<uint64_t> bytesSent{0}, bytesReceived{0};
-  std::atomic<uint64_t> partialWrites{0}, partialReads{0};
+  std::atomic<uint64_t> partialWrites{0}, partialReads{0};  // frames that took several calls
   std::atomic<uint64_t> creditStalls{0};  // frames that waited for the kernel's credit
 
   // proxy-thread state per channel
@@ -153,6 +153,7 @@ struct NetProxy {
     int phase = 0;  // 0: waiting for a ready slot, 1: writing a frame
     unsigned char hdr[kNetFrameHeaderBytes];
     uint64_t bytes = 0, off = 0;
+    bool partial = false;     // this frame took several writes
     int ctlHave = 0;  // bytes of a close frame received from downstream
     unsigned char ctl[kNetFrameHeaderBytes];
     bool peerClosed = false;  // downstream sent its close frame
