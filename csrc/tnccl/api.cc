@@ -101,6 +101,22 @@ extern "C" tncclResult tncclCommGetInfo(tncclComm_t comm, tncclCommInfo* info) {
   return TNCCL_SUCCESS;
 }
 
+extern "C" tncclResult tncclCommGetNetStats(tncclComm_t comm, tncclNetStats* stats) {
+  if (comm == nullptr || stats == nullptr) return TNCCL_INVALID_ARGUMENT;
+  *stats = tncclNetStats{};
+  const NetProxy* p = comm->net.proxy;
+  if (p == nullptr) return TNCCL_SUCCESS;
+  stats->framesSent = p->framesSent.load();
+  stats->framesReceived = p->framesReceived.load();
+  stats->bytesSent = p->bytesSent.load();
+  stats->bytesReceived = p->bytesReceived.load();
+  stats->partialWrites = p->partialWrites.load();
+  stats->partialReads = p->partialReads.load();
+  stats->creditStalls = p->creditStalls.load();
+  stats->failed = p->error.load();
+  return TNCCL_SUCCESS;
+}
+
 extern "C" tncclResult tncclCommValidate(tncclComm_t comm, int* corrupted) {
   if (comm == nullptr || corrupted == nullptr) return TNCCL_INVALID_ARGUMENT;
   if (comm->streamBound && cudaStreamSynchronize(comm->boundStream) != cudaSuccess)

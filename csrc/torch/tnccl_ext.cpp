@@ -170,6 +170,22 @@ class Communicator {
     return d;
   }
 
+  py::dict netStats() const {
+    live();
+    tncclNetStats st{};
+    check(tncclCommGetNetStats(comm_, &st), "tncclCommGetNetStats");
+    py::dict d;
+    d["frames_sent"] = st.framesSent;
+    d["frames_received"] = st.framesReceived;
+    d["bytes_sent"] = st.bytesSent;
+    d["bytes_received"] = st.bytesReceived;
+    d["partial_writes"] = st.partialWrites;
+    d["partial_reads"] = st.partialReads;
+    d["credit_stalls"] = st.creditStalls;
+    d["failed"] = st.failed;
+    return d;
+  }
+
   // Diagnostic: mean ms per launch of one NVLink/HBM primitive (diag.cu).
   double diagBench(int mode, uint64_t bytes, int ctas, int threads, int unroll, uint64_t chunk,
                    int iters) {
@@ -295,6 +311,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("abort", &Communicator::abort)
       .def("destroy", &Communicator::destroy)
       .def("info", &Communicator::info)
+      .def("net_stats", &Communicator::netStats)
       .def("diag_bench", &Communicator::diagBench)
       .def("diag_wait_timeout", &Communicator::diagWaitTimeout)
       .def("trace_read", &Communicator::traceRead)

@@ -156,6 +156,16 @@ typedef struct {
 } tncclCommInfo;
 
 tncclResult tncclCommGetInfo(tncclComm_t comm, tncclCommInfo* info);
+
+/* Traffic of this rank's socket ring edges (all zero without them). */
+typedef struct {
+  unsigned long long framesSent, framesReceived;
+  unsigned long long bytesSent, bytesReceived;
+  unsigned long long partialWrites, partialReads; /* frames that took several calls */
+  unsigned long long creditStalls; /* received frames that waited for the kernel */
+  int failed;                      /* tncclResult of the proxy's failure, 0 if none */
+} tncclNetStats;
+tncclResult tncclCommGetNetStats(tncclComm_t comm, tncclNetStats* stats);
 tncclResult tncclCommCount(tncclComm_t comm, int* nranks);
 tncclResult tncclCommUserRank(tncclComm_t comm, int* rank);
 tncclResult tncclCommCuDevice(tncclComm_t comm, int* device);

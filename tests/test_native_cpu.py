@@ -20,7 +20,7 @@ def test_c_abi_surface(built):
     names = ["tncclGetUniqueId", "tncclCommInitRank", "tncclAllReduceSumF32", "tncclCommDestroy",
              "tncclGetErrorString", "tncclAllReduce", "tncclAllReduceEx", "tncclCommGetInfo",
              "tncclCommGetAsyncError", "tncclCommAbort", "tncclCommSelectAlgo", "tncclGetVersion",
-             "tncclGetLaunchCount", "tncclGetUniqueIdTcp"]
+             "tncclGetLaunchCount", "tncclGetUniqueIdTcp", "tncclCommGetNetStats"]
     for n in names:
         assert hasattr(lib, n), n
     lib.tncclGetErrorString.restype = ctypes.c_char_p

@@ -107,6 +107,8 @@ def main():
         torch.cuda.synchronize()
         ok = ok and bool((y == 2.0 * world).all()) and comm.async_error() == 0
         ok = ok and check_graph(comm, stream, dev, rank, world)
+        st = comm.net_stats()
+        ok = ok and st["frames_sent"] > 0 and st["frames_received"] > 0 and st["failed"] == 0
         flag = torch.tensor([1.0 if ok else 0.0])
         dist.all_reduce(flag, op=dist.ReduceOp.MIN)
         if rank == 0:

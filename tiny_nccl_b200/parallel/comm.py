@@ -89,6 +89,12 @@ class Communicator:
     def info(self) -> dict:
         return self._c.info()
 
+    def net_stats(self) -> dict:
+        """Traffic of this rank's socket ring edges: frames and bytes each
+        way, frames that took several socket calls, received frames that
+        waited for the kernel's credit, and the proxy's failure code."""
+        return self._c.net_stats()
+
     # -- collectives ----------------------------------------------------------
     def all_reduce(self, tensor: torch.Tensor, out: torch.Tensor | None = None, op: str = "sum",
                    scale: float = 1.0, algo: str = "auto") -> torch.Tensor:
