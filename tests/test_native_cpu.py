@@ -239,3 +239,16 @@ def test_tcgen05_gemm_rejects_bad_arguments_before_device_work(built):
     ]
     for x, w, b, pre, act, M, N, K, gelu in cases:
         assert f(x, w, b or None, pre or None, act or None, M, N, K, gelu, None) == 1
+
+
+def test_example_makes_tcp_ids_for_multi_host_runs(built):
+    """examples/allreduce.cc --make-id prints a TCP rendezvous id as hex (no
+    GPU needed); malformed multi-host arguments are usage errors."""
+    exe = os.path.join(ROOT, "build", "bin", "tnccl_allreduce")
+    r = run([exe, "--make-id", "127.0.0.1:29500"], timeout=60)
+    assert r.returncode == 0, r.stderr
+    hexid = r.stdout.strip()
+    assert len(hexid) == 256 and bytes.fromhex(hexid)[:8] == b"TNCBT003"
+    assert run([exe, "--make-id", "localhost:29500"], timeout=60).returncode == 2
+    assert run([exe, "2", "10", "--ranks", "0:1", "--id", "zz"], timeout=60).returncode == 2
+    assert run([exe, "2", "10", "--ranks", "1:2", "--id", hexid], timeout=60).returncode == 2
