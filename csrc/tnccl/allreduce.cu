@@ -136,7 +136,10 @@ cudaError_t launchEmulatedTyped(const EmulatedLaunch& e, int channels, int threa
   const dim3 grid((unsigned)channels, (unsigned)e.nranks);
   const dim3 block((unsigned)threads);
   void* args[] = {const_cast<EmulatedLaunch*>(&e)};
-  if (e.algo == TNCCL_ALGO_RING && (e.comm[0].netSend || e.comm[0].netRecv))
+  bool socketEdges = false;
+  for (int k = 0; k < e.nranks; ++k)
+    socketEdges = socketEdges || e.comm[k].netSend != nullptr || e.comm[k].netRecv != nullptr;
+  if (e.algo == TNCCL_ALGO_RING && socketEdges)
     return cudaLaunchCooperativeKernel((const void*)emulatedNetRingKernel<T>, grid, block, args,
                                        0, stream);
   const void* fn = e.nranks <= 2   ? (const void*)emulatedKernel<T, 2>

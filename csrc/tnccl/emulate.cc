@@ -16,7 +16,9 @@
 // virtual rank gets host-mapped send / receive FIFOs and a proxy thread, and
 // the edges are loopback TCP connections inside this process; the ring then
 // runs through the same socket path (ringBody<T, true>) as ranks on
-// different hosts.
+// different hosts. TNCCL_EMU_HOSTS=<id>,<id>,... (one per virtual rank)
+// instead makes only the edges between different ids socket edges, so NVLink
+// and socket edges mix in one ring.
 #include <string.h>
 #include <unistd.h>
 
@@ -86,10 +88,11 @@ void emuNetFailure(void* arg, tncclResult code) {
                               __ATOMIC_SEQ_CST);
 }
 
-// Socket edges between the virtual ranks: FIFOs, loopback connections (edge
-// k -> k+1 is connected, accepted and acknowledged in turn; the listen
-// backlog holds the connections meanwhile) and one proxy per virtual rank.
-tncclResult setupEmuNet(tncclEmu* e) {
+// Socket edges between the virtual ranks (edge k -> k+1 where socket[k]):
+// FIFOs, loopback connections (each edge is connected, accepted and
+// acknowledged in turn; the listen backlog holds the connections meanwhile)
+// and one proxy per virtual rank that has a socket edge.
+tncclResult setupEmuNet(tncclEmu* e, const std::vector<char>& socket) {
   const int P = e->nranks;
   NetOptions o;
   o.channels = e->cfg.netChannels;
@@ -120,15 +123,18 @@ tncclResult setupEmuNet(tncclEmu* e) {
   uint32_t ip = 0;
   parseIpv4("127.0.0.1", &ip);
   for (int k = 0; k < P; ++k) {
+    const bool sendSock = socket[(size_t)k] != 0, recvSock = socket[(size_t)((k + P - 1) % P)] != 0;
     char* sendDev = nullptr;
     char* recvDev = nullptr;
-    if (!alloc(&e->netSend[(size_t)k], &sendDev) || !alloc(&e->netRecv[(size_t)k], &recvDev))
+    if ((sendSock && !alloc(&e->netSend[(size_t)k], &sendDev)) ||
+        (recvSock && !alloc(&e->netRecv[(size_t)k], &recvDev)))
       return TNCCL_CUDA_ERROR;
     e->dev[k].netSend = sendDev;
     e->dev[k].netRecv = recvDev;
     e->dev[k].netLayout = L;
   }
   for (int k = 0; k < P; ++k) {
+    if (!socket[(size_t)k]) continue;
     const int next = (k + 1) % P;
     int port = 0;
     const int lfd = tcpListen("127.0.0.1", 0, o.channels + 4, &port);
@@ -143,6 +149,7 @@ tncclResult setupEmuNet(tncclEmu* e) {
     if (r != TNCCL_SUCCESS) return r;
   }
   for (int k = 0; k < P; ++k) {
+    if (e->netSend[(size_t)k] == nullptr && e->netRecv[(size_t)k] == nullptr) continue;
     e->rings[(size_t)k].channels = o.channels;
     e->proxies[(size_t)k] = new (std::nothrow) NetProxy;
     if (e->proxies[(size_t)k] == nullptr) return TNCCL_SYSTEM_ERROR;
@@ -241,8 +248,28 @@ extern "C" tncclResult tncclEmuCreate(tncclEmu_t* out, int nranks) {
     dc.nvlsStage = (uint32_t)e->cfg.nvlsStage;
     dc.stageMinBytes = (uint32_t)e->cfg.stageMinBytes;
   }
-  if (e->cfg.netMode == 2) {
-    r = setupEmuNet(e);
+  // Which ring edges are socket edges (edge k -> k+1).
+  std::vector<char> socket((size_t)nranks, e->cfg.netMode == 2 ? 1 : 0);
+  const std::string hosts = envStr("TNCCL_EMU_HOSTS", "");
+  if (!hosts.empty()) {
+    std::vector<long> ids;
+    for (size_t pos = 0; pos <= hosts.size();) {
+      const size_t comma = std::min(hosts.find(',', pos), hosts.size());
+      ids.push_back(strtol(hosts.substr(pos, comma - pos).c_str(), nullptr, 10));
+      pos = comma + 1;
+    }
+    if ((int)ids.size() != nranks) {
+      freeEmu(e);
+      delete e;
+      return TNCCL_INVALID_ARGUMENT;
+    }
+    for (int k = 0; k < nranks; ++k)
+      socket[(size_t)k] = ids[(size_t)k] != ids[(size_t)((k + 1) % nranks)] ? 1 : 0;
+  }
+  bool anySocket = false;
+  for (char c : socket) anySocket = anySocket || c;
+  if (anySocket) {
+    r = setupEmuNet(e, socket);
     if (r != TNCCL_SUCCESS) {
       freeEmu(e);
       delete e;

@@ -153,14 +153,19 @@ def test_emulated_twoshot_staging_paths(built, P, stage_min):
 @pytest.mark.skipif(os.environ.get("TNCCL_TEST_SOCKET_EDGES") != "1",
                     reason="socket-edge GPU path not yet run on a GPU; "
                            "set TNCCL_TEST_SOCKET_EDGES=1")
-@pytest.mark.parametrize("P", [2, 4])
-def test_emulated_socket_ring(built, P):
+@pytest.mark.parametrize("P,hosts", [(2, None), (4, None), (4, "0,0,1,1"), (8, "0,0,0,1,1,2,2,2")])
+def test_emulated_socket_ring(built, P, hosts):
     """The ring over socket edges on one GPU: emulated ranks joined by
-    host-mapped FIFOs, in-process proxy threads and loopback TCP
-    (TNCCL_NET=force, 2 channels), bit for bit against the ring oracle, then
-    30 collectives in a row on the same FIFOs."""
+    host-mapped FIFOs, in-process proxy threads and loopback TCP (every edge
+    with TNCCL_NET=force; with TNCCL_EMU_HOSTS only the edges between
+    different host ids, the others over mailboxes), 2 channels, bit for bit
+    against the ring oracle, then 30 collectives in a row on the same FIFOs."""
     import tiny_nccl_b200 as tn
-    env = {"TNCCL_NET": "force", "TNCCL_NET_CHANNELS": "2", "TNCCL_NCHANNELS": str(CHANNELS)}
+    env = {"TNCCL_NET_CHANNELS": "2", "TNCCL_NCHANNELS": str(CHANNELS)}
+    if hosts is None:
+        env["TNCCL_NET"] = "force"
+    else:
+        env["TNCCL_EMU_HOSTS"] = hosts
     old = {k: os.environ.get(k) for k in env}
     os.environ.update(env)
     try:
