@@ -10,8 +10,14 @@
 # has neither setup.py nor pyproject.toml. Its CMakeLists.txt accepts only
 # numeric CMAKE_CUDA_ARCHITECTURES, so "100a" is refused and "100" (sm_100,
 # which runs on B200) is used.
+#
+#   baseline/build_reference.sh <reference source directory>
 set -euo pipefail
-SRC=${1:-/root/reference}
+if [ $# -ne 1 ]; then
+  echo "usage: $0 <reference source directory>" >&2
+  exit 2
+fi
+SRC=$1
 HERE=$(cd "$(dirname "$0")" && pwd)
 OUT="$HERE/_ref"
 WORK=$(mktemp -d /tmp/tnccl_ref.XXXXXX)

@@ -35,6 +35,7 @@ import datetime
 import json
 import os
 import socket
+import subprocess
 import sys
 import time
 
@@ -249,9 +250,13 @@ def main():
     args.warmup = max(args.warmup, 3)
 
     if args.impl == "reference" and not os.path.exists(REF_LIB):
+        # baseline/build_reference.sh installs it; TNCCL_REFERENCE_SRC names
+        # the reference source to build it from here.
         script = os.path.join(ROOT, "baseline", "build_reference.sh")
-        if os.path.isdir("/root/reference"):
-            os.system(f"bash {script} /root/reference > /dev/null 2>&1")
+        src = os.environ.get("TNCCL_REFERENCE_SRC", "")
+        if src and os.path.isdir(src):
+            subprocess.run(["bash", script, src], stdout=subprocess.DEVNULL,
+                           stderr=subprocess.DEVNULL, check=False)
         if not os.path.exists(REF_LIB):
             if int(os.environ.get("RANK", "0")) == 0:
                 print(json.dumps({"impl": "reference", "unavailable":
