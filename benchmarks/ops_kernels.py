@@ -21,6 +21,8 @@ def main():
     ap.add_argument("--kernel", default="ln_bwd")
     ap.add_argument("--rows", type=int, default=8 * 1024)
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--persistent", action="store_true",
+                    help="gemm_gelu: one CTA per SM with two TMEM accumulators")
     args = ap.parse_args()
     import tiny_nccl_b200 as tn
 
@@ -67,7 +69,7 @@ def main():
         w = (torch.randn(4 * C, C, device=dev) * 0.02).to(torch.bfloat16)
         b = (torch.randn(4 * C, device=dev) * 0.02).to(torch.bfloat16)
         if args.kernel == "gemm_gelu":
-            fn = lambda: ops.gemm_bias_act(x, w, b, True)  # noqa: E731
+            fn = lambda: ops.gemm_bias_act(x, w, b, True, args.persistent)  # noqa: E731
         else:
             fn = lambda: torch.nn.functional.gelu(torch.addmm(b, x, w.t()),  # noqa: E731
                                                   approximate="tanh")

@@ -168,6 +168,39 @@ __device__ __forceinline__ float geluTanh(float x) {
   return 0.5f * x * (1.0f + tanhf(k0 * (x + k1 * x * x * x)));
 }
 
+// Epilogue of 32 accumulator columns of one row: bias, rounding to bf16,
+// GELU of the rounded value, 16-byte stores of pre and act.
+template <bool GELU>
+__device__ __forceinline__ void storeChunk(const float (&v)[32], int row, int col0, int M, int N,
+                                           const uint16_t* __restrict__ bias,
+                                           uint16_t* __restrict__ pre,
+                                           uint16_t* __restrict__ act) {
+  if (row >= M || col0 >= N) return;
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const int col = col0 + g * 8;
+    if (col >= N) break;  // N % 8 == 0: a vector is all in or all out
+    uint32_t pw[4], aw[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float x0 = v[g * 8 + 2 * i], x1 = v[g * 8 + 2 * i + 1];
+      if (bias) {
+        x0 += bf2f(bias[col + 2 * i]);
+        x1 += bf2f(bias[col + 2 * i + 1]);
+      }
+      const uint16_t p0 = f2bf(x0), p1 = f2bf(x1);
+      pw[i] = (uint32_t)p0 | ((uint32_t)p1 << 16);
+      if (GELU) {
+        const uint16_t a0 = f2bf(geluTanh(bf2f(p0))), a1 = f2bf(geluTanh(bf2f(p1)));
+        aw[i] = (uint32_t)a0 | ((uint32_t)a1 << 16);
+      }
+    }
+    const size_t off = (size_t)row * N + col;
+    if (pre) *reinterpret_cast<uint4*>(pre + off) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
+    if (GELU) *reinterpret_cast<uint4*>(act + off) = make_uint4(aw[0], aw[1], aw[2], aw[3]);
+  }
+}
+
 template <bool GELU>
 __global__ void __launch_bounds__(kThreads, 1)
     gemmBiasActKernel(const __grid_constant__ CUtensorMap mapA,
@@ -254,31 +287,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < kBN; c += 32) {
         float v[32];
         tmemLoad32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c, v);
-        const int col0 = n0 + c;
-        if (row >= M || col0 >= N) continue;
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          const int col = col0 + g * 8;
-          if (col >= N) break;  // N % 8 == 0: a vector is all in or all out
-          uint32_t pw[4], aw[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            float x0 = v[g * 8 + 2 * i], x1 = v[g * 8 + 2 * i + 1];
-            if (bias) {
-              x0 += bf2f(bias[col + 2 * i]);
-              x1 += bf2f(bias[col + 2 * i + 1]);
-            }
-            const uint16_t p0 = f2bf(x0), p1 = f2bf(x1);
-            pw[i] = (uint32_t)p0 | ((uint32_t)p1 << 16);
-            if (GELU) {
-              const uint16_t a0 = f2bf(geluTanh(bf2f(p0))), a1 = f2bf(geluTanh(bf2f(p1)));
-              aw[i] = (uint32_t)a0 | ((uint32_t)a1 << 16);
-            }
-          }
-          const size_t off = (size_t)row * N + col;
-          if (pre) *reinterpret_cast<uint4*>(pre + off) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
-          if (GELU) *reinterpret_cast<uint4*>(act + off) = make_uint4(aw[0], aw[1], aw[2], aw[3]);
-        }
+        storeChunk<GELU>(v, row, n0 + c, M, N, bias, pre, act);
       }
     }
   }
@@ -288,6 +297,142 @@ __global__ void __launch_bounds__(kThreads, 1)
     fenceAfterSync();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                  "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+__device__ __forceinline__ void mbarArrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smemAddr(bar)) : "memory");
+}
+
+// Persistent variant: one CTA per SM walks the tiles t = blockIdx.x,
+// blockIdx.x + gridDim.x, ... (row-tile major, so neighbouring CTAs share A).
+// The producer's stage ring runs across tile boundaries, and the 512 TMEM
+// columns hold two accumulators: the MMA issuer fills accumulator t % 2 while
+// the epilogue drains the other. accFull[b] (MMA commit) and accEmpty[b] (one
+// arrival per epilogue warp after its last tcgen05.ld of that buffer) hand
+// the buffers back and forth; use u of buffer b waits for phase u of
+// accFull[b] and, on the MMA side, for phase u - 1 of accEmpty[b].
+template <bool GELU>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemmBiasActPersistentKernel(const __grid_constant__ CUtensorMap mapA,
+                                const __grid_constant__ CUtensorMap mapB,
+                                const uint16_t* __restrict__ bias, uint16_t* __restrict__ pre,
+                                uint16_t* __restrict__ act, int M, int N, int K) {
+  __shared__ __align__(8) uint64_t sFull[kStages];
+  __shared__ __align__(8) uint64_t sEmpty[kStages];
+  __shared__ __align__(8) uint64_t sAccFull[2];
+  __shared__ __align__(8) uint64_t sAccEmpty[2];
+  __shared__ __align__(8) uint64_t sDone;
+  __shared__ uint32_t sTmem;
+  __shared__ int sAbort;
+  extern __shared__ uint8_t dsmem[];
+  const uint32_t base = (smemAddr(dsmem) + 1023u) & ~1023u;
+  const uint32_t stageA0 = base, stageB0 = base + kStages * kStageA;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tilesN = (N + kBN - 1) / kBN;
+  const int tiles = tilesN * ((M + kBM - 1) / kBM);
+  const int kBlocks = (K + kBK - 1) / kBK;
+  volatile int* abort = &sAbort;
+
+  if (threadIdx.x == 0) {
+    sAbort = 0;
+    for (int s = 0; s < kStages; ++s) {
+      mbarInit(&sFull[s], 1);
+      mbarInit(&sEmpty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbarInit(&sAccFull[b], 1);
+      mbarInit(&sAccEmpty[b], 4);  // the four epilogue warps
+    }
+    mbarInit(&sDone, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smemAddr(&sTmem)),
+                 "r"(2 * kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  fenceBeforeSync();
+  __syncthreads();
+  fenceAfterSync();
+  const uint32_t tmem = sTmem;
+
+  if (warp == 0 && lane == 0) {
+    // Producer: one stage sequence over all of this CTA's tiles.
+    uint32_t g = 0;  // K blocks issued
+    for (int t = blockIdx.x; t < tiles && !*abort; t += gridDim.x) {
+      const int m0 = (t / tilesN) * kBM, n0 = (t % tilesN) * kBN;
+      for (int kb = 0; kb < kBlocks; ++kb, ++g) {
+        const uint32_t s = g % kStages, round = g / kStages;
+        if (!mbarWait(&sEmpty[s], (round & 1u) ^ 1u, abort, 1)) break;
+        mbarExpectTx(&sFull[s], kStageA + kStageB);
+        tmaLoad2d(stageA0 + s * kStageA, &mapA, kb * kBK, m0, &sFull[s]);
+        tmaLoad2d(stageB0 + s * kStageB, &mapB, kb * kBK, n0, &sFull[s]);
+      }
+    }
+    if (*abort)
+      for (uint32_t q = g > (uint32_t)kStages ? g - kStages : 0; q < g; ++q)
+        mbarWait(&sFull[q % kStages], (q / kStages) & 1u, abort, 4, true);
+  } else if (warp == 1 && lane == 0) {
+    // MMA issuer.
+    uint32_t g = 0, local = 0;
+    for (int t = blockIdx.x; t < tiles && !*abort; t += gridDim.x, ++local) {
+      const uint32_t b = local & 1u, use = local >> 1;
+      if (!mbarWait(&sAccEmpty[b], (use & 1u) ^ 1u, abort, 2)) break;
+      fenceAfterSync();
+      const uint32_t acc = tmem + b * kTmemCols;
+      bool ok = true;
+      for (int kb = 0; kb < kBlocks; ++kb, ++g) {
+        const uint32_t s = g % kStages;
+        if (!(ok = mbarWait(&sFull[s], (g / kStages) & 1u, abort, 2))) break;
+        fenceAfterSync();
+        const uint32_t a = stageA0 + s * kStageA, bb = stageB0 + s * kStageB;
+#pragma unroll
+        for (int k = 0; k < kBK / 16; ++k)
+          mma(acc, smemDesc(a + k * 32), smemDesc(bb + k * 32), (kb | k) != 0 ? 1u : 0u);
+        commit(&sEmpty[s]);
+      }
+      if (!ok) break;
+      commit(&sAccFull[b]);
+    }
+    commit(&sDone);  // every MMA issued so far
+    if (*abort) mbarWait(&sDone, 0, abort, 5, true);
+  } else if (warp >= 2) {
+    // Epilogue.
+    const int quarter = warp & 3;
+    uint32_t local = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++local) {
+      const uint32_t b = local & 1u, use = local >> 1;
+      const bool ready = mbarWait(&sAccFull[b], use & 1u, abort, 3);
+      if (!__all_sync(0xffffffffu, ready)) break;
+      fenceAfterSync();
+      const int m0 = (t / tilesN) * kBM, n0 = (t % tilesN) * kBN;
+      const int row = m0 + quarter * 32 + lane;
+      const uint32_t acc = tmem + b * kTmemCols + ((uint32_t)(quarter * 32) << 16);
+#pragma unroll 1
+      for (int c = 0; c < kBN; c += 32) {
+        float v[32];
+        tmemLoad32(acc + (uint32_t)c, v);
+        if (c + 32 == kBN) {
+          // Last read of this buffer: hand it back before the stores.
+          fenceBeforeSync();
+          __syncwarp();
+          if (lane == 0) mbarArrive(&sAccEmpty[b]);
+        }
+        storeChunk<GELU>(v, row, n0 + c, M, N, bias, pre, act);
+      }
+    }
+  }
+  fenceBeforeSync();
+  __syncthreads();
+  if (warp == 1) {
+    fenceAfterSync();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(2 * kTmemCols)
                  : "memory");
   }
 }
@@ -324,24 +469,34 @@ bool makeMap(CUtensorMap* map, const void* base, int rows, int K, int boxRows) {
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <bool GELU>
+template <bool GELU, bool PERSISTENT>
 int launchGemm(const void* x, const void* w, const void* bias, void* pre, void* act, int M, int N,
                int K, cudaStream_t stream) {
-  // Opt in to the shared memory once per device (bit d of `done`).
+  auto kernel = PERSISTENT ? gemmBiasActPersistentKernel<GELU> : gemmBiasActKernel<GELU>;
+  // Opt in to the shared memory once per device (bit d of `done`); the SM
+  // count of that device sizes the persistent grid.
   static std::atomic<uint64_t> done{0};
+  static int sms[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 3;
   const uint64_t bit = dev < 64 ? (1ull << dev) : 0;
   if (!(done.load(std::memory_order_acquire) & bit)) {
-    if (cudaFuncSetAttribute(gemmBiasActKernel<GELU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)kSmemBytes) != cudaSuccess)
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kSmemBytes) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms[dev & 63], cudaDevAttrMultiProcessorCount, dev) !=
+            cudaSuccess)
       return 3;
     done.fetch_or(bit, std::memory_order_acq_rel);
   }
   CUtensorMap mapA, mapB;
   if (!makeMap(&mapA, x, M, K, kBM) || !makeMap(&mapB, w, N, K, kBN)) return 4;
-  const dim3 grid((unsigned)((N + kBN - 1) / kBN), (unsigned)((M + kBM - 1) / kBM));
-  gemmBiasActKernel<GELU><<<grid, kThreads, kSmemBytes, stream>>>(
+  const int tilesN = (N + kBN - 1) / kBN, tilesM = (M + kBM - 1) / kBM;
+  dim3 grid((unsigned)tilesN, (unsigned)tilesM);
+  if (PERSISTENT) {
+    const int tiles = tilesN * tilesM, n = sms[dev & 63] > 0 ? sms[dev & 63] : 148;
+    grid = dim3((unsigned)(tiles < n ? tiles : n));
+  }
+  kernel<<<grid, kThreads, kSmemBytes, stream>>>(
       mapA, mapB, static_cast<const uint16_t*>(bias), static_cast<uint16_t*>(pre),
       static_cast<uint16_t*>(act), M, N, K);
   gLaunches.fetch_add(1, std::memory_order_relaxed);
@@ -356,17 +511,22 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 using namespace tnops;
 
 // pre = bf16(x w^T + bias) and, with gelu, act = bf16(gelu_tanh(pre)); bias
-// and pre may be null (not both outputs). Requirements: K % 8 == 0 (TMA row
-// pitch), N % 8 == 0, 16-byte aligned x, w, pre, act. Returns 0 on launch.
+// and pre may be null (not both outputs). `persistent` selects the kernel
+// with one CTA per SM and two TMEM accumulators. Requirements: K % 8 == 0
+// (TMA row pitch), N % 8 == 0, 16-byte aligned x, w, pre, act. Returns 0 on
+// launch.
 extern "C" int tnops_gemm_bias_act(const void* x, const void* w, const void* bias, void* pre,
-                                   void* act, int M, int N, int K, int gelu,
+                                   void* act, int M, int N, int K, int gelu, int persistent,
                                    cudaStream_t stream) {
   if (M <= 0 || N <= 0 || K <= 0 || K % 8 != 0 || N % 8 != 0 || !aligned16(x) ||
       !aligned16(w) || (pre && !aligned16(pre)) || (act && !aligned16(act)) ||
       (gelu && act == nullptr) || (!gelu && pre == nullptr))
     return 1;
-  return gelu ? launchGemm<true>(x, w, bias, pre, act, M, N, K, stream)
-              : launchGemm<false>(x, w, bias, pre, act, M, N, K, stream);
+  if (persistent)
+    return gelu ? launchGemm<true, true>(x, w, bias, pre, act, M, N, K, stream)
+                : launchGemm<false, true>(x, w, bias, pre, act, M, N, K, stream);
+  return gelu ? launchGemm<true, false>(x, w, bias, pre, act, M, N, K, stream)
+              : launchGemm<false, false>(x, w, bias, pre, act, M, N, K, stream);
 }
 
 // First failure code a tcgen05 GEMM recorded (1-3: a wait of the producer,

@@ -74,10 +74,11 @@ int tnops_adamw(const tnops_adamw_list* list, float lr, float beta1, float beta2
 // bf16 GEMM on the tcgen05 tensor cores with a fused epilogue:
 // pre = bf16(x w^T + bias), and with `gelu` act = bf16(gelu_tanh(pre)).
 // x [M, K], w [N, K] (nn.Linear layout), bias [N] (may be null), pre / act
-// [M, N] (pre may be null with gelu). K % 8 == 0, N % 8 == 0, x, w, pre,
-// act 16-byte aligned; 1 (invalid argument) otherwise.
+// [M, N] (pre may be null with gelu). `persistent`: one CTA per SM with two
+// TMEM accumulators instead of one CTA per 128 x 256 tile. K % 8 == 0,
+// N % 8 == 0, x, w, pre, act 16-byte aligned; 1 (invalid argument) otherwise.
 int tnops_gemm_bias_act(const void* x, const void* w, const void* bias, void* pre, void* act,
-                        int M, int N, int K, int gelu, cudaStream_t stream);
+                        int M, int N, int K, int gelu, int persistent, cudaStream_t stream);
 // First failure code recorded by a tcgen05 GEMM (a bounded wait that expired),
 // 0 if none; `reset` clears it. Synchronises the device.
 unsigned tnops_tcgen05_status(int reset);

@@ -226,7 +226,7 @@ def test_tcgen05_gemm_rejects_bad_arguments_before_device_work(built):
     and returns 1 (invalid argument) without touching the device."""
     lib = ctypes.CDLL(os.path.join(ROOT, "tiny_nccl_b200", "lib", "libtnccl_ops.so"))
     f = lib.tnops_gemm_bias_act
-    f.argtypes = [ctypes.c_void_p] * 5 + [ctypes.c_int] * 4 + [ctypes.c_void_p]
+    f.argtypes = [ctypes.c_void_p] * 5 + [ctypes.c_int] * 5 + [ctypes.c_void_p]
     f.restype = ctypes.c_int
     p = 1 << 20  # aligned address; never dereferenced on these paths
     cases = [
@@ -238,7 +238,9 @@ def test_tcgen05_gemm_rejects_bad_arguments_before_device_work(built):
         (p, p, 0, p, p, 0, 256, 64, 1),       # empty M
     ]
     for x, w, b, pre, act, M, N, K, gelu in cases:
-        assert f(x, w, b or None, pre or None, act or None, M, N, K, gelu, None) == 1
+        for persistent in (0, 1):
+            assert f(x, w, b or None, pre or None, act or None, M, N, K, gelu, persistent,
+                     None) == 1
 
 
 def test_example_makes_tcp_ids_for_multi_host_runs(built):

@@ -1,6 +1,7 @@
 """The tcgen05 GEMM with the fused bias + GELU epilogue (csrc/ops/
-gemm_tcgen05.cu) against an fp32 PyTorch reference of the same op, on the
-GPT-2 MLP shape and on shapes with M, N and K tails.
+gemm_tcgen05.cu), one CTA per tile and persistent, against an fp32 PyTorch
+reference of the same op, on the GPT-2 MLP shape and on shapes with M, N and
+K tails.
 
 These run only with TNCCL_TEST_TCGEN05=1: the kernel has not yet run on a
 GPU, and it joins the default GPU suite (and the model) once it has."""
@@ -20,7 +21,8 @@ SHAPES = [(128, 256, 64), (256, 264, 72), (1000, 3072, 768), (8192, 3072, 768)]
 
 @pytest.mark.parametrize("M,N,K", SHAPES)
 @pytest.mark.parametrize("gelu", [True, False])
-def test_gemm_bias_act_matches_fp32_reference(built, M, N, K, gelu):
+@pytest.mark.parametrize("persistent", [False, True])
+def test_gemm_bias_act_matches_fp32_reference(built, M, N, K, gelu, persistent):
     import tiny_nccl_b200 as tn
 
     ops = tn.load().ops
@@ -28,7 +30,7 @@ def test_gemm_bias_act_matches_fp32_reference(built, M, N, K, gelu):
     x = (torch.randn(M, K, device="cuda", generator=g) * 0.5).to(torch.bfloat16)
     w = (torch.randn(N, K, device="cuda", generator=g) * 0.05).to(torch.bfloat16)
     b = (torch.randn(N, device="cuda", generator=g) * 0.1).to(torch.bfloat16)
-    out = ops.gemm_bias_act(x, w, b, gelu)
+    out = ops.gemm_bias_act(x, w, b, gelu, persistent)
     torch.cuda.synchronize()
     assert ops.tcgen05_status(True) == 0
     ref = x.float() @ w.float().t() + b.float()
