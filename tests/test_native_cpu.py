@@ -77,6 +77,15 @@ def test_socket_ring_edges(built):
     assert "net_proxy_test: PASS" in r.stdout
 
 
+def test_gemm_pipeline_model(built):
+    """The mbarrier hand-offs of both tcgen05 GEMM kernels (stage ring,
+    accumulator buffers, abort path) as threads with asynchronous TMA / MMA
+    units, under random timing."""
+    r = run([os.path.join(ROOT, "build", "bin", "gemm_pipeline_model_test")], timeout=300)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "gemm_pipeline_model_test: PASS" in r.stdout
+
+
 def test_config_and_partitions(built):
     r = run([os.path.join(ROOT, "build", "bin", "config_test")], timeout=120)
     assert r.returncode == 0, r.stdout + r.stderr

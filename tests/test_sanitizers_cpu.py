@@ -64,3 +64,14 @@ def test_socket_proxy_under_asan_ubsan():
     env = dict(os.environ, ASAN_OPTIONS="detect_leaks=1:abort_on_error=1")
     r = subprocess.run([exe], capture_output=True, text=True, timeout=300, env=env)
     assert r.returncode == 0 and "net_proxy_test: PASS" in r.stdout, r.stdout[-2000:] + r.stderr[-4000:]
+
+
+@pytest.mark.skipif(shutil.which("g++") is None, reason="needs g++")
+def test_gemm_pipeline_model_under_tsan():
+    exe = _build("gemm_pipeline_tsan", ["tests/cpp/gemm_pipeline_model_test.cc"],
+                 ["-fsanitize=thread"])
+    env = dict(os.environ, TSAN_OPTIONS="halt_on_error=1")
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=600, env=env)
+    assert r.returncode == 0 and "gemm_pipeline_model_test: PASS" in r.stdout, \
+        r.stdout[-2000:] + r.stderr[-4000:]
+    assert "WARNING: ThreadSanitizer" not in r.stderr, r.stderr[-4000:]

@@ -165,6 +165,8 @@ PROGRAMS = {
     "rank_model_test": ROOT / "tests" / "cpp" / "rank_model_test.cc",
     # socket ring edges: connection set-up, proxy thread, ring over sockets
     "net_proxy_test": ROOT / "tests" / "cpp" / "net_proxy_test.cc",
+    # mbarrier hand-offs of the tcgen05 GEMM pipelines, as threads
+    "gemm_pipeline_model_test": ROOT / "tests" / "cpp" / "gemm_pipeline_model_test.cc",
     # host configuration / partition checks, built with the library's config code
     "config_test": (ROOT / "tests" / "cpp" / "config_test.cc", TNCCL_SRC / "common.cc"),
 }
