@@ -5,6 +5,8 @@ missing extension or an unsupported shape raises.
 """
 from __future__ import annotations
 
+import os
+
 import torch
 
 from .._native import load
@@ -121,6 +123,12 @@ class _LinearBias(torch.autograd.Function):
         return gy @ w16, _wgrad(gy, x), _ops().bias_grad(gy)
 
 
+# TNCCL_TCGEN05_GEMM=1 (or =persistent) computes the forward of linear_gelu
+# with the tcgen05 GEMM and its fused bias + GELU epilogue instead of cuBLAS
+# and a separate GELU. Off by default: that kernel has not run on a GPU yet.
+_TCGEN05 = os.environ.get("TNCCL_TCGEN05_GEMM", "0")
+
+
 class _LinearGelu(torch.autograd.Function):
     """y = GELU_tanh(x W^T + b). Backward: one kernel computes the GELU
     gradient and the bias gradient (column sums of that gradient); dX and dW
@@ -129,9 +137,13 @@ class _LinearGelu(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, weight, bias):
         w16 = weight.to(torch.bfloat16)
-        with torch.autocast("cuda", enabled=False):
-            pre = torch.addmm(bias.to(torch.bfloat16), x, w16.t())
-            y = torch.nn.functional.gelu(pre, approximate="tanh")
+        b16 = bias.to(torch.bfloat16)
+        if _TCGEN05 != "0":
+            pre, y = _ops().gemm_bias_act(x, w16, b16, True, _TCGEN05 == "persistent")
+        else:
+            with torch.autocast("cuda", enabled=False):
+                pre = torch.addmm(b16, x, w16.t())
+                y = torch.nn.functional.gelu(pre, approximate="tanh")
         ctx.save_for_backward(x, w16, pre)
         return y
 
