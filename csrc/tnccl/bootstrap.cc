@@ -215,7 +215,8 @@ Io recvFrameFds(int fd, uint16_t type, uint32_t op, void* payload, size_t bytes,
 sockaddr_un addressOf(const char* path, socklen_t* len) {
   sockaddr_un a{};
   a.sun_family = AF_UNIX;
-  strncpy(a.sun_path, path, sizeof(a.sun_path) - 1);
+  const size_t n = strnlen(path, sizeof(a.sun_path) - 1);
+  memcpy(a.sun_path, path, n);  // the rest is zero: a{} above
   *len = (socklen_t)(offsetof(sockaddr_un, sun_path) + strlen(a.sun_path) + 1);
   return a;
 }
@@ -401,7 +402,7 @@ tncclResult bootstrapOpen(Bootstrap* b, const tncclUniqueId& id, int nranks,
         bootstrapClose(b);  // path not owned: never unlink another rendezvous
         return TNCCL_SYSTEM_ERROR;
       }
-      strncpy(b->path, path, sizeof(b->path) - 1);
+      memcpy(b->path, path, strnlen(path, sizeof(b->path) - 1) + 1);
       b->ownsPath = true;
       if (chmod(path, S_IRUSR | S_IWUSR) != 0 || listen(b->listenFd, nranks) != 0) {
         bootstrapClose(b);
