@@ -123,7 +123,7 @@ __device__ __forceinline__ uint64_t smemDesc(uint32_t addr) {
 }
 // Instruction descriptor of kind::f16: bf16 x bf16 -> f32, both K-major,
 // M = 128, N = 256, dense.
-constexpr uint32_t instrDesc() {
+__host__ __device__ constexpr uint32_t instrDesc() {
   return (1u << 4)                       // D format f32, bits [4,6)
          | (1u << 7)                     // A format bf16, bits [7,10)
          | (1u << 10)                    // B format bf16, bits [10,13)
