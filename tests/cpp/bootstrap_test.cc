@@ -342,6 +342,45 @@ void testTcpNonceMismatch() {
                                    codes[1] == TNCCL_INVALID_ARGUMENT);
 }
 
+// A TCP rendezvous is reachable by anything on the network: random bytes
+// instead of a hello must make rank 0 fail the rendezvous, not crash or hang.
+void testFuzzedHello() {
+  bool ok = true;
+  for (int seed = 0; seed < 20 && ok; ++seed) {
+    int port = 0;
+    int fd0 = tcpListen("127.0.0.1", 0, 1, &port);
+    if (fd0 >= 0) close(fd0);
+    tncclUniqueId id{};
+    bootstrapNewTcpId(&id, "127.0.0.1", port);
+    pid_t kid = fork();
+    if (kid == 0) {
+      Bootstrap b;
+      _exit(bootstrapOpen(&b, id, 2, 0, 1, 3000) == TNCCL_SUCCESS ? 0 : 1);
+    }
+    uint32_t ip = 0;
+    parseIpv4("127.0.0.1", &ip);
+    Io why = Io::kOk;
+    int fd = tcpConnect(ip, port, deadlineIn(3000), &why);
+    if (fd >= 0) {
+      unsigned char junk[256];
+      uint64_t x = 0x9e3779b97f4a7c15ull * (uint64_t)(seed + 1);
+      const size_t n = 1 + (size_t)(x % sizeof(junk));
+      for (size_t i = 0; i < n; ++i) {
+        x ^= x << 13;
+        x ^= x >> 7;
+        x ^= x << 17;
+        junk[i] = (unsigned char)x;
+      }
+      (void)writeAll(fd, junk, n, deadlineIn(1000));
+      close(fd);
+    }
+    int st = 0;
+    waitpid(kid, &st, 0);
+    ok = fd >= 0 && WIFEXITED(st) && WEXITSTATUS(st) == 1;
+  }
+  report("tcp rendezvous: fuzzed hello", ok);
+}
+
 }  // namespace
 
 int main() {
@@ -359,6 +398,7 @@ int main() {
   testTcpNonceMismatch();
   testLargeGather(false);
   testLargeGather(true);
+  testFuzzedHello();
   printf("bootstrap_test: %s\n", gFailed ? "FAIL" : "PASS");
   return gFailed ? 1 : 0;
 }

@@ -18,7 +18,9 @@
 //    closes without a close frame, an out-of-order ticket, an oversized
 //    frame, a foreign hello (refused, the edge still connects), a mismatched
 //    hello (edge fails), a rank that dies inside a collective (the others'
-//    waits end through the failure hook, long before their timeout);
+//    waits end through the failure hook, long before their timeout), random
+//    bytes on a receive connection (a recorded failure, nothing written
+//    past the FIFO);
 //  * no descriptor leaks.
 #include <dirent.h>
 #include <stdio.h>
@@ -457,6 +459,50 @@ void testEdgeFailures() {
   }
 }
 
+// Random bytes on a receive connection (sometimes after valid frames) must
+// end in a recorded failure, never in a crash, a hang or a payload written
+// past its slot.
+void testFuzzedStreams() {
+  NetOptions o;
+  o.channels = 1;
+  o.spinUs = 20;
+  const NetFifoLayout L = makeNetFifoLayout(1, 4, 4096);
+  bool ok = true;
+  for (int seed = 0; seed < 40 && ok; ++seed) {
+    std::mt19937 g((unsigned)seed);
+    Edge e = connectEdge(1, o);
+    Buf rb(L.totalBytes + 4096);  // guard bytes after the FIFO
+    netFifoInit(rb.p(), L);
+    memset(rb.p() + L.totalBytes, 0x5A, 4096);
+    std::atomic<int> err{0};
+    NetProxy pb;
+    ok = e.ok && netProxyStart(&pb, o, L, nullptr, rb.p(), &e.b, hookSetError, &err) ==
+                     TNCCL_SUCCESS;
+    std::vector<unsigned char> bytes;
+    const int valid = (int)(g() % 3);  // a few well-formed frames first
+    for (int t = 0; t < valid; ++t) {
+      unsigned char h[kNetFrameHeaderBytes];
+      netEncodeHeader(h, (uint64_t)t, 16);
+      bytes.insert(bytes.end(), h, h + sizeof(h));
+      for (int k = 0; k < 16; ++k) bytes.push_back((unsigned char)g());
+    }
+    const int junk = 1 + (int)(g() % 300);
+    for (int k = 0; k < junk; ++k) bytes.push_back((unsigned char)g());
+    Deadline d = deadlineIn(2000);
+    if (ok) (void)writeAll(e.a.sendFds[0], bytes.data(), bytes.size(), d);
+    netCloseRing(&e.a);  // the sender goes away without a close frame
+    auto t0 = steady_clock::now();
+    while (ok && !err.load() && steady_clock::now() - t0 < Ms(3000))
+      std::this_thread::sleep_for(Ms(1));
+    netProxyStop(&pb, false);
+    netCloseRing(&e.b);
+    bool guard = true;
+    for (int k = 0; k < 4096; ++k) guard = guard && (unsigned char)rb.p()[L.totalBytes + k] == 0x5A;
+    ok = ok && err.load() != 0 && guard;
+  }
+  report("40 fuzzed receive streams: failure recorded, FIFO bounds kept", ok);
+}
+
 // ---------------------------------------------------------------------------
 // Ring all-reduce: P host threads run the ring kernel's protocol; edges are
 // NVLink-like (shared mailboxes) or socket edges (host FIFO + proxy + TCP).
@@ -741,6 +787,7 @@ int main() {
   testCodecAndLayout();
   testStream();
   testEdgeFailures();
+  testFuzzedStreams();
   testRing();
   const int fds1 = countFds();
   report("no descriptor leaks", fds0 == fds1);
