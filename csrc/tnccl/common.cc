@@ -2,6 +2,7 @@
 
 #include "protocol.h"
 
+#include <errno.h>
 #include <stdio.h>
 #include <string.h>
 #include <strings.h>
@@ -218,16 +219,23 @@ bool parseTuningTable(const std::string& text, TuningTable* out, std::string* er
     if (line.find_first_not_of(" \t\r") == std::string::npos) continue;
     int nranks = 0;
     unsigned long long maxBytes = 0;
+    char sizeText[32] = {0};
     char algoName[32] = {0};
     char extra[2] = {0};
-    if (sscanf(line.c_str(), "%d %llu %31s %1s", &nranks, &maxBytes, algoName, extra) != 3 ||
-        nranks < 1 || nranks > kMaxRanks) {
+    // The size is read as text first: %llu alone would take "-1" as 2^64 - 1.
+    char* sizeEnd = nullptr;
+    errno = 0;
+    if (sscanf(line.c_str(), "%d %31s %31s %1s", &nranks, sizeText, algoName, extra) != 3 ||
+        nranks < 1 || nranks > kMaxRanks || sizeText[0] < '0' || sizeText[0] > '9' ||
+        (maxBytes = strtoull(sizeText, &sizeEnd, 10), *sizeEnd != '\0' || errno == ERANGE)) {
       if (error) *error = "line " + std::to_string(lineNo) + ": want <nranks> <max_bytes> <algo>";
+      out->entries.clear();
       return false;
     }
     const int algo = parseAlgo(algoName);
     if (algo <= TNCCL_ALGO_AUTO) {
       if (error) *error = "line " + std::to_string(lineNo) + ": unknown algorithm " + algoName;
+      out->entries.clear();
       return false;
     }
     out->entries.push_back(TuningEntry{nranks, (uint64_t)maxBytes, algo});

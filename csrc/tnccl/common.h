@@ -42,7 +42,8 @@ struct TuningEntry {
 struct TuningTable {
   std::vector<TuningEntry> entries;  // sorted by (nranks, maxBytes)
 };
-// Parses `text`; false (and *error set) on a malformed line.
+// Parses `text`; false (*error set, the table left empty) on a malformed
+// line.
 bool parseTuningTable(const std::string& text, TuningTable* out, std::string* error);
 // The table's algorithm for (nranks, bytes), or -1 when no line applies.
 int tunedAlgo(const TuningTable& t, int nranks, uint64_t bytes);

@@ -342,6 +342,35 @@ void testTcpNonceMismatch() {
                                    codes[1] == TNCCL_INVALID_ARGUMENT);
 }
 
+// Random 128-byte ids decode as neither kind unless their magic matches,
+// and never crash the decoders.
+void testFuzzedIds() {
+  uint64_t x = 88172645463325252ull;
+  auto next = [&x] {
+    x ^= x << 13;
+    x ^= x >> 7;
+    x ^= x << 17;
+    return x;
+  };
+  bool ok = true;
+  for (int it = 0; it < 20000; ++it) {
+    tncclUniqueId id{};
+    for (auto& b : id.bytes) b = (unsigned char)next();
+    if (it % 4 == 1) memcpy(id.bytes, "TNCBB002", 8);  // right magic, random rest
+    if (it % 4 == 2) memcpy(id.bytes, "TNCBT003", 8);
+    char path[108];
+    uint32_t ip = 0;
+    int port = 0;
+    uint64_t nonce = 0;
+    const bool un = bootstrapDecodeId(id, path);
+    const bool tcp = bootstrapDecodeTcpId(id, &ip, &port, &nonce);
+    ok = ok && !(un && tcp);
+    if (un) ok = ok && path[0] == '/' && strlen(path) < sizeof(path);
+    if (tcp) ok = ok && port > 0 && port < 65536 && nonce != 0;
+  }
+  report("fuzzed ids", ok);
+}
+
 // A TCP rendezvous is reachable by anything on the network: random bytes
 // instead of a hello must make rank 0 fail the rendezvous, not crash or hang.
 void testFuzzedHello() {
@@ -399,6 +428,7 @@ int main() {
   testLargeGather(false);
   testLargeGather(true);
   testFuzzedHello();
+  testFuzzedIds();
   printf("bootstrap_test: %s\n", gFailed ? "FAIL" : "PASS");
   return gFailed ? 1 : 0;
 }

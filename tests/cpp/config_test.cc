@@ -148,6 +148,49 @@ void hashes() {
   check(configHash(a) == configHash(b), "configHash ignores rank-local knobs");
 }
 
+// Random text never crashes the tuning-table parser; whatever it accepts is
+// sorted and holds only valid rank counts and algorithms.
+void fuzzedTuningTables() {
+  uint64_t x = 0x2545F4914F6CDD1Dull;
+  auto next = [&x] {
+    x ^= x << 13;
+    x ^= x >> 7;
+    x ^= x << 17;
+    return x;
+  };
+  const char* pieces[] = {"8", "4", " ", "1048576", "oneshot", "twoshot", "ring", "nvls",
+                          "\n", "#", "x", "-1", "99", "18446744073709551615", "\t", "auto"};
+  bool ok = true;
+  for (int it = 0; it < 5000; ++it) {
+    std::string text;
+    const int n = (int)(next() % 40);
+    for (int k = 0; k < n; ++k) text += pieces[next() % (sizeof(pieces) / sizeof(pieces[0]))];
+    TuningTable t;
+    std::string err;
+    if (parseTuningTable(text, &t, &err)) {
+      for (size_t i = 0; i < t.entries.size(); ++i) {
+        const TuningEntry& e = t.entries[i];
+        ok = ok && e.nranks >= 1 && e.nranks <= kMaxRanks && e.algo > TNCCL_ALGO_AUTO &&
+             e.algo < TNCCL_NUM_ALGOS;
+        if (i) {
+          const TuningEntry& p = t.entries[i - 1];
+          ok = ok && (p.nranks < e.nranks || (p.nranks == e.nranks && p.maxBytes <= e.maxBytes));
+        }
+      }
+    } else {
+      ok = ok && !err.empty() && t.entries.empty();
+    }
+  }
+  check(ok, "fuzzed tuning tables");
+  TuningTable t;
+  std::string err;
+  check(!parseTuningTable("8 -1 ring\n", &t, &err) &&
+            !parseTuningTable("8 99999999999999999999999 ring\n", &t, &err) &&
+            !parseTuningTable("8 12abc ring\n", &t, &err) &&
+            !parseTuningTable("8 4096 ring\n8 x ring\n", &t, &err) && t.entries.empty(),
+        "tuning: negative / overflowing / malformed sizes rejected, table left empty");
+}
+
 void tuningTables() {
   TuningTable t;
   std::string err;
@@ -298,6 +341,7 @@ int main() {
   adaptChunks();
   hashes();
   tuningTables();
+  fuzzedTuningTables();
   teamSplits();
   layouts();
   plans();
