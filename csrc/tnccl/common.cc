@@ -142,8 +142,9 @@ Config loadConfig() {
 
 int parseSplit(const std::string& s, int dflt) {
   int a = 0, b = 0;
+  char extra = 0;
   if (s.empty()) return dflt;
-  if (sscanf(s.c_str(), "%d,%d", &a, &b) != 2 || a < 1 || b < 1 || a + b > 7) {
+  if (sscanf(s.c_str(), "%d,%d%c", &a, &b, &extra) != 2 || a < 1 || b < 1 || a + b > 7) {
     TN_WARN("malformed team split '%s' (want a,b in eighths, a + b <= 7); using default",
             s.c_str());
     return dflt;

@@ -72,7 +72,8 @@ void defaultsAndOverrides() {
   check(c.tsSplit == (2 | (4 << 4)) && c.nvlsSplit == (1 | (4 << 4)),
         "malformed splits fall back to the defaults");
   check(parseSplit("", 7) == 7 && parseSplit("1,1", 0) == (1 | (1 << 4)) &&
-            parseSplit("0,3", 9) == 9 && parseSplit("4,4", 9) == 9,
+            parseSplit("0,3", 9) == 9 && parseSplit("4,4", 9) == 9 &&
+            parseSplit("3,2x", 9) == 9,
         "parseSplit bounds");
 
   setenv("TNCCL_TWOSHOT_STAGES", "8", 1);
