@@ -365,7 +365,9 @@ tncclResult netAcceptEdge(int listenFd, const NetHello& expect, const NetOptions
       break;
     }
     NetHello h{};
-    Io io = readAll(fd, &h, sizeof(h), d);
+    // A connection gets one second for its hello, so a silent stray one
+    // cannot use up the whole deadline.
+    Io io = readAll(fd, &h, sizeof(h), std::min(d, deadlineIn(1000)));
     if (io != Io::kOk) {
       // Not one of ours (or it gave up): drop it and keep waiting.
       close(fd);

@@ -501,6 +501,44 @@ void testFuzzedStreams() {
     ok = ok && err.load() != 0 && guard;
   }
   report("40 fuzzed receive streams: failure recorded, FIFO bounds kept", ok);
+
+  // Junk connections to a listening edge (short reads, foreign hellos of
+  // random bytes) are dropped; the real connector still gets through.
+  ok = true;
+  for (int seed = 0; seed < 10 && ok; ++seed) {
+    std::mt19937 g((unsigned)(100 + seed));
+    int port = 0;
+    const int lfd = tcpListen("127.0.0.1", 0, 32, &port);
+    uint32_t ip = 0;
+    parseIpv4("127.0.0.1", &ip);
+    NetHello good{kNetHelloMagic, kNetVersion, 0, 0, 1, 4242, 4096, 4, 1};
+    tncclResult acc = TNCCL_SYSTEM_ERROR;
+    int fdsB[kMaxNetChannels];
+    std::thread acceptor([&] { acc = netAcceptEdge(lfd, good, o, fdsB, 5000); });
+    // One stray connection that stays open and silent: it is dropped after
+    // its hello's one-second allowance, not at the accept deadline.
+    Io whySilent = Io::kOk;
+    const int silent = seed == 0 ? tcpConnect(ip, port, deadlineIn(2000), &whySilent) : -1;
+    for (int j = 0; j < 4; ++j) {
+      Io why = Io::kOk;
+      const int fd = tcpConnect(ip, port, deadlineIn(2000), &why);
+      if (fd < 0) continue;
+      std::vector<unsigned char> junk((size_t)(1 + g() % (2 * sizeof(NetHello))));
+      for (auto& c : junk) c = (unsigned char)g();
+      (void)writeAll(fd, junk.data(), junk.size(), deadlineIn(1000));
+      close(fd);
+    }
+    int fdsA[kMaxNetChannels];
+    const tncclResult c = netConnectEdge(ip, port, good, o, fdsA, 3000);
+    const tncclResult w = c == TNCCL_SUCCESS ? netWaitAcks(fdsA, 1, 3000) : c;
+    acceptor.join();
+    close(lfd);
+    if (silent >= 0) close(silent);
+    if (c == TNCCL_SUCCESS) close(fdsA[0]);
+    if (acc == TNCCL_SUCCESS) close(fdsB[0]);
+    ok = w == TNCCL_SUCCESS && acc == TNCCL_SUCCESS;
+  }
+  report("junk connections to a listening edge are dropped", ok);
 }
 
 // ---------------------------------------------------------------------------
