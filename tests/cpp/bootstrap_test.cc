@@ -8,6 +8,7 @@
 #include <stdlib.h>
 #include <string.h>
 #include <sys/mman.h>
+#include <sys/socket.h>
 #include <sys/wait.h>
 #include <unistd.h>
 
@@ -342,6 +343,46 @@ void testTcpNonceMismatch() {
                                    codes[1] == TNCCL_INVALID_ARGUMENT);
 }
 
+// A peer whose "rank 0" answers its hello with random bytes (or a frame
+// header claiming a huge payload) fails the rendezvous instead of crashing,
+// hanging past its deadline or allocating what the header claims.
+void testFuzzedHub() {
+  bool ok = true;
+  for (int seed = 0; seed < 20 && ok; ++seed) {
+    int port = 0;
+    const int lfd = tcpListen("127.0.0.1", 0, 4, &port);
+    tncclUniqueId id{};
+    bootstrapNewTcpId(&id, "127.0.0.1", port);
+    pid_t kid = fork();
+    if (kid == 0) {
+      Bootstrap b;
+      _exit(bootstrapOpen(&b, id, 2, 1, 1, 3000) == TNCCL_SUCCESS ? 0 : 1);
+    }
+    Io why = Io::kOk;
+    const int fd = acceptOne(lfd, deadlineIn(3000), &why);
+    if (fd >= 0) {
+      unsigned char buf[512];
+      (void)recv(fd, buf, sizeof(buf), 0);  // the hello
+      uint64_t x = 0x9e3779b97f4a7c15ull * (uint64_t)(seed + 7);
+      const size_t n = 1 + (size_t)(x % sizeof(buf));
+      for (size_t i = 0; i < n; ++i) {
+        x ^= x << 13;
+        x ^= x >> 7;
+        x ^= x << 17;
+        buf[i] = (unsigned char)x;
+      }
+      if (seed % 2 == 0 && n >= 24) memset(buf + 16, 0xff, 8);  // a huge "payload" length
+      (void)writeAll(fd, buf, n, deadlineIn(1000));
+      close(fd);
+    }
+    close(lfd);
+    int st = 0;
+    waitpid(kid, &st, 0);
+    ok = fd >= 0 && WIFEXITED(st) && WEXITSTATUS(st) == 1;
+  }
+  report("fuzzed answers from rank 0", ok);
+}
+
 // Random 128-byte ids decode as neither kind unless their magic matches,
 // and never crash the decoders.
 void testFuzzedIds() {
@@ -429,6 +470,7 @@ int main() {
   testLargeGather(true);
   testFuzzedHello();
   testFuzzedIds();
+  testFuzzedHub();
   printf("bootstrap_test: %s\n", gFailed ? "FAIL" : "PASS");
   return gFailed ? 1 : 0;
 }
