@@ -263,3 +263,19 @@ def test_example_makes_tcp_ids_for_multi_host_runs(built):
     assert run([exe, "--make-id", "localhost:29500"], timeout=60).returncode == 2
     assert run([exe, "2", "10", "--ranks", "0:1", "--id", "zz"], timeout=60).returncode == 2
     assert run([exe, "2", "10", "--ranks", "1:2", "--id", hexid], timeout=60).returncode == 2
+
+
+def test_environment_report(built):
+    """python -m tiny_nccl_b200 reports versions, devices, the peer matrix and
+    the TNCCL_* settings as JSON (no devices on a CPU-only host)."""
+    import json
+    import sys
+
+    r = run([sys.executable, "-m", "tiny_nccl_b200"], timeout=120,
+            env={"TNCCL_NET": "auto"})
+    assert r.returncode == 0, r.stderr[-2000:]
+    info = json.loads(r.stdout)
+    assert info["tnccl_version"] >= 10000 and info["env"]["TNCCL_NET"] == "auto"
+    assert isinstance(info["devices"], list) and isinstance(info["peers"], list)
+    t = run([sys.executable, "-m", "tiny_nccl_b200", "--text"], timeout=120)
+    assert t.returncode == 0 and "tnccl" in t.stdout
