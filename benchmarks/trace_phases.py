@@ -7,6 +7,14 @@ spread of the time channel 0..C-1 spend between consecutive marks.
 
     TNCCL_TRACE=1 python -m torch.distributed.run --nproc-per-node 2 \
         --master-addr 127.0.0.1 benchmarks/trace_phases.py --algo twoshot --bytes 64M
+
+`--chrome trace.json` also writes the marks of every rank as one Chrome /
+Perfetto trace (process = rank, thread = channel; team busy intervals as
+spans, the other marks as instants). A `--dump` file converts offline, no
+GPU needed:
+
+    python benchmarks/trace_phases.py --convert dump.rank0.json --algo twoshot \
+        --chrome trace.json
 """
 from __future__ import annotations
 
@@ -69,6 +77,40 @@ def team_stats(raw: dict, fam: int) -> dict:
     return out
 
 
+def chrome_events(raw: dict, fam: int, rank: int) -> list:
+    """Trace Event Format events of one rank's marks: raw maps a channel to
+    its [(globaltimer ns, phase, tile)] list. Timestamps are microseconds
+    from the rank's first mark."""
+    marks = [t for ev in raw.values() for t, _, _ in ev]
+    if not marks:
+        return []
+    t0 = min(marks)
+    names = NAMES.get(fam, {})
+    spans = {e: (team, s) for team, (s, e) in TEAMS.get(fam, {}).items() if s is not None}
+    out = [{"ph": "M", "name": "process_name", "pid": rank, "args": {"name": f"rank {rank}"}}]
+    for c, ev in sorted(raw.items(), key=lambda kv: int(kv[0])):
+        c = int(c)
+        out.append({"ph": "M", "name": "thread_name", "pid": rank, "tid": c,
+                    "args": {"name": f"channel {c}"}})
+        start = {}
+        for t, p, tile in ev:
+            us = (t - t0) / 1e3
+            if p in spans and (spans[p][1], tile) in start:
+                b = start.pop((spans[p][1], tile))
+                out.append({"ph": "X", "name": spans[p][0], "pid": rank, "tid": c, "ts": b,
+                            "dur": max(us - b, 0.0), "args": {"tile": tile}})
+            else:
+                start[(p, tile)] = us
+                out.append({"ph": "i", "s": "t", "name": names.get(p, f"phase {p}"),
+                            "pid": rank, "tid": c, "ts": us, "args": {"tile": tile}})
+    return out
+
+
+def write_chrome(path: str, events: list) -> None:
+    with open(path, "w") as f:
+        json.dump({"traceEvents": events, "displayTimeUnit": "ns"}, f)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--algo", default="twoshot")
@@ -76,7 +118,15 @@ def main():
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--out", default="")
     ap.add_argument("--dump", default="", help="write every channel's raw events (JSON) here")
+    ap.add_argument("--chrome", default="", help="write a Chrome / Perfetto trace here")
+    ap.add_argument("--convert", default="", help="a --dump file to convert (no run)")
     args = ap.parse_args()
+    if args.convert:
+        with open(args.convert) as f:
+            raw = {int(c): [tuple(e) for e in ev] for c, ev in json.load(f).items()}
+        write_chrome(args.chrome or args.convert + ".trace.json",
+                     chrome_events(raw, FAMILY[args.algo], 0))
+        return
     assert os.environ.get("TNCCL_TRACE") == "1", "run with TNCCL_TRACE=1"
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     torch.cuda.set_device(rank)
@@ -120,6 +170,11 @@ def main():
             json.dump(raw, f)
     allrec = [None] * world
     dist.all_gather_object(allrec, rec)
+    if args.chrome:
+        events = [None] * world
+        dist.all_gather_object(events, chrome_events(raw, fam, rank))
+        if rank == 0:
+            write_chrome(args.chrome, [e for ev in events for e in ev])
     if rank == 0:
         for r in allrec:
             print(json.dumps(r))

@@ -279,3 +279,26 @@ def test_environment_report(built):
     assert isinstance(info["devices"], list) and isinstance(info["peers"], list)
     t = run([sys.executable, "-m", "tiny_nccl_b200", "--text"], timeout=120)
     assert t.returncode == 0 and "tnccl" in t.stdout
+
+
+def test_trace_to_chrome_conversion(tmp_path):
+    """benchmarks/trace_phases.py turns a phase-trace dump into a Chrome /
+    Perfetto trace: team busy intervals as spans, other marks as instants."""
+    import json
+    import sys
+
+    # Two channels of a two-shot trace: (globaltimer ns, phase, tile).
+    raw = {"0": [[1000, 0, 0], [1500, 1, 0], [4000, 2, 0], [4500, 4, 0], [9000, 5, 0]],
+           "3": [[1200, 0, 0], [2000, 1, 0], [5000, 2, 0]]}
+    dump = tmp_path / "dump.rank0.json"
+    dump.write_text(json.dumps(raw))
+    out = tmp_path / "trace.json"
+    r = run([sys.executable, os.path.join(ROOT, "benchmarks", "trace_phases.py"), "--convert",
+             str(dump), "--algo", "twoshot", "--chrome", str(out)], timeout=120)
+    assert r.returncode == 0, r.stderr[-2000:]
+    ev = json.loads(out.read_text())["traceEvents"]
+    spans = [e for e in ev if e["ph"] == "X"]
+    assert {(e["name"], e["tid"]) for e in spans} == {("reduce", 0), ("gather", 0), ("reduce", 3)}
+    red0 = next(e for e in spans if e["name"] == "reduce" and e["tid"] == 0)
+    assert abs(red0["ts"] - 0.5) < 1e-9 and abs(red0["dur"] - 2.5) < 1e-9
+    assert any(e["ph"] == "i" and e["name"] == "pushed+published" for e in ev)
