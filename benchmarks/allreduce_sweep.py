@@ -14,6 +14,11 @@ ranks of (elapsed / K). Bus bandwidth follows the nccl-tests convention
 busBW = bytes / t * 2(P-1)/P. Buffers are Normal(0,1) seeded per rank and
 are much larger than L2 from 256 MiB up; smaller sizes run L2-resident, as
 they do in nccl-tests. Each line of the output file is one JSON record.
+
+``--impls nvls_zc`` runs the NVLS algorithm on buffers from tncclMemAlloc
+registered with the communicator; with TNCCL_NVLS_ZERO_COPY=1 in the
+environment that is the zero-copy kernel (no copy through the communicator's
+multicast region), otherwise the staged one.
 """
 from __future__ import annotations
 
@@ -115,8 +120,9 @@ def main():
     stream = torch.cuda.Stream(device=dev)
     comm = tn.init_from_torch_distributed(device=local)
     info = comm.info()
-    if "nvls" in impls and not info["nvls"]:
-        impls.remove("nvls")
+    for name in ("nvls", "nvls_zc"):
+        if name in impls and not info["nvls"]:
+            impls.remove(name)
     ref = None
     if "ref" in impls:
         path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
@@ -137,6 +143,15 @@ def main():
     gen.manual_seed(1234 + rank)
     src = torch.randn(maxn, dtype=torch.float32, device=dev, generator=gen).to(dtype)
     dst = torch.empty_like(src)
+    # nvls_zc: the NVLS kernel on buffers registered with the communicator
+    # (zero-copy when TNCCL_NVLS_ZERO_COPY=1, the staged kernel otherwise).
+    reg = None
+    if "nvls_zc" in impls:
+        from tiny_nccl_b200.parallel import empty_registrable
+        rsrc = empty_registrable(maxn, dtype, dev)
+        rdst = empty_registrable(maxn, dtype, dev)
+        rsrc.copy_(src)
+        reg = (rsrc, rdst, comm.register(rsrc), comm.register(rdst))
     out = open(args.out, "a") if (args.out and rank == 0) else None
     results = []
     for size in sizes:
@@ -152,6 +167,8 @@ def main():
                     dist.all_reduce(y)  # in place, like NCCL's own bench
                 elif impl == "ref":
                     ref.all_reduce(x.data_ptr(), y.data_ptr(), n, stream.cuda_stream)
+                elif impl == "nvls_zc":
+                    comm.all_reduce(reg[0][:n], reg[1][:n], algo="nvls")
                 else:
                     comm.all_reduce(x, y, algo=impl)
 
@@ -194,7 +211,8 @@ def main():
                     dist.all_reduce(ref_y)
                     op()
                 torch.cuda.synchronize()
-                err = (y.float() - ref_y.float()).abs().max().item()
+                got = reg[1][:n] if impl == "nvls_zc" else y
+                err = (got.float() - ref_y.float()).abs().max().item()
                 rec["max_abs_err_vs_nccl"] = err
             results.append(rec)
             if rank == 0:
@@ -208,6 +226,9 @@ def main():
     dist.barrier()
     if ref is not None:
         ref.destroy()
+    if reg is not None:
+        comm.deregister(reg[2])
+        comm.deregister(reg[3])
     comm.destroy()
     dist.destroy_process_group()
 

@@ -37,8 +37,9 @@ NAMES = {
         4: "reduced+acked"},
     3: {1: "copied in", 2: "all copied in", 3: "switch reduce+store counted",
         4: "all stored", 5: "copied out"},
+    4: {1: "all entered", 2: "reduced+stored", 3: "all stored"},
 }
-FAMILY = {"ring": 0, "oneshot": 1, "twoshot": 2, "nvls": 3}
+FAMILY = {"ring": 0, "oneshot": 1, "twoshot": 2, "nvls": 3, "nvls_zc": 4}
 
 # Warp-specialised kernels: each team marks its own phases. (start mark,
 # end mark) pairs give a team's busy time per tile; (end of tile t-1, start

@@ -26,7 +26,9 @@
 //            rank's share in the NVSwitch (multimem.ld_reduce) and broadcast
 //            it with multimem.st, and copy the result out; the barriers
 //            between them are per-slot counters that every rank increments
-//            on every GPU with one multimem.red.
+//            on every GPU with one multimem.red. For buffers registered with
+//            tncclCommRegister a zero-copy variant reduces and broadcasts
+//            straight from and into the user's buffers.
 //
 // Every wait is bounded (device.cuh); a CTA whose wait fails stops, leaves
 // its sequence number untouched and the host sees the recorded error.
@@ -211,6 +213,10 @@ cudaError_t launchTyped(const DevComm& comm, const AllReduceArgs& a, int algo, i
         oneShotKernel<T, 16><<<a.block.channels, block, 0, stream>>>(comm, a);
       break;
     case TNCCL_ALGO_NVLS: {
+      if (a.mcSend != nullptr) {
+        nvlsZeroCopyKernel<T><<<a.zcChannels, block, 0, stream>>>(comm, a);
+        break;
+      }
       const uint32_t smem = nvlsSmemBytes(comm);
       cudaError_t err = allowSmem<nvlsKernel<T>>(smem);
       if (err != cudaSuccess) return err;

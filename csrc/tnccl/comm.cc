@@ -450,6 +450,7 @@ extern "C" tncclResult tncclCommDestroy(tncclComm_t comm) {
   if (b1 != TNCCL_SUCCESS) result = b1;
   netStopProxy(comm, b1 == TNCCL_SUCCESS, &result);  // no frame is in flight any more
   nvlsUnmap(comm, &result);
+  registrationsUnmap(comm, &result);
   closePeerMailboxes(comm, &result);
   tncclResult b2 = bootstrapBarrier(&comm->bootstrap);  // every importer has closed
   if (b2 != TNCCL_SUCCESS && result == TNCCL_SUCCESS) result = b2;
@@ -457,6 +458,7 @@ extern "C" tncclResult tncclCommDestroy(tncclComm_t comm) {
   // socket FIFOs whatever the barriers returned.
   netRelease(comm, true);
   if (b1 == TNCCL_SUCCESS && b2 == TNCCL_SUCCESS) {
+    registrationsRelease(comm, &result);
     nvlsRelease(comm, &result);
     freeLocalMailbox(comm, &result);
     freeDeviceState(comm);

@@ -9,6 +9,7 @@
 #include "bootstrap.h"
 #include "common.h"
 #include "devcomm.h"
+#include "driver.h"
 #include "net.h"
 #include "tnccl.h"
 
@@ -61,6 +62,25 @@ struct NvlsState {
   bool mcMapped = false;
 };
 
+// A buffer registered with tncclCommRegister: a range of a tncclMemAlloc
+// allocation bound to a multicast object of its own on every rank, for the
+// zero-copy NVLS all-reduce.
+constexpr int kMaxRegistrations = 32;
+struct Registration {
+  bool used = false;
+  char* base = nullptr;     // the caller's pointer (this process's unicast view)
+  size_t userBytes = 0;     // bytes the caller registered
+  size_t bytes = 0;         // bytes bound (multicast granularity)
+  void* allocation = nullptr;  // base of the tncclMemAlloc allocation it lies in
+  CUmemGenericAllocationHandle mc = 0;
+  bool mcValid = false;
+  bool deviceAdded = false;
+  bool bound = false;
+  CUdeviceptr mcVa = 0;
+  bool reserved = false;
+  bool mapped = false;
+};
+
 // Exchanged through the bootstrap all-gather at init.
 struct PeerMeta {
   int32_t status;
@@ -103,6 +123,7 @@ struct tncclComm {
   tnccl::LocalMailbox local;
   tnccl::PeerMailbox peers[tnccl::kMaxRanks];
   tnccl::NvlsState nvls;
+  tnccl::Registration regs[tnccl::kMaxRegistrations];
   tnccl::NetState net;
   bool allPeersMapped = true;  // every peer is on this host and mapped
   tnccl::DevComm dev{};
@@ -123,6 +144,13 @@ struct tncclComm {
 namespace tnccl {
 
 // transport.cc
+CUmemAllocationProp deviceProp(int device, bool exportable);
+// Logs a failed driver call; true on CUDA_SUCCESS.
+bool cuOk(CUresult r, const char* what);
+// Maps handle at a fresh VA range of `bytes` with read/write access for
+// `device`.
+bool mapHandle(const DriverApi* api, CUmemGenericAllocationHandle h, size_t bytes, size_t align,
+               int device, CUdeviceptr* va, bool* reserved, bool* mapped);
 tncclResult allocLocalMailbox(tncclComm* comm, size_t bytes, bool tryCuMem);
 tncclResult importPeerMailbox(tncclComm* comm, int peer, int fd,
                               const PeerMeta& meta);
@@ -132,6 +160,13 @@ bool nvlsLocallyCapable(const tncclComm* comm);
 tncclResult setupNvls(tncclComm* comm);
 void nvlsUnmap(tncclComm* comm, tncclResult* result);
 void nvlsRelease(tncclComm* comm, tncclResult* result);
+
+// register.cc: the registration holding [p, p + bytes), or nullptr.
+const Registration* findRegistration(const tncclComm* comm, const void* p, size_t bytes);
+// Destroy's halves: unmap and unbind every registration (after barrier 1),
+// release the multicast objects (after barrier 2).
+void registrationsUnmap(tncclComm* comm, tncclResult* result);
+void registrationsRelease(tncclComm* comm, tncclResult* result);
 
 // enqueue.cc
 tncclAlgo_t selectAlgo(const tncclComm* comm, uint64_t bytes);

@@ -89,6 +89,10 @@ Config loadConfig() {
   c.nvlsChannels = clampInt(envInt("TNCCL_NVLS_CHANNELS", 64), 1, kMaxChannels);
   c.nvlsTileBytes = roundTo16(envInt("TNCCL_NVLS_TILE_BYTES", 512 << 10));
   c.nvlsEnable = (int)envInt("TNCCL_NVLS_ENABLE", 1);
+  // Off until it has been measured against the staged kernel.
+  c.nvlsZeroCopy = envInt("TNCCL_NVLS_ZERO_COPY", 0) ? 1 : 0;
+  c.nvlsZcMinBytes = envInt("TNCCL_NVLS_ZC_MIN_BYTES", 1 << 20);
+  c.nvlsZcChannels = clampInt(envInt("TNCCL_NVLS_ZC_CHANNELS", 32), 1, kMaxChannels);
   int algo = parseAlgo(envStr("TNCCL_ALGO", "auto"));
   if (algo < 0) {
     TN_WARN("unknown TNCCL_ALGO; using auto");
@@ -172,6 +176,9 @@ uint64_t configHash(const Config& c) {
   mix(c.nvlsChannels);
   mix(c.nvlsTileBytes);
   mix(c.nvlsEnable);
+  mix(c.nvlsZeroCopy);
+  mix(c.nvlsZcMinBytes);
+  mix(c.nvlsZcChannels);
   mix(c.forcedAlgo);
   mix(c.useCuMem);
   mix(c.oneShotMaxBytes);

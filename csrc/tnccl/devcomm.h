@@ -82,6 +82,13 @@ struct AllReduceArgs {
   // partition (ring / two-shot use chunk, one-shot / NVLS use block)
   ChunkPlan chunk;
   BlockPlan block;
+  // Zero-copy NVLS (set only for buffers registered with tncclCommRegister):
+  // multicast views of send and recv, the message in 16-byte vectors and the
+  // channel count (protocol.h nvlsZcSpan). Null mcSend: the staged kernels.
+  const char* mcSend;
+  char* mcRecv;
+  uint64_t zcVecs;
+  int zcChannels;
 };
 
 // One cooperative launch that emulates `nranks` ranks on one GPU (tests and

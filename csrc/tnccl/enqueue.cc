@@ -122,7 +122,20 @@ extern "C" tncclResult tncclAllReduceEx(const void* send, void* recv, size_t cou
     return TNCCL_SUCCESS;
   }
 
-  tncclAlgo_t chosen = algo == TNCCL_ALGO_AUTO ? selectAlgo(comm, bytes) : algo;
+  // Zero-copy NVLS: both buffers registered (every rank registered the same
+  // buffers, so every rank makes the same choice), whole 16-byte vectors.
+  const Registration* regSend = nullptr;
+  const Registration* regRecv = nullptr;
+  if (comm->cfg.nvlsZeroCopy && comm->nvls.enabled && vectorized && bytes % kVectorBytes == 0 &&
+      (algo == TNCCL_ALGO_NVLS ||
+       (algo == TNCCL_ALGO_AUTO && comm->cfg.forcedAlgo == TNCCL_ALGO_AUTO &&
+        bytes >= (uint64_t)comm->cfg.nvlsZcMinBytes))) {
+    regSend = findRegistration(comm, send, bytes);
+    regRecv = regSend ? findRegistration(comm, recv, bytes) : nullptr;
+  }
+  const bool zeroCopy = regSend != nullptr && regRecv != nullptr;
+  tncclAlgo_t chosen =
+      zeroCopy ? TNCCL_ALGO_NVLS : algo == TNCCL_ALGO_AUTO ? selectAlgo(comm, bytes) : algo;
   if (chosen == TNCCL_ALGO_NVLS && !comm->nvls.enabled) return TNCCL_UNSUPPORTED;
   // The all-peer algorithms need every peer mapped.
   if (chosen != TNCCL_ALGO_RING && !comm->allPeersMapped) return TNCCL_UNSUPPORTED;
@@ -157,6 +170,17 @@ extern "C" tncclResult tncclAllReduceEx(const void* send, void* recv, size_t cou
                               kOneShotMinTileBytes / es, V);
       break;
     case TNCCL_ALGO_NVLS:
+      if (zeroCopy) {
+        a.mcSend = reinterpret_cast<const char*>(regSend->mcVa) +
+                   (static_cast<const char*>(send) - regSend->base);
+        a.mcRecv = reinterpret_cast<char*>(regRecv->mcVa) +
+                   (static_cast<char*>(recv) - regRecv->base);
+        a.zcVecs = bytes / kVectorBytes;
+        // From the message size and the configuration only: equal on every rank.
+        a.zcChannels = nvlsZcChannels(a.zcVecs, comm->nranks, cap(cfg.nvlsZcChannels),
+                                      kNvlsMinTileBytes / kVectorBytes);
+        break;
+      }
       a.block = makeBlockPlan(count, cap(comm->nvls.channels), comm->nvls.tileBytes / es,
                               kNvlsMinTileBytes / es, V);
       break;
@@ -164,8 +188,8 @@ extern "C" tncclResult tncclAllReduceEx(const void* send, void* recv, size_t cou
       return TNCCL_INVALID_ARGUMENT;
   }
   if (cudaGetLastError() != cudaSuccess) return TNCCL_CUDA_ERROR;
-  TN_TRACE("rank %d: allreduce %zu x %zu B algo %s", comm->rank, count, es,
-           tncclAlgoName(chosen));
+  TN_TRACE("rank %d: allreduce %zu x %zu B algo %s%s", comm->rank, count, es,
+           tncclAlgoName(chosen), zeroCopy ? " (zero-copy)" : "");
   NvtxRange range("tncclAllReduce %s %zu B rank %d", tncclAlgoName(chosen), bytes, comm->rank);
   if (launchAllReduceKernel(comm->dev, a, (int)chosen, cfg.threads, stream) != cudaSuccess)
     return TNCCL_CUDA_ERROR;

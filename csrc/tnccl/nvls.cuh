@@ -170,5 +170,88 @@ __global__ void __launch_bounds__(kMaxThreads)
   if (threadIdx.x == 0 && !sFail) comm.counters[kCounterNvls * kMaxChannels + c] = seq0 + ntiles;
 }
 
+// ---------------------------------------------------------------------------
+// Zero-copy NVLS over buffers registered with tncclCommRegister. send and
+// recv are bound to multicast objects of their own, so the switch reads every
+// rank's send directly (multimem.ld_reduce) and multimem.st writes every
+// rank's recv: nothing is copied in or out, and each GPU moves about
+// (1 + 1/P) x the message per NVLink direction.
+//
+// Channel c of every rank counts two phases on every GPU with one
+// multimem.red each: "entered" (this rank's stream reached the kernel, so its
+// send is final and its recv no longer in use) and "stored" (its stores into
+// everyone's recv are issued). A CTA reduces only after all P ranks entered
+// and leaves only after all P stored, so recv is complete when the kernel
+// ends on any rank, and no rank's buffers are touched after its kernel ended.
+// The counters are monotone: launch k of channel c waits for P x (k + 1).
+// Every rank must pass buffers at the same offsets inside their registrations
+// (the multicast address names the same offset on every GPU).
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(kMaxThreads)
+    nvlsZeroCopyKernel(const __grid_constant__ DevComm comm,
+                       const __grid_constant__ AllReduceArgs a) {
+  using Pk = Pack<T>;
+  constexpr int V = Pk::V;
+  const int c = blockIdx.x, P = comm.nranks, r = comm.rank;
+  const float alpha = a.scale;
+  const bool scale = alpha != 1.0f;
+  __shared__ int sFail;
+  if (threadIdx.x == 0) sFail = 0;
+  const uint64_t seq0 = comm.counters[kCounterNvlsZc * kMaxChannels + c];
+  const uint64_t target = (uint64_t)P * (seq0 + 1);
+  auto counterOff = [&](int phase) {
+    return nvlsZcCounterAt(comm.nvlsTileBytes, comm.nvlsChannels, phase, c);
+  };
+  // Counts `phase` on every rank, then waits until all P ranks counted it.
+  auto barrier = [&](int phase) -> bool {
+    fenceProxyAlias();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      multimemAddRelease(reinterpret_cast<uint64_t*>(comm.nvlsMc + counterOff(phase)), 1);
+      if (!waitFlag(comm, reinterpret_cast<const uint64_t*>(comm.nvlsUc + counterOff(phase)),
+                    target, whereCode(kCounterNvlsZc, c, phase + 1)))
+        sFail = 1;
+    }
+    __syncthreads();
+    fenceProxyAlias();
+    return sFail == 0;
+  };
+  if (!barrier(0)) return;
+  traceMark(comm, c, kCounterNvlsZc, 1, seq0);
+  const Span sp = nvlsZcSpan(a.zcVecs, P, r, a.zcChannels, c);
+  const char* const in = a.mcSend + sp.offset * 16;
+  char* const out = a.mcRecv + sp.offset * 16;
+  const uint64_t NT = blockDim.x;
+  constexpr int UN = 8;  // switch reductions in flight per thread
+  for (uint64_t base = threadIdx.x; base < sp.count; base += NT * UN) {
+    uint4 v[UN];
+#pragma unroll
+    for (int u = 0; u < UN; ++u) {
+      const uint64_t i = base + u * NT;
+      if (i < sp.count) v[u] = Multimem<T>::ldReduce(in + i * 16);
+    }
+#pragma unroll
+    for (int u = 0; u < UN; ++u) {
+      const uint64_t i = base + u * NT;
+      if (i < sp.count) {
+        uint4 w = v[u];
+        if (scale) {
+          float f[V];
+          Pk::unpack(w, f);
+#pragma unroll
+          for (int e = 0; e < V; ++e) f[e] = scaled(alpha, f[e]);
+          w = Pk::pack(f);
+        }
+        Multimem<T>::st(out + i * 16, w);
+      }
+    }
+  }
+  traceMark(comm, c, kCounterNvlsZc, 2, seq0);
+  if (!barrier(1)) return;
+  traceMark(comm, c, kCounterNvlsZc, 3, seq0);
+  if (threadIdx.x == 0) comm.counters[kCounterNvlsZc * kMaxChannels + c] = seq0 + 1;
+}
+
 }  // namespace
 }  // namespace tnccl

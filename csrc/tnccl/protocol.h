@@ -49,7 +49,8 @@ enum CounterFamily : int {
   kCounterOneShot = 1,
   kCounterTwoShot = 2,
   kCounterNvls = 3,
-  kNumCounterFamilies = 4
+  kCounterNvlsZc = 4,  // zero-copy NVLS over registered buffers
+  kNumCounterFamilies = 5
 };
 
 TN_HD uint64_t divUp(uint64_t a, uint64_t b) { return (a + b - 1) / b; }
@@ -345,8 +346,36 @@ TN_HD uint64_t nvlsCounterAt(uint64_t tileBytes, int channels, int phase, int c,
   return nvlsDataBytes(tileBytes, channels) +
          (((uint64_t)phase * kMaxChannels + c) * kNvlsSlots + slot) * 8;
 }
+// After those, the zero-copy kernel's barrier counters: one 64-bit word per
+// phase ("entered", "stored") and channel, counted once per launch by every
+// rank, so P x launches means every rank finished that phase of a launch.
+TN_HD uint64_t nvlsZcCounterAt(uint64_t tileBytes, int channels, int phase, int c) {
+  return nvlsDataBytes(tileBytes, channels) + 2ull * kMaxChannels * kNvlsSlots * 8 +
+         ((uint64_t)phase * kMaxChannels + c) * 8;
+}
 TN_HD uint64_t nvlsRegionBytes(uint64_t tileBytes, int channels) {
-  return nvlsDataBytes(tileBytes, channels) + alignUp(2ull * kMaxChannels * kNvlsSlots * 8, 4096);
+  return nvlsDataBytes(tileBytes, channels) +
+         alignUp(2ull * kMaxChannels * kNvlsSlots * 8 + 2ull * kMaxChannels * 8, 4096);
+}
+
+// ---------------------------------------------------------------------------
+// Zero-copy NVLS (buffers registered with tncclCommRegister): the message is
+// nv 16-byte vectors; rank r reduces its share blockShare(nv, P, r, 1), and
+// channel c of C takes an even contiguous part of that share. C depends on
+// the message size only, so it is the same on every rank, and every channel
+// runs (possibly with nothing to reduce) so that the barrier counts agree.
+// ---------------------------------------------------------------------------
+TN_HD int nvlsZcChannels(uint64_t nv, int nranks, int maxChannels, uint64_t minVecsPerChannel) {
+  const uint64_t perRank = divUp(nv, (uint64_t)nranks);
+  const uint64_t want = divUp(perRank, minVecsPerChannel == 0 ? 1 : minVecsPerChannel);
+  const uint64_t cap = maxChannels < 1 ? 1 : (uint64_t)maxChannels;
+  return (int)(want < 1 ? 1 : minU64(want, cap));
+}
+TN_HD Span nvlsZcSpan(uint64_t nv, int nranks, int rank, int channels, int c) {
+  const Span share = blockShare(nv, nranks, rank, 1);
+  const uint64_t per = divUp(share.count, (uint64_t)channels);
+  const uint64_t off = minU64((uint64_t)c * per, share.count);
+  return Span{share.offset + off, minU64(per, share.count - off)};
 }
 
 // ---------------------------------------------------------------------------

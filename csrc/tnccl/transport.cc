@@ -17,7 +17,6 @@
 #include "driver.h"
 
 namespace tnccl {
-namespace {
 
 CUmemAllocationProp deviceProp(int device, bool exportable) {
   CUmemAllocationProp prop{};
@@ -51,8 +50,6 @@ bool mapHandle(const DriverApi* api, CUmemGenericAllocationHandle h, size_t byte
   acc.flags = CU_MEM_ACCESS_FLAGS_PROT_READWRITE;
   return cuOk(api->cuMemSetAccess(*va, bytes, &acc, 1), "cuMemSetAccess");
 }
-
-}  // namespace
 
 tncclResult allocLocalMailbox(tncclComm* comm, size_t bytes, bool tryCuMem) {
   LocalMailbox& m = comm->local;

@@ -222,6 +222,34 @@ class Communicator {
     return std::vector<uint64_t>(buf.begin(), buf.begin() + 2 * n);
   }
 
+  // Collective: binds a tensor that lies in tncclMemAlloc memory (memEmpty)
+  // for the zero-copy NVLS all-reduce; returns the registration handle.
+  uint64_t registerTensor(const at::Tensor& t) {
+    live();
+    TORCH_CHECK(t.is_cuda() && t.get_device() == info_.device && t.is_contiguous(),
+                "tnccl: register needs a contiguous tensor on the communicator's device");
+    c10::cuda::CUDAGuard guard(info_.device);
+    void* h = nullptr;
+    tncclResult r;
+    {
+      py::gil_scoped_release nogil;  // blocking collective
+      r = tncclCommRegister(comm_, t.data_ptr(), (size_t)t.nbytes(), &h);
+    }
+    check(r, "tncclCommRegister");
+    return reinterpret_cast<uint64_t>(h);
+  }
+
+  void deregister(uint64_t handle) {
+    live();
+    c10::cuda::CUDAGuard guard(info_.device);
+    tncclResult r;
+    {
+      py::gil_scoped_release nogil;  // blocking collective
+      r = tncclCommDeregister(comm_, reinterpret_cast<void*>(handle));
+    }
+    check(r, "tncclCommDeregister");
+  }
+
   int rank() const { return info_.rank; }
   int size() const { return info_.nranks; }
   int device() const { return info_.device; }
@@ -276,6 +304,18 @@ class Emulator {
   tncclEmu_t emu_ = nullptr;
 };
 
+// nbytes of tncclMemAlloc memory on `device` as a uint8 tensor; the memory
+// goes back through tncclMemFree when the last view of the tensor dies.
+at::Tensor memEmpty(int64_t nbytes, int device) {
+  TORCH_CHECK(nbytes > 0, "tnccl: mem_empty needs a positive size");
+  c10::cuda::CUDAGuard guard(device);
+  void* p = nullptr;
+  check(tncclMemAlloc(&p, (size_t)nbytes), "tncclMemAlloc");
+  return torch::from_blob(
+      p, {nbytes}, [](void* q) { tncclMemFree(q); },
+      at::TensorOptions().dtype(at::kByte).device(at::kCUDA, device));
+}
+
 py::bytes getUniqueId() {
   tncclUniqueId id;
   check(tncclGetUniqueId(&id), "tncclGetUniqueId");
@@ -315,6 +355,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("diag_bench", &Communicator::diagBench)
       .def("diag_wait_timeout", &Communicator::diagWaitTimeout)
       .def("trace_read", &Communicator::traceRead)
+      .def("register", &Communicator::registerTensor, py::arg("tensor"))
+      .def("deregister", &Communicator::deregister, py::arg("handle"))
       .def_property_readonly("rank", &Communicator::rank)
       .def_property_readonly("size", &Communicator::size)
       .def_property_readonly("device", &Communicator::device)
@@ -326,6 +368,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("async_error", &Emulator::asyncError)
       .def("destroy", &Emulator::destroy);
   m.def("get_unique_id", &getUniqueId);
+  m.def("mem_empty", &memEmpty, py::arg("nbytes"), py::arg("device"));
   m.def("get_unique_id_tcp", &getUniqueIdTcp);
   m.def("launch_count", []() { return tncclGetLaunchCount(); });
   m.def("error_string", [](int r) { return std::string(tncclGetErrorString((tncclResult)r)); });

@@ -202,6 +202,31 @@ tncclResult tncclCommAbort(tncclComm_t comm);
  * TNCCL_BOOTSTRAP_ADDR=<ipv4>:<port> is set. */
 tncclResult tncclGetUniqueIdTcp(tncclUniqueId* id, const char* ipv4, int port);
 
+/* ---- registered buffers (zero-copy NVLS) ---------------------------------
+ * tncclMemAlloc returns device memory on the current device (a cuMem
+ * allocation, rounded up to the multicast granularity) that can be bound to
+ * an NVSwitch multicast object; cudaMalloc memory cannot. tncclMemFree
+ * synchronizes the device first, like cudaFree, and refuses memory that is
+ * still registered. */
+tncclResult tncclMemAlloc(void** ptr, size_t size);
+tncclResult tncclMemFree(void* ptr);
+
+/* Collective: every rank calls it in the same order with a buffer of the
+ * same size inside a tncclMemAlloc allocation (at its start, or at an offset
+ * that is a multiple of the multicast granularity). It binds the buffer to a
+ * multicast object of its own on every rank. An NVLS all-reduce whose send
+ * and recv both lie in registered buffers, at the same offsets on every
+ * rank, 16-byte aligned and a multiple of 16 bytes long, then reduces
+ * straight from the senders' buffers and stores into every receiver's, with
+ * no copy through the communicator's own region (opt-in while it has not
+ * been measured: TNCCL_NVLS_ZERO_COPY=1). TNCCL_UNSUPPORTED when the
+ * communicator has no NVLS. */
+tncclResult tncclCommRegister(tncclComm_t comm, void* buff, size_t size, void** handle);
+/* Collective: waits for the bound stream, then unbinds on every rank
+ * (two barriers, as tncclCommDestroy). tncclCommDestroy deregisters what is
+ * left. */
+tncclResult tncclCommDeregister(tncclComm_t comm, void* handle);
+
 const char* tncclAlgoName(tncclAlgo_t algo);
 tncclResult tncclGetVersion(int* version);
 

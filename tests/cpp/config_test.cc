@@ -147,6 +147,15 @@ void hashes() {
   b.tsSplit = 3 | (3 << 4);
   b.timeoutMs = 5;
   check(configHash(a) == configHash(b), "configHash ignores rank-local knobs");
+  // Whether and with how many CTAs the zero-copy NVLS kernel runs must agree.
+  b = a;
+  b.nvlsZeroCopy = !a.nvlsZeroCopy;
+  check(configHash(a) != configHash(b), "configHash covers TNCCL_NVLS_ZERO_COPY");
+  b = a;
+  b.nvlsZcChannels = a.nvlsZcChannels + 1;
+  check(configHash(a) != configHash(b), "configHash covers TNCCL_NVLS_ZC_CHANNELS");
+  check(a.nvlsZeroCopy == 0 && a.nvlsZcMinBytes == (1 << 20) && a.nvlsZcChannels == 32,
+        "defaults: zero-copy NVLS off, 1 MiB, 32 channels");
 }
 
 // Random text never crashes the tuning-table parser; whatever it accepts is
@@ -288,6 +297,9 @@ void layouts() {
   check(nvlsCounterAt(tb, 64, 1, 127, kNvlsSlots - 1) + 8 <= nvlsRegionBytes(tb, 64) &&
             nvlsCounterAt(tb, 64, 0, 0, 0) == nvlsDataBytes(tb, 64),
         "NVLS counters follow the data blocks inside the region");
+  check(nvlsZcCounterAt(tb, 64, 0, 0) == nvlsCounterAt(tb, 64, 1, kMaxChannels - 1, kNvlsSlots - 1) + 8 &&
+            nvlsZcCounterAt(tb, 64, 1, kMaxChannels - 1) + 8 <= nvlsRegionBytes(tb, 64),
+        "zero-copy NVLS counters follow the staged kernel's inside the region");
 }
 
 void plans() {

@@ -46,7 +46,7 @@ void report(const char* what, bool ok) {
   if (!ok) ++gFailed;
 }
 
-enum Algo { kRing = 1, kOneShot = 2, kTwoShot = 3, kNvls = 4 };
+enum Algo { kRing = 1, kOneShot = 2, kTwoShot = 3, kNvls = 4, kNvlsZc = 5 };
 
 struct Config {
   int P = 4;
@@ -123,6 +123,33 @@ struct World {
     auto start = std::chrono::steady_clock::now();
     uint64_t spins = 0;
     while (mcCounter(r, phase, c, s).load(std::memory_order_acquire) < want) {
+      if ((++spins & 1023) == 0) {
+        if (error.load()) return false;
+        if (std::chrono::steady_clock::now() - start > std::chrono::milliseconds(cfg.timeoutMs)) {
+          error.store(5);
+          return false;
+        }
+        std::this_thread::yield();
+      }
+    }
+    return true;
+  }
+
+  // Zero-copy NVLS barrier counters ("entered", "stored") per rank and channel.
+  std::unique_ptr<std::atomic<uint64_t>[]> zcCount{
+      new std::atomic<uint64_t>[(size_t)kMaxRanks * 2 * kMaxChannels]()};
+  std::atomic<uint64_t>& zcCounter(int r, int phase, int c) {
+    return zcCount[((size_t)r * 2 + phase) * kMaxChannels + c];
+  }
+  void zcAdd(int self, int phase, int c) {
+    int n = __atomic_fetch_add(&published[(size_t)self], 1, __ATOMIC_RELAXED);
+    if (self == dropRank && n == dropAt) return;  // injected loss
+    for (int q = 0; q < cfg.P; ++q) zcCounter(q, phase, c).fetch_add(1, std::memory_order_release);
+  }
+  bool zcWait(int r, int phase, int c, uint64_t want) {
+    auto start = std::chrono::steady_clock::now();
+    uint64_t spins = 0;
+    while (zcCounter(r, phase, c).load(std::memory_order_acquire) < want) {
       if ((++spins & 1023) == 0) {
         if (error.load()) return false;
         if (std::chrono::steady_clock::now() - start > std::chrono::milliseconds(cfg.timeoutMs)) {
@@ -393,6 +420,51 @@ bool nvls(World& w, int r, const Job& j, uint64_t count) {
   return true;
 }
 
+bool nvlsZeroCopy(World& w, int r, const Job& j, uint64_t count) {
+  // Same structure as nvlsZeroCopyKernel: one thread per channel; every
+  // channel of every rank counts "entered" and "stored" on every rank, and
+  // the switch reads every rank's buffer and writes every rank's output in
+  // place. In place really is one buffer here (reads go to y, which starts
+  // as a copy of x), so a read after another rank's store would show.
+  // Messages that are not whole vectors take the staged kernel, as the host
+  // does.
+  const Config& c = w.cfg;
+  if (count % c.vec != 0) return nvls(w, r, j, count);
+  const int P = c.P;
+  const uint64_t nv = count / c.vec;
+  const int C = nvlsZcChannels(nv, P, c.nvlsChannels, 2);
+  std::vector<std::vector<float>>& y = *j.y;
+  const std::vector<std::vector<float>>& in = j.inPlace ? y : *j.x;
+  std::atomic<int> fail{0};
+  auto channel = [&](int ch) {
+    uint64_t& seq = w.counters[(size_t)r][kCounterNvlsZc * kMaxChannels + ch];
+    const uint64_t target = (uint64_t)P * (seq + 1);
+    w.zcAdd(r, 0, ch);
+    if (!w.zcWait(r, 0, ch, target)) {
+      fail.store(1);
+      return;
+    }
+    const Span sp = nvlsZcSpan(nv, P, r, C, ch);
+    for (uint64_t e = sp.offset * c.vec; e < (sp.offset + sp.count) * c.vec; ++e) {
+      float acc = in[0][e];
+      for (int q = 1; q < P; ++q) acc = oracle::add(acc, in[(size_t)q][e]);
+      const float v = rnd(j.dtype, oracle::mul(j.alpha, acc));
+      for (int q = 0; q < P; ++q) y[(size_t)q][e] = v;  // multicast store
+    }
+    w.zcAdd(r, 1, ch);
+    if (!w.zcWait(r, 1, ch, target)) {
+      fail.store(1);
+      return;
+    }
+    ++seq;
+  };
+  std::vector<std::thread> th;
+  for (int ch = 1; ch < C; ++ch) th.emplace_back(channel, ch);
+  channel(0);
+  for (auto& t : th) t.join();
+  return fail.load() == 0;
+}
+
 bool ring(World& w, int r, const Job& j, uint64_t count) {
   const Config& c = w.cfg;
   const int P = c.P;
@@ -488,6 +560,7 @@ bool collective(World& w, Algo a, const Job& j, uint64_t count) {
       bool res = a == kRing      ? ring(w, r, j, count)
                  : a == kOneShot ? oneShot(w, r, j, count)
                  : a == kNvls    ? nvls(w, r, j, count)
+                 : a == kNvlsZc  ? nvlsZeroCopy(w, r, j, count)
                                  : twoShot(w, r, j, count);
       ok[(size_t)r] = res ? 1 : 0;
     });
@@ -522,7 +595,7 @@ bool checkOne(World& w, Algo a, int dtype, uint64_t count, bool inPlace, bool av
     ChunkPlan pl = makeChunkPlan(count, P, w.cfg.channels, w.cfg.ringChunkElems, w.cfg.minChunk,
                                  w.cfg.vec);
     oracle::ring(dtype, x, alpha, pl, w.cfg.vec, want);
-  } else if (a == kNvls) {
+  } else if (a == kNvls || a == kNvlsZc) {
     // The switch sums first and the pre-scale applies to the sum.
     want.resize(count);
     for (uint64_t e = 0; e < count; ++e) {
@@ -544,11 +617,15 @@ bool checkOne(World& w, Algo a, int dtype, uint64_t count, bool inPlace, bool av
 }
 
 const char* algoName(Algo a) {
-  return a == kRing ? "ring" : a == kOneShot ? "oneshot" : a == kNvls ? "nvls" : "twoshot";
+  return a == kRing      ? "ring"
+         : a == kOneShot ? "oneshot"
+         : a == kNvls    ? "nvls"
+         : a == kNvlsZc  ? "nvls zero-copy"
+                         : "twoshot";
 }
 
 void referenceMatrix() {
-  for (Algo a : {kRing, kOneShot, kTwoShot, kNvls}) {
+  for (Algo a : {kRing, kOneShot, kTwoShot, kNvls, kNvlsZc}) {
     bool ok = true;
     for (int P : {1, 2, 3, 4, 7}) {
       Config c;
@@ -578,7 +655,7 @@ void baselineConfig1() {
   c.ringSlots = 8;
   c.ringChunkElems = 16384;  // 64 KiB of fp32 per slot
   c.channels = 4;
-  for (Algo a : {kRing, kTwoShot, kOneShot, kNvls}) {
+  for (Algo a : {kRing, kTwoShot, kOneShot, kNvls, kNvlsZc}) {
     for (int t : {oracle::kF32, oracle::kBF16}) {
       World w(c);
       bool ok = true;
@@ -607,7 +684,7 @@ void sequenceContinuity() {
   uint64_t seed = 5;
   // 200 collectives of varying size and algorithm on the same mailboxes.
   for (int i = 0; i < 200 && ok; ++i) {
-    Algo a = (Algo)(1 + i % 4);
+    Algo a = (Algo)(1 + i % 5);
     uint64_t n = (uint64_t)((i * 37) % 900);
     ok = checkOne(w, a, i % 2 ? oracle::kBF16 : oracle::kF32, n, i % 5 == 0, i % 7 == 0, seed++);
   }
@@ -641,7 +718,7 @@ void randomized() {
     c.nvlsTileElems = 4 * (1 + rnd(32));
     World w(c);
     for (int k = 0; k < 3 && ok; ++k) {
-      const Algo a = (Algo)(1 + rnd(4));
+      const Algo a = (Algo)(1 + rnd(5));
       const uint64_t n = rnd(5) == 0 ? rnd(8) : rnd(20000);
       ok = checkOne(w, a, rnd(2) ? oracle::kBF16 : oracle::kF32, n, rnd(2) == 0, rnd(3) == 0,
                     1000 + (uint64_t)worlds * 3 + (uint64_t)k);
@@ -652,6 +729,30 @@ void randomized() {
   char name[96];
   snprintf(name, sizeof(name), "randomised configurations (%d worlds x 3)", worlds);
   report(name, ok);
+}
+
+// nvlsZcSpan over all (rank, channel) pairs covers [0, nv) exactly once, and
+// nvlsZcChannels stays within 1 .. maxChannels.
+void zeroCopyPartition() {
+  bool ok = true;
+  for (int P = 2; P <= kMaxRanks && ok; ++P)
+    for (uint64_t nv : {0ull, 1ull, 2ull, 7ull, 15ull, 16ull, 17ull, 1000ull, 65537ull, 1ull << 26})
+      for (int maxC : {1, 3, 32, kMaxChannels}) {
+        const int C = nvlsZcChannels(nv, P, maxC, 1024);
+        ok = ok && C >= 1 && C <= maxC;
+        uint64_t next = 0;
+        for (int r = 0; r < P && ok; ++r)
+          for (int c = 0; c < C && ok; ++c) {
+            const Span sp = nvlsZcSpan(nv, P, r, C, c);
+            // Spans are contiguous in (rank, channel) order; empty ones may sit anywhere.
+            if (sp.count == 0) continue;
+            ok = sp.offset == next;
+            next = sp.offset + sp.count;
+          }
+        ok = ok && next == nv;
+        if (!ok) printf("  P=%d nv=%llu maxC=%d C=%d\n", P, (unsigned long long)nv, maxC, C);
+      }
+  report("zero-copy NVLS partition covers every vector once", ok);
 }
 
 void ticketReplay() {
@@ -672,7 +773,7 @@ void ticketReplay() {
 }
 
 void faultInjection() {
-  for (Algo a : {kRing, kOneShot, kTwoShot, kNvls}) {
+  for (Algo a : {kRing, kOneShot, kTwoShot, kNvls, kNvlsZc}) {
     Config c;
     c.P = 4;
     c.timeoutMs = 200;
@@ -702,6 +803,7 @@ int main() {
   baselineConfig1();
   sequenceContinuity();
   randomized();
+  zeroCopyPartition();
   ticketReplay();
   faultInjection();
   printf("rank_model_test: %s\n", gFailed ? "FAIL" : "PASS");

@@ -1,5 +1,7 @@
 """Multi-process tests. GPU ones need 2 GPUs (skipped otherwise); the store
 exchange runs on CPU with gloo ranks."""
+import os
+
 import pytest
 
 from conftest import gpu_count, torchrun
@@ -45,3 +47,17 @@ def test_bounded_wait_timeout_two_ranks(built):
     env = {"TNCCL_TIMEOUT_MS": "1500", "TNCCL_NVLS_ENABLE": "0", "NCCL_NVLS_ENABLE": "0"}
     r = torchrun(2, ["tests/workers/timeout_worker.py"], timeout=300, env=env)
     assert r.returncode == 0 and "PASS" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(gpu_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.skipif(os.environ.get("TNCCL_TEST_NVLS_ZC") != "1",
+                    reason="zero-copy NVLS has not run on a GPU yet: TNCCL_TEST_NVLS_ZC=1")
+def test_nvls_zero_copy_registered_buffers(built):
+    r = torchrun(2, ["tests/workers/nvls_zero_copy_worker.py"], timeout=600,
+                 env={"TNCCL_NVLS_ZERO_COPY": "1", "TNCCL_DEBUG": "TRACE",
+                      "TNCCL_TIMEOUT_MS": "5000"})
+    out = r.stdout + r.stderr
+    assert r.returncode == 0 and ("PASS" in r.stdout or "SKIP" in r.stdout), out[-4000:]
+    if "PASS" in r.stdout:
+        assert "(zero-copy)" in r.stderr, "the zero-copy kernel never ran"

@@ -20,7 +20,8 @@ def test_c_abi_surface(built):
     names = ["tncclGetUniqueId", "tncclCommInitRank", "tncclAllReduceSumF32", "tncclCommDestroy",
              "tncclGetErrorString", "tncclAllReduce", "tncclAllReduceEx", "tncclCommGetInfo",
              "tncclCommGetAsyncError", "tncclCommAbort", "tncclCommSelectAlgo", "tncclGetVersion",
-             "tncclGetLaunchCount", "tncclGetUniqueIdTcp", "tncclCommGetNetStats"]
+             "tncclGetLaunchCount", "tncclGetUniqueIdTcp", "tncclCommGetNetStats",
+             "tncclMemAlloc", "tncclMemFree", "tncclCommRegister", "tncclCommDeregister"]
     for n in names:
         assert hasattr(lib, n), n
     lib.tncclGetErrorString.restype = ctypes.c_char_p
@@ -44,6 +45,21 @@ def test_c_abi_surface(built):
     assert lib.tncclCommDestroy(None) == 1
     assert lib.tncclAllReduceSumF32(None, None, 0, None, None) == 1
     assert lib.tncclGetUniqueId(None) == 1
+    # Registered-buffer entry points: argument checks before any device work.
+    ptr = ctypes.c_void_p()
+    lib.tncclMemAlloc.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_size_t]
+    lib.tncclMemFree.argtypes = [ctypes.c_void_p]
+    lib.tncclCommRegister.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
+                                      ctypes.POINTER(ctypes.c_void_p)]
+    lib.tncclCommDeregister.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+    assert lib.tncclMemAlloc(None, 4096) == 1
+    assert lib.tncclMemAlloc(ctypes.byref(ptr), 0) == 1
+    assert lib.tncclMemFree(None) == 0
+    assert lib.tncclMemFree(ctypes.c_void_p(0x1000)) == 1  # not from tncclMemAlloc
+    assert lib.tncclCommRegister(None, ctypes.c_void_p(0x1000), 4096, ctypes.byref(ptr)) == 1
+    assert lib.tncclCommDeregister(None, None) == 1
+    if __import__("conftest").gpu_count() == 0:
+        assert lib.tncclMemAlloc(ctypes.byref(ptr), 1 << 20) == 2  # no driver
     # TCP rendezvous ids: address and port are validated.
     lib.tncclGetUniqueIdTcp.argtypes = [ctypes.POINTER(Uid), ctypes.c_char_p, ctypes.c_int]
     tcp = Uid()

@@ -1,0 +1,112 @@
+"""2+ ranks: the zero-copy NVLS all-reduce over registered buffers
+(tncclMemAlloc + tncclCommRegister, TNCCL_NVLS_ZERO_COPY=1) gives the exact
+sums of integer-valued inputs (fp32 and bf16, in and out of place, pre-scale
+1/W), over many back-to-back launches interleaved with staged launches on
+unregistered buffers; then deregisters and destroys. Prints the time per
+launch of the zero-copy and the staged NVLS kernel at 256 MiB, and PASS on
+rank 0 (SKIP when the communicator has no NVLS)."""
+import datetime
+import os
+import sys
+
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))))
+
+
+def main():
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    import tiny_nccl_b200 as tn
+    from tiny_nccl_b200.parallel import empty_registrable
+
+    comm = tn.init_from_torch_distributed(device=rank)
+    if not comm.info()["nvls"]:
+        if rank == 0:
+            print("SKIP: no NVLS on this communicator")
+        comm.destroy()
+        dist.destroy_process_group()
+        return
+    ok = True
+    g = torch.Generator(device="cpu")
+    g.manual_seed(1234 + rank)
+    live = []  # (handle, tensor): registrations kept across iterations
+    for dtype in (torch.float32, torch.bfloat16):
+        for n in (1 << 22, 8 * 1000 + 8, 1 << 12):
+            x = empty_registrable(n, dtype, dev)
+            y = empty_registrable(n, dtype, dev)
+            hx, hy = comm.register(x), comm.register(y)
+            plain = torch.empty(n, dtype=dtype, device=dev)  # caching allocator: staged path
+            for it in range(10):
+                src = torch.randint(-8, 9, (n,), generator=g).to(dtype).to(dev)
+                want = src.float()
+                dist.all_reduce(want)
+                avg = it % 3 == 2
+                if avg:
+                    want = want / world
+                want = want.to(dtype)
+                x.copy_(src)
+                if it % 2:
+                    comm.all_reduce(x, None, op="avg" if avg else "sum", algo="nvls")
+                    got = x
+                else:
+                    comm.all_reduce(x, y, op="avg" if avg else "sum", algo="nvls")
+                    got = y
+                plain.copy_(src)
+                comm.all_reduce(plain, algo="nvls")  # staged kernel in between
+                torch.cuda.synchronize()
+                if avg:  # sum * (1/W) against sum / W
+                    tol = 1e-2 if dtype == torch.bfloat16 else 1e-6
+                    good = torch.allclose(got.float(), want.float(), rtol=tol, atol=tol)
+                else:
+                    good = torch.equal(got, want)
+                if not good:
+                    ok = False
+                    diff = (got.float() - want.float()).abs().max().item()
+                    print(f"rank {rank}: {dtype} n={n} it={it} max diff {diff}", flush=True)
+            comm.deregister(hx)
+            live.append((hy, y))
+    for h, _ in live:
+        comm.deregister(h)
+    live.clear()
+    # Time per launch at 256 MiB fp32: zero-copy vs staged NVLS.
+    n = 64 << 20
+    x = empty_registrable(n, torch.float32, dev)
+    h = comm.register(x)
+    x.normal_()
+    plain = torch.randn(n, device=dev)
+    times = {}
+    for name, buf in (("zero-copy", x), ("staged", plain)):
+        for _ in range(3):
+            comm.all_reduce(buf, algo="nvls", op="avg")
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dist.barrier()
+        torch.cuda.synchronize()
+        start.record()
+        for _ in range(10):
+            comm.all_reduce(buf, algo="nvls", op="avg")
+        end.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([start.elapsed_time(end) / 10], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        times[name] = t.item()
+    comm.deregister(h)
+    ok = ok and comm.async_error() == 0
+    flag = torch.tensor([1.0 if ok else 0.0], device=dev)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    if rank == 0:
+        bus = lambda ms: n * 4 / (ms * 1e-3) * 2 * (world - 1) / world / 1e9
+        for name, ms in times.items():
+            print(f"{name}: {ms:.3f} ms per 256 MiB fp32 all-reduce = {bus(ms):.1f} GB/s bus")
+        print("PASS" if flag.item() == 1.0 else "FAIL")
+    torch.cuda.synchronize()
+    comm.destroy()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -59,6 +59,23 @@ def default_bootstrap_addr(env=None) -> str | None:
     return f"{socket.gethostbyname(env['MASTER_ADDR'])}:{port}"
 
 
+def empty_registrable(shape, dtype: torch.dtype, device=None) -> torch.Tensor:
+    """An uninitialised tensor in ``tncclMemAlloc`` memory, which, unlike the
+    caching allocator's ``cudaMalloc`` memory, :meth:`Communicator.register`
+    can bind to an NVSwitch multicast object. The memory is rounded up to the
+    multicast granularity (2 MiB or more) and freed with the tensor, which
+    must be deregistered first (memory still registered is not freed)."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None \
+        else torch.device(device)
+    shape = (shape,) if isinstance(shape, int) else tuple(shape)
+    numel = 1
+    for d in shape:
+        numel *= int(d)
+    es = torch.empty((), dtype=dtype).element_size()
+    raw = load().mem_empty(max(numel * es, es), dev.index)
+    return raw.view(dtype)[:numel].view(shape)
+
+
 class Communicator:
     """One rank's handle on a tnccl communicator.
 
@@ -113,6 +130,18 @@ class Communicator:
         if stream is None:
             stream = torch.cuda.current_stream(self.device).cuda_stream
         self._c.all_reduce_ptr(send, recv, count, code, op, float(scale), algo, stream)
+
+    def register(self, tensor: torch.Tensor) -> int:
+        """Collective: binds ``tensor`` (from :func:`empty_registrable`, the
+        same size on every rank) to an NVSwitch multicast object of its own,
+        so that an NVLS all-reduce on it reads and writes it in place instead
+        of copying it through the communicator's region (used when
+        ``TNCCL_NVLS_ZERO_COPY=1``). Returns a handle for :meth:`deregister`."""
+        return self._c.register(tensor)
+
+    def deregister(self, handle: int) -> None:
+        """Collective: waits for the bound stream and unbinds on every rank."""
+        self._c.deregister(int(handle))
 
     def validate(self) -> int:
         """Waits for the bound stream and returns how many of this rank's
