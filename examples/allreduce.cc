@@ -12,6 +12,12 @@
 //       rank - first); every host is given the same id. Ring edges between
 //       hosts use the socket data plane (TNCCL_NET=auto).
 //
+// TNCCL_EXAMPLE_REGISTERED=1 allocates the buffers with tncclMemAlloc and
+// registers them with the communicator (tncclCommRegister), so that with
+// TNCCL_NVLS_ZERO_COPY=1 an NVLS all-reduce of 1 MiB or more runs the
+// zero-copy kernel on them; without NVLS the registration is refused and the
+// buffers are used unregistered.
+//
 // Same contract as tiny-nccl's examples/allreduce.cc:22-127: rank r
 // contributes r + 1 everywhere, and every element must equal n(n+1)/2; the
 // parent waits for every child and exits 0 only if all passed.
@@ -48,15 +54,35 @@ int runRank(int rank, int device, int nranks, size_t count, tncclUniqueId id) {
   float* buf = nullptr;
   float* out = nullptr;
   std::vector<float> host(count, (float)(rank + 1));
+  const char* regEnv = getenv("TNCCL_EXAMPLE_REGISTERED");
+  const bool registered = regEnv != nullptr && atoi(regEnv) != 0 && count != 0;
+  void* handles[2] = {nullptr, nullptr};
   bool ok = check(cudaStreamCreate(&stream), "cudaStreamCreate", rank);
-  if (ok && count) {
-    ok = check(cudaMalloc(reinterpret_cast<void**>(&buf), count * sizeof(float)), "cudaMalloc", rank) &&
-         check(cudaMalloc(reinterpret_cast<void**>(&out), count * sizeof(float)), "cudaMalloc",
+  if (ok && registered) {
+    // Registration is collective: every rank makes both calls, in this order.
+    ok = tncclMemAlloc(reinterpret_cast<void**>(&buf), count * sizeof(float)) == TNCCL_SUCCESS &&
+         tncclMemAlloc(reinterpret_cast<void**>(&out), count * sizeof(float)) == TNCCL_SUCCESS;
+    if (!ok) fprintf(stderr, "rank %d: tncclMemAlloc failed\n", rank);
+    for (int k = 0; ok && k < 2; ++k) {
+      r = tncclCommRegister(comm, k == 0 ? (void*)buf : (void*)out, count * sizeof(float),
+                            &handles[k]);
+      if (r == TNCCL_UNSUPPORTED) {
+        if (rank == 0 && k == 0) printf("no NVLS: buffers stay unregistered\n");
+      } else if (r != TNCCL_SUCCESS) {
+        fprintf(stderr, "rank %d: register: %s\n", rank, tncclGetErrorString(r));
+        ok = false;
+      }
+    }
+  } else if (ok && count) {
+    ok = check(cudaMalloc(reinterpret_cast<void**>(&buf), count * sizeof(float)), "cudaMalloc",
                rank) &&
-         check(cudaMemcpyAsync(buf, host.data(), count * sizeof(float), cudaMemcpyHostToDevice,
+         check(cudaMalloc(reinterpret_cast<void**>(&out), count * sizeof(float)), "cudaMalloc",
+               rank);
+  }
+  if (ok && count)
+    ok = check(cudaMemcpyAsync(buf, host.data(), count * sizeof(float), cudaMemcpyHostToDevice,
                                stream),
                "copy in", rank);
-  }
   if (ok) {
     r = tncclAllReduceSumF32(buf, out, count, comm, stream);
     if (r != TNCCL_SUCCESS) {
@@ -76,9 +102,16 @@ int runRank(int rank, int device, int nranks, size_t count, tncclUniqueId id) {
       ok = false;
     }
   }
+  for (void* h : handles)
+    if (h != nullptr && tncclCommDeregister(comm, h) != TNCCL_SUCCESS) ok = false;
   if (tncclCommDestroy(comm) != TNCCL_SUCCESS) ok = false;
-  if (buf) cudaFree(buf);
-  if (out) cudaFree(out);
+  if (registered) {
+    tncclMemFree(buf);
+    tncclMemFree(out);
+  } else {
+    if (buf) cudaFree(buf);
+    if (out) cudaFree(out);
+  }
   if (stream) cudaStreamDestroy(stream);
   return ok ? 0 : 1;
 }

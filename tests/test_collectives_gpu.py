@@ -33,6 +33,18 @@ def test_example_single_gpu(built):
     assert r.returncode == 0 and "all ranks: ok" in r.stdout, r.stdout + r.stderr
 
 
+@pytest.mark.skipif(os.environ.get("TNCCL_TEST_NVLS_ZC") != "1",
+                    reason="registered buffers have not run on a GPU yet: TNCCL_TEST_NVLS_ZC=1")
+def test_example_registered_buffers(built):
+    # One rank: tncclMemAlloc / tncclMemFree and a refused registration (no
+    # NVLS); two or more: registered buffers on the zero-copy NVLS kernel.
+    n = min(gpu_count(), 8)
+    r = run([os.path.join(ROOT, "build", "bin", "tnccl_allreduce"), str(n), str(1 << 22)],
+            timeout=300, env={"TNCCL_EXAMPLE_REGISTERED": "1", "TNCCL_NVLS_ZERO_COPY": "1",
+                              "TNCCL_TIMEOUT_MS": "10000", "TNCCL_DEBUG": "TRACE"})
+    assert r.returncode == 0 and "all ranks: ok" in r.stdout, r.stdout + r.stderr[-4000:]
+
+
 @pytest.mark.skipif(gpu_count() < 2, reason="needs 2 GPUs")
 def test_two_rank_bit_exact(built):
     r = run([os.path.join(ROOT, "build", "bin", "allreduce_gpu_test"), "2", "quick"], timeout=600,
