@@ -207,6 +207,7 @@ def build_tnccl_trainer(args, rank, world, dev):
 
     def close():
         torch.cuda.synchronize()
+        trainer.close()
         comm.destroy()
 
     return trainer.step, launches, close
@@ -228,6 +229,8 @@ def make_record(impl, world, B, T, steps, warmup, ms_max, clocks, launches, e2e,
             "config": {"model": "GPT-2 small (124M): 12 layers, d_model 768, 12 heads, vocab 50257",
                        "global_batch": B * world, "micro_batch_per_gpu": B, "seq_len": T,
                        "parallelism": f"dp{world}", "optimizer": "AdamW", "amp": "bf16 autocast",
+                       "grad_reducer": (os.environ.get("TNCCL_DP_REDUCER", "ddp")
+                                        if impl == "tnccl" else "ddp"),
                        "l2": "no flush: one step touches several GB (activations, 124M-param "
                              "weights/grads/optimizer state), far above the 126 MB L2"},
             "clocks": clocks, "gpu_launches": launches, "e2e": e2e,

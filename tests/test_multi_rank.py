@@ -8,6 +8,12 @@ from conftest import gpu_count, torchrun
 
 
 @pytest.mark.skipif(gpu_count() > 0, reason="CPU-only behaviour")
+def test_flat_reducer_matches_ddp_cpu_ranks():
+    r = torchrun(2, ["tests/workers/flat_reducer_worker.py"], timeout=180)
+    assert r.returncode == 0 and "PASS" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
+
+
+@pytest.mark.skipif(gpu_count() > 0, reason="CPU-only behaviour")
 def test_store_exchange_cpu_ranks(built):
     r = torchrun(2, ["tests/workers/store_exchange_worker.py"], timeout=180)
     assert r.returncode == 0 and "PASS" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
@@ -61,3 +67,13 @@ def test_nvls_zero_copy_registered_buffers(built):
     assert r.returncode == 0 and ("PASS" in r.stdout or "SKIP" in r.stdout), out[-4000:]
     if "PASS" in r.stdout:
         assert "(zero-copy)" in r.stderr, "the zero-copy kernel never ran"
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(gpu_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.skipif(os.environ.get("TNCCL_TEST_NVLS_ZC") != "1",
+                    reason="the flat reducer has not run on a GPU yet: TNCCL_TEST_NVLS_ZC=1")
+def test_flat_reducer_registered_buffer(built):
+    r = torchrun(2, ["tests/workers/flat_trainer_worker.py"], timeout=600,
+                 env={"TNCCL_NVLS_ZERO_COPY": "1", "TNCCL_TIMEOUT_MS": "10000"})
+    assert r.returncode == 0 and "PASS" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]

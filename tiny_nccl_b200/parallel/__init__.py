@@ -8,6 +8,7 @@ __all__ = [
     "init_from_store",
     "init_from_torch_distributed", "TncclHookState", "register_tnccl_hook", "tnccl_allreduce_hook",
 ]
+from .reducer import FlatGradReducer  # noqa: E402
 from .trainer import DataParallelTrainer  # noqa: E402
 
-__all__.append("DataParallelTrainer")
+__all__ += ["FlatGradReducer", "DataParallelTrainer"]

@@ -1,0 +1,124 @@
+"""Data-parallel gradient reduction over one flat gradient buffer.
+
+An alternative to ``DistributedDataParallel`` + the tnccl comm hook
+(:mod:`.ddp`). Every parameter's ``.grad`` is a view into one flat buffer,
+cut into buckets of about ``bucket_bytes``; a post-accumulate-grad hook per
+parameter counts the bucket's gradients as backward produces them, and a
+bucket is all-reduced (on a side stream, averaged over ranks) as soon as it is
+complete. Buckets are launched strictly in index order, so every rank issues
+the same collectives in the same order whatever order its hooks fire in
+(collectives of one communicator must match across ranks).
+
+What the flat buffer adds over DDP's own buckets is where it lives: with
+``alloc=empty_registrable`` it is tncclMemAlloc memory that the communicator
+can register, so with ``TNCCL_NVLS_ZERO_COPY=1`` every bucket all-reduce is
+the zero-copy NVLS kernel (the NVSwitch reduces; the kernel only issues
+multimem loads and stores, so it needs few SMs while backward runs). Bucket
+boundaries and parameter offsets are multiples of 16 bytes, as that kernel
+requires, and they are the same on every rank because every rank builds the
+layout from the same parameter list.
+
+tiny-nccl has no trainer; the bucketing follows DDP's (reverse registration
+order, ~25 MB buckets, launch in bucket order).
+"""
+from __future__ import annotations
+
+from typing import Callable, Iterable
+
+import torch
+
+
+class FlatGradReducer:
+    """Owns the gradients of ``params``.
+
+    ``all_reduce(t)`` must average ``t`` in place over the ranks (it is called
+    on ``stream`` when one is given). Call :meth:`finish` after every
+    backward and before the optimizer step, and :meth:`zero_grad` instead of
+    the optimizer's ``zero_grad`` (the ``.grad`` views must stay in place).
+    """
+
+    def __init__(self, params: Iterable[torch.nn.Parameter],
+                 all_reduce: Callable[[torch.Tensor], None], *,
+                 bucket_bytes: int = 25 << 20,
+                 alloc: Callable[..., torch.Tensor] | None = None,
+                 stream: torch.cuda.Stream | None = None):
+        params = [p for p in params if p.requires_grad]
+        if not params:
+            raise ValueError("FlatGradReducer: no parameter requires a gradient")
+        dtype, device = params[0].dtype, params[0].device
+        if any(p.dtype != dtype or p.device != device for p in params):
+            raise ValueError("FlatGradReducer: parameters must share one dtype and device")
+        es = torch.empty((), dtype=dtype).element_size()
+        align = max(1, 16 // es)  # 16-byte offsets and bucket ends
+        cap = max(align, bucket_bytes // es)
+        # Backward produces gradients roughly in reverse registration order.
+        order = list(reversed(params))
+        offsets, buckets, bucket_of = [], [], []
+        off = start = 0
+        for p in order:
+            n = p.numel()
+            if off > start and off + n - start > cap:
+                buckets.append((start, off))
+                start = off
+            offsets.append(off)
+            bucket_of.append(len(buckets))
+            off += -(-n // align) * align
+        buckets.append((start, off))
+        self.total = off
+        self.flat = (alloc(off, dtype, device) if alloc is not None
+                     else torch.empty(off, dtype=dtype, device=device))
+        self.flat.zero_()
+        self.buckets = buckets
+        self.params = order
+        self._bucket_of = {}
+        self._need = [0] * len(buckets)
+        for p, o, b in zip(order, offsets, bucket_of):
+            p.grad = self.flat[o:o + p.numel()].view_as(p)
+            self._bucket_of[id(p)] = b
+            self._need[b] += 1
+        self._all_reduce = all_reduce
+        self._stream = stream
+        self._pending = list(self._need)
+        self._next = 0  # first bucket not launched yet
+        self.launched = 0
+        self._hooks = [p.register_post_accumulate_grad_hook(self._ready) for p in order]
+
+    # -- hooks ----------------------------------------------------------------
+    def _ready(self, p: torch.Tensor) -> None:
+        b = self._bucket_of[id(p)]
+        self._pending[b] -= 1
+        while self._next < len(self.buckets) and self._pending[self._next] == 0:
+            self._launch(self._next)
+            self._next += 1
+
+    def _launch(self, b: int) -> None:
+        s, e = self.buckets[b]
+        chunk = self.flat[s:e]
+        if self._stream is None:
+            self._all_reduce(chunk)
+        else:
+            self._stream.wait_stream(torch.cuda.current_stream(self.flat.device))
+            with torch.cuda.stream(self._stream):
+                self._all_reduce(chunk)
+        self.launched += 1
+
+    # -- per step ---------------------------------------------------------------
+    def finish(self) -> None:
+        """Launches the buckets still waiting (parameters that got no gradient
+        this step), makes the current stream wait for every all-reduce and
+        re-arms the counters for the next backward."""
+        while self._next < len(self.buckets):
+            self._launch(self._next)
+            self._next += 1
+        if self._stream is not None:
+            torch.cuda.current_stream(self.flat.device).wait_stream(self._stream)
+        self._pending = list(self._need)
+        self._next = 0
+
+    def zero_grad(self) -> None:
+        self.flat.zero_()
+
+    def remove(self) -> None:
+        for h in self._hooks:
+            h.remove()
+        self._hooks = []

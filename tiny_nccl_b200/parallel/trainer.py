@@ -1,6 +1,12 @@
 """Data-parallel training step: DistributedDataParallel with the tnccl comm
 hook (gradient buckets all-reduced on a side stream, 1/world fused into the
 kernel, overlapped with backward) and the fused AdamW kernel.
+
+``reducer="flat"`` (or ``TNCCL_DP_REDUCER=flat``) replaces DDP with
+:class:`FlatGradReducer`: the gradients live in one flat buffer, which with
+``registered=True`` (``TNCCL_DP_REGISTERED=1``) is tncclMemAlloc memory
+registered with the communicator, for the zero-copy NVLS all-reduce
+(``TNCCL_NVLS_ZERO_COPY=1``). Opt-in: not yet run on a GPU.
 """
 from __future__ import annotations
 
@@ -11,15 +17,17 @@ import torch.distributed as dist
 from torch.nn.parallel import DistributedDataParallel as DDP
 
 from ..ops.optim import AdamW, gpt2_param_groups
-from .comm import Communicator
+from .comm import Communicator, empty_registrable
 from .ddp import register_tnccl_hook
+from .reducer import FlatGradReducer
 
 
 class DataParallelTrainer:
     def __init__(self, model: torch.nn.Module, comm: Communicator, lr: float = 6e-4,
                  weight_decay: float = 0.1, betas=(0.9, 0.95), bucket_cap_mb: int = 25,
                  algo: str = "auto", wire_dtype: torch.dtype | None = None,
-                 amp_dtype: torch.dtype = torch.bfloat16, max_channels: int | None = None):
+                 amp_dtype: torch.dtype = torch.bfloat16, max_channels: int | None = None,
+                 reducer: str | None = None, registered: bool | None = None):
         if not dist.is_initialized():
             raise RuntimeError("DataParallelTrainer needs torch.distributed initialised")
         self.comm = comm
@@ -31,10 +39,36 @@ class DataParallelTrainer:
         self.model = model
         self.amp_dtype = amp_dtype
         dev = comm.device
-        self.ddp = DDP(model, device_ids=[dev.index], output_device=dev.index,
-                       bucket_cap_mb=bucket_cap_mb, gradient_as_bucket_view=True,
-                       static_graph=True, broadcast_buffers=False)
-        self.hook_state = register_tnccl_hook(self.ddp, comm, algo=algo, wire_dtype=wire_dtype)
+        if reducer is None:
+            reducer = os.environ.get("TNCCL_DP_REDUCER", "ddp")
+        if registered is None:
+            registered = os.environ.get("TNCCL_DP_REGISTERED", "0") == "1"
+        self.reducer = None
+        self.registration = None
+        if reducer == "flat":
+            # DDP would broadcast rank 0's parameters; do the same once.
+            with torch.no_grad():
+                for t in list(model.parameters()) + list(model.buffers()):
+                    dist.broadcast(t, 0)
+            # Registration is collective and refused on every rank alike when
+            # the communicator has no NVLS; the buffer then stays unregistered.
+            alloc = ((lambda n, dt, d: empty_registrable(n, dt, d)) if registered
+                     and comm.size > 1 and comm.info()["nvls"] else None)
+            self.reducer = FlatGradReducer(
+                model.parameters(), lambda t: comm.all_reduce(t, op="avg", algo=algo),
+                bucket_bytes=bucket_cap_mb << 20, alloc=alloc, stream=comm.side_stream())
+            if alloc is not None:
+                self.registration = comm.register(self.reducer.flat)
+            self.ddp = model
+            self.hook_state = None
+        elif reducer == "ddp":
+            self.ddp = DDP(model, device_ids=[dev.index], output_device=dev.index,
+                           bucket_cap_mb=bucket_cap_mb, gradient_as_bucket_view=True,
+                           static_graph=True, broadcast_buffers=False)
+            self.hook_state = register_tnccl_hook(self.ddp, comm, algo=algo,
+                                                  wire_dtype=wire_dtype)
+        else:
+            raise ValueError(f"reducer must be 'ddp' or 'flat', not {reducer!r}")
         self.opt = AdamW(gpt2_param_groups(model, weight_decay), lr=lr, betas=betas)
 
     def step(self, idx: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
@@ -42,9 +76,21 @@ class DataParallelTrainer:
         with torch.autocast("cuda", dtype=self.amp_dtype):
             loss = self.ddp(idx, targets)
         loss.backward()
-        self.opt.step()
-        self.opt.zero_grad(set_to_none=True)
+        if self.reducer is not None:
+            self.reducer.finish()
+            self.opt.step()
+            self.reducer.zero_grad()
+        else:
+            self.opt.step()
+            self.opt.zero_grad(set_to_none=True)
         return loss.detach()
+
+    def close(self) -> None:
+        """Deregisters the flat gradient buffer (collective); call before the
+        communicator is destroyed."""
+        if self.registration is not None:
+            self.comm.deregister(self.registration)
+            self.registration = None
 
     def state_dict(self) -> dict:
         return {"model": self.model.state_dict(), "opt": self.opt.state_dict(),
