@@ -15,6 +15,10 @@ events on each stream, max over ranks.
 
     python -m torch.distributed.run --nproc-per-node 8 --master-addr 127.0.0.1 \\
         benchmarks/bucket_overlap.py --out bucket.jsonl
+
+``--registered`` puts the buckets (and their outputs) in two tncclMemAlloc
+regions registered with the communicator; with TNCCL_NVLS_ZERO_COPY=1 every
+tnccl bucket all-reduce is then the zero-copy NVLS kernel.
 """
 from __future__ import annotations
 
@@ -45,6 +49,8 @@ def main():
     ap.add_argument("--gemm-iters", type=int, default=40)
     ap.add_argument("--channels", type=int, default=32, help="tnccl CTA cap while overlapping")
     ap.add_argument("--out", default="")
+    ap.add_argument("--registered", action="store_true",
+                    help="buckets in tncclMemAlloc memory registered with the communicator")
     args = ap.parse_args()
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -60,6 +66,16 @@ def main():
     buckets = [(torch.randn(n, device=dev, generator=g) * 1e-3).to(torch.bfloat16)
                for _ in range(args.buckets)]
     outs = [torch.empty_like(b) for b in buckets]
+    handles = []
+    if args.registered and comm.info()["nvls"]:
+        from tiny_nccl_b200.parallel import empty_registrable
+        src = empty_registrable(n * args.buckets, torch.bfloat16, dev)
+        dst = empty_registrable(n * args.buckets, torch.bfloat16, dev)
+        for k, b in enumerate(buckets):
+            src[k * n:(k + 1) * n].copy_(b)
+        buckets = [src[k * n:(k + 1) * n] for k in range(args.buckets)]
+        outs = [dst[k * n:(k + 1) * n] for k in range(args.buckets)]
+        handles = [comm.register(src), comm.register(dst)]
     a = torch.randn(args.gemm, args.gemm, device=dev, dtype=torch.bfloat16)
     bm = torch.randn(args.gemm, args.gemm, device=dev, dtype=torch.bfloat16)
     cm = torch.empty_like(a)
@@ -126,7 +142,10 @@ def main():
             rec = {"impl": impl, "overlap": overlap, "n_gpus": world, "buckets": args.buckets,
                    "bucket_mb": args.bucket_mb, "dtype": "bf16", "op": "avg (pre-scale fused)",
                    "comm_ms": tc, "per_bucket_us": per_bucket * 1e3, "busbw_gbs": bus,
-                   "total_bytes": total_bytes}
+                   "total_bytes": total_bytes,
+                   "registered": bool(handles) and impl == "tnccl",
+                   "zero_copy": bool(handles) and impl == "tnccl"
+                   and os.environ.get("TNCCL_NVLS_ZERO_COPY") == "1"}
             if overlap:
                 rec.update({"compute_ms": tg, "compute_alone_ms": comp_alone,
                             "compute_slowdown": tg / comp_alone,
@@ -150,6 +169,8 @@ def main():
                 for r in results:
                     f.write(json.dumps(r) + "\n")
     torch.cuda.synchronize()
+    for h in handles:
+        comm.deregister(h)
     comm.destroy()
     dist.barrier()
     dist.destroy_process_group()
