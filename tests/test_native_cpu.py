@@ -69,6 +69,14 @@ def test_c_abi_surface(built):
     assert lib.tncclGetUniqueIdTcp(ctypes.byref(tcp), b"127.0.0.1", 0) == 1
 
 
+def test_registration_control_plane(built):
+    # tncclMemAlloc / tncclCommRegister / tncclCommDeregister over forked
+    # ranks, a real bootstrap and a fake driver with failures injected.
+    r = run([os.path.join(ROOT, "build", "bin", "register_test")], timeout=120)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "register_test: PASS" in r.stdout
+
+
 def test_bootstrap_forked_ranks(built):
     r = run([os.path.join(ROOT, "build", "bin", "bootstrap_test")], timeout=120)
     assert r.returncode == 0, r.stdout + r.stderr

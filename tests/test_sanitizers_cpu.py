@@ -1,7 +1,9 @@
 """Host sanitizer runs (compute-sanitizer is closed on the GPU pool): the
 threaded CPU rank model under ThreadSanitizer (data races in the flag
 protocol model) and the bootstrap tests under AddressSanitizer +
-UndefinedBehaviorSanitizer (memory errors in the socket control plane)."""
+UndefinedBehaviorSanitizer (memory errors in the socket control plane), the
+socket proxy under both, and the registered-buffer control plane under
+AddressSanitizer + UndefinedBehaviorSanitizer."""
 import os
 import shutil
 import subprocess
@@ -75,3 +77,15 @@ def test_gemm_pipeline_model_under_tsan():
     assert r.returncode == 0 and "gemm_pipeline_model_test: PASS" in r.stdout, \
         r.stdout[-2000:] + r.stderr[-4000:]
     assert "WARNING: ThreadSanitizer" not in r.stderr, r.stderr[-4000:]
+
+
+@pytest.mark.skipif(shutil.which("g++") is None, reason="needs g++")
+def test_registration_under_asan_ubsan():
+    exe = _build("register_asan", ["tests/cpp/register_test.cc", "csrc/tnccl/register.cc",
+                                   "csrc/tnccl/bootstrap.cc", "csrc/tnccl/common.cc",
+                                   "csrc/tnccl/sockio.cc"],
+                 ["-fsanitize=address,undefined", "-fno-omit-frame-pointer",
+                  "-fno-sanitize-recover=undefined"])
+    env = dict(os.environ, ASAN_OPTIONS="detect_leaks=1:abort_on_error=1")
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=300, env=env)
+    assert r.returncode == 0 and "register_test: PASS" in r.stdout, r.stdout[-2000:] + r.stderr[-4000:]

@@ -172,6 +172,33 @@ PROGRAMS = {
 }
 
 
+# C++ tests built from sources with g++ alone (no libtnccl, no CUDA runtime:
+# they bring their own fakes of the CUDA calls the sources make).
+STANDALONE = {
+    # registered buffers: forked ranks, real bootstrap, fake driver
+    "register_test": [ROOT / "tests" / "cpp" / "register_test.cc", TNCCL_SRC / "register.cc",
+                      TNCCL_SRC / "bootstrap.cc", TNCCL_SRC / "sockio.cc",
+                      TNCCL_SRC / "common.cc"],
+}
+
+
+def build_standalone() -> list[Path]:
+    BIN.mkdir(parents=True, exist_ok=True)
+    outs = []
+    for name, srcs in STANDALONE.items():
+        out = BIN / name
+        stamp = BIN / (name + ".stamp")
+        deps = srcs + _headers(ROOT / "tests" / "cpp") + _headers(TNCCL_SRC) + \
+            [ROOT / "include" / "tnccl.h"]
+        key = _hash(deps, "standalone " + " ".join(CXXFLAGS))
+        if not (out.exists() and stamp.exists() and stamp.read_text() == key):
+            _run(["g++", *CXXFLAGS, "-O1", *INCLUDES, f"-I{ROOT / 'tests' / 'cpp'}",
+                  *[str(s) for s in srcs], "-o", str(out), "-lpthread"])
+            stamp.write_text(key)
+        outs.append(out)
+    return outs
+
+
 def build_programs() -> list[Path]:
     """Builds the example and the C++ test programs into build/bin."""
     lib = build_tnccl()
@@ -203,7 +230,8 @@ def build_programs() -> list[Path]:
 
 
 def build_all(verbose: bool = False) -> None:
-    paths = [build_tnccl(), build_ops(), build_torch_ext(), *build_programs()]
+    paths = [build_tnccl(), build_ops(), build_torch_ext(), *build_programs(),
+             *build_standalone()]
     if verbose:
         for p in paths:
             if p is not None:
