@@ -2,8 +2,9 @@
 all-reduced in order from post-accumulate-grad hooks) gives the same
 gradients and parameters as DistributedDataParallel over three SGD steps,
 with tiny buckets (many of them), odd parameter sizes (16-byte padding) and a
-parameter that gets no gradient (its bucket is launched by finish()).
-Prints PASS on rank 0."""
+parameter that gets no gradient (its bucket is launched by finish()); and
+SGD applied per bucket from the on_reduced callback during backward gives
+bit-identical parameters to SGD after backward. Prints PASS on rank 0."""
 import copy
 import datetime
 import os
@@ -35,6 +36,7 @@ def main():
     torch.manual_seed(0)
     net_a = Net()
     net_b = copy.deepcopy(net_a)
+    net_c = copy.deepcopy(net_a)
     ddp = DDP(net_b, find_unused_parameters=True)
 
     def avg(t):
@@ -42,6 +44,13 @@ def main():
         t.div_(world)
 
     red = FlatGradReducer(net_a.parameters(), avg, bucket_bytes=256)
+
+    def sgd(params):
+        with torch.no_grad():
+            for p in params:
+                p -= 0.1 * p.grad
+
+    red_c = FlatGradReducer(net_c.parameters(), avg, bucket_bytes=256, on_reduced=sgd)
     ok = len(red.buckets) >= 3
     ok = ok and all((s * 4) % 16 == 0 and (e * 4) % 16 == 0 for s, e in red.buckets)
     g = torch.Generator()
@@ -51,6 +60,9 @@ def main():
         net_a(x).pow(2).mean().backward()
         red.finish()
         ddp(x).pow(2).mean().backward()
+        net_c(x).pow(2).mean().backward()  # updated bucket by bucket inside backward
+        red_c.finish()
+        red_c.zero_grad()
         for (n, pa), (_, pb) in zip(net_a.named_parameters(), net_b.named_parameters()):
             gb = pb.grad if pb.grad is not None else torch.zeros_like(pb)
             if not torch.allclose(pa.grad, gb, rtol=1e-6, atol=1e-7):
@@ -70,6 +82,10 @@ def main():
                     for p in net_a.parameters())
     for pa, pb in zip(net_a.parameters(), net_b.parameters()):
         ok = ok and torch.allclose(pa, pb, rtol=1e-6, atol=1e-7)
+    for pa, pc in zip(net_a.parameters(), net_c.parameters()):
+        if not torch.equal(pa, pc):
+            ok = False
+            print(f"rank {rank}: per-bucket update differs", flush=True)
     flag = torch.tensor([1.0 if ok else 0.0])
     dist.all_reduce(flag, op=dist.ReduceOp.MIN)
     if rank == 0:

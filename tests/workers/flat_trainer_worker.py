@@ -1,8 +1,8 @@
 """2+ ranks: gradients through FlatGradReducer on a flat buffer registered
 with the communicator (zero-copy NVLS when TNCCL_NVLS_ZERO_COPY=1) match DDP
 with the tnccl hook, and DataParallelTrainer(reducer="flat", registered=True)
-trains GPT-2 (small config) in step with reducer="ddp". Prints PASS on
-rank 0."""
+trains GPT-2 (small config) in step with reducer="ddp", also with AdamW
+overlapped with backward (overlap_optimizer=True). Prints PASS on rank 0."""
 import datetime
 import math
 import os
@@ -66,22 +66,29 @@ def main():
     a = GPT2(cfg, impl="fused").to(dev)
     b = GPT2(cfg, impl="fused").to(dev)
     b.load_state_dict(a.state_dict())
+    c = GPT2(cfg, impl="fused").to(dev)
+    c.load_state_dict(a.state_dict())
     ta = DataParallelTrainer(a, comm, reducer="flat", registered=True)
     tb = DataParallelTrainer(b, comm, reducer="ddp")
+    # AdamW applied bucket by bucket on the comm stream during backward.
+    tc = DataParallelTrainer(c, comm, reducer="flat", registered=True, overlap_optimizer=True)
     for step in range(3):
         g.manual_seed(1000 * step + rank)
         idx = torch.randint(0, 2048, (2, 129), generator=g).to(dev)
         la = ta.step(idx[:, :-1], idx[:, 1:]).item()
         lb = tb.step(idx[:, :-1], idx[:, 1:]).item()
-        ok = ok and math.isfinite(la) and abs(la - lb) < 1e-2
+        lc = tc.step(idx[:, :-1], idx[:, 1:]).item()
+        ok = ok and math.isfinite(la) and abs(la - lb) < 1e-2 and abs(la - lc) < 1e-4
     pd = max((x - y).abs().max().item() for x, y in zip(a.parameters(), b.parameters()))
-    ok = ok and pd < 5e-3 and comm.async_error() == 0
+    pc = max((x - y).abs().max().item() for x, y in zip(a.parameters(), c.parameters()))
+    ok = ok and pd < 5e-3 and pc < 1e-5 and comm.async_error() == 0
     ta.close()
+    tc.close()
     flag = torch.tensor([1.0 if ok else 0.0], device=dev)
     dist.all_reduce(flag, op=dist.ReduceOp.MIN)
     if rank == 0:
         print(f"nvls={nvls} buckets={len(red.buckets)} worst_rel_grad_diff={worst:.3e} "
-              f"param_diff_after_3_steps={pd:.3e}")
+              f"param_diff_after_3_steps={pd:.3e} overlapped_optimizer_diff={pc:.3e}")
         print("PASS" if flag.item() == 1.0 else "FAIL")
     torch.cuda.synchronize()
     comm.destroy()

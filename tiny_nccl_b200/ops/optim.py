@@ -21,12 +21,27 @@ class AdamW(torch.optim.Optimizer):
     @torch.no_grad()
     def step(self, closure=None):
         loss = closure() if closure is not None else None
+        self.begin_step()
+        self.step_params()
+        return loss
+
+    def begin_step(self) -> None:
+        """Advances the step count (bias correction) of a step whose update is
+        applied in parts with :meth:`step_params`."""
         self._step += 1
+
+    @torch.no_grad()
+    def step_params(self, only=None) -> None:
+        """Applies the current step to the parameters in ``only`` (all when
+        None) that have a gradient. The update is elementwise, so a step split
+        into parts (one per gradient bucket, as its all-reduce completes)
+        gives the same result as one call."""
         ops = load().ops
+        sel = None if only is None else {id(p) for p in only}
         for group in self.param_groups:
             ps, gs, ms, vs, wds = [], [], [], [], []
             for p in group["params"]:
-                if p.grad is None:
+                if p.grad is None or (sel is not None and id(p) not in sel):
                     continue
                 st = self.state[p]
                 if not st:
@@ -41,7 +56,6 @@ class AdamW(torch.optim.Optimizer):
                 b1, b2 = group["betas"]
                 ops.adamw(ps, gs, ms, vs, wds, float(group["lr"]), float(b1), float(b2),
                           float(group["eps"]), self._step, 1.0)
-        return loss
 
 
 def gpt2_param_groups(model: torch.nn.Module, weight_decay: float = 0.1):

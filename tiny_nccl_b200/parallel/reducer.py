@@ -18,6 +18,14 @@ boundaries and parameter offsets are multiples of 16 bytes, as that kernel
 requires, and they are the same on every rank because every rank builds the
 layout from the same parameter list.
 
+``on_reduced(params)``, when given, is called right after a bucket's
+all-reduce is enqueued, on the same stream, with the bucket's parameters: an
+optimizer can update them there (``AdamW.step_params``) while backward
+still runs for the layers below, instead of after the whole backward. That
+is safe because a parameter's gradient hook fires only after the backward
+node that read the parameter has been enqueued, and the side stream waits
+for everything enqueued before the hook.
+
 tiny-nccl has no trainer; the bucketing follows DDP's (reverse registration
 order, ~25 MB buckets, launch in bucket order).
 """
@@ -41,7 +49,8 @@ class FlatGradReducer:
                  all_reduce: Callable[[torch.Tensor], None], *,
                  bucket_bytes: int = 25 << 20,
                  alloc: Callable[..., torch.Tensor] | None = None,
-                 stream: torch.cuda.Stream | None = None):
+                 stream: torch.cuda.Stream | None = None,
+                 on_reduced: Callable[[list], None] | None = None):
         params = [p for p in params if p.requires_grad]
         if not params:
             raise ValueError("FlatGradReducer: no parameter requires a gradient")
@@ -76,7 +85,11 @@ class FlatGradReducer:
             p.grad = self.flat[o:o + p.numel()].view_as(p)
             self._bucket_of[id(p)] = b
             self._need[b] += 1
+        self.bucket_params = [[] for _ in buckets]
+        for p, b in zip(order, bucket_of):
+            self.bucket_params[b].append(p)
         self._all_reduce = all_reduce
+        self._on_reduced = on_reduced
         self._stream = stream
         self._pending = list(self._need)
         self._next = 0  # first bucket not launched yet
@@ -96,10 +109,14 @@ class FlatGradReducer:
         chunk = self.flat[s:e]
         if self._stream is None:
             self._all_reduce(chunk)
+            if self._on_reduced is not None:
+                self._on_reduced(self.bucket_params[b])
         else:
             self._stream.wait_stream(torch.cuda.current_stream(self.flat.device))
             with torch.cuda.stream(self._stream):
                 self._all_reduce(chunk)
+                if self._on_reduced is not None:
+                    self._on_reduced(self.bucket_params[b])
         self.launched += 1
 
     # -- per step ---------------------------------------------------------------

@@ -6,7 +6,10 @@ kernel, overlapped with backward) and the fused AdamW kernel.
 :class:`FlatGradReducer`: the gradients live in one flat buffer, which with
 ``registered=True`` (``TNCCL_DP_REGISTERED=1``) is tncclMemAlloc memory
 registered with the communicator, for the zero-copy NVLS all-reduce
-(``TNCCL_NVLS_ZERO_COPY=1``). Opt-in: not yet run on a GPU.
+(``TNCCL_NVLS_ZERO_COPY=1``), and with ``overlap_optimizer=True``
+(``TNCCL_DP_OVERLAP_OPT=1``) AdamW updates each bucket's parameters on the
+communication stream as soon as its all-reduce is enqueued, overlapping the
+optimizer with the rest of backward. Opt-in: not yet run on a GPU.
 """
 from __future__ import annotations
 
@@ -27,7 +30,8 @@ class DataParallelTrainer:
                  weight_decay: float = 0.1, betas=(0.9, 0.95), bucket_cap_mb: int = 25,
                  algo: str = "auto", wire_dtype: torch.dtype | None = None,
                  amp_dtype: torch.dtype = torch.bfloat16, max_channels: int | None = None,
-                 reducer: str | None = None, registered: bool | None = None):
+                 reducer: str | None = None, registered: bool | None = None,
+                 overlap_optimizer: bool | None = None):
         if not dist.is_initialized():
             raise RuntimeError("DataParallelTrainer needs torch.distributed initialised")
         self.comm = comm
@@ -43,6 +47,10 @@ class DataParallelTrainer:
             reducer = os.environ.get("TNCCL_DP_REDUCER", "ddp")
         if registered is None:
             registered = os.environ.get("TNCCL_DP_REGISTERED", "0") == "1"
+        if overlap_optimizer is None:
+            overlap_optimizer = os.environ.get("TNCCL_DP_OVERLAP_OPT", "0") == "1"
+        self.overlap_optimizer = overlap_optimizer and reducer == "flat"
+        self.opt = AdamW(gpt2_param_groups(model, weight_decay), lr=lr, betas=betas)
         self.reducer = None
         self.registration = None
         if reducer == "flat":
@@ -56,7 +64,8 @@ class DataParallelTrainer:
                      and comm.size > 1 and comm.info()["nvls"] else None)
             self.reducer = FlatGradReducer(
                 model.parameters(), lambda t: comm.all_reduce(t, op="avg", algo=algo),
-                bucket_bytes=bucket_cap_mb << 20, alloc=alloc, stream=comm.side_stream())
+                bucket_bytes=bucket_cap_mb << 20, alloc=alloc, stream=comm.side_stream(),
+                on_reduced=self.opt.step_params if self.overlap_optimizer else None)
             if alloc is not None:
                 self.registration = comm.register(self.reducer.flat)
             self.ddp = model
@@ -69,16 +78,18 @@ class DataParallelTrainer:
                                                   wire_dtype=wire_dtype)
         else:
             raise ValueError(f"reducer must be 'ddp' or 'flat', not {reducer!r}")
-        self.opt = AdamW(gpt2_param_groups(model, weight_decay), lr=lr, betas=betas)
 
     def step(self, idx: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
         """One optimizer step; returns the (device) loss without synchronizing."""
+        if self.overlap_optimizer:
+            self.opt.begin_step()  # the buckets' hooks apply it during backward
         with torch.autocast("cuda", dtype=self.amp_dtype):
             loss = self.ddp(idx, targets)
         loss.backward()
         if self.reducer is not None:
             self.reducer.finish()
-            self.opt.step()
+            if not self.overlap_optimizer:
+                self.opt.step()
             self.reducer.zero_grad()
         else:
             self.opt.step()
