@@ -213,6 +213,19 @@ def build_tnccl_trainer(args, rank, world, dev):
     return trainer.step, launches, close
 
 
+def reducer_desc() -> str:
+    """The tnccl trainer's gradient path as its environment selects it."""
+    r = os.environ.get("TNCCL_DP_REDUCER", "ddp")
+    if r == "flat":
+        if os.environ.get("TNCCL_DP_REGISTERED") == "1":
+            r += "+registered"
+        if os.environ.get("TNCCL_DP_OVERLAP_OPT") == "1":
+            r += "+overlapped-adamw"
+    if os.environ.get("TNCCL_NVLS_ZERO_COPY") == "1":
+        r += "+nvls-zero-copy"
+    return r
+
+
 def make_record(impl, world, B, T, steps, warmup, ms_max, clocks, launches, e2e, loss):
     """The one JSON line bench.py prints (rank 0): whole-job tokens/s from the
     device step time (max over ranks), plus the end-to-end number, clocks and
@@ -229,8 +242,7 @@ def make_record(impl, world, B, T, steps, warmup, ms_max, clocks, launches, e2e,
             "config": {"model": "GPT-2 small (124M): 12 layers, d_model 768, 12 heads, vocab 50257",
                        "global_batch": B * world, "micro_batch_per_gpu": B, "seq_len": T,
                        "parallelism": f"dp{world}", "optimizer": "AdamW", "amp": "bf16 autocast",
-                       "grad_reducer": (os.environ.get("TNCCL_DP_REDUCER", "ddp")
-                                        if impl == "tnccl" else "ddp"),
+                       "grad_reducer": reducer_desc() if impl == "tnccl" else "ddp",
                        "l2": "no flush: one step touches several GB (activations, 124M-param "
                              "weights/grads/optimizer state), far above the 126 MB L2"},
             "clocks": clocks, "gpu_launches": launches, "e2e": e2e,
