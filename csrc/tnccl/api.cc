@@ -98,6 +98,8 @@ extern "C" tncclResult tncclCommGetInfo(tncclComm_t comm, tncclCommInfo* info) {
   info->netSendSocket = comm->net.send ? 1 : 0;
   info->netRecvSocket = comm->net.recv ? 1 : 0;
   info->netChannels = comm->net.any ? comm->net.layout.channels : 0;
+  for (const Registration& g : comm->regs) info->registrations += g.used ? 1 : 0;
+  info->zeroCopyLaunches = comm->zeroCopyLaunches;
   return TNCCL_SUCCESS;
 }
 

@@ -139,6 +139,7 @@ struct tncclComm {
   uint64_t oneShotMaxBytes = 0;
   uint64_t nvlsMinBytes = 0;
   int maxChannels = 0;  // tncclCommSetMaxChannels cap (0: none)
+  uint64_t zeroCopyLaunches = 0;  // launches of the zero-copy NVLS kernel
 };
 
 namespace tnccl {

@@ -194,6 +194,7 @@ extern "C" tncclResult tncclAllReduceEx(const void* send, void* recv, size_t cou
   if (launchAllReduceKernel(comm->dev, a, (int)chosen, cfg.threads, stream) != cudaSuccess)
     return TNCCL_CUDA_ERROR;
   gLaunchCount.fetch_add(1, std::memory_order_relaxed);
+  if (zeroCopy) ++comm->zeroCopyLaunches;
   bindStream(comm, stream);
   return TNCCL_SUCCESS;
 }

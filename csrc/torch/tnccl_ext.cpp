@@ -152,7 +152,8 @@ class Communicator {
     check(r, "tncclCommDestroy");
   }
 
-  py::dict info() const {
+  py::dict info() {
+    if (comm_ != nullptr) check(tncclCommGetInfo(comm_, &info_), "tncclCommGetInfo");
     py::dict d;
     d["rank"] = info_.rank;
     d["nranks"] = info_.nranks;
@@ -167,6 +168,8 @@ class Communicator {
     d["socket_send_edge"] = (bool)info_.netSendSocket;
     d["socket_recv_edge"] = (bool)info_.netRecvSocket;
     d["socket_channels"] = info_.netChannels;
+    d["registrations"] = info_.registrations;
+    d["zero_copy_launches"] = (uint64_t)info_.zeroCopyLaunches;
     return d;
   }
 

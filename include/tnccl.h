@@ -153,6 +153,8 @@ typedef struct {
   int netSendSocket;        /* 1: this rank's ring edge to rank + 1 is a socket edge */
   int netRecvSocket;        /* 1: its ring edge from rank - 1 is a socket edge */
   int netChannels;          /* ring channels when the communicator has socket edges */
+  int registrations;        /* live tncclCommRegister registrations */
+  unsigned long long zeroCopyLaunches; /* all-reduces that ran the zero-copy NVLS kernel */
 } tncclCommInfo;
 
 tncclResult tncclCommGetInfo(tncclComm_t comm, tncclCommInfo* info);

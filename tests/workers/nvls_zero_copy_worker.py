@@ -94,13 +94,17 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         times[name] = t.item()
     comm.deregister(h)
-    ok = ok and comm.async_error() == 0
+    info = comm.info()
+    ok = ok and comm.async_error() == 0 and info["registrations"] == 0
+    if os.environ.get("TNCCL_NVLS_ZERO_COPY") == "1":
+        ok = ok and info["zero_copy_launches"] > 0
     flag = torch.tensor([1.0 if ok else 0.0], device=dev)
     dist.all_reduce(flag, op=dist.ReduceOp.MIN)
     if rank == 0:
         bus = lambda ms: n * 4 / (ms * 1e-3) * 2 * (world - 1) / world / 1e9
         for name, ms in times.items():
             print(f"{name}: {ms:.3f} ms per 256 MiB fp32 all-reduce = {bus(ms):.1f} GB/s bus")
+        print(f"zero-copy launches on rank 0: {info['zero_copy_launches']}")
         print("PASS" if flag.item() == 1.0 else "FAIL")
     torch.cuda.synchronize()
     comm.destroy()
