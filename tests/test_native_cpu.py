@@ -24,6 +24,14 @@ def test_c_abi_surface(built):
              "tncclMemAlloc", "tncclMemFree", "tncclCommRegister", "tncclCommDeregister"]
     for n in names:
         assert hasattr(lib, n), n
+    # Every function the public header declares is exported.
+    import re
+    with open(os.path.join(ROOT, "include", "tnccl.h")) as f:
+        declared = set(re.findall(r"^\s*(?:[A-Za-z_][\w\s\*]*?)\b(tnccl[A-Z]\w*)\s*\(",
+                                  f.read(), re.M))
+    assert len(declared) >= 25
+    missing = [n for n in sorted(declared) if not hasattr(lib, n)]
+    assert not missing, missing
     lib.tncclGetErrorString.restype = ctypes.c_char_p
     # Values of the tiny-nccl result codes are kept; new codes are appended.
     assert lib.tncclGetErrorString(0) == b"success"
