@@ -235,7 +235,7 @@ extern "C" tncclResult tncclCommRegister(tncclComm_t comm, void* buff, size_t si
     if (!comm->regs[k].used) slot = k;
   if (st == TNCCL_SUCCESS && slot < 0) st = TNCCL_SYSTEM_ERROR;
 
-  // Round 0: statuses and bound sizes must agree.
+  // First status exchange: statuses and bound sizes must agree.
   struct Status {
     int32_t st;
     int32_t pad;
