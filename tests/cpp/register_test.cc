@@ -7,8 +7,14 @@
 // balanced; failures are injected on one rank at each stage and every rank
 // must fail the registration, in step, without waiting for a deadline.
 //
+// The same binary checks the enqueue side (csrc/tnccl/enqueue.cc): which
+// all-reduces take the zero-copy NVLS kernel and the multicast addresses,
+// vector count and channel count they launch with, through a launcher that
+// records its arguments.
+//
 // Built from sources without the CUDA runtime: this file provides the few
-// runtime calls register.cc makes and the transport helpers it uses.
+// runtime calls register.cc and enqueue.cc make, the transport helpers and
+// the kernel launchers.
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
@@ -24,6 +30,7 @@
 
 #include "comm.h"
 #include "driver.h"
+#include "launch.h"
 
 using namespace tnccl;
 
@@ -38,7 +45,33 @@ cudaError_t cudaGetDevice(int* d) {
 cudaError_t cudaSetDevice(int) { return cudaSuccess; }
 cudaError_t cudaStreamSynchronize(cudaStream_t) { return cudaSuccess; }
 cudaError_t cudaDeviceSynchronize() { return cudaSuccess; }
+cudaError_t cudaGetLastError() { return cudaSuccess; }
+cudaError_t cudaMemcpyAsync(void*, const void*, size_t, cudaMemcpyKind, cudaStream_t) {
+  return cudaSuccess;
 }
+const char* tncclAlgoName(tncclAlgo_t) { return "fake"; }
+}
+
+// Kernel launchers: record the last all-reduce launch.
+namespace {
+struct Launch {
+  int count = 0;
+  int algo = -1;
+  AllReduceArgs args{};
+} gLast;
+}  // namespace
+namespace tnccl {
+cudaError_t launchAllReduceKernel(const DevComm&, const AllReduceArgs& a, int algo, int,
+                                  cudaStream_t) {
+  ++gLast.count;
+  gLast.algo = algo;
+  gLast.args = a;
+  return cudaSuccess;
+}
+cudaError_t launchScale(const void*, void*, uint64_t, int, float, int, cudaStream_t) {
+  return cudaSuccess;
+}
+}  // namespace tnccl
 
 namespace {
 
@@ -355,9 +388,85 @@ void injectedFailures() {
   }
 }
 
+// Enqueue: registrations filled in directly (one process), launches recorded.
+void zeroCopySelection() {
+  setenv("TNCCL_NVLS_ZERO_COPY", "1", 1);
+  tncclComm comm;
+  comm.rank = 0;
+  comm.nranks = 4;
+  comm.device = 0;
+  comm.cfg = loadConfig();
+  comm.nvls.enabled = true;
+  comm.nvls.channels = comm.cfg.nvlsChannels;
+  comm.nvls.tileBytes = (uint64_t)comm.cfg.nvlsTileBytes;
+  comm.oneShotMaxBytes = 1 << 20;
+  comm.nvlsMinBytes = ~0ull;  // the staged NVLS kernel is never AUTO's choice
+  alignas(16) static char bufA[8 << 20], bufB[8 << 20], plain[8 << 20];
+  auto reg = [&](int k, char* base, size_t bytes, uint64_t mcVa) {
+    Registration& g = comm.regs[k];
+    g.used = g.bound = g.mapped = true;
+    g.base = base;
+    g.userBytes = bytes;
+    g.bytes = bytes;
+    g.mcVa = mcVa;
+  };
+  reg(0, bufA, sizeof(bufA), 0x100000000ull);
+  reg(1, bufB, sizeof(bufB), 0x200000000ull);
+  auto run = [&](const void* s, void* r, size_t count, tncclDataType_t t, tncclAlgo_t algo) {
+    gLast = Launch{};
+    return tncclAllReduceEx(s, r, count, t, tncclSum, 1.0f, algo, &comm, nullptr) ==
+           TNCCL_SUCCESS;
+  };
+  const size_t n4m = (4u << 20) / 4;
+  bool ok = true;
+  // Registered in place, AUTO, 4 MiB fp32: zero copy with the mc addresses.
+  ok = ok && run(bufA + 4096, bufA + 4096, n4m, tncclFloat32, TNCCL_ALGO_AUTO);
+  ok = ok && gLast.algo == TNCCL_ALGO_NVLS &&
+       gLast.args.mcSend == reinterpret_cast<const char*>(0x100000000ull + 4096) &&
+       gLast.args.mcRecv == reinterpret_cast<char*>(0x100000000ull + 4096) &&
+       gLast.args.zcVecs == (4u << 20) / 16 && gLast.args.zcChannels >= 1 &&
+       gLast.args.zcChannels <= comm.cfg.nvlsZcChannels && comm.zeroCopyLaunches == 1;
+  report("zero copy: registered, AUTO, 4 MiB", ok);
+  // Send in one registration, recv in another.
+  ok = run(bufA, bufB + (1 << 20), n4m, tncclBfloat16, TNCCL_ALGO_AUTO) &&
+       gLast.args.mcSend == reinterpret_cast<const char*>(0x100000000ull) &&
+       gLast.args.mcRecv == reinterpret_cast<char*>(0x200000000ull + (1 << 20)) &&
+       gLast.args.zcVecs == n4m * 2 / 16;
+  report("zero copy: send and recv in different registrations", ok);
+  // Not zero copy: unregistered recv, unaligned, not whole vectors, below the
+  // AUTO minimum (but zero copy when NVLS is asked for), past the end.
+  ok = run(bufA, plain, n4m, tncclFloat32, TNCCL_ALGO_AUTO) && gLast.args.mcSend == nullptr &&
+       gLast.algo != TNCCL_ALGO_NVLS;
+  ok = ok && run(bufA + 4, bufA + 4, n4m, tncclFloat32, TNCCL_ALGO_AUTO) &&
+       gLast.args.mcSend == nullptr;
+  ok = ok && run(bufA, bufA, n4m + 1, tncclFloat32, TNCCL_ALGO_AUTO) &&
+       gLast.args.mcSend == nullptr;
+  ok = ok && run(bufA, bufA, 1024, tncclFloat32, TNCCL_ALGO_AUTO) &&
+       gLast.args.mcSend == nullptr;
+  ok = ok && run(bufA, bufA, 1024, tncclFloat32, TNCCL_ALGO_NVLS) &&
+       gLast.args.mcSend != nullptr && gLast.args.zcChannels == 1;
+  ok = ok && run(bufA + (6 << 20), bufA + (6 << 20), n4m, tncclFloat32, TNCCL_ALGO_AUTO) &&
+       gLast.args.mcSend == nullptr;
+  ok = ok && run(bufA, bufA, n4m, tncclFloat32, TNCCL_ALGO_TWOSHOT) &&
+       gLast.args.mcSend == nullptr && gLast.algo == TNCCL_ALGO_TWOSHOT;
+  report("not zero copy: unregistered, unaligned, ragged, small, past end, other algo", ok);
+  // The channel cap applies to the zero-copy kernel too.
+  comm.maxChannels = 3;  // what tncclCommSetMaxChannels(comm, 3) sets
+  ok = run(bufA, bufA, 2 * n4m, tncclFloat32, TNCCL_ALGO_AUTO) && gLast.args.mcSend != nullptr &&
+       gLast.args.zcChannels == 3;
+  comm.maxChannels = 0;
+  // Off by default: without TNCCL_NVLS_ZERO_COPY the staged paths run.
+  comm.cfg.nvlsZeroCopy = 0;
+  ok = ok && run(bufA, bufA, n4m, tncclFloat32, TNCCL_ALGO_NVLS) && gLast.args.mcSend == nullptr &&
+       gLast.algo == TNCCL_ALGO_NVLS;
+  report("zero copy: channel cap, and off without TNCCL_NVLS_ZERO_COPY", ok);
+  unsetenv("TNCCL_NVLS_ZERO_COPY");
+}
+
 }  // namespace
 
 int main() {
+  zeroCopySelection();
   allocAndFree();
   registerAndDeregister();
   argumentErrors();

@@ -82,8 +82,8 @@ def test_gemm_pipeline_model_under_tsan():
 @pytest.mark.skipif(shutil.which("g++") is None, reason="needs g++")
 def test_registration_under_asan_ubsan():
     exe = _build("register_asan", ["tests/cpp/register_test.cc", "csrc/tnccl/register.cc",
-                                   "csrc/tnccl/bootstrap.cc", "csrc/tnccl/common.cc",
-                                   "csrc/tnccl/sockio.cc"],
+                                   "csrc/tnccl/enqueue.cc", "csrc/tnccl/bootstrap.cc",
+                                   "csrc/tnccl/common.cc", "csrc/tnccl/sockio.cc"],
                  ["-fsanitize=address,undefined", "-fno-omit-frame-pointer",
                   "-fno-sanitize-recover=undefined"])
     env = dict(os.environ, ASAN_OPTIONS="detect_leaks=1:abort_on_error=1")

@@ -177,8 +177,8 @@ PROGRAMS = {
 STANDALONE = {
     # registered buffers: forked ranks, real bootstrap, fake driver
     "register_test": [ROOT / "tests" / "cpp" / "register_test.cc", TNCCL_SRC / "register.cc",
-                      TNCCL_SRC / "bootstrap.cc", TNCCL_SRC / "sockio.cc",
-                      TNCCL_SRC / "common.cc"],
+                      TNCCL_SRC / "enqueue.cc", TNCCL_SRC / "bootstrap.cc",
+                      TNCCL_SRC / "sockio.cc", TNCCL_SRC / "common.cc"],
 }
 
 
@@ -193,7 +193,7 @@ def build_standalone() -> list[Path]:
         key = _hash(deps, "standalone " + " ".join(CXXFLAGS))
         if not (out.exists() and stamp.exists() and stamp.read_text() == key):
             _run(["g++", *CXXFLAGS, "-O1", *INCLUDES, f"-I{ROOT / 'tests' / 'cpp'}",
-                  *[str(s) for s in srcs], "-o", str(out), "-lpthread"])
+                  *[str(s) for s in srcs], "-o", str(out), "-lpthread", "-ldl"])
             stamp.write_text(key)
         outs.append(out)
     return outs
