@@ -123,10 +123,12 @@ extern "C" tncclResult tncclAllReduceEx(const void* send, void* recv, size_t cou
   }
 
   // Zero-copy NVLS: both buffers registered (every rank registered the same
-  // buffers, so every rank makes the same choice), whole 16-byte vectors.
+  // buffers, so every rank makes the same choice), whole 16-byte vectors, and
+  // no socket edges (with them AUTO keeps every message on the ring).
   const Registration* regSend = nullptr;
   const Registration* regRecv = nullptr;
-  if (comm->cfg.nvlsZeroCopy && comm->nvls.enabled && vectorized && bytes % kVectorBytes == 0 &&
+  if (comm->cfg.nvlsZeroCopy && comm->nvls.enabled && !comm->net.any && vectorized &&
+      bytes % kVectorBytes == 0 &&
       (algo == TNCCL_ALGO_NVLS ||
        (algo == TNCCL_ALGO_AUTO && comm->cfg.forcedAlgo == TNCCL_ALGO_AUTO &&
         bytes >= (uint64_t)comm->cfg.nvlsZcMinBytes))) {
