@@ -54,6 +54,8 @@ class DataParallelTrainer:
         self.reducer = None
         self.registration = None
         if reducer == "flat":
+            if wire_dtype is not None:
+                raise ValueError("wire_dtype is an option of reducer='ddp'")
             # DDP would broadcast rank 0's parameters; do the same once.
             with torch.no_grad():
                 for t in list(model.parameters()) + list(model.buffers()):
