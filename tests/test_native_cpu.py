@@ -334,3 +334,65 @@ def test_trace_to_chrome_conversion(tmp_path):
     red0 = next(e for e in spans if e["name"] == "reduce" and e["tid"] == 0)
     assert abs(red0["ts"] - 0.5) < 1e-9 and abs(red0["dur"] - 2.5) < 1e-9
     assert any(e["ph"] == "i" and e["name"] == "pushed+published" for e in ev)
+
+
+def test_empty_registrable_views(monkeypatch):
+    """empty_registrable: the tncclMemAlloc bytes are viewed as the requested
+    dtype and shape (stand-in allocator on the CPU, which records sizes)."""
+    import torch
+
+    from tiny_nccl_b200.parallel import comm as C
+
+    asked = []
+
+    class FakeNative:
+        def mem_empty(self, nbytes, device):
+            asked.append((nbytes, device))
+            return torch.empty(nbytes, dtype=torch.uint8)
+
+    monkeypatch.setattr(C, "load", lambda: FakeNative())
+    t = C.empty_registrable((3, 5), torch.float32, "cpu")
+    assert t.shape == (3, 5) and t.dtype == torch.float32 and asked[-1][0] == 60
+    b = C.empty_registrable(7, torch.bfloat16, "cpu")
+    assert b.shape == (7,) and b.dtype == torch.bfloat16 and asked[-1][0] == 14
+    # Every view starts at the allocation's first byte (offset 0 is what
+    # tncclCommRegister binds).
+    assert b.untyped_storage().data_ptr() == b.data_ptr()
+    z = C.empty_registrable(0, torch.float16, "cpu")
+    assert z.numel() == 0 and asked[-1][0] == 2
+
+
+def test_flat_reducer_launches_in_bucket_order():
+    """FlatGradReducer launches bucket all-reduces strictly in bucket order
+    (what keeps ranks' collectives in step) even when gradients complete out
+    of order; offsets and bucket ends are 16-byte aligned; the .grad tensors
+    are views of the flat buffer."""
+    import torch
+
+    from tiny_nccl_b200.parallel.reducer import FlatGradReducer
+
+    params = [torch.nn.Parameter(torch.zeros(n)) for n in (5, 3, 9, 4, 7)]
+    order = []
+    red = FlatGradReducer(params, lambda t: order.append(t.data_ptr()), bucket_bytes=32)
+    starts = [red.flat[s:e].data_ptr() for s, e in red.buckets]
+    assert len(red.buckets) >= 3
+    assert all(s % 4 == 0 and e % 4 == 0 for s, e in red.buckets)
+    for p in params:
+        assert red.flat.data_ptr() <= p.grad.data_ptr() < red.flat.data_ptr() + red.flat.numel() * 4
+        assert (p.grad.data_ptr() - red.flat.data_ptr()) % 16 == 0
+    # Complete the buckets back to front: nothing may launch before bucket 0.
+    for b in reversed(range(1, len(red.buckets))):
+        for p in red.bucket_params[b]:
+            red._ready(p)
+    assert order == []
+    for p in red.bucket_params[0]:
+        red._ready(p)
+    assert order == starts
+    red.finish()
+    assert red.launched == len(red.buckets)
+    # finish() launches what never completed, still in order, and re-arms.
+    order.clear()
+    red._ready(red.bucket_params[1][0])
+    red.finish()
+    assert order == starts
+    red.remove()
