@@ -198,6 +198,19 @@ __global__ void __launch_bounds__(kMaxThreads)
   const bool scale = alpha != 1.0f;
   __shared__ int sFail;
   if (threadIdx.x == 0) sFail = 0;
+#if TNCCL_DEVICE_CHECKS
+  // The grid is the plan's channel count and both multicast views are
+  // 16-byte aligned (the host guarantees both; a debug build verifies).
+  if (threadIdx.x == 0 &&
+      ((int)gridDim.x != a.zcChannels ||
+       ((reinterpret_cast<uintptr_t>(a.mcSend) | reinterpret_cast<uintptr_t>(a.mcRecv)) & 15))) {
+    recordFailure(comm, 3, whereCode(kCounterNvlsZc, c, kCheckPhase), (uint64_t)a.zcChannels,
+                  (uint64_t)gridDim.x);
+    sFail = 1;
+  }
+  __syncthreads();
+  if (sFail) return;
+#endif
   const uint64_t seq0 = comm.counters[kCounterNvlsZc * kMaxChannels + c];
   const uint64_t target = (uint64_t)P * (seq0 + 1);
   auto counterOff = [&](int phase) {
