@@ -159,6 +159,7 @@ def main():
         x = src[:n]
         y = dst[:n]
         for impl in impls:
+            zc0 = comm.info()["zero_copy_launches"]
             if impl == "ref" and size > parse_size(args.ref_max_bytes):
                 continue
 
@@ -205,6 +206,8 @@ def main():
                    "us": t * 1e6, "algbw_gbs": algbw, "busbw_gbs": busbw, "iters": k,
                    "chosen": comm.select_algo(n, dtype) if impl == "auto" else impl,
                    "frac_link": busbw / LINK_GBS}
+            if impl == "nvls_zc":  # did the zero-copy kernel run (TNCCL_NVLS_ZERO_COPY=1)?
+                rec["zero_copy"] = comm.info()["zero_copy_launches"] > zc0
             if args.check and impl != "nccl":
                 ref_y = x.clone()
                 with torch.cuda.stream(stream):
