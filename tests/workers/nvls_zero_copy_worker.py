@@ -2,7 +2,8 @@
 (tncclMemAlloc + tncclCommRegister, TNCCL_NVLS_ZERO_COPY=1) gives the exact
 sums of integer-valued inputs (fp32 and bf16, in and out of place, pre-scale
 1/W), over many back-to-back launches interleaved with staged launches on
-unregistered buffers; then deregisters and destroys. Prints the time per
+unregistered buffers; replays zero-copy launches captured in a CUDA graph;
+then deregisters and destroys. Prints the time per
 launch of the zero-copy and the staged NVLS kernel at 256 MiB, and PASS on
 rank 0 (SKIP when the communicator has no NVLS)."""
 import datetime
@@ -72,6 +73,35 @@ def main():
     for h, _ in live:
         comm.deregister(h)
     live.clear()
+    # CUDA graph: zero-copy launches captured once and replayed (their barrier
+    # counters live in device memory), on a second communicator bound to a
+    # side stream.
+    comm2 = tn.init_from_torch_distributed(device=rank)
+    stream = torch.cuda.Stream(device=dev)
+    xg = empty_registrable(1 << 20, torch.float32, dev)
+    hg = comm2.register(xg)
+    with torch.cuda.stream(stream):
+        xg.fill_(1.0)
+        comm2.all_reduce(xg, algo="nvls")  # eager: binds the stream
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        comm2.all_reduce(xg, algo="nvls", op="avg")
+        comm2.all_reduce(xg, algo="nvls")
+    for it in range(3):
+        with torch.cuda.stream(stream):
+            xg.fill_(float(rank + 1 + it))
+            graph.replay()
+        torch.cuda.synchronize()
+        want = float(sum(r + 1 + it for r in range(world)))
+        if not torch.allclose(xg, torch.full_like(xg, want), rtol=1e-6):
+            ok = False
+            print(f"rank {rank}: graph replay {it} wrong", flush=True)
+    del graph
+    torch.cuda.synchronize()
+    comm2.deregister(hg)
+    ok = ok and comm2.async_error() == 0
+    comm2.destroy()
     # Time per launch at 256 MiB fp32: zero-copy vs staged NVLS.
     n = 64 << 20
     x = empty_registrable(n, torch.float32, dev)
