@@ -130,8 +130,10 @@ extern "C" tncclResult tncclAllReduceEx(const void* send, void* recv, size_t cou
   if (comm->cfg.nvlsZeroCopy && comm->nvls.enabled && !comm->net.any && vectorized &&
       bytes % kVectorBytes == 0 &&
       (algo == TNCCL_ALGO_NVLS ||
-       (algo == TNCCL_ALGO_AUTO && comm->cfg.forcedAlgo == TNCCL_ALGO_AUTO &&
-        bytes >= (uint64_t)comm->cfg.nvlsZcMinBytes))) {
+       (algo == TNCCL_ALGO_AUTO &&
+        (comm->cfg.forcedAlgo == TNCCL_ALGO_NVLS ||
+         (comm->cfg.forcedAlgo == TNCCL_ALGO_AUTO &&
+          bytes >= (uint64_t)comm->cfg.nvlsZcMinBytes))))) {
     regSend = findRegistration(comm, send, bytes);
     regRecv = regSend ? findRegistration(comm, recv, bytes) : nullptr;
   }

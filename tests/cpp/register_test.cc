@@ -450,6 +450,15 @@ void zeroCopySelection() {
   ok = ok && run(bufA, bufA, n4m, tncclFloat32, TNCCL_ALGO_TWOSHOT) &&
        gLast.args.mcSend == nullptr && gLast.algo == TNCCL_ALGO_TWOSHOT;
   report("not zero copy: unregistered, unaligned, ragged, small, past end, other algo", ok);
+  // TNCCL_ALGO=nvls (forced) counts like an explicit NVLS request; another
+  // forced algorithm keeps AUTO calls off the zero-copy kernel.
+  comm.cfg.forcedAlgo = TNCCL_ALGO_NVLS;
+  ok = run(bufA, bufA, 1024, tncclFloat32, TNCCL_ALGO_AUTO) && gLast.args.mcSend != nullptr;
+  comm.cfg.forcedAlgo = TNCCL_ALGO_TWOSHOT;
+  ok = ok && run(bufA, bufA, n4m, tncclFloat32, TNCCL_ALGO_AUTO) &&
+       gLast.args.mcSend == nullptr && gLast.algo == TNCCL_ALGO_TWOSHOT;
+  comm.cfg.forcedAlgo = TNCCL_ALGO_AUTO;
+  report("zero copy: TNCCL_ALGO=nvls yes, TNCCL_ALGO=twoshot no", ok);
   // The channel cap applies to the zero-copy kernel too.
   comm.maxChannels = 3;  // what tncclCommSetMaxChannels(comm, 3) sets
   ok = run(bufA, bufA, 2 * n4m, tncclFloat32, TNCCL_ALGO_AUTO) && gLast.args.mcSend != nullptr &&
