@@ -265,10 +265,12 @@ def main():
     args.warmup = max(args.warmup, 3)
 
     if args.impl == "reference" and not os.path.exists(REF_LIB):
-        # baseline/build_reference.sh installs it; TNCCL_REFERENCE_SRC names
-        # the reference source to build it from here.
+        # baseline/build_reference.sh installs it (build() in __graft_entry__
+        # runs it); TNCCL_REFERENCE_SRC, else a `reference` directory beside
+        # this repository, names the reference source to build it from here.
         script = os.path.join(ROOT, "baseline", "build_reference.sh")
-        src = os.environ.get("TNCCL_REFERENCE_SRC", "")
+        src = os.environ.get("TNCCL_REFERENCE_SRC") or os.path.join(os.path.dirname(ROOT),
+                                                                    "reference")
         if src and os.path.isdir(src):
             subprocess.run(["bash", script, src], stdout=subprocess.DEVNULL,
                            stderr=subprocess.DEVNULL, check=False)

@@ -36,6 +36,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <utility>
+
 #include <atomic>
 
 #include "device.cuh"
@@ -173,14 +175,27 @@ int emulatedMaxCtasTyped(int threads) {
   return perSm * sms;
 }
 
+// Launches `kernel` and returns that launch's own error. A triple-chevron
+// launch followed by cudaGetLastError would also report (and clear) an
+// unrelated error that an earlier call of the caller left behind.
+template <typename... Params, typename... Args>
+cudaError_t launchOwn(void (*kernel)(Params...), unsigned grid, dim3 block, uint32_t smem,
+                      cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 template <typename T, int MAXP>
 cudaError_t launchTwoShot(const DevComm& comm, const AllReduceArgs& a, dim3 block,
                           cudaStream_t stream) {
   const uint32_t smem = twoShotSmemBytes(comm, MAXP);
   cudaError_t err = allowSmem<twoShotKernel<T, MAXP>>(smem);
   if (err != cudaSuccess) return err;
-  twoShotKernel<T, MAXP><<<a.chunk.channels, block, smem, stream>>>(comm, a);
-  return cudaGetLastError();
+  return launchOwn(twoShotKernel<T, MAXP>, a.chunk.channels, block, smem, stream, comm, a);
 }
 
 template <typename T>
@@ -190,10 +205,8 @@ cudaError_t launchTyped(const DevComm& comm, const AllReduceArgs& a, int algo, i
   switch (algo) {
     case TNCCL_ALGO_RING:
       if (comm.netSend || comm.netRecv)
-        ringKernel<T, true><<<a.chunk.channels, block, 0, stream>>>(comm, a);
-      else
-        ringKernel<T, false><<<a.chunk.channels, block, 0, stream>>>(comm, a);
-      break;
+        return launchOwn(ringKernel<T, true>, a.chunk.channels, block, 0, stream, comm, a);
+      return launchOwn(ringKernel<T, false>, a.chunk.channels, block, 0, stream, comm, a);
     case TNCCL_ALGO_TWOSHOT:
       if (comm.nranks <= 2)
         return launchTwoShot<T, 2>(comm, a, block, stream);
@@ -204,29 +217,23 @@ cudaError_t launchTyped(const DevComm& comm, const AllReduceArgs& a, int algo, i
       return launchTwoShot<T, 16>(comm, a, block, stream);
     case TNCCL_ALGO_ONESHOT:
       if (comm.nranks <= 2)
-        oneShotKernel<T, 2><<<a.block.channels, block, 0, stream>>>(comm, a);
-      else if (comm.nranks <= 4)
-        oneShotKernel<T, 4><<<a.block.channels, block, 0, stream>>>(comm, a);
-      else if (comm.nranks <= 8)
-        oneShotKernel<T, 8><<<a.block.channels, block, 0, stream>>>(comm, a);
-      else
-        oneShotKernel<T, 16><<<a.block.channels, block, 0, stream>>>(comm, a);
-      break;
+        return launchOwn(oneShotKernel<T, 2>, a.block.channels, block, 0, stream, comm, a);
+      if (comm.nranks <= 4)
+        return launchOwn(oneShotKernel<T, 4>, a.block.channels, block, 0, stream, comm, a);
+      if (comm.nranks <= 8)
+        return launchOwn(oneShotKernel<T, 8>, a.block.channels, block, 0, stream, comm, a);
+      return launchOwn(oneShotKernel<T, 16>, a.block.channels, block, 0, stream, comm, a);
     case TNCCL_ALGO_NVLS: {
-      if (a.mcSend != nullptr) {
-        nvlsZeroCopyKernel<T><<<a.zcChannels, block, 0, stream>>>(comm, a);
-        break;
-      }
+      if (a.mcSend != nullptr)
+        return launchOwn(nvlsZeroCopyKernel<T>, a.zcChannels, block, 0, stream, comm, a);
       const uint32_t smem = nvlsSmemBytes(comm);
       cudaError_t err = allowSmem<nvlsKernel<T>>(smem);
       if (err != cudaSuccess) return err;
-      nvlsKernel<T><<<a.block.channels, block, smem, stream>>>(comm, a);
-      break;
+      return launchOwn(nvlsKernel<T>, a.block.channels, block, smem, stream, comm, a);
     }
     default:
       return cudaErrorInvalidValue;
   }
-  return cudaGetLastError();
 }
 
 template <typename T>
@@ -235,9 +242,8 @@ cudaError_t launchScaleTyped(const void* x, void* y, uint64_t n, float alpha, in
   const uint64_t work = vectorized ? n / Pack<T>::V + 1 : n;
   unsigned blocks = (unsigned)minU64(divUp(work, 256), 148ull * 8);
   if (blocks == 0) blocks = 1;
-  scaleKernel<T><<<blocks, 256, 0, stream>>>(static_cast<const T*>(x), static_cast<T*>(y), n,
-                                             alpha, vectorized);
-  return cudaGetLastError();
+  return launchOwn(scaleKernel<T>, blocks, dim3(256), 0, stream, static_cast<const T*>(x),
+                   static_cast<T*>(y), n, alpha, vectorized);
 }
 
 }  // namespace

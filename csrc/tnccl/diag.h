@@ -9,26 +9,14 @@
 extern "C" {
 #endif
 
-// Times `iters` launches of one NVLink/HBM primitive (see diag.cu) on this
-// rank and returns the mean milliseconds per launch. Every rank must call it
-// with the same arguments at the same time. It overwrites the ring data area
-// of the mailboxes, which holds no state between collectives.
-tncclResult tncclDiagBench(tncclComm_t comm, int mode, size_t bytes, int ctas, int threads,
-                           int unroll, size_t chunk, int iters, cudaStream_t stream,
-                           float* msPerIter);
-
-#ifdef __cplusplus
-}
-#endif
-
-#ifdef __cplusplus
-extern "C" {
-#endif
-
 // Launches one kernel that waits, bounded by timeoutMs, on a device word that
 // is never written. After the stream completes, tncclCommGetAsyncError
 // reports TNCCL_TIMEOUT and the communicator refuses further collectives.
 tncclResult tncclDiagWaitTimeout(tncclComm_t comm, int timeoutMs, cudaStream_t stream);
+
+// 1 if this build of the library has the kernels' debug protocol checks
+// compiled in (TNCCL_DEVICE_CHECKS=1), 0 otherwise.
+int tncclDiagDeviceChecks(void);
 
 // Overwrites guard line `which` (0 .. 4) of this rank's mailbox from the host
 // (cudaMemset), so a test can check that tncclCommValidate notices.

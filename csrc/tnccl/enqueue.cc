@@ -191,7 +191,6 @@ extern "C" tncclResult tncclAllReduceEx(const void* send, void* recv, size_t cou
     default:
       return TNCCL_INVALID_ARGUMENT;
   }
-  if (cudaGetLastError() != cudaSuccess) return TNCCL_CUDA_ERROR;
   TN_TRACE("rank %d: allreduce %zu x %zu B algo %s%s", comm->rank, count, es,
            tncclAlgoName(chosen), zeroCopy ? " (zero-copy)" : "");
   NvtxRange range("tncclAllReduce %s %zu B rank %d", tncclAlgoName(chosen), bytes, comm->rank);

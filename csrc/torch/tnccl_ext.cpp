@@ -189,23 +189,6 @@ class Communicator {
     return d;
   }
 
-  // Diagnostic: mean ms per launch of one NVLink/HBM primitive (diag.cu).
-  double diagBench(int mode, uint64_t bytes, int ctas, int threads, int unroll, uint64_t chunk,
-                   int iters) {
-    live();
-    c10::cuda::CUDAGuard guard(info_.device);
-    float ms = 0.f;
-    cudaStream_t stream = c10::cuda::getCurrentCUDAStream(info_.device).stream();
-    tncclResult r;
-    {
-      py::gil_scoped_release nogil;
-      r = tncclDiagBench(comm_, mode, (size_t)bytes, ctas, threads, unroll, (size_t)chunk, iters,
-                         stream, &ms);
-    }
-    check(r, "tncclDiagBench");
-    return ms;
-  }
-
   // Self test of the bounded device waits (see tncclDiagWaitTimeout).
   void diagWaitTimeout(int timeoutMs) {
     live();
@@ -355,7 +338,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("destroy", &Communicator::destroy)
       .def("info", &Communicator::info)
       .def("net_stats", &Communicator::netStats)
-      .def("diag_bench", &Communicator::diagBench)
       .def("diag_wait_timeout", &Communicator::diagWaitTimeout)
       .def("trace_read", &Communicator::traceRead)
       .def("register", &Communicator::registerTensor, py::arg("tensor"))
@@ -374,6 +356,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mem_empty", &memEmpty, py::arg("nbytes"), py::arg("device"));
   m.def("get_unique_id_tcp", &getUniqueIdTcp);
   m.def("launch_count", []() { return tncclGetLaunchCount(); });
+  // 1 when the loaded collective library is the build with the device
+  // protocol checks (lib/checked/libtnccl.so).
+  m.def("device_checks", []() { return tncclDiagDeviceChecks(); });
   m.def("error_string", [](int r) { return std::string(tncclGetErrorString((tncclResult)r)); });
   m.def("version", []() {
     int v = 0;

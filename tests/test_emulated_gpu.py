@@ -3,13 +3,31 @@ cooperative launch (tncclEmu*), so the ring / one-shot / two-shot device code
 is exercised with 2, 4 and 8 ranks even when a single GPU is available.
 Results are compared bit for bit with an order-aware fp32 oracle: rank order
 0..P-1 for one-shot/two-shot, the ring's s+1 ... s rotation (rounded to the
-wire type at every hop) for the ring."""
+wire type at every hop) for the ring.
+
+The last test runs this module again in a child process on the build with the
+kernels' debug protocol checks (lib/checked/libtnccl.so, preloaded): every
+launch checks its plan against the mailbox capacities and the ring checks
+each sequence number it waits for, so a protocol slip fails a test instead of
+passing silently."""
 import os
+import sys
 
 import pytest
 import torch
 
 pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+@pytest.fixture(autouse=True)
+def _expected_build():
+    """In the child process of the device-checks test, the debug build must
+    really be the one loaded."""
+    if os.environ.get("TNCCL_EXPECT_DEVICE_CHECKS") == "1":
+        import tiny_nccl_b200 as tn
+        assert tn.load().device_checks() == 1
 
 CHANNELS = 8  # small enough that channels x ranks CTAs are co-resident
 RING_CHUNK = 256 << 10
@@ -150,9 +168,6 @@ def test_emulated_twoshot_staging_paths(built, P, stage_min):
         emu.destroy()
 
 
-@pytest.mark.skipif(os.environ.get("TNCCL_TEST_SOCKET_EDGES") != "1",
-                    reason="socket-edge GPU path not yet run on a GPU; "
-                           "set TNCCL_TEST_SOCKET_EDGES=1")
 @pytest.mark.parametrize("P,hosts", [(2, None), (4, None), (4, "0,0,1,1"), (8, "0,0,0,1,1,2,2,2")])
 def test_emulated_socket_ring(built, P, hosts):
     """The ring over socket edges on one GPU: emulated ranks joined by
@@ -200,3 +215,17 @@ def test_emulated_socket_ring(built, P, hosts):
         assert emu.async_error() == 0
     finally:
         emu.destroy()
+
+
+@pytest.mark.skipif(os.environ.get("TNCCL_EXPECT_DEVICE_CHECKS") == "1",
+                    reason="already inside the device-checks run")
+def test_emulated_suite_with_device_checks(built):
+    """Every other test of this module, on the debug build of the library."""
+    from conftest import run
+    lib = os.path.join(ROOT, "tiny_nccl_b200", "lib", "checked", "libtnccl.so")
+    assert os.path.exists(lib), "build_all() builds lib/checked/libtnccl.so"
+    env = {"LD_PRELOAD": lib, "TNCCL_EXPECT_DEVICE_CHECKS": "1"}
+    r = run([sys.executable, "-m", "pytest", "tests/test_emulated_gpu.py", "-q", "-x", "-m", "gpu",
+             "-p", "no:cacheprovider"], timeout=1200, env=env)
+    assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-4000:]
+    assert " passed" in r.stdout and " failed" not in r.stdout, r.stdout[-2000:]

@@ -1,20 +1,11 @@
 """The tcgen05 GEMM with the fused bias + GELU epilogue (csrc/ops/
 gemm_tcgen05.cu), one CTA per tile and persistent, against an fp32 PyTorch
 reference of the same op, on the GPT-2 MLP shape and on shapes with M, N and
-K tails.
-
-These run only with TNCCL_TEST_TCGEN05=1: the kernel has not yet run on a
-GPU, and it joins the default GPU suite (and the model) once it has."""
-import os
-
+K tails."""
 import pytest
 import torch
 
-pytestmark = [
-    pytest.mark.gpu,
-    pytest.mark.skipif(os.environ.get("TNCCL_TEST_TCGEN05") != "1",
-                       reason="tcgen05 GEMM not yet run on a GPU; set TNCCL_TEST_TCGEN05=1"),
-]
+pytestmark = pytest.mark.gpu
 
 SHAPES = [(128, 256, 64), (256, 264, 72), (1000, 3072, 768), (8192, 3072, 768)]
 

@@ -11,6 +11,11 @@ Builds three shared objects next to this file (``lib/``), all for sm_100a:
                          plain C launcher interface.
 * ``_C.*.so``          - the PyTorch binding (``csrc/torch``), compiled with g++
                          only and linked against the two libraries above.
+* ``checked/libtnccl.so`` - the collective library again, with the kernels'
+                         debug protocol checks compiled in (-DTNCCL_DEVICE_CHECKS=1).
+                         Both collective libraries carry the SONAME
+                         ``libtnccl.so``, so a process that preloads the checked
+                         one (LD_PRELOAD) runs the binding on it.
 
 A build is skipped when a stamp file records the same source/flag hash, so the
 ``.so`` files that travel with the repository are reused as they are.
@@ -63,12 +68,12 @@ def _run(cmd, cwd=ROOT):
     return r
 
 
-def _compile(src: Path, obj: Path, extra_inc=()):
+def _compile(src: Path, obj: Path, extra_inc=(), defines=()):
     obj.parent.mkdir(parents=True, exist_ok=True)
     if src.suffix == ".cu":
-        cmd = [NVCC, *NVCCFLAGS, *INCLUDES, *extra_inc, "-c", str(src), "-o", str(obj)]
+        cmd = [NVCC, *NVCCFLAGS, *defines, *INCLUDES, *extra_inc, "-c", str(src), "-o", str(obj)]
     else:
-        cmd = ["g++", *CXXFLAGS, *INCLUDES, *extra_inc, "-c", str(src), "-o", str(obj)]
+        cmd = ["g++", *CXXFLAGS, *defines, *INCLUDES, *extra_inc, "-c", str(src), "-o", str(obj)]
     _run(cmd)
     return obj
 
@@ -77,20 +82,24 @@ def _headers(d: Path):
     return [p for p in d.rglob("*") if p.suffix in (".h", ".cuh", ".hpp")]
 
 
-def _build_shared(name: str, srcs, deps, link_extra=(), extra_inc=(), jobs=8) -> Path:
-    out = LIB / name
-    stamp = LIB / (name + ".stamp")
-    key = _hash(list(srcs) + list(deps), " ".join(NVCCFLAGS + CXXFLAGS + list(link_extra)))
+def _build_shared(name: str, srcs, deps, link_extra=(), extra_inc=(), jobs=8,
+                  subdir: str = "", defines=()) -> Path:
+    outdir = LIB / subdir if subdir else LIB
+    out = outdir / name
+    stamp = outdir / (name + ".stamp")
+    key = _hash(list(srcs) + list(deps),
+                " ".join(NVCCFLAGS + list(defines) + CXXFLAGS + list(link_extra)))
     if out.exists() and stamp.exists() and stamp.read_text() == key:
         return out
-    LIB.mkdir(parents=True, exist_ok=True)
-    objdir = OBJ / name
+    outdir.mkdir(parents=True, exist_ok=True)
+    objdir = OBJ / (subdir + "_" + name if subdir else name)
     with cf.ThreadPoolExecutor(max_workers=jobs) as ex:
         objs = list(ex.map(lambda s: _compile(s, objdir / (s.stem + s.suffix.replace(".", "_") + ".o"),
-                                              extra_inc), srcs))
+                                              extra_inc, defines), srcs))
     tmp = out.with_suffix(".so.tmp")
     cmd = [NVCC, *ARCH, "-shared", "-cudart", "static", "-o", str(tmp), *map(str, objs),
-           "-Xlinker", "-rpath,$ORIGIN", *link_extra, "-lpthread", "-ldl", "-lrt"]
+           "-Xlinker", "-rpath,$ORIGIN", "-Xlinker", f"-soname,{name}", *link_extra,
+           "-lpthread", "-ldl", "-lrt"]
     _run(cmd)
     os.replace(tmp, out)
     stamp.write_text(key)
@@ -101,6 +110,14 @@ def build_tnccl() -> Path:
     srcs = sorted(TNCCL_SRC.glob("*.cc")) + sorted(TNCCL_SRC.glob("*.cu"))
     deps = _headers(TNCCL_SRC) + [ROOT / "include" / "tnccl.h"]
     return _build_shared("libtnccl.so", srcs, deps)
+
+
+def build_tnccl_checked() -> Path:
+    """libtnccl.so with the device protocol checks, in lib/checked/."""
+    srcs = sorted(TNCCL_SRC.glob("*.cc")) + sorted(TNCCL_SRC.glob("*.cu"))
+    deps = _headers(TNCCL_SRC) + [ROOT / "include" / "tnccl.h"]
+    return _build_shared("libtnccl.so", srcs, deps, subdir="checked",
+                         defines=["-DTNCCL_DEVICE_CHECKS=1"])
 
 
 def build_ops() -> Path | None:
@@ -230,8 +247,8 @@ def build_programs() -> list[Path]:
 
 
 def build_all(verbose: bool = False) -> None:
-    paths = [build_tnccl(), build_ops(), build_torch_ext(), *build_programs(),
-             *build_standalone()]
+    paths = [build_tnccl(), build_tnccl_checked(), build_ops(), build_torch_ext(),
+             *build_programs(), *build_standalone()]
     if verbose:
         for p in paths:
             if p is not None:
