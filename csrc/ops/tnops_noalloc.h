@@ -35,7 +35,10 @@ extern "C" {
 //    launching anything.
 //  * The first call on a device looks up the device address of the built-in
 //    scratch for that device (the device must be current). Make that first
-//    call before any CUDA stream capture starts.
+//    call before any CUDA stream capture starts. The address is kept for the
+//    life of the process's context on that device: after cudaDeviceReset (or
+//    anything else that destroys the primary context) do not call this
+//    entry point again in the same process.
 //  * All calls share one scratch buffer per device, which keeps what the
 //    last call wrote. Every element a call reads is written earlier in the
 //    same call, so nothing has to be cleared between calls. Calls whose
