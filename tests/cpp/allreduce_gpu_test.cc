@@ -1,6 +1,6 @@
 // allreduce_gpu_test.cc - multi-process all-reduce correctness on real GPUs.
 //
-// Usage: allreduce_gpu_test <nranks> [quick|full|stress] [algo,...]
+// Usage: allreduce_gpu_test <nranks> [quick|full|stress|nvls_order] [algo,...]
 //
 // Forks one process per GPU (rank r uses device r). Every rank generates all
 // ranks' seeded Uniform[-1,1) inputs on the host, so each rank can compute the
@@ -13,6 +13,13 @@
 // fresh inputs on one bound stream, every iteration checked. The other modes
 // end by checking that device memory did not grow across collectives of 4 to
 // 64 MiB and that the mailbox guard lines are intact.
+//
+// "nvls_order" studies the switch's fp32 reduction: the same inputs are
+// reduced 5 times by the NVLS kernel (run-to-run stability must be exact),
+// and the result is compared element by element with candidate summation
+// orders (rank order 0..P-1, its reverse, a balanced pairwise tree, and the
+// P rotations that start at rank k); rank 0 prints the fraction of elements
+// each candidate reproduces.
 #include <cuda_runtime_api.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -21,6 +28,7 @@
 #include <unistd.h>
 
 #include <cmath>
+#include <utility>
 #include <string>
 #include <vector>
 
@@ -152,6 +160,8 @@ struct Runner {
   }
 };
 
+int nvlsOrderStudy(struct Runner& R);
+
 int runRank(int rank, int P, const std::string& mode, const std::vector<tncclAlgo_t>& algosIn,
             tncclUniqueId id) {
   if (!cudaOk(cudaSetDevice(rank), rank, "cudaSetDevice")) return 1;
@@ -171,7 +181,9 @@ int runRank(int rank, int P, const std::string& mode, const std::vector<tncclAlg
     if (a != TNCCL_ALGO_NVLS || R.info.nvlsEnabled) algos.push_back(a);
   bool hard = false;
   uint64_t seed = 1;
-  if (mode == "stress") {
+  if (mode == "nvls_order") {
+    hard = nvlsOrderStudy(R) != 0;
+  } else if (mode == "stress") {
     for (int it = 0; it < 100 && !hard; ++it)
       hard = !R.run(Case{TNCCL_ALGO_AUTO, 0, 1048576, false, false, 0}, 1000 + (uint64_t)it);
   } else {
@@ -197,7 +209,7 @@ int runRank(int rank, int P, const std::string& mode, const std::vector<tncclAlg
     for (size_t n : {(size_t)0, (size_t)4096, (size_t)0, (size_t)3 << 20, (size_t)0})
       if (!hard) hard = !R.run(Case{TNCCL_ALGO_AUTO, 0, n, false, false, 0}, seed++);
   }
-  if (!hard && mode != "stress") {
+  if (!hard && mode != "stress" && mode != "nvls_order") {
     // Communication memory is constant: no device allocation grows with the
     // message (the buffers of this test are freed around the measurement),
     // and the guard lines after every mailbox area are intact.
@@ -235,6 +247,87 @@ int runRank(int rank, int P, const std::string& mode, const std::vector<tncclAlg
   cudaFree(R.drecv);
   cudaStreamDestroy(R.stream);
   return (hard || R.failures) ? 1 : 0;
+}
+
+// fp32 sums of P values in the candidate orders of the nvls_order study.
+float sumOrder(const std::vector<float>& v, const std::vector<int>& order) {
+  float a = v[(size_t)order[0]];
+  for (size_t i = 1; i < order.size(); ++i) a = oracle::add(a, v[(size_t)order[i]]);
+  return a;
+}
+float sumTree(const std::vector<float>& v, int lo, int hi) {
+  if (hi - lo == 1) return v[(size_t)lo];
+  const int mid = lo + (hi - lo + 1) / 2;
+  return oracle::add(sumTree(v, lo, mid), sumTree(v, mid, hi));
+}
+
+// Returns 0 when the NVLS results are stable run to run; prints the order study.
+int nvlsOrderStudy(Runner& R) {
+  const int P = R.P;
+  if (!R.info.nvlsEnabled) {
+    if (R.rank == 0) printf("nvls_order: NVLS not enabled on this communicator (skipped)\n");
+    return 0;
+  }
+  const size_t n = 1 << 20;
+  if (!R.ensure(n * 4 + 64)) return 1;
+  std::vector<std::vector<float>> x((size_t)P);
+  std::vector<unsigned char> raw, mine;
+  for (int r = 0; r < P; ++r) {
+    oracle::fillInput(oracle::kF32, 77, r, n, x[(size_t)r], raw);
+    // Spread the magnitudes so that different orders round differently.
+    for (size_t i = 0; i < n; ++i) x[(size_t)r][i] *= (float)(1u << ((i + (size_t)r * 7) % 23));
+    if (r == R.rank) {
+      mine.resize(n * 4);
+      memcpy(mine.data(), x[(size_t)r].data(), n * 4);
+    }
+  }
+  std::vector<float> first(n), got(n);
+  int unstable = 0;
+  for (int run = 0; run < 5; ++run) {
+    if (!cudaOk(cudaMemcpyAsync(R.dsend, mine.data(), n * 4, cudaMemcpyHostToDevice, R.stream),
+                R.rank, "H2D"))
+      return 1;
+    if (tncclAllReduceEx(R.dsend, R.drecv, n, tncclFloat32, tncclSum, 1.0f, TNCCL_ALGO_NVLS,
+                         R.comm, R.stream) != TNCCL_SUCCESS)
+      return 1;
+    if (!cudaOk(cudaMemcpyAsync(got.data(), R.drecv, n * 4, cudaMemcpyDeviceToHost, R.stream),
+                R.rank, "D2H") ||
+        !cudaOk(cudaStreamSynchronize(R.stream), R.rank, "sync"))
+      return 1;
+    if (run == 0)
+      first = got;
+    else if (memcmp(first.data(), got.data(), n * 4) != 0)
+      ++unstable;
+  }
+  std::vector<std::pair<std::string, std::vector<int>>> orders;
+  std::vector<int> seq((size_t)P);
+  for (int r = 0; r < P; ++r) seq[(size_t)r] = r;
+  orders.push_back({"rank order 0..P-1", seq});
+  orders.push_back({"reverse", std::vector<int>(seq.rbegin(), seq.rend())});
+  for (int k = 1; k < P; ++k) {
+    std::vector<int> rot((size_t)P);
+    for (int r = 0; r < P; ++r) rot[(size_t)r] = (k + r) % P;
+    orders.push_back({"rotation from rank " + std::to_string(k), rot});
+  }
+  std::vector<size_t> match(orders.size() + 1, 0);
+  std::vector<float> v((size_t)P);
+  for (size_t i = 0; i < n; ++i) {
+    for (int r = 0; r < P; ++r) v[(size_t)r] = x[(size_t)r][i];
+    for (size_t o = 0; o < orders.size(); ++o)
+      if (sumOrder(v, orders[o].second) == first[i]) ++match[o];
+    if (sumTree(v, 0, P) == first[i]) ++match[orders.size()];
+  }
+  if (R.rank == 0) {
+    printf("nvls_order: P=%d, %zu fp32 elements, runs bit-identical: %s\n", P, n,
+           unstable ? "NO" : "yes");
+    for (size_t o = 0; o < orders.size(); ++o)
+      printf("nvls_order:   %-26s matches %6.2f %%\n", orders[o].first.c_str(),
+             100.0 * (double)match[o] / (double)n);
+    printf("nvls_order:   %-26s matches %6.2f %%\n", "balanced pairwise tree",
+           100.0 * (double)match[orders.size()] / (double)n);
+    fflush(stdout);
+  }
+  return unstable ? 1 : 0;
 }
 
 }  // namespace

@@ -59,6 +59,43 @@ def test_two_rank_config2_stress(built):
     assert r.returncode == 0, r.stdout + r.stderr
 
 
+@pytest.mark.skipif(gpu_count() < 4, reason="needs 4 GPUs")
+@pytest.mark.parametrize("P", [4, 8])
+def test_multi_rank_bit_exact(built, P):
+    """Every algorithm on P ranks: counts 1 .. 1,048,581 across tile
+    boundaries, fp32 / bf16 / fp16, in and out of place, averaging,
+    misaligned buffers; ring, one-shot and two-shot bit for bit against the
+    order-aware oracle; constant communication memory; guard lines intact."""
+    if gpu_count() < P:
+        pytest.skip(f"needs {P} GPUs")
+    r = run([os.path.join(ROOT, "build", "bin", "allreduce_gpu_test"), str(P), "quick"],
+            timeout=900, env={"TNCCL_TIMEOUT_MS": "10000"})
+    assert r.returncode == 0, r.stdout + r.stderr[-4000:]
+
+
+@pytest.mark.skipif(gpu_count() < 4, reason="needs 4 GPUs")
+@pytest.mark.parametrize("P", [4, 8])
+def test_multi_rank_stress(built, P):
+    """100 consecutive checked all-reduces of 1,048,576 fp32 on one stream."""
+    if gpu_count() < P:
+        pytest.skip(f"needs {P} GPUs")
+    r = run([os.path.join(ROOT, "build", "bin", "allreduce_gpu_test"), str(P), "stress"],
+            timeout=900, env={"TNCCL_TIMEOUT_MS": "10000"})
+    assert r.returncode == 0, r.stdout + r.stderr[-4000:]
+
+
+@pytest.mark.skipif(gpu_count() < 2, reason="needs 2 GPUs")
+def test_nvls_summation_order_is_stable(built):
+    """The switch's fp32 reduction on all visible GPUs (up to 8): five runs
+    on the same inputs agree bit for bit; the printed study says which
+    candidate summation order reproduces the result."""
+    P = min(gpu_count(), 8)
+    r = run([os.path.join(ROOT, "build", "bin", "allreduce_gpu_test"), str(P), "nvls_order"],
+            timeout=600, env={"TNCCL_TIMEOUT_MS": "10000"})
+    assert r.returncode == 0, r.stdout + r.stderr[-4000:]
+    print(r.stdout)
+
+
 def test_bounded_wait_self_test(built):
     """A device wait on a word nothing writes gives up after its bound and
     reports TNCCL_TIMEOUT; the communicator then refuses collectives."""
