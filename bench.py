@@ -223,6 +223,8 @@ def reducer_desc() -> str:
             r += "+overlapped-adamw"
     if os.environ.get("TNCCL_NVLS_ZERO_COPY") == "1":
         r += "+nvls-zero-copy"
+    if os.environ.get("TNCCL_CUDA_GRAPH") == "1":
+        r += "+cuda-graph"
     return r
 
 

@@ -10,8 +10,8 @@
 // owns 256 columns (8 per lane, one 16-byte load per row) and every 8th row
 // of the block, 4 rows in flight; the 8 warp sums are added in warp order
 // into one fp32 partial per block. Pass 2 adds the partials of a column in
-// block order. The summation order depends only on (M, N), never on
-// scheduling. Rounding of the GELU gradient to bf16 happens before it is
+// block order (colReduce, common.cuh). The summation order depends only on
+// (M, N), never on scheduling. Rounding of the GELU gradient to bf16 happens before it is
 // summed, as when the gradient tensor is materialised and then reduced.
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -107,15 +107,6 @@ __global__ void __launch_bounds__(kWarps * 32)
   }
 }
 
-__global__ void colsumFinish(const float* __restrict__ partial, float* __restrict__ db, int nparts,
-                             int N) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= N) return;
-  float s = 0.f;
-  for (int k = 0; k < nparts; ++k) s += partial[(size_t)k * N + c];
-  db[c] = s;
-}
-
 }  // namespace
 }  // namespace tnops
 
@@ -139,7 +130,8 @@ static int launchColsum(const uint16_t* gy, const uint16_t* pre, uint16_t* gout,
     colsumPartial<true><<<grid, kWarps * 32, 0, stream>>>(gy, pre, gout, partial, M, N, rowsPer);
   else
     colsumPartial<false><<<grid, kWarps * 32, 0, stream>>>(gy, pre, gout, partial, M, N, rowsPer);
-  colsumFinish<<<(N + 255) / 256, 256, 0, stream>>>(partial, db, parts, N);
+  colReduce<<<(N + 31) / 32, kColReduceWarps * 32, 0, stream>>>(partial, parts, N, N, N, db,
+                                                                 nullptr);
   gLaunches.fetch_add(2, std::memory_order_relaxed);
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }

@@ -46,4 +46,47 @@ __device__ __forceinline__ float warpMax(float v) {
 
 constexpr int kSMs = 148;
 
+// Second pass of the deterministic column sums (bias gradients, LayerNorm
+// dweight / dbias): out[c] = sum over p of in[p * ld + c] for c < ncols,
+// written to out0[c] for c < split and to out1[c - split] above. A CTA of 32
+// warps owns 32 columns; warp w adds rows w, w + 32, w + 64, ... in row order
+// (eight independent loads in flight), then warp 0 adds the 32 warp sums in
+// warp order. The order depends only on nparts, never on scheduling, and the
+// short per-warp chains keep the pass from being latency-bound (a partial
+// count of 100-300 rows is common).
+constexpr int kColReduceWarps = 32;
+namespace {  // one copy per translation unit
+__global__ void __launch_bounds__(kColReduceWarps * 32)
+    colReduce(const float* __restrict__ in, int nparts, int ld, int ncols, int split,
+              float* __restrict__ out0, float* __restrict__ out1) {
+  __shared__ float s[kColReduceWarps][33];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int col = blockIdx.x * 32 + lane;
+  float acc = 0.f;
+  if (col < ncols) {
+    int p = warp;
+    constexpr int U = 8;
+    for (; p + (U - 1) * kColReduceWarps < nparts; p += U * kColReduceWarps) {
+      float v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) v[u] = in[(size_t)(p + u * kColReduceWarps) * ld + col];
+#pragma unroll
+      for (int u = 0; u < U; ++u) acc += v[u];
+    }
+    for (; p < nparts; p += kColReduceWarps) acc += in[(size_t)p * ld + col];
+  }
+  s[warp][lane] = acc;
+  __syncthreads();
+  if (warp == 0 && col < ncols) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < kColReduceWarps; ++w) t += s[w][lane];
+    if (col < split)
+      out0[col] = t;
+    else
+      out1[col - split] = t;
+  }
+}
+}  // namespace
+
 }  // namespace tnops

@@ -98,7 +98,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
 // each warp live in shared memory (one row of C floats per warp and
 // quantity), which leaves the registers to the loads in flight. Summation
 // order per column: the rows of each warp in row order, then the 8 warps in
-// warp order (here), then the CTAs in order (reducePartials).
+// warp order (here), then the CTAs in order (colReduce, common.cuh).
 template <int K>
 __global__ void __launch_bounds__(kWarpsPerBlock * 32, 2)
     lnBwdKernel(const uint16_t* __restrict__ gy, const float* __restrict__ gres,
@@ -196,31 +196,6 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, 2)
   }
 }
 
-// One CTA per 32 columns of [dw | db]: its 8 warps sum disjoint sets of
-// partial rows (coalesced 128-byte reads), then warp 0 adds the 8 warp sums
-// in a fixed order, so the result does not depend on scheduling.
-__global__ void __launch_bounds__(256)
-    reducePartials(const float* __restrict__ partial, float* __restrict__ dw,
-                   float* __restrict__ db, int nparts, int C) {
-  __shared__ float s[8][33];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int col = blockIdx.x * 32 + lane;
-  float acc = 0.f;
-  if (col < 2 * C)
-    for (int p = warp; p < nparts; p += 8) acc += partial[(size_t)p * 2 * C + col];
-  s[warp][lane] = acc;
-  __syncthreads();
-  if (warp == 0 && col < 2 * C) {
-    float t = 0.f;
-#pragma unroll
-    for (int w = 0; w < 8; ++w) t += s[w][lane];
-    if (col < C)
-      dw[col] = t;
-    else
-      db[col - C] = t;
-  }
-}
-
 template <int K>
 cudaError_t fwdK(const float* x, const uint16_t* d, const float* w, const float* b, float* xo,
                  uint16_t* y, float* m, float* r, int rows, int C, float eps, cudaStream_t st) {
@@ -294,7 +269,9 @@ extern "C" int tnops_ln_bwd(const uint16_t* gy, const float* g_res, const float*
   if (launched(e) != 0) return (int)e;
   int nparts = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock;
   if (nparts > kPartialRows) nparts = kPartialRows;
-  reducePartials<<<(2 * C + 31) / 32, 256, 0, stream>>>(partial, dw, db, nparts, C);
+  // dw = column sums of the first C partial columns, db of the next C.
+  colReduce<<<(2 * C + 31) / 32, kColReduceWarps * 32, 0, stream>>>(partial, nparts, 2 * C,
+                                                                    2 * C, C, dw, db);
   return launched(cudaGetLastError());
 }
 

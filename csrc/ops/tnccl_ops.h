@@ -70,6 +70,11 @@ typedef struct {
 
 int tnops_adamw(const tnops_adamw_list* list, float lr, float beta1, float beta2, float eps,
                 int64_t step, float grad_scale, cudaStream_t stream);
+// The same update with the step read from device memory (*step >= 1) when
+// the kernel runs: a launch captured in a CUDA graph then takes the step of
+// each replay (the caller advances the counter on the same stream).
+int tnops_adamw_dev(const tnops_adamw_list* list, float lr, float beta1, float beta2, float eps,
+                    const int64_t* step, float grad_scale, cudaStream_t stream);
 
 // bf16 GEMM on the tcgen05 tensor cores with a fused epilogue:
 // pre = bf16(x w^T + bias), and with `gelu` act = bf16(gelu_tanh(pre)).

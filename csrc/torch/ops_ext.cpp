@@ -167,7 +167,12 @@ void scaleBf16(at::Tensor x, const at::Tensor& scale) {
 void adamw(const std::vector<at::Tensor>& params, const std::vector<at::Tensor>& grads,
            const std::vector<at::Tensor>& m, const std::vector<at::Tensor>& v,
            const std::vector<double>& wd, double lr, double b1, double b2, double eps,
-           int64_t step, double gscale) {
+           int64_t step, double gscale, const c10::optional<at::Tensor>& stepDev) {
+  if (stepDev.has_value()) {
+    TORCH_CHECK(stepDev->is_cuda() && stepDev->scalar_type() == at::kLong &&
+                    stepDev->numel() == 1,
+                "adamw: step_tensor must be one int64 on the GPU");
+  }
   const size_t n = params.size();
   TORCH_CHECK(grads.size() == n && m.size() == n && v.size() == n && wd.size() == n,
               "adamw: list lengths differ");
@@ -190,8 +195,13 @@ void adamw(const std::vector<at::Tensor>& params, const std::vector<at::Tensor>&
       L.numel[i] = params[k].numel();
       L.weight_decay[i] = (float)wd[k];
     }
-    ok(tnops_adamw(&L, (float)lr, (float)b1, (float)b2, (float)eps, step, (float)gscale, st),
-       "tnops_adamw");
+    if (stepDev.has_value())
+      ok(tnops_adamw_dev(&L, (float)lr, (float)b1, (float)b2, (float)eps,
+                         stepDev->data_ptr<int64_t>(), (float)gscale, st),
+         "tnops_adamw_dev");
+    else
+      ok(tnops_adamw(&L, (float)lr, (float)b1, (float)b2, (float)eps, step, (float)gscale, st),
+         "tnops_adamw");
   }
 }
 
@@ -213,6 +223,9 @@ void registerOps(py::module_& m) {
   ops.def("tcgen05_status", [](bool reset) { return tnops_tcgen05_status(reset ? 1 : 0); },
           py::arg("reset") = false);
   ops.def("scale_bf16_", &scaleBf16);
-  ops.def("adamw", &adamw);
+  ops.def("adamw", &adamw, py::arg("params"), py::arg("grads"), py::arg("exp_avg"),
+          py::arg("exp_avg_sq"), py::arg("weight_decay"), py::arg("lr"), py::arg("beta1"),
+          py::arg("beta2"), py::arg("eps"), py::arg("step"), py::arg("grad_scale"),
+          py::arg("step_tensor") = py::none());
   ops.def("launch_count", []() { return tnops_launch_count(); });
 }

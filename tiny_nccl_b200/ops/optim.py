@@ -17,6 +17,11 @@ class AdamW(torch.optim.Optimizer):
         defaults = dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay)
         super().__init__(params, defaults)
         self._step = 0
+        # With device_step, the step count also lives in device memory and the
+        # kernel reads it when it runs, so a step captured in a CUDA graph
+        # uses the right bias correction on every replay.
+        self.device_step = False
+        self._step_t = None
 
     @torch.no_grad()
     def step(self, closure=None):
@@ -29,6 +34,18 @@ class AdamW(torch.optim.Optimizer):
         """Advances the step count (bias correction) of a step whose update is
         applied in parts with :meth:`step_params`."""
         self._step += 1
+        if self.device_step:
+            if self._step_t is None:
+                dev = self.param_groups[0]["params"][0].device
+                self._step_t = torch.full((1,), self._step, dtype=torch.int64, device=dev)
+            else:
+                self._step_t.add_(1)
+
+    def set_step(self, n: int) -> None:
+        """Sets the number of completed steps (e.g. from a checkpoint)."""
+        self._step = int(n)
+        if self._step_t is not None:
+            self._step_t.fill_(self._step)
 
     @torch.no_grad()
     def step_params(self, only=None) -> None:
@@ -55,7 +72,8 @@ class AdamW(torch.optim.Optimizer):
             if ps:
                 b1, b2 = group["betas"]
                 ops.adamw(ps, gs, ms, vs, wds, float(group["lr"]), float(b1), float(b2),
-                          float(group["eps"]), self._step, 1.0)
+                          float(group["eps"]), self._step, 1.0,
+                          self._step_t if self.device_step else None)
 
 
 def gpt2_param_groups(model: torch.nn.Module, weight_decay: float = 0.1):

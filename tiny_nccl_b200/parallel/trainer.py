@@ -9,7 +9,15 @@ registered with the communicator, for the zero-copy NVLS all-reduce
 (``TNCCL_NVLS_ZERO_COPY=1``), and with ``overlap_optimizer=True``
 (``TNCCL_DP_OVERLAP_OPT=1``) AdamW updates each bucket's parameters on the
 communication stream as soon as its all-reduce is enqueued, overlapping the
-optimizer with the rest of backward. Opt-in: not yet run on a GPU.
+optimizer with the rest of backward.
+
+``cuda_graph=True`` (or ``TNCCL_CUDA_GRAPH=1``; needs the flat reducer)
+captures the whole training step (forward, backward with its bucket
+all-reduces on the side stream, optimizer, gradient zeroing) in one CUDA
+graph after three eager warm-up steps, and replays it for every later step:
+the ~600 kernel launches of a GPT-2 small step then cost one graph launch
+instead of the host time of the eager step. Inputs are copied into static
+buffers first; the optimizer reads its step count from device memory.
 """
 from __future__ import annotations
 
@@ -31,7 +39,7 @@ class DataParallelTrainer:
                  algo: str = "auto", wire_dtype: torch.dtype | None = None,
                  amp_dtype: torch.dtype = torch.bfloat16, max_channels: int | None = None,
                  reducer: str | None = None, registered: bool | None = None,
-                 overlap_optimizer: bool | None = None):
+                 overlap_optimizer: bool | None = None, cuda_graph: bool | None = None):
         if not dist.is_initialized():
             raise RuntimeError("DataParallelTrainer needs torch.distributed initialised")
         self.comm = comm
@@ -49,8 +57,18 @@ class DataParallelTrainer:
             registered = os.environ.get("TNCCL_DP_REGISTERED", "0") == "1"
         if overlap_optimizer is None:
             overlap_optimizer = os.environ.get("TNCCL_DP_OVERLAP_OPT", "0") == "1"
+        if cuda_graph is None:
+            cuda_graph = os.environ.get("TNCCL_CUDA_GRAPH", "0") == "1"
+        if cuda_graph and reducer != "flat":
+            raise ValueError("cuda_graph needs reducer='flat' (DDP's reducer runs host "
+                             "logic during backward that a graph replay would skip)")
+        self.cuda_graph = cuda_graph
+        self._graph = None
+        self._eager_steps = 0
+        self._graph_stream = torch.cuda.Stream(device=dev) if cuda_graph else None
         self.overlap_optimizer = overlap_optimizer and reducer == "flat"
         self.opt = AdamW(gpt2_param_groups(model, weight_decay), lr=lr, betas=betas)
+        self.opt.device_step = cuda_graph
         self.reducer = None
         self.registration = None
         if reducer == "flat":
@@ -83,9 +101,40 @@ class DataParallelTrainer:
 
     def step(self, idx: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
         """One optimizer step; returns the (device) loss without synchronizing."""
+        if not self.cuda_graph:
+            return self._step_eager(idx, targets)
+        cur = torch.cuda.current_stream(idx.device)
+        if self._graph is None and self._eager_steps < 3:
+            # Warm-up outside the capture (kernel loading, cuBLAS / cuDNN
+            # plans, optimizer state), on the stream the capture will use.
+            self._eager_steps += 1
+            self._graph_stream.wait_stream(cur)
+            with torch.cuda.stream(self._graph_stream):
+                loss = self._step_eager(idx, targets)
+            cur.wait_stream(self._graph_stream)
+            return loss
+        if self._graph is None:
+            self._capture(idx, targets)
+        self._static_idx.copy_(idx)
+        self._static_tgt.copy_(targets)
+        self._graph.replay()
+        return self._static_loss.clone()
+
+    def _capture(self, idx: torch.Tensor, targets: torch.Tensor) -> None:
+        self._static_idx = idx.clone()
+        self._static_tgt = targets.clone()
+        torch.cuda.synchronize(idx.device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=self._graph_stream):
+            self._static_loss = self._step_eager(self._static_idx, self._static_tgt)
+        self._graph = graph
+
+    def _step_eager(self, idx: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
         if self.overlap_optimizer:
             self.opt.begin_step()  # the buckets' hooks apply it during backward
-        with torch.autocast("cuda", dtype=self.amp_dtype):
+        # Autocast's weight-cast cache is off under graph capture: cached
+        # casts would be freed at the end of the region inside the capture.
+        with torch.autocast("cuda", dtype=self.amp_dtype, cache_enabled=not self.cuda_graph):
             loss = self.ddp(idx, targets)
         loss.backward()
         if self.reducer is not None:
@@ -101,6 +150,9 @@ class DataParallelTrainer:
     def close(self) -> None:
         """Deregisters the flat gradient buffer (collective); call before the
         communicator is destroyed."""
+        if self._graph is not None:
+            torch.cuda.synchronize()
+            self._graph = None  # releases the captured collectives' graph
         if self.registration is not None:
             self.comm.deregister(self.registration)
             self.registration = None
@@ -112,4 +164,4 @@ class DataParallelTrainer:
     def load_state_dict(self, sd: dict) -> None:
         self.model.load_state_dict(sd["model"])
         self.opt.load_state_dict(sd["opt"])
-        self.opt._step = sd["step"]
+        self.opt.set_step(sd["step"])
