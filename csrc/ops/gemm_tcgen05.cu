@@ -14,9 +14,12 @@
 //              tcgen05.mma 128x256x16 per K block, then tcgen05.commit to the
 //              stage's "empty" barrier (the stage is free once those MMAs have
 //              read it) and, after the last block, to the accumulator barrier;
-//   warps 2-5  wait for the accumulator, read it with tcgen05.ld (warp w owns
-//              TMEM lanes 32 (w % 4) .. +31, i.e. those output rows), add the
-//              bias, apply GELU, round to bf16 and store.
+//   warps 2-9  wait for the accumulator, read it with tcgen05.ld (warp w owns
+//              TMEM lanes 32 (w % 4) .. +31, i.e. those output rows; warps
+//              2-5 take columns 0-127 of the tile, warps 6-9 columns
+//              128-255), add the bias, apply GELU, round to bf16 and store.
+//              Eight epilogue warps, two per SM sub-partition, keep the
+//              epilogue of a tile shorter than the main loop of the next.
 // Operands are K-major in shared memory, rows of 128 bytes in 8-row swizzle
 // atoms of 1024 bytes: the UMMA descriptor holds the start address, a
 // leading offset of 16 bytes and an 8-row stride of 1024 bytes, layout
@@ -44,7 +47,8 @@ constexpr int kBM = 128;
 constexpr int kBN = 256;
 constexpr int kBK = 64;  // bf16: 128 bytes, one swizzle row
 constexpr int kStages = 4;
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;  // two per TMEM lane quarter
+constexpr int kThreads = 64 + kEpiWarps * 32;
 constexpr uint32_t kTmemCols = 256;
 constexpr uint32_t kStageA = kBM * kBK * 2;  // 16 KiB
 constexpr uint32_t kStageB = kBN * kBK * 2;  // 32 KiB
@@ -162,38 +166,55 @@ __device__ __forceinline__ void tmemLoad32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// tanh-GELU, 0.5 x (1 + tanh(k0 (x + k1 x^3))) = x (0.5 + 0.5 tanh(u)), with
+// the hardware tanh approximation (PTX tanh.approx.f32, relative error about
+// 2^-11, well below the bf16 rounding of the result).
+__device__ __forceinline__ float tanhApprox(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ float geluTanh(float x) {
   const float k0 = 0.7978845608028654f;  // sqrt(2 / pi)
-  const float k1 = 0.044715f;
-  return 0.5f * x * (1.0f + tanhf(k0 * (x + k1 * x * x * x)));
+  const float k0k1 = 0.7978845608028654f * 0.044715f;
+  const float u = x * fmaf(k0k1, x * x, k0);
+  return x * fmaf(0.5f, tanhApprox(u), 0.5f);
+}
+__device__ __forceinline__ uint32_t packBf16(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Epilogue of 32 accumulator columns of one row: bias, rounding to bf16,
+// Epilogue of 32 accumulator columns of one row: bias (the same 32 values
+// for every lane, loaded as four broadcast 16-byte reads), rounding to bf16,
 // GELU of the rounded value, 16-byte stores of pre and act.
 template <bool GELU>
 __device__ __forceinline__ void storeChunk(const float (&v)[32], int row, int col0, int M, int N,
                                            const uint16_t* __restrict__ bias,
                                            uint16_t* __restrict__ pre,
                                            uint16_t* __restrict__ act) {
-  if (row >= M || col0 >= N) return;
+  if (col0 >= N) return;
+  uint4 bb[4] = {};
+  if (bias) {
+#pragma unroll
+    for (int g = 0; g < 4; ++g)
+      if (col0 + g * 8 < N) bb[g] = __ldg(reinterpret_cast<const uint4*>(bias + col0) + g);
+  }
+  if (row >= M) return;
 #pragma unroll
   for (int g = 0; g < 4; ++g) {
     const int col = col0 + g * 8;
     if (col >= N) break;  // N % 8 == 0: a vector is all in or all out
+    const uint32_t bw[4] = {bb[g].x, bb[g].y, bb[g].z, bb[g].w};
     uint32_t pw[4], aw[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      float x0 = v[g * 8 + 2 * i], x1 = v[g * 8 + 2 * i + 1];
-      if (bias) {
-        x0 += bf2f(bias[col + 2 * i]);
-        x1 += bf2f(bias[col + 2 * i + 1]);
-      }
-      const uint16_t p0 = f2bf(x0), p1 = f2bf(x1);
-      pw[i] = (uint32_t)p0 | ((uint32_t)p1 << 16);
-      if (GELU) {
-        const uint16_t a0 = f2bf(geluTanh(bf2f(p0))), a1 = f2bf(geluTanh(bf2f(p1)));
-        aw[i] = (uint32_t)a0 | ((uint32_t)a1 << 16);
-      }
+      const float x0 = v[g * 8 + 2 * i] + __uint_as_float(bw[i] << 16);
+      const float x1 = v[g * 8 + 2 * i + 1] + __uint_as_float(bw[i] & 0xffff0000u);
+      pw[i] = packBf16(x0, x1);
+      if (GELU)
+        aw[i] = packBf16(geluTanh(__uint_as_float(pw[i] << 16)),
+                         geluTanh(__uint_as_float(pw[i] & 0xffff0000u)));
     }
     const size_t off = (size_t)row * N + col;
     if (pre) *reinterpret_cast<uint4*>(pre + off) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
@@ -275,8 +296,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     commit(&sAccum);  // also after an abort: the MMAs issued so far
     if (*abort) mbarWait(&sAccum, 0, abort, 5, true);
   } else if (warp >= 2) {
-    // Epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 = tile rows.
+    // Epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 = tile rows, in
+    // the column half (warp - 2) / 4.
     const int quarter = warp & 3;
+    const int c0 = ((warp - 2) >> 2) * (kBN / 2);
     const int row = m0 + quarter * 32 + lane;
     // tcgen05.ld is warp-collective: the whole warp proceeds only if every
     // lane saw the accumulator complete.
@@ -284,7 +307,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (__all_sync(0xffffffffu, ready)) {
       fenceAfterSync();
 #pragma unroll 1
-      for (int c = 0; c < kBN; c += 32) {
+      for (int c = c0; c < c0 + kBN / 2; c += 32) {
         float v[32];
         tmemLoad32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c, v);
         storeChunk<GELU>(v, row, n0 + c, M, N, bias, pre, act);
@@ -344,7 +367,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbarInit(&sAccFull[b], 1);
-      mbarInit(&sAccEmpty[b], 4);  // the four epilogue warps
+      mbarInit(&sAccEmpty[b], kEpiWarps);  // one arrival per epilogue warp
     }
     mbarInit(&sDone, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -402,8 +425,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     commit(&sDone);  // every MMA issued so far
     if (*abort) mbarWait(&sDone, 0, abort, 5, true);
   } else if (warp >= 2) {
-    // Epilogue.
+    // Epilogue: TMEM lane quarter warp % 4, column half (warp - 2) / 4.
     const int quarter = warp & 3;
+    const int c0 = ((warp - 2) >> 2) * (kBN / 2);
     uint32_t local = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++local) {
       const uint32_t b = local & 1u, use = local >> 1;
@@ -414,10 +438,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row = m0 + quarter * 32 + lane;
       const uint32_t acc = tmem + b * kTmemCols + ((uint32_t)(quarter * 32) << 16);
 #pragma unroll 1
-      for (int c = 0; c < kBN; c += 32) {
+      for (int c = c0; c < c0 + kBN / 2; c += 32) {
         float v[32];
         tmemLoad32(acc + (uint32_t)c, v);
-        if (c + 32 == kBN) {
+        if (c + 32 == c0 + kBN / 2) {
           // Last read of this buffer: hand it back before the stores.
           fenceBeforeSync();
           __syncwarp();

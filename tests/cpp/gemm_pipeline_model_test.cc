@@ -3,7 +3,7 @@
 // the persistent kernel with two TMEM accumulators.
 //
 // The roles run as threads with the kernels' loop structure and parity
-// formulas: the TMA producer, the MMA issuer and four epilogue warps. An
+// formulas: the TMA producer, the MMA issuer and eight epilogue warps. An
 // mbarrier is modelled with the PTX semantics the kernels rely on (a pending
 // arrival count and a transaction count; a phase completes when both reach
 // zero; try_wait.parity(p) succeeds once the phase with parity p completed,
@@ -139,6 +139,7 @@ struct Engine {
 };
 
 constexpr int kStages = 4;
+constexpr int kEpiWarps = 8;  // two per TMEM lane quarter, one column half each
 
 struct Result {
   bool ok = true;
@@ -157,7 +158,7 @@ Result runPersistent(int tiles, int kBlocks, int seed, int stopAt = -1) {
   }
   for (int b = 0; b < 2; ++b) {
     accFull[b].init(1);
-    accEmpty[b].init(4);
+    accEmpty[b].init(kEpiWarps);
   }
   done.init(1);
   std::atomic<int> abort{0};
@@ -226,15 +227,15 @@ Result runPersistent(int tiles, int kBlocks, int seed, int stopAt = -1) {
       if (abort.load()) waitBar(done, 0, abort, true);
     });
     std::vector<std::thread> epi;
-    for (int w = 0; w < 4; ++w) {
+    for (int w = 0; w < kEpiWarps; ++w) {
       epi.emplace_back([&, w] {
         std::mt19937 g((unsigned)(seed * 13 + w));
         unsigned local = 0;
         for (int t = 0; t < tiles; ++t, ++local) {
           const unsigned b = local & 1u, use = local >> 1;
           if (!waitBar(accFull[b], use & 1u, abort)) break;
-          // The eight tcgen05.ld of this warp's rows.
-          for (int c = 0; c < 8; ++c) {
+          // The four tcgen05.ld of this warp's rows and column half.
+          for (int c = 0; c < 4; ++c) {
             if (accTile[b].load() != t || accBlocks[b].load() != kBlocks) bad = true;
             jitter(g, 3);
           }
@@ -299,7 +300,7 @@ Result runSingle(int kBlocks, int seed) {
       mmaUnit.push([&] { accum.arrive(); });
     });
     std::vector<std::thread> epi;
-    for (int w = 0; w < 4; ++w)
+    for (int w = 0; w < kEpiWarps; ++w)
       epi.emplace_back([&] {
         if (!waitBar(accum, 0, abort)) return;
         if (blocks.load() != kBlocks) bad = true;
@@ -310,7 +311,7 @@ Result runSingle(int kBlocks, int seed) {
     for (auto& th : epi) th.join();
     res.aborted = abort.load() != 0;
   }
-  res.stored = storedWarps.load() == 4 ? 1 : 0;
+  res.stored = storedWarps.load() == kEpiWarps ? 1 : 0;
   res.ok = !bad.load();
   return res;
 }
