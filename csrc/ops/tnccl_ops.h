@@ -66,6 +66,9 @@ typedef struct {
   float* exp_avg_sq[64];
   int64_t numel[64];
   float weight_decay[64];
+  // Optional (null entries skip it): a bf16 copy of each updated parameter,
+  // written in the same pass, for the next forward's bf16 GEMMs.
+  uint16_t* param_bf16[64];
 } tnops_adamw_list;
 
 int tnops_adamw(const tnops_adamw_list* list, float lr, float beta1, float beta2, float eps,

@@ -167,7 +167,10 @@ void scaleBf16(at::Tensor x, const at::Tensor& scale) {
 void adamw(const std::vector<at::Tensor>& params, const std::vector<at::Tensor>& grads,
            const std::vector<at::Tensor>& m, const std::vector<at::Tensor>& v,
            const std::vector<double>& wd, double lr, double b1, double b2, double eps,
-           int64_t step, double gscale, const c10::optional<at::Tensor>& stepDev) {
+           int64_t step, double gscale, const c10::optional<at::Tensor>& stepDev,
+           const std::vector<at::Tensor>& bf16Copies) {
+  TORCH_CHECK(bf16Copies.empty() || bf16Copies.size() == params.size(),
+              "adamw: param_bf16 must be empty or one tensor per parameter");
   if (stepDev.has_value()) {
     TORCH_CHECK(stepDev->is_cuda() && stepDev->scalar_type() == at::kLong &&
                     stepDev->numel() == 1,
@@ -194,6 +197,13 @@ void adamw(const std::vector<at::Tensor>& params, const std::vector<at::Tensor>&
       L.exp_avg_sq[i] = v[k].data_ptr<float>();
       L.numel[i] = params[k].numel();
       L.weight_decay[i] = (float)wd[k];
+      if (!bf16Copies.empty()) {
+        const at::Tensor& c = bf16Copies[k];
+        TORCH_CHECK(c.scalar_type() == at::kBFloat16 && c.is_contiguous() &&
+                        c.numel() == params[k].numel() && c.device() == params[k].device(),
+                    "adamw: param_bf16 must be contiguous bf16 of the parameter's size");
+        L.param_bf16[i] = reinterpret_cast<uint16_t*>(c.data_ptr());
+      }
     }
     if (stepDev.has_value())
       ok(tnops_adamw_dev(&L, (float)lr, (float)b1, (float)b2, (float)eps,
@@ -226,6 +236,7 @@ void registerOps(py::module_& m) {
   ops.def("adamw", &adamw, py::arg("params"), py::arg("grads"), py::arg("exp_avg"),
           py::arg("exp_avg_sq"), py::arg("weight_decay"), py::arg("lr"), py::arg("beta1"),
           py::arg("beta2"), py::arg("eps"), py::arg("step"), py::arg("grad_scale"),
-          py::arg("step_tensor") = py::none());
+          py::arg("step_tensor") = py::none(),
+          py::arg("param_bf16") = std::vector<at::Tensor>());
   ops.def("launch_count", []() { return tnops_launch_count(); });
 }

@@ -167,6 +167,7 @@ class GPT2(nn.Module):
             nxt = self.blocks[i + 1].ln_1 if i + 1 < L else self.ln_f
             x, h = ops.add_layer_norm(x, m, nxt.weight, nxt.bias)
         if targets is None:
-            return F.linear(h.view(B, T, C)[:, -1], self.wte.weight)[..., :self.cfg.vocab_size]
-        logits = F.linear(h, self.wte.weight)
+            last = h.view(B, T, C)[:, -1]
+            return ops.linear_nobias(last, self.wte.weight)[..., :self.cfg.vocab_size]
+        logits = ops.linear_nobias(h, self.wte.weight)
         return ops.cross_entropy(logits, targets.reshape(-1), classes=self.cfg.vocab_size)

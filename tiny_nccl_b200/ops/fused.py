@@ -97,6 +97,16 @@ def cross_entropy(logits: torch.Tensor, target: torch.Tensor,
     return _CrossEntropy.apply(logits.contiguous(), target.contiguous(), int(classes))
 
 
+def bf16_weight(p: torch.Tensor) -> torch.Tensor:
+    """The bf16 value of an fp32 parameter for a GEMM operand: the copy the
+    fused AdamW wrote in its last update while it is current (the
+    parameter's version unchanged since), else a cast."""
+    c = getattr(p, "_tn_bf16", None)
+    if c is not None and c[1] == p._version:
+        return c[0]
+    return p.to(torch.bfloat16)
+
+
 def _wgrad(gy: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
     """dW = gy^T x with bf16 operands and the fp32 result written by the GEMM
     itself (no bf16 rounding, no separate cast to the fp32 parameter)."""
@@ -110,9 +120,9 @@ class _LinearBias(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, x, weight, bias):
-        w16 = weight.to(torch.bfloat16)
+        w16 = bf16_weight(weight)
         with torch.autocast("cuda", enabled=False):
-            y = torch.addmm(bias.to(torch.bfloat16), x, w16.t())
+            y = torch.addmm(bf16_weight(bias), x, w16.t())
         ctx.save_for_backward(x, w16)
         return y
 
@@ -136,8 +146,8 @@ class _LinearGelu(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, x, weight, bias):
-        w16 = weight.to(torch.bfloat16)
-        b16 = bias.to(torch.bfloat16)
+        w16 = bf16_weight(weight)
+        b16 = bf16_weight(bias)
         if _TCGEN05 != "0":
             pre, y = _ops().gemm_bias_act(x, w16, b16, True, _TCGEN05 == "persistent")
         else:
@@ -154,6 +164,25 @@ class _LinearGelu(torch.autograd.Function):
         return gpre @ w16, _wgrad(gpre, x), db
 
 
+class _LinearNoBias(torch.autograd.Function):
+    """y = x W^T in bf16 for an fp32 weight (the tied LM head): dX on cuBLAS,
+    dW written in fp32 by the GEMM itself."""
+
+    @staticmethod
+    def forward(ctx, x, weight):
+        w16 = bf16_weight(weight)
+        with torch.autocast("cuda", enabled=False):
+            y = torch.mm(x, w16.t())
+        ctx.save_for_backward(x, w16)
+        return y
+
+    @staticmethod
+    def backward(ctx, gy):
+        x, w16 = ctx.saved_tensors
+        gy = gy.contiguous()
+        return gy @ w16, _wgrad(gy, x)
+
+
 def _rows(x: torch.Tensor) -> torch.Tensor:
     x = x.reshape(-1, x.shape[-1])
     return (x if x.dtype == torch.bfloat16 else x.to(torch.bfloat16)).contiguous()
@@ -162,6 +191,12 @@ def _rows(x: torch.Tensor) -> torch.Tensor:
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
     """bf16 x W^T + b over the last dimension of x (fp32 weight and bias)."""
     y = _LinearBias.apply(_rows(x), weight, bias)
+    return y.view(*x.shape[:-1], weight.shape[0])
+
+
+def linear_nobias(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    """bf16 x W^T over the last dimension of x (fp32 weight, no bias)."""
+    y = _LinearNoBias.apply(_rows(x), weight)
     return y.view(*x.shape[:-1], weight.shape[0])
 
 

@@ -22,6 +22,11 @@ class AdamW(torch.optim.Optimizer):
         # uses the right bias correction on every replay.
         self.device_step = False
         self._step_t = None
+        # With bf16_copies, every update also writes a bf16 copy of the
+        # parameter (same kernel pass); the fused linear layers use it instead
+        # of casting the fp32 parameter again in the next forward
+        # (tiny_nccl_b200.ops.fused.bf16_weight).
+        self.bf16_copies = False
 
     @torch.no_grad()
     def step(self, closure=None):
@@ -56,7 +61,7 @@ class AdamW(torch.optim.Optimizer):
         ops = load().ops
         sel = None if only is None else {id(p) for p in only}
         for group in self.param_groups:
-            ps, gs, ms, vs, wds = [], [], [], [], []
+            ps, gs, ms, vs, wds, cs = [], [], [], [], [], []
             for p in group["params"]:
                 if p.grad is None or (sel is not None and id(p) not in sel):
                     continue
@@ -64,7 +69,11 @@ class AdamW(torch.optim.Optimizer):
                 if not st:
                     st["exp_avg"] = torch.zeros_like(p, memory_format=torch.contiguous_format)
                     st["exp_avg_sq"] = torch.zeros_like(p, memory_format=torch.contiguous_format)
+                if self.bf16_copies and "bf16" not in st:
+                    st["bf16"] = torch.empty(p.shape, dtype=torch.bfloat16, device=p.device)
                 ps.append(p)
+                if self.bf16_copies:
+                    cs.append(st["bf16"])
                 gs.append(p.grad if p.grad.is_contiguous() else p.grad.contiguous())
                 ms.append(st["exp_avg"])
                 vs.append(st["exp_avg_sq"])
@@ -73,7 +82,13 @@ class AdamW(torch.optim.Optimizer):
                 b1, b2 = group["betas"]
                 ops.adamw(ps, gs, ms, vs, wds, float(group["lr"]), float(b1), float(b2),
                           float(group["eps"]), self._step, 1.0,
-                          self._step_t if self.device_step else None)
+                          self._step_t if self.device_step else None, cs)
+                # The kernel writes through raw pointers, so the parameter's
+                # version counter stays put: a copy is current as long as the
+                # version is the one recorded here (any other in-place change
+                # of the parameter moves it on and retires the copy).
+                for p, c in zip(ps, cs):
+                    p._tn_bf16 = (c, p._version)
 
 
 def gpt2_param_groups(model: torch.nn.Module, weight_decay: float = 0.1):

@@ -69,6 +69,8 @@ class DataParallelTrainer:
         self.overlap_optimizer = overlap_optimizer and reducer == "flat"
         self.opt = AdamW(gpt2_param_groups(model, weight_decay), lr=lr, betas=betas)
         self.opt.device_step = cuda_graph
+        # AdamW also writes the bf16 copies the next forward's GEMMs read.
+        self.opt.bf16_copies = True
         self.reducer = None
         self.registration = None
         if reducer == "flat":
