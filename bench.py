@@ -203,7 +203,9 @@ def build_tnccl_trainer(args, rank, world, dev):
     trainer = DataParallelTrainer(model, comm, algo=args.algo)
 
     def launches():
-        return tn.launch_count() + tn.load().ops.launch_count()
+        # API launches, plus this library's kernel nodes that CUDA-graph
+        # replays of the training step launched.
+        return tn.launch_count() + tn.load().ops.launch_count() + trainer.replayed_launches
 
     def close():
         torch.cuda.synchronize()

@@ -261,6 +261,12 @@ __global__ void __launch_bounds__(kMaxThreads)
     }
   }
   traceMark(comm, c, kCounterNvlsZc, 2, seq0);
+  // The stores went to the recv buffers' multicast object, the barrier
+  // counters live in the communicator's: a release on the counter does not
+  // order stores to another multicast object, so every thread waits for its
+  // own stores to be performed at system scope before the CTA counts
+  // "stored".
+  __threadfence_system();
   if (!barrier(1)) return;
   traceMark(comm, c, kCounterNvlsZc, 3, seq0);
   if (threadIdx.x == 0) comm.counters[kCounterNvlsZc * kMaxChannels + c] = seq0 + 1;

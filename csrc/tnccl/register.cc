@@ -56,15 +56,20 @@ bool multicastApi(const DriverApi* api) {
          api->cuMulticastBindMem && api->cuMulticastUnbind && api->cuMulticastGetGranularity;
 }
 
-// Minimum multicast granularity for `numDevices` devices (0 if unknown).
-size_t multicastGranularity(const DriverApi* api, unsigned numDevices, size_t bytes) {
+// Minimum (or, with recommended, the driver's recommended) multicast
+// granularity for `numDevices` devices (0 if unknown).
+size_t multicastGranularity(const DriverApi* api, unsigned numDevices, size_t bytes,
+                            bool recommended = false) {
   if (!multicastApi(api)) return 0;
   CUmulticastObjectProp mp{};
   mp.numDevices = numDevices;
   mp.handleTypes = CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR;
   mp.size = bytes;
   size_t g = 0;
-  if (api->cuMulticastGetGranularity(&g, &mp, CU_MULTICAST_GRANULARITY_MINIMUM) != CUDA_SUCCESS)
+  if (api->cuMulticastGetGranularity(&g, &mp,
+                                     recommended ? CU_MULTICAST_GRANULARITY_RECOMMENDED
+                                                 : CU_MULTICAST_GRANULARITY_MINIMUM) !=
+      CUDA_SUCCESS)
     return 0;
   return g;
 }
@@ -345,8 +350,9 @@ extern "C" tncclResult tncclCommRegister(tncclComm_t comm, void* buff, size_t si
     return b != TNCCL_SUCCESS ? b : r;
   }
   *handle = &g;
-  TN_INFO("rank %d: registered %zu bytes at %p for zero-copy NVLS (%zu bound)", comm->rank, size,
-          buff, bytes);
+  TN_INFO("rank %d: registered %zu bytes at %p for zero-copy NVLS (%zu bound; multicast "
+          "granularity %zu, recommended %zu)", comm->rank, size, buff, bytes, gran,
+          multicastGranularity(api, (unsigned)comm->nranks, size, true));
   return TNCCL_SUCCESS;
 }
 

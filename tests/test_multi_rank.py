@@ -57,6 +57,17 @@ def test_bounded_wait_timeout_two_ranks(built):
 
 @pytest.mark.gpu
 @pytest.mark.skipif(gpu_count() < 2, reason="needs 2 GPUs")
+def test_graph_trainer_matches_ddp(built):
+    """Flat gradient buffer + whole-step CUDA graph on 2 ranks against the
+    eager DDP + tnccl hook trainer (NVLS off: the bucket all-reduces take the
+    peer-memory kernels)."""
+    r = torchrun(2, ["tests/workers/graph_trainer_worker.py"], timeout=600,
+                 env={"TNCCL_TIMEOUT_MS": "10000"})
+    assert r.returncode == 0 and "PASS" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(gpu_count() < 2, reason="needs 2 GPUs")
 @pytest.mark.skipif(os.environ.get("TNCCL_TEST_NVLS_ZC") != "1",
                     reason="zero-copy NVLS has not run on a GPU yet: TNCCL_TEST_NVLS_ZC=1")
 def test_nvls_zero_copy_registered_buffers(built):

@@ -66,8 +66,14 @@ def main():
                     good = torch.equal(got, want)
                 if not good:
                     ok = False
-                    diff = (got.float() - want.float()).abs().max().item()
-                    print(f"rank {rank}: {dtype} n={n} it={it} max diff {diff}", flush=True)
+                    d = (got.float() - want.float()).abs()
+                    bad = (d > (1e-2 if avg else 0)).nonzero().flatten()
+                    i0, i1 = int(bad[0]), int(bad[-1])
+                    half = (n + world - 1) // world  # rank r reduces about [r*half, (r+1)*half)
+                    print(f"rank {rank}: {dtype} n={n} it={it} inplace={it % 2} avg={avg} "
+                          f"max diff {d.max().item()} bad {bad.numel()} first {i0} last {i1} "
+                          f"(shards of ~{half}) got {got[i0].item()} want {want[i0].item()} "
+                          f"x {src[i0].item()}", flush=True)
             comm.deregister(hx)
             live.append((hy, y))
     for h, _ in live:

@@ -65,6 +65,8 @@ class DataParallelTrainer:
         self.cuda_graph = cuda_graph
         self._graph = None
         self._eager_steps = 0
+        self._graph_kernels = 0  # this library's kernels in the captured step
+        self.replayed_launches = 0  # of those, launched by graph replays so far
         self._graph_stream = torch.cuda.Stream(device=dev) if cuda_graph else None
         self.overlap_optimizer = overlap_optimizer and reducer == "flat"
         self.opt = AdamW(gpt2_param_groups(model, weight_decay), lr=lr, betas=betas)
@@ -120,15 +122,22 @@ class DataParallelTrainer:
         self._static_idx.copy_(idx)
         self._static_tgt.copy_(targets)
         self._graph.replay()
+        self.replayed_launches += self._graph_kernels
         return self._static_loss.clone()
 
     def _capture(self, idx: torch.Tensor, targets: torch.Tensor) -> None:
         self._static_idx = idx.clone()
         self._static_tgt = targets.clone()
         torch.cuda.synchronize(idx.device)
+        from .. import launch_count
+        from .._native import load
+        before = launch_count() + load().ops.launch_count()
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=self._graph_stream):
             self._static_loss = self._step_eager(self._static_idx, self._static_tgt)
+        # Every launch through the library during the capture is a kernel
+        # node of the graph, launched again by each replay.
+        self._graph_kernels = launch_count() + load().ops.launch_count() - before
         self._graph = graph
 
     def _step_eager(self, idx: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
