@@ -11,8 +11,12 @@ random initialisation, synthetic token ids Uniform[0, 50257) seeded per rank.
 Weak scaling: every GPU processes 8 x 1024 tokens per step.
 
 --impl tnccl (default): the framework's GPT-2 (fused sm_100a LayerNorm /
-  cross-entropy / AdamW kernels) under DistributedDataParallel with the tnccl
-  comm hook (gradient buckets all-reduced by tnccl kernels over NVLink).
+  cross-entropy / AdamW kernels) in DataParallelTrainer: gradients in one
+  flat buffer whose ~25 MB buckets are all-reduced by tnccl kernels over
+  NVLink on a side stream as backward produces them, and the whole step
+  (forward, backward with those all-reduces, AdamW) captured once in a CUDA
+  graph and replayed (TNCCL_DP_REDUCER=ddp: DDP with the tnccl comm hook,
+  eager).
 --impl reference: the unmodified tiny-nccl reference (baseline/_ref, built by
   baseline/build_reference.sh) all-reduces the gradient buckets through its
   public tncclAllReduceSumF32, inside stock PyTorch: Hugging Face GPT2LMHeadModel,
@@ -212,25 +216,12 @@ def build_tnccl_trainer(args, rank, world, dev):
         trainer.close()
         comm.destroy()
 
+    close.describe = trainer.describe
     return trainer.step, launches, close
 
 
-def reducer_desc() -> str:
-    """The tnccl trainer's gradient path as its environment selects it."""
-    r = os.environ.get("TNCCL_DP_REDUCER", "ddp")
-    if r == "flat":
-        if os.environ.get("TNCCL_DP_REGISTERED") == "1":
-            r += "+registered"
-        if os.environ.get("TNCCL_DP_OVERLAP_OPT") == "1":
-            r += "+overlapped-adamw"
-    if os.environ.get("TNCCL_NVLS_ZERO_COPY") == "1":
-        r += "+nvls-zero-copy"
-    if os.environ.get("TNCCL_CUDA_GRAPH") == "1":
-        r += "+cuda-graph"
-    return r
-
-
-def make_record(impl, world, B, T, steps, warmup, ms_max, clocks, launches, e2e, loss):
+def make_record(impl, world, B, T, steps, warmup, ms_max, clocks, launches, e2e, loss,
+                grad_reducer="ddp"):
     """The one JSON line bench.py prints (rank 0): whole-job tokens/s from the
     device step time (max over ranks), plus the end-to-end number, clocks and
     the kernel-launch count of this repository's kernels."""
@@ -246,7 +237,7 @@ def make_record(impl, world, B, T, steps, warmup, ms_max, clocks, launches, e2e,
             "config": {"model": "GPT-2 small (124M): 12 layers, d_model 768, 12 heads, vocab 50257",
                        "global_batch": B * world, "micro_batch_per_gpu": B, "seq_len": T,
                        "parallelism": f"dp{world}", "optimizer": "AdamW", "amp": "bf16 autocast",
-                       "grad_reducer": reducer_desc() if impl == "tnccl" else "ddp",
+                       "grad_reducer": grad_reducer,
                        "l2": "no flush: one step touches several GB (activations, 124M-param "
                              "weights/grads/optimizer state), far above the 126 MB L2"},
             "clocks": clocks, "gpu_launches": launches, "e2e": e2e,
@@ -395,8 +386,9 @@ def main():
                "ms_per_step": wall_max * 1e3 / args.steps, "timing": "host wall clock, max over ranks"}
 
     if rank == 0:
+        desc = getattr(close, "describe", None)
         rec = make_record(args.impl, world, B, T, args.steps, args.warmup, ms_max, clocks,
-                          int(l1 - l0), e2e, last_loss)
+                          int(l1 - l0), e2e, last_loss, desc() if desc else "ddp")
         rec["warmup_steps_run"] = warm
         print(json.dumps(rec), flush=True)
     close()

@@ -11,7 +11,8 @@ registered with the communicator, for the zero-copy NVLS all-reduce
 communication stream as soon as its all-reduce is enqueued, overlapping the
 optimizer with the rest of backward.
 
-``cuda_graph=True`` (or ``TNCCL_CUDA_GRAPH=1``; needs the flat reducer)
+``reducer="flat"`` is the default (``TNCCL_DP_REDUCER=ddp`` selects DDP),
+and with it ``cuda_graph=True`` (``TNCCL_CUDA_GRAPH=0`` turns it off)
 captures the whole training step (forward, backward with its bucket
 all-reduces on the side stream, optimizer, gradient zeroing) in one CUDA
 graph after three eager warm-up steps, and replays it for every later step:
@@ -52,13 +53,14 @@ class DataParallelTrainer:
         self.amp_dtype = amp_dtype
         dev = comm.device
         if reducer is None:
-            reducer = os.environ.get("TNCCL_DP_REDUCER", "ddp")
+            reducer = os.environ.get("TNCCL_DP_REDUCER", "flat")
         if registered is None:
             registered = os.environ.get("TNCCL_DP_REGISTERED", "0") == "1"
         if overlap_optimizer is None:
             overlap_optimizer = os.environ.get("TNCCL_DP_OVERLAP_OPT", "0") == "1"
         if cuda_graph is None:
-            cuda_graph = os.environ.get("TNCCL_CUDA_GRAPH", "0") == "1"
+            # On by default with the flat reducer (DDP cannot be replayed).
+            cuda_graph = os.environ.get("TNCCL_CUDA_GRAPH", "1") == "1" and reducer == "flat"
         if cuda_graph and reducer != "flat":
             raise ValueError("cuda_graph needs reducer='flat' (DDP's reducer runs host "
                              "logic during backward that a graph replay would skip)")
@@ -172,7 +174,26 @@ class DataParallelTrainer:
         return {"model": self.model.state_dict(), "opt": self.opt.state_dict(),
                 "step": self.opt._step}
 
+    def describe(self) -> str:
+        """The gradient path and step execution in use, e.g. 'flat+cuda-graph'."""
+        d = "flat" if self.reducer is not None else "ddp"
+        if self.registration is not None:
+            d += "+registered"
+        if self.overlap_optimizer:
+            d += "+overlapped-adamw"
+        if os.environ.get("TNCCL_NVLS_ZERO_COPY") == "1":
+            d += "+nvls-zero-copy"
+        if self.cuda_graph:
+            d += "+cuda-graph"
+        return d
+
     def load_state_dict(self, sd: dict) -> None:
         self.model.load_state_dict(sd["model"])
         self.opt.load_state_dict(sd["opt"])
         self.opt.set_step(sd["step"])
+        # The loaded optimizer state lives in new tensors: capture again
+        # (after fresh warm-up steps) instead of replaying the old graph.
+        if self._graph is not None:
+            torch.cuda.synchronize()
+            self._graph = None
+        self._eager_steps = 0
