@@ -43,7 +43,7 @@ def main():
             plain = torch.empty(n, dtype=dtype, device=dev)  # caching allocator: staged path
             for it in range(10):
                 src = torch.randint(-8, 9, (n,), generator=g).to(dtype).to(dev)
-                want = src.float()
+                want = src.float().clone()  # .float() of fp32 is src itself
                 dist.all_reduce(want)
                 avg = it % 3 == 2
                 if avg:

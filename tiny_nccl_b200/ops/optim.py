@@ -27,6 +27,10 @@ class AdamW(torch.optim.Optimizer):
         # of casting the fp32 parameter again in the next forward
         # (tiny_nccl_b200.ops.fused.bf16_weight).
         self.bf16_copies = False
+        # Kept outside self.state: Optimizer.load_state_dict casts state
+        # tensors to the parameter's dtype, and the copies are derived data
+        # (rewritten by the next update) that a checkpoint need not hold.
+        self._bf16 = {}
 
     @torch.no_grad()
     def step(self, closure=None):
@@ -69,11 +73,12 @@ class AdamW(torch.optim.Optimizer):
                 if not st:
                     st["exp_avg"] = torch.zeros_like(p, memory_format=torch.contiguous_format)
                     st["exp_avg_sq"] = torch.zeros_like(p, memory_format=torch.contiguous_format)
-                if self.bf16_copies and "bf16" not in st:
-                    st["bf16"] = torch.empty(p.shape, dtype=torch.bfloat16, device=p.device)
                 ps.append(p)
                 if self.bf16_copies:
-                    cs.append(st["bf16"])
+                    if id(p) not in self._bf16:
+                        self._bf16[id(p)] = torch.empty(p.shape, dtype=torch.bfloat16,
+                                                        device=p.device)
+                    cs.append(self._bf16[id(p)])
                 gs.append(p.grad if p.grad.is_contiguous() else p.grad.contiguous())
                 ms.append(st["exp_avg"])
                 vs.append(st["exp_avg_sq"])
