@@ -90,8 +90,8 @@ Config loadConfig() {
   c.nvlsTileBytes = roundTo16(envInt("TNCCL_NVLS_TILE_BYTES", 512 << 10));
   c.nvlsEnable = (int)envInt("TNCCL_NVLS_ENABLE", 1);
   // Off until it has been measured against the staged kernel.
-  c.nvlsZeroCopy = envInt("TNCCL_NVLS_ZERO_COPY", 0) ? 1 : 0;
-  c.nvlsZcMinBytes = envInt("TNCCL_NVLS_ZC_MIN_BYTES", 1 << 20);
+  c.nvlsZeroCopy = envInt("TNCCL_NVLS_ZERO_COPY", 1) ? 1 : 0;
+  c.nvlsZcMinBytes = envInt("TNCCL_NVLS_ZC_MIN_BYTES", -1);  // -1: by rank count
   c.nvlsZcChannels = clampInt(envInt("TNCCL_NVLS_ZC_CHANNELS", 32), 1, kMaxChannels);
   int algo = parseAlgo(envStr("TNCCL_ALGO", "auto"));
   if (algo < 0) {
@@ -210,6 +210,14 @@ void adaptConfig(Config& c, int nranks) {
     chunk = chunk < (32 << 10) ? (32 << 10) : chunk > (256 << 10) ? (256 << 10) : chunk;
     c.tsChunkBytes = chunk / 16 * 16;
   }
+  // Smallest registered message AUTO sends through the zero-copy NVLS
+  // kernel. Measured on 8 x B200: it beats two-shot from 32 MiB and NCCL
+  // from 32 MiB to 4 GiB (fp32 and bf16), is level with two-shot at 16 MiB
+  // and behind below; on 2 x B200 two-shot wins at every size (the switch
+  // step moves 1.5 x the message per direction there, two-shot 1 x), so
+  // 2 ranks never take it. 3 to 7 ranks: not measured; 64 MiB.
+  if (c.nvlsZcMinBytes < 0)
+    c.nvlsZcMinBytes = nranks >= 8 ? (16ll << 20) : nranks >= 3 ? (64ll << 20) : INT64_MAX;
 }
 
 bool parseTuningTable(const std::string& text, TuningTable* out, std::string* error) {

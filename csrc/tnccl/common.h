@@ -62,8 +62,9 @@ struct Config {
   int64_t nvlsTileBytes;   // TNCCL_NVLS_TILE_BYTES
   int nvlsEnable;          // TNCCL_NVLS_ENABLE (0 off, 1 on if supported)
   // Zero-copy NVLS over registered buffers (register.cc).
-  int nvlsZeroCopy;        // TNCCL_NVLS_ZERO_COPY (0 off, 1 on)
+  int nvlsZeroCopy;        // TNCCL_NVLS_ZERO_COPY (1 on, the default; 0 off)
   int64_t nvlsZcMinBytes;  // TNCCL_NVLS_ZC_MIN_BYTES: AUTO uses it from here up
+                           // (-1: by rank count, resolved by adaptConfig)
   int nvlsZcChannels;      // TNCCL_NVLS_ZC_CHANNELS (CTAs per launch)
   int forcedAlgo;          // TNCCL_ALGO (tncclAlgo_t)
   int64_t timeoutMs;       // TNCCL_TIMEOUT_MS: device wait bound

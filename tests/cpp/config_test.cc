@@ -154,8 +154,15 @@ void hashes() {
   b = a;
   b.nvlsZcChannels = a.nvlsZcChannels + 1;
   check(configHash(a) != configHash(b), "configHash covers TNCCL_NVLS_ZC_CHANNELS");
-  check(a.nvlsZeroCopy == 0 && a.nvlsZcMinBytes == (1 << 20) && a.nvlsZcChannels == 32,
-        "defaults: zero-copy NVLS off, 1 MiB, 32 channels");
+  check(a.nvlsZeroCopy == 1 && a.nvlsZcMinBytes == -1 && a.nvlsZcChannels == 32,
+        "defaults: zero-copy NVLS on, minimum by rank count, 32 channels");
+  Config r2 = a, r4 = a, r8 = a;
+  adaptConfig(r2, 2);
+  adaptConfig(r4, 4);
+  adaptConfig(r8, 8);
+  check(r2.nvlsZcMinBytes == INT64_MAX && r4.nvlsZcMinBytes == (64ll << 20) &&
+            r8.nvlsZcMinBytes == (16ll << 20),
+        "zero-copy AUTO minimum: never on 2 ranks, 64 MiB on 4, 16 MiB on 8");
 }
 
 // Random text never crashes the tuning-table parser; whatever it accepts is

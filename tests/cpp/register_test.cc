@@ -396,6 +396,7 @@ void zeroCopySelection() {
   comm.nranks = 4;
   comm.device = 0;
   comm.cfg = loadConfig();
+  comm.cfg.nvlsZcMinBytes = 1 << 20;  // what TNCCL_NVLS_ZC_MIN_BYTES=1048576 sets
   comm.nvls.enabled = true;
   comm.nvls.channels = comm.cfg.nvlsChannels;
   comm.nvls.tileBytes = (uint64_t)comm.cfg.nvlsTileBytes;

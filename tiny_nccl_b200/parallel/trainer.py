@@ -4,9 +4,9 @@ kernel, overlapped with backward) and the fused AdamW kernel.
 
 ``reducer="flat"`` (or ``TNCCL_DP_REDUCER=flat``) replaces DDP with
 :class:`FlatGradReducer`: the gradients live in one flat buffer, which with
-``registered=True`` (``TNCCL_DP_REGISTERED=1``) is tncclMemAlloc memory
+``registered=True`` (the default; ``TNCCL_DP_REGISTERED=0`` turns it off) is tncclMemAlloc memory
 registered with the communicator, for the zero-copy NVLS all-reduce
-(``TNCCL_NVLS_ZERO_COPY=1``), and with ``overlap_optimizer=True``
+(on by default; ``TNCCL_NVLS_ZERO_COPY=0`` turns it off), and with ``overlap_optimizer=True``
 (``TNCCL_DP_OVERLAP_OPT=1``) AdamW updates each bucket's parameters on the
 communication stream as soon as its all-reduce is enqueued, overlapping the
 optimizer with the rest of backward.
@@ -55,7 +55,10 @@ class DataParallelTrainer:
         if reducer is None:
             reducer = os.environ.get("TNCCL_DP_REDUCER", "flat")
         if registered is None:
-            registered = os.environ.get("TNCCL_DP_REGISTERED", "0") == "1"
+            # On by default: with NVLS, AUTO sends the large buckets of a
+            # registered buffer through the zero-copy kernel (8 ranks: from
+            # 16 MiB); TNCCL_DP_REGISTERED=0 keeps the buffer unregistered.
+            registered = os.environ.get("TNCCL_DP_REGISTERED", "1") == "1"
         if overlap_optimizer is None:
             overlap_optimizer = os.environ.get("TNCCL_DP_OVERLAP_OPT", "0") == "1"
         if cuda_graph is None:
