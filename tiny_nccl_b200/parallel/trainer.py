@@ -1,24 +1,28 @@
-"""Data-parallel training step: DistributedDataParallel with the tnccl comm
-hook (gradient buckets all-reduced on a side stream, 1/world fused into the
-kernel, overlapped with backward) and the fused AdamW kernel.
+"""Data-parallel training step of the fused GPT-2: gradients averaged over
+the ranks by tnccl kernels while backward runs, then the fused AdamW.
 
-``reducer="flat"`` (or ``TNCCL_DP_REDUCER=flat``) replaces DDP with
-:class:`FlatGradReducer`: the gradients live in one flat buffer, which with
-``registered=True`` (the default; ``TNCCL_DP_REGISTERED=0`` turns it off) is tncclMemAlloc memory
-registered with the communicator, for the zero-copy NVLS all-reduce
-(on by default; ``TNCCL_NVLS_ZERO_COPY=0`` turns it off), and with ``overlap_optimizer=True``
-(``TNCCL_DP_OVERLAP_OPT=1``) AdamW updates each bucket's parameters on the
-communication stream as soon as its all-reduce is enqueued, overlapping the
-optimizer with the rest of backward.
+Default (``reducer="flat"``): :class:`FlatGradReducer` keeps every ``.grad``
+in one flat buffer cut into ~25 MB buckets and all-reduces each bucket on the
+communicator's side stream as soon as backward has produced it (1/world
+fused into the kernel). The buffer is tncclMemAlloc memory registered with
+the communicator (``registered``, ``TNCCL_DP_REGISTERED=0`` turns it off), so
+on 8 ranks AUTO sends its buckets through the zero-copy NVLS kernel (the
+switch reduces straight from every GPU's buffer). The whole step (forward,
+backward with the bucket all-reduces, AdamW, gradient zeroing) is captured
+in one CUDA graph after three eager warm-up steps and replayed for every
+later step (``cuda_graph``, ``TNCCL_CUDA_GRAPH=0`` turns it off): the ~500
+kernel launches of a GPT-2 small step then cost one graph launch instead of
+more host time than the GPU needs for the step. Inputs are copied into
+static buffers first, and the optimizer reads its step count from device
+memory. AdamW also writes the bf16 copies of the weights that the next
+forward's GEMMs read.
 
-``reducer="flat"`` is the default (``TNCCL_DP_REDUCER=ddp`` selects DDP),
-and with it ``cuda_graph=True`` (``TNCCL_CUDA_GRAPH=0`` turns it off)
-captures the whole training step (forward, backward with its bucket
-all-reduces on the side stream, optimizer, gradient zeroing) in one CUDA
-graph after three eager warm-up steps, and replays it for every later step:
-the ~600 kernel launches of a GPT-2 small step then cost one graph launch
-instead of the host time of the eager step. Inputs are copied into static
-buffers first; the optimizer reads its step count from device memory.
+``overlap_optimizer=True`` (``TNCCL_DP_OVERLAP_OPT=1``) runs AdamW on each
+bucket's parameters on the communication stream right after its all-reduce.
+
+``reducer="ddp"`` (``TNCCL_DP_REDUCER=ddp``): DistributedDataParallel with
+the tnccl comm hook, eager (DDP's reducer runs host logic during backward
+that a graph replay would skip).
 """
 from __future__ import annotations
 
