@@ -33,8 +33,6 @@ def test_example_single_gpu(built):
     assert r.returncode == 0 and "all ranks: ok" in r.stdout, r.stdout + r.stderr
 
 
-@pytest.mark.skipif(os.environ.get("TNCCL_TEST_NVLS_ZC") != "1",
-                    reason="registered buffers have not run on a GPU yet: TNCCL_TEST_NVLS_ZC=1")
 def test_example_registered_buffers(built):
     # One rank: tncclMemAlloc / tncclMemFree and a refused registration (no
     # NVLS); two or more: registered buffers on the zero-copy NVLS kernel.

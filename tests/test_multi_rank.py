@@ -1,6 +1,5 @@
 """Multi-process tests. GPU ones need 2 GPUs (skipped otherwise); the store
 exchange runs on CPU with gloo ranks."""
-import os
 
 import pytest
 
@@ -68,8 +67,6 @@ def test_graph_trainer_matches_ddp(built):
 
 @pytest.mark.gpu
 @pytest.mark.skipif(gpu_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.skipif(os.environ.get("TNCCL_TEST_NVLS_ZC") != "1",
-                    reason="zero-copy NVLS has not run on a GPU yet: TNCCL_TEST_NVLS_ZC=1")
 def test_nvls_zero_copy_registered_buffers(built):
     r = torchrun(2, ["tests/workers/nvls_zero_copy_worker.py"], timeout=600,
                  env={"TNCCL_NVLS_ZERO_COPY": "1", "TNCCL_DEBUG": "TRACE",
@@ -82,9 +79,11 @@ def test_nvls_zero_copy_registered_buffers(built):
 
 @pytest.mark.gpu
 @pytest.mark.skipif(gpu_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.skipif(os.environ.get("TNCCL_TEST_NVLS_ZC") != "1",
-                    reason="the flat reducer has not run on a GPU yet: TNCCL_TEST_NVLS_ZC=1")
 def test_flat_reducer_registered_buffer(built):
     r = torchrun(2, ["tests/workers/flat_trainer_worker.py"], timeout=600,
-                 env={"TNCCL_NVLS_ZERO_COPY": "1", "TNCCL_TIMEOUT_MS": "10000"})
+                 # 2 ranks: AUTO never picks the zero-copy kernel by itself
+                 # (two-shot is faster there); a 1 MiB minimum makes every
+                 # bucket take it, which is what this test is about.
+                 env={"TNCCL_NVLS_ZERO_COPY": "1", "TNCCL_NVLS_ZC_MIN_BYTES": "1048576",
+                      "TNCCL_TIMEOUT_MS": "10000"})
     assert r.returncode == 0 and "PASS" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]

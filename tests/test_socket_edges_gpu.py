@@ -2,12 +2,7 @@
 FIFOs and the proxy thread, on one host with every edge forced onto sockets,
 with every rank posing as its own host over a TCP rendezvous, and the
 failure path of a rank that leaves between steps. The host side of the same
-path is covered on CPU by tests/cpp/net_proxy_test.cc.
-
-These run only with TNCCL_TEST_SOCKET_EDGES=1: the socket-edge kernel path
-has not yet run on a GPU, and it joins the default GPU suite once it has."""
-import os
-
+path is covered on CPU by tests/cpp/net_proxy_test.cc."""
 import pytest
 
 from conftest import gpu_count, torchrun
@@ -15,9 +10,6 @@ from conftest import gpu_count, torchrun
 pytestmark = [
     pytest.mark.gpu,
     pytest.mark.skipif(gpu_count() < 2, reason="needs 2 GPUs"),
-    pytest.mark.skipif(os.environ.get("TNCCL_TEST_SOCKET_EDGES") != "1",
-                       reason="socket-edge GPU path not yet run on a GPU; "
-                              "set TNCCL_TEST_SOCKET_EDGES=1"),
 ]
 
 _BASE = {"TNCCL_NVLS_ENABLE": "0", "NCCL_NVLS_ENABLE": "0", "TNCCL_TIMEOUT_MS": "20000"}
