@@ -23,6 +23,8 @@ def main():
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--persistent", action="store_true",
                     help="gemm_gelu: one CTA per SM with two TMEM accumulators")
+    ap.add_argument("--pair", action="store_true",
+                    help="gemm_gelu: persistent CTA pairs (cta_group::2, 256 x 256 tiles)")
     args = ap.parse_args()
     import tiny_nccl_b200 as tn
 
@@ -69,7 +71,8 @@ def main():
         w = (torch.randn(4 * C, C, device=dev) * 0.02).to(torch.bfloat16)
         b = (torch.randn(4 * C, device=dev) * 0.02).to(torch.bfloat16)
         if args.kernel == "gemm_gelu":
-            fn = lambda: ops.gemm_bias_act(x, w, b, True, args.persistent)  # noqa: E731
+            variant = 2 if args.pair else 1 if args.persistent else 0
+            fn = lambda: ops.gemm_bias_act(x, w, b, True, variant)  # noqa: E731
         else:
             fn = lambda: torch.nn.functional.gelu(torch.addmm(b, x, w.t()),  # noqa: E731
                                                   approximate="tanh")

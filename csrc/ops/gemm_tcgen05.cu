@@ -461,6 +461,233 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// CTA-pair variant (tcgen05 cta_group::2): a cluster of two CTAs on the two
+// SMs of a TPC computes one 256 x 256 tile per step, persistent over the
+// tiles. CTA r of the pair stages rows 128 r .. +127 of the tile's A block
+// and of its B block (16 KiB each per 64-wide K block) in its own shared
+// memory; the even CTA issues tcgen05.mma.cta_group::2 (M 256, N 256), which
+// reads A and B from both CTAs at the same shared-memory offsets and writes
+// the fp32 accumulator rows 128 r .. +127 into CTA r's TMEM. Per K block each
+// SM loads 32 KiB from L2 for 128 x 256 x 64 of MMA, two thirds of the
+// one-CTA tile's 48 KiB, and six stages fit in shared memory.
+//
+// Hand-offs (the even CTA's barriers unless noted):
+//   full[s]      the even producer arms it for both CTAs' bytes (64 KiB);
+//                both producers' TMA loads (cta_group::2 form, no multicast)
+//                complete on it;
+//   empty[s]     in each CTA, count 1: the MMA commit multicast to the pair;
+//   accFull[b]   in each CTA: the commit after a tile's last K block;
+//   accEmpty[b]  count 2 x 8: every epilogue warp of both CTAs arrives
+//                (the odd CTA's remotely) after its last read of buffer b.
+// Both CTAs meet at cluster barriers after set-up and before teardown, so
+// neither leaves while the other can still reach its shared memory or TMEM.
+// Every wait is bounded as in the other variants; on expiry the even CTA
+// drains its loads and MMAs and the odd CTA, whose loads complete on the
+// even CTA's barriers, gives its loads a bounded grace period before the
+// final cluster barrier.
+// ---------------------------------------------------------------------------
+constexpr int kPairBM = 256;
+constexpr int kPairStages = 6;
+constexpr uint32_t kHalf = 128 * kBK * 2;  // 16 KiB: 128 rows x 64 K of bf16
+constexpr uint32_t kPairSmemBytes = kPairStages * 2 * kHalf + 1024;
+
+__device__ __forceinline__ uint32_t clusterRank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address of the same shared variable in CTA 0 of the cluster.
+__device__ __forceinline__ uint32_t inLeader(const void* p) {
+  uint32_t d;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(d) : "r"(smemAddr(p)));
+  return d;
+}
+__device__ __forceinline__ void clusterSync() {
+  asm volatile("barrier.cluster.arrive.release;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
+}
+__device__ __forceinline__ void tmaLoadPair(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                            uint32_t leaderBar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(leaderBar)
+      : "memory");
+}
+__host__ __device__ constexpr uint32_t instrDescPair() {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(256 >> 3) << 17) |
+         ((uint32_t)(kPairBM >> 4) << 24);
+}
+__device__ __forceinline__ void mmaPair(uint32_t tmemD, uint64_t a, uint64_t b,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, "
+      "{%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}" ::"r"(tmemD),
+      "l"(a), "l"(b), "r"(instrDescPair()), "r"(accumulate), "r"(0u)
+      : "memory");
+}
+// Arrives on `bar` in both CTAs of the pair once the pair MMAs issued so far
+// have completed.
+__device__ __forceinline__ void commitPair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 "
+      "[%0], %1;" ::"r"(smemAddr(bar)),
+      "h"((uint16_t)3)
+      : "memory");
+}
+__device__ __forceinline__ void commitPairLocal(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smemAddr(bar))
+               : "memory");
+}
+__device__ __forceinline__ void mbarArriveRemote(uint32_t clusterAddr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(clusterAddr)
+               : "memory");
+}
+
+template <bool GELU>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemmBiasActPairKernel(const __grid_constant__ CUtensorMap mapA,
+                          const __grid_constant__ CUtensorMap mapB,
+                          const uint16_t* __restrict__ bias, uint16_t* __restrict__ pre,
+                          uint16_t* __restrict__ act, int M, int N, int K) {
+  __shared__ __align__(8) uint64_t sFull[kPairStages];
+  __shared__ __align__(8) uint64_t sEmpty[kPairStages];
+  __shared__ __align__(8) uint64_t sAccFull[2];
+  __shared__ __align__(8) uint64_t sAccEmpty[2];
+  __shared__ __align__(8) uint64_t sDone;
+  __shared__ uint32_t sTmem;
+  __shared__ int sAbort;
+  extern __shared__ uint8_t dsmem[];
+  const uint32_t base = (smemAddr(dsmem) + 1023u) & ~1023u;
+  const uint32_t stageA0 = base, stageB0 = base + kPairStages * kHalf;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = clusterRank();
+  const int pair = (int)(blockIdx.x >> 1), pairs = (int)(gridDim.x >> 1);
+  const int tilesN = (N + 255) / 256;
+  const int tiles = tilesN * ((M + kPairBM - 1) / kPairBM);
+  const int kBlocks = (K + kBK - 1) / kBK;
+  volatile int* abort = &sAbort;
+
+  if (threadIdx.x == 0) {
+    sAbort = 0;
+    for (int s = 0; s < kPairStages; ++s) {
+      mbarInit(&sFull[s], 1);
+      mbarInit(&sEmpty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbarInit(&sAccFull[b], 1);
+      mbarInit(&sAccEmpty[b], 2 * kEpiWarps);
+    }
+    mbarInit(&sDone, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    // Both CTAs' warp 1, the same shared-memory destination in each.
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smemAddr(&sTmem)),
+                 "r"(2 * kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  fenceBeforeSync();
+  __syncthreads();
+  clusterSync();  // barriers initialised and TMEM allocated in both CTAs
+  fenceAfterSync();
+  const uint32_t tmem = sTmem;
+
+  if (warp == 0 && lane == 0) {
+    // Producer (both CTAs): this CTA's halves of A and B.
+    uint32_t g = 0;
+    for (int t = pair; t < tiles && !*abort; t += pairs) {
+      const int m0 = (t / tilesN) * kPairBM + (int)rank * 128;
+      const int n0 = (t % tilesN) * 256 + (int)rank * 128;
+      for (int kb = 0; kb < kBlocks; ++kb, ++g) {
+        const uint32_t s = g % kPairStages, round = g / kPairStages;
+        if (!mbarWait(&sEmpty[s], (round & 1u) ^ 1u, abort, 1)) break;
+        if (rank == 0) mbarExpectTx(&sFull[s], 4 * kHalf);  // both CTAs' A and B halves
+        const uint32_t bar = inLeader(&sFull[s]);
+        tmaLoadPair(stageA0 + s * kHalf, &mapA, kb * kBK, m0, bar);
+        tmaLoadPair(stageB0 + s * kHalf, &mapB, kb * kBK, n0, bar);
+      }
+    }
+    if (*abort) {
+      if (rank == 0) {
+        for (uint32_t q = g > (uint32_t)kPairStages ? g - kPairStages : 0; q < g; ++q)
+          mbarWait(&sFull[q % kPairStages], (q / kPairStages) & 1u, abort, 4, true);
+      } else {
+        // This CTA's loads complete on the even CTA's barriers: let them land.
+        const uint64_t t0 = globalTimer();
+        while (globalTimer() - t0 < 200000ull) {
+        }
+      }
+    }
+  } else if (warp == 1 && lane == 0 && rank == 0) {
+    // MMA issuer (even CTA only).
+    uint32_t g = 0, local = 0;
+    for (int t = pair; t < tiles && !*abort; t += pairs, ++local) {
+      const uint32_t b = local & 1u, use = local >> 1;
+      if (!mbarWait(&sAccEmpty[b], (use & 1u) ^ 1u, abort, 2)) break;
+      fenceAfterSync();
+      const uint32_t acc = tmem + b * kTmemCols;
+      bool ok = true;
+      for (int kb = 0; kb < kBlocks; ++kb, ++g) {
+        const uint32_t s = g % kPairStages;
+        if (!(ok = mbarWait(&sFull[s], (g / kPairStages) & 1u, abort, 2))) break;
+        fenceAfterSync();
+        const uint32_t a = stageA0 + s * kHalf, bb = stageB0 + s * kHalf;
+#pragma unroll
+        for (int k = 0; k < kBK / 16; ++k)
+          mmaPair(acc, smemDesc(a + k * 32), smemDesc(bb + k * 32), (kb | k) != 0 ? 1u : 0u);
+        commitPair(&sEmpty[s]);
+      }
+      if (!ok) break;
+      commitPair(&sAccFull[b]);
+    }
+    commitPairLocal(&sDone);
+    if (*abort) mbarWait(&sDone, 0, abort, 5, true);
+  } else if (warp >= 2) {
+    // Epilogue (both CTAs): this CTA's 128 rows of the tile; TMEM lane
+    // quarter warp % 4, column half (warp - 2) / 4.
+    const int quarter = warp & 3;
+    const int c0 = ((warp - 2) >> 2) * 128;
+    uint32_t local = 0;
+    for (int t = pair; t < tiles; t += pairs, ++local) {
+      const uint32_t b = local & 1u, use = local >> 1;
+      const bool ready = mbarWait(&sAccFull[b], use & 1u, abort, 3);
+      if (!__all_sync(0xffffffffu, ready)) break;
+      fenceAfterSync();
+      const int m0 = (t / tilesN) * kPairBM + (int)rank * 128, n0 = (t % tilesN) * 256;
+      const int row = m0 + quarter * 32 + lane;
+      const uint32_t acc = tmem + b * kTmemCols + ((uint32_t)(quarter * 32) << 16);
+#pragma unroll 1
+      for (int c = c0; c < c0 + 128; c += 32) {
+        float v[32];
+        tmemLoad32(acc + (uint32_t)c, v);
+        if (c + 32 == c0 + 128) {
+          fenceBeforeSync();
+          __syncwarp();
+          if (lane == 0) mbarArriveRemote(inLeader(&sAccEmpty[b]));
+        }
+        storeChunk<GELU>(v, row, n0 + c, M, N, bias, pre, act);
+      }
+    }
+  }
+  fenceBeforeSync();
+  __syncthreads();
+  clusterSync();  // neither CTA leaves while the pair's MMAs or arrivals can reach it
+  if (warp == 1) {
+    fenceAfterSync();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(2 * kTmemCols)
+                 : "memory");
+  }
+}
+
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
                                    const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
@@ -527,6 +754,36 @@ int launchGemm(const void* x, const void* w, const void* bias, void* pre, void* 
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }
 
+template <bool GELU>
+int launchGemmPair(const void* x, const void* w, const void* bias, void* pre, void* act, int M,
+                   int N, int K, cudaStream_t stream) {
+  auto kernel = gemmBiasActPairKernel<GELU>;
+  static std::atomic<uint64_t> done{0};
+  static int sms[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 3;
+  const uint64_t bit = dev < 64 ? (1ull << dev) : 0;
+  if (!(done.load(std::memory_order_acquire) & bit)) {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kPairSmemBytes) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms[dev & 63], cudaDevAttrMultiProcessorCount, dev) !=
+            cudaSuccess)
+      return 3;
+    done.fetch_or(bit, std::memory_order_acq_rel);
+  }
+  // Each CTA of a pair loads 128 rows of A and 128 rows of B per K block.
+  CUtensorMap mapA, mapB;
+  if (!makeMap(&mapA, x, M, K, 128) || !makeMap(&mapB, w, N, K, 128)) return 4;
+  const int tiles = ((N + 255) / 256) * ((M + kPairBM - 1) / kPairBM);
+  const int pairs = (sms[dev & 63] > 0 ? sms[dev & 63] : 148) / 2;
+  const unsigned grid = 2u * (unsigned)(tiles < pairs ? tiles : pairs);
+  kernel<<<grid, kThreads, kPairSmemBytes, stream>>>(
+      mapA, mapB, static_cast<const uint16_t*>(bias), static_cast<uint16_t*>(pre),
+      static_cast<uint16_t*>(act), M, N, K);
+  gLaunches.fetch_add(1, std::memory_order_relaxed);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
@@ -535,8 +792,9 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 using namespace tnops;
 
 // pre = bf16(x w^T + bias) and, with gelu, act = bf16(gelu_tanh(pre)); bias
-// and pre may be null (not both outputs). `persistent` selects the kernel
-// with one CTA per SM and two TMEM accumulators. Requirements: K % 8 == 0
+// and pre may be null (not both outputs). `persistent` selects the kernel:
+// 0 one 128 x 256 tile per CTA, 1 one CTA per SM walking the tiles with two
+// TMEM accumulators, 2 CTA pairs (cta_group::2) walking 256 x 256 tiles. Requirements: K % 8 == 0
 // (TMA row pitch), N % 8 == 0, 16-byte aligned x, w, pre, act. Returns 0 on
 // launch.
 extern "C" int tnops_gemm_bias_act(const void* x, const void* w, const void* bias, void* pre,
@@ -546,6 +804,9 @@ extern "C" int tnops_gemm_bias_act(const void* x, const void* w, const void* bia
       !aligned16(w) || (pre && !aligned16(pre)) || (act && !aligned16(act)) ||
       (gelu && act == nullptr) || (!gelu && pre == nullptr))
     return 1;
+  if (persistent == 2)
+    return gelu ? launchGemmPair<true>(x, w, bias, pre, act, M, N, K, stream)
+                : launchGemmPair<false>(x, w, bias, pre, act, M, N, K, stream);
   if (persistent)
     return gelu ? launchGemm<true, true>(x, w, bias, pre, act, M, N, K, stream)
                 : launchGemm<false, true>(x, w, bias, pre, act, M, N, K, stream);

@@ -82,8 +82,9 @@ int tnops_adamw_dev(const tnops_adamw_list* list, float lr, float beta1, float b
 // bf16 GEMM on the tcgen05 tensor cores with a fused epilogue:
 // pre = bf16(x w^T + bias), and with `gelu` act = bf16(gelu_tanh(pre)).
 // x [M, K], w [N, K] (nn.Linear layout), bias [N] (may be null), pre / act
-// [M, N] (pre may be null with gelu). `persistent`: one CTA per SM with two
-// TMEM accumulators instead of one CTA per 128 x 256 tile. K % 8 == 0,
+// [M, N] (pre may be null with gelu). `persistent`: 0 one CTA per 128 x 256
+// tile, 1 one CTA per SM walking the tiles with two TMEM accumulators, 2 CTA
+// pairs (cta_group::2) walking 256 x 256 tiles. K % 8 == 0,
 // N % 8 == 0, x, w, pre, act 16-byte aligned; 1 (invalid argument) otherwise.
 int tnops_gemm_bias_act(const void* x, const void* w, const void* bias, void* pre, void* act,
                         int M, int N, int K, int gelu, int persistent, cudaStream_t stream);

@@ -116,7 +116,7 @@ at::Tensor biasGrad(const at::Tensor& g) {
 // [pre, act] (bf16 [M, N]) from the tcgen05 GEMM with the fused epilogue.
 std::vector<at::Tensor> gemmBiasAct(const at::Tensor& x, const at::Tensor& w,
                                     const c10::optional<at::Tensor>& bias, bool gelu,
-                                    bool persistent) {
+                                    int64_t persistent) {
   need(x, at::kBFloat16, "x");
   need(w, at::kBFloat16, "weight");
   TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1),
@@ -133,7 +133,7 @@ std::vector<at::Tensor> gemmBiasAct(const at::Tensor& x, const at::Tensor& w,
   at::Tensor act = gelu ? at::empty({M, N}, x.options()) : at::Tensor();
   const int rc = tnops_gemm_bias_act(x.data_ptr(), w.data_ptr(), bias ? bias->data_ptr() : nullptr,
                                      pre.data_ptr(), gelu ? act.data_ptr() : nullptr, M, N, K,
-                                     gelu ? 1 : 0, persistent ? 1 : 0, streamOf(x));
+                                     gelu ? 1 : 0, (int)persistent, streamOf(x));
   TORCH_CHECK(rc == 0, "tnops_gemm_bias_act failed (code ", rc, ")");
   if (gelu) return {pre, act};
   return {pre};
@@ -229,7 +229,7 @@ void registerOps(py::module_& m) {
   ops.def("bias_grad", &biasGrad, py::arg("grad"));
   ops.def("gelu_bwd_bias", &geluBwdBias, py::arg("grad_y"), py::arg("pre"));
   ops.def("gemm_bias_act", &gemmBiasAct, py::arg("x"), py::arg("weight"), py::arg("bias"),
-          py::arg("gelu"), py::arg("persistent") = false);
+          py::arg("gelu"), py::arg("persistent") = 0);
   ops.def("tcgen05_status", [](bool reset) { return tnops_tcgen05_status(reset ? 1 : 0); },
           py::arg("reset") = false);
   ops.def("scale_bf16_", &scaleBf16);

@@ -1,5 +1,6 @@
 """The tcgen05 GEMM with the fused bias + GELU epilogue (csrc/ops/
-gemm_tcgen05.cu), one CTA per tile and persistent, against an fp32 PyTorch
+gemm_tcgen05.cu), one CTA per tile, persistent, and persistent CTA pairs
+(cta_group::2, 256 x 256 tiles), against an fp32 PyTorch
 reference of the same op, on the GPT-2 MLP shape and on shapes with M, N and
 K tails."""
 import pytest
@@ -12,7 +13,7 @@ SHAPES = [(128, 256, 64), (256, 264, 72), (1000, 3072, 768), (8192, 3072, 768)]
 
 @pytest.mark.parametrize("M,N,K", SHAPES)
 @pytest.mark.parametrize("gelu", [True, False])
-@pytest.mark.parametrize("persistent", [False, True])
+@pytest.mark.parametrize("persistent", [0, 1, 2])  # one tile per CTA, persistent, CTA pairs
 def test_gemm_bias_act_matches_fp32_reference(built, M, N, K, gelu, persistent):
     import tiny_nccl_b200 as tn
 

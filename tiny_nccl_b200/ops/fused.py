@@ -133,10 +133,12 @@ class _LinearBias(torch.autograd.Function):
         return gy @ w16, _wgrad(gy, x), _ops().bias_grad(gy)
 
 
-# TNCCL_TCGEN05_GEMM=1 (or =persistent) computes the forward of linear_gelu
-# with the tcgen05 GEMM and its fused bias + GELU epilogue instead of cuBLAS
-# and a separate GELU. Off by default: that kernel has not run on a GPU yet.
+# TNCCL_TCGEN05_GEMM=1 / persistent / pair computes the forward of
+# linear_gelu with the tcgen05 GEMM (one tile per CTA / persistent / CTA
+# pairs) and its fused bias + GELU epilogue instead of cuBLAS and a separate
+# GELU kernel.
 _TCGEN05 = os.environ.get("TNCCL_TCGEN05_GEMM", "0")
+_TCGEN05_VARIANT = {"1": 0, "persistent": 1, "pair": 2}.get(_TCGEN05, 0)
 
 
 class _LinearGelu(torch.autograd.Function):
@@ -149,7 +151,7 @@ class _LinearGelu(torch.autograd.Function):
         w16 = bf16_weight(weight)
         b16 = bf16_weight(bias)
         if _TCGEN05 != "0":
-            pre, y = _ops().gemm_bias_act(x, w16, b16, True, _TCGEN05 == "persistent")
+            pre, y = _ops().gemm_bias_act(x, w16, b16, True, _TCGEN05_VARIANT)
         else:
             with torch.autocast("cuda", enabled=False):
                 pre = torch.addmm(b16, x, w16.t())
