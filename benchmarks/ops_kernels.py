@@ -23,6 +23,8 @@ def main():
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--persistent", action="store_true",
                     help="gemm_gelu: one CTA per SM with two TMEM accumulators")
+    ap.add_argument("--k", type=int, default=768, help="gemm_gelu: inner dimension")
+    ap.add_argument("--no-gelu", action="store_true", help="gemm_gelu: bias only (pre)")
     ap.add_argument("--pair", action="store_true",
                     help="gemm_gelu: persistent CTA pairs (cta_group::2, 256 x 256 tiles)")
     args = ap.parse_args()
@@ -67,16 +69,16 @@ def main():
             ops.adamw(ps, gs, ms, vs, wd, 6e-4, 0.9, 0.95, 1e-8, step[0], 1.0)
         nbytes = sum(p.numel() for p in ps) * 4 * 7
     elif args.kernel in ("gemm_gelu", "gemm_gelu_ref"):
-        x = (torch.randn(rows, C, device=dev) * 0.5).to(torch.bfloat16)
-        w = (torch.randn(4 * C, C, device=dev) * 0.02).to(torch.bfloat16)
+        x = (torch.randn(rows, args.k, device=dev) * 0.5).to(torch.bfloat16)
+        w = (torch.randn(4 * C, args.k, device=dev) * 0.02).to(torch.bfloat16)
         b = (torch.randn(4 * C, device=dev) * 0.02).to(torch.bfloat16)
         if args.kernel == "gemm_gelu":
             variant = 2 if args.pair else 1 if args.persistent else 0
-            fn = lambda: ops.gemm_bias_act(x, w, b, True, variant)  # noqa: E731
+            fn = lambda: ops.gemm_bias_act(x, w, b, not args.no_gelu, variant)  # noqa: E731
         else:
             fn = lambda: torch.nn.functional.gelu(torch.addmm(b, x, w.t()),  # noqa: E731
                                                   approximate="tanh")
-        flops = 2.0 * rows * 4 * C * C
+        flops = 2.0 * rows * 4 * C * args.k
         nbytes = None
     else:
         raise SystemExit(f"unknown kernel {args.kernel}")

@@ -52,7 +52,12 @@ constexpr int kThreads = 64 + kEpiWarps * 32;
 constexpr uint32_t kTmemCols = 256;
 constexpr uint32_t kStageA = kBM * kBK * 2;  // 16 KiB
 constexpr uint32_t kStageB = kBN * kBK * 2;  // 32 KiB
-constexpr uint32_t kSmemBytes = kStages * (kStageA + kStageB) + 1024;  // + alignment slack
+// Epilogue staging: per epilogue warp a 32 x 32 bf16 block of pre and one of
+// act (2 KiB each, 64-byte swizzle), written out by TMA tensor stores.
+constexpr uint32_t kEpiBuf = 4096;
+constexpr uint32_t kEpiBytes = kEpiWarps * kEpiBuf;
+constexpr uint32_t kSmemBytes =
+    kStages * (kStageA + kStageB) + kEpiBytes + 1024;  // + alignment slack
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s per wait
 
 __device__ unsigned int gTcgen05Status;  // first failure code (0: none)
@@ -185,48 +190,85 @@ __device__ __forceinline__ uint32_t packBf16(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Epilogue of 32 accumulator columns of one row: bias (the same 32 values
-// for every lane, loaded as four broadcast 16-byte reads), rounding to bf16,
-// GELU of the rounded value, 16-byte stores of pre and act.
+__device__ __forceinline__ void tmaStore2d(const CUtensorMap* map, int x, int y, uint32_t src) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(src)
+               : "memory");
+}
+__device__ __forceinline__ void stShared16(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                           uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
+}
+
+// Epilogue of one warp's 32 x 32 block (lane = row row0 + lane, columns
+// col0 .. +31, the fp32 accumulator values in v): bias (the same 32 values
+// for every lane, four broadcast 16-byte loads), rounding to bf16, GELU of
+// the rounded value; the bf16 rows go to this warp's staging buffers in the
+// 64-byte swizzle (16-byte piece j of row r at piece j ^ ((r >> 1) & 3),
+// which keeps the eight lanes of each store phase on distinct banks), and
+// one lane writes each block with a TMA tensor store. The tensor maps clip
+// rows and columns past M and N; a block that starts past them is skipped. A buffer is rewritten only after the
+// previous store from it has been read.
 template <bool GELU>
-__device__ __forceinline__ void storeChunk(const float (&v)[32], int row, int col0, int M, int N,
-                                           const uint16_t* __restrict__ bias,
-                                           uint16_t* __restrict__ pre,
-                                           uint16_t* __restrict__ act) {
-  if (col0 >= N) return;
+__device__ __forceinline__ void epilogueChunk(const float (&v)[32], int lane, int row0, int col0,
+                                              int M, int N, const uint16_t* __restrict__ bias,
+                                              const CUtensorMap* mapPre,
+                                              const CUtensorMap* mapAct, uint32_t bufPre,
+                                              uint32_t bufAct, bool hasPre) {
   uint4 bb[4] = {};
   if (bias) {
 #pragma unroll
     for (int g = 0; g < 4; ++g)
       if (col0 + g * 8 < N) bb[g] = __ldg(reinterpret_cast<const uint4*>(bias + col0) + g);
   }
-  if (row >= M) return;
+  uint32_t pw[16], aw[16];
 #pragma unroll
   for (int g = 0; g < 4; ++g) {
-    const int col = col0 + g * 8;
-    if (col >= N) break;  // N % 8 == 0: a vector is all in or all out
     const uint32_t bw[4] = {bb[g].x, bb[g].y, bb[g].z, bb[g].w};
-    uint32_t pw[4], aw[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const float x0 = v[g * 8 + 2 * i] + __uint_as_float(bw[i] << 16);
       const float x1 = v[g * 8 + 2 * i + 1] + __uint_as_float(bw[i] & 0xffff0000u);
-      pw[i] = packBf16(x0, x1);
+      const uint32_t p = packBf16(x0, x1);
+      pw[g * 4 + i] = p;
       if (GELU)
-        aw[i] = packBf16(geluTanh(__uint_as_float(pw[i] << 16)),
-                         geluTanh(__uint_as_float(pw[i] & 0xffff0000u)));
+        aw[g * 4 + i] = packBf16(geluTanh(__uint_as_float(p << 16)),
+                                 geluTanh(__uint_as_float(p & 0xffff0000u)));
     }
-    const size_t off = (size_t)row * N + col;
-    if (pre) *reinterpret_cast<uint4*>(pre + off) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
-    if (GELU) *reinterpret_cast<uint4*>(act + off) = make_uint4(aw[0], aw[1], aw[2], aw[3]);
   }
+  if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+  __syncwarp();
+  const uint32_t rowOff = (uint32_t)lane * 64u, sw = ((uint32_t)lane >> 1) & 3u;
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const uint32_t at = rowOff + 16u * ((uint32_t)g ^ sw);
+    if (hasPre) stShared16(bufPre + at, pw[4 * g], pw[4 * g + 1], pw[4 * g + 2], pw[4 * g + 3]);
+    if (GELU) stShared16(bufAct + at, aw[4 * g], aw[4 * g + 1], aw[4 * g + 2], aw[4 * g + 3]);
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  __syncwarp();
+  if (lane == 0 && row0 < M && col0 < N) {  // blocks wholly past the edge are not stored
+    if (hasPre) tmaStore2d(mapPre, col0, row0, bufPre);
+    if (GELU) tmaStore2d(mapAct, col0, row0, bufAct);
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+  }
+}
+// Before a warp's staging buffers go away: its stores have completed.
+__device__ __forceinline__ void epilogueDrain(int lane) {
+  if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+  __syncwarp();
 }
 
 template <bool GELU>
 __global__ void __launch_bounds__(kThreads, 1)
     gemmBiasActKernel(const __grid_constant__ CUtensorMap mapA,
-                      const __grid_constant__ CUtensorMap mapB, const uint16_t* __restrict__ bias,
-                      uint16_t* __restrict__ pre, uint16_t* __restrict__ act, int M, int N, int K) {
+                      const __grid_constant__ CUtensorMap mapB,
+                      const __grid_constant__ CUtensorMap mapPre,
+                      const __grid_constant__ CUtensorMap mapAct,
+                      const uint16_t* __restrict__ bias, int hasPre, int M, int N, int K) {
   __shared__ __align__(8) uint64_t sFull[kStages];
   __shared__ __align__(8) uint64_t sEmpty[kStages];
   __shared__ __align__(8) uint64_t sAccum;
@@ -236,6 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Stage buffers start on a 1024-byte boundary (swizzle atoms).
   const uint32_t base = (smemAddr(dsmem) + 1023u) & ~1023u;
   const uint32_t stageA0 = base, stageB0 = base + kStages * kStageA;
+  const uint32_t epi0 = base + kStages * (kStageA + kStageB);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * kBN, m0 = blockIdx.y * kBM;
@@ -300,7 +343,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // the column half (warp - 2) / 4.
     const int quarter = warp & 3;
     const int c0 = ((warp - 2) >> 2) * (kBN / 2);
-    const int row = m0 + quarter * 32 + lane;
+    const uint32_t bufPre = epi0 + (uint32_t)(warp - 2) * kEpiBuf, bufAct = bufPre + kEpiBuf / 2;
     // tcgen05.ld is warp-collective: the whole warp proceeds only if every
     // lane saw the accumulator complete.
     const bool ready = mbarWait(&sAccum, 0, abort, 3);
@@ -310,9 +353,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = c0; c < c0 + kBN / 2; c += 32) {
         float v[32];
         tmemLoad32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c, v);
-        storeChunk<GELU>(v, row, n0 + c, M, N, bias, pre, act);
+        epilogueChunk<GELU>(v, lane, m0 + quarter * 32, n0 + c, M, N, bias, &mapPre, &mapAct,
+                            bufPre, bufAct, hasPre != 0);
       }
     }
+    epilogueDrain(lane);
   }
   fenceBeforeSync();
   __syncthreads();
@@ -340,8 +385,10 @@ template <bool GELU>
 __global__ void __launch_bounds__(kThreads, 1)
     gemmBiasActPersistentKernel(const __grid_constant__ CUtensorMap mapA,
                                 const __grid_constant__ CUtensorMap mapB,
-                                const uint16_t* __restrict__ bias, uint16_t* __restrict__ pre,
-                                uint16_t* __restrict__ act, int M, int N, int K) {
+                                const __grid_constant__ CUtensorMap mapPre,
+                                const __grid_constant__ CUtensorMap mapAct,
+                                const uint16_t* __restrict__ bias, int hasPre, int M, int N,
+                                int K) {
   __shared__ __align__(8) uint64_t sFull[kStages];
   __shared__ __align__(8) uint64_t sEmpty[kStages];
   __shared__ __align__(8) uint64_t sAccFull[2];
@@ -352,6 +399,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t dsmem[];
   const uint32_t base = (smemAddr(dsmem) + 1023u) & ~1023u;
   const uint32_t stageA0 = base, stageB0 = base + kStages * kStageA;
+  const uint32_t epi0 = base + kStages * (kStageA + kStageB);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tilesN = (N + kBN - 1) / kBN;
@@ -428,6 +476,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Epilogue: TMEM lane quarter warp % 4, column half (warp - 2) / 4.
     const int quarter = warp & 3;
     const int c0 = ((warp - 2) >> 2) * (kBN / 2);
+    const uint32_t bufPre = epi0 + (uint32_t)(warp - 2) * kEpiBuf, bufAct = bufPre + kEpiBuf / 2;
     uint32_t local = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++local) {
       const uint32_t b = local & 1u, use = local >> 1;
@@ -435,7 +484,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!__all_sync(0xffffffffu, ready)) break;
       fenceAfterSync();
       const int m0 = (t / tilesN) * kBM, n0 = (t % tilesN) * kBN;
-      const int row = m0 + quarter * 32 + lane;
       const uint32_t acc = tmem + b * kTmemCols + ((uint32_t)(quarter * 32) << 16);
 #pragma unroll 1
       for (int c = c0; c < c0 + kBN / 2; c += 32) {
@@ -447,9 +495,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           if (lane == 0) mbarArrive(&sAccEmpty[b]);
         }
-        storeChunk<GELU>(v, row, n0 + c, M, N, bias, pre, act);
+        epilogueChunk<GELU>(v, lane, m0 + quarter * 32, n0 + c, M, N, bias, &mapPre, &mapAct,
+                            bufPre, bufAct, hasPre != 0);
       }
     }
+    epilogueDrain(lane);
   }
   fenceBeforeSync();
   __syncthreads();
@@ -490,7 +540,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 constexpr int kPairBM = 256;
 constexpr int kPairStages = 6;
 constexpr uint32_t kHalf = 128 * kBK * 2;  // 16 KiB: 128 rows x 64 K of bf16
-constexpr uint32_t kPairSmemBytes = kPairStages * 2 * kHalf + 1024;
+constexpr uint32_t kPairSmemBytes = kPairStages * 2 * kHalf + kEpiBytes + 1024;
 
 __device__ __forceinline__ uint32_t clusterRank() {
   uint32_t r;
@@ -552,8 +602,9 @@ template <bool GELU>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemmBiasActPairKernel(const __grid_constant__ CUtensorMap mapA,
                           const __grid_constant__ CUtensorMap mapB,
-                          const uint16_t* __restrict__ bias, uint16_t* __restrict__ pre,
-                          uint16_t* __restrict__ act, int M, int N, int K) {
+                          const __grid_constant__ CUtensorMap mapPre,
+                          const __grid_constant__ CUtensorMap mapAct,
+                          const uint16_t* __restrict__ bias, int hasPre, int M, int N, int K) {
   __shared__ __align__(8) uint64_t sFull[kPairStages];
   __shared__ __align__(8) uint64_t sEmpty[kPairStages];
   __shared__ __align__(8) uint64_t sAccFull[2];
@@ -564,6 +615,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t dsmem[];
   const uint32_t base = (smemAddr(dsmem) + 1023u) & ~1023u;
   const uint32_t stageA0 = base, stageB0 = base + kPairStages * kHalf;
+  const uint32_t epi0 = base + kPairStages * 2 * kHalf;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = clusterRank();
@@ -655,6 +707,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // quarter warp % 4, column half (warp - 2) / 4.
     const int quarter = warp & 3;
     const int c0 = ((warp - 2) >> 2) * 128;
+    const uint32_t bufPre = epi0 + (uint32_t)(warp - 2) * kEpiBuf, bufAct = bufPre + kEpiBuf / 2;
     uint32_t local = 0;
     for (int t = pair; t < tiles; t += pairs, ++local) {
       const uint32_t b = local & 1u, use = local >> 1;
@@ -662,7 +715,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if (!__all_sync(0xffffffffu, ready)) break;
       fenceAfterSync();
       const int m0 = (t / tilesN) * kPairBM + (int)rank * 128, n0 = (t % tilesN) * 256;
-      const int row = m0 + quarter * 32 + lane;
       const uint32_t acc = tmem + b * kTmemCols + ((uint32_t)(quarter * 32) << 16);
 #pragma unroll 1
       for (int c = c0; c < c0 + 128; c += 32) {
@@ -673,9 +725,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           __syncwarp();
           if (lane == 0) mbarArriveRemote(inLeader(&sAccEmpty[b]));
         }
-        storeChunk<GELU>(v, row, n0 + c, M, N, bias, pre, act);
+        epilogueChunk<GELU>(v, lane, m0 + quarter * 32, n0 + c, M, N, bias, &mapPre, &mapAct,
+                            bufPre, bufAct, hasPre != 0);
       }
     }
+    epilogueDrain(lane);
   }
   fenceBeforeSync();
   __syncthreads();
@@ -720,6 +774,31 @@ bool makeMap(CUtensorMap* map, const void* base, int rows, int K, int boxRows) {
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// [rows, cols] row-major bf16 output, box {32, 32} (one epilogue warp's
+// block), 64-byte swizzle, as the epilogue stages it.
+bool makeOutMap(CUtensorMap* map, const void* base, int rows, int cols) {
+  EncodeTiledFn fn = encodeTiled();
+  if (fn == nullptr) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  const cuuint32_t box[2] = {32, 32};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Output maps of pre and act; a missing output gets a copy of the other
+// map (never stored through: hasPre / GELU select the stores).
+bool makeOutMaps(CUtensorMap* mapPre, CUtensorMap* mapAct, const void* pre, const void* act,
+                 int M, int N) {
+  if (pre && !makeOutMap(mapPre, pre, M, N)) return false;
+  if (act && !makeOutMap(mapAct, act, M, N)) return false;
+  if (!pre) *mapPre = *mapAct;
+  if (!act) *mapAct = *mapPre;
+  return true;
+}
+
 template <bool GELU, bool PERSISTENT>
 int launchGemm(const void* x, const void* w, const void* bias, void* pre, void* act, int M, int N,
                int K, cudaStream_t stream) {
@@ -739,17 +818,19 @@ int launchGemm(const void* x, const void* w, const void* bias, void* pre, void* 
       return 3;
     done.fetch_or(bit, std::memory_order_acq_rel);
   }
-  CUtensorMap mapA, mapB;
-  if (!makeMap(&mapA, x, M, K, kBM) || !makeMap(&mapB, w, N, K, kBN)) return 4;
+  CUtensorMap mapA, mapB, mapPre, mapAct;
+  if (!makeMap(&mapA, x, M, K, kBM) || !makeMap(&mapB, w, N, K, kBN) ||
+      !makeOutMaps(&mapPre, &mapAct, pre, act, M, N))
+    return 4;
   const int tilesN = (N + kBN - 1) / kBN, tilesM = (M + kBM - 1) / kBM;
   dim3 grid((unsigned)tilesN, (unsigned)tilesM);
   if (PERSISTENT) {
     const int tiles = tilesN * tilesM, n = sms[dev & 63] > 0 ? sms[dev & 63] : 148;
     grid = dim3((unsigned)(tiles < n ? tiles : n));
   }
-  kernel<<<grid, kThreads, kSmemBytes, stream>>>(
-      mapA, mapB, static_cast<const uint16_t*>(bias), static_cast<uint16_t*>(pre),
-      static_cast<uint16_t*>(act), M, N, K);
+  kernel<<<grid, kThreads, kSmemBytes, stream>>>(mapA, mapB, mapPre, mapAct,
+                                                 static_cast<const uint16_t*>(bias),
+                                                 pre != nullptr ? 1 : 0, M, N, K);
   gLaunches.fetch_add(1, std::memory_order_relaxed);
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }
@@ -772,14 +853,16 @@ int launchGemmPair(const void* x, const void* w, const void* bias, void* pre, vo
     done.fetch_or(bit, std::memory_order_acq_rel);
   }
   // Each CTA of a pair loads 128 rows of A and 128 rows of B per K block.
-  CUtensorMap mapA, mapB;
-  if (!makeMap(&mapA, x, M, K, 128) || !makeMap(&mapB, w, N, K, 128)) return 4;
+  CUtensorMap mapA, mapB, mapPre, mapAct;
+  if (!makeMap(&mapA, x, M, K, 128) || !makeMap(&mapB, w, N, K, 128) ||
+      !makeOutMaps(&mapPre, &mapAct, pre, act, M, N))
+    return 4;
   const int tiles = ((N + 255) / 256) * ((M + kPairBM - 1) / kPairBM);
   const int pairs = (sms[dev & 63] > 0 ? sms[dev & 63] : 148) / 2;
   const unsigned grid = 2u * (unsigned)(tiles < pairs ? tiles : pairs);
-  kernel<<<grid, kThreads, kPairSmemBytes, stream>>>(
-      mapA, mapB, static_cast<const uint16_t*>(bias), static_cast<uint16_t*>(pre),
-      static_cast<uint16_t*>(act), M, N, K);
+  kernel<<<grid, kThreads, kPairSmemBytes, stream>>>(mapA, mapB, mapPre, mapAct,
+                                                     static_cast<const uint16_t*>(bias),
+                                                     pre != nullptr ? 1 : 0, M, N, K);
   gLaunches.fetch_add(1, std::memory_order_relaxed);
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }
