@@ -133,18 +133,21 @@ class _LinearBias(torch.autograd.Function):
         return gy @ w16, _wgrad(gy, x), _ops().bias_grad(gy)
 
 
-# TNCCL_TCGEN05_GEMM=1 / persistent / pair computes the forward of
-# linear_gelu with the tcgen05 GEMM (one tile per CTA / persistent / CTA
-# pairs) and its fused bias + GELU epilogue instead of cuBLAS and a separate
-# GELU kernel.
-_TCGEN05 = os.environ.get("TNCCL_TCGEN05_GEMM", "0")
+# The forward of linear_gelu runs this library's tcgen05 GEMM with its fused
+# bias + GELU epilogue: TNCCL_TCGEN05_GEMM=pair (default: persistent CTA
+# pairs, cta_group::2), persistent (one CTA per SM) or 1 (one tile per CTA);
+# 0 selects cuBLAS and a separate GELU kernel. The persistent variants
+# assume they get (nearly) every SM: in training they run in the forward
+# pass, when no gradient all-reduce is in flight.
+_TCGEN05 = os.environ.get("TNCCL_TCGEN05_GEMM", "pair")
 _TCGEN05_VARIANT = {"1": 0, "persistent": 1, "pair": 2}.get(_TCGEN05, 0)
 
 
 class _LinearGelu(torch.autograd.Function):
-    """y = GELU_tanh(x W^T + b). Backward: one kernel computes the GELU
-    gradient and the bias gradient (column sums of that gradient); dX and dW
-    on cuBLAS."""
+    """y = GELU_tanh(x W^T + b): one tcgen05 GEMM with the bias and GELU in
+    its epilogue (or cuBLAS + GELU with TNCCL_TCGEN05_GEMM=0). Backward: one
+    kernel computes the GELU gradient and the bias gradient (column sums of
+    that gradient); dX and dW on cuBLAS."""
 
     @staticmethod
     def forward(ctx, x, weight, bias):
