@@ -188,8 +188,8 @@ class DataParallelTrainer:
             d += "+registered"
         if self.overlap_optimizer:
             d += "+overlapped-adamw"
-        if os.environ.get("TNCCL_NVLS_ZERO_COPY") == "1":
-            d += "+nvls-zero-copy"
+        if self.registration is not None and self.comm.info().get("zero_copy_launches", 0) > 0:
+            d += "+nvls-zero-copy"  # some bucket all-reduces took the zero-copy kernel
         if self.cuda_graph:
             d += "+cuda-graph"
         return d
