@@ -20,10 +20,21 @@ namespace tnops {
 namespace {
 
 constexpr int kThreads = 512;
+constexpr int kUnroll = 4;  // 16-byte loads in flight per thread in each pass
 
 struct MaxSum {
   float m, s;
 };
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+// 2^x on the hardware approximation (PTX ex2.approx.ftz.f32); the exponent
+// arithmetic around it is folded into one FMA per element below.
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 __device__ __forceinline__ MaxSum combine(MaxSum a, MaxSum b) {
   const float m = fmaxf(a.m, b.m);
@@ -31,12 +42,22 @@ __device__ __forceinline__ MaxSum combine(MaxSum a, MaxSum b) {
   return {m, a.s * __expf(a.m - m) + b.s * __expf(b.m - m)};
 }
 
+__device__ __forceinline__ void unpack8(const uint4& u, float* v) {
+  v[0] = __uint_as_float(u.x << 16); v[1] = __uint_as_float(u.x & 0xffff0000u);
+  v[2] = __uint_as_float(u.y << 16); v[3] = __uint_as_float(u.y & 0xffff0000u);
+  v[4] = __uint_as_float(u.z << 16); v[5] = __uint_as_float(u.z & 0xffff0000u);
+  v[6] = __uint_as_float(u.w << 16); v[7] = __uint_as_float(u.w & 0xffff0000u);
+}
+
+// Running (max, sum of exp(v - max)) over n more values: exp(v - m) is
+// 2^(v log2e - m log2e), one FMA and one ex2 per value.
 __device__ __forceinline__ void accumulate(MaxSum& st, const float* v, int n) {
   float lm = v[0];
   for (int i = 1; i < n; ++i) lm = fmaxf(lm, v[i]);
   const float m = fmaxf(st.m, lm);
-  float s = st.m == -INFINITY ? 0.f : st.s * __expf(st.m - m);
-  for (int i = 0; i < n; ++i) s += __expf(v[i] - m);
+  const float nm = -m * kLog2e;
+  float s = st.m == -INFINITY ? 0.f : st.s * ex2(fmaf(st.m, kLog2e, nm));
+  for (int i = 0; i < n; ++i) s += ex2(fmaf(v[i], kLog2e, nm));
   st = {m, s};
 }
 
@@ -59,13 +80,21 @@ __global__ void __launch_bounds__(kThreads)
   if (threadIdx.x == 0) sTarget = (tgt >= 0 && tgt < V) ? bf2f(row[tgt]) : 0.f;
 
   MaxSum st{-INFINITY, 0.f};
-  for (int i = threadIdx.x; i < nvec; i += kThreads) {
-    const uint4 u = body[i];
+  // kUnroll vectors per thread per step: their loads are all issued before
+  // any is used, and one (max, sum) update covers 32 values.
+  int i0 = threadIdx.x;
+  for (; i0 + (kUnroll - 1) * kThreads < nvec; i0 += kUnroll * kThreads) {
+    uint4 u[kUnroll];
+#pragma unroll
+    for (int j = 0; j < kUnroll; ++j) u[j] = body[i0 + j * kThreads];  // stays in L2 for pass 2
+    float v[8 * kUnroll];
+#pragma unroll
+    for (int j = 0; j < kUnroll; ++j) unpack8(u[j], v + 8 * j);
+    accumulate(st, v, 8 * kUnroll);
+  }
+  for (int i = i0; i < nvec; i += kThreads) {
     float v[8];
-    v[0] = __uint_as_float(u.x << 16); v[1] = __uint_as_float(u.x & 0xffff0000u);
-    v[2] = __uint_as_float(u.y << 16); v[3] = __uint_as_float(u.y & 0xffff0000u);
-    v[4] = __uint_as_float(u.z << 16); v[5] = __uint_as_float(u.z & 0xffff0000u);
-    v[6] = __uint_as_float(u.w << 16); v[7] = __uint_as_float(u.w & 0xffff0000u);
+    unpack8(body[i], v);
     accumulate(st, v, 8);
   }
   for (int i = threadIdx.x; i < head; i += kThreads) {
@@ -95,36 +124,49 @@ __global__ void __launch_bounds__(kThreads)
   }
   __syncthreads();
   const float M = sAll.m;
-  const float invS = 1.0f / sAll.s;
   const bool valid = tgt >= 0 && tgt < V;
   if (threadIdx.x == 0) loss[r] = valid ? (logf(sAll.s) + M - sTarget) : 0.f;
   const float scale = valid ? invValid : 0.f;
+  // p * scale = 2^(a log2e + nb) with nb = -(M log2e + log2 S) + log2 scale;
+  // the target column subtracts scale (softmax minus one-hot, scaled).
+  const float nb = valid ? -(M * kLog2e) - __log2f(sAll.s) + __log2f(invValid) : 0.f;
   // Pass 2: gradient in place.
   uint4* wbody = reinterpret_cast<uint4*>(row + head);
-  for (int i = threadIdx.x; i < nvec; i += kThreads) {
-    const uint4 u = wbody[i];
+  auto grad8 = [&](const uint4& u, int i) {
     const int e0 = head + i * 8;
-    uint32_t in[4] = {u.x, u.y, u.z, u.w};
+    const uint32_t in[4] = {u.x, u.y, u.z, u.w};
     uint32_t out[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const float a = __uint_as_float(in[k] << 16), b = __uint_as_float(in[k] & 0xffff0000u);
-      float pa = __expf(a - M) * invS, pb = __expf(b - M) * invS;
-      if (e0 + 2 * k == tgt) pa -= 1.f;
-      if (e0 + 2 * k + 1 == tgt) pb -= 1.f;
-      out[k] = (uint32_t)f2bf(pa * scale) | ((uint32_t)f2bf(pb * scale) << 16);
+      float pa = valid ? ex2(fmaf(a, kLog2e, nb)) : 0.f;
+      float pb = valid ? ex2(fmaf(b, kLog2e, nb)) : 0.f;
+      if (e0 + 2 * k == tgt) pa -= scale;
+      if (e0 + 2 * k + 1 == tgt) pb -= scale;
+      __nv_bfloat162 h = __floats2bfloat162_rn(pa, pb);
+      out[k] = *reinterpret_cast<uint32_t*>(&h);
     }
-    wbody[i] = make_uint4(out[0], out[1], out[2], out[3]);
+    return make_uint4(out[0], out[1], out[2], out[3]);
+  };
+  i0 = threadIdx.x;
+  for (; i0 + (kUnroll - 1) * kThreads < nvec; i0 += kUnroll * kThreads) {
+    uint4 u[kUnroll];
+#pragma unroll
+    for (int j = 0; j < kUnroll; ++j) u[j] = wbody[i0 + j * kThreads];
+#pragma unroll
+    for (int j = 0; j < kUnroll; ++j)
+      __stcs(wbody + i0 + j * kThreads, grad8(u[j], i0 + j * kThreads));
   }
+  for (int i = i0; i < nvec; i += kThreads) wbody[i] = grad8(wbody[i], i);
   for (int i = threadIdx.x; i < head; i += kThreads) {
-    float p = __expf(bf2f(row[i]) - M) * invS;
-    if (i == tgt) p -= 1.f;
-    row[i] = f2bf(p * scale);
+    float p = valid ? ex2(fmaf(bf2f(row[i]), kLog2e, nb)) : 0.f;
+    if (i == tgt) p -= scale;
+    row[i] = f2bf(p);
   }
   for (int i = bodyEnd + threadIdx.x; i < V; i += kThreads) {
-    float p = __expf(bf2f(row[i]) - M) * invS;
-    if (i == tgt) p -= 1.f;
-    row[i] = f2bf(p * scale);
+    float p = valid ? ex2(fmaf(bf2f(row[i]), kLog2e, nb)) : 0.f;
+    if (i == tgt) p -= scale;
+    row[i] = f2bf(p);
   }
   for (int i = V + threadIdx.x; i < ld; i += kThreads) row[i] = 0;
 }
