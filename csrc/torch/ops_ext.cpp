@@ -57,7 +57,9 @@ std::vector<at::Tensor> lnFwd(const at::Tensor& x, const c10::optional<at::Tenso
 
 std::vector<at::Tensor> lnBwd(const at::Tensor& gy, const c10::optional<at::Tensor>& gres,
                               const at::Tensor& xo, const at::Tensor& w, const at::Tensor& mean,
-                              const at::Tensor& rstd, bool wantBf16) {
+                              const at::Tensor& rstd, bool wantBf16,
+                              const c10::optional<at::Tensor>& dwOut,
+                              const c10::optional<at::Tensor>& dbOut) {
   need(gy, at::kBFloat16, "grad_y");
   need(xo, at::kFloat, "x_out");
   need(w, at::kFloat, "weight");
@@ -68,8 +70,13 @@ std::vector<at::Tensor> lnBwd(const at::Tensor& gy, const c10::optional<at::Tens
   auto dx = at::empty_like(xo);
   at::Tensor dxb;
   if (wantBf16) dxb = at::empty(xo.sizes(), xo.options().dtype(at::kBFloat16));
-  auto dw = at::empty({C}, xo.options());
-  auto db = at::empty({C}, xo.options());
+  // dw / db go to the caller's tensors when given (e.g. the parameters'
+  // slices of a flat gradient buffer), so that no copy follows.
+  auto dw = dwOut ? *dwOut : at::empty({C}, xo.options());
+  auto db = dbOut ? *dbOut : at::empty({C}, xo.options());
+  need(dw, at::kFloat, "dw_out");
+  need(db, at::kFloat, "db_out");
+  TORCH_CHECK(dw.numel() == C && db.numel() == C, "ln_bwd: dw_out / db_out need C elements");
   auto partial = at::empty({(int64_t)tnops_ln_partial_rows() * 2 * C}, xo.options());
   ok(tnops_ln_bwd(bf(gy), gres ? gres->data_ptr<float>() : nullptr, xo.data_ptr<float>(),
                   w.data_ptr<float>(), mean.data_ptr<float>(), rstd.data_ptr<float>(),
@@ -100,12 +107,14 @@ at::Tensor crossEntropy(at::Tensor logits, const at::Tensor& target, int64_t val
 }
 
 // g bf16 [M, N] -> db fp32 [N] (column sums)
-at::Tensor biasGrad(const at::Tensor& g) {
+at::Tensor biasGrad(const at::Tensor& g, const c10::optional<at::Tensor>& out) {
   need(g, at::kBFloat16, "grad");
   TORCH_CHECK(g.dim() == 2 && g.size(1) % 8 == 0, "bias_grad: want [M, N] with N % 8 == 0");
   c10::cuda::CUDAGuard guard(g.device());
   const int M = (int)g.size(0), N = (int)g.size(1);
-  auto db = at::empty({N}, g.options().dtype(at::kFloat));
+  auto db = out ? *out : at::empty({N}, g.options().dtype(at::kFloat));
+  need(db, at::kFloat, "out");
+  TORCH_CHECK(db.numel() == N, "bias_grad: out needs N elements");
   auto part = at::empty({(int64_t)tnops_colsum_parts(M, N) * N}, g.options().dtype(at::kFloat));
   ok(tnops_bias_grad(bf(g), db.data_ptr<float>(), part.data_ptr<float>(), M, N, streamOf(g)),
      "tnops_bias_grad");
@@ -140,7 +149,8 @@ std::vector<at::Tensor> gemmBiasAct(const at::Tensor& x, const at::Tensor& w,
 }
 
 // gy, pre bf16 [M, N] -> (gpre bf16 [M, N], db fp32 [N])
-std::vector<at::Tensor> geluBwdBias(const at::Tensor& gy, const at::Tensor& pre) {
+std::vector<at::Tensor> geluBwdBias(const at::Tensor& gy, const at::Tensor& pre,
+                                    const c10::optional<at::Tensor>& dbOut) {
   need(gy, at::kBFloat16, "grad_y");
   need(pre, at::kBFloat16, "pre");
   TORCH_CHECK(gy.dim() == 2 && gy.sizes() == pre.sizes() && gy.size(1) % 8 == 0,
@@ -148,7 +158,9 @@ std::vector<at::Tensor> geluBwdBias(const at::Tensor& gy, const at::Tensor& pre)
   c10::cuda::CUDAGuard guard(gy.device());
   const int M = (int)gy.size(0), N = (int)gy.size(1);
   auto gpre = at::empty_like(gy);
-  auto db = at::empty({N}, gy.options().dtype(at::kFloat));
+  auto db = dbOut ? *dbOut : at::empty({N}, gy.options().dtype(at::kFloat));
+  need(db, at::kFloat, "db_out");
+  TORCH_CHECK(db.numel() == N, "gelu_bwd_bias: db_out needs N elements");
   auto part = at::empty({(int64_t)tnops_colsum_parts(M, N) * N}, gy.options().dtype(at::kFloat));
   ok(tnops_gelu_bwd_bias(bf(gy), bf(pre), bf(gpre), db.data_ptr<float>(), part.data_ptr<float>(),
                          M, N, streamOf(gy)),
@@ -223,11 +235,13 @@ void registerOps(py::module_& m) {
   ops.def("ln_fwd", &lnFwd, py::arg("x"), py::arg("delta"), py::arg("weight"), py::arg("bias"),
           py::arg("eps"));
   ops.def("ln_bwd", &lnBwd, py::arg("grad_y"), py::arg("grad_residual"), py::arg("x_out"),
-          py::arg("weight"), py::arg("mean"), py::arg("rstd"), py::arg("want_bf16"));
+          py::arg("weight"), py::arg("mean"), py::arg("rstd"), py::arg("want_bf16"),
+          py::arg("dw_out") = py::none(), py::arg("db_out") = py::none());
   ops.def("cross_entropy_fwd_bwd", &crossEntropy, py::arg("logits"), py::arg("target"),
           py::arg("valid"), py::arg("classes") = 0);
-  ops.def("bias_grad", &biasGrad, py::arg("grad"));
-  ops.def("gelu_bwd_bias", &geluBwdBias, py::arg("grad_y"), py::arg("pre"));
+  ops.def("bias_grad", &biasGrad, py::arg("grad"), py::arg("out") = py::none());
+  ops.def("gelu_bwd_bias", &geluBwdBias, py::arg("grad_y"), py::arg("pre"),
+          py::arg("db_out") = py::none());
   ops.def("gemm_bias_act", &gemmBiasAct, py::arg("x"), py::arg("weight"), py::arg("bias"),
           py::arg("gelu"), py::arg("persistent") = 0);
   ops.def("tcgen05_status", [](bool reset) { return tnops_tcgen05_status(reset ? 1 : 0); },

@@ -59,6 +59,11 @@ def main():
         x = torch.randn(8, 16, generator=g)
         net_a(x).pow(2).mean().backward()
         red.finish()
+        # After every backward each .grad is its slice of the flat buffer
+        # (zero_grad unsets them; the gradients land in the slices again).
+        ptr = red.flat.data_ptr()
+        ok = ok and all(p.grad is not None and ptr <= p.grad.data_ptr() < ptr + red.flat.numel() * 4
+                        for p in net_a.parameters())
         ddp(x).pow(2).mean().backward()
         net_c(x).pow(2).mean().backward()  # updated bucket by bucket inside backward
         red_c.finish()
@@ -76,10 +81,6 @@ def main():
         red.zero_grad()
         net_b.zero_grad(set_to_none=True)
     ok = ok and red.launched == 3 * len(red.buckets)
-    # The .grad views still point into the flat buffer after the steps.
-    ptr = red.flat.data_ptr()
-    ok = ok and all(ptr <= p.grad.data_ptr() < ptr + red.flat.numel() * 4
-                    for p in net_a.parameters())
     for pa, pb in zip(net_a.parameters(), net_b.parameters()):
         ok = ok and torch.allclose(pa, pb, rtol=1e-6, atol=1e-7)
     for pa, pc in zip(net_a.parameters(), net_c.parameters()):

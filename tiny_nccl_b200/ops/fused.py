@@ -31,6 +31,7 @@ class _AddLayerNorm(torch.autograd.Function):
         d2 = delta.reshape(-1, C) if delta is not None else None
         x_out, y, mean, rstd = _ops().ln_fwd(x2, d2, weight, bias, eps)
         ctx.save_for_backward(x_out, weight, mean, rstd)
+        ctx.params = (weight, bias)
         ctx.has_delta = delta is not None
         ctx.shape = x.shape
         return x_out.view(x.shape), y.view(x.shape)
@@ -42,8 +43,10 @@ class _AddLayerNorm(torch.autograd.Function):
         if g_y is None:
             g_y = torch.zeros(x_out.shape, dtype=torch.bfloat16, device=x_out.device)
         gres = g_xout.reshape(-1, C).contiguous() if g_xout is not None else None
+        pw, pb = ctx.params
         dx, dxb, dw, db = _ops().ln_bwd(g_y.reshape(-1, C).contiguous(), gres, x_out, weight,
-                                        mean, rstd, ctx.has_delta)
+                                        mean, rstd, ctx.has_delta,
+                                        grad_destination(pw), grad_destination(pb))
         ddelta = dxb.view(ctx.shape) if ctx.has_delta else None
         return dx.view(ctx.shape), ddelta, dw, db, None
 
@@ -107,9 +110,26 @@ def bf16_weight(p: torch.Tensor) -> torch.Tensor:
     return p.to(torch.bfloat16)
 
 
-def _wgrad(gy: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+def grad_destination(p: torch.Tensor):
+    """Where the gradient of parameter p can be written directly: its slice
+    of a flat gradient buffer (FlatGradReducer sets ``p._tn_grad_dest``), as
+    long as p has no gradient yet in this backward. The backward functions
+    below write their parameter gradients there and return that slice, which
+    autograd then adopts as ``p.grad`` as it is (no copy, no accumulation
+    kernel). None otherwise: a new tensor is returned and autograd handles it
+    as usual."""
+    d = getattr(p, "_tn_grad_dest", None)
+    # A new tensor object on the same memory: autograd adopts a gradient
+    # without copying only when nothing else holds the object.
+    return d.detach() if d is not None and p.grad is None else None
+
+
+def _wgrad(gy: torch.Tensor, x: torch.Tensor, dest: torch.Tensor | None = None) -> torch.Tensor:
     """dW = gy^T x with bf16 operands and the fp32 result written by the GEMM
-    itself (no bf16 rounding, no separate cast to the fp32 parameter)."""
+    itself (no bf16 rounding, no separate cast to the fp32 parameter),
+    into ``dest`` when given."""
+    if dest is not None:
+        return torch.mm(gy.t(), x, out_dtype=torch.float32, out=dest)
     return torch.mm(gy.t(), x, out_dtype=torch.float32)
 
 
@@ -124,13 +144,16 @@ class _LinearBias(torch.autograd.Function):
         with torch.autocast("cuda", enabled=False):
             y = torch.addmm(bf16_weight(bias), x, w16.t())
         ctx.save_for_backward(x, w16)
+        ctx.params = (weight, bias)
         return y
 
     @staticmethod
     def backward(ctx, gy):
         x, w16 = ctx.saved_tensors
+        pw, pb = ctx.params
         gy = gy.contiguous()
-        return gy @ w16, _wgrad(gy, x), _ops().bias_grad(gy)
+        return (gy @ w16, _wgrad(gy, x, grad_destination(pw)),
+                _ops().bias_grad(gy, out=grad_destination(pb)))
 
 
 # The forward of linear_gelu runs this library's tcgen05 GEMM with its fused
@@ -160,13 +183,15 @@ class _LinearGelu(torch.autograd.Function):
                 pre = torch.addmm(b16, x, w16.t())
                 y = torch.nn.functional.gelu(pre, approximate="tanh")
         ctx.save_for_backward(x, w16, pre)
+        ctx.params = (weight, bias)
         return y
 
     @staticmethod
     def backward(ctx, gy):
         x, w16, pre = ctx.saved_tensors
-        gpre, db = _ops().gelu_bwd_bias(gy.contiguous(), pre)
-        return gpre @ w16, _wgrad(gpre, x), db
+        pw, pb = ctx.params
+        gpre, db = _ops().gelu_bwd_bias(gy.contiguous(), pre, grad_destination(pb))
+        return gpre @ w16, _wgrad(gpre, x, grad_destination(pw)), db
 
 
 class _LinearNoBias(torch.autograd.Function):
@@ -179,13 +204,14 @@ class _LinearNoBias(torch.autograd.Function):
         with torch.autocast("cuda", enabled=False):
             y = torch.mm(x, w16.t())
         ctx.save_for_backward(x, w16)
+        ctx.weight = weight
         return y
 
     @staticmethod
     def backward(ctx, gy):
         x, w16 = ctx.saved_tensors
         gy = gy.contiguous()
-        return gy @ w16, _wgrad(gy, x)
+        return gy @ w16, _wgrad(gy, x, grad_destination(ctx.weight))
 
 
 def _rows(x: torch.Tensor) -> torch.Tensor:

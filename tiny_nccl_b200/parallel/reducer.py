@@ -41,8 +41,10 @@ class FlatGradReducer:
 
     ``all_reduce(t)`` must average ``t`` in place over the ranks (it is called
     on ``stream`` when one is given). Call :meth:`finish` after every
-    backward and before the optimizer step, and :meth:`zero_grad` instead of
-    the optimizer's ``zero_grad`` (the ``.grad`` views must stay in place).
+    backward and before the optimizer step, and :meth:`zero_grad` after the
+    step: it unsets every ``.grad``, and the next backward puts each one back
+    as its slice of the flat buffer (written there directly by the fused
+    backward kernels, copied there from any other op).
     """
 
     def __init__(self, params: Iterable[torch.nn.Parameter],
@@ -80,9 +82,15 @@ class FlatGradReducer:
         self.buckets = buckets
         self.params = order
         self._bucket_of = {}
+        self._views = {}
         self._need = [0] * len(buckets)
         for p, o, b in zip(order, offsets, bucket_of):
-            p.grad = self.flat[o:o + p.numel()].view_as(p)
+            view = self.flat[o:o + p.numel()].view_as(p)
+            p.grad = view
+            # The fused backward kernels write p's gradient straight into
+            # this slice while p.grad is unset (ops.fused.grad_destination).
+            p._tn_grad_dest = view
+            self._views[id(p)] = view
             self._bucket_of[id(p)] = b
             self._need[b] += 1
         self.bucket_params = [[] for _ in buckets]
@@ -93,11 +101,21 @@ class FlatGradReducer:
         self._stream = stream
         self._pending = list(self._need)
         self._next = 0  # first bucket not launched yet
+        self._fired = set()
         self.launched = 0
         self._hooks = [p.register_post_accumulate_grad_hook(self._ready) for p in order]
 
     # -- hooks ----------------------------------------------------------------
     def _ready(self, p: torch.Tensor) -> None:
+        # After zero_grad() the gradient arrives in one of two ways: written
+        # into p's slice by a fused backward kernel (adopted as it is), or as
+        # a new tensor from any other op, which goes into the slice here.
+        view = self._views[id(p)]
+        g = p.grad
+        if g.data_ptr() != view.data_ptr() or g.stride() != view.stride():
+            view.copy_(g)
+            p.grad = view
+        self._fired.add(id(p))
         b = self._bucket_of[id(p)]
         self._pending[b] -= 1
         while self._next < len(self.buckets) and self._pending[self._next] == 0:
@@ -124,6 +142,11 @@ class FlatGradReducer:
         """Launches the buckets still waiting (parameters that got no gradient
         this step), makes the current stream wait for every all-reduce and
         re-arms the counters for the next backward."""
+        for p in self.params:  # no gradient this step: its slice holds zeros
+            if id(p) not in self._fired:
+                view = self._views[id(p)]
+                view.zero_()
+                p.grad = view
         while self._next < len(self.buckets):
             self._launch(self._next)
             self._next += 1
@@ -131,11 +154,19 @@ class FlatGradReducer:
             torch.cuda.current_stream(self.flat.device).wait_stream(self._stream)
         self._pending = list(self._need)
         self._next = 0
+        self._fired = set()
 
     def zero_grad(self) -> None:
-        self.flat.zero_()
+        """Unsets every ``.grad`` (no kernel): the next backward writes each
+        gradient into its slice of the flat buffer instead of adding it to
+        a zeroed one."""
+        for p in self.params:
+            p.grad = None
 
     def remove(self) -> None:
         for h in self._hooks:
             h.remove()
         self._hooks = []
+        for p in self.params:
+            if getattr(p, "_tn_grad_dest", None) is self._views[id(p)]:
+                del p._tn_grad_dest
