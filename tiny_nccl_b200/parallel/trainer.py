@@ -22,7 +22,8 @@ bucket's parameters on the communication stream right after its all-reduce.
 
 ``reducer="ddp"`` (``TNCCL_DP_REDUCER=ddp``): DistributedDataParallel with
 the tnccl comm hook, eager (DDP's reducer runs host logic during backward
-that a graph replay would skip).
+that a graph replay would skip). ``reducer="nccl-ddp"``: the same with DDP's
+own NCCL all-reduce, the control that isolates the collective.
 """
 from __future__ import annotations
 
@@ -103,14 +104,18 @@ class DataParallelTrainer:
                 self.registration = comm.register(self.reducer.flat)
             self.ddp = model
             self.hook_state = None
-        elif reducer == "ddp":
+        elif reducer in ("ddp", "nccl-ddp"):
             self.ddp = DDP(model, device_ids=[dev.index], output_device=dev.index,
                            bucket_cap_mb=bucket_cap_mb, gradient_as_bucket_view=True,
                            static_graph=True, broadcast_buffers=False)
-            self.hook_state = register_tnccl_hook(self.ddp, comm, algo=algo,
-                                                  wire_dtype=wire_dtype)
+            # "nccl-ddp" keeps DDP's own NCCL all-reduce: the control that
+            # isolates the collective (same model, same buckets, same steps).
+            self.hook_state = (register_tnccl_hook(self.ddp, comm, algo=algo,
+                                                   wire_dtype=wire_dtype)
+                               if reducer == "ddp" else None)
         else:
-            raise ValueError(f"reducer must be 'ddp' or 'flat', not {reducer!r}")
+            raise ValueError(f"reducer must be 'flat', 'ddp' or 'nccl-ddp', not {reducer!r}")
+        self.reducer_name = reducer
 
     def step(self, idx: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
         """One optimizer step; returns the (device) loss without synchronizing."""
@@ -183,7 +188,7 @@ class DataParallelTrainer:
 
     def describe(self) -> str:
         """The gradient path and step execution in use, e.g. 'flat+cuda-graph'."""
-        d = "flat" if self.reducer is not None else "ddp"
+        d = "flat" if self.reducer is not None else self.reducer_name
         if self.registration is not None:
             d += "+registered"
         if self.overlap_optimizer:
