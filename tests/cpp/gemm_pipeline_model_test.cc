@@ -1,6 +1,9 @@
 // gemm_pipeline_model_test.cc - threaded CPU model of the synchronisation of
-// the tcgen05 GEMM kernels (csrc/ops/gemm_tcgen05.cu): one CTA per tile and
-// the persistent kernel with two TMEM accumulators.
+// the tcgen05 GEMM kernels (csrc/ops/gemm_tcgen05.cu): one CTA per tile, the
+// persistent kernel with two TMEM accumulators, and the persistent CTA pair
+// (cta_group::2: the even CTA's full barrier armed for both CTAs' bytes and
+// completed by both CTAs' loads, commits multicast to both CTAs' empty and
+// accFull barriers, accEmpty collecting both CTAs' epilogue warps).
 //
 // The roles run as threads with the kernels' loop structure and parity
 // formulas: the TMA producer, the MMA issuer and eight epilogue warps. An
@@ -258,6 +261,125 @@ Result runPersistent(int tiles, int kBlocks, int seed, int stopAt = -1) {
   return res;
 }
 
+// The CTA-pair kernel (gemmBiasActPairKernel) for one pair that owns `tiles`
+// tiles. Barriers per CTA r; only CTA 0's full and accEmpty barriers are used.
+Result runPair(int tiles, int kBlocks, int seed) {
+  constexpr int kPairStages = 6;
+  constexpr long kHalfBytes = 2 * 16 * 1024;  // one CTA's A and B halves per K block
+  MBarrier full[2][kPairStages], empty[2][kPairStages], accFull[2][2], accEmpty[2][2], done;
+  for (int r = 0; r < 2; ++r) {
+    for (int s = 0; s < kPairStages; ++s) {
+      full[r][s].init(1);
+      empty[r][s].init(1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      accFull[r][b].init(1);
+      accEmpty[r][b].init(2 * kEpiWarps);
+    }
+  }
+  done.init(1);
+  std::atomic<int> abort{0};
+  std::atomic<long> stage[2][kPairStages];
+  std::atomic<long> accTile[2][2], accBlocks[2][2];
+  for (auto& cta : stage)
+    for (auto& x : cta) x = -1;
+  for (int r = 0; r < 2; ++r)
+    for (int b = 0; b < 2; ++b) accTile[r][b] = accBlocks[r][b] = -1;
+  std::atomic<bool> bad{false};
+  std::vector<std::atomic<int>> storedCount((size_t)tiles * 2);
+  for (auto& c : storedCount) c = 0;
+  Result res;
+  {
+    Engine tma0(seed * 7 + 1, 30), tma1(seed * 7 + 3, 30), mmaUnit(seed * 7 + 2, 20);
+    Engine* tmaOf[2] = {&tma0, &tma1};
+    std::vector<std::thread> threads;
+    for (int r = 0; r < 2; ++r) {
+      threads.emplace_back([&, r] {  // producer of CTA r
+        std::mt19937 g((unsigned)(seed + 17 * r));
+        unsigned gk = 0;
+        for (int t = 0; t < tiles && !abort.load(); ++t) {
+          for (int kb = 0; kb < kBlocks; ++kb, ++gk) {
+            const unsigned s = gk % kPairStages, round = gk / kPairStages;
+            if (!waitBar(empty[r][s], (round & 1u) ^ 1u, abort)) break;
+            if (r == 0) full[0][s].arriveExpectTx(2 * kHalfBytes);  // both CTAs' bytes
+            const long tag = (long)t * 1000 + kb;
+            // This CTA's loads land in its own stage and complete on CTA 0's barrier.
+            tmaOf[r]->push([&, r, s, tag] {
+              stage[r][s].store(tag);
+              full[0][s].completeTx(kHalfBytes);
+            });
+            jitter(g, 5);
+          }
+        }
+      });
+    }
+    threads.emplace_back([&] {  // MMA issuer, CTA 0
+      std::mt19937 g((unsigned)seed + 1);
+      unsigned gk = 0, local = 0;
+      for (int t = 0; t < tiles && !abort.load(); ++t, ++local) {
+        const unsigned b = local & 1u, use = local >> 1;
+        if (!waitBar(accEmpty[0][b], (use & 1u) ^ 1u, abort)) break;
+        bool ok = true;
+        for (int kb = 0; kb < kBlocks; ++kb, ++gk) {
+          const unsigned s = gk % kPairStages;
+          if (!(ok = waitBar(full[0][s], (gk / kPairStages) & 1u, abort))) break;
+          const long want = (long)t * 1000 + kb;
+          mmaUnit.push([&, s, b, t, kb, want] {
+            // The pair MMA reads both CTAs' stages and writes both TMEMs.
+            if (stage[0][s].load() != want || stage[1][s].load() != want) bad = true;
+            for (int r = 0; r < 2; ++r) {
+              if (kb == 0) {
+                accTile[r][b] = t;
+                accBlocks[r][b] = 1;
+              } else {
+                if (accTile[r][b].load() != t) bad = true;
+                accBlocks[r][b].fetch_add(1);
+              }
+            }
+          });
+          mmaUnit.push([&, s] {  // commit multicast to the pair
+            empty[0][s].arrive();
+            empty[1][s].arrive();
+          });
+          jitter(g, 5);
+        }
+        if (!ok) break;
+        mmaUnit.push([&, b] {
+          accFull[0][b].arrive();
+          accFull[1][b].arrive();
+        });
+      }
+      mmaUnit.push([&] { done.arrive(); });
+      if (abort.load()) waitBar(done, 0, abort, true);
+    });
+    for (int r = 0; r < 2; ++r)
+      for (int w = 0; w < kEpiWarps; ++w)
+        threads.emplace_back([&, r, w] {  // epilogue warps of CTA r
+          std::mt19937 g((unsigned)(seed * 13 + 100 * r + w));
+          unsigned local = 0;
+          for (int t = 0; t < tiles; ++t, ++local) {
+            const unsigned b = local & 1u, use = local >> 1;
+            if (!waitBar(accFull[r][b], use & 1u, abort)) break;
+            for (int c = 0; c < 4; ++c) {
+              if (accTile[r][b].load() != t || accBlocks[r][b].load() != kBlocks) bad = true;
+              jitter(g, 3);
+            }
+            accEmpty[0][b].arrive();  // remote for CTA 1
+            jitter(g, 10);
+            if (w == 0) storedCount[(size_t)t * 2 + r].fetch_add(1);
+          }
+        });
+    for (auto& th : threads) th.join();
+    res.aborted = abort.load() != 0;
+  }
+  for (auto& c : storedCount) {
+    if (c.load() == 1) ++res.stored;
+    if (c.load() > 1) res.ok = false;
+  }
+  res.ok = res.ok && !bad.load();
+  return res;
+}
+
 // The one-tile kernel (gemmBiasActKernel): one accumulator, one commit.
 Result runSingle(int kBlocks, int seed) {
   MBarrier full[kStages], empty[kStages], accum;
@@ -339,6 +461,19 @@ int main() {
         }
       }
   report("persistent kernel: stage ring across tiles, two accumulators", ok);
+
+  ok = true;
+  for (int seed = 0; seed < 15 && ok; ++seed)
+    for (int tiles : {1, 2, 5})
+      for (int kBlocks : {1, 4, 7, 12}) {
+        Result r = runPair(tiles, kBlocks, seed);
+        if (!(r.ok && !r.aborted && r.stored == 2 * tiles)) {
+          printf("  pair seed %d tiles %d kBlocks %d: ok %d aborted %d stored %d\n", seed, tiles,
+                 kBlocks, r.ok, r.aborted, r.stored);
+          ok = false;
+        }
+      }
+  report("CTA pair: shared full barrier, multicast commits, accEmpty x2", ok);
 
   ok = true;
   for (int seed = 0; seed < 10 && ok; ++seed) {
