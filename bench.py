@@ -247,7 +247,7 @@ def make_record(impl, world, B, T, steps, warmup, ms_max, clocks, launches, e2e,
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="tnccl", choices=["tnccl", "reference", "nccl-ddp"])
     ap.add_argument("--batch", type=int, default=8)
