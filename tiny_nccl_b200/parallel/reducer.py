@@ -52,7 +52,8 @@ class FlatGradReducer:
                  bucket_bytes: int = 25 << 20,
                  alloc: Callable[..., torch.Tensor] | None = None,
                  stream: torch.cuda.Stream | None = None,
-                 on_reduced: Callable[[list], None] | None = None):
+                 on_reduced: Callable[[list], None] | None = None,
+                 last_all_reduce: Callable[[torch.Tensor], None] | None = None):
         params = [p for p in params if p.requires_grad]
         if not params:
             raise ValueError("FlatGradReducer: no parameter requires a gradient")
@@ -97,6 +98,10 @@ class FlatGradReducer:
         for p, b in zip(order, bucket_of):
             self.bucket_params[b].append(p)
         self._all_reduce = all_reduce
+        # The last bucket (the first parameters registered, e.g. the token
+        # embedding, whose gradient is complete only at the end of backward)
+        # may be reduced differently: nothing is left to overlap with it.
+        self._last_all_reduce = last_all_reduce or all_reduce
         self._on_reduced = on_reduced
         self._stream = stream
         self._pending = list(self._need)
@@ -125,14 +130,15 @@ class FlatGradReducer:
     def _launch(self, b: int) -> None:
         s, e = self.buckets[b]
         chunk = self.flat[s:e]
+        reduce = self._last_all_reduce if b == len(self.buckets) - 1 else self._all_reduce
         if self._stream is None:
-            self._all_reduce(chunk)
+            reduce(chunk)
             if self._on_reduced is not None:
                 self._on_reduced(self.bucket_params[b])
         else:
             self._stream.wait_stream(torch.cuda.current_stream(self.flat.device))
             with torch.cuda.stream(self._stream):
-                self._all_reduce(chunk)
+                reduce(chunk)
                 if self._on_reduced is not None:
                     self._on_reduced(self.bucket_params[b])
         self.launched += 1

@@ -96,10 +96,22 @@ class DataParallelTrainer:
             # the communicator has no NVLS; the buffer then stays unregistered.
             alloc = ((lambda n, dt, d: empty_registrable(n, dt, d)) if registered
                      and comm.size > 1 and comm.info()["nvls"] else None)
+            # The last bucket (the token embedding, tied to the LM head: its
+            # gradient is complete only after the last backward node) overlaps
+            # nothing, so it takes every channel (TNCCL_DP_TAIL_CHANNELS; 0 =
+            # the communicator's configured count).
+            tail = int(os.environ.get("TNCCL_DP_TAIL_CHANNELS", "0"))
+
+            def last_all_reduce(t):
+                comm.set_max_channels(tail)
+                comm.all_reduce(t, op="avg", algo=algo)
+                comm.set_max_channels(max_channels)
+
             self.reducer = FlatGradReducer(
                 model.parameters(), lambda t: comm.all_reduce(t, op="avg", algo=algo),
                 bucket_bytes=bucket_cap_mb << 20, alloc=alloc, stream=comm.side_stream(),
-                on_reduced=self.opt.step_params if self.overlap_optimizer else None)
+                on_reduced=self.opt.step_params if self.overlap_optimizer else None,
+                last_all_reduce=last_all_reduce)
             if alloc is not None:
                 self.registration = comm.register(self.reducer.flat)
             self.ddp = model
