@@ -171,19 +171,23 @@ __device__ __forceinline__ void tmemLoad32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// tanh-GELU, 0.5 x (1 + tanh(k0 (x + k1 x^3))) = x (0.5 + 0.5 tanh(u)), with
-// the hardware tanh approximation (PTX tanh.approx.f32, relative error about
-// 2^-11, well below the bf16 rounding of the result).
-__device__ __forceinline__ float tanhApprox(float x) {
+// tanh-GELU, 0.5 x (1 + tanh(u)) with u = k0 (x + k1 x^3), evaluated in the
+// equivalent form x / (1 + e^(-2u)) (1 + tanh(u) = 2 / (1 + e^(-2u))): no
+// cancellation where tanh(u) is near -1, so the relative error stays near
+// that of the hardware ex2 and the fast division (~1e-6), far below the bf16
+// rounding of the result. Saturates correctly: x for large u, -0 for very
+// negative u.
+__device__ __forceinline__ float ex2Approx(float x) {
   float y;
-  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
 __device__ __forceinline__ float geluTanh(float x) {
   const float k0 = 0.7978845608028654f;  // sqrt(2 / pi)
   const float k0k1 = 0.7978845608028654f * 0.044715f;
+  const float m2log2e = -2.0f * 1.4426950408889634f;
   const float u = x * fmaf(k0k1, x * x, k0);
-  return x * fmaf(0.5f, tanhApprox(u), 0.5f);
+  return __fdividef(x, 1.0f + ex2Approx(u * m2log2e));
 }
 __device__ __forceinline__ uint32_t packBf16(float lo, float hi) {
   __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
