@@ -16,9 +16,9 @@ are much larger than L2 from 256 MiB up; smaller sizes run L2-resident, as
 they do in nccl-tests. Each line of the output file is one JSON record.
 
 ``--impls nvls_zc`` runs the NVLS algorithm on buffers from tncclMemAlloc
-registered with the communicator; with TNCCL_NVLS_ZERO_COPY=1 in the
-environment that is the zero-copy kernel (no copy through the communicator's
-multicast region), otherwise the staged one.
+registered with the communicator: the zero-copy kernel (no copy through the
+communicator's multicast region), or the staged one with
+TNCCL_NVLS_ZERO_COPY=0 in the environment.
 """
 from __future__ import annotations
 
@@ -144,7 +144,7 @@ def main():
     src = torch.randn(maxn, dtype=torch.float32, device=dev, generator=gen).to(dtype)
     dst = torch.empty_like(src)
     # nvls_zc: the NVLS kernel on buffers registered with the communicator
-    # (zero-copy when TNCCL_NVLS_ZERO_COPY=1, the staged kernel otherwise).
+    # (zero-copy unless TNCCL_NVLS_ZERO_COPY=0, then the staged kernel).
     reg = None
     if "nvls_zc" in impls:
         from tiny_nccl_b200.parallel import empty_registrable
@@ -206,7 +206,7 @@ def main():
                    "us": t * 1e6, "algbw_gbs": algbw, "busbw_gbs": busbw, "iters": k,
                    "chosen": comm.select_algo(n, dtype) if impl == "auto" else impl,
                    "frac_link": busbw / LINK_GBS}
-            if impl == "nvls_zc":  # did the zero-copy kernel run (TNCCL_NVLS_ZERO_COPY=1)?
+            if impl == "nvls_zc":  # did the zero-copy kernel run?
                 rec["zero_copy"] = comm.info()["zero_copy_launches"] > zc0
             if args.check and impl != "nccl":
                 ref_y = x.clone()

@@ -17,8 +17,9 @@ events on each stream, max over ranks.
         benchmarks/bucket_overlap.py --out bucket.jsonl
 
 ``--registered`` puts the buckets (and their outputs) in two tncclMemAlloc
-regions registered with the communicator; with TNCCL_NVLS_ZERO_COPY=1 every
-tnccl bucket all-reduce is then the zero-copy NVLS kernel.
+regions registered with the communicator; every tnccl bucket all-reduce that
+AUTO sends through NVLS (on 8 ranks from 16 MiB) is then the zero-copy
+kernel (TNCCL_NVLS_ZERO_COPY=0 turns that off).
 """
 from __future__ import annotations
 

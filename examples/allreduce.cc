@@ -13,10 +13,11 @@
 //       hosts use the socket data plane (TNCCL_NET=auto).
 //
 // TNCCL_EXAMPLE_REGISTERED=1 allocates the buffers with tncclMemAlloc and
-// registers them with the communicator (tncclCommRegister), so that with
-// TNCCL_NVLS_ZERO_COPY=1 an NVLS all-reduce of 1 MiB or more runs the
-// zero-copy kernel on them; without NVLS the registration is refused and the
-// buffers are used unregistered.
+// registers them with the communicator (tncclCommRegister), so that an NVLS
+// all-reduce runs the zero-copy kernel on them (explicitly with
+// TNCCL_ALGO=nvls, or chosen by AUTO from TNCCL_NVLS_ZC_MIN_BYTES: 16 MiB on
+// 8 ranks); without NVLS the registration is refused and the buffers are
+// used unregistered.
 //
 // Same contract as tiny-nccl's examples/allreduce.cc:22-127: rank r
 // contributes r + 1 everywhere, and every element must equal n(n+1)/2; the

@@ -220,9 +220,9 @@ tncclResult tncclMemFree(void* ptr);
  * and recv both lie in registered buffers, at the same offsets on every
  * rank, 16-byte aligned and a multiple of 16 bytes long, then reduces
  * straight from the senders' buffers and stores into every receiver's, with
- * no copy through the communicator's own region (opt-in while it has not
- * been measured: TNCCL_NVLS_ZERO_COPY=1). TNCCL_UNSUPPORTED when the
- * communicator has no NVLS. */
+ * no copy through the communicator's own region (TNCCL_NVLS_ZERO_COPY=0
+ * turns that off; AUTO takes it from TNCCL_NVLS_ZC_MIN_BYTES, 16 MiB on 8
+ * ranks). TNCCL_UNSUPPORTED when the communicator has no NVLS. */
 tncclResult tncclCommRegister(tncclComm_t comm, void* buff, size_t size, void** handle);
 /* Collective: waits for the bound stream, then unbinds on every rank
  * (two barriers, as tncclCommDestroy). tncclCommDestroy deregisters what is

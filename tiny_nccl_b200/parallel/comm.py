@@ -135,8 +135,9 @@ class Communicator:
         """Collective: binds ``tensor`` (from :func:`empty_registrable`, the
         same size on every rank) to an NVSwitch multicast object of its own,
         so that an NVLS all-reduce on it reads and writes it in place instead
-        of copying it through the communicator's region (used when
-        ``TNCCL_NVLS_ZERO_COPY=1``). Returns a handle for :meth:`deregister`."""
+        of copying it through the communicator's region (on by default,
+        ``TNCCL_NVLS_ZERO_COPY=0`` turns it off). Returns a handle for
+        :meth:`deregister`."""
         return self._c.register(tensor)
 
     def deregister(self, handle: int) -> None:

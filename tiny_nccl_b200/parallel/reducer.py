@@ -11,8 +11,8 @@ the same collectives in the same order whatever order its hooks fire in
 
 What the flat buffer adds over DDP's own buckets is where it lives: with
 ``alloc=empty_registrable`` it is tncclMemAlloc memory that the communicator
-can register, so with ``TNCCL_NVLS_ZERO_COPY=1`` every bucket all-reduce is
-the zero-copy NVLS kernel (the NVSwitch reduces; the kernel only issues
+can register, so every bucket all-reduce that AUTO sends through NVLS (8
+ranks, buckets from 16 MiB) is the zero-copy kernel (the NVSwitch reduces; the kernel only issues
 multimem loads and stores, so it needs few SMs while backward runs). Bucket
 boundaries and parameter offsets are multiples of 16 bytes, as that kernel
 requires, and they are the same on every rank because every rank builds the
