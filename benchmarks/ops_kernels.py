@@ -2,7 +2,8 @@
 for ncu captures and CUDA-event timing of the kernel alone.
 
     python benchmarks/ops_kernels.py --kernel ln_bwd --iters 20
-Kernels: ln_fwd, ln_bwd, cross_entropy, adamw, gemm_gelu (the tcgen05 GEMM of
+Kernels: ln_fwd, ln_bwd, cross_entropy, adamw, gelu_bwd (GELU backward + bias
+gradient of the MLP), gemm_gelu (the tcgen05 GEMM of
 the MLP's first layer with its bias + GELU epilogue, M = rows, N = 3072,
 K = 768; reported in TFLOP/s) and gemm_gelu_ref (cuBLAS addmm + GELU on the
 same shapes, for comparison).
@@ -68,6 +69,12 @@ def main():
             step[0] += 1
             ops.adamw(ps, gs, ms, vs, wd, 6e-4, 0.9, 0.95, 1e-8, step[0], 1.0)
         nbytes = sum(p.numel() for p in ps) * 4 * 7
+    elif args.kernel == "gelu_bwd":
+        # The MLP's GELU backward fused with its bias gradient, [rows, 3072].
+        gy = torch.randn(rows, 4 * C, device=dev).to(torch.bfloat16)
+        pre = (2 * torch.randn(rows, 4 * C, device=dev)).to(torch.bfloat16)
+        fn = lambda: ops.gelu_bwd_bias(gy, pre)  # noqa: E731
+        nbytes = rows * 4 * C * 2 * 3
     elif args.kernel in ("gemm_gelu", "gemm_gelu_ref"):
         x = (torch.randn(rows, args.k, device=dev) * 0.5).to(torch.bfloat16)
         w = (torch.randn(4 * C, args.k, device=dev) * 0.02).to(torch.bfloat16)

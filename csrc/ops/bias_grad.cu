@@ -35,14 +35,30 @@ __device__ __forceinline__ void bf16x8ToF(uint4 v, float (&f)[8]) {
   }
 }
 
-// Derivative of the tanh approximation of GELU,
-// 0.5 x (1 + tanh(k0 (x + k1 x^3))), written from the product rule.
+// Derivative of the tanh approximation of GELU, 0.5 x (1 + tanh(u)) with
+// u = k0 (x + k1 x^3), from the product rule:
+//   0.5 (1 + t) + 0.5 x (1 - t^2) u',  t = tanh(u),  u' = k0 + 3 k0 k1 x^2.
+// With e = e^(-2u) and r = 1 / (1 + e): 0.5 (1 + t) = r and
+// 1 - t^2 = 4 r (1 - r) = 4 r (e r), so the derivative is
+// r + 2 x r (e r) u': one ex2 and one fast division, and 1 - t^2 comes from
+// e r directly, never from 1 - t*t (which cancels where |t| is near 1).
+__device__ __forceinline__ float ex2Approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ float geluTanhGrad(float x) {
   const float k0 = 0.7978845608028654f;  // sqrt(2 / pi)
-  const float k1 = 0.044715f;
+  const float k0k1 = 0.7978845608028654f * 0.044715f;
+  const float m2log2e = -2.0f * 1.4426950408889634f;
   const float x2 = x * x;
-  const float t = tanhf(k0 * (x + k1 * x2 * x));
-  return 0.5f * (1.0f + t) + 0.5f * x * (1.0f - t * t) * k0 * (1.0f + 3.0f * k1 * x2);
+  // |u| <= 40 keeps e and r finite (e^80 < FLT_MAX); the derivative is 0 or
+  // 1 to float precision well before that.
+  const float u = fminf(fmaxf(x * fmaf(k0k1, x2, k0), -40.0f), 40.0f);
+  const float e = ex2Approx(u * m2log2e);
+  const float r = __fdividef(1.0f, 1.0f + e);
+  const float du = fmaf(3.0f * k0k1, x2, k0);
+  return fmaf(2.0f * x * r * (e * r), du, r);
 }
 
 template <bool GELU>

@@ -186,7 +186,8 @@ __device__ __forceinline__ float geluTanh(float x) {
   const float k0 = 0.7978845608028654f;  // sqrt(2 / pi)
   const float k0k1 = 0.7978845608028654f * 0.044715f;
   const float m2log2e = -2.0f * 1.4426950408889634f;
-  const float u = x * fmaf(k0k1, x * x, k0);
+  // |u| <= 40 keeps e^(-2u) finite; gelu is x or -0 to float precision there.
+  const float u = fminf(fmaxf(x * fmaf(k0k1, x * x, k0), -40.0f), 40.0f);
   return __fdividef(x, 1.0f + ex2Approx(u * m2log2e));
 }
 __device__ __forceinline__ uint32_t packBf16(float lo, float hi) {
