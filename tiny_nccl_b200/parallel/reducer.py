@@ -108,6 +108,10 @@ class FlatGradReducer:
         self._next = 0  # first bucket not launched yet
         self._fired = set()
         self.launched = 0
+        # Recorded on the side stream after the next-to-last bucket's
+        # all-reduce: finish(split_last=True) lets the caller start on every
+        # other bucket while the last one is still being reduced.
+        self._before_last = torch.cuda.Event() if stream is not None else None
         self._hooks = [p.register_post_accumulate_grad_hook(self._ready) for p in order]
 
     # -- hooks ----------------------------------------------------------------
@@ -141,13 +145,17 @@ class FlatGradReducer:
                 reduce(chunk)
                 if self._on_reduced is not None:
                     self._on_reduced(self.bucket_params[b])
+                if b == len(self.buckets) - 2:
+                    self._before_last.record(self._stream)
         self.launched += 1
 
     # -- per step ---------------------------------------------------------------
-    def finish(self) -> None:
+    def finish(self, split_last: bool = False) -> None:
         """Launches the buckets still waiting (parameters that got no gradient
         this step), makes the current stream wait for every all-reduce and
-        re-arms the counters for the next backward."""
+        re-arms the counters for the next backward. With ``split_last`` the
+        current stream waits only for the buckets before the last one; call
+        :meth:`wait_last` before using the last bucket's gradients."""
         for p in self.params:  # no gradient this step: its slice holds zeros
             if id(p) not in self._fired:
                 view = self._views[id(p)]
@@ -157,10 +165,20 @@ class FlatGradReducer:
             self._launch(self._next)
             self._next += 1
         if self._stream is not None:
-            torch.cuda.current_stream(self.flat.device).wait_stream(self._stream)
+            cur = torch.cuda.current_stream(self.flat.device)
+            if split_last and len(self.buckets) >= 2:
+                cur.wait_event(self._before_last)
+            else:
+                cur.wait_stream(self._stream)
         self._pending = list(self._need)
         self._next = 0
         self._fired = set()
+
+    def wait_last(self) -> None:
+        """After ``finish(split_last=True)``: the current stream waits for the
+        last bucket's all-reduce too."""
+        if self._stream is not None:
+            torch.cuda.current_stream(self.flat.device).wait_stream(self._stream)
 
     def zero_grad(self) -> None:
         """Unsets every ``.grad`` (no kernel): the next backward writes each

@@ -114,6 +114,10 @@ class DataParallelTrainer:
                 last_all_reduce=last_all_reduce)
             if alloc is not None:
                 self.registration = comm.register(self.reducer.flat)
+            # TNCCL_DP_SPLIT_LAST=0: AdamW waits for every bucket (A/B switch).
+            self._split_last = os.environ.get("TNCCL_DP_SPLIT_LAST", "1") == "1"
+            last = {id(p) for p in self.reducer.bucket_params[-1]}
+            self._before_last_params = [p for p in self.reducer.params if id(p) not in last]
             self.ddp = model
             self.hook_state = None
         elif reducer in ("ddp", "nccl-ddp"):
@@ -175,9 +179,19 @@ class DataParallelTrainer:
             loss = self.ddp(idx, targets)
         loss.backward()
         if self.reducer is not None:
-            self.reducer.finish()
-            if not self.overlap_optimizer:
-                self.opt.step()
+            if self.overlap_optimizer or not self._split_last:
+                self.reducer.finish()
+                if not self.overlap_optimizer:
+                    self.opt.step()
+            else:
+                # AdamW updates every other bucket's parameters while the last
+                # bucket (the token embedding, complete only at the end of
+                # backward) is still being reduced, then that bucket's.
+                self.reducer.finish(split_last=True)
+                self.opt.begin_step()
+                self.opt.step_params(self._before_last_params)
+                self.reducer.wait_last()
+                self.opt.step_params(self.reducer.bucket_params[-1])
             self.reducer.zero_grad()
         else:
             self.opt.step()
