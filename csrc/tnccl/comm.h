@@ -136,6 +136,7 @@ struct tncclComm {
   cudaStream_t boundStream = nullptr;
   bool streamBound = false;
   bool aborted = false;
+  bool deviceErrorReported = false;  // the warning below is printed once
   uint64_t oneShotMaxBytes = 0;
   uint64_t nvlsMinBytes = 0;
   int maxChannels = 0;  // tncclCommSetMaxChannels cap (0: none)

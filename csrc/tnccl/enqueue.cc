@@ -90,7 +90,29 @@ extern "C" tncclResult tncclAllReduceEx(const void* send, void* recv, size_t cou
   if (comm->aborted) return TNCCL_ABORTED;
   if (comm->hostStatus && comm->hostStatus->error != 0) {
     const int e = comm->hostStatus->error;
-    return e > 0 && e < TNCCL_NUM_RESULTS ? (tncclResult)e : TNCCL_SYSTEM_ERROR;
+    const tncclResult r = e > 0 && e < TNCCL_NUM_RESULTS ? (tncclResult)e : TNCCL_SYSTEM_ERROR;
+    if (!comm->deviceErrorReported) {
+      comm->deviceErrorReported = true;
+      // where = (counter family << 24) | (channel << 8) | phase (device.cuh).
+      const int where = comm->hostStatus->where;
+      const int family = (where >> 24) & 0x7f, channel = (where >> 8) & 0xffff;
+      const int phase = where & 0xff;
+      // The zero-copy kernel's entry barrier waits for every rank to reach
+      // the same launch: ranks that chose differently (a buffer registered on
+      // one rank only, different offsets or sizes, different channel caps)
+      // launch different kernels and meet it only at the wait bound.
+      const bool zcEntry = family == kCounterNvlsZc && phase == 1;
+      TN_WARN("rank %d: a device wait gave up (result %d) in counter family %d, channel %d, "
+              "phase %d; expected %llu, observed %llu%s",
+              comm->rank, (int)r, family, channel, phase,
+              (unsigned long long)comm->hostStatus->expectedSeq,
+              (unsigned long long)comm->hostStatus->observedSeq,
+              zcEntry ? ": the zero-copy NVLS entry barrier; every rank must pass registered "
+                        "buffers at the same offsets, with the same size and the same "
+                        "tncclCommSetMaxChannels value"
+                      : "");
+    }
+    return r;
   }
   float scale = preScale;
   if (op == tncclAvg) scale = preScale / (float)comm->nranks;

@@ -176,8 +176,9 @@ tncclResult tncclCommCuDevice(tncclComm_t comm, int* device);
  * launch on this communicator at maxChannels (clamped to 1 .. the configured
  * count; 0 restores the configured count). A collective that overlaps with
  * compute (the DDP hook) leaves the other SMs to the compute kernels. Local
- * to the rank and stream-ordered like any launch parameter; ranks should use
- * the same cap. */
+ * to the rank and stream-ordered like any launch parameter; ranks must use
+ * the same cap for collectives on registered buffers (the zero-copy NVLS
+ * kernel's grid follows it, and its barriers count every CTA of every rank). */
 tncclResult tncclCommSetMaxChannels(tncclComm_t comm, int maxChannels);
 
 /* Waits for the bound stream, then checks the guard lines placed after every
