@@ -1,7 +1,7 @@
 """Runs one fused model kernel on GPT-2-small training shapes (8 x 1024 rows),
 for ncu captures and CUDA-event timing of the kernel alone.
 
-    python benchmarks/ops_kernels.py --kernel ln_bwd --iters 20
+    python benchmarks/ops_kernels.py --kernel ln_bwd --iters 20 [--graph]
 Kernels: ln_fwd, ln_bwd, cross_entropy, adamw, gelu_bwd (GELU backward + bias
 gradient of the MLP), gemm_gelu (the tcgen05 GEMM of
 the MLP's first layer with its bias + GELU epilogue, M = rows, N = 3072,
@@ -28,6 +28,8 @@ def main():
     ap.add_argument("--no-gelu", action="store_true", help="gemm_gelu: bias only (pre)")
     ap.add_argument("--pair", action="store_true",
                     help="gemm_gelu: persistent CTA pairs (cta_group::2, 256 x 256 tiles)")
+    ap.add_argument("--graph", action="store_true",
+                    help="time the launches as one CUDA-graph replay (no host launch cost)")
     args = ap.parse_args()
     import tiny_nccl_b200 as tn
 
@@ -36,18 +38,32 @@ def main():
     dev = "cuda"
     torch.manual_seed(0)
     if args.kernel in ("ln_fwd", "ln_bwd"):
-        x = torch.randn(rows, C, device=dev)
-        d = torch.randn(rows, C, device=dev).to(torch.bfloat16)
-        w = torch.ones(C, device=dev)
-        b = torch.zeros(C, device=dev)
-        xo, y, mean, rstd = ops.ln_fwd(x, d, w, b, 1e-5)
-        gy = torch.randn(rows, C, device=dev).to(torch.bfloat16)
-        gr = torch.randn(rows, C, device=dev)
+        # Three input sets used in turn: consecutive launches do not find
+        # each other's data in L2 (8192 rows take about 100 MB per launch).
+        sets = []
+        for _ in range(3):
+            x = torch.randn(rows, C, device=dev)
+            d = torch.randn(rows, C, device=dev).to(torch.bfloat16)
+            w = torch.ones(C, device=dev)
+            b = torch.zeros(C, device=dev)
+            xo, y, mean, rstd = ops.ln_fwd(x, d, w, b, 1e-5)
+            gy = torch.randn(rows, C, device=dev).to(torch.bfloat16)
+            gr = torch.randn(rows, C, device=dev)
+            sets.append((x, d, w, b, xo, mean, rstd, gy, gr))
+        turn = [0]
+
+        def next_set():
+            turn[0] = (turn[0] + 1) % len(sets)
+            return sets[turn[0]]
         if args.kernel == "ln_fwd":
-            fn = lambda: ops.ln_fwd(x, d, w, b, 1e-5)  # noqa: E731
+            def fn():
+                x, d, w, b = next_set()[:4]
+                return ops.ln_fwd(x, d, w, b, 1e-5)
             nbytes = rows * C * (4 + 2 + 4 + 2)
         else:
-            fn = lambda: ops.ln_bwd(gy, gr, xo, w, mean, rstd, True)  # noqa: E731
+            def fn():
+                _, _, w, _, xo, mean, rstd, gy, gr = next_set()
+                return ops.ln_bwd(gy, gr, xo, w, mean, rstd, True)
             nbytes = rows * C * (2 + 4 + 4 + 4 + 2)
     elif args.kernel == "cross_entropy":
         Vp = 50304
@@ -89,12 +105,25 @@ def main():
         nbytes = None
     else:
         raise SystemExit(f"unknown kernel {args.kernel}")
-    fn()
+    for _ in range(3):
+        fn()
     torch.cuda.synchronize()
+    run = lambda: [fn() for _ in range(args.iters)]  # noqa: E731
+    if args.graph:
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            run()
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            run()
+        graph.replay()
+        torch.cuda.synchronize()
+        run = graph.replay
     e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
     e0.record()
-    for _ in range(args.iters):
-        fn()
+    run()
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.iters

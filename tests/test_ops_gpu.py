@@ -12,7 +12,10 @@ def ops(built):
     return o
 
 
-@pytest.mark.parametrize("rows,C", [(64, 768), (257, 1024), (8, 128), (33, 640)])
+# C % 8 == 0 takes the pipelined backward (cp.async row stages), C = 772 and
+# 36 the one-row-per-warp kernel; 4096 rows give every warp several rows.
+@pytest.mark.parametrize("rows,C", [(64, 768), (257, 1024), (8, 128), (33, 640), (4096, 768),
+                                    (100, 772), (3, 36)])
 @pytest.mark.parametrize("with_delta", [False, True])
 def test_add_layer_norm(ops, rows, C, with_delta):
     torch.manual_seed(0)
