@@ -5,13 +5,14 @@
 // Backward: with xhat = (x_out - mean) * rstd and gw = gy * w,
 //           dx = g_res + rstd * (gw - mean(gw) - xhat * mean(gw * xhat))
 //           dw = sum_rows gy * xhat,  db = sum_rows gy
-// dw/db are reduced deterministically: each CTA keeps per-warp column sums,
-// combines its warps in shared memory and writes one partial row; a second
-// kernel sums the partial rows in a fixed order. The backward has two
-// kernels: a pipelined one (rows of C % 8 == 0 staged through shared memory
-// with cp.async, several rows in flight per warp) and one that loads each
-// row straight into registers (any C % 4 == 0).
+// dw/db are reduced deterministically: each CTA keeps per-thread column sums,
+// combines them in shared memory and writes one partial row; a second kernel
+// sums the partial rows in a fixed order. The backward has two kernels: the
+// default gives each row to a group of threads with one float4 column group
+// per thread (several rows per CTA, cp.async prefetch two rows ahead); the
+// other gives each row to one warp (TNOPS_LN_BWD=warp, kept for A/B timing).
 #include <stdlib.h>
+#include <string.h>
 
 #include "common.cuh"
 #include "tnccl_ops.h"
@@ -202,22 +203,35 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, 2)
 }
 
 // ---------------------------------------------------------------------------
-// Pipelined backward for C % 8 == 0 and 16-byte aligned rows (the usual
-// case; the kernel above handles the rest). One CTA of 8 warps per SM; each
-// warp owns rows warp + 8 * blockIdx.x + j * (8 * gridDim.x) and keeps its
-// next S - 1 rows in flight while it computes the current one: the row's gy,
-// x_out and residual gradient are copied global -> shared with 16-byte
-// cp.async into a ring of S per-warp stages, so the memory system always
-// has requests queued and the warp never waits on a load it has just
-// issued. The dW / dB sums stay in registers (the loads no longer occupy
-// them). Summation order per column: each warp's rows in row order, the 8
-// warps in warp order, then the CTAs in order (colReduce).
+// Row-group backward (the default for every supported shape). A group of
+// G = 32 * ceil(C / 128) threads owns one row at a time, one float4 column
+// group per thread; a CTA of R groups (R * G <= 1024, R <= 8) runs one per
+// SM and walks rows blockIdx.x * R + g, + gridDim.x * R, ... Compared with
+// one warp per row this gives each SM ~30 warps instead of 8-16 to hide
+// latency, and every thread carries a few registers of state instead of a
+// whole row slice.
+//
+// Each thread prefetches its own bytes of the next kGroupStages - 1 rows (gy 8 B,
+// x_out 16 B, residual gradient 16 B) into a per-group ring of shared-memory
+// stages with cp.async; a thread only ever reads what it copied itself, so
+// the copies need no barrier, only cp.async.wait_group. The two row sums
+// (of gy * w and of gy * w * xhat) go through one named barrier per row and
+// group: warp sums are written to a slot double-buffered by row parity, so
+// the next row's writes cannot overwrite values another warp is still
+// reading. Summation order per column: each group's rows in row order, the
+// groups in group order (here), then the CTAs in order (colReduce).
 // ---------------------------------------------------------------------------
-constexpr int kPipeWarps = 8;
+constexpr int kGroupMaxRows = 8;   // R limit: named barriers 1..8
+constexpr int kGroupStages = 3;    // rows in the ring per group (2 ahead)
+constexpr int kGroupRedFloats = kGroupMaxRows * 2 * 8 * 2;  // [R][parity][warp][2]
 
 __device__ __forceinline__ void cpAsync16(void* dst, const void* src) {
   const unsigned s = (unsigned)__cvta_generic_to_shared(dst);
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cpAsync8(void* dst, const void* src) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(s), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cpAsyncCommit() {
   asm volatile("cp.async.commit_group;\n" ::: "memory");
@@ -226,138 +240,133 @@ template <int N>
 __device__ __forceinline__ void cpAsyncWait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
-
-// Stage layout (bytes): gy [2C] | x_out [4C] | g_res [4C]; every part starts
-// on a 16-byte boundary because C % 8 == 0.
-__device__ __forceinline__ void lnBwdIssueRow(char* st, const uint16_t* gy, const float* xo,
-                                              const float* gres, size_t base, int C, int lane) {
-  const char* g = reinterpret_cast<const char*>(gy + base);
-  const char* x = reinterpret_cast<const char*>(xo + base);
-  for (int q = lane; q < (C >> 3); q += 32) cpAsync16(st + 16 * q, g + 16 * q);
-  for (int q = lane; q < (C >> 2); q += 32) cpAsync16(st + 2 * C + 16 * q, x + 16 * q);
-  if (gres) {
-    const char* r = reinterpret_cast<const char*>(gres + base);
-    for (int q = lane; q < (C >> 2); q += 32) cpAsync16(st + 6 * C + 16 * q, r + 16 * q);
-  }
+__device__ __forceinline__ void namedBarrier(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(nthreads) : "memory");
 }
 
-template <int K, int S>
-__global__ void __launch_bounds__(kPipeWarps * 32, 1)
-    lnBwdPipeKernel(const uint16_t* __restrict__ gy, const float* __restrict__ gres,
-                    const float* __restrict__ xo, const float* __restrict__ w,
-                    const float* __restrict__ mean, const float* __restrict__ rstd,
-                    float* __restrict__ dx, uint16_t* __restrict__ dxb,
-                    float* __restrict__ partial, int rows, int C) {
-  extern __shared__ __align__(16) char sPipe[];
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
+// Bytes of one stage of one group: gy [8 G] | x_out [16 G] | g_res [16 G].
+__host__ __device__ constexpr int groupStageBytes(int G) { return 40 * G; }
+
+__global__ void __launch_bounds__(1024, 1)
+    lnBwdGroupKernel(const uint16_t* __restrict__ gy, const float* __restrict__ gres,
+                     const float* __restrict__ xo, const float* __restrict__ w,
+                     const float* __restrict__ mean, const float* __restrict__ rstd,
+                     float* __restrict__ dx, uint16_t* __restrict__ dxb,
+                     float* __restrict__ partial, int rows, int C, int G, int R) {
+  extern __shared__ __align__(16) float sGroup[];
+  const int t = threadIdx.x;
+  const int grp = t / G;
+  const int gt = t - grp * G;  // this thread's float4 column group
+  const int lane = t & 31, gwarp = gt >> 5, nwarps = G >> 5;
   const int C4 = C >> 2;
+  const bool act = gt < C4;
   const float invC = 1.0f / (float)C;
-  const size_t stageBytes = (size_t)10 * C;
-  char* ring = sPipe + (size_t)warp * S * stageBytes;
-  const float4* w4 = reinterpret_cast<const float4*>(w);
-  const int stride = gridDim.x * kPipeWarps;
-  const int first = blockIdx.x * kPipeWarps + warp;
+  float* sRed = sGroup;
+  char* ring = reinterpret_cast<char*>(sGroup + kGroupRedFloats) +
+               (size_t)grp * kGroupStages * groupStageBytes(G);
+  char* myG = ring + 8 * gt;            // + stage * stageBytes
+  char* myX = ring + 8 * G + 16 * gt;
+  char* myR = ring + 24 * G + 16 * gt;
+  const int stageBytes = groupStageBytes(G);
 
-  float4 aw[K], ab[K];
-#pragma unroll
-  for (int k = 0; k < K; ++k) {
-    aw[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-    ab[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-  // Prologue: rows 0 .. S-2 of this warp, one commit group each (empty
-  // groups past the end keep the group count uniform).
-#pragma unroll
-  for (int j = 0; j < S - 1; ++j) {
-    const int row = first + j * stride;
-    if (row < rows) lnBwdIssueRow(ring + j * stageBytes, gy, xo, gres, (size_t)row * C, C, lane);
-    cpAsyncCommit();
-  }
-  int slot = 0;
-  for (int row = first; row < rows; row += stride) {
-    // Refill the stage computed in the previous iteration with the row S-1
-    // ahead, then wait for all but the newest S-1 groups: this row's copies.
-    const int ahead = row + (S - 1) * stride;
-    const int aslot = slot == 0 ? S - 1 : slot - 1;
-    if (ahead < rows)
-      lnBwdIssueRow(ring + aslot * stageBytes, gy, xo, gres, (size_t)ahead * C, C, lane);
-    cpAsyncCommit();
-    cpAsyncWait<S - 1>();
-    __syncwarp();  // the copies of every lane of the warp are visible
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+  const float4 wv = act ? reinterpret_cast<const float4*>(w)[gt] : zero;
+  float4 aw = zero, ab = zero;
+  const int stride = gridDim.x * R;
+  const int first = blockIdx.x * R + grp;
 
-    const char* st = ring + slot * stageBytes;
-    const uint2* gs = reinterpret_cast<const uint2*>(st);
-    const float4* xs = reinterpret_cast<const float4*>(st + 2 * C);
-    const float4* rsm = reinterpret_cast<const float4*>(st + 6 * C);
-    const float mu = mean[row], rs = rstd[row];
-    float4 g[K], xh[K];
-    float s1 = 0.f, s2 = 0.f;
-#pragma unroll
-    for (int k = 0; k < K; ++k) {
-      const int i = lane + 32 * k;
-      if (i < C4) {
-        g[k] = bf4(gs[i]);
-        const float4 xv = xs[i];
-        xh[k] = make_float4((xv.x - mu) * rs, (xv.y - mu) * rs, (xv.z - mu) * rs,
-                            (xv.w - mu) * rs);
-        const float4 ww = w4[i];
-        const float4 gw = make_float4(g[k].x * ww.x, g[k].y * ww.y, g[k].z * ww.z, g[k].w * ww.w);
-        s1 += (gw.x + gw.y) + (gw.z + gw.w);
-        s2 += (gw.x * xh[k].x + gw.y * xh[k].y) + (gw.z * xh[k].z + gw.w * xh[k].w);
-        aw[k].x += g[k].x * xh[k].x;
-        aw[k].y += g[k].y * xh[k].y;
-        aw[k].z += g[k].z * xh[k].z;
-        aw[k].w += g[k].w * xh[k].w;
-        ab[k].x += g[k].x;
-        ab[k].y += g[k].y;
-        ab[k].z += g[k].z;
-        ab[k].w += g[k].w;
-      }
-    }
-    const float m1 = warpSum(s1) * invC, m2 = warpSum(s2) * invC;
+  auto issue = [&](int stage, int row) {
     const size_t base = (size_t)row * C;
-    float4* dr = reinterpret_cast<float4*>(dx + base);
-    uint2* dbr = dxb ? reinterpret_cast<uint2*>(dxb + base) : nullptr;
+    const int off = stage * stageBytes;
+    cpAsync8(myG + off, reinterpret_cast<const uint2*>(gy + base) + gt);
+    cpAsync16(myX + off, reinterpret_cast<const float4*>(xo + base) + gt);
+    if (gres) cpAsync16(myR + off, reinterpret_cast<const float4*>(gres + base) + gt);
+  };
 #pragma unroll
-    for (int k = 0; k < K; ++k) {
-      const int i = lane + 32 * k;
-      if (i < C4) {
-        const float4 ww = w4[i];
-        const float4 res = gres ? rsm[i] : make_float4(0.f, 0.f, 0.f, 0.f);
-        float4 o;
-        o.x = rs * (g[k].x * ww.x - m1 - xh[k].x * m2) + res.x;
-        o.y = rs * (g[k].y * ww.y - m1 - xh[k].y * m2) + res.y;
-        o.z = rs * (g[k].z * ww.z - m1 - xh[k].z * m2) + res.z;
-        o.w = rs * (g[k].w * ww.w - m1 - xh[k].w * m2) + res.w;
-        dr[i] = o;
-        if (dbr) dbr[i] = tobf4(o);
-      }
+  for (int j = 0; j < kGroupStages - 1; ++j) {
+    const int row = first + j * stride;
+    if (act && row < rows) issue(j, row);
+    cpAsyncCommit();
+  }
+  float mu = 0.f, rs = 0.f;
+  if (first < rows) {
+    mu = mean[first];
+    rs = rstd[first];
+  }
+  int slot = 0, parity = 0;
+  for (int row = first; row < rows; row += stride) {
+    const int next = row + stride;
+    float nmu = 0.f, nrs = 0.f;
+    if (next < rows) {
+      nmu = mean[next];
+      nrs = rstd[next];
     }
-    __syncwarp();  // every lane is done with this stage before it is refilled
-    slot = slot + 1 == S ? 0 : slot + 1;
+    const int ahead = row + (kGroupStages - 1) * stride;
+    if (act && ahead < rows) issue(slot == 0 ? kGroupStages - 1 : slot - 1, ahead);
+    cpAsyncCommit();
+    cpAsyncWait<kGroupStages - 1>();  // this thread's copies of `row` have landed
+
+    float4 g = zero, xh = zero, res = zero;
+    if (act) {
+      const int off = slot * stageBytes;
+      g = bf4(*reinterpret_cast<const uint2*>(myG + off));
+      const float4 xv = *reinterpret_cast<const float4*>(myX + off);
+      if (gres) res = *reinterpret_cast<const float4*>(myR + off);
+      xh = make_float4((xv.x - mu) * rs, (xv.y - mu) * rs, (xv.z - mu) * rs, (xv.w - mu) * rs);
+    }
+    const float4 gw = make_float4(g.x * wv.x, g.y * wv.y, g.z * wv.z, g.w * wv.w);
+    float s1 = (gw.x + gw.y) + (gw.z + gw.w);
+    float s2 = (gw.x * xh.x + gw.y * xh.y) + (gw.z * xh.z + gw.w * xh.w);
+    s1 = warpSum(s1);
+    s2 = warpSum(s2);
+    float* red = sRed + ((grp * 2 + parity) * 8) * 2;
+    if (lane == 0) {
+      red[2 * gwarp] = s1;
+      red[2 * gwarp + 1] = s2;
+    }
+    namedBarrier(1 + grp, G);
+    float t1 = 0.f, t2 = 0.f;
+    for (int k = 0; k < nwarps; ++k) {
+      t1 += red[2 * k];
+      t2 += red[2 * k + 1];
+    }
+    const float m1 = t1 * invC, m2 = t2 * invC;
+    if (act) {
+      float4 o;
+      o.x = rs * (gw.x - m1 - xh.x * m2) + res.x;
+      o.y = rs * (gw.y - m1 - xh.y * m2) + res.y;
+      o.z = rs * (gw.z - m1 - xh.z * m2) + res.z;
+      o.w = rs * (gw.w - m1 - xh.w * m2) + res.w;
+      const size_t base = (size_t)row * C;
+      reinterpret_cast<float4*>(dx + base)[gt] = o;
+      if (dxb) reinterpret_cast<uint2*>(dxb + base)[gt] = tobf4(o);
+      aw.x += g.x * xh.x;
+      aw.y += g.y * xh.y;
+      aw.z += g.z * xh.z;
+      aw.w += g.w * xh.w;
+      ab.x += g.x;
+      ab.y += g.y;
+      ab.z += g.z;
+      ab.w += g.w;
+    }
+    mu = nmu;
+    rs = nrs;
+    parity ^= 1;
+    slot = slot + 1 == kGroupStages ? 0 : slot + 1;
   }
   cpAsyncWait<0>();
-  // Combine the warps of this CTA into one partial row of [dw | db], reusing
-  // the stages (8 warps x 2C floats = 64 C bytes <= 80 C S bytes).
+  // Combine the groups of this CTA into one partial row of [dw | db]; the
+  // accumulators reuse the stage memory (R * 2C floats <= R * 3 * 40 G bytes).
   __syncthreads();
-  float* acc = reinterpret_cast<float*>(sPipe);
-  float4* myDw = reinterpret_cast<float4*>(acc + (size_t)warp * C);
-  float4* myDb = reinterpret_cast<float4*>(acc + (size_t)(kPipeWarps + warp) * C);
-#pragma unroll
-  for (int k = 0; k < K; ++k) {
-    const int i = lane + 32 * k;
-    if (i < C4) {
-      myDw[i] = aw[k];
-      myDb[i] = ab[k];
-    }
+  float* acc = reinterpret_cast<float*>(sGroup + kGroupRedFloats);
+  if (act) {
+    reinterpret_cast<float4*>(acc + (size_t)grp * 2 * C)[gt] = aw;
+    reinterpret_cast<float4*>(acc + (size_t)grp * 2 * C + C)[gt] = ab;
   }
   __syncthreads();
-  for (int c = threadIdx.x; c < 2 * C; c += blockDim.x) {
-    const int q = c / C, col = c - q * C;
-    const float* src = acc + (size_t)q * kPipeWarps * C + col;
+  for (int c = t; c < 2 * C; c += blockDim.x) {
     float a = 0.f;
-#pragma unroll
-    for (int wv = 0; wv < kPipeWarps; ++wv) a += src[(size_t)wv * C];
+    for (int q = 0; q < R; ++q) a += acc[(size_t)q * 2 * C + c];
     partial[(size_t)blockIdx.x * 2 * C + c] = a;
   }
 }
@@ -394,37 +403,41 @@ cudaError_t bwdK(const uint16_t* gy, const float* gres, const float* xo, const f
   return cudaGetLastError();
 }
 
-template <int K, int S>
-cudaError_t bwdPipeK(const uint16_t* gy, const float* gres, const float* xo, const float* w,
+// Launches lnBwdGroupKernel; *nparts = the partial rows it writes (<= kSMs).
+cudaError_t bwdGroup(const uint16_t* gy, const float* gres, const float* xo, const float* w,
                      const float* m, const float* r, float* dx, uint16_t* dxb, float* partial,
                      int rows, int C, int* nparts, cudaStream_t st) {
-  static_assert(S >= 2, "at least one row in flight while another is computed");
-  int blocks = (rows + kPipeWarps - 1) / kPipeWarps;
+  const int G = 32 * ((C / 4 + 31) / 32);
+  int R = 1024 / G;
+  if (R > kGroupMaxRows) R = kGroupMaxRows;
+  int blocks = (rows + R - 1) / R;
   if (blocks > kSMs) blocks = kSMs;
   *nparts = blocks;
-  const int smem = S * kPipeWarps * 10 * C;
+  const int smem = kGroupRedFloats * (int)sizeof(float) + R * kGroupStages * groupStageBytes(G);
+  // Largest request (C = 1024: G = 256, R = 4), opted in once per device.
+  constexpr int kMaxSmem = kGroupRedFloats * (int)sizeof(float) + 4 * kGroupStages * 40 * 256;
   static std::atomic<uint64_t> done{0};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   const uint64_t bit = dev < 64 ? (1ull << dev) : 0;
   if (!(done.load(std::memory_order_acquire) & bit)) {
-    e = cudaFuncSetAttribute(lnBwdPipeKernel<K, S>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             S * kPipeWarps * 10 * 128 * K);
+    e = cudaFuncSetAttribute(lnBwdGroupKernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kMaxSmem);
     if (e != cudaSuccess) return e;
     done.fetch_or(bit, std::memory_order_acq_rel);
   }
-  lnBwdPipeKernel<K, S><<<blocks, kPipeWarps * 32, smem, st>>>(gy, gres, xo, w, m, r, dx, dxb,
-                                                               partial, rows, C);
+  lnBwdGroupKernel<<<blocks, R * G, smem, st>>>(gy, gres, xo, w, m, r, dx, dxb, partial, rows, C,
+                                               G, R);
   return cudaGetLastError();
 }
 
-// TNOPS_LN_BWD_PIPE=0 selects the one-row-per-warp kernel for every shape
-// (A/B timing); by default the pipelined kernel takes the shapes it supports.
-bool pipeEnabled() {
+// TNOPS_LN_BWD=warp selects the one-warp-per-row kernel for every shape (A/B
+// timing); by default the row-group kernel takes every aligned input.
+bool groupEnabled() {
   static const bool on = [] {
-    const char* v = getenv("TNOPS_LN_BWD_PIPE");
-    return v == nullptr || v[0] != '0';
+    const char* v = getenv("TNOPS_LN_BWD");
+    return v == nullptr || strcmp(v, "warp") != 0;
   }();
   return on;
 }
@@ -459,19 +472,17 @@ extern "C" int tnops_ln_bwd(const uint16_t* gy, const float* g_res, const float*
                             int C, cudaStream_t stream) {
   if (C % 4 != 0 || C > 128 * 8 || rows <= 0) return (int)cudaErrorInvalidValue;
   const int K = (C + 127) / 128;
-  const uintptr_t rowAlign = reinterpret_cast<uintptr_t>(gy) |
-                             reinterpret_cast<uintptr_t>(g_res) |
-                             reinterpret_cast<uintptr_t>(x_out);
-  if (C % 8 == 0 && (rowAlign & 15) == 0 && pipeEnabled()) {
+  // Both kernels move 4 columns at a time: 8-byte pieces of the bf16 rows and
+  // 16-byte pieces of the fp32 rows (C % 4 == 0 keeps every row on those
+  // boundaries when the base pointers are).
+  const uintptr_t a16 = reinterpret_cast<uintptr_t>(g_res) | reinterpret_cast<uintptr_t>(x_out) |
+                        reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(dx);
+  const uintptr_t a8 = reinterpret_cast<uintptr_t>(gy) | reinterpret_cast<uintptr_t>(dx_bf16);
+  if ((a16 & 15) != 0 || (a8 & 7) != 0) return (int)cudaErrorInvalidValue;
+  if (groupEnabled()) {
     int nparts = 0;
-    cudaError_t e;
-    switch (K) {
-      case 1: e = bwdPipeK<1, 3>(gy, g_res, x_out, w, mean, rstd, dx, dx_bf16, partial, rows, C, &nparts, stream); break;
-      case 2: e = bwdPipeK<2, 3>(gy, g_res, x_out, w, mean, rstd, dx, dx_bf16, partial, rows, C, &nparts, stream); break;
-      case 3: case 4: e = bwdPipeK<4, 3>(gy, g_res, x_out, w, mean, rstd, dx, dx_bf16, partial, rows, C, &nparts, stream); break;
-      case 5: case 6: e = bwdPipeK<6, 3>(gy, g_res, x_out, w, mean, rstd, dx, dx_bf16, partial, rows, C, &nparts, stream); break;
-      default: e = bwdPipeK<8, 2>(gy, g_res, x_out, w, mean, rstd, dx, dx_bf16, partial, rows, C, &nparts, stream); break;
-    }
+    const cudaError_t e = bwdGroup(gy, g_res, x_out, w, mean, rstd, dx, dx_bf16, partial, rows, C,
+                                   &nparts, stream);
     if (launched(e) != 0) return (int)e;
     colReduce<<<(2 * C + 31) / 32, kColReduceWarps * 32, 0, stream>>>(partial, nparts, 2 * C,
                                                                       2 * C, C, dw, db);

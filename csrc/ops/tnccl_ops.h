@@ -25,7 +25,9 @@ int tnops_ln_fwd(const float* x, const uint16_t* delta, const float* w, const fl
 // rstd from the forward. Writes dx fp32 = g_res + dLN/dx, optionally dx_bf16
 // (the same value for the bf16 `delta` input), and dw/db fp32 [C] (overwritten,
 // deterministic two-stage reduction through `partial`, which must hold
-// 2 * tnops_ln_partial_rows() * C floats).
+// 2 * tnops_ln_partial_rows() * C floats). C % 4 == 0 and C <= 1024; g_res,
+// x_out, w and dx 16-byte aligned, gy and dx_bf16 8-byte aligned; anything
+// else returns 1 (invalid argument) without a launch.
 int tnops_ln_bwd(const uint16_t* gy, const float* g_res, const float* x_out, const float* w,
                  const float* mean, const float* rstd, float* dx, uint16_t* dx_bf16, float* dw,
                  float* db, float* partial, int rows, int C, cudaStream_t stream);

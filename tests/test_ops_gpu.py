@@ -1,6 +1,10 @@
 """Fused sm_100a model kernels vs plain PyTorch fp32 references."""
+import sys
+
 import pytest
 import torch
+
+from conftest import run
 
 pytestmark = pytest.mark.gpu
 
@@ -49,6 +53,29 @@ def test_add_layer_norm(ops, rows, C, with_delta):
     torch.testing.assert_close(x.grad, xr.grad, atol=1e-3, rtol=1e-3)
     torch.testing.assert_close(w.grad, wr.grad, atol=1e-2, rtol=1e-3)
     torch.testing.assert_close(b.grad, br.grad, atol=1e-2, rtol=1e-3)
+
+
+@pytest.mark.parametrize("variant", ["group", "warp"])
+def test_ln_bwd_kernel_variants(built, variant):
+    """Both LayerNorm backward kernels (row groups, the default; one warp
+    per row, TNOPS_LN_BWD=warp) against fp32 autograd, in a fresh process
+    because the library reads the switch once."""
+    r = run([sys.executable, "tests/workers/ln_bwd_variant_worker.py"],
+            env={"TNOPS_LN_BWD": variant})
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-3000:]
+
+
+def test_ln_bwd_refuses_misaligned_rows(ops):
+    """Rows that do not start on 16 bytes are refused before any launch."""
+    import tiny_nccl_b200 as tn
+    C, rows = 768, 4
+    base = torch.zeros(rows * C + 1, device="cuda")
+    xo = base[1:].view(rows, C)  # 4 bytes past a 16-byte boundary
+    w = torch.ones(C, device="cuda")
+    stats = torch.ones(rows, device="cuda")
+    gy = torch.zeros(rows, C, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError):
+        tn.load().ops.ln_bwd(gy, None, xo, w, stats, stats, True)
 
 
 @pytest.mark.parametrize("rows,V", [(16, 50257), (7, 1000), (3, 9)])
