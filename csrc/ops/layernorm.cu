@@ -203,27 +203,31 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, 2)
 }
 
 // ---------------------------------------------------------------------------
-// Row-group backward (the default for every supported shape). A group of
-// G = 32 * ceil(C / 128) threads owns one row at a time, one float4 column
-// group per thread; a CTA of R groups (R * G <= 1024, R <= 8) runs one per
-// SM and walks rows blockIdx.x * R + g, + gridDim.x * R, ... Compared with
-// one warp per row this gives each SM ~30 warps instead of 8-16 to hide
-// latency, and every thread carries a few registers of state instead of a
-// whole row slice.
+// Row-group backward (the default). A group of G threads owns one row at a
+// time; each thread owns K consecutive float4 column groups (4K columns:
+// K = 2 when C % 8 == 0 and the bf16 rows are 16-byte aligned, else 1), so
+// G = 32 * ceil(C / (128 K)). A CTA of R groups runs one per SM and walks
+// rows blockIdx.x * R + g, + gridDim.x * R, ... Against one warp per row this
+// gives each SM 24-30 warps instead of 8-16 to hide latency, and every
+// thread carries a few registers of state instead of a whole row slice;
+// K = 2 halves the per-row bookkeeping (row sums, barrier, addressing) per
+// column against K = 1, which issue-bound the kernel.
 //
-// Each thread prefetches its own bytes of the next kGroupStages - 1 rows (gy 8 B,
-// x_out 16 B, residual gradient 16 B) into a per-group ring of shared-memory
-// stages with cp.async; a thread only ever reads what it copied itself, so
-// the copies need no barrier, only cp.async.wait_group. The two row sums
-// (of gy * w and of gy * w * xhat) go through one named barrier per row and
-// group: warp sums are written to a slot double-buffered by row parity, so
-// the next row's writes cannot overwrite values another warp is still
-// reading. Summation order per column: each group's rows in row order, the
-// groups in group order (here), then the CTAs in order (colReduce).
+// Each thread prefetches its own bytes of the next kGroupStages - 1 rows
+// (gy 8K B, x_out and residual gradient 16K B each) into a per-group ring
+// of shared-memory stages with cp.async; a thread only ever reads what it
+// copied itself, so the copies need no barrier, only cp.async.wait_group.
+// The two row sums (of gy * w and of gy * w * xhat) go through one named
+// barrier per row and group: warp sums are written to a slot double-
+// buffered by row parity, so the next row's writes cannot overwrite values
+// another warp is still reading. Summation order per column: each group's
+// rows in row order, the groups in group order (here), then the CTAs in
+// order (colReduce).
 // ---------------------------------------------------------------------------
-constexpr int kGroupMaxRows = 8;   // R limit: named barriers 1..8
+constexpr int kGroupMaxRows = 15;  // R limit: named barriers 1..15
 constexpr int kGroupStages = 3;    // rows in the ring per group (2 ahead)
-constexpr int kGroupRedFloats = kGroupMaxRows * 2 * 8 * 2;  // [R][parity][warp][2]
+constexpr int kGroupRedFloats = 16 * 2 * 8 * 2;  // [R][parity][warp][2]
+constexpr int kGroupSmemBudget = 200 * 1024;     // stage ring bytes per CTA
 
 __device__ __forceinline__ void cpAsync16(void* dst, const void* src) {
   const unsigned s = (unsigned)__cvta_generic_to_shared(dst);
@@ -244,10 +248,12 @@ __device__ __forceinline__ void namedBarrier(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(nthreads) : "memory");
 }
 
-// Bytes of one stage of one group: gy [8 G] | x_out [16 G] | g_res [16 G].
-__host__ __device__ constexpr int groupStageBytes(int G) { return 40 * G; }
+// Bytes of one stage of one group: gy [8K G] | x_out [16K G] | g_res [16K G].
+__host__ __device__ constexpr int groupStageBytes(int K, int G) { return 40 * K * G; }
+__host__ __device__ constexpr int groupMaxThreads(int K) { return K == 1 ? 1024 : 768; }
 
-__global__ void __launch_bounds__(1024, 1)
+template <int K>
+__global__ void __launch_bounds__(groupMaxThreads(K), 1)
     lnBwdGroupKernel(const uint16_t* __restrict__ gy, const float* __restrict__ gres,
                      const float* __restrict__ xo, const float* __restrict__ w,
                      const float* __restrict__ mean, const float* __restrict__ rstd,
@@ -256,31 +262,43 @@ __global__ void __launch_bounds__(1024, 1)
   extern __shared__ __align__(16) float sGroup[];
   const int t = threadIdx.x;
   const int grp = t / G;
-  const int gt = t - grp * G;  // this thread's float4 column group
+  const int gt = t - grp * G;  // this thread owns float4 groups K*gt .. K*gt+K-1
   const int lane = t & 31, gwarp = gt >> 5, nwarps = G >> 5;
-  const int C4 = C >> 2;
-  const bool act = gt < C4;
+  const bool act = gt < (C >> 2) / K;
   const float invC = 1.0f / (float)C;
-  float* sRed = sGroup;
+  const int stageBytes = groupStageBytes(K, G);
   char* ring = reinterpret_cast<char*>(sGroup + kGroupRedFloats) +
-               (size_t)grp * kGroupStages * groupStageBytes(G);
-  char* myG = ring + 8 * gt;            // + stage * stageBytes
-  char* myX = ring + 8 * G + 16 * gt;
-  char* myR = ring + 24 * G + 16 * gt;
-  const int stageBytes = groupStageBytes(G);
+               (size_t)grp * kGroupStages * stageBytes;
+  char* myG = ring + 8 * K * gt;  // + stage * stageBytes
+  char* myX = ring + 8 * K * G + 16 * K * gt;
+  char* myR = ring + 24 * K * G + 16 * K * gt;
+  const int col = 4 * K * gt;     // first column of this thread
 
   const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
-  const float4 wv = act ? reinterpret_cast<const float4*>(w)[gt] : zero;
-  float4 aw = zero, ab = zero;
+  float4 wv[K], aw[K], ab[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    wv[k] = act ? reinterpret_cast<const float4*>(w + col)[k] : zero;
+    aw[k] = zero;
+    ab[k] = zero;
+  }
   const int stride = gridDim.x * R;
   const int first = blockIdx.x * R + grp;
 
   auto issue = [&](int stage, int row) {
-    const size_t base = (size_t)row * C;
+    const size_t base = (size_t)row * C + col;
     const int off = stage * stageBytes;
-    cpAsync8(myG + off, reinterpret_cast<const uint2*>(gy + base) + gt);
-    cpAsync16(myX + off, reinterpret_cast<const float4*>(xo + base) + gt);
-    if (gres) cpAsync16(myR + off, reinterpret_cast<const float4*>(gres + base) + gt);
+    if (K == 2) {
+      cpAsync16(myG + off, gy + base);
+    } else {
+      cpAsync8(myG + off, gy + base);
+    }
+#pragma unroll
+    for (int k = 0; k < K; ++k) cpAsync16(myX + off + 16 * k, xo + base + 4 * k);
+    if (gres) {
+#pragma unroll
+      for (int k = 0; k < K; ++k) cpAsync16(myR + off + 16 * k, gres + base + 4 * k);
+    }
   };
 #pragma unroll
   for (int j = 0; j < kGroupStages - 1; ++j) {
@@ -306,48 +324,68 @@ __global__ void __launch_bounds__(1024, 1)
     cpAsyncCommit();
     cpAsyncWait<kGroupStages - 1>();  // this thread's copies of `row` have landed
 
-    float4 g = zero, xh = zero, res = zero;
-    if (act) {
-      const int off = slot * stageBytes;
-      g = bf4(*reinterpret_cast<const uint2*>(myG + off));
-      const float4 xv = *reinterpret_cast<const float4*>(myX + off);
-      if (gres) res = *reinterpret_cast<const float4*>(myR + off);
-      xh = make_float4((xv.x - mu) * rs, (xv.y - mu) * rs, (xv.z - mu) * rs, (xv.w - mu) * rs);
+    float4 g[K], xh[K], res[K];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      g[k] = zero;
+      xh[k] = zero;
+      res[k] = zero;
+      if (act) {
+        const int off = slot * stageBytes;
+        g[k] = bf4(reinterpret_cast<const uint2*>(myG + off)[k]);
+        const float4 xv = reinterpret_cast<const float4*>(myX + off)[k];
+        if (gres) res[k] = reinterpret_cast<const float4*>(myR + off)[k];
+        xh[k] = make_float4((xv.x - mu) * rs, (xv.y - mu) * rs, (xv.z - mu) * rs,
+                            (xv.w - mu) * rs);
+      }
+      // g becomes gy * w from here on; the dW / dB sums use gy itself.
+      aw[k].x += g[k].x * xh[k].x;
+      aw[k].y += g[k].y * xh[k].y;
+      aw[k].z += g[k].z * xh[k].z;
+      aw[k].w += g[k].w * xh[k].w;
+      ab[k].x += g[k].x;
+      ab[k].y += g[k].y;
+      ab[k].z += g[k].z;
+      ab[k].w += g[k].w;
+      g[k] = make_float4(g[k].x * wv[k].x, g[k].y * wv[k].y, g[k].z * wv[k].z, g[k].w * wv[k].w);
+      s1 += (g[k].x + g[k].y) + (g[k].z + g[k].w);
+      s2 += (g[k].x * xh[k].x + g[k].y * xh[k].y) + (g[k].z * xh[k].z + g[k].w * xh[k].w);
     }
-    const float4 gw = make_float4(g.x * wv.x, g.y * wv.y, g.z * wv.z, g.w * wv.w);
-    float s1 = (gw.x + gw.y) + (gw.z + gw.w);
-    float s2 = (gw.x * xh.x + gw.y * xh.y) + (gw.z * xh.z + gw.w * xh.w);
     s1 = warpSum(s1);
     s2 = warpSum(s2);
-    float* red = sRed + ((grp * 2 + parity) * 8) * 2;
-    if (lane == 0) {
-      red[2 * gwarp] = s1;
-      red[2 * gwarp + 1] = s2;
-    }
+    float2* red = reinterpret_cast<float2*>(sGroup) + (grp * 2 + parity) * 8;
+    if (lane == 0) red[gwarp] = make_float2(s1, s2);
     namedBarrier(1 + grp, G);
     float t1 = 0.f, t2 = 0.f;
-    for (int k = 0; k < nwarps; ++k) {
-      t1 += red[2 * k];
-      t2 += red[2 * k + 1];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (k < nwarps) {
+        const float2 v = red[k];
+        t1 += v.x;
+        t2 += v.y;
+      }
     }
     const float m1 = t1 * invC, m2 = t2 * invC;
     if (act) {
-      float4 o;
-      o.x = rs * (gw.x - m1 - xh.x * m2) + res.x;
-      o.y = rs * (gw.y - m1 - xh.y * m2) + res.y;
-      o.z = rs * (gw.z - m1 - xh.z * m2) + res.z;
-      o.w = rs * (gw.w - m1 - xh.w * m2) + res.w;
-      const size_t base = (size_t)row * C;
-      reinterpret_cast<float4*>(dx + base)[gt] = o;
-      if (dxb) reinterpret_cast<uint2*>(dxb + base)[gt] = tobf4(o);
-      aw.x += g.x * xh.x;
-      aw.y += g.y * xh.y;
-      aw.z += g.z * xh.z;
-      aw.w += g.w * xh.w;
-      ab.x += g.x;
-      ab.y += g.y;
-      ab.z += g.z;
-      ab.w += g.w;
+      const size_t base = (size_t)row * C + col;
+      float4 o[K];
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        o[k].x = rs * (g[k].x - m1 - xh[k].x * m2) + res[k].x;
+        o[k].y = rs * (g[k].y - m1 - xh[k].y * m2) + res[k].y;
+        o[k].z = rs * (g[k].z - m1 - xh[k].z * m2) + res[k].z;
+        o[k].w = rs * (g[k].w - m1 - xh[k].w * m2) + res[k].w;
+        reinterpret_cast<float4*>(dx + base)[k] = o[k];
+      }
+      if (dxb) {
+        if (K == 2) {
+          const uint2 lo = tobf4(o[0]), hi = tobf4(o[K - 1]);
+          *reinterpret_cast<uint4*>(dxb + base) = make_uint4(lo.x, lo.y, hi.x, hi.y);
+        } else {
+          *reinterpret_cast<uint2*>(dxb + base) = tobf4(o[0]);
+        }
+      }
     }
     mu = nmu;
     rs = nrs;
@@ -356,12 +394,15 @@ __global__ void __launch_bounds__(1024, 1)
   }
   cpAsyncWait<0>();
   // Combine the groups of this CTA into one partial row of [dw | db]; the
-  // accumulators reuse the stage memory (R * 2C floats <= R * 3 * 40 G bytes).
+  // accumulators reuse the stage memory (R * 2C floats <= R * 3 * 40 K G bytes).
   __syncthreads();
-  float* acc = reinterpret_cast<float*>(sGroup + kGroupRedFloats);
+  float* acc = sGroup + kGroupRedFloats;
   if (act) {
-    reinterpret_cast<float4*>(acc + (size_t)grp * 2 * C)[gt] = aw;
-    reinterpret_cast<float4*>(acc + (size_t)grp * 2 * C + C)[gt] = ab;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      reinterpret_cast<float4*>(acc + (size_t)grp * 2 * C + col)[k] = aw[k];
+      reinterpret_cast<float4*>(acc + (size_t)grp * 2 * C + C + col)[k] = ab[k];
+    }
   }
   __syncthreads();
   for (int c = t; c < 2 * C; c += blockDim.x) {
@@ -403,32 +444,34 @@ cudaError_t bwdK(const uint16_t* gy, const float* gres, const float* xo, const f
   return cudaGetLastError();
 }
 
-// Launches lnBwdGroupKernel; *nparts = the partial rows it writes (<= kSMs).
+// Launches lnBwdGroupKernel<K>; *nparts = the partial rows it writes (<= kSMs).
+template <int K>
 cudaError_t bwdGroup(const uint16_t* gy, const float* gres, const float* xo, const float* w,
                      const float* m, const float* r, float* dx, uint16_t* dxb, float* partial,
                      int rows, int C, int* nparts, cudaStream_t st) {
-  const int G = 32 * ((C / 4 + 31) / 32);
-  int R = 1024 / G;
+  const int G = 32 * ((C / (4 * K) + 31) / 32);
+  int R = groupMaxThreads(K) / G;
   if (R > kGroupMaxRows) R = kGroupMaxRows;
+  const int ringR = kGroupSmemBudget / (kGroupStages * groupStageBytes(K, G));
+  if (R > ringR) R = ringR;
   int blocks = (rows + R - 1) / R;
   if (blocks > kSMs) blocks = kSMs;
   *nparts = blocks;
-  const int smem = kGroupRedFloats * (int)sizeof(float) + R * kGroupStages * groupStageBytes(G);
-  // Largest request (C = 1024: G = 256, R = 4), opted in once per device.
-  constexpr int kMaxSmem = kGroupRedFloats * (int)sizeof(float) + 4 * kGroupStages * 40 * 256;
+  const int smem = kGroupRedFloats * (int)sizeof(float) + R * kGroupStages * groupStageBytes(K, G);
+  constexpr int kMaxSmem = kGroupRedFloats * (int)sizeof(float) + kGroupSmemBudget;
   static std::atomic<uint64_t> done{0};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   const uint64_t bit = dev < 64 ? (1ull << dev) : 0;
   if (!(done.load(std::memory_order_acquire) & bit)) {
-    e = cudaFuncSetAttribute(lnBwdGroupKernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(lnBwdGroupKernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kMaxSmem);
     if (e != cudaSuccess) return e;
     done.fetch_or(bit, std::memory_order_acq_rel);
   }
-  lnBwdGroupKernel<<<blocks, R * G, smem, st>>>(gy, gres, xo, w, m, r, dx, dxb, partial, rows, C,
-                                               G, R);
+  lnBwdGroupKernel<K><<<blocks, R * G, smem, st>>>(gy, gres, xo, w, m, r, dx, dxb, partial, rows,
+                                                  C, G, R);
   return cudaGetLastError();
 }
 
@@ -481,8 +524,13 @@ extern "C" int tnops_ln_bwd(const uint16_t* gy, const float* g_res, const float*
   if ((a16 & 15) != 0 || (a8 & 7) != 0) return (int)cudaErrorInvalidValue;
   if (groupEnabled()) {
     int nparts = 0;
-    const cudaError_t e = bwdGroup(gy, g_res, x_out, w, mean, rstd, dx, dx_bf16, partial, rows, C,
-                                   &nparts, stream);
+    // Two float4 groups per thread where the bf16 rows allow 16-byte pieces.
+    const bool pairs = C % 8 == 0 && (a8 & 15) == 0;
+    const cudaError_t e =
+        pairs ? bwdGroup<2>(gy, g_res, x_out, w, mean, rstd, dx, dx_bf16, partial, rows, C,
+                            &nparts, stream)
+              : bwdGroup<1>(gy, g_res, x_out, w, mean, rstd, dx, dx_bf16, partial, rows, C,
+                            &nparts, stream);
     if (launched(e) != 0) return (int)e;
     colReduce<<<(2 * C + 31) / 32, kColReduceWarps * 32, 0, stream>>>(partial, nparts, 2 * C,
                                                                       2 * C, C, dw, db);
