@@ -111,7 +111,6 @@ __global__ void __launch_bounds__(kWarps * 32)
       }
     }
   }
-  allowDependentLaunch();
 #pragma unroll
   for (int e = 0; e < 8; ++e) sAcc[w][lane * 8 + e] = acc[e];
   __syncthreads();
@@ -147,11 +146,10 @@ static int launchColsum(const uint16_t* gy, const uint16_t* pre, uint16_t* gout,
     colsumPartial<true><<<grid, kWarps * 32, 0, stream>>>(gy, pre, gout, partial, M, N, rowsPer);
   else
     colsumPartial<false><<<grid, kWarps * 32, 0, stream>>>(gy, pre, gout, partial, M, N, rowsPer);
-  if (cudaGetLastError() != cudaSuccess) return 2;
-  gLaunches.fetch_add(1, std::memory_order_relaxed);
-  if (launchColReduce(partial, parts, N, N, N, db, nullptr, stream) != cudaSuccess) return 2;
-  gLaunches.fetch_add(1, std::memory_order_relaxed);
-  return 0;
+  colReduce<<<(N + 31) / 32, kColReduceWarps * 32, 0, stream>>>(partial, parts, N, N, N, db,
+                                                                 nullptr);
+  gLaunches.fetch_add(2, std::memory_order_relaxed);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }
 
 // partial: tnops_colsum_parts(M, N) * N floats of scratch.

@@ -4,7 +4,6 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
-#include <stdlib.h>
 
 #include <atomic>
 
@@ -61,10 +60,6 @@ __global__ void __launch_bounds__(kColReduceWarps * 32)
     colReduce(const float* __restrict__ in, int nparts, int ld, int ncols, int split,
               float* __restrict__ out0, float* __restrict__ out1) {
   __shared__ float s[kColReduceWarps][33];
-  // Launched as a programmatic dependent of the kernel that wrote `in`
-  // (launchColReduce): wait until that grid has completed and its writes are
-  // visible. Returns at once for an ordinary launch.
-  asm volatile("griddepcontrol.wait;\n" ::: "memory");
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int col = blockIdx.x * 32 + lane;
   float acc = 0.f;
@@ -93,51 +88,5 @@ __global__ void __launch_bounds__(kColReduceWarps * 32)
   }
 }
 }  // namespace
-
-// Lets the next kernel on the stream, when it was launched as a programmatic
-// dependent, be scheduled from here on (it still waits for this grid to
-// complete in griddepcontrol.wait). A no-op otherwise.
-__device__ __forceinline__ void allowDependentLaunch() {
-  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
-}
-
-// TNOPS_PDL=0 launches the column-sum second pass as an ordinary
-// stream-ordered kernel instead of a programmatic dependent launch.
-inline bool pdlEnabled() {
-  static const bool on = [] {
-    const char* v = getenv("TNOPS_PDL");
-    return v == nullptr || v[0] != '0';
-  }();
-  return on;
-}
-
-// Second pass of a column sum, launched with programmatic stream
-// serialization: its CTAs can be scheduled while the first pass drains (once
-// every first-pass CTA has called allowDependentLaunch or exited), hiding
-// the launch latency of this short kernel; colReduce itself waits for the
-// first pass in griddepcontrol.wait. Falls back to an ordinary launch if the
-// attribute is refused.
-inline cudaError_t launchColReduce(const float* in, int nparts, int ld, int ncols, int split,
-                                   float* out0, float* out1, cudaStream_t st) {
-  const dim3 grid((unsigned)((ncols + 31) / 32)), block(kColReduceWarps * 32);
-  if (pdlEnabled()) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = block;
-    cfg.dynamicSmemBytes = 0;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    const cudaError_t e =
-        cudaLaunchKernelEx(&cfg, colReduce, in, nparts, ld, ncols, split, out0, out1);
-    if (e == cudaSuccess) return e;
-    (void)cudaGetLastError();  // the refused launch's own (non-sticky) error
-  }
-  colReduce<<<grid, block, 0, st>>>(in, nparts, ld, ncols, split, out0, out1);
-  return cudaGetLastError();
-}
 
 }  // namespace tnops

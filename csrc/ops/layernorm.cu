@@ -393,7 +393,6 @@ __global__ void __launch_bounds__(groupMaxThreads(K), 1)
     slot = slot + 1 == kGroupStages ? 0 : slot + 1;
   }
   cpAsyncWait<0>();
-  allowDependentLaunch();
   // Combine the groups of this CTA into one partial row of [dw | db]; the
   // accumulators reuse the stage memory (R * 2C floats <= R * 3 * 40 K G bytes).
   __syncthreads();
@@ -533,7 +532,9 @@ extern "C" int tnops_ln_bwd(const uint16_t* gy, const float* g_res, const float*
               : bwdGroup<1>(gy, g_res, x_out, w, mean, rstd, dx, dx_bf16, partial, rows, C,
                             &nparts, stream);
     if (launched(e) != 0) return (int)e;
-    return launched(launchColReduce(partial, nparts, 2 * C, 2 * C, C, dw, db, stream));
+    colReduce<<<(2 * C + 31) / 32, kColReduceWarps * 32, 0, stream>>>(partial, nparts, 2 * C,
+                                                                      2 * C, C, dw, db);
+    return launched(cudaGetLastError());
   }
   cudaError_t e;
   switch (K) {
@@ -547,7 +548,9 @@ extern "C" int tnops_ln_bwd(const uint16_t* gy, const float* g_res, const float*
   int nparts = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock;
   if (nparts > kPartialRows) nparts = kPartialRows;
   // dw = column sums of the first C partial columns, db of the next C.
-  return launched(launchColReduce(partial, nparts, 2 * C, 2 * C, C, dw, db, stream));
+  colReduce<<<(2 * C + 31) / 32, kColReduceWarps * 32, 0, stream>>>(partial, nparts, 2 * C,
+                                                                    2 * C, C, dw, db);
+  return launched(cudaGetLastError());
 }
 
 // ---------------------------------------------------------------------------
