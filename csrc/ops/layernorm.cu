@@ -412,148 +412,6 @@ __global__ void __launch_bounds__(groupMaxThreads(K), 1)
   }
 }
 
-// Row-group forward, the same layout as lnBwdGroupKernel: a group of G
-// threads per row, K float4 column groups per thread, R groups per CTA and
-// one CTA per SM, each thread prefetching its own bytes of x and delta two
-// rows ahead with cp.async. Two named barriers per row and group join the
-// row sums: the mean, then the sum of squared deviations (two passes over
-// the registers, as in the one-warp kernel, so a large mean does not cancel
-// the variance). The sums use separate slots, so no parity is needed: a
-// thread writes the first sum of row j+1 only after the second barrier of
-// row j, which every thread reaches after reading the first sum of row j
-// (and likewise for the second sum across the next first barrier).
-// Stage bytes per group: x [16K G] | delta [8K G].
-__host__ __device__ constexpr int fwdStageBytes(int K, int G) { return 24 * K * G; }
-
-template <int K>
-__global__ void __launch_bounds__(groupMaxThreads(K), 1)
-    lnFwdGroupKernel(const float* __restrict__ x, const uint16_t* __restrict__ delta,
-                     const float* __restrict__ w, const float* __restrict__ b,
-                     float* __restrict__ xo, uint16_t* __restrict__ y,
-                     float* __restrict__ mean, float* __restrict__ rstd, int rows, int C,
-                     float eps, int G, int R) {
-  extern __shared__ __align__(16) float sGroup[];
-  const int t = threadIdx.x;
-  const int grp = t / G;
-  const int gt = t - grp * G;
-  const int lane = t & 31, gwarp = gt >> 5, nwarps = G >> 5;
-  const bool act = gt < (C >> 2) / K;
-  const float invC = 1.0f / (float)C;
-  const int stageBytes = fwdStageBytes(K, G);
-  char* ring = reinterpret_cast<char*>(sGroup + kGroupRedFloats) +
-               (size_t)grp * kGroupStages * stageBytes;
-  char* myX = ring + 16 * K * gt;
-  char* myD = ring + 16 * K * G + 8 * K * gt;
-  const int col = 4 * K * gt;
-
-  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
-  float4 wv[K], bv[K];
-#pragma unroll
-  for (int k = 0; k < K; ++k) {
-    wv[k] = act ? reinterpret_cast<const float4*>(w + col)[k] : zero;
-    bv[k] = act ? reinterpret_cast<const float4*>(b + col)[k] : zero;
-  }
-  const int stride = gridDim.x * R;
-  const int first = blockIdx.x * R + grp;
-  auto issue = [&](int stage, int row) {
-    const size_t base = (size_t)row * C + col;
-    const int off = stage * stageBytes;
-#pragma unroll
-    for (int k = 0; k < K; ++k) cpAsync16(myX + off + 16 * k, x + base + 4 * k);
-    if (delta) {
-      if (K == 2) {
-        cpAsync16(myD + off, delta + base);
-      } else {
-        cpAsync8(myD + off, delta + base);
-      }
-    }
-  };
-#pragma unroll
-  for (int j = 0; j < kGroupStages - 1; ++j) {
-    const int row = first + j * stride;
-    if (act && row < rows) issue(j, row);
-    cpAsyncCommit();
-  }
-  // [R][2 sums][8 warps]
-  float* red1 = sGroup + grp * 16;
-  float* red2 = red1 + 8;
-  int slot = 0;
-  for (int row = first; row < rows; row += stride) {
-    const int ahead = row + (kGroupStages - 1) * stride;
-    if (act && ahead < rows) issue(slot == 0 ? kGroupStages - 1 : slot - 1, ahead);
-    cpAsyncCommit();
-    cpAsyncWait<kGroupStages - 1>();
-
-    const size_t base = (size_t)row * C + col;
-    float4 v[K];
-    float s = 0.f;
-#pragma unroll
-    for (int k = 0; k < K; ++k) {
-      v[k] = zero;
-      if (act) {
-        const int off = slot * stageBytes;
-        v[k] = reinterpret_cast<const float4*>(myX + off)[k];
-        if (delta) {
-          const float4 d = bf4(reinterpret_cast<const uint2*>(myD + off)[k]);
-          v[k].x += d.x;
-          v[k].y += d.y;
-          v[k].z += d.z;
-          v[k].w += d.w;
-        }
-        reinterpret_cast<float4*>(xo + base)[k] = v[k];
-      }
-      s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
-    }
-    s = warpSum(s);
-    if (lane == 0) red1[gwarp] = s;
-    namedBarrier(1 + grp, G);
-    float tot = 0.f;
-#pragma unroll
-    for (int k = 0; k < 8; ++k)
-      if (k < nwarps) tot += red1[k];
-    const float mu = tot * invC;
-    float q = 0.f;
-#pragma unroll
-    for (int k = 0; k < K; ++k) {
-      if (act) {
-        const float a = v[k].x - mu, bb = v[k].y - mu, c = v[k].z - mu, d = v[k].w - mu;
-        q += (a * a + bb * bb) + (c * c + d * d);
-      }
-    }
-    q = warpSum(q);
-    if (lane == 0) red2[gwarp] = q;
-    namedBarrier(1 + grp, G);
-    float qt = 0.f;
-#pragma unroll
-    for (int k = 0; k < 8; ++k)
-      if (k < nwarps) qt += red2[k];
-    const float rs = rsqrtf(qt * invC + eps);
-    if (act) {
-      uint2 o[K];
-#pragma unroll
-      for (int k = 0; k < K; ++k) {
-        float4 r;
-        r.x = (v[k].x - mu) * rs * wv[k].x + bv[k].x;
-        r.y = (v[k].y - mu) * rs * wv[k].y + bv[k].y;
-        r.z = (v[k].z - mu) * rs * wv[k].z + bv[k].z;
-        r.w = (v[k].w - mu) * rs * wv[k].w + bv[k].w;
-        o[k] = tobf4(r);
-      }
-      if (K == 2) {
-        *reinterpret_cast<uint4*>(y + base) = make_uint4(o[0].x, o[0].y, o[K - 1].x, o[K - 1].y);
-      } else {
-        *reinterpret_cast<uint2*>(y + base) = o[0];
-      }
-    }
-    if (gt == 0) {
-      mean[row] = mu;
-      rstd[row] = rs;
-    }
-    slot = slot + 1 == kGroupStages ? 0 : slot + 1;
-  }
-  cpAsyncWait<0>();
-}
-
 template <int K>
 cudaError_t fwdK(const float* x, const uint16_t* d, const float* w, const float* b, float* xo,
                  uint16_t* y, float* m, float* r, int rows, int C, float eps, cudaStream_t st) {
@@ -617,44 +475,6 @@ cudaError_t bwdGroup(const uint16_t* gy, const float* gres, const float* xo, con
   return cudaGetLastError();
 }
 
-// Launches lnFwdGroupKernel<K> (G <= 256: at most 8 warps per row group).
-template <int K>
-cudaError_t fwdGroup(const float* x, const uint16_t* d, const float* w, const float* b,
-                     float* xo, uint16_t* y, float* m, float* r, int rows, int C, float eps,
-                     cudaStream_t st) {
-  const int G = 32 * ((C / (4 * K) + 31) / 32);
-  int R = groupMaxThreads(K) / G;
-  if (R > kGroupMaxRows) R = kGroupMaxRows;
-  const int ringR = kGroupSmemBudget / (kGroupStages * fwdStageBytes(K, G));
-  if (R > ringR) R = ringR;
-  int blocks = (rows + R - 1) / R;
-  if (blocks > kSMs) blocks = kSMs;
-  const int smem = kGroupRedFloats * (int)sizeof(float) + R * kGroupStages * fwdStageBytes(K, G);
-  constexpr int kMaxSmem = kGroupRedFloats * (int)sizeof(float) + kGroupSmemBudget;
-  static std::atomic<uint64_t> done{0};
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  const uint64_t bit = dev < 64 ? (1ull << dev) : 0;
-  if (!(done.load(std::memory_order_acquire) & bit)) {
-    e = cudaFuncSetAttribute(lnFwdGroupKernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kMaxSmem);
-    if (e != cudaSuccess) return e;
-    done.fetch_or(bit, std::memory_order_acq_rel);
-  }
-  lnFwdGroupKernel<K><<<blocks, R * G, smem, st>>>(x, d, w, b, xo, y, m, r, rows, C, eps, G, R);
-  return cudaGetLastError();
-}
-
-// TNOPS_LN_FWD=warp selects the one-warp-per-row forward (A/B timing).
-bool fwdGroupEnabled() {
-  static const bool on = [] {
-    const char* v = getenv("TNOPS_LN_FWD");
-    return v == nullptr || strcmp(v, "warp") != 0;
-  }();
-  return on;
-}
-
 // TNOPS_LN_BWD=warp selects the one-warp-per-row kernel for every shape (A/B
 // timing); by default the row-group kernel takes every aligned input.
 bool groupEnabled() {
@@ -676,20 +496,6 @@ extern "C" int tnops_ln_fwd(const float* x, const uint16_t* delta, const float* 
                             float* x_out, uint16_t* y, float* mean, float* rstd, int rows, int C,
                             float eps, cudaStream_t stream) {
   if (C % 4 != 0 || C > 128 * 16 || rows <= 0) return (int)cudaErrorInvalidValue;
-  // Every kernel moves 4 columns at a time: 16-byte pieces of the fp32 rows
-  // and parameters, 8-byte pieces of the bf16 rows.
-  const uintptr_t a16 = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(x_out) |
-                        reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(b);
-  const uintptr_t a8 = reinterpret_cast<uintptr_t>(delta) | reinterpret_cast<uintptr_t>(y);
-  if ((a16 & 15) != 0 || (a8 & 7) != 0) return (int)cudaErrorInvalidValue;
-  if (fwdGroupEnabled()) {
-    // Two float4 groups per thread where the bf16 rows allow 16-byte pieces;
-    // one per thread up to C = 1024 otherwise (at most 8 warps per row).
-    if (C % 8 == 0 && (a8 & 15) == 0)
-      return launched(fwdGroup<2>(x, delta, w, b, x_out, y, mean, rstd, rows, C, eps, stream));
-    if (C <= 1024)
-      return launched(fwdGroup<1>(x, delta, w, b, x_out, y, mean, rstd, rows, C, eps, stream));
-  }
   const int K = (C + 127) / 128;
   cudaError_t e;
   switch (K) {
