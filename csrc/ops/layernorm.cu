@@ -15,6 +15,7 @@
 #include <string.h>
 
 #include "common.cuh"
+#include "ln_plan.h"
 #include "tnccl_ops.h"
 
 namespace tnops {
@@ -222,12 +223,10 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, 2)
 // buffered by row parity, so the next row's writes cannot overwrite values
 // another warp is still reading. Summation order per column: each group's
 // rows in row order, the groups in group order (here), then the CTAs in
-// order (colReduce).
+// order (colReduce). Launch geometry and shared-memory layout: ln_plan.h.
 // ---------------------------------------------------------------------------
-constexpr int kGroupMaxRows = 15;  // R limit: named barriers 1..15
-constexpr int kGroupStages = 3;    // rows in the ring per group (2 ahead)
-constexpr int kGroupRedFloats = 16 * 2 * 8 * 2;  // [R][parity][warp][2]
-constexpr int kGroupSmemBudget = 200 * 1024;     // stage ring bytes per CTA
+constexpr int kGroupStages = kLnStages;
+constexpr int kGroupRedFloats = kLnRedFloats;
 
 __device__ __forceinline__ void cpAsync16(void* dst, const void* src) {
   const unsigned s = (unsigned)__cvta_generic_to_shared(dst);
@@ -248,12 +247,8 @@ __device__ __forceinline__ void namedBarrier(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(nthreads) : "memory");
 }
 
-// Bytes of one stage of one group: gy [8K G] | x_out [16K G] | g_res [16K G].
-__host__ __device__ constexpr int groupStageBytes(int K, int G) { return 40 * K * G; }
-__host__ __device__ constexpr int groupMaxThreads(int K) { return K == 1 ? 1024 : 768; }
-
 template <int K>
-__global__ void __launch_bounds__(groupMaxThreads(K), 1)
+__global__ void __launch_bounds__(lnMaxThreads(K), 1)
     lnBwdGroupKernel(const uint16_t* __restrict__ gy, const float* __restrict__ gres,
                      const float* __restrict__ xo, const float* __restrict__ w,
                      const float* __restrict__ mean, const float* __restrict__ rstd,
@@ -266,7 +261,7 @@ __global__ void __launch_bounds__(groupMaxThreads(K), 1)
   const int lane = t & 31, gwarp = gt >> 5, nwarps = G >> 5;
   const bool act = gt < (C >> 2) / K;
   const float invC = 1.0f / (float)C;
-  const int stageBytes = groupStageBytes(K, G);
+  const int stageBytes = lnStageBytes(K, G);
   char* ring = reinterpret_cast<char*>(sGroup + kGroupRedFloats) +
                (size_t)grp * kGroupStages * stageBytes;
   char* myG = ring + 8 * K * gt;  // + stage * stageBytes
@@ -354,12 +349,12 @@ __global__ void __launch_bounds__(groupMaxThreads(K), 1)
     }
     s1 = warpSum(s1);
     s2 = warpSum(s2);
-    float2* red = reinterpret_cast<float2*>(sGroup) + (grp * 2 + parity) * 8;
+    float2* red = reinterpret_cast<float2*>(sGroup) + (grp * 2 + parity) * kLnMaxWarpsPerGroup;
     if (lane == 0) red[gwarp] = make_float2(s1, s2);
     namedBarrier(1 + grp, G);
     float t1 = 0.f, t2 = 0.f;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
+    for (int k = 0; k < kLnMaxWarpsPerGroup; ++k) {
       if (k < nwarps) {
         const float2 v = red[k];
         t1 += v.x;
@@ -449,16 +444,8 @@ template <int K>
 cudaError_t bwdGroup(const uint16_t* gy, const float* gres, const float* xo, const float* w,
                      const float* m, const float* r, float* dx, uint16_t* dxb, float* partial,
                      int rows, int C, int* nparts, cudaStream_t st) {
-  const int G = 32 * ((C / (4 * K) + 31) / 32);
-  int R = groupMaxThreads(K) / G;
-  if (R > kGroupMaxRows) R = kGroupMaxRows;
-  const int ringR = kGroupSmemBudget / (kGroupStages * groupStageBytes(K, G));
-  if (R > ringR) R = ringR;
-  int blocks = (rows + R - 1) / R;
-  if (blocks > kSMs) blocks = kSMs;
-  *nparts = blocks;
-  const int smem = kGroupRedFloats * (int)sizeof(float) + R * kGroupStages * groupStageBytes(K, G);
-  constexpr int kMaxSmem = kGroupRedFloats * (int)sizeof(float) + kGroupSmemBudget;
+  const LnGroupPlan plan = lnGroupPlan(rows, C, K, kSMs);
+  *nparts = plan.blocks;
   static std::atomic<uint64_t> done{0};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -466,12 +453,12 @@ cudaError_t bwdGroup(const uint16_t* gy, const float* gres, const float* xo, con
   const uint64_t bit = dev < 64 ? (1ull << dev) : 0;
   if (!(done.load(std::memory_order_acquire) & bit)) {
     e = cudaFuncSetAttribute(lnBwdGroupKernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kMaxSmem);
+                             kLnMaxSmemBytes);
     if (e != cudaSuccess) return e;
     done.fetch_or(bit, std::memory_order_acq_rel);
   }
-  lnBwdGroupKernel<K><<<blocks, R * G, smem, st>>>(gy, gres, xo, w, m, r, dx, dxb, partial, rows,
-                                                  C, G, R);
+  lnBwdGroupKernel<K><<<plan.blocks, plan.R * plan.G, plan.smemBytes, st>>>(
+      gy, gres, xo, w, m, r, dx, dxb, partial, rows, C, plan.G, plan.R);
   return cudaGetLastError();
 }
 

@@ -118,6 +118,15 @@ def test_gemm_pipeline_model(built):
     assert "gemm_pipeline_model_test: PASS" in r.stdout
 
 
+def test_ln_plan(built):
+    """Launch geometry of the row-group LayerNorm backward (the header the
+    launcher uses) for every C and a spread of row counts, its row walk and
+    stage ring, and the parity-buffered warp sums with real threads."""
+    r = run([os.path.join(ROOT, "build", "bin", "ln_plan_test")], timeout=300)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "ln_plan_test:" in r.stdout and "PASS" in r.stdout
+
+
 def test_config_and_partitions(built):
     r = run([os.path.join(ROOT, "build", "bin", "config_test")], timeout=120)
     assert r.returncode == 0, r.stdout + r.stderr

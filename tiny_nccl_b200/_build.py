@@ -184,6 +184,8 @@ PROGRAMS = {
     "net_proxy_test": ROOT / "tests" / "cpp" / "net_proxy_test.cc",
     # mbarrier hand-offs of the tcgen05 GEMM pipelines, as threads
     "gemm_pipeline_model_test": ROOT / "tests" / "cpp" / "gemm_pipeline_model_test.cc",
+    # launch geometry and schedule of the row-group LayerNorm backward
+    "ln_plan_test": ROOT / "tests" / "cpp" / "ln_plan_test.cc",
     # host configuration / partition checks, built with the library's config code
     "config_test": (ROOT / "tests" / "cpp" / "config_test.cc", TNCCL_SRC / "common.cc"),
 }
@@ -228,15 +230,15 @@ def build_programs() -> list[Path]:
         out = BIN / name
         stamp = BIN / (name + ".stamp")
         deps = srcs + _headers(ROOT / "tests" / "cpp") + _headers(TNCCL_SRC) + \
-            [ROOT / "include" / "tnccl.h"]
+            _headers(OPS_SRC) + [ROOT / "include" / "tnccl.h"]
         key = _hash(deps, "prog " + " ".join(CXXFLAGS) + str(lib.stat().st_size))
         if not (out.exists() and stamp.exists() and stamp.read_text() == key):
             objs = []
             for k, src in enumerate(srcs):
                 obj = OBJ / "bin" / f"{name}.{k}.o"
                 obj.parent.mkdir(parents=True, exist_ok=True)
-                _run(["g++", *CXXFLAGS, "-O2", *INCLUDES, f"-I{ROOT / 'tests' / 'cpp'}", "-c",
-                      str(src), "-o", str(obj)])
+                _run(["g++", *CXXFLAGS, "-O2", *INCLUDES, f"-I{ROOT / 'tests' / 'cpp'}",
+                      f"-I{OPS_SRC}", "-c", str(src), "-o", str(obj)])
                 objs.append(str(obj))
             _run([NVCC, *ARCH, "-o", str(out), *objs, f"-L{LIB}", "-ltnccl",
                   "-Xlinker", f"-rpath,{LIB}", "-Xlinker", "-rpath,$ORIGIN/../../tiny_nccl_b200/lib",
