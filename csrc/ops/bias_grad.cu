@@ -139,6 +139,11 @@ extern "C" int tnops_colsum_parts(int M, int N) {
 static int launchColsum(const uint16_t* gy, const uint16_t* pre, uint16_t* gout, float* db,
                         float* partial, int M, int N, bool gelu, cudaStream_t stream) {
   if (M <= 0 || N <= 0 || N % 8 != 0) return 1;
+  // 16-byte pieces of every row: N % 8 == 0 keeps the rows on the boundary
+  // when the base pointers are.
+  if ((reinterpret_cast<uintptr_t>(gy) | reinterpret_cast<uintptr_t>(pre) |
+       reinterpret_cast<uintptr_t>(gout)) & 15)
+    return 1;
   const int parts = tnops_colsum_parts(M, N);
   const int rowsPer = (M + parts - 1) / parts;
   const dim3 grid((unsigned)((N + kCols - 1) / kCols), (unsigned)parts);

@@ -483,6 +483,12 @@ extern "C" int tnops_ln_fwd(const float* x, const uint16_t* delta, const float* 
                             float* x_out, uint16_t* y, float* mean, float* rstd, int rows, int C,
                             float eps, cudaStream_t stream) {
   if (C % 4 != 0 || C > 128 * 16 || rows <= 0) return (int)cudaErrorInvalidValue;
+  // 16-byte pieces of the fp32 rows and parameters, 8-byte pieces of the bf16
+  // rows (C % 4 == 0 keeps every row on those boundaries).
+  if (((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(x_out) |
+        reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(b)) & 15) ||
+      ((reinterpret_cast<uintptr_t>(delta) | reinterpret_cast<uintptr_t>(y)) & 7))
+    return (int)cudaErrorInvalidValue;
   const int K = (C + 127) / 128;
   cudaError_t e;
   switch (K) {

@@ -16,6 +16,8 @@ extern "C" {
 
 // x_out = x + delta (delta optional, bf16); y = LayerNorm(x_out) * w + b in
 // bf16; mean/rstd saved in fp32. x, x_out fp32 [rows, C]; w, b fp32 [C].
+// C % 4 == 0 and C <= 2048; x, x_out, w, b 16-byte aligned, delta and y
+// 8-byte aligned; anything else returns 1 (invalid argument), no launch.
 int tnops_ln_fwd(const float* x, const uint16_t* delta, const float* w, const float* b,
                  float* x_out, uint16_t* y, float* mean, float* rstd, int rows, int C, float eps,
                  cudaStream_t stream);
@@ -44,7 +46,9 @@ int tnops_cross_entropy_fwd_bwd(uint16_t* logits, const int64_t* target, float* 
 
 // Bias gradient of a linear layer: db[n] = sum_m g[m, n] (g bf16 [M, N],
 // db fp32 [N], N a multiple of 8), deterministic two-pass column sum through
-// `partial` (tnops_colsum_parts(M, N) * N floats).
+// `partial` (tnops_colsum_parts(M, N) * N floats). The bf16 matrices of this
+// and the next function must be 16-byte aligned; otherwise, or with N % 8
+// != 0, they return 1 without a launch.
 int tnops_bias_grad(const uint16_t* g, float* db, float* partial, int M, int N,
                     cudaStream_t stream);
 // Fused tanh-GELU backward and bias gradient of the linear layer feeding the

@@ -293,6 +293,43 @@ def test_tcgen05_gemm_rejects_bad_arguments_before_device_work(built):
                      None) == 1
 
 
+def test_model_kernels_reject_misaligned_rows_before_device_work(built):
+    """The LayerNorm and column-sum launchers move 8- and 16-byte pieces of
+    each row; a base pointer off those boundaries is refused on the host
+    (return 1) before any CUDA call, instead of faulting in the kernel."""
+    lib = ctypes.CDLL(os.path.join(ROOT, "tiny_nccl_b200", "lib", "libtnccl_ops.so"))
+    P, I = ctypes.c_void_p, ctypes.c_int
+    p = 1 << 20  # aligned address; never dereferenced on these paths
+    fwd = lib.tnops_ln_fwd
+    fwd.argtypes = [P] * 8 + [I, I, ctypes.c_float, P]
+    fwd.restype = I
+    # x, delta, w, b, x_out, y, mean, rstd
+    ok = [p, p, p, p, p, p, p, p]
+    for i, off in [(0, 4), (2, 8), (3, 4), (4, 8), (1, 2), (5, 4)]:
+        args = list(ok)
+        args[i] += off
+        assert fwd(*args, 16, 768, 1e-5, None) == 1, (i, off)
+    bwd = lib.tnops_ln_bwd
+    bwd.argtypes = [P] * 11 + [I, I, P]
+    bwd.restype = I
+    # gy, g_res, x_out, w, mean, rstd, dx, dx_bf16, dw, db, partial
+    ok = [p] * 11
+    for i, off in [(0, 4), (1, 8), (2, 4), (3, 8), (6, 4), (7, 2)]:
+        args = list(ok)
+        args[i] += off
+        assert bwd(*args, 16, 768, None) == 1, (i, off)
+    for name, nargs in (("tnops_bias_grad", 3), ("tnops_gelu_bwd_bias", 5)):
+        f = getattr(lib, name)
+        f.argtypes = [P] * nargs + [I, I, P]
+        f.restype = I
+        bf16_args = [0] if nargs == 3 else [0, 1, 2]
+        for i in bf16_args:
+            args = [p] * nargs
+            args[i] += 8
+            assert f(*args, 64, 768, None) == 1, (name, i)
+        assert f(*([p] * nargs), 64, 770, None) == 1, name  # N % 8 != 0
+
+
 def test_example_makes_tcp_ids_for_multi_host_runs(built):
     """examples/allreduce.cc --make-id prints a TCP rendezvous id as hex (no
     GPU needed); malformed multi-host arguments are usage errors."""
