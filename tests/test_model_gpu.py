@@ -65,7 +65,8 @@ def test_cuda_graph_step_matches_eager(built):
     from tiny_nccl_b200.models import GPT2, GPT2Config
     from tiny_nccl_b200.parallel import DataParallelTrainer
 
-    if not dist.is_initialized():
+    own_group = not dist.is_initialized()
+    if own_group:
         os.environ.update({"MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(free_port())})
         dist.init_process_group("nccl", rank=0, world_size=1,
                                 device_id=torch.device("cuda", 0),
@@ -74,15 +75,19 @@ def test_cuda_graph_step_matches_eager(built):
     data = torch.randint(0, 64, (4, 65), device="cuda", generator=torch.Generator(
         device="cuda").manual_seed(5))
     runs = {}
-    for graph in (False, True):
-        comm = tn.init_from_torch_distributed(device=0)
-        torch.manual_seed(0)
-        model = GPT2(cfg, impl="fused").cuda()
-        tr = DataParallelTrainer(model, comm, lr=3e-3, reducer="flat", cuda_graph=graph)
-        losses = [tr.step(data[:, :-1], data[:, 1:]).item() for _ in range(8)]
-        runs[graph] = (losses, [p.detach().clone() for p in model.parameters()])
-        tr.close()
-        comm.destroy()
+    try:
+        for graph in (False, True):
+            comm = tn.init_from_torch_distributed(device=0)
+            torch.manual_seed(0)
+            model = GPT2(cfg, impl="fused").cuda()
+            tr = DataParallelTrainer(model, comm, lr=3e-3, reducer="flat", cuda_graph=graph)
+            losses = [tr.step(data[:, :-1], data[:, 1:]).item() for _ in range(8)]
+            runs[graph] = (losses, [p.detach().clone() for p in model.parameters()])
+            tr.close()  # releases the captured graph before the group goes away
+            comm.destroy()
+    finally:
+        if own_group:
+            dist.destroy_process_group()
     (le, pe), (lg, pg) = runs[False], runs[True]
     assert lg[-1] < lg[0] - 0.5, lg
     for a, b in zip(le, lg):
