@@ -24,6 +24,7 @@
 //  * no descriptor leaks.
 #include <dirent.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 #include <unistd.h>
 
@@ -300,6 +301,76 @@ void testStream() {
     netCloseRing(&e.a);
     netCloseRing(&e.b);
   }
+}
+
+// Throughput of one socket edge over loopback TCP: full frames of `chunk`
+// bytes on C channels through both proxies, host-memory FIFOs, no payload
+// writes or checks (the producer only publishes sizes). Returns GB/s of
+// payload, or a negative value on failure.
+double measureStream(int C, uint64_t chunk, uint64_t totalBytes) {
+  NetOptions o;
+  o.channels = C;
+  o.spinUs = 200;
+  const int S = 4;
+  const uint64_t N = totalBytes / (chunk * (uint64_t)C);  // frames per channel
+  NetFifoLayout L = makeNetFifoLayout(C, S, chunk);
+  Edge e;
+  {
+    int port = 0;
+    int lfd = tcpListen("127.0.0.1", 0, 16, &port);
+    uint32_t ip = 0;
+    parseIpv4("127.0.0.1", &ip);
+    NetHello h{kNetHelloMagic, kNetVersion, 0, 0, 1, 77, chunk, S, C};
+    e.ok = lfd >= 0 && netConnectEdge(ip, port, h, o, e.a.sendFds, 5000) == TNCCL_SUCCESS &&
+           netAcceptEdge(lfd, h, o, e.b.recvFds, 5000) == TNCCL_SUCCESS &&
+           netWaitAcks(e.a.sendFds, C, 5000) == TNCCL_SUCCESS;
+    if (lfd >= 0) close(lfd);
+    e.a.channels = e.b.channels = C;
+  }
+  Buf sendBuf(L.totalBytes), recvBuf(L.totalBytes);
+  netFifoInit(sendBuf.p(), L);
+  netFifoInit(recvBuf.p(), L);
+  std::atomic<int> errA{0}, errB{0}, bad{0};
+  NetProxy pa, pb;
+  const bool ok = e.ok &&
+                  netProxyStart(&pa, o, L, sendBuf.p(), nullptr, &e.a, hookSetError, &errA) ==
+                      TNCCL_SUCCESS &&
+                  netProxyStart(&pb, o, L, nullptr, recvBuf.p(), &e.b, hookSetError, &errB) ==
+                      TNCCL_SUCCESS;
+  RingFifo out = netRingFifo(sendBuf.p(), L), in = netRingFifo(recvBuf.p(), L);
+  const auto t0 = steady_clock::now();
+  std::thread producer([&] {
+    for (uint64_t t = 0; t < N && ok && !bad.load(); ++t)
+      for (int c = 0; c < C; ++c) {
+        const uint64_t i = ringFifoIndex(out, c, t);
+        if (!waitWord(out.credit + i, t, errA, 20000)) {
+          bad = 1;
+          return;
+        }
+        __atomic_store_n(out.bytes + i, chunk, __ATOMIC_RELAXED);
+        __atomic_store_n(out.ready + i, t + 1, __ATOMIC_RELEASE);
+      }
+  });
+  std::thread consumer([&] {
+    for (uint64_t t = 0; t < N && ok && !bad.load(); ++t)
+      for (int c = 0; c < C; ++c) {
+        const uint64_t i = ringFifoIndex(in, c, t);
+        if (!waitWord(in.ready + i, t + 1, errB, 20000)) {
+          bad = 2;
+          return;
+        }
+        if (__atomic_load_n(in.bytes + i, __ATOMIC_RELAXED) != chunk) bad = 3;
+        __atomic_store_n(in.credit + i, t + (uint64_t)S, __ATOMIC_RELEASE);
+      }
+  });
+  producer.join();
+  consumer.join();
+  const double sec = std::chrono::duration<double>(steady_clock::now() - t0).count();
+  const tncclResult sa = netProxyStop(&pa, true), sb = netProxyStop(&pb, true);
+  netCloseRing(&e.a);
+  netCloseRing(&e.b);
+  if (!ok || bad.load() || sa != TNCCL_SUCCESS || sb != TNCCL_SUCCESS) return -1.0;
+  return (double)(N * (uint64_t)C * chunk) / sec / 1e9;
 }
 
 // ---------------------------------------------------------------------------
@@ -820,7 +891,20 @@ void testRing() {
 
 }  // namespace
 
-int main() {
+int main(int argc, char** argv) {
+  if (argc > 1 && strcmp(argv[1], "--bench") == 0) {
+    // net_proxy_test --bench [total MiB]: loopback throughput of one edge.
+    const uint64_t total = (argc > 2 ? strtoull(argv[2], nullptr, 10) : 2048) << 20;
+    for (int C : {1, 2, 4})
+      for (uint64_t chunk : {64ull << 10, 256ull << 10, 1ull << 20}) {
+        const double gbs = measureStream(C, chunk, total);
+        printf("socket edge loopback: %d channel(s), %4llu KiB frames: %.2f GB/s\n", C,
+               (unsigned long long)(chunk >> 10), gbs);
+        fflush(stdout);
+        if (gbs < 0) return 1;
+      }
+    return 0;
+  }
   const int fds0 = countFds();
   testCodecAndLayout();
   testStream();

@@ -109,6 +109,16 @@ def test_socket_ring_edges(built):
     assert "net_proxy_test: PASS" in r.stdout
 
 
+def test_socket_edge_loopback_throughput_mode(built):
+    """The loopback throughput mode of the socket-edge test (full frames
+    through both proxies) completes for every channel count and frame size."""
+    r = run([os.path.join(ROOT, "build", "bin", "net_proxy_test"), "--bench", "64"], timeout=120)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    rates = [float(line.split(":")[-1].split()[0]) for line in r.stdout.splitlines()
+             if line.startswith("socket edge loopback")]
+    assert len(rates) == 9 and min(rates) > 0, r.stdout
+
+
 def test_gemm_pipeline_model(built):
     """The mbarrier hand-offs of both tcgen05 GEMM kernels (stage ring,
     accumulator buffers, abort path) as threads with asynchronous TMA / MMA
