@@ -2,8 +2,9 @@
 threaded CPU rank model under ThreadSanitizer (data races in the flag
 protocol model) and the bootstrap tests under AddressSanitizer +
 UndefinedBehaviorSanitizer (memory errors in the socket control plane), the
-socket proxy under both, and the registered-buffer control plane under
-AddressSanitizer + UndefinedBehaviorSanitizer."""
+socket proxy under both, the registered-buffer control plane under
+AddressSanitizer + UndefinedBehaviorSanitizer, and the LayerNorm plan test
+under both."""
 import os
 import shutil
 import subprocess
@@ -89,3 +90,19 @@ def test_registration_under_asan_ubsan():
     env = dict(os.environ, ASAN_OPTIONS="detect_leaks=1:abort_on_error=1")
     r = subprocess.run([exe], capture_output=True, text=True, timeout=300, env=env)
     assert r.returncode == 0 and "register_test: PASS" in r.stdout, r.stdout[-2000:] + r.stderr[-4000:]
+
+
+@pytest.mark.skipif(shutil.which("g++") is None, reason="needs g++")
+def test_ln_plan_under_tsan_and_asan():
+    """The LayerNorm plan test (its parity-slot check runs real threads)
+    under ThreadSanitizer, and its host restatements under ASan / UBSan."""
+    for name, flags, opts in (
+            ("ln_plan_tsan", ["-fsanitize=thread"], ("TSAN_OPTIONS", "halt_on_error=1")),
+            ("ln_plan_asan", ["-fsanitize=address,undefined", "-fno-omit-frame-pointer",
+                              "-fno-sanitize-recover=undefined"],
+             ("ASAN_OPTIONS", "detect_leaks=1:abort_on_error=1"))):
+        exe = _build(name, ["tests/cpp/ln_plan_test.cc"], [*flags, f"-I{ROOT}/csrc/ops"])
+        env = dict(os.environ, **{opts[0]: opts[1]})
+        r = subprocess.run([exe], capture_output=True, text=True, timeout=600, env=env)
+        assert r.returncode == 0 and "PASS" in r.stdout, r.stdout[-2000:] + r.stderr[-4000:]
+        assert "WARNING: ThreadSanitizer" not in r.stderr, r.stderr[-4000:]
